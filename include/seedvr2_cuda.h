@@ -1,0 +1,199 @@
+/* libseedvr2_cuda -- B200 (sm_100a) implementation of the SeedVR2 DiT block
+ * hot path: the AdaptiveWindowAttention and SharedLinear custom layers and
+ * the block arithmetic around them.
+ *
+ * C ABI: plain pointers and sizes, no C++ or torch types.  Unless a comment
+ * says "host", pointers are CUDA device pointers owned by the caller; the
+ * library owns only its context workspace and plan/model objects.  All work
+ * is enqueued on the context's stream; nothing synchronises unless stated.
+ *
+ * Error convention (the reference layers' own codes plus three):
+ *    0 ok, -1 invalid argument / shape, -2 inconsistent window plan,
+ *   -100 allocation failure      (adaptive_window_attention.cpp:769-845, :642-653)
+ *   -3 CUDA error, -4 a bounded device wait expired, -5 unsupported device.
+ *
+ * Reference paths below are relative to the reference checkout
+ * (Chisato623/seedvr2_ncnn).
+ */
+#ifndef SEEDVR2_CUDA_H
+#define SEEDVR2_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define S2_OK 0
+#define S2_ERR_INVALID (-1)
+#define S2_ERR_PLAN (-2)
+#define S2_ERR_CUDA (-3)
+#define S2_ERR_TIMEOUT (-4)
+#define S2_ERR_DEVICE (-5)
+#define S2_ERR_ALLOC (-100)
+
+#define S2_DTYPE_F32 0
+#define S2_DTYPE_BF16 1
+
+/* window_mode: how the AdaptiveWindowAttention window tuple is read. */
+#define S2_WINDOW_TARGET 0 /* reference: target window COUNT per axis (param ids 2-4) */
+#define S2_WINDOW_EXTENT 1 /* extension: window extent (t,h,w) in tokens */
+
+/* SharedLinear epilogues (out = A W^T + bias, then): */
+#define S2_EPI_STORE 0         /* out (bf16 or fp32) = acc */
+#define S2_EPI_GELU_TANH 1     /* out (bf16) = gelu_tanh(acc) */
+#define S2_EPI_GATE_RESIDUAL 2 /* out (fp32, in place) += acc * gate[n] */
+
+typedef struct s2_context s2_context;
+typedef struct s2_plan s2_plan;
+typedef struct s2_dit s2_dit;
+
+/* ---------------------------------------------------------------------------
+ * Context.  Replaces the Vulkan device / VkCompute / allocator set-up the
+ * layers get from ncnn (create_pipeline / upload_model lifecycle,
+ * adaptive_window_attention.cpp:981-1057, shared_linear.cpp:99-126).
+ * stream: a cudaStream_t (NULL = legacy default stream). */
+int s2_init(int device, void* stream, s2_context** out);
+void s2_destroy(s2_context* ctx);
+int s2_set_stream(s2_context* ctx, void* stream);
+/* Synchronises the stream and returns (then clears) the first error any
+ * kernel recorded in the device status word (S2_ERR_TIMEOUT / S2_ERR_INVALID). */
+int s2_status(s2_context* ctx);
+const char* s2_error_string(int code);
+int s2_version(void);
+/* Count of this library's kernel launches on ctx since creation. */
+uint64_t s2_launch_count(const s2_context* ctx);
+
+/* ---------------------------------------------------------------------------
+ * Window plan.  Replaces build_adaptive_window_plan
+ * (adaptive_window_attention.h:46-49, .cpp:565-655), bit-exact for
+ * S2_WINDOW_TARGET; S2_WINDOW_EXTENT applies the same shift/truncation rule
+ * to explicit extents.  video_shapes: host [batch][3] (t,h,w). */
+int s2_plan_build(const int* video_shapes, int batch, const int* window, int window_mode, int shifted,
+                  s2_plan** out);
+int s2_plan_info(const s2_plan* plan, int* num_windows, int* num_tokens, int* max_window_tokens);
+/* Host copies of the plan (AdaptiveWindowPlan fields, adaptive_window_attention.h:16-36).
+ * windows: 9 ints per window (sample, t0,t1,h0,h1,w0,w1, partition_offset, token_count);
+ * local_positions: 3 ints per token.  Any pointer may be NULL. */
+int s2_plan_copy(const s2_plan* plan, int* windows, int* sample_window_count, int* video_indices,
+                 int* inverse_video_indices, int* local_positions);
+void s2_plan_free(s2_plan* plan);
+
+/* ---------------------------------------------------------------------------
+ * AdaptiveWindowAttention forward.  Replaces
+ * AdaptiveWindowAttention::forward (CPU :764-978, Vulkan :1059-1270) with
+ * the layer's parameters (param ids 0-10, :700-714) and weights (:716-738).
+ *
+ * Inputs: the fused layout is q,k,v at column offsets 0, inner, 2*inner of
+ * one [tokens][3*inner] row (pass video_k = video_q + inner elements etc. and
+ * ld = 3*inner); the split layout (8-blob form) passes three [tokens][inner]
+ * arrays with ld = inner.  in_dtype S2_DTYPE_F32 or S2_DTYPE_BF16.
+ * Outputs: video_out [Nv][inner], text_out [Nt][inner] in out_dtype, fully
+ * overwritten (video rows scattered back to source order; text rows averaged
+ * over the sample's windows).  q/k/v enter the tensor cores as bf16 with
+ * fp32 softmax and accumulation. */
+typedef struct
+{
+    int heads;                   /* param 0 */
+    int head_dim;                /* param 1 (must be 128) */
+    int window[3];               /* params 2-4 */
+    int window_mode;             /* S2_WINDOW_TARGET (reference) or S2_WINDOW_EXTENT */
+    int shifted;                 /* param 5 */
+    float epsilon;               /* param 6 */
+    int rope_pairs;              /* param 7 */
+    int official_bf16_attention; /* param 10: round the context to bf16 */
+    const float* norm_weights;   /* device [4][head_dim]: video_q, video_k, text_q, text_k */
+    const float* rope_freqs;     /* device [rope_pairs] */
+} s2_awa_params;
+
+int s2_awa_forward(s2_context* ctx, const s2_awa_params* params, const s2_plan* plan, const int* video_shapes,
+                   const int* text_lengths, int batch, int in_dtype, const void* video_q, const void* video_k,
+                   const void* video_v, int64_t video_ld, const void* text_q, const void* text_k,
+                   const void* text_v, int64_t text_ld, int out_dtype, void* video_out, void* text_out);
+
+/* ---------------------------------------------------------------------------
+ * SharedLinear forward.  Replaces SharedLinear::forward (shared_linear.cpp:83-96,
+ * :128-143): one weight W [N][K] (bf16, row-major, i.e. ncnn's
+ * [num_output][num_input]) applied to two token streams A0 [M0][K] and
+ * A1 [M1][K] (bf16) in ONE launch, out_s = A_s W^T + bias, then the epilogue.
+ * bias: fp32 [N] or NULL.  gate: fp32 [N] (S2_EPI_GATE_RESIDUAL only).
+ * out_dtype: S2_DTYPE_BF16 / S2_DTYPE_F32 for S2_EPI_STORE, bf16 for GELU,
+ * fp32 (read-modify-write) for GATE_RESIDUAL.  M1 may be 0 (A1/out1 unused).
+ * K must be a multiple of 8. */
+int s2_shared_linear(s2_context* ctx, int M0, int M1, int N, int K, const void* A0, const void* A1, const void* W,
+                     const float* bias, int epilogue, const float* gate, int out_dtype, void* out0, void* out1);
+
+/* ---------------------------------------------------------------------------
+ * Block arithmetic around the layers (ops of the exported block graph).
+ * ada_rmsnorm: out[r] (bf16) = x[r] * rsqrt(mean(x[r]^2) + eps) * scale + shift,
+ * x fp32 [rows][D], shift/scale fp32 [D]. */
+int s2_ada_rmsnorm(s2_context* ctx, int rows, int D, const float* x, float eps, const float* shift,
+                   const float* scale, void* out_bf16);
+/* fp32 -> bf16 (round to nearest even). */
+int s2_convert_f32_bf16(s2_context* ctx, const float* in, void* out, int64_t count);
+
+/* ---------------------------------------------------------------------------
+ * DiT block stack.  Replaces SeedVR2DiTBlocks' block graph
+ * (seedvr2_dit.h:48-86; load :531-634 registers the two custom layers and
+ * loads blocks/seedvr2_blocks.ncnn; forward(DiTBlockInputs) :1096-1181).
+ * Weights are bf16 on the device; see s2_dit_config for the block shape. */
+typedef struct
+{
+    int num_blocks;    /* 32 */
+    int hidden;        /* D = 2560 */
+    int heads;         /* 20 */
+    int head_dim;      /* 128 */
+    int mlp_hidden;    /* F = 10240 */
+    int rope_pairs;    /* 21 */
+    int window[3];     /* AWA window tuple */
+    int window_mode;   /* S2_WINDOW_TARGET / S2_WINDOW_EXTENT */
+    float norm_eps;    /* block RMSNorm eps (1e-5) */
+    float qk_eps;      /* AWA epsilon (1e-5) */
+    int qkv_bias;      /* SharedLinear bias_term of each projection */
+    int out_bias;
+    int mlp_bias;
+} s2_dit_config;
+
+/* Host fp32 weights of one block (converted to bf16 on upload):
+ * ada [6][D]: per-block modulation offsets (attn shift/scale/gate, mlp shift/scale/gate);
+ * w_qkv [3D][D], w_out [D][D], w_up [F][D], w_down [D][F] (SharedLinear layout), biases or NULL;
+ * qk_norm [4][head_dim]; rope_freqs [rope_pairs]. */
+typedef struct
+{
+    const float* ada;
+    const float* w_qkv;
+    const float* b_qkv;
+    const float* w_out;
+    const float* b_out;
+    const float* w_up;
+    const float* b_up;
+    const float* w_down;
+    const float* b_down;
+    const float* qk_norm;
+    const float* rope_freqs;
+} s2_block_host_weights;
+
+int s2_dit_create(s2_context* ctx, const s2_dit_config* cfg, s2_dit** out);
+void s2_dit_free(s2_dit* dit);
+int s2_dit_set_block_weights(s2_dit* dit, int block, const s2_block_host_weights* w);
+/* Seeded synthetic weights generated on the device (weights ~N(0,0.02),
+ * ada offsets ~N(0,1)/sqrt(D) (+1 on the scale rows), qk norms ~N(1,0.02),
+ * rope freqs 1/10000^(2i/(2*pairs))). */
+int s2_dit_init_random(s2_dit* dit, uint64_t seed);
+/* Device-resident forward of all blocks for ONE sample:
+ * x: fp32 [Nv + Nt][D] (video rows then text rows), updated in place;
+ * modulation: fp32 [6][D] device (frontend outputs out2..out7). */
+int s2_dit_forward(s2_dit* dit, const int* video_shape, int text_length, float* x, const float* modulation);
+/* Same, host buffers in and out (the DiTBlockInputs call), batch >= 1,
+ * samples run one after another like the reference (seedvr2_dit.cpp:1107-1121):
+ * video [Nv_total][D], text [Nt_total][D], modulation [6][batch][D] (host fp32). */
+int s2_dit_forward_host(s2_dit* dit, const int* video_shapes, const int* text_lengths, int batch,
+                        const float* video, const float* text, const float* modulation, float* video_out,
+                        float* text_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

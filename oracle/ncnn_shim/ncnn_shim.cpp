@@ -1,0 +1,224 @@
+// CPU restatements of the two ncnn built-in layers the reference's hot-path
+// layers instantiate, so that the reference sources link into the oracle.
+// TEST INFRASTRUCTURE ONLY (never linked into the shipped library).
+//
+// ncnn itself (Tencent/ncnn @ 3b7bdba7fc8aea8fd46779533eee027df77c639d,
+// pinned in the reference's CMakeLists.txt:10) is not available here, so the
+// published behaviour of its layers is restated:
+//
+//   SDPA   (configured in adaptive_window_attention.cpp:847-861: param 5
+//           attn_mask=0, 6 scale=0 -> 1/sqrt(head_dim), 7 kv_cache=0)
+//          out[h][i] = sum_j softmax_j(scale * q[h][i] . k[h][j]) v[h][j],
+//          fp32, max-subtracted softmax over all keys, no mask.
+//
+//   Gemm   (configured in shared_linear.cpp:27-59: alpha=1, beta=1, transA=0,
+//           transB=1, constantB=1, constantC=1, N=num_output, K=num_input,
+//           broadcast_type_C 4 = per-output row vector, -1 = no C)
+//          out[m][n] = sum_k A[m][k] * B[n][k] + C[n], fp32.
+//
+// Both loops parallelise with OpenMP over independent outputs, so results do
+// not depend on the thread count.
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "layer.h"
+
+namespace ncnn {
+
+namespace {
+
+class ShimSDPA : public Layer
+{
+public:
+    ShimSDPA() : attn_mask(0), scale(0.f), kv_cache(0)
+    {
+        one_blob_only = false;
+        support_inplace = false;
+    }
+
+    virtual int load_param(const ParamDict& pd)
+    {
+        attn_mask = pd.get(5, 0);
+        scale = pd.get(6, 0.f);
+        kv_cache = pd.get(7, 0);
+        return (attn_mask != 0 || kv_cache != 0) ? -1 : 0;
+    }
+
+    virtual int forward(const std::vector<Mat>& bottom, std::vector<Mat>& top, const Option& opt) const
+    {
+        if (bottom.size() != 3 || top.size() != 1) return -1;
+        const Mat& q = bottom[0];
+        const Mat& k = bottom[1];
+        const Mat& v = bottom[2];
+        const int d = q.w;
+        const int sq = q.h;
+        const int heads = q.c;
+        const int sk = k.h;
+        const int dv = v.w;
+        if (k.w != d || k.c != heads || v.h != sk || v.c != heads) return -1;
+        const float s = scale == 0.f ? 1.f / std::sqrt((float)d) : scale;
+
+        Mat& out = top[0];
+        out.create(dv, sq, heads, 4u, opt.blob_allocator);
+        if (out.empty()) return -100;
+
+#pragma omp parallel for schedule(dynamic, 1) collapse(2)
+        for (int h = 0; h < heads; h++)
+        {
+            for (int i = 0; i < sq; i++)
+            {
+                std::vector<float> logits(sk);
+                const float* qi = q.channel(h).row(i);
+                float m = -INFINITY;
+                for (int j = 0; j < sk; j++)
+                {
+                    const float* kj = k.channel(h).row(j);
+                    float acc = 0.f;
+                    for (int t = 0; t < d; t++) acc += qi[t] * kj[t];
+                    logits[j] = acc * s;
+                    if (logits[j] > m) m = logits[j];
+                }
+                float sum = 0.f;
+                for (int j = 0; j < sk; j++)
+                {
+                    logits[j] = std::exp(logits[j] - m);
+                    sum += logits[j];
+                }
+                const float inv = 1.f / sum;
+                float* oi = out.channel(h).row(i);
+                for (int t = 0; t < dv; t++) oi[t] = 0.f;
+                for (int j = 0; j < sk; j++)
+                {
+                    const float p = logits[j] * inv;
+                    const float* vj = v.channel(h).row(j);
+                    for (int t = 0; t < dv; t++) oi[t] += p * vj[t];
+                }
+            }
+        }
+        return 0;
+    }
+
+private:
+    int attn_mask;
+    float scale;
+    int kv_cache;
+};
+
+class ShimGemm : public Layer
+{
+public:
+    ShimGemm() : alpha(1.f), beta(1.f), transA(0), transB(0), constantB(0), constantC(0), N(0), K(0), bcastC(-1)
+    {
+        one_blob_only = true;
+        support_inplace = false;
+    }
+
+    virtual int load_param(const ParamDict& pd)
+    {
+        alpha = pd.get(0, 1.f);
+        beta = pd.get(1, 1.f);
+        transA = pd.get(2, 0);
+        transB = pd.get(3, 0);
+        constantB = pd.get(5, 0);
+        constantC = pd.get(6, 0);
+        N = pd.get(8, 0);
+        K = pd.get(9, 0);
+        bcastC = pd.get(10, 0);
+        // Only the configuration SharedLinear uses is restated.
+        if (transA != 0 || transB != 1 || constantB != 1 || constantC != 1 || N <= 0 || K <= 0) return -1;
+        if (bcastC != 4 && bcastC != -1) return -1;
+        return 0;
+    }
+
+    virtual int load_model(const ModelBin& mb)
+    {
+        B = mb.load(K * N, 0);
+        if (B.empty()) return -100;
+        if (bcastC == 4)
+        {
+            C = mb.load(N, 0);
+            if (C.empty()) return -100;
+        }
+        return 0;
+    }
+
+    virtual int forward(const Mat& A, Mat& out, const Option& opt) const
+    {
+        if (A.dims != 2 || A.w != K) return -1;
+        const int M = A.h;
+        out.create(N, M, 4u, opt.blob_allocator);
+        if (out.empty()) return -100;
+        const float* bdata = (const float*)B.data;
+        const float* cdata = bcastC == 4 ? (const float*)C.data : 0;
+
+        // 4x4 register tiles of dot products over contiguous K.
+#pragma omp parallel for schedule(dynamic, 1)
+        for (int m0 = 0; m0 < M; m0 += 4)
+        {
+            const int mr = M - m0 < 4 ? M - m0 : 4;
+            for (int n0 = 0; n0 < N; n0 += 4)
+            {
+                const int nr = N - n0 < 4 ? N - n0 : 4;
+                float acc[4][4] = {{0.f}};
+                const float* a[4];
+                const float* b[4];
+                for (int r = 0; r < 4; r++)
+                {
+                    a[r] = A.row(m0 + (r < mr ? r : 0));
+                    b[r] = bdata + (size_t)(n0 + (r < nr ? r : 0)) * K;
+                }
+                for (int r = 0; r < 4; r++)
+                {
+                    for (int c = 0; c < 4; c++)
+                    {
+                        float s = 0.f;
+                        const float* ar = a[r];
+                        const float* bc = b[c];
+#pragma omp simd reduction(+ : s)
+                        for (int t = 0; t < K; t++) s += ar[t] * bc[t];
+                        acc[r][c] = s;
+                    }
+                }
+                for (int r = 0; r < mr; r++)
+                {
+                    float* o = out.row(m0 + r);
+                    for (int c = 0; c < nr; c++)
+                        o[n0 + c] = alpha * acc[r][c] + (cdata ? beta * cdata[n0 + c] : 0.f);
+                }
+            }
+        }
+        return 0;
+    }
+
+private:
+    float alpha;
+    float beta;
+    int transA;
+    int transB;
+    int constantB;
+    int constantC;
+    int N;
+    int K;
+    int bcastC;
+    Mat B;
+    Mat C;
+};
+
+} // namespace
+
+Layer* create_layer(const char* type)
+{
+    const std::string t(type ? type : "");
+    if (t == "SDPA") return new ShimSDPA;
+    if (t == "Gemm") return new ShimGemm;
+    return 0;
+}
+
+Layer* create_layer_cpu(const char* type)
+{
+    return create_layer(type);
+}
+
+} // namespace ncnn

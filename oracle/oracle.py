@@ -1,0 +1,254 @@
+"""ctypes front-end for the CPU checkers (TEST INFRASTRUCTURE ONLY).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline /
+reference arm import this module, and only as the checker or the timed CPU
+baseline; the shipped package never imports it.
+
+* :class:`Port` wraps ``oracle/libs2_oracle.so`` -- our C restatement of the
+  reference's hot path (``s2_oracle.c``).
+* :class:`Ref` wraps ``oracle/_ref/libs2_ref.so`` -- the reference's OWN
+  ``adaptive_window_attention.cpp`` / ``shared_linear.cpp`` compiled against
+  the clean-room ncnn API shim (built only where the reference tree exists).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PORT_SO = os.path.join(HERE, "libs2_oracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libs2_ref.so")
+
+WINDOW_TARGET = 0
+WINDOW_EXTENT = 1
+
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+
+
+def build(ref_tree: str | None = None) -> None:
+    """Compile the port (always) and the reference build (when its tree exists)."""
+    subprocess.run(["make", "-s", "-C", HERE, "port"], check=True)
+    tree = ref_tree or os.environ.get("S2_REFERENCE_TREE", "/root/reference")
+    if os.path.isdir(os.path.join(tree, "src", "seedvr2")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={tree}"], check=True)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.int32)
+
+
+class Plan:
+    """Window plan arrays (AdaptiveWindowPlan, adaptive_window_attention.h:29-36)."""
+
+    def __init__(self, windows, sample_window_count, video_indices, inverse, local_positions):
+        self.windows = windows  # [nw, 9]
+        self.sample_window_count = sample_window_count
+        self.video_indices = video_indices
+        self.inverse_video_indices = inverse
+        self.local_positions = local_positions  # [n, 3]
+
+    def as_dict(self):
+        return {
+            "windows": self.windows,
+            "sample_window_count": self.sample_window_count,
+            "video_indices": self.video_indices,
+            "inverse_video_indices": self.inverse_video_indices,
+            "local_positions": self.local_positions,
+        }
+
+
+class Port:
+    """Our C restatement (oracle/s2_oracle.c)."""
+
+    def __init__(self, path: str = PORT_SO):
+        if not os.path.exists(path):
+            build()
+        lib = C.CDLL(path)
+        lib.s2o_plan_sizes.argtypes = [_i32p, C.c_int, C.c_int, _i32p, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        lib.s2o_plan_build.argtypes = [_i32p, C.c_int, C.c_int, _i32p, C.c_int, _i32p, _i32p, _i32p, _i32p, _i32p]
+        lib.s2o_round_bf16.argtypes = [C.c_float]
+        lib.s2o_round_bf16.restype = C.c_float
+        lib.s2o_awa_forward.argtypes = [_i32p, C.c_float, _f32p, _f32p, _i32p, _i32p, C.c_int,
+                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, _f32p, _f32p]
+        lib.s2o_linear.argtypes = [_f32p, C.c_int, C.c_int, _f32p, C.c_void_p, C.c_int, _f32p]
+        lib.s2o_block_forward.argtypes = [_i32p, C.c_float, C.c_float, C.c_void_p, _f32p, _i32p, _i32p, C.c_int,
+                                          _f32p, _f32p, C.c_int]
+        self.lib = lib
+
+    def plan(self, shapes, window, shifted, mode=WINDOW_TARGET) -> Plan:
+        shapes = _i32(shapes).reshape(-1, 3)
+        win = _i32(window)
+        nw, nt = C.c_int(), C.c_int()
+        r = self.lib.s2o_plan_sizes(shapes, len(shapes), mode, win, int(shifted), C.byref(nw), C.byref(nt))
+        if r != 0:
+            raise ValueError(f"s2o_plan_sizes returned {r}")
+        windows = np.zeros((nw.value, 9), np.int32)
+        swc = np.zeros(len(shapes), np.int32)
+        vi = np.zeros(nt.value, np.int32)
+        inv = np.zeros(nt.value, np.int32)
+        pos = np.zeros((nt.value, 3), np.int32)
+        r = self.lib.s2o_plan_build(shapes, len(shapes), mode, win, int(shifted), windows, swc, vi, inv, pos)
+        if r != 0:
+            raise ValueError(f"s2o_plan_build returned {r}")
+        return Plan(windows, swc, vi, inv, pos)
+
+    def round_bf16(self, x):
+        x = _f32(x)
+        # vectorised restatement of the same rule, checked against the C one
+        b = x.view(np.uint32).astype(np.uint64)
+        finite = (b & 0x7F800000) != 0x7F800000
+        b = np.where(finite, b + 0x7FFF + ((b >> 16) & 1), b) & 0xFFFF0000
+        return b.astype(np.uint32).view(np.float32)
+
+    def awa_forward(self, *, heads, head_dim, window, shifted, eps, rope_pairs, norms, freqs, shapes,
+                    text_lengths, video_qkv=None, text_qkv=None, split=None, mode=WINDOW_TARGET,
+                    bf16=False):
+        """norms: [4, head_dim]; video_qkv [Nv, 3*inner] or split=(vq,vk,vv,tq,tk,tv)."""
+        inner = heads * head_dim
+        shapes = _i32(shapes).reshape(-1, 3)
+        tl = _i32(text_lengths)
+        nv = int(np.prod(shapes, axis=1).sum())
+        nt = int(tl.sum())
+        keep = []
+        if split is None:
+            v = _f32(video_qkv)
+            t = _f32(text_qkv)
+            keep += [v, t]
+            vb, tb = v.ctypes.data, t.ctypes.data
+            ptrs = [vb, vb + inner * 4, vb + 2 * inner * 4, tb, tb + inner * 4, tb + 2 * inner * 4]
+            vld = tld = 3 * inner
+        else:
+            arrs = [_f32(a) for a in split]
+            keep += arrs
+            ptrs = [a.ctypes.data for a in arrs]
+            vld = tld = inner
+        ip = _i32([heads, head_dim, window[0], window[1], window[2], int(shifted), rope_pairs, mode, int(bf16)])
+        vo = np.zeros((nv, inner), np.float32)
+        to = np.zeros((nt, inner), np.float32)
+        r = self.lib.s2o_awa_forward(ip, eps, _f32(norms).reshape(-1), _f32(freqs), shapes, tl, len(shapes),
+                                     ptrs[0], ptrs[1], ptrs[2], vld, ptrs[3], ptrs[4], ptrs[5], tld, vo, to)
+        if r != 0:
+            raise ValueError(f"s2o_awa_forward returned {r}")
+        return vo, to
+
+    def linear(self, a, w, bias=None):
+        a = _f32(a)
+        w = _f32(w)
+        out = np.zeros((a.shape[0], w.shape[0]), np.float32)
+        b = _f32(bias) if bias is not None else None
+        self.lib.s2o_linear(a, a.shape[0], a.shape[1], w, b.ctypes.data if b is not None else None,
+                            w.shape[0], out)
+        return out
+
+    def block_forward(self, *, dims, eps_norm, eps_qk, weights: dict, modulation, shapes, text_lengths,
+                      x_video, x_text, emulate_bf16=False):
+        """weights: dict of fp32 arrays keyed like s2o_block_weights; returns updated (xv, xt)."""
+
+        class W(C.Structure):
+            _fields_ = [(n, C.c_void_p) for n in
+                        ("ada", "w_qkv", "b_qkv", "w_out", "b_out", "w_up", "b_up", "w_down", "b_down",
+                         "qk_norm", "freqs")]
+
+        keep = {k: (_f32(v) if v is not None else None) for k, v in weights.items()}
+        w = W(*[(keep[n].ctypes.data if keep.get(n) is not None else None) for n, _ in W._fields_])
+        xv = _f32(x_video).copy()
+        xt = _f32(x_text).copy()
+        shapes = _i32(shapes).reshape(-1, 3)
+        r = self.lib.s2o_block_forward(_i32(dims), eps_norm, eps_qk, C.addressof(w), _f32(modulation).reshape(-1),
+                                       shapes, _i32(text_lengths), len(shapes), xv, xt, int(emulate_bf16))
+        if r != 0:
+            raise ValueError(f"s2o_block_forward returned {r}")
+        return xv, xt
+
+
+class Ref:
+    """The reference's own layer code (oracle/_ref/libs2_ref.so)."""
+
+    def __init__(self, path: str = REF_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        lib = C.CDLL(path)
+        lib.s2ref_plan_build.argtypes = [_i32p, C.c_int, _i32p, C.c_int, C.POINTER(C.c_void_p)]
+        lib.s2ref_plan_sizes.argtypes = [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        lib.s2ref_plan_copy.argtypes = [C.c_void_p, _i32p, _i32p, _i32p, _i32p, _i32p]
+        lib.s2ref_plan_free.argtypes = [C.c_void_p]
+        lib.s2ref_awa_forward.argtypes = [_i32p, C.c_float, _f32p, C.c_int, C.c_int, C.POINTER(C.c_void_p),
+                                          C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, _f32p, _f32p]
+        lib.s2ref_shared_linear_forward.argtypes = [C.c_int, C.c_int, C.c_int, _f32p, _f32p, C.c_int, _f32p,
+                                                    C.c_int, _f32p, _f32p]
+        self.lib = lib
+
+    def plan(self, shapes, target, shifted) -> Plan:
+        shapes = _i32(shapes).reshape(-1, 3)
+        h = C.c_void_p()
+        r = self.lib.s2ref_plan_build(shapes, len(shapes), _i32(target), int(shifted), C.byref(h))
+        if r != 0:
+            raise ValueError(f"build_adaptive_window_plan returned {r}")
+        nw, nt, ns = C.c_int(), C.c_int(), C.c_int()
+        self.lib.s2ref_plan_sizes(h, C.byref(nw), C.byref(nt), C.byref(ns))
+        windows = np.zeros((nw.value, 9), np.int32)
+        swc = np.zeros(ns.value, np.int32)
+        vi = np.zeros(nt.value, np.int32)
+        inv = np.zeros(nt.value, np.int32)
+        pos = np.zeros((nt.value, 3), np.int32)
+        self.lib.s2ref_plan_copy(h, windows, swc, vi, inv, pos)
+        self.lib.s2ref_plan_free(h)
+        return Plan(windows, swc, vi, inv, pos)
+
+    def awa_forward(self, *, heads, head_dim, target, shifted, eps, rope_pairs, norms, freqs, shapes,
+                    text_lengths, video_qkv=None, text_qkv=None, split=None, shared_norm=False,
+                    shape_int32=False, bf16=False):
+        inner = heads * head_dim
+        shapes = _i32(shapes).reshape(-1, 3)
+        tl = _i32(text_lengths)
+        nv = int(np.prod(shapes, axis=1).sum())
+        nt = int(tl.sum())
+        norms = _f32(norms).reshape(4, head_dim)
+        wts = [norms[0], norms[1]] + ([] if shared_norm else [norms[2], norms[3]]) + [_f32(freqs)]
+        wflat = np.concatenate(wts).astype(np.float32)
+        if split is None:
+            arrs = [_f32(video_qkv), _f32(text_qkv)]
+            nv, nt = arrs[0].shape[0], arrs[1].shape[0]  # blob heights as given (the layer validates them)
+        else:
+            arrs = [_f32(a) for a in split]
+            nv, nt = arrs[0].shape[0], arrs[3].shape[0]
+        ptrs = (C.c_void_p * len(arrs))(*[a.ctypes.data for a in arrs])
+        if shape_int32:
+            sb = shapes.astype(np.int32)
+            tb = tl.astype(np.int32)
+        else:
+            sb = shapes.astype(np.float32)
+            tb = tl.astype(np.float32)
+        sb = np.ascontiguousarray(sb)
+        tb = np.ascontiguousarray(tb)
+        ip = _i32([heads, head_dim, target[0], target[1], target[2], int(shifted), rope_pairs, int(shared_norm),
+                   int(shape_int32), int(bf16)])
+        vo = np.zeros((nv, inner), np.float32)
+        to = np.zeros((nt, inner), np.float32)
+        r = self.lib.s2ref_awa_forward(ip, eps, wflat, len(wflat), 0 if split is None else 1, ptrs, nv, nt,
+                                       sb.ctypes.data, tb.ctypes.data, len(shapes), vo, to)
+        if r != 0:
+            raise ValueError(f"AdaptiveWindowAttention::forward returned {r}")
+        return vo, to
+
+    def shared_linear(self, video, text, weight, bias=None):
+        video = _f32(video)
+        text = _f32(text)
+        n, k = weight.shape
+        flat = _f32(weight).reshape(-1) if bias is None else np.concatenate([_f32(weight).reshape(-1), _f32(bias)])
+        vo = np.zeros((video.shape[0], n), np.float32)
+        to = np.zeros((text.shape[0], n), np.float32)
+        r = self.lib.s2ref_shared_linear_forward(n, k, int(bias is not None), _f32(flat), video, video.shape[0],
+                                                 text, text.shape[0], vo, to)
+        if r != 0:
+            raise ValueError(f"SharedLinear::forward returned {r}")
+        return vo, to

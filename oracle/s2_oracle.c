@@ -1,0 +1,525 @@
+/* CPU oracle: plain-C restatement of the SeedVR2 DiT block hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY -- see s2_oracle.h.  Reference citations are
+ * relative to the reference checkout (Chisato623/seedvr2_ncnn).
+ */
+#include "s2_oracle.h"
+
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ceil_div_extent (src/seedvr2/adaptive_window_attention.cpp:434-437) */
+static int ceil_div(int extent, int window)
+{
+    return (extent + window - 1) / window;
+}
+
+/* Window extents of one sample.
+ * S2O_WINDOW_TARGET follows build_adaptive_window_plan
+ * (adaptive_window_attention.cpp:577-588): the tuple is a target window
+ * count on a ~3600-token resized grid, rounded half-to-even like Python's
+ * round() (python_round_positive, :439-444).
+ * S2O_WINDOW_EXTENT takes the tuple as the extent itself (an extension: the
+ * BASELINE configs name extents that no integer target count produces). */
+static int window_extents(int t, int h, int w, int mode, const int* win, int* wt, int* wh, int* ww)
+{
+    if (t <= 0 || h <= 0 || w <= 0 || win[0] <= 0 || win[1] <= 0 || win[2] <= 0) return -1;
+    if (mode == S2O_WINDOW_EXTENT)
+    {
+        *wt = win[0];
+        *wh = win[1];
+        *ww = win[2];
+    }
+    else if (mode == S2O_WINDOW_TARGET)
+    {
+        const double scale = sqrt(3600.0 / (double)(h * w));
+        const int rh = (int)nearbyint(h * scale);
+        const int rw = (int)nearbyint(w * scale);
+        *wt = ceil_div(t < 30 ? t : 30, win[0]);
+        *wh = ceil_div(rh, win[1]);
+        *ww = ceil_div(rw, win[2]);
+    }
+    else
+        return -1;
+    if (*wt <= 0 || *wh <= 0 || *ww <= 0) return -1;
+    return 0;
+}
+
+/* Half-window shifted bounds (adaptive_window_attention.cpp:592-629):
+ * axis shift 0.5 only when shifted and window < extent; window i covers
+ * [max(int((i-s)*win),0), min(int((i-s+1)*win),ext)), truncating toward 0.
+ * Unshifted: [i*win, min((i+1)*win, ext)). */
+static int axis_count(int ext, int win, int shifted, double* s)
+{
+    *s = (shifted && win < ext) ? 0.5 : 0.0;
+    if (!shifted) return ceil_div(ext, win);
+    return *s > 0.0 ? (int)ceil((ext - *s) / win) + 1 : 1;
+}
+
+static void axis_bounds(int i, int ext, int win, int shifted, double s, int* lo, int* hi)
+{
+    if (shifted)
+    {
+        const int a = (int)((i - s) * win);
+        const int b = (int)((i - s + 1.0) * win);
+        *lo = a > 0 ? a : 0;
+        *hi = b < ext ? b : ext;
+    }
+    else
+    {
+        *lo = i * win;
+        *hi = (i + 1) * win < ext ? (i + 1) * win : ext;
+    }
+}
+
+/* Shared walk for sizes and fill.  Window order: w outer, h, t inner
+ * (:600-630); token order inside a window t, h, w (append_slice, :446-473). */
+static int plan_walk(const int* shapes, int batch, int mode, const int* win, int shifted, int* num_windows,
+                     int* num_tokens, int* windows, int* sample_window_count, int* video_indices,
+                     int* local_positions)
+{
+    int nwin = 0, ntok = 0, sample_offset = 0;
+    for (int s = 0; s < batch; s++)
+    {
+        const int t = shapes[s * 3], h = shapes[s * 3 + 1], w = shapes[s * 3 + 2];
+        int wt, wh, ww;
+        if (window_extents(t, h, w, mode, win, &wt, &wh, &ww) != 0) return -1;
+        double st, sh, sw;
+        const int nt = axis_count(t, wt, shifted, &st);
+        const int nh = axis_count(h, wh, shifted, &sh);
+        const int nw = axis_count(w, ww, shifted, &sw);
+        const int first = nwin;
+        for (int iw = 0; iw < nw; iw++)
+        {
+            int w0, w1;
+            axis_bounds(iw, w, ww, shifted, sw, &w0, &w1);
+            if (w1 <= w0) continue;
+            for (int ih = 0; ih < nh; ih++)
+            {
+                int h0, h1;
+                axis_bounds(ih, h, wh, shifted, sh, &h0, &h1);
+                if (h1 <= h0) continue;
+                for (int it = 0; it < nt; it++)
+                {
+                    int t0, t1;
+                    axis_bounds(it, t, wt, shifted, st, &t0, &t1);
+                    if (t1 <= t0) continue;
+                    const int count = (t1 - t0) * (h1 - h0) * (w1 - w0);
+                    if (windows)
+                    {
+                        int* o = windows + (size_t)nwin * 9;
+                        o[0] = s;
+                        o[1] = t0;
+                        o[2] = t1;
+                        o[3] = h0;
+                        o[4] = h1;
+                        o[5] = w0;
+                        o[6] = w1;
+                        o[7] = ntok;
+                        o[8] = count;
+                        int p = ntok;
+                        for (int ti = t0; ti < t1; ti++)
+                            for (int hi = h0; hi < h1; hi++)
+                                for (int wi = w0; wi < w1; wi++, p++)
+                                {
+                                    video_indices[p] = sample_offset + (ti * h + hi) * w + wi;
+                                    local_positions[p * 3] = ti - t0;
+                                    local_positions[p * 3 + 1] = hi - h0;
+                                    local_positions[p * 3 + 2] = wi - w0;
+                                }
+                    }
+                    nwin++;
+                    ntok += count;
+                }
+            }
+        }
+        if (sample_window_count) sample_window_count[s] = nwin - first;
+        sample_offset += t * h * w;
+    }
+    *num_windows = nwin;
+    *num_tokens = ntok;
+    return sample_offset == ntok ? 0 : -2;
+}
+
+int s2o_plan_sizes(const int* shapes, int batch, int window_mode, const int* window, int shifted,
+                   int* num_windows, int* num_tokens)
+{
+    if (batch <= 0) return -1;
+    const int r = plan_walk(shapes, batch, window_mode, window, shifted, num_windows, num_tokens, 0, 0, 0, 0);
+    return r == -1 ? -1 : 0;
+}
+
+/* build_adaptive_window_plan (adaptive_window_attention.cpp:565-655),
+ * including the coverage/inverse-permutation checks (:642-653). */
+int s2o_plan_build(const int* shapes, int batch, int window_mode, const int* window, int shifted,
+                   int* windows, int* sample_window_count, int* video_indices, int* inverse_video_indices,
+                   int* local_positions)
+{
+    int nwin, ntok;
+    if (batch <= 0) return -1;
+    const int r = plan_walk(shapes, batch, window_mode, window, shifted, &nwin, &ntok, windows,
+                            sample_window_count, video_indices, local_positions);
+    if (r != 0) return r;
+    for (int i = 0; i < ntok; i++) inverse_video_indices[i] = -1;
+    for (int p = 0; p < ntok; p++)
+    {
+        const int src = video_indices[p];
+        if (src < 0 || src >= ntok || inverse_video_indices[src] != -1) return -2;
+        inverse_video_indices[src] = p;
+    }
+    return 0;
+}
+
+/* round_bf16 (adaptive_window_attention.cpp:499-508): round-to-nearest-even
+ * on the upper 16 bits; Inf/NaN exponents are truncated, not rounded. */
+float s2o_round_bf16(float v)
+{
+    uint32_t bits;
+    memcpy(&bits, &v, 4);
+    if ((bits & 0x7f800000u) != 0x7f800000u) bits += 0x00007fffu + ((bits >> 16) & 1u);
+    bits &= 0xffff0000u;
+    memcpy(&v, &bits, 4);
+    return v;
+}
+
+/* rms_norm (adaptive_window_attention.cpp:510-519): sequential fp32 sum of
+ * squares, x * (1/sqrt(mean + eps)) * w. */
+static void rms_norm_head(const float* x, const float* w, int n, float eps, float* y)
+{
+    float ss = 0.f;
+    for (int i = 0; i < n; i++) ss += x[i] * x[i];
+    const float inv = 1.f / sqrtf(ss / n + eps);
+    for (int i = 0; i < n; i++) y[i] = x[i] * inv * w[i];
+}
+
+/* apply_mm_rope (adaptive_window_attention.cpp:521-543): three axes (t,h,w)
+ * of `pairs` interleaved (even, odd) pairs each; angle = pos[axis]*freq[pair];
+ * dims >= 6*pairs pass through; skipped entirely if 6*pairs > head_dim. */
+static void mm_rope(float* x, int head_dim, const float* freqs, int pairs, const int* pos)
+{
+    const int axis_width = pairs * 2;
+    if (axis_width * 3 > head_dim) return;
+    for (int axis = 0; axis < 3; axis++)
+    {
+        float* a = x + axis * axis_width;
+        for (int p = 0; p < pairs; p++)
+        {
+            const float ang = pos[axis] * freqs[p];
+            const float c = cosf(ang), s = sinf(ang);
+            const float x0 = a[2 * p], x1 = a[2 * p + 1];
+            a[2 * p] = x0 * c - x1 * s;
+            a[2 * p + 1] = x0 * s + x1 * c;
+        }
+    }
+}
+
+/* softmax(q k^T / sqrt(d)) v for one head of one window: ncnn SDPA as
+ * configured at adaptive_window_attention.cpp:850-861 (scale 0 => 1/sqrt(d),
+ * no mask).  q,k,v,o: [S][d]. */
+static void sdpa_head(const float* q, const float* k, const float* v, int S, int d, float* o, float* scratch)
+{
+    const float scale = 1.f / sqrtf((float)d);
+    for (int i = 0; i < S; i++)
+    {
+        float m = -INFINITY;
+        for (int j = 0; j < S; j++)
+        {
+            float acc = 0.f;
+            for (int t = 0; t < d; t++) acc += q[(size_t)i * d + t] * k[(size_t)j * d + t];
+            scratch[j] = acc * scale;
+            if (scratch[j] > m) m = scratch[j];
+        }
+        float sum = 0.f;
+        for (int j = 0; j < S; j++)
+        {
+            scratch[j] = expf(scratch[j] - m);
+            sum += scratch[j];
+        }
+        const float inv = 1.f / sum;
+        float* oi = o + (size_t)i * d;
+        for (int t = 0; t < d; t++) oi[t] = 0.f;
+        for (int j = 0; j < S; j++)
+        {
+            const float p = scratch[j] * inv;
+            for (int t = 0; t < d; t++) oi[t] += p * v[(size_t)j * d + t];
+        }
+    }
+}
+
+/* AdaptiveWindowAttention::forward, CPU path (adaptive_window_attention.cpp:764-978):
+ * per window, gather the window's video rows then the sample's text rows,
+ * RMSNorm q/k per head (video or text weights), RoPE at window-local
+ * positions (t + text_len, h, w) for video and (i, i, i) for text, optional
+ * bf16 rounding of q/k/v and of the context, SDPA, then scatter video rows to
+ * their source index and add text rows * (1 / windows in sample). */
+int s2o_awa_forward(const int* ip, float eps, const float* norms, const float* freqs, const int* shapes,
+                    const int* text_lengths, int batch, const float* vq, const float* vk, const float* vv, int v_ld,
+                    const float* tq, const float* tk, const float* tv, int t_ld, float* video_out, float* text_out)
+{
+    const int heads = ip[0], d = ip[1], shifted = ip[5], pairs = ip[6], mode = ip[7], bf16 = ip[8];
+    const int win[3] = {ip[2], ip[3], ip[4]};
+    if (heads <= 0 || d <= 0 || pairs * 6 > d || batch <= 0) return -1;
+    const int inner = heads * d;
+    int nwin, ntok;
+    if (s2o_plan_sizes(shapes, batch, mode, win, shifted, &nwin, &ntok) != 0) return -1;
+    int total_text = 0;
+    for (int s = 0; s < batch; s++)
+    {
+        if (text_lengths[s] <= 0) return -1;
+        total_text += text_lengths[s];
+    }
+    int* windows = (int*)malloc(sizeof(int) * 9 * (size_t)nwin);
+    int* swc = (int*)malloc(sizeof(int) * (size_t)batch);
+    int* vidx = (int*)malloc(sizeof(int) * (size_t)ntok);
+    int* inv = (int*)malloc(sizeof(int) * (size_t)ntok);
+    int* pos = (int*)malloc(sizeof(int) * 3 * (size_t)ntok);
+    int* toff = (int*)malloc(sizeof(int) * (size_t)batch);
+    int ret = s2o_plan_build(shapes, batch, mode, win, shifted, windows, swc, vidx, inv, pos);
+    if (ret != 0) goto done;
+    toff[0] = 0;
+    for (int s = 1; s < batch; s++) toff[s] = toff[s - 1] + text_lengths[s - 1];
+    memset(video_out, 0, sizeof(float) * (size_t)ntok * inner);
+    memset(text_out, 0, sizeof(float) * (size_t)total_text * inner);
+
+    for (int wi = 0; wi < nwin; wi++)
+    {
+        const int* wnd = windows + (size_t)wi * 9;
+        const int s = wnd[0], off = wnd[7], L = wnd[8], T = text_lengths[s];
+        const int S = L + T;
+        float* Q = (float*)malloc(sizeof(float) * (size_t)heads * S * d);
+        float* K = (float*)malloc(sizeof(float) * (size_t)heads * S * d);
+        float* V = (float*)malloc(sizeof(float) * (size_t)heads * S * d);
+        float* O = (float*)malloc(sizeof(float) * (size_t)heads * S * d);
+        float* scratch = (float*)malloc(sizeof(float) * (size_t)S);
+        for (int r = 0; r < S; r++)
+        {
+            const float *sq, *sk, *sv;
+            const float *wq, *wk;
+            int p3[3];
+            if (r < L)
+            {
+                const int p = off + r, src = vidx[p];
+                sq = vq + (size_t)src * v_ld;
+                sk = vk + (size_t)src * v_ld;
+                sv = vv + (size_t)src * v_ld;
+                wq = norms;
+                wk = norms + d;
+                p3[0] = pos[p * 3] + T;
+                p3[1] = pos[p * 3 + 1];
+                p3[2] = pos[p * 3 + 2];
+            }
+            else
+            {
+                const int j = r - L, src = toff[s] + j;
+                sq = tq + (size_t)src * t_ld;
+                sk = tk + (size_t)src * t_ld;
+                sv = tv + (size_t)src * t_ld;
+                wq = norms + 2 * d;
+                wk = norms + 3 * d;
+                p3[0] = p3[1] = p3[2] = j;
+            }
+            for (int h = 0; h < heads; h++)
+            {
+                float* q = Q + ((size_t)h * S + r) * d;
+                float* k = K + ((size_t)h * S + r) * d;
+                float* v = V + ((size_t)h * S + r) * d;
+                rms_norm_head(sq + h * d, wq, d, eps, q);
+                rms_norm_head(sk + h * d, wk, d, eps, k);
+                memcpy(v, sv + h * d, sizeof(float) * d);
+                mm_rope(q, d, freqs, pairs, p3);
+                mm_rope(k, d, freqs, pairs, p3);
+                if (bf16)
+                    for (int t = 0; t < d; t++)
+                    {
+                        q[t] = s2o_round_bf16(q[t]);
+                        k[t] = s2o_round_bf16(k[t]);
+                        v[t] = s2o_round_bf16(v[t]);
+                    }
+            }
+        }
+        for (int h = 0; h < heads; h++)
+            sdpa_head(Q + (size_t)h * S * d, K + (size_t)h * S * d, V + (size_t)h * S * d, S, d,
+                      O + (size_t)h * S * d, scratch);
+        if (bf16)
+            for (size_t i = 0; i < (size_t)heads * S * d; i++) O[i] = s2o_round_bf16(O[i]);
+        const float pool = 1.f / swc[s];
+        for (int r = 0; r < S; r++)
+        {
+            for (int h = 0; h < heads; h++)
+            {
+                const float* o = O + ((size_t)h * S + r) * d;
+                if (r < L)
+                {
+                    float* dst = video_out + (size_t)vidx[off + r] * inner + h * d;
+                    memcpy(dst, o, sizeof(float) * d);
+                }
+                else
+                {
+                    float* dst = text_out + (size_t)(toff[s] + r - L) * inner + h * d;
+                    for (int t = 0; t < d; t++) dst[t] += o[t] * pool;
+                }
+            }
+        }
+        free(Q);
+        free(K);
+        free(V);
+        free(O);
+        free(scratch);
+    }
+done:
+    free(windows);
+    free(swc);
+    free(vidx);
+    free(inv);
+    free(pos);
+    free(toff);
+    return ret;
+}
+
+/* SharedLinear projection (shared_linear.cpp:27-96 through ncnn Gemm with
+ * transB=1 and a per-output C row): out = a w^T + bias, fp32. */
+void s2o_linear(const float* a, int m, int k, const float* w, const float* bias, int n, float* out)
+{
+#pragma omp parallel for schedule(static)
+    for (int i = 0; i < m; i++)
+    {
+        const float* ai = a + (size_t)i * k;
+        for (int j = 0; j < n; j++)
+        {
+            const float* wj = w + (size_t)j * k;
+            float s = 0.f;
+#pragma omp simd reduction(+ : s)
+            for (int t = 0; t < k; t++) s += ai[t] * wj[t];
+            out[(size_t)i * n + j] = s + (bias ? bias[j] : 0.f);
+        }
+    }
+}
+
+static float maybe_bf16(float v, int on)
+{
+    return on ? s2o_round_bf16(v) : v;
+}
+
+/* Block-level RMSNorm (no affine) followed by AdaSingle-style modulation:
+ * y = x * rsqrt(mean(x^2) + eps) * scale + shift, with the shift/scale rows
+ * of each row's sample (mods: [batch][6][D], k0 = index of the shift row). */
+static void ada_norm(const float* x, int rows, int D, float eps, const float* mods, const int* row_sample, int k0,
+                     float* y, int bf16)
+{
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; r++)
+    {
+        const float* xr = x + (size_t)r * D;
+        const float* shift = mods + ((size_t)row_sample[r] * 6 + k0) * D;
+        const float* scale = shift + D;
+        double ss = 0.0;
+        for (int i = 0; i < D; i++) ss += (double)xr[i] * xr[i];
+        const float inv = 1.f / sqrtf((float)(ss / D) + eps);
+        for (int i = 0; i < D; i++) y[(size_t)r * D + i] = maybe_bf16(xr[i] * inv * scale[i] + shift[i], bf16);
+    }
+}
+
+static float gelu_tanh(float x)
+{
+    const float k0 = 0.7978845608028654f; /* sqrt(2/pi) */
+    return 0.5f * x * (1.f + tanhf(k0 * (x + 0.044715f * x * x * x)));
+}
+
+/* One DiT block of the exported graph, restated (the exported .param is not
+ * part of the reference tree, so this sequence is an assumption taken from
+ * the graph's I/O contract -- six shared modulation inputs in4..in9
+ * (src/seedvr2/seedvr2_dit.cpp:730-738), residual streams in0/in1 -- and
+ * the published SeedVR2 block design):
+ *
+ *   mod_k = modulation[k] + ada[k], k = attn shift/scale/gate, mlp shift/scale/gate
+ *   h   = rmsnorm(x) * scale_a + shift_a
+ *   qkv = SharedLinear_qkv(h);  (cv, ct) = AWA(qkv_v, qkv_t)
+ *   x  += SharedLinear_out(c) * gate_a
+ *   h   = rmsnorm(x) * scale_m + shift_m
+ *   x  += SharedLinear_down(gelu_tanh(SharedLinear_up(h))) * gate_m
+ *
+ * dims: D, heads, head_dim, F, rope_pairs, window_mode, window0..2, shifted.
+ * modulation: [batch][6][D].  emulate_bf16 rounds the activations the GPU
+ * path stores in bf16 (h, qkv, attention q/k/v/context, u). */
+int s2o_block_forward(const int* dims, float eps_norm, float eps_qk, const s2o_block_weights* W,
+                      const float* modulation, const int* shapes, const int* text_lengths, int batch, float* xv,
+                      float* xt, int bf16)
+{
+    const int D = dims[0], heads = dims[1], hd = dims[2], F = dims[3], pairs = dims[4], mode = dims[5];
+    const int shifted = dims[9];
+    if (heads * hd != D) return -1;
+    int Nv = 0, Nt = 0;
+    for (int s = 0; s < batch; s++)
+    {
+        Nv += shapes[s * 3] * shapes[s * 3 + 1] * shapes[s * 3 + 2];
+        Nt += text_lengths[s];
+    }
+    const int M = Nv + Nt;
+    float* x = (float*)malloc(sizeof(float) * (size_t)M * D);
+    float* h = (float*)malloc(sizeof(float) * (size_t)M * D);
+    float* qkv = (float*)malloc(sizeof(float) * (size_t)M * 3 * D);
+    float* ctx = (float*)malloc(sizeof(float) * (size_t)M * D);
+    float* o = (float*)malloc(sizeof(float) * (size_t)M * D);
+    float* u = (float*)malloc(sizeof(float) * (size_t)M * F);
+    float* mods = (float*)malloc(sizeof(float) * (size_t)batch * 6 * D);
+    int* row_sample = (int*)malloc(sizeof(int) * (size_t)M);
+    memcpy(x, xv, sizeof(float) * (size_t)Nv * D);
+    memcpy(x + (size_t)Nv * D, xt, sizeof(float) * (size_t)Nt * D);
+    {
+        int r = 0;
+        for (int s = 0; s < batch; s++)
+            for (int i = 0; i < shapes[s * 3] * shapes[s * 3 + 1] * shapes[s * 3 + 2]; i++) row_sample[r++] = s;
+        for (int s = 0; s < batch; s++)
+            for (int i = 0; i < text_lengths[s]; i++) row_sample[r++] = s;
+    }
+    for (int s = 0; s < batch; s++)
+        for (int k = 0; k < 6; k++)
+            for (int i = 0; i < D; i++)
+                mods[((size_t)s * 6 + k) * D + i] = modulation[((size_t)s * 6 + k) * D + i] + W->ada[(size_t)k * D + i];
+
+    int ret = 0;
+    /* attention half */
+    ada_norm(x, M, D, eps_norm, mods, row_sample, 0, h, bf16);
+    s2o_linear(h, M, D, W->w_qkv, W->b_qkv, 3 * D, qkv);
+    if (bf16)
+        for (size_t i = 0; i < (size_t)M * 3 * D; i++) qkv[i] = s2o_round_bf16(qkv[i]);
+    {
+        int ip[9] = {heads, hd, dims[6], dims[7], dims[8], shifted, pairs, mode, bf16};
+        ret = s2o_awa_forward(ip, eps_qk, W->qk_norm, W->freqs, shapes, text_lengths, batch, qkv, qkv + D,
+                              qkv + 2 * D, 3 * D, qkv + (size_t)Nv * 3 * D, qkv + (size_t)Nv * 3 * D + D,
+                              qkv + (size_t)Nv * 3 * D + 2 * D, 3 * D, ctx, ctx + (size_t)Nv * D);
+        if (ret != 0) goto done;
+        if (bf16)
+            for (size_t i = 0; i < (size_t)M * D; i++) ctx[i] = s2o_round_bf16(ctx[i]);
+    }
+    s2o_linear(ctx, M, D, W->w_out, W->b_out, D, o);
+    for (int r = 0; r < M; r++)
+    {
+        const float* g = mods + (size_t)row_sample[r] * 6 * D + 2 * D;
+        for (int i = 0; i < D; i++) x[(size_t)r * D + i] += o[(size_t)r * D + i] * g[i];
+    }
+    /* mlp half */
+    ada_norm(x, M, D, eps_norm, mods, row_sample, 3, h, bf16);
+    s2o_linear(h, M, D, W->w_up, W->b_up, F, u);
+    for (size_t i = 0; i < (size_t)M * F; i++) u[i] = maybe_bf16(gelu_tanh(u[i]), bf16);
+    s2o_linear(u, M, F, W->w_down, W->b_down, D, o);
+    for (int r = 0; r < M; r++)
+    {
+        const float* g = mods + (size_t)row_sample[r] * 6 * D + 5 * D;
+        for (int i = 0; i < D; i++) x[(size_t)r * D + i] += o[(size_t)r * D + i] * g[i];
+    }
+    memcpy(xv, x, sizeof(float) * (size_t)Nv * D);
+    memcpy(xt, x + (size_t)Nv * D, sizeof(float) * (size_t)Nt * D);
+done:
+    free(x);
+    free(h);
+    free(qkv);
+    free(ctx);
+    free(o);
+    free(u);
+    free(mods);
+    free(row_sample);
+    return ret;
+}

@@ -1,0 +1,79 @@
+/* CPU oracle: a plain-C restatement of the SeedVR2 DiT block hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  tests/, __graft_entry__.smoke() and bench.py's
+ * CPU-baseline leg call it as the checker; the shipped library never links
+ * or calls it.  Every function cites the reference code it restates
+ * (paths relative to the reference checkout).
+ *
+ * Parity pin: the restatement is checked bit-for-bit (plan) and to fp32
+ * rounding (AWA, SharedLinear) against the reference's OWN layer sources
+ * compiled into oracle/_ref/libs2_ref.so (see oracle/Makefile), and against
+ * the committed golden fixtures in tests/golden/.
+ */
+#ifndef S2_ORACLE_H
+#define S2_ORACLE_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* window_mode for the plan */
+#define S2O_WINDOW_TARGET 0 /* reference: tuple = target window COUNT */
+#define S2O_WINDOW_EXTENT 1 /* extension: tuple = window extent (t,h,w) */
+
+/* Plan sizes. Returns 0, -1 (bad shape/target). */
+int s2o_plan_sizes(const int* shapes, int batch, int window_mode, const int* window, int shifted,
+                   int* num_windows, int* num_tokens);
+
+/* Fills the plan arrays (capacities from s2o_plan_sizes).
+ * windows: 9 ints per window (sample, t0,t1,h0,h1,w0,w1, partition_offset, token_count).
+ * Returns 0, -1 (bad shape), -2 (inconsistent plan). */
+int s2o_plan_build(const int* shapes, int batch, int window_mode, const int* window, int shifted,
+                   int* windows, int* sample_window_count, int* video_indices, int* inverse_video_indices,
+                   int* local_positions);
+
+float s2o_round_bf16(float v);
+
+/* AdaptiveWindowAttention forward in fp32.
+ * iparams: heads, head_dim, window0..2, shifted, rope_pairs, window_mode, official_bf16_attention
+ * norms: [4][head_dim] video_q, video_k, text_q, text_k;  freqs: [rope_pairs]
+ * vq/vk/vv: row pointers' base + row stride (elements) for video, same for text.
+ * video_out [Nv][inner], text_out [Nt][inner] (fully overwritten). */
+int s2o_awa_forward(const int* iparams, float epsilon, const float* norms, const float* freqs,
+                    const int* shapes, const int* text_lengths, int batch,
+                    const float* vq, const float* vk, const float* vv, int v_ld,
+                    const float* tq, const float* tk, const float* tv, int t_ld,
+                    float* video_out, float* text_out);
+
+/* out[m][n] = sum_k a[m][k] * w[n][k] + bias[n] (bias may be NULL). */
+void s2o_linear(const float* a, int m, int k, const float* w, const float* bias, int n, float* out);
+
+/* Block restatement; see s2_oracle.c for the op sequence.
+ * dims: D (hidden), heads, head_dim, F (mlp), rope_pairs, window_mode, window0..2, shifted
+ * x_video [Nv][D] and x_text [Nt][D] are updated in place (fp32 residual). */
+typedef struct
+{
+    const float* ada;     /* [6][D] per-block modulation offsets */
+    const float* w_qkv;   /* [3D][D] */
+    const float* b_qkv;   /* [3D] or NULL */
+    const float* w_out;   /* [D][D] */
+    const float* b_out;   /* [D] or NULL */
+    const float* w_up;    /* [F][D] */
+    const float* b_up;    /* [F] or NULL */
+    const float* w_down;  /* [D][F] */
+    const float* b_down;  /* [D] or NULL */
+    const float* qk_norm; /* [4][head_dim] */
+    const float* freqs;   /* [rope_pairs] */
+} s2o_block_weights;
+
+int s2o_block_forward(const int* dims, float eps_norm, float eps_qk, const s2o_block_weights* wts,
+                      const float* modulation /* [6][D] */, const int* shapes, const int* text_lengths,
+                      int batch, float* x_video, float* x_text, int emulate_bf16);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,332 @@
+"""ctypes bindings of libseedvr2_cuda (include/seedvr2_cuda.h).
+
+Device buffers are passed as raw pointers; the helpers here accept torch
+tensors for convenience (torch is used only for device memory and streams).
+Every entry point returns the library's integer status; :func:`check` turns a
+non-zero status into :class:`S2Error`.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+from . import LIB_PATH
+
+S2_OK = 0
+S2_ERR_INVALID = -1
+S2_ERR_PLAN = -2
+S2_ERR_CUDA = -3
+S2_ERR_TIMEOUT = -4
+S2_ERR_DEVICE = -5
+S2_ERR_ALLOC = -100
+
+S2_DTYPE_F32 = 0
+S2_DTYPE_BF16 = 1
+
+S2_WINDOW_TARGET = 0
+S2_WINDOW_EXTENT = 1
+
+S2_EPI_STORE = 0
+S2_EPI_GELU_TANH = 1
+S2_EPI_GATE_RESIDUAL = 2
+
+# Every symbol include/seedvr2_cuda.h declares.
+EXPORTED = [
+    "s2_init", "s2_destroy", "s2_set_stream", "s2_status", "s2_error_string", "s2_version", "s2_launch_count",
+    "s2_plan_build", "s2_plan_info", "s2_plan_copy", "s2_plan_free",
+    "s2_awa_forward", "s2_shared_linear", "s2_ada_rmsnorm", "s2_convert_f32_bf16",
+    "s2_dit_create", "s2_dit_free", "s2_dit_set_block_weights", "s2_dit_init_random", "s2_dit_forward",
+    "s2_dit_forward_host",
+]
+
+
+class S2Error(RuntimeError):
+    def __init__(self, code: int, what: str):
+        super().__init__(f"{what} failed: {code} ({error_string(code)})")
+        self.code = code
+
+
+class AwaParams(C.Structure):
+    _fields_ = [
+        ("heads", C.c_int), ("head_dim", C.c_int), ("window", C.c_int * 3), ("window_mode", C.c_int),
+        ("shifted", C.c_int), ("epsilon", C.c_float), ("rope_pairs", C.c_int),
+        ("official_bf16_attention", C.c_int), ("norm_weights", C.c_void_p), ("rope_freqs", C.c_void_p),
+    ]
+
+
+class DitConfig(C.Structure):
+    _fields_ = [
+        ("num_blocks", C.c_int), ("hidden", C.c_int), ("heads", C.c_int), ("head_dim", C.c_int),
+        ("mlp_hidden", C.c_int), ("rope_pairs", C.c_int), ("window", C.c_int * 3), ("window_mode", C.c_int),
+        ("norm_eps", C.c_float), ("qk_eps", C.c_float), ("qkv_bias", C.c_int), ("out_bias", C.c_int),
+        ("mlp_bias", C.c_int),
+    ]
+
+
+class BlockHostWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("ada", "w_qkv", "b_qkv", "w_out", "b_out", "w_up", "b_up", "w_down",
+                                          "b_down", "qk_norm", "rope_freqs")]
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Loads libseedvr2_cuda.so (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python -m seedvr2_ncnn_b200.build` "
+                          "(there is no fallback implementation)")
+    L = C.CDLL(LIB_PATH)
+    vp, ip, i64 = C.c_void_p, C.c_int, C.c_int64
+    pint = C.POINTER(C.c_int)
+    L.s2_init.argtypes = [ip, vp, C.POINTER(vp)]
+    L.s2_destroy.argtypes = [vp]
+    L.s2_destroy.restype = None
+    L.s2_set_stream.argtypes = [vp, vp]
+    L.s2_status.argtypes = [vp]
+    L.s2_error_string.argtypes = [ip]
+    L.s2_error_string.restype = C.c_char_p
+    L.s2_version.argtypes = []
+    L.s2_launch_count.argtypes = [vp]
+    L.s2_launch_count.restype = C.c_uint64
+    L.s2_plan_build.argtypes = [pint, ip, pint, ip, ip, C.POINTER(vp)]
+    L.s2_plan_info.argtypes = [vp, pint, pint, pint]
+    L.s2_plan_copy.argtypes = [vp, pint, pint, pint, pint, pint]
+    L.s2_plan_free.argtypes = [vp]
+    L.s2_plan_free.restype = None
+    L.s2_awa_forward.argtypes = [vp, C.POINTER(AwaParams), vp, pint, pint, ip, ip, vp, vp, vp, i64, vp, vp, vp, i64,
+                                 ip, vp, vp]
+    L.s2_shared_linear.argtypes = [vp, ip, ip, ip, ip, vp, vp, vp, vp, ip, vp, ip, vp, vp]
+    L.s2_ada_rmsnorm.argtypes = [vp, ip, ip, vp, C.c_float, vp, vp, vp]
+    L.s2_convert_f32_bf16.argtypes = [vp, vp, vp, i64]
+    L.s2_dit_create.argtypes = [vp, C.POINTER(DitConfig), C.POINTER(vp)]
+    L.s2_dit_free.argtypes = [vp]
+    L.s2_dit_free.restype = None
+    L.s2_dit_set_block_weights.argtypes = [vp, ip, C.POINTER(BlockHostWeights)]
+    L.s2_dit_init_random.argtypes = [vp, C.c_uint64]
+    L.s2_dit_forward.argtypes = [vp, pint, ip, vp, vp]
+    L.s2_dit_forward_host.argtypes = [vp, pint, pint, ip, vp, vp, vp, vp, vp]
+    _lib = L
+    return L
+
+
+def error_string(code: int) -> str:
+    try:
+        return lib().s2_error_string(code).decode()
+    except ImportError:
+        return "library not loaded"
+
+
+def check(code: int, what: str) -> None:
+    if code != S2_OK:
+        raise S2Error(code, what)
+
+
+def _ints(values) -> C.Array:
+    values = [int(v) for v in values]
+    return (C.c_int * len(values))(*values)
+
+
+def ptr(t) -> int | None:
+    """Device (or host) address of a torch tensor / numpy array, or None."""
+    if t is None:
+        return None
+    if hasattr(t, "data_ptr"):
+        return t.data_ptr()
+    return t.ctypes.data
+
+
+class Context:
+    """An s2_context on one device and stream (torch's current stream by default)."""
+
+    def __init__(self, device: int = 0, stream=None):
+        import torch
+
+        self.device = device
+        if stream is None:
+            stream = torch.cuda.current_stream(device)
+        self.stream = stream
+        h = C.c_void_p()
+        check(lib().s2_init(device, C.c_void_p(stream.cuda_stream), C.byref(h)), "s2_init")
+        self.handle = h
+
+    def close(self):
+        if self.handle:
+            lib().s2_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def status(self) -> int:
+        return lib().s2_status(self.handle)
+
+    def launches(self) -> int:
+        return int(lib().s2_launch_count(self.handle))
+
+
+class Plan:
+    """A window plan (s2_plan) -- AdaptiveWindowPlan of the reference."""
+
+    def __init__(self, shapes, window, window_mode=S2_WINDOW_TARGET, shifted=False):
+        flat = [int(v) for s in shapes for v in s]
+        self.batch = len(flat) // 3
+        h = C.c_void_p()
+        check(lib().s2_plan_build(_ints(flat), self.batch, _ints(window), window_mode, int(bool(shifted)),
+                                  C.byref(h)), "s2_plan_build")
+        self.handle = h
+
+    def __del__(self):
+        try:
+            if self.handle:
+                lib().s2_plan_free(self.handle)
+                self.handle = None
+        except Exception:
+            pass
+
+    def arrays(self) -> dict:
+        import numpy as np
+
+        nw, nt, mx = C.c_int(), C.c_int(), C.c_int()
+        check(lib().s2_plan_info(self.handle, C.byref(nw), C.byref(nt), C.byref(mx)), "s2_plan_info")
+        windows = np.zeros((nw.value, 9), np.int32)
+        swc = np.zeros(self.batch, np.int32)
+        vi = np.zeros(nt.value, np.int32)
+        inv = np.zeros(nt.value, np.int32)
+        pos = np.zeros((nt.value, 3), np.int32)
+        P = lambda a: a.ctypes.data_as(C.POINTER(C.c_int))  # noqa: E731
+        check(lib().s2_plan_copy(self.handle, P(windows), P(swc), P(vi), P(inv), P(pos)), "s2_plan_copy")
+        return {"windows": windows, "sample_window_count": swc, "video_indices": vi,
+                "inverse_video_indices": inv, "local_positions": pos, "max_window_tokens": mx.value}
+
+
+def awa_forward(ctx: Context, *, heads, head_dim, window, window_mode, shifted, eps, rope_pairs, norms, freqs,
+                shapes, text_lengths, video_qkv=None, text_qkv=None, split=None, out_dtype=S2_DTYPE_F32,
+                official_bf16=False, video_out=None, text_out=None, plan: Plan | None = None):
+    """AdaptiveWindowAttention forward on torch CUDA tensors (fp32 or bf16)."""
+    import torch
+
+    inner = heads * head_dim
+    nv = sum(int(s[0]) * int(s[1]) * int(s[2]) for s in shapes)
+    nt = sum(int(t) for t in text_lengths)
+    if split is None:
+        vq, tq = video_qkv, text_qkv
+        esz = vq.element_size()
+        ptrs = [vq.data_ptr(), vq.data_ptr() + inner * esz, vq.data_ptr() + 2 * inner * esz,
+                tq.data_ptr(), tq.data_ptr() + inner * esz, tq.data_ptr() + 2 * inner * esz]
+        vld, tld = vq.stride(0), tq.stride(0)
+        dt = vq.dtype
+    else:
+        ptrs = [t.data_ptr() for t in split]
+        vld, tld = split[0].stride(0), split[3].stride(0)
+        dt = split[0].dtype
+    in_dtype = S2_DTYPE_BF16 if dt == torch.bfloat16 else S2_DTYPE_F32
+    tdt = torch.float32 if out_dtype == S2_DTYPE_F32 else torch.bfloat16
+    dev = torch.device("cuda", ctx.device)
+    if video_out is None:
+        video_out = torch.empty((nv, inner), dtype=tdt, device=dev)
+    if text_out is None:
+        text_out = torch.empty((nt, inner), dtype=tdt, device=dev)
+    p = AwaParams()
+    p.heads, p.head_dim = heads, head_dim
+    p.window[:] = [int(w) for w in window]
+    p.window_mode, p.shifted, p.epsilon, p.rope_pairs = window_mode, int(bool(shifted)), float(eps), rope_pairs
+    p.official_bf16_attention = int(bool(official_bf16))
+    p.norm_weights, p.rope_freqs = norms.data_ptr(), freqs.data_ptr()
+    flat = [int(v) for s in shapes for v in s]
+    r = lib().s2_awa_forward(ctx.handle, C.byref(p), plan.handle if plan is not None else None, _ints(flat),
+                             _ints(text_lengths), len(shapes), in_dtype, ptrs[0], ptrs[1], ptrs[2], vld, ptrs[3],
+                             ptrs[4], ptrs[5], tld, out_dtype, video_out.data_ptr(), text_out.data_ptr())
+    check(r, "s2_awa_forward")
+    return video_out, text_out
+
+
+def shared_linear(ctx: Context, a0, weight, bias=None, *, a1=None, epilogue=S2_EPI_STORE, gate=None,
+                  out_dtype=S2_DTYPE_BF16, out0=None, out1=None):
+    """out_s = a_s @ weight.T + bias (+ epilogue); a_s, weight bf16 CUDA tensors."""
+    import torch
+
+    M0, K = a0.shape
+    M1 = a1.shape[0] if a1 is not None else 0
+    N = weight.shape[0]
+    tdt = torch.float32 if out_dtype == S2_DTYPE_F32 else torch.bfloat16
+    if out0 is None:
+        out0 = torch.empty((M0, N), dtype=tdt, device=a0.device)
+    if a1 is not None and out1 is None:
+        out1 = torch.empty((M1, N), dtype=tdt, device=a0.device)
+    r = lib().s2_shared_linear(ctx.handle, M0, M1, N, K, a0.data_ptr(), ptr(a1), weight.data_ptr(), ptr(bias),
+                               epilogue, ptr(gate), out_dtype, out0.data_ptr(), ptr(out1))
+    check(r, "s2_shared_linear")
+    return out0, out1
+
+
+def ada_rmsnorm(ctx: Context, x, eps, shift, scale, out=None):
+    import torch
+
+    rows, D = x.shape
+    if out is None:
+        out = torch.empty((rows, D), dtype=torch.bfloat16, device=x.device)
+    check(lib().s2_ada_rmsnorm(ctx.handle, rows, D, x.data_ptr(), float(eps), shift.data_ptr(), scale.data_ptr(),
+                               out.data_ptr()), "s2_ada_rmsnorm")
+    return out
+
+
+class Dit:
+    """s2_dit: the block stack (SeedVR2DiTBlocks' block graph)."""
+
+    def __init__(self, ctx: Context, *, num_blocks=32, hidden=2560, heads=20, head_dim=128, mlp_hidden=10240,
+                 rope_pairs=21, window=(4, 3, 3), window_mode=S2_WINDOW_TARGET, norm_eps=1e-5, qk_eps=1e-5,
+                 bias=True):
+        cfg = DitConfig()
+        cfg.num_blocks, cfg.hidden, cfg.heads, cfg.head_dim = num_blocks, hidden, heads, head_dim
+        cfg.mlp_hidden, cfg.rope_pairs = mlp_hidden, rope_pairs
+        cfg.window[:] = [int(w) for w in window]
+        cfg.window_mode, cfg.norm_eps, cfg.qk_eps = window_mode, norm_eps, qk_eps
+        cfg.qkv_bias = cfg.out_bias = cfg.mlp_bias = int(bool(bias))
+        self.cfg = cfg
+        self.ctx = ctx
+        h = C.c_void_p()
+        check(lib().s2_dit_create(ctx.handle, C.byref(cfg), C.byref(h)), "s2_dit_create")
+        self.handle = h
+
+    def close(self):
+        if self.handle:
+            lib().s2_dit_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def init_random(self, seed: int):
+        check(lib().s2_dit_init_random(self.handle, seed), "s2_dit_init_random")
+
+    def set_block_weights(self, block: int, w: dict):
+        """w: dict of contiguous fp32 numpy arrays (keys of BlockHostWeights; biases may be None)."""
+        import numpy as np
+
+        keep = {k: (np.ascontiguousarray(v, dtype=np.float32) if v is not None else None) for k, v in w.items()}
+        hw = BlockHostWeights(*[(keep[n].ctypes.data if keep.get(n) is not None else None)
+                                for n, _ in BlockHostWeights._fields_])
+        check(lib().s2_dit_set_block_weights(self.handle, block, C.byref(hw)), "s2_dit_set_block_weights")
+
+    def forward(self, video_shape, text_length, x, modulation):
+        """x: fp32 CUDA [Nv+Nt, D] (updated in place); modulation fp32 CUDA [6, D]."""
+        check(lib().s2_dit_forward(self.handle, _ints(video_shape), int(text_length), x.data_ptr(),
+                                   modulation.data_ptr()), "s2_dit_forward")
+        return x
+
+    def forward_host(self, video_shapes, text_lengths, video, text, modulation, video_out, text_out):
+        """Host buffers (numpy or pinned torch CPU tensors, fp32)."""
+        flat = [int(v) for s in video_shapes for v in s]
+        check(lib().s2_dit_forward_host(self.handle, _ints(flat), _ints(text_lengths), len(video_shapes),
+                                        ptr(video), ptr(text), ptr(modulation), ptr(video_out), ptr(text_out)),
+              "s2_dit_forward_host")

@@ -1,0 +1,81 @@
+"""Builds libseedvr2_cuda.so in-tree for sm_100a with nvcc.
+
+    python -m seedvr2_ncnn_b200.build          # or: python seedvr2_ncnn_b200/build.py
+
+Objects go to seedvr2_ncnn_b200/_build/, the library to
+seedvr2_ncnn_b200/libseedvr2_cuda.so (next to this file, so it travels with
+the source tree).  The CUDA runtime is linked statically; the driver entry
+point for TMA descriptors is resolved at run time.
+"""
+from __future__ import annotations
+
+import concurrent.futures as cf
+import hashlib
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+BUILD = os.path.join(HERE, "_build")
+LIB = os.path.join(HERE, "libseedvr2_cuda.so")
+ROOT = os.path.dirname(HERE)
+
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I" + os.path.join(ROOT, "include"),
+          "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills", "-Wno-deprecated-gpu-targets"]
+
+SOURCES = ["s2_api.cu", "dit.cu", "gemm_sm100.cu", "attention_sm100.cu", "elementwise.cu", "plan.cpp"]
+
+
+def _headers_digest() -> str:
+    h = hashlib.sha256()
+    for d in (CSRC, os.path.join(ROOT, "include")):
+        for f in sorted(os.listdir(d)):
+            if f.endswith((".h", ".cuh")):
+                with open(os.path.join(d, f), "rb") as fh:
+                    h.update(fh.read())
+    return h.hexdigest()[:16]
+
+
+def _compile(src: str, extra: list[str], hdr: str) -> str:
+    obj = os.path.join(BUILD, os.path.splitext(src)[0] + ".o")
+    stamp = obj + ".hdr"
+    path = os.path.join(CSRC, src)
+    fresh = (os.path.exists(obj) and os.path.getmtime(obj) >= os.path.getmtime(path) and os.path.exists(stamp)
+             and open(stamp).read() == hdr + " ".join(extra))
+    if fresh:
+        return obj
+    cmd = [NVCC] + ARCH + COMMON + extra + ["-c", path, "-o", obj]
+    if src.endswith(".cpp"):
+        cmd = [NVCC] + COMMON + extra + ["-x", "c++", "-c", path, "-o", obj]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {src}:\n{r.stdout}\n{r.stderr}")
+    if r.stderr.strip():
+        sys.stderr.write(r.stderr)
+    with open(stamp, "w") as fh:
+        fh.write(hdr + " ".join(extra))
+    return obj
+
+
+def build(verbose: bool = False, extra: list[str] | None = None) -> str:
+    extra = list(extra or [])
+    os.makedirs(BUILD, exist_ok=True)
+    hdr = _headers_digest()
+    with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 2)) as ex:
+        objs = list(ex.map(lambda s: _compile(s, extra, hdr), SOURCES))
+    if not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
+        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-cudart", "static", "-lcuda" if False else ""]
+        cmd = [c for c in cmd if c]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    if verbose:
+        print(LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    build(verbose=True, extra=sys.argv[1:])

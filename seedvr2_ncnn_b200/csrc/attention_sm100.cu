@@ -1,0 +1,425 @@
+// Varlen window attention on sm_100a (tcgen05 + TMEM + TMA).
+//
+// Replaces the per-window ncnn SDPA call and the scatter shader of
+// AdaptiveWindowAttention::forward (adaptive_window_attention.cpp:873-975 CPU,
+// :1172-1268 Vulkan, scatter shader :353-409).  Each window's sequence is its
+// L video rows followed by the sample's T text rows, packed contiguously
+// (window after window) in bf16 [rows][heads*128] by the prepare kernel.
+//
+// One CTA = (window q-tile of 128 rows, head).  Warp roles:
+//   warp 0     TMA: Q tile once, then K/V tiles into a 2-stage ring;
+//   warp 1     one thread issues tcgen05.mma: S = Q K^T (M=N=128, K=128) into
+//              one of two TMEM S buffers, O_j = P_j V_j into a TMEM O buffer;
+//   warps 2-5  softmax: one query row per thread (TMEM lane), fp32 online
+//              softmax with exp2, P written to shared memory in the 128-byte
+//              swizzled K-major layout the PV MMA reads, O accumulated in
+//              registers, then the epilogue: video rows stored straight to
+//              their source token (the scatter), text rows to a per-window
+//              fp32 partial that text_pool averages over the sample's windows.
+// Keys past the window's sequence length are masked; query rows past it are
+// computed but never stored.
+#include "s2_common.cuh"
+#include "s2_internal.h"
+
+namespace s2 {
+
+namespace {
+
+constexpr int HD = 128;           // head_dim
+constexpr int TILE = 128;         // q rows / keys per tile
+constexpr int CHUNK_BYTES = TILE * 128; // 128 rows x 64 bf16 (one swizzle row each)
+constexpr int TILE_BYTES = 2 * CHUNK_BYTES; // 128 x 128 bf16
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 512; // S0 [0,128) S1 [128,256) O [256,384)
+constexpr uint32_t IDESC_S = umma_idesc_bf16(128, 128, 0, 0);
+constexpr uint32_t IDESC_O = umma_idesc_bf16(128, 128, 0, 1); // B (= V) MN-major
+constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;      // Q, K x2, V x2, P
+
+struct AttnArgs
+{
+    const int4* win_info; // {seq_offset, L, T, partition_offset}
+    const int* win_pool;  // partial row of the window's first text row
+    const int2* items;    // {window, q0}
+    const int* video_indices;
+    int inner;
+    float scale_log2;
+    int out_f32;
+    int round_bf16;
+    void* video_out;
+    float* text_partial;
+    int* status;
+};
+
+__device__ __forceinline__ float ex2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float bf16_round_f32(float x)
+{
+    return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status)
+{
+    int ok = 0;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort, status) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    return ok != 0;
+}
+
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity)
+{
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (global_timer_ns() - t0 > kWaitLimitNs) break;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    window_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                            const __grid_constant__ CUtensorMap tv, const AttnArgs args)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = sQ + TILE_BYTES;     // 2 stages
+    uint8_t* sV = sK + 2 * TILE_BYTES; // 2 stages
+    uint8_t* sP = sV + 2 * TILE_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + TILE_BYTES);
+    uint64_t* q_full = bars + 0;
+    uint64_t* k_full = bars + 1;  // [2]
+    uint64_t* v_full = bars + 3;  // [2]
+    uint64_t* kv_empty = bars + 5; // [2]
+    uint64_t* s_full = bars + 7;  // [2]
+    uint64_t* p_full = bars + 9;
+    uint64_t* o_full = bars + 10;
+    uint64_t* drain = bars + 11;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int head = blockIdx.y;
+    const int2 item = args.items[blockIdx.x];
+    const int4 wi = args.win_info[item.x];
+    const int seq_off = wi.x, L = wi.y, T = wi.z, part_off = wi.w;
+    const int S_len = L + T;
+    const int q0 = item.y;
+    const int nkv = (S_len + TILE - 1) / TILE;
+
+    if (threadIdx.x == 0)
+    {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < 2; s++)
+        {
+            mbar_init(&k_full[s], 1);
+            mbar_init(&v_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+            mbar_init(&s_full[s], 1);
+        }
+        mbar_init(p_full, 128);
+        mbar_init(o_full, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0)
+    {
+        if (lane == 0)
+        {
+            const int x0 = head * HD;
+            bool issued_q = false;
+            int issued_stage[2] = {0, 0};
+            uint32_t last_parity[2] = {0, 0};
+            mbar_arrive_expect_tx(q_full, TILE_BYTES);
+            tma_load_2d(sQ, &tq, q_full, x0, seq_off + q0);
+            tma_load_2d(sQ + CHUNK_BYTES, &tq, q_full, x0 + 64, seq_off + q0);
+            issued_q = true;
+            for (int j = 0; j < nkv; j++)
+            {
+                const int st = j & 1;
+                const uint32_t par = (j >> 1) & 1;
+                if (!mbar_wait(&kv_empty[st], par ^ 1, abort_flag, args.status)) break;
+                const int y = seq_off + j * TILE;
+                mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+                tma_load_2d(sK + st * TILE_BYTES, &tk, &k_full[st], x0, y);
+                tma_load_2d(sK + st * TILE_BYTES + CHUNK_BYTES, &tk, &k_full[st], x0 + 64, y);
+                mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
+                tma_load_2d(sV + st * TILE_BYTES, &tv, &v_full[st], x0, y);
+                tma_load_2d(sV + st * TILE_BYTES + CHUNK_BYTES, &tv, &v_full[st], x0 + 64, y);
+                issued_stage[st] = 1;
+                last_parity[st] = par;
+            }
+            if (*abort_flag)
+            {
+                if (issued_q) drain_wait(q_full, 0);
+                for (int s = 0; s < 2; s++)
+                    if (issued_stage[s])
+                    {
+                        drain_wait(&k_full[s], last_parity[s]);
+                        drain_wait(&v_full[s], last_parity[s]);
+                    }
+            }
+        }
+    }
+    else if (warp == 1)
+    {
+        if (lane == 0)
+        {
+            bool any = false;
+            const uint32_t q_addr = smem_u32(sQ);
+            const uint32_t p_addr = smem_u32(sP);
+            auto issue_s = [&](int j) {
+                const int st = j & 1;
+                const uint32_t k_addr = smem_u32(sK + st * TILE_BYTES);
+                const uint32_t d = tmem + st * 128;
+#pragma unroll
+                for (int k = 0; k < HD / 16; k++)
+                {
+                    const uint32_t off = (k >> 2) * CHUNK_BYTES + (k & 3) * 32;
+                    umma_bf16(d, umma_desc_sw128(q_addr + off, 16, 1024), umma_desc_sw128(k_addr + off, 16, 1024),
+                              IDESC_S, k != 0);
+                }
+                umma_commit(&s_full[st]);
+            };
+            do
+            {
+                if (!mbar_wait(q_full, 0, abort_flag, args.status)) break;
+                if (!mbar_wait(&k_full[0], 0, abort_flag, args.status)) break;
+                tc_fence_after();
+                issue_s(0);
+                any = true;
+                for (int j = 0; j < nkv; j++)
+                {
+                    const int st = j & 1;
+                    const uint32_t par = (j >> 1) & 1;
+                    if (j + 1 < nkv)
+                    {
+                        if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, args.status)) break;
+                        tc_fence_after();
+                        issue_s(j + 1);
+                    }
+                    if (!mbar_wait(p_full, j & 1, abort_flag, args.status)) break;
+                    if (!mbar_wait(&v_full[st], par, abort_flag, args.status)) break;
+                    tc_fence_after();
+                    const uint32_t v_addr = smem_u32(sV + st * TILE_BYTES);
+#pragma unroll
+                    for (int k = 0; k < TILE / 16; k++)
+                    {
+                        const uint32_t a_off = (k >> 2) * CHUNK_BYTES + (k & 3) * 32;
+                        const uint32_t b_off = k * 16 * 128;
+                        umma_bf16(tmem + 256, umma_desc_sw128(p_addr + a_off, 16, 1024),
+                                  umma_desc_sw128(v_addr + b_off, CHUNK_BYTES, 1024), IDESC_O, k != 0);
+                    }
+                    umma_commit(o_full);
+                    umma_commit(&kv_empty[st]);
+                }
+            } while (0);
+            if (any)
+            {
+                umma_commit(drain);
+                drain_wait(drain, 0);
+            }
+        }
+    }
+    else
+    {
+        // softmax + epilogue warps
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+        float o_acc[HD];
+#pragma unroll
+        for (int i = 0; i < HD; i++) o_acc[i] = 0.f;
+        float m_run = -INFINITY;
+        float l_run = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nkv && ok; j++)
+        {
+            const int st = j & 1;
+            if (!warp_wait(&s_full[st], (j >> 1) & 1, abort_flag, args.status))
+            {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int valid = S_len - j * TILE; // >= 1
+            const uint32_t s_addr = tmem + lane_base + st * 128;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+            {
+                uint32_t v[32];
+                tmem_ld32(s_addr + c * 32, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    if (c * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(v[i]));
+            }
+            const float m_new = fmaxf(m_run, mx * args.scale_log2);
+            const float alpha = ex2(m_run - m_new); // m_run = -inf on the first tile -> 0
+            float rowsum = 0.f;
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+            {
+                uint32_t v[32];
+                tmem_ld32(s_addr + c * 32, v);
+                tmem_ld_wait();
+                uint32_t packed[16];
+#pragma unroll
+                for (int i = 0; i < 32; i += 2)
+                {
+                    const float p0 = (c * 32 + i < valid) ? ex2(__uint_as_float(v[i]) * args.scale_log2 - m_new) : 0.f;
+                    const float p1 =
+                        (c * 32 + i + 1 < valid) ? ex2(__uint_as_float(v[i + 1]) * args.scale_log2 - m_new) : 0.f;
+                    rowsum += p0 + p1;
+                    packed[i >> 1] = pack_bf16x2(p0, p1);
+                }
+                // columns c*32 .. c*32+31 = chunk c/2, 16-byte units (c%2)*4 .. +3
+                uint8_t* prow = sP + (c >> 1) * CHUNK_BYTES + row * 128;
+#pragma unroll
+                for (int u = 0; u < 4; u++)
+                {
+                    const int unit = (c & 1) * 4 + u;
+                    *reinterpret_cast<uint4*>(prow + ((unit ^ (row & 7)) << 4)) =
+                        make_uint4(packed[u * 4], packed[u * 4 + 1], packed[u * 4 + 2], packed[u * 4 + 3]);
+                }
+            }
+            l_run = l_run * alpha + rowsum;
+            m_run = m_new;
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(p_full);
+            if (!warp_wait(o_full, j & 1, abort_flag, args.status))
+            {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+            {
+                uint32_t v[32];
+                tmem_ld32(tmem + lane_base + 256 + c * 32, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; i++) o_acc[c * 32 + i] = o_acc[c * 32 + i] * alpha + __uint_as_float(v[i]);
+            }
+            tc_fence_before();
+        }
+        const int qi = q0 + row;
+        if (ok && qi < S_len)
+        {
+            const float inv = 1.f / l_run;
+            if (qi < L)
+            {
+                const int src = args.video_indices[part_off + qi];
+                const size_t base = (size_t)src * args.inner + head * HD;
+                if (args.out_f32)
+                {
+                    float* o = reinterpret_cast<float*>(args.video_out) + base;
+#pragma unroll
+                    for (int i = 0; i < HD; i += 4)
+                    {
+                        float4 w = make_float4(o_acc[i] * inv, o_acc[i + 1] * inv, o_acc[i + 2] * inv,
+                                               o_acc[i + 3] * inv);
+                        if (args.round_bf16)
+                        {
+                            w.x = bf16_round_f32(w.x);
+                            w.y = bf16_round_f32(w.y);
+                            w.z = bf16_round_f32(w.z);
+                            w.w = bf16_round_f32(w.w);
+                        }
+                        *reinterpret_cast<float4*>(o + i) = w;
+                    }
+                }
+                else
+                {
+                    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(args.video_out) + base;
+#pragma unroll
+                    for (int i = 0; i < HD; i += 8)
+                    {
+                        uint4 p;
+                        p.x = pack_bf16x2(o_acc[i] * inv, o_acc[i + 1] * inv);
+                        p.y = pack_bf16x2(o_acc[i + 2] * inv, o_acc[i + 3] * inv);
+                        p.z = pack_bf16x2(o_acc[i + 4] * inv, o_acc[i + 5] * inv);
+                        p.w = pack_bf16x2(o_acc[i + 6] * inv, o_acc[i + 7] * inv);
+                        *reinterpret_cast<uint4*>(o + i) = p;
+                    }
+                }
+            }
+            else
+            {
+                float* o = args.text_partial + (size_t)(args.win_pool[item.x] + (qi - L)) * args.inner + head * HD;
+#pragma unroll
+                for (int i = 0; i < HD; i += 4)
+                {
+                    float4 w = make_float4(o_acc[i] * inv, o_acc[i + 1] * inv, o_acc[i + 2] * inv,
+                                           o_acc[i + 3] * inv);
+                    if (args.round_bf16)
+                    {
+                        w.x = bf16_round_f32(w.x);
+                        w.y = bf16_round_f32(w.y);
+                        w.z = bf16_round_f32(w.z);
+                        w.w = bf16_round_f32(w.w);
+                    }
+                    *reinterpret_cast<float4*>(o + i) = w;
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+} // namespace
+
+int launch_window_attention(Context& ctx, const AttnSchedule& s, int heads, const void* q, const void* k,
+                            const void* v, int out_f32, int round_bf16, void* video_out, float* text_partial)
+{
+    if (s.num_items <= 0) return S2_OK;
+    const int inner = heads * HD;
+    CUtensorMap mq, mk, mv;
+    int r = make_tmap_bf16_2d(&mq, q, inner, s.packed_rows, (uint64_t)inner * 2, 64, TILE);
+    if (r == 0) r = make_tmap_bf16_2d(&mk, k, inner, s.packed_rows, (uint64_t)inner * 2, 64, TILE);
+    if (r == 0) r = make_tmap_bf16_2d(&mv, v, inner, s.packed_rows, (uint64_t)inner * 2, 64, TILE);
+    if (r != 0) return r;
+    AttnArgs a;
+    a.win_info = s.win_info;
+    a.win_pool = s.win_pool;
+    a.items = s.items;
+    a.video_indices = s.video_indices;
+    a.inner = inner;
+    a.scale_log2 = 1.4426950408889634f / sqrtf((float)HD);
+    a.out_f32 = out_f32;
+    a.round_bf16 = round_bf16;
+    a.video_out = video_out;
+    a.text_partial = text_partial;
+    a.status = ctx.status;
+    static bool configured = false;
+    if (!configured)
+    {
+        if (cudaFuncSetAttribute(window_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+            cudaSuccess)
+            return S2_ERR_CUDA;
+        configured = true;
+    }
+    dim3 grid(s.num_items, heads);
+    window_attention_kernel<<<grid, NUM_THREADS, SMEM_BYTES, ctx.stream>>>(mq, mk, mv, a);
+    ctx.launches++;
+    return cudaGetLastError() == cudaSuccess ? S2_OK : S2_ERR_CUDA;
+}
+
+} // namespace s2

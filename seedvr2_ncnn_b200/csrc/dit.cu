@@ -1,0 +1,326 @@
+// DiT block stack: the 32 fused blocks of blocks/seedvr2_blocks.ncnn run as
+// a fixed sequence of this library's kernels (replaces the ncnn block graph
+// that SeedVR2DiTBlocks::load registers the custom layers into and
+// record_blocks walks, seedvr2_dit.cpp:531-634, :636-1094).
+//
+// Per block (the exported graph is not part of the reference tree; this op
+// sequence is the assumption the CPU oracle restates in s2o_block_forward):
+//   h   = rmsnorm(x) * (mod[1] + ada[1]) + (mod[0] + ada[0])          bf16
+//   qkv = SharedLinear_qkv(h)                                        bf16
+//   ctx = AdaptiveWindowAttention(qkv)   (odd blocks: shifted windows) bf16
+//   x  += SharedLinear_out(ctx) * (mod[2] + ada[2])                  fp32
+//   h   = rmsnorm(x) * (mod[4] + ada[4]) + (mod[3] + ada[3])          bf16
+//   u   = gelu_tanh(SharedLinear_up(h))                              bf16
+//   x  += SharedLinear_down(u) * (mod[5] + ada[5])                   fp32
+// x holds the video rows then the text rows of one sample, so every
+// token-wise op is a single launch over both streams.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <vector>
+
+#include "s2_common.cuh"
+#include "s2_internal.h"
+#include "s2_objects.h"
+
+struct s2_dit
+{
+    s2_context* ctx = nullptr;
+    s2_dit_config cfg;
+    struct Block
+    {
+        __nv_bfloat16 *w_qkv, *w_out, *w_up, *w_down;
+        float *b_qkv, *b_out, *b_up, *b_down;
+        float* qk_norm;
+        float* freqs;
+    };
+    std::vector<Block> blocks;
+    float* ada_all = nullptr; // [blocks][6][D]
+    void* weights = nullptr;  // one allocation for all weights
+    size_t weight_bytes = 0;
+    // per-shape plans (unshifted, shifted)
+    std::map<std::vector<int>, std::unique_ptr<s2_plan>> plans;
+    s2::DeviceBuffer act; // activations of one forward
+    s2::DeviceBuffer mods; // [blocks][6][D]
+    s2::DeviceBuffer host_x; // staging for s2_dit_forward_host
+};
+
+namespace {
+
+size_t align256(size_t b)
+{
+    return (b + 255) & ~size_t(255);
+}
+
+int get_plan(s2_dit* d, const int* shape, int shifted, s2_plan** out)
+{
+    std::vector<int> key(shape, shape + 3);
+    key.push_back(shifted);
+    std::unique_ptr<s2_plan>& slot = d->plans[key];
+    if (!slot)
+    {
+        std::unique_ptr<s2_plan> p(new s2_plan);
+        const int r = s2::build_plan(shape, 1, d->cfg.window, d->cfg.window_mode, shifted, p->plan);
+        if (r != S2_OK)
+        {
+            d->plans.erase(key);
+            return r;
+        }
+        slot = std::move(p);
+    }
+    *out = slot.get();
+    return S2_OK;
+}
+
+} // namespace
+
+extern "C" {
+
+int s2_dit_create(s2_context* ctx, const s2_dit_config* cfg, s2_dit** out)
+{
+    if (!ctx || !cfg || !out) return S2_ERR_INVALID;
+    *out = nullptr;
+    const int D = cfg->hidden, F = cfg->mlp_hidden;
+    if (cfg->num_blocks <= 0 || cfg->head_dim != 128 || cfg->heads * cfg->head_dim != D || F <= 0 || F % 64 ||
+        cfg->rope_pairs <= 0 || cfg->rope_pairs * 6 > cfg->head_dim)
+        return S2_ERR_INVALID;
+    if (cudaSetDevice(ctx->c.device) != cudaSuccess) return S2_ERR_CUDA;
+    std::unique_ptr<s2_dit> d(new s2_dit);
+    d->ctx = ctx;
+    d->cfg = *cfg;
+    const size_t w_elems = (size_t)3 * D * D + (size_t)D * D + (size_t)2 * F * D;
+    const size_t per_block = align256(w_elems * 2) + align256((size_t)(3 * D + D + F + D) * 4) +
+                             align256((size_t)4 * cfg->head_dim * 4) + align256((size_t)cfg->rope_pairs * 4);
+    d->weight_bytes = per_block * cfg->num_blocks + align256((size_t)cfg->num_blocks * 6 * D * 4);
+    if (cudaMalloc(&d->weights, d->weight_bytes) != cudaSuccess) return S2_ERR_ALLOC;
+    if (cudaMemset(d->weights, 0, d->weight_bytes) != cudaSuccess) return S2_ERR_CUDA;
+    uint8_t* p = static_cast<uint8_t*>(d->weights);
+    d->blocks.resize(cfg->num_blocks);
+    for (int b = 0; b < cfg->num_blocks; b++)
+    {
+        s2_dit::Block& bl = d->blocks[b];
+        uint8_t* q = p + per_block * b;
+        bl.w_qkv = reinterpret_cast<__nv_bfloat16*>(q);
+        bl.w_out = bl.w_qkv + (size_t)3 * D * D;
+        bl.w_up = bl.w_out + (size_t)D * D;
+        bl.w_down = bl.w_up + (size_t)F * D;
+        q += align256(w_elems * 2);
+        bl.b_qkv = reinterpret_cast<float*>(q);
+        bl.b_out = bl.b_qkv + 3 * D;
+        bl.b_up = bl.b_out + D;
+        bl.b_down = bl.b_up + F;
+        q += align256((size_t)(3 * D + D + F + D) * 4);
+        bl.qk_norm = reinterpret_cast<float*>(q);
+        q += align256((size_t)4 * cfg->head_dim * 4);
+        bl.freqs = reinterpret_cast<float*>(q);
+    }
+    d->ada_all = reinterpret_cast<float*>(p + per_block * cfg->num_blocks);
+    *out = d.release();
+    return S2_OK;
+}
+
+void s2_dit_free(s2_dit* d)
+{
+    if (!d) return;
+    cudaSetDevice(d->ctx->c.device);
+    cudaStreamSynchronize(d->ctx->c.stream);
+    d->plans.clear();
+    if (d->weights) cudaFree(d->weights);
+    delete d;
+}
+
+int s2_dit_set_block_weights(s2_dit* d, int block, const s2_block_host_weights* w)
+{
+    if (!d || !w || block < 0 || block >= d->cfg.num_blocks || !w->ada || !w->w_qkv || !w->w_out || !w->w_up ||
+        !w->w_down || !w->qk_norm || !w->rope_freqs)
+        return S2_ERR_INVALID;
+    s2::Context& c = d->ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    const int D = d->cfg.hidden, F = d->cfg.mlp_hidden;
+    const s2_dit::Block& bl = d->blocks[block];
+    // Upload fp32, convert to bf16 on the device (ncnn use_bf16_storage analogue).
+    s2::DeviceBuffer tmp;
+    const size_t biggest = (size_t)F * D;
+    if (tmp.ensure(biggest * 4) != S2_OK) return S2_ERR_ALLOC;
+    auto up_bf16 = [&](const float* src, __nv_bfloat16* dst, size_t n) -> int {
+        if (cudaMemcpyAsync(tmp.ptr, src, n * 4, cudaMemcpyHostToDevice, c.stream) != cudaSuccess) return S2_ERR_CUDA;
+        return s2::launch_convert_f32_bf16(c, static_cast<float*>(tmp.ptr), dst, (int64_t)n);
+    };
+    auto up_f32 = [&](const float* src, float* dst, size_t n) -> int {
+        if (!src) return cudaMemsetAsync(dst, 0, n * 4, c.stream) == cudaSuccess ? S2_OK : S2_ERR_CUDA;
+        return cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyHostToDevice, c.stream) == cudaSuccess ? S2_OK
+                                                                                                 : S2_ERR_CUDA;
+    };
+    int r = S2_OK;
+    if (r == S2_OK) r = up_bf16(w->w_qkv, bl.w_qkv, (size_t)3 * D * D);
+    if (r == S2_OK) r = up_bf16(w->w_out, bl.w_out, (size_t)D * D);
+    if (r == S2_OK) r = up_bf16(w->w_up, bl.w_up, (size_t)F * D);
+    if (r == S2_OK) r = up_bf16(w->w_down, bl.w_down, (size_t)D * F);
+    if (r == S2_OK) r = up_f32(w->b_qkv, bl.b_qkv, 3 * D);
+    if (r == S2_OK) r = up_f32(w->b_out, bl.b_out, D);
+    if (r == S2_OK) r = up_f32(w->b_up, bl.b_up, F);
+    if (r == S2_OK) r = up_f32(w->b_down, bl.b_down, D);
+    if (r == S2_OK) r = up_f32(w->qk_norm, bl.qk_norm, 4 * d->cfg.head_dim);
+    if (r == S2_OK) r = up_f32(w->rope_freqs, bl.freqs, d->cfg.rope_pairs);
+    if (r == S2_OK) r = up_f32(w->ada, d->ada_all + (size_t)block * 6 * D, 6 * D);
+    if (r == S2_OK && cudaStreamSynchronize(c.stream) != cudaSuccess) r = S2_ERR_CUDA;
+    return r;
+}
+
+int s2_dit_init_random(s2_dit* d, uint64_t seed)
+{
+    if (!d) return S2_ERR_INVALID;
+    s2::Context& c = d->ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    const int D = d->cfg.hidden, F = d->cfg.mlp_hidden, hd = d->cfg.head_dim, np = d->cfg.rope_pairs;
+    std::vector<float> freqs(np);
+    for (int i = 0; i < np; i++) freqs[i] = (float)(1.0 / std::pow(10000.0, (2.0 * i) / (2.0 * np)));
+    int r = S2_OK;
+    for (int b = 0; b < d->cfg.num_blocks && r == S2_OK; b++)
+    {
+        const s2_dit::Block& bl = d->blocks[b];
+        const uint64_t s = seed * 1000003ull + (uint64_t)b * 64;
+        r = s2::launch_fill_normal_bf16(c, bl.w_qkv, (int64_t)3 * D * D, s + 1, 0.f, 0.02f);
+        if (r == S2_OK) r = s2::launch_fill_normal_bf16(c, bl.w_out, (int64_t)D * D, s + 2, 0.f, 0.02f);
+        if (r == S2_OK) r = s2::launch_fill_normal_bf16(c, bl.w_up, (int64_t)F * D, s + 3, 0.f, 0.02f);
+        if (r == S2_OK) r = s2::launch_fill_normal_bf16(c, bl.w_down, (int64_t)D * F, s + 4, 0.f, 0.02f);
+        if (r == S2_OK) r = s2::launch_fill_normal_f32(c, bl.b_qkv, (int64_t)3 * D + D + F + D, s + 5, 0.f, 0.02f);
+        if (r == S2_OK) r = s2::launch_fill_normal_f32(c, bl.qk_norm, (int64_t)4 * hd, s + 6, 1.f, 0.02f);
+        if (r == S2_OK)
+            r = cudaMemcpyAsync(bl.freqs, freqs.data(), np * 4, cudaMemcpyHostToDevice, c.stream) == cudaSuccess
+                    ? S2_OK
+                    : S2_ERR_CUDA;
+        float* ada = d->ada_all + (size_t)b * 6 * D;
+        const float sd = 1.f / std::sqrt((float)D);
+        for (int k = 0; k < 6 && r == S2_OK; k++)
+            r = s2::launch_fill_normal_f32(c, ada + (size_t)k * D, D, s + 10 + k, (k == 1 || k == 4) ? 1.f : 0.f, sd);
+    }
+    if (r == S2_OK && cudaStreamSynchronize(c.stream) != cudaSuccess) r = S2_ERR_CUDA;
+    return r;
+}
+
+int s2_dit_forward(s2_dit* d, const int* video_shape, int text_length, float* x, const float* modulation)
+{
+    if (!d || !video_shape || text_length <= 0 || !x || !modulation) return S2_ERR_INVALID;
+    s2::Context& c = d->ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    const s2_dit_config& cfg = d->cfg;
+    const int D = cfg.hidden, F = cfg.mlp_hidden, H = cfg.heads;
+    int r;
+    s2_plan* plans[2];
+    const s2::AttnSchedule* sched[2];
+    for (int s = 0; s < 2; s++)
+    {
+        if ((r = get_plan(d, video_shape, s, &plans[s])) != S2_OK) return r;
+        if ((r = s2::ensure_schedule(plans[s], &text_length, c, &sched[s])) != S2_OK) return r;
+    }
+    const int Nv = video_shape[0] * video_shape[1] * video_shape[2];
+    const int Nt = text_length;
+    const int M = Nv + Nt;
+    int max_packed = 0, max_partial = 0;
+    for (int s = 0; s < 2; s++)
+    {
+        max_packed = std::max(max_packed, sched[s]->packed_rows);
+        max_partial = std::max(max_partial, sched[s]->partial_rows);
+    }
+    // activations: h [M][D] bf16 | qkv [M][3D] bf16 | Q,K,V [R][D] bf16 | ctx [M][D] bf16 |
+    //              partial [P][D] f32 | u [M][F] bf16
+    const size_t sz_h = align256((size_t)M * D * 2), sz_qkv = align256((size_t)M * 3 * D * 2),
+                 sz_pk = align256((size_t)max_packed * D * 2), sz_ctx = sz_h,
+                 sz_part = align256((size_t)max_partial * D * 4), sz_u = align256((size_t)M * F * 2);
+    if ((r = d->act.ensure(sz_h + sz_qkv + 3 * sz_pk + sz_ctx + sz_part + sz_u)) != S2_OK) return r;
+    if ((r = d->mods.ensure((size_t)cfg.num_blocks * 6 * D * 4)) != S2_OK) return r;
+    uint8_t* a = static_cast<uint8_t*>(d->act.ptr);
+    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(a);
+    __nv_bfloat16* qkv = reinterpret_cast<__nv_bfloat16*>(a + sz_h);
+    uint8_t* pk = a + sz_h + sz_qkv;
+    __nv_bfloat16* ctxb = reinterpret_cast<__nv_bfloat16*>(pk + 3 * sz_pk);
+    float* partial = reinterpret_cast<float*>(pk + 3 * sz_pk + sz_ctx);
+    __nv_bfloat16* u = reinterpret_cast<__nv_bfloat16*>(pk + 3 * sz_pk + sz_ctx + sz_part);
+    float* mods = static_cast<float*>(d->mods.ptr);
+
+    // per-block modulation = shared frontend modulation + block offsets
+    if ((r = s2::launch_add_vectors(c, d->ada_all, modulation, mods, cfg.num_blocks * 6 * D, 6 * D)) != S2_OK)
+        return r;
+
+    for (int b = 0; b < cfg.num_blocks; b++)
+    {
+        const s2_dit::Block& bl = d->blocks[b];
+        const float* mb = mods + (size_t)b * 6 * D;
+        const int sh = b & 1; // odd blocks use the half-shifted windows
+        const s2::AttnSchedule& S = *sched[sh];
+        if ((r = s2::launch_ada_rmsnorm(c, M, D, x, cfg.norm_eps, mb, mb + D, h)) != S2_OK) return r;
+        if ((r = s2::launch_shared_linear(c, M, 0, 3 * D, D, h, nullptr, bl.w_qkv, cfg.qkv_bias ? bl.b_qkv : nullptr,
+                                          s2::EPI_STORE, nullptr, 0, qkv, nullptr)) != S2_OK)
+            return r;
+        const size_t pk_elems = (size_t)S.packed_rows * D;
+        __nv_bfloat16* Qp = reinterpret_cast<__nv_bfloat16*>(pk);
+        __nv_bfloat16* Kp = reinterpret_cast<__nv_bfloat16*>(pk + sz_pk);
+        __nv_bfloat16* Vp = reinterpret_cast<__nv_bfloat16*>(pk + 2 * sz_pk);
+        (void)pk_elems;
+        const __nv_bfloat16* tq = qkv + (size_t)Nv * 3 * D;
+        if ((r = s2::launch_prepare_qkv(c, S, H, cfg.head_dim, cfg.rope_pairs, cfg.qk_eps, bl.qk_norm, bl.freqs, 1, qkv,
+                                        qkv + D, qkv + 2 * D, 3 * D, tq, tq + D, tq + 2 * D, 3 * D, Qp, Kp, Vp)) !=
+            S2_OK)
+            return r;
+        if ((r = s2::launch_window_attention(c, S, H, Qp, Kp, Vp, 0, 0, ctxb, partial)) != S2_OK) return r;
+        if ((r = s2::launch_text_pool(c, S, D, partial, 0, 0, ctxb + (size_t)Nv * D)) != S2_OK) return r;
+        if ((r = s2::launch_shared_linear(c, M, 0, D, D, ctxb, nullptr, bl.w_out, cfg.out_bias ? bl.b_out : nullptr,
+                                          s2::EPI_GATE_RESIDUAL, mb + 2 * D, 1, x, nullptr)) != S2_OK)
+            return r;
+        if ((r = s2::launch_ada_rmsnorm(c, M, D, x, cfg.norm_eps, mb + 3 * D, mb + 4 * D, h)) != S2_OK) return r;
+        if ((r = s2::launch_shared_linear(c, M, 0, F, D, h, nullptr, bl.w_up, cfg.mlp_bias ? bl.b_up : nullptr,
+                                          s2::EPI_GELU_TANH, nullptr, 0, u, nullptr)) != S2_OK)
+            return r;
+        if ((r = s2::launch_shared_linear(c, M, 0, D, F, u, nullptr, bl.w_down, cfg.mlp_bias ? bl.b_down : nullptr,
+                                          s2::EPI_GATE_RESIDUAL, mb + 5 * D, 1, x, nullptr)) != S2_OK)
+            return r;
+    }
+    return S2_OK;
+}
+
+int s2_dit_forward_host(s2_dit* d, const int* video_shapes, const int* text_lengths, int batch, const float* video,
+                        const float* text, const float* modulation, float* video_out, float* text_out)
+{
+    if (!d || !video_shapes || !text_lengths || batch <= 0 || !video || !text || !modulation || !video_out ||
+        !text_out)
+        return S2_ERR_INVALID;
+    s2::Context& c = d->ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    const int D = d->cfg.hidden;
+    size_t v_off = 0, t_off = 0;
+    int r = S2_OK;
+    for (int s = 0; s < batch && r == S2_OK; s++)
+    {
+        const int* shp = video_shapes + 3 * s;
+        if (shp[0] <= 0 || shp[1] <= 0 || shp[2] <= 0 || text_lengths[s] <= 0) return S2_ERR_INVALID;
+        const size_t nv = (size_t)shp[0] * shp[1] * shp[2], nt = text_lengths[s];
+        const size_t x_bytes = (nv + nt) * D * 4;
+        if ((r = d->host_x.ensure(x_bytes + (size_t)6 * D * 4)) != S2_OK) return r;
+        float* x = static_cast<float*>(d->host_x.ptr);
+        float* mod = x + (nv + nt) * D;
+        if (cudaMemcpyAsync(x, video + v_off * D, nv * D * 4, cudaMemcpyHostToDevice, c.stream) != cudaSuccess ||
+            cudaMemcpyAsync(x + nv * D, text + t_off * D, nt * D * 4, cudaMemcpyHostToDevice, c.stream) !=
+                cudaSuccess)
+            return S2_ERR_CUDA;
+        // modulation host layout [6][batch][D] (six frontend outputs, one row per sample)
+        for (int k = 0; k < 6; k++)
+            if (cudaMemcpyAsync(mod + (size_t)k * D, modulation + ((size_t)k * batch + s) * D, (size_t)D * 4,
+                                cudaMemcpyHostToDevice, c.stream) != cudaSuccess)
+                return S2_ERR_CUDA;
+        r = s2_dit_forward(d, shp, text_lengths[s], x, mod);
+        if (r != S2_OK) return r;
+        if (cudaMemcpyAsync(video_out + v_off * D, x, nv * D * 4, cudaMemcpyDeviceToHost, c.stream) != cudaSuccess ||
+            cudaMemcpyAsync(text_out + t_off * D, x + nv * D, nt * D * 4, cudaMemcpyDeviceToHost, c.stream) !=
+                cudaSuccess)
+            return S2_ERR_CUDA;
+        v_off += nv;
+        t_off += nt;
+    }
+    if (cudaStreamSynchronize(c.stream) != cudaSuccess) return S2_ERR_CUDA;
+    return r;
+}
+
+} // extern "C"

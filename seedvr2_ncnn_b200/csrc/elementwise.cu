@@ -1,0 +1,353 @@
+// HBM-bound passes of the block: QK-RMSNorm + 3-axis RoPE + window gather
+// (prepare_qkv), the text-pool average over windows, AdaLN-style RMSNorm
+// modulation, and small utilities.  All are 16-byte vectorised, one warp (or
+// 16-lane group) per row, grids sized by rows.
+#include "s2_common.cuh"
+#include "s2_internal.h"
+
+namespace s2 {
+
+namespace {
+
+// ---------------------------------------------------------------- prepare_qkv
+// Replaces the prepare_qkv / prepare_qkv_split shaders
+// (adaptive_window_attention.cpp:21-172, :178-333) and the CPU gather of
+// :886-938: for packed row r (window w's video row or text row) and head h,
+//   q = x_q * (1/sqrt(mean(x_q^2) + eps)) * w_q, same for k (video or text
+//   weights), RoPE over 3 axes x `pairs` interleaved pairs at the row's
+//   position (angle = pos[axis] * freq[pair]), v copied; all stored as bf16.
+// One 16-lane group per (row, head): 8 consecutive dims per lane.
+template <typename Tin>
+__device__ __forceinline__ void load8(const Tin* p, float (&x)[8]);
+
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&x)[8])
+{
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p + 4));
+    x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+}
+
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&x)[8])
+{
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    float2 f;
+    f = unpack_bf16x2(u.x), x[0] = f.x, x[1] = f.y;
+    f = unpack_bf16x2(u.y), x[2] = f.x, x[3] = f.y;
+    f = unpack_bf16x2(u.z), x[4] = f.x, x[5] = f.y;
+    f = unpack_bf16x2(u.w), x[6] = f.x, x[7] = f.y;
+}
+
+__device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, const float (&x)[8])
+{
+    uint4 u;
+    u.x = pack_bf16x2(x[0], x[1]);
+    u.y = pack_bf16x2(x[2], x[3]);
+    u.z = pack_bf16x2(x[4], x[5]);
+    u.w = pack_bf16x2(x[6], x[7]);
+    *reinterpret_cast<uint4*>(p) = u;
+}
+
+template <typename Tin>
+__global__ void prepare_qkv_kernel(const int* __restrict__ row_src, const int* __restrict__ row_pos, int heads,
+                                   int head_dim, int pairs, float eps, const float* __restrict__ norms,
+                                   const float* __restrict__ freqs, const Tin* vq, const Tin* vk, const Tin* vv,
+                                   int64_t v_ld, const Tin* tq, const Tin* tk, const Tin* tv, int64_t t_ld,
+                                   __nv_bfloat16* qo, __nv_bfloat16* ko, __nv_bfloat16* vo)
+{
+    const int r = blockIdx.x;
+    // The block is rounded up to whole warps; lanes past the last head work on
+    // head 0 (in-bounds reads, full-warp shuffles) and store nothing.
+    const bool active = (int)(threadIdx.x >> 4) < heads;
+    const int h = active ? (int)(threadIdx.x >> 4) : 0;
+    const int sub = threadIdx.x & 15;
+    const int d0 = sub * 8;
+    const int src = row_src[r];
+    const Tin *pq, *pk, *pv;
+    const float *wq, *wk;
+    if (src >= 0)
+    {
+        pq = vq + (int64_t)src * v_ld;
+        pk = vk + (int64_t)src * v_ld;
+        pv = vv + (int64_t)src * v_ld;
+        wq = norms;
+        wk = norms + head_dim;
+    }
+    else
+    {
+        const int t = -1 - src;
+        pq = tq + (int64_t)t * t_ld;
+        pk = tk + (int64_t)t * t_ld;
+        pv = tv + (int64_t)t * t_ld;
+        wq = norms + 2 * head_dim;
+        wk = norms + 3 * head_dim;
+    }
+    const int off = h * head_dim + d0;
+    float q[8], k[8], v[8];
+    load8<Tin>(pq + off, q);
+    load8<Tin>(pk + off, k);
+    load8<Tin>(pv + off, v);
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+    {
+        sq += q[i] * q[i];
+        sk += k[i] * k[i];
+    }
+#pragma unroll
+    for (int m = 8; m >= 1; m >>= 1)
+    {
+        sq += __shfl_xor_sync(0xffffffffu, sq, m);
+        sk += __shfl_xor_sync(0xffffffffu, sk, m);
+    }
+    const float inv_q = 1.f / sqrtf(sq / head_dim + eps);
+    const float inv_k = 1.f / sqrtf(sk / head_dim + eps);
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+    {
+        q[i] = q[i] * inv_q * __ldg(wq + d0 + i);
+        k[i] = k[i] * inv_k * __ldg(wk + d0 + i);
+    }
+    const int axis_width = pairs * 2;
+    const int p0 = __ldg(row_pos + r * 3), p1 = __ldg(row_pos + r * 3 + 1), p2 = __ldg(row_pos + r * 3 + 2);
+#pragma unroll
+    for (int i = 0; i < 8; i += 2)
+    {
+        const int d = d0 + i;
+        if (d < axis_width * 3)
+        {
+            const int axis = d / axis_width;
+            const int pair = (d - axis * axis_width) >> 1;
+            const int pos = axis == 0 ? p0 : (axis == 1 ? p1 : p2);
+            const float ang = (float)pos * __ldg(freqs + pair);
+            float s, c;
+            sincosf(ang, &s, &c);
+            const float q0 = q[i], q1 = q[i + 1], k0 = k[i], k1 = k[i + 1];
+            q[i] = q0 * c - q1 * s;
+            q[i + 1] = q0 * s + q1 * c;
+            k[i] = k0 * c - k1 * s;
+            k[i + 1] = k0 * s + k1 * c;
+        }
+    }
+    if (!active) return;
+    const int64_t out = (int64_t)r * heads * head_dim + off;
+    store8_bf16(qo + out, q);
+    store8_bf16(ko + out, k);
+    store8_bf16(vo + out, v);
+}
+
+// ---------------------------------------------------------------- text pool
+// Replaces the text branch of the scatter (CPU :963-974, shader :395-407):
+// text_out[t] = sum over the sample's windows (in window order) of
+// partial[w][t] * (1 / windows in sample).
+__global__ void text_pool_kernel(const int4* __restrict__ reduce, const float* __restrict__ scale_of, int inner,
+                                 const float* __restrict__ partial, int out_f32, void* out)
+{
+    const int t = blockIdx.x;
+    const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
+    if (c >= inner) return;
+    const int4 rd = reduce[t];
+    const float sc = scale_of[t];
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < rd.z; i++)
+    {
+        const float4 p = __ldg(reinterpret_cast<const float4*>(partial + (int64_t)(rd.x + i * rd.y) * inner + c));
+        acc.x += p.x * sc;
+        acc.y += p.y * sc;
+        acc.z += p.z * sc;
+        acc.w += p.w * sc;
+    }
+    if (out_f32)
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (int64_t)t * inner + c) = acc;
+    else
+    {
+        uint2 u;
+        u.x = pack_bf16x2(acc.x, acc.y);
+        u.y = pack_bf16x2(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(out) + (int64_t)t * inner + c) = u;
+    }
+}
+
+// ---------------------------------------------------------------- ada_rmsnorm
+// y = x * (1/sqrt(mean(x^2) + eps)) * scale + shift -> bf16; one warp per row,
+// 8 dims per lane per step.
+__global__ void ada_rmsnorm_kernel(int rows, int D, const float* __restrict__ x, float eps,
+                                   const float* __restrict__ shift, const float* __restrict__ scale,
+                                   __nv_bfloat16* __restrict__ y)
+{
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* xr = x + (int64_t)row * D;
+    float ss = 0.f;
+    for (int c = lane * 8; c < D; c += 256)
+    {
+        float v[8];
+        load8<float>(xr + c, v);
+#pragma unroll
+        for (int i = 0; i < 8; i++) ss += v[i] * v[i];
+    }
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+    const float inv = 1.f / sqrtf(ss / D + eps);
+    __nv_bfloat16* yr = y + (int64_t)row * D;
+    for (int c = lane * 8; c < D; c += 256)
+    {
+        float v[8], sc[8], sh[8];
+        load8<float>(xr + c, v);
+        load8<float>(scale + c, sc);
+        load8<float>(shift + c, sh);
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = v[i] * inv * sc[i] + sh[i];
+        store8_bf16(yr + c, v);
+    }
+}
+
+__global__ void convert_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, int64_t count)
+{
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride)
+        out[i] = __float2bfloat16_rn(in[i]);
+}
+
+// out[i] = a[i] + b[i % period] (per-block modulation = shared + offset).
+__global__ void add_kernel(const float* a, const float* b, float* out, int count, int period)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < count) out[i] = a[i] + b[i % period];
+}
+
+// Counter-based normal samples (splitmix64 hash -> Box-Muller), deterministic
+// for (seed, index).
+__device__ __forceinline__ uint64_t mix64(uint64_t z)
+{
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ float normal_at(uint64_t seed, int64_t i)
+{
+    const uint64_t h = mix64(seed * 0x100000001B3ull ^ mix64((uint64_t)i));
+    const float u1 = ((uint32_t)(h >> 40) + 1.0f) * (1.0f / 16777217.0f); // (0,1]
+    const float u2 = (uint32_t)(h & 0xFFFFFFu) * (1.0f / 16777216.0f);
+    return sqrtf(-2.f * logf(u1)) * cospif(2.f * u2);
+}
+
+__global__ void fill_normal_bf16_kernel(__nv_bfloat16* out, int64_t count, uint64_t seed, float mean, float stddev)
+{
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride)
+        out[i] = __float2bfloat16_rn(mean + stddev * normal_at(seed, i));
+}
+
+__global__ void fill_normal_f32_kernel(float* out, int64_t count, uint64_t seed, float mean, float stddev)
+{
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride)
+        out[i] = mean + stddev * normal_at(seed, i);
+}
+
+inline int finish(Context& ctx)
+{
+    ctx.launches++;
+    return cudaGetLastError() == cudaSuccess ? S2_OK : S2_ERR_CUDA;
+}
+
+inline bool aligned16(const void* p)
+{
+    return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+
+} // namespace
+
+int launch_prepare_qkv(Context& ctx, const AttnSchedule& s, int heads, int head_dim, int rope_pairs, float eps,
+                       const float* norms, const float* freqs, int in_bf16, const void* vq, const void* vk,
+                       const void* vv, int64_t v_ld, const void* tq, const void* tk, const void* tv, int64_t t_ld,
+                       void* q_out, void* k_out, void* v_out)
+{
+    if (head_dim != 128 || heads <= 0 || heads * 16 > 1024 || rope_pairs * 6 > head_dim) return S2_ERR_INVALID;
+    const int esz = in_bf16 ? 2 : 4;
+    // 16-byte vector loads need every row and head offset 16-byte aligned.
+    if ((v_ld * esz) % 16 || (t_ld * esz) % 16 || !aligned16(vq) || !aligned16(vk) || !aligned16(vv) ||
+        !aligned16(tq) || !aligned16(tk) || !aligned16(tv))
+        return S2_ERR_INVALID;
+    if (s.packed_rows == 0) return S2_OK;
+    const dim3 grid(s.packed_rows), block((heads * 16 + 31) & ~31);
+    if (in_bf16)
+        prepare_qkv_kernel<__nv_bfloat16><<<grid, block, 0, ctx.stream>>>(
+            s.row_src, s.row_pos, heads, head_dim, rope_pairs, eps, norms, freqs, (const __nv_bfloat16*)vq,
+            (const __nv_bfloat16*)vk, (const __nv_bfloat16*)vv, v_ld, (const __nv_bfloat16*)tq,
+            (const __nv_bfloat16*)tk, (const __nv_bfloat16*)tv, t_ld, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_out,
+            (__nv_bfloat16*)v_out);
+    else
+        prepare_qkv_kernel<float><<<grid, block, 0, ctx.stream>>>(
+            s.row_src, s.row_pos, heads, head_dim, rope_pairs, eps, norms, freqs, (const float*)vq, (const float*)vk,
+            (const float*)vv, v_ld, (const float*)tq, (const float*)tk, (const float*)tv, t_ld, (__nv_bfloat16*)q_out,
+            (__nv_bfloat16*)k_out, (__nv_bfloat16*)v_out);
+    return finish(ctx);
+}
+
+int launch_text_pool(Context& ctx, const AttnSchedule& s, int inner, const float* partial, int out_f32,
+                     int round_bf16, void* text_out)
+{
+    (void)round_bf16;
+    if (s.total_text == 0) return S2_OK;
+    if (inner % 4) return S2_ERR_INVALID;
+    const int threads = 256;
+    const dim3 grid(s.total_text, (inner / 4 + threads - 1) / threads);
+    text_pool_kernel<<<grid, threads, 0, ctx.stream>>>(s.text_reduce, s.text_scale, inner, partial, out_f32,
+                                                        text_out);
+    return finish(ctx);
+}
+
+int launch_ada_rmsnorm(Context& ctx, int rows, int D, const float* x, float eps, const float* shift,
+                       const float* scale, void* out)
+{
+    if (rows < 0 || D <= 0 || D % 8 || !aligned16(x) || !aligned16(shift) || !aligned16(scale) || !aligned16(out))
+        return S2_ERR_INVALID;
+    if (rows == 0) return S2_OK;
+    const int warps = 8;
+    ada_rmsnorm_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, ctx.stream>>>(rows, D, x, eps, shift, scale,
+                                                                                (__nv_bfloat16*)out);
+    return finish(ctx);
+}
+
+int launch_convert_f32_bf16(Context& ctx, const float* in, void* out, int64_t count)
+{
+    if (count <= 0) return count == 0 ? S2_OK : S2_ERR_INVALID;
+    int64_t blocks = (count + 255) / 256;
+    if (blocks > ctx.num_sms * 16) blocks = ctx.num_sms * 16;
+    convert_kernel<<<(int)blocks, 256, 0, ctx.stream>>>(in, (__nv_bfloat16*)out, count);
+    return finish(ctx);
+}
+
+int launch_add_vectors(Context& ctx, const float* a, const float* b, float* out, int count, int period)
+{
+    if (count <= 0) return S2_OK;
+    if (period <= 0) return S2_ERR_INVALID;
+    add_kernel<<<(count + 255) / 256, 256, 0, ctx.stream>>>(a, b, out, count, period);
+    return finish(ctx);
+}
+
+int launch_fill_normal_bf16(Context& ctx, void* out, int64_t count, uint64_t seed, float mean, float stddev)
+{
+    if (count <= 0) return S2_OK;
+    int64_t blocks = (count + 255) / 256;
+    if (blocks > ctx.num_sms * 32) blocks = ctx.num_sms * 32;
+    fill_normal_bf16_kernel<<<(int)blocks, 256, 0, ctx.stream>>>((__nv_bfloat16*)out, count, seed, mean, stddev);
+    return finish(ctx);
+}
+
+int launch_fill_normal_f32(Context& ctx, float* out, int64_t count, uint64_t seed, float mean, float stddev)
+{
+    if (count <= 0) return S2_OK;
+    int64_t blocks = (count + 255) / 256;
+    if (blocks > ctx.num_sms * 32) blocks = ctx.num_sms * 32;
+    fill_normal_f32_kernel<<<(int)blocks, 256, 0, ctx.stream>>>(out, count, seed, mean, stddev);
+    return finish(ctx);
+}
+
+} // namespace s2

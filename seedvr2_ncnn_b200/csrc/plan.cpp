@@ -1,0 +1,337 @@
+// Host side of the window path: the window plan (bit-exact with the
+// reference's build_adaptive_window_plan), the device attention schedule
+// derived from it, TMA descriptor encoding and workspace buffers.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <numeric>
+
+#include "s2_internal.h"
+
+namespace s2 {
+
+// ---------------------------------------------------------------- plan
+namespace {
+
+int ceil_div(int a, int b)
+{
+    return (a + b - 1) / b;
+}
+
+// Extents per axis.  Target mode: adaptive_window_attention.cpp:577-588 --
+// scale = sqrt(3600 / (h*w)), resized extents rounded half-to-even
+// (nearbyint under the default rounding mode, :439-444), window =
+// ceil(min(t,30)/n_t), ceil(round(h*scale)/n_h), ceil(round(w*scale)/n_w).
+// Extent mode: the tuple is the window extent itself.
+int extents(int t, int h, int w, int mode, const int* win, int& wt, int& wh, int& ww)
+{
+    if (t <= 0 || h <= 0 || w <= 0 || win[0] <= 0 || win[1] <= 0 || win[2] <= 0) return S2_ERR_INVALID;
+    if (mode == S2_WINDOW_TARGET)
+    {
+        const double scale = std::sqrt(3600.0 / static_cast<double>(h * w));
+        const int rh = static_cast<int>(std::nearbyint(h * scale));
+        const int rw = static_cast<int>(std::nearbyint(w * scale));
+        wt = ceil_div(std::min(t, 30), win[0]);
+        wh = ceil_div(rh, win[1]);
+        ww = ceil_div(rw, win[2]);
+    }
+    else if (mode == S2_WINDOW_EXTENT)
+    {
+        wt = win[0];
+        wh = win[1];
+        ww = win[2];
+    }
+    else
+        return S2_ERR_INVALID;
+    return (wt > 0 && wh > 0 && ww > 0) ? S2_OK : S2_ERR_INVALID;
+}
+
+struct Axis
+{
+    int count;
+    double shift;
+};
+
+// :592-598: a half-window shift applies only when shifted and window < extent;
+// shifted count = ceil((ext - 0.5) / win) + 1, else ceil(ext / win).
+Axis axis(int ext, int win, int shifted)
+{
+    Axis a;
+    a.shift = (shifted && win < ext) ? 0.5 : 0.0;
+    if (!shifted)
+        a.count = ceil_div(ext, win);
+    else
+        a.count = a.shift > 0.0 ? static_cast<int>(std::ceil((ext - a.shift) / win)) + 1 : 1;
+    return a;
+}
+
+// :611-629: shifted bounds truncate toward zero (static_cast<int>) before the clamp.
+void bounds(int i, int ext, int win, int shifted, double s, int& lo, int& hi)
+{
+    if (shifted)
+    {
+        lo = std::max(static_cast<int>((i - s) * win), 0);
+        hi = std::min(static_cast<int>((i - s + 1.0) * win), ext);
+    }
+    else
+    {
+        lo = i * win;
+        hi = std::min((i + 1) * win, ext);
+    }
+}
+
+} // namespace
+
+int build_plan(const int* shapes, int batch, const int* window, int window_mode, int shifted, Plan& plan)
+{
+    plan = Plan();
+    if (!shapes || !window || batch <= 0) return S2_ERR_INVALID;
+    plan.batch = batch;
+    plan.shapes.assign(shapes, shapes + 3 * batch);
+    int total = 0;
+    for (int s = 0; s < batch; s++)
+    {
+        const int t = shapes[3 * s], h = shapes[3 * s + 1], w = shapes[3 * s + 2];
+        int wt, wh, ww;
+        const int r = extents(t, h, w, window_mode, window, wt, wh, ww);
+        if (r != S2_OK) return r;
+        const Axis at = axis(t, wt, shifted), ah = axis(h, wh, shifted), aw = axis(w, ww, shifted);
+        const int first = static_cast<int>(plan.windows.size() / 9);
+        plan.sample_first_window.push_back(first);
+        // Window order w outer, h, t inner (:600-630); tokens t, h, w inside
+        // a window (append_slice, :446-473).
+        for (int iw = 0; iw < aw.count; iw++)
+        {
+            int w0, w1;
+            bounds(iw, w, ww, shifted, aw.shift, w0, w1);
+            if (w1 <= w0) continue;
+            for (int ih = 0; ih < ah.count; ih++)
+            {
+                int h0, h1;
+                bounds(ih, h, wh, shifted, ah.shift, h0, h1);
+                if (h1 <= h0) continue;
+                for (int it = 0; it < at.count; it++)
+                {
+                    int t0, t1;
+                    bounds(it, t, wt, shifted, at.shift, t0, t1);
+                    if (t1 <= t0) continue;
+                    const int offset = static_cast<int>(plan.video_indices.size());
+                    const int count = (t1 - t0) * (h1 - h0) * (w1 - w0);
+                    const int rec[9] = {s, t0, t1, h0, h1, w0, w1, offset, count};
+                    plan.windows.insert(plan.windows.end(), rec, rec + 9);
+                    plan.max_window_tokens = std::max(plan.max_window_tokens, count);
+                    for (int ti = t0; ti < t1; ti++)
+                        for (int hi = h0; hi < h1; hi++)
+                            for (int wi = w0; wi < w1; wi++)
+                            {
+                                plan.video_indices.push_back(total + (ti * h + hi) * w + wi);
+                                plan.local_positions.push_back(ti - t0);
+                                plan.local_positions.push_back(hi - h0);
+                                plan.local_positions.push_back(wi - w0);
+                            }
+                }
+            }
+        }
+        plan.sample_window_count.push_back(static_cast<int>(plan.windows.size() / 9) - first);
+        total += t * h * w;
+    }
+    // Coverage: every token exactly once (:642-653).
+    if (static_cast<int>(plan.video_indices.size()) != total) return S2_ERR_PLAN;
+    plan.inverse_video_indices.assign(total, -1);
+    for (int p = 0; p < total; p++)
+    {
+        const int src = plan.video_indices[p];
+        if (src < 0 || src >= total || plan.inverse_video_indices[src] != -1) return S2_ERR_PLAN;
+        plan.inverse_video_indices[src] = p;
+    }
+    return S2_OK;
+}
+
+// ---------------------------------------------------------------- schedule
+AttnSchedule::~AttnSchedule()
+{
+    if (block) cudaFree(block);
+}
+
+int build_schedule(const Plan& plan, const int* text_lengths, AttnSchedule& s, cudaStream_t stream)
+{
+    const int nw = static_cast<int>(plan.windows.size() / 9);
+    std::vector<int> text_offset(plan.batch, 0);
+    int total_text = 0, max_text = 0;
+    for (int b = 0; b < plan.batch; b++)
+    {
+        if (text_lengths[b] <= 0) return S2_ERR_INVALID;
+        text_offset[b] = total_text;
+        total_text += text_lengths[b];
+        max_text = std::max(max_text, text_lengths[b]);
+    }
+    std::vector<int> row_src, row_pos;
+    std::vector<int4> win_info(nw);
+    std::vector<int> win_pool(nw);
+    std::vector<int2> items;
+    std::vector<int> item_cost;
+    int seq = 0, pool = 0;
+    for (int w = 0; w < nw; w++)
+    {
+        const int* rec = &plan.windows[9 * w];
+        const int sample = rec[0], part = rec[7], L = rec[8], T = text_lengths[sample];
+        win_info[w] = make_int4(seq, L, T, part);
+        win_pool[w] = pool;
+        for (int r = 0; r < L; r++)
+        {
+            row_src.push_back(plan.video_indices[part + r]);
+            // video RoPE position: window-local (t + text_len, h, w) (:904-905)
+            row_pos.push_back(plan.local_positions[3 * (part + r)] + T);
+            row_pos.push_back(plan.local_positions[3 * (part + r) + 1]);
+            row_pos.push_back(plan.local_positions[3 * (part + r) + 2]);
+        }
+        for (int j = 0; j < T; j++)
+        {
+            row_src.push_back(-1 - (text_offset[sample] + j));
+            // text RoPE position (i, i, i) (:915)
+            row_pos.push_back(j);
+            row_pos.push_back(j);
+            row_pos.push_back(j);
+        }
+        const int S = L + T;
+        const int ntiles = (S + 127) / 128;
+        for (int q0 = 0; q0 < S; q0 += 128)
+        {
+            items.push_back(make_int2(w, q0));
+            item_cost.push_back(ntiles);
+        }
+        seq += S;
+        pool += T;
+    }
+    // Longest-first: q-tiles of the biggest windows start first.
+    std::vector<int> order(items.size());
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return item_cost[a] > item_cost[b]; });
+    std::vector<int2> sorted(items.size());
+    for (size_t i = 0; i < order.size(); i++) sorted[i] = items[order[i]];
+
+    std::vector<int4> reduce(total_text);
+    std::vector<float> scale(total_text);
+    for (int b = 0; b < plan.batch; b++)
+    {
+        const int fw = plan.sample_first_window[b], cnt = plan.sample_window_count[b];
+        for (int j = 0; j < text_lengths[b]; j++)
+        {
+            reduce[text_offset[b] + j] = make_int4(cnt > 0 ? win_pool[fw] + j : 0, text_lengths[b], cnt, 0);
+            scale[text_offset[b] + j] = cnt > 0 ? 1.f / cnt : 0.f;
+        }
+    }
+
+    // One device block for every table.
+    const size_t n_tok = plan.video_indices.size();
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off += (bytes + 255) & ~size_t(255);
+        return o;
+    };
+    const size_t o_src = take(row_src.size() * 4), o_pos = take(row_pos.size() * 4), o_win = take(nw * 16),
+                 o_pool = take(nw * 4), o_items = take(sorted.size() * 8), o_vi = take(n_tok * 4),
+                 o_red = take(total_text * 16), o_scale = take(total_text * 4);
+    if (s.block)
+    {
+        cudaFree(s.block);
+        s.block = nullptr;
+    }
+    if (cudaMalloc(&s.block, off ? off : 256) != cudaSuccess) return S2_ERR_ALLOC;
+    std::vector<uint8_t> host(off ? off : 256, 0);
+    auto put = [&](size_t o, const void* src, size_t bytes) {
+        if (bytes) std::memcpy(host.data() + o, src, bytes);
+    };
+    put(o_src, row_src.data(), row_src.size() * 4);
+    put(o_pos, row_pos.data(), row_pos.size() * 4);
+    put(o_win, win_info.data(), nw * 16);
+    put(o_pool, win_pool.data(), nw * 4);
+    put(o_items, sorted.data(), sorted.size() * 8);
+    put(o_vi, plan.video_indices.data(), n_tok * 4);
+    put(o_red, reduce.data(), total_text * 16);
+    put(o_scale, scale.data(), total_text * 4);
+    if (cudaMemcpyAsync(s.block, host.data(), host.size(), cudaMemcpyHostToDevice, stream) != cudaSuccess ||
+        cudaStreamSynchronize(stream) != cudaSuccess)
+        return S2_ERR_CUDA;
+    uint8_t* base = static_cast<uint8_t*>(s.block);
+    s.row_src = reinterpret_cast<int*>(base + o_src);
+    s.row_pos = reinterpret_cast<int*>(base + o_pos);
+    s.win_info = reinterpret_cast<int4*>(base + o_win);
+    s.win_pool = reinterpret_cast<int*>(base + o_pool);
+    s.items = reinterpret_cast<int2*>(base + o_items);
+    s.video_indices = reinterpret_cast<int*>(base + o_vi);
+    s.text_reduce = reinterpret_cast<int4*>(base + o_red);
+    s.text_scale = reinterpret_cast<float*>(base + o_scale);
+    s.num_windows = nw;
+    s.packed_rows = seq;
+    s.num_items = static_cast<int>(sorted.size());
+    s.total_text = total_text;
+    s.max_text = max_text;
+    s.partial_rows = pool;
+    return S2_OK;
+}
+
+// ---------------------------------------------------------------- TMA maps
+namespace {
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    if (!fn)
+    {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+} // namespace
+
+// 2-D bf16 tensor [outer][inner] with 128-byte swizzle; box = box_inner x
+// box_outer (box_inner * 2 bytes must be 128); out-of-range elements read 0.
+int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                      uint32_t box_inner, uint32_t box_outer)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return S2_ERR_DEVICE;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_stride_bytes & 15) || box_inner * 2 != 128)
+        return S2_ERR_INVALID;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_stride_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? S2_OK : S2_ERR_INVALID;
+}
+
+// ---------------------------------------------------------------- buffers
+int DeviceBuffer::ensure(size_t want)
+{
+    if (want <= bytes) return S2_OK;
+    release();
+    want = (want + 4095) & ~size_t(4095);
+    if (cudaMalloc(&ptr, want) != cudaSuccess)
+    {
+        ptr = nullptr;
+        return S2_ERR_ALLOC;
+    }
+    bytes = want;
+    return S2_OK;
+}
+
+void DeviceBuffer::release()
+{
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    bytes = 0;
+}
+
+} // namespace s2

@@ -1,0 +1,110 @@
+// Internal (non-ABI) declarations shared by the library's translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <memory>
+#include <vector>
+
+#include "../../include/seedvr2_cuda.h"
+
+namespace s2 {
+
+enum
+{
+    EPI_STORE = S2_EPI_STORE,
+    EPI_GELU_TANH = S2_EPI_GELU_TANH,
+    EPI_GATE_RESIDUAL = S2_EPI_GATE_RESIDUAL,
+};
+
+// Grow-only device workspace slot.
+struct DeviceBuffer
+{
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    int ensure(size_t want);
+    void release();
+    ~DeviceBuffer() { release(); }
+};
+
+struct Context
+{
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int num_sms = 148;
+    int* status = nullptr; // device status word
+    uint64_t launches = 0;
+    // workspace slots (see s2_api.cu for their use)
+    DeviceBuffer ws[8];
+};
+
+// Host window plan (AdaptiveWindowPlan) plus its device-side attention
+// schedule, built once per (shapes, window tuple, shift) and cached.
+struct Plan
+{
+    int batch = 0;
+    std::vector<int> shapes;              // [batch][3]
+    std::vector<int> windows;             // [nw][9]
+    std::vector<int> sample_window_count; // [batch]
+    std::vector<int> sample_first_window; // [batch]
+    std::vector<int> video_indices;       // [n]
+    std::vector<int> inverse_video_indices;
+    std::vector<int> local_positions; // [n][3]
+    int max_window_tokens = 0;
+};
+
+int build_plan(const int* shapes, int batch, const int* window, int window_mode, int shifted, Plan& plan);
+
+// Device tables for one (plan, text_lengths) pair.
+struct AttnSchedule
+{
+    int num_windows = 0;
+    int packed_rows = 0;    // sum over windows of (L_w + T_s)
+    int num_items = 0;      // q-tiles (window, q0) in longest-first order
+    int total_text = 0;
+    int max_text = 0;
+    // device arrays
+    int* row_src = nullptr;    // [packed_rows] video row (>= 0) or -(1 + text row)
+    int* row_pos = nullptr;    // [packed_rows][3] rope positions
+    int4* win_info = nullptr;  // [nw] {seq_offset, L, T, partition_offset}
+    int* win_pool = nullptr;   // [nw] partial-row offset of the window's text rows
+    int2* items = nullptr;     // [num_items] {window, q0}
+    int* video_indices = nullptr; // [n]
+    int4* text_reduce = nullptr;  // [total_text] {first partial row, stride (T), count (nw_s), 0}
+    float* text_scale = nullptr;  // [total_text] 1/nw_s
+    int partial_rows = 0;         // sum over windows of T_s
+    void* block = nullptr;        // single device allocation backing the arrays
+    ~AttnSchedule();
+};
+
+int build_schedule(const Plan& plan, const int* text_lengths, AttnSchedule& sched, cudaStream_t stream);
+
+int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                      uint32_t box_inner, uint32_t box_outer);
+
+// kernels (launchers return S2_* codes)
+int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void* A0, const void* A1, const void* W,
+                         const float* bias, int epilogue, const float* gate, int out_f32, void* out0, void* out1);
+
+int launch_prepare_qkv(Context& ctx, const AttnSchedule& s, int heads, int head_dim, int rope_pairs, float eps,
+                       const float* norms, const float* freqs, int in_bf16, const void* vq, const void* vk,
+                       const void* vv, int64_t v_ld, const void* tq, const void* tk, const void* tv, int64_t t_ld,
+                       void* q_out, void* k_out, void* v_out);
+
+int launch_window_attention(Context& ctx, const AttnSchedule& s, int heads, const void* q, const void* k,
+                            const void* v, int out_f32, int round_bf16, void* video_out, float* text_partial);
+
+int launch_text_pool(Context& ctx, const AttnSchedule& s, int inner, const float* partial, int out_f32,
+                     int round_bf16, void* text_out);
+
+int launch_ada_rmsnorm(Context& ctx, int rows, int D, const float* x, float eps, const float* shift,
+                       const float* scale, void* out);
+
+int launch_convert_f32_bf16(Context& ctx, const float* in, void* out, int64_t count);
+int launch_add_vectors(Context& ctx, const float* a, const float* b, float* out, int count, int period);
+int launch_fill_normal_bf16(Context& ctx, void* out, int64_t count, uint64_t seed, float mean, float stddev);
+int launch_fill_normal_f32(Context& ctx, float* out, int64_t count, uint64_t seed, float mean, float stddev);
+
+} // namespace s2

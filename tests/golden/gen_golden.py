@@ -1,0 +1,137 @@
+"""Generates the golden fixtures in tests/golden/ from the reference's OWN
+layer code (oracle/_ref/libs2_ref.so: src/seedvr2/adaptive_window_attention.cpp
+and src/seedvr2/shared_linear.cpp compiled unmodified against the clean-room
+ncnn API shim).  Run from the repository root where the reference tree is
+available:
+
+    python tests/golden/gen_golden.py [--reference-tree PATH]
+
+Outputs:
+  plans.npz   -- build_adaptive_window_plan for every BASELINE shape, both
+                 shift states, several target tuples, a 2-sample batch and a
+                 set of ragged shapes.  Small plans store every array; large
+                 plans store the window table plus SHA-256 digests of the
+                 index/position arrays.
+  awa.npz     -- AdaptiveWindowAttention::forward (CPU) on a seeded 2-sample
+                 batch, fused-QKV input, shifted/unshifted x bf16 on/off.
+  linear.npz  -- SharedLinear::forward on seeded inputs, with and without bias.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+
+from oracle import oracle  # noqa: E402
+
+OUT = os.path.dirname(os.path.abspath(__file__))
+
+# (name, shapes, target, shifted)
+PLAN_CASES = [
+    ("c1_default", [[1, 32, 32]], (4, 3, 3)),
+    ("c2_default", [[1, 64, 64]], (4, 3, 3)),
+    ("c3_default", [[6, 45, 80]], (4, 3, 3)),
+    ("c3_434", [[6, 45, 80]], (4, 3, 4)),
+    ("c5_default", [[12, 68, 120]], (4, 3, 3)),
+    ("c5_433_21f", [[21, 90, 160]], (4, 3, 3)),
+    ("batch2", [[2, 6, 8], [1, 4, 4]], (2, 2, 2)),
+    ("ragged_a", [[3, 7, 11]], (2, 3, 2)),
+    ("ragged_b", [[1, 1, 1]], (4, 3, 3)),
+    ("ragged_c", [[5, 13, 9]], (5, 1, 7)),
+    ("ragged_d", [[31, 17, 29]], (4, 3, 3)),
+    ("wide", [[1, 9, 400]], (1, 2, 9)),
+]
+FULL_ARRAYS_MAX_TOKENS = 4096
+
+
+def digest(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a, dtype=np.int32).tobytes()).hexdigest()
+
+
+def gen_plans(ref: oracle.Ref) -> None:
+    out = {}
+    for name, shapes, target in PLAN_CASES:
+        for shifted in (0, 1):
+            key = f"{name}_s{shifted}"
+            p = ref.plan(shapes, target, shifted)
+            out[f"{key}__shapes"] = np.asarray(shapes, np.int32)
+            out[f"{key}__target"] = np.asarray(target, np.int32)
+            out[f"{key}__windows"] = p.windows
+            out[f"{key}__sample_window_count"] = p.sample_window_count
+            for arr_name in ("video_indices", "inverse_video_indices", "local_positions"):
+                arr = getattr(p, arr_name)
+                out[f"{key}__sha_{arr_name}"] = np.frombuffer(digest(arr).encode(), np.uint8)
+                if len(p.video_indices) <= FULL_ARRAYS_MAX_TOKENS:
+                    out[f"{key}__{arr_name}"] = arr
+    np.savez_compressed(os.path.join(OUT, "plans.npz"), **out)
+
+
+AWA_SEED = 1234
+
+
+def awa_inputs():
+    rng = np.random.default_rng(AWA_SEED)
+    heads, hd = 2, 128
+    shapes = np.asarray([[1, 6, 8], [2, 2, 3]], np.int32)
+    text_lengths = np.asarray([5, 3], np.int32)
+    nv = int(np.prod(shapes, axis=1).sum())
+    nt = int(text_lengths.sum())
+    inner = heads * hd
+    video_qkv = rng.standard_normal((nv, 3 * inner)).astype(np.float32)
+    text_qkv = rng.standard_normal((nt, 3 * inner)).astype(np.float32)
+    norms = (1.0 + 0.02 * rng.standard_normal((4, hd))).astype(np.float32)
+    freqs = (1.0 / 10000.0 ** (np.arange(21) * 2.0 / 42.0)).astype(np.float32)
+    return dict(heads=heads, head_dim=hd, shapes=shapes, text_lengths=text_lengths, video_qkv=video_qkv,
+                text_qkv=text_qkv, norms=norms, freqs=freqs, target=np.asarray([2, 2, 2], np.int32),
+                eps=np.float32(1e-5), rope_pairs=21)
+
+
+def gen_awa(ref: oracle.Ref) -> None:
+    inp = awa_inputs()
+    out = {k: np.asarray(v) for k, v in inp.items()}
+    for shifted in (0, 1):
+        for bf16 in (0, 1):
+            vo, to = ref.awa_forward(heads=inp["heads"], head_dim=inp["head_dim"], target=inp["target"],
+                                     shifted=shifted, eps=float(inp["eps"]), rope_pairs=inp["rope_pairs"],
+                                     norms=inp["norms"], freqs=inp["freqs"], shapes=inp["shapes"],
+                                     text_lengths=inp["text_lengths"], video_qkv=inp["video_qkv"],
+                                     text_qkv=inp["text_qkv"], bf16=bool(bf16))
+            out[f"video_out_s{shifted}_b{bf16}"] = vo
+            out[f"text_out_s{shifted}_b{bf16}"] = to
+    np.savez_compressed(os.path.join(OUT, "awa.npz"), **out)
+
+
+def gen_linear(ref: oracle.Ref) -> None:
+    rng = np.random.default_rng(99)
+    k, n = 96, 80
+    video = rng.standard_normal((37, k)).astype(np.float32)
+    text = rng.standard_normal((5, k)).astype(np.float32)
+    weight = (0.02 * rng.standard_normal((n, k))).astype(np.float32)
+    bias = (0.02 * rng.standard_normal(n)).astype(np.float32)
+    vo_b, to_b = ref.shared_linear(video, text, weight, bias)
+    vo_n, to_n = ref.shared_linear(video, text, weight, None)
+    np.savez_compressed(os.path.join(OUT, "linear.npz"), video=video, text=text, weight=weight, bias=bias,
+                        video_out_bias=vo_b, text_out_bias=to_b, video_out_nobias=vo_n, text_out_nobias=to_n)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference-tree", default=os.environ.get("S2_REFERENCE_TREE", "/root/reference"))
+    args = ap.parse_args()
+    oracle.build(args.reference_tree)
+    ref = oracle.Ref()
+    gen_plans(ref)
+    gen_awa(ref)
+    gen_linear(ref)
+    for f in ("plans.npz", "awa.npz", "linear.npz"):
+        print(f, os.path.getsize(os.path.join(OUT, f)), "bytes")
+
+
+if __name__ == "__main__":
+    main()
