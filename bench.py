@@ -1,0 +1,367 @@
+"""Benchmark of the SeedVR2 DiT block hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--impl ours|reference]
+
+One step = one full 32-block DiT forward (one denoising step's block stack)
+over one sample of the chosen configuration, synthetic seeded inputs and
+random-init weights of the BASELINE architecture (hidden 2560, 20x128 heads,
+MLP 10240 GELU-tanh, 58 text tokens).  Default workload: BASELINE config 3,
+720p x 21 frames -> 6x45x80 = 21600 video tokens, windows 2x15x20 (the
+reference's own target-count rule with target (4,3,4)), half-shifted in odd
+blocks.
+
+Prints one JSON line (rank 0).  ``value`` = tokens/s of the device-resident
+forward; ``e2e`` = the same metric through s2_dit_forward_host with host
+buffers (H2D + D2H inside the timed region); ``roofline`` = the dominant
+kernel from the library's own per-kernel counters (CUDA events inside the
+timed region); ``window_attention`` = the same for the attention kernel;
+``cpu_baseline`` = the reference's CPU layer code (oracle/_ref) or the oracle
+port on a bounded sample of the same workload.
+
+``--impl reference`` times the reference's CPU implementation (oracle/_ref,
+the reference's own AdaptiveWindowAttention/SharedLinear sources built
+against a clean-room ncnn API shim; the oracle port when that build is
+absent) with all host threads, on the same config and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+D, HEADS, HD, F, TEXT, PAIRS, BLOCKS = 2560, 20, 128, 10240, 58, 21, 32
+
+# name -> (video shape t,h,w ; window tuple ; window mode 0=target count (reference) 1=extent ; description)
+CONFIGS = {
+    "c1": ([1, 32, 32], [1, 16, 16], 1, "BASELINE config 1 geometry: 1x32x32 tokens, windows 16x16"),
+    "c2": ([1, 64, 64], [1, 16, 16], 1, "BASELINE config 2: 1024x1024 image, 64x64 tokens, windows 1x16x16"),
+    "c3": ([6, 45, 80], [4, 3, 4], 0, "BASELINE config 3: 720p x 21 frames, 6x45x80 tokens, windows 2x15x20"),
+    "c5": ([12, 68, 120], [4, 17, 30], 1, "BASELINE config 5: 1080p x 45 frames, 12x68x120 tokens, windows 4x17x30"),
+}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return {"hbm_gbs": j["hbm_gbs"], "bf16_tflops": j["bf16_tflops"],
+                "bf16_tflops_sustained": j.get("bf16_tflops_sustained", j["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
+             "clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------- CPU baseline
+def cpu_sample(kind_pref: str = "reference", threads: int | None = None):
+    """Times one window-block of the config-3 workload on the host: the reference's
+    AdaptiveWindowAttention (one 2x15x20 window + 58 text tokens) and its four
+    SharedLinear projections (QKV, out, MLP up, MLP down) over those 658 tokens.
+    Returns (seconds, kind, cores)."""
+    import numpy as np
+
+    from oracle import oracle
+
+    if threads:
+        os.environ["OMP_NUM_THREADS"] = str(threads)
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    rng = np.random.default_rng(0)
+    shape, T = [2, 15, 20], TEXT
+    nv = 600
+    inner = HEADS * HD
+    x = rng.standard_normal((nv, D)).astype(np.float32)
+    xt = rng.standard_normal((T, D)).astype(np.float32)
+    w_qkv = (0.02 * rng.standard_normal((3 * D, D))).astype(np.float32)
+    w_out = (0.02 * rng.standard_normal((D, D))).astype(np.float32)
+    w_up = (0.02 * rng.standard_normal((F, D))).astype(np.float32)
+    w_down = (0.02 * rng.standard_normal((D, F))).astype(np.float32)
+    b = lambda n: (0.02 * rng.standard_normal(n)).astype(np.float32)  # noqa: E731
+    norms = (1 + 0.02 * rng.standard_normal((4, HD))).astype(np.float32)
+    freqs = (1.0 / 10000 ** (np.arange(PAIRS) * 2 / 42)).astype(np.float32)
+    use_ref = kind_pref == "reference" and os.path.exists(oracle.REF_SO)
+    if use_ref:
+        lib = oracle.Ref()
+        t0 = time.perf_counter()
+        qv, qt = lib.shared_linear(x, xt, w_qkv, b(3 * D))
+        # one window covering the slab: target (1,1,1) -> a single 2x15x20 window
+        cv, ct = lib.awa_forward(heads=HEADS, head_dim=HD, target=[1, 1, 1], shifted=0, eps=1e-5, rope_pairs=PAIRS,
+                                 norms=norms, freqs=freqs, shapes=[shape], text_lengths=[T], video_qkv=qv,
+                                 text_qkv=qt)
+        ov, ot = lib.shared_linear(cv, ct, w_out, b(D))
+        uv, ut = lib.shared_linear(ov, ot, w_up, b(F))
+        lib.shared_linear(uv, ut, w_down, b(D))
+        dt = time.perf_counter() - t0
+        return dt, "reference", cores
+    lib = oracle.Port()
+    t0 = time.perf_counter()
+    a = np.concatenate([x, xt])
+    qkv = lib.linear(a, w_qkv, b(3 * D))
+    cv, ct = lib.awa_forward(heads=HEADS, head_dim=HD, window=[2, 15, 20], shifted=0, eps=1e-5, rope_pairs=PAIRS,
+                             norms=norms, freqs=freqs, shapes=[shape], text_lengths=[T], video_qkv=qkv[:nv],
+                             text_qkv=qkv[nv:], mode=oracle.WINDOW_EXTENT)
+    o = lib.linear(np.concatenate([cv, ct]), w_out, b(D))
+    u = lib.linear(o, w_up, b(F))
+    lib.linear(u, w_down, b(D))
+    dt = time.perf_counter() - t0
+    return dt, "port", cores
+
+
+def cpu_tokens_per_s(sample_s: float, cfg_name: str) -> float:
+    """Extrapolates one window-block (600 video + 58 text tokens) to a full 32-block step:
+    step time = 32 blocks x (video tokens / 600) window-blocks x sample time."""
+    shape = CONFIGS[cfg_name][0]
+    nv = shape[0] * shape[1] * shape[2]
+    step_s = BLOCKS * (nv / 600.0) * sample_s
+    return (nv + TEXT) / step_s
+
+
+# ---------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c3", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    shape, window, mode, desc = CONFIGS[args.config]
+    nv = shape[0] * shape[1] * shape[2]
+    M = nv + TEXT
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        for _ in range(args.warmup):
+            cpu_sample("reference")
+        samples = []
+        kind = cores = None
+        for _ in range(args.steps):
+            dt, kind, cores = cpu_sample("reference")
+            samples.append(dt)
+        sample_s = statistics.median(samples)
+        v = cpu_tokens_per_s(sample_s, args.config)
+        step_ms = BLOCKS * (nv / 600.0) * sample_s * 1000.0
+        print(json.dumps({
+            "impl": "reference", "metric": "DiT tokens/sec/GPU (32-block step)", "value": v, "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": desc, "config": args.config, "tokens": M},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind,
+                             "sample": "one 2x15x20 window + 58 text tokens through AWA and the 4 SharedLinear "
+                                       "projections of one block (fp32), extrapolated x32 blocks x windows"},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }))
+        return
+
+    import torch
+
+    from seedvr2_ncnn_b200 import abi
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import torch.distributed as dist
+
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+    ctx = abi.Context(local_rank)
+    dit = abi.Dit(ctx, num_blocks=BLOCKS, hidden=D, heads=HEADS, head_dim=HD, mlp_hidden=F, rope_pairs=PAIRS,
+                  window=window, window_mode=mode)
+    dit.init_random(1234)
+    g = torch.Generator(device="cuda").manual_seed(100 + rank)
+    x0 = torch.randn(M, D, device="cuda", generator=g)
+    mod = torch.randn(6, D, device="cuda", generator=g)
+    x = torch.empty_like(x0)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        x.copy_(x0)
+        dit.forward(shape, TEXT, x, mod)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    status = ctx.status()
+    if status != 0:
+        raise RuntimeError(f"device status {status} after warm-up")
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    ctx.profile(True)
+    launches0 = ctx.launches()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    launches = ctx.launches() - launches0
+    counters = ctx.counters()
+    ctx.profile(False)
+    clk = clocks.stop()
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * M / (ms / 1000.0)
+
+    # end to end through the host-buffer entry point (pinned host memory)
+    hv = x0[:nv].cpu().pin_memory()
+    ht = x0[nv:].cpu().pin_memory()
+    hm = mod.reshape(6, 1, D).cpu().pin_memory()
+    ov = torch.empty_like(hv).pin_memory()
+    ot = torch.empty_like(ht).pin_memory()
+
+    def e2e_step():
+        dit.forward_host([shape], [TEXT], hv, ht, hm, ov, ot)
+
+    e2e_step()
+    barrier()
+    e2e_steps = max(1, min(args.steps, 5))
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    status = ctx.status()
+
+    peaks = load_peaks()
+
+    def roof(name, bound):
+        c = counters[name]
+        per_launch_ms = c["ms"] / max(c["launches"], 1)
+        if bound == "tensor":
+            achieved = c["flops"] / (c["ms"] / 1000.0) / 1e12
+            peak = peaks["bf16_tflops_sustained"]
+            unit = "TFLOP/s"
+        else:
+            achieved = c["bytes"] / (c["ms"] / 1000.0) / 1e9
+            peak = peaks["hbm_gbs"]
+            unit = "GB/s"
+        return {"kernel": name, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                "frac": achieved / peak, "peak_source": f"{peaks['source']} "
+                + ("bf16 sustained (kernel timed inside a long step)" if bound == "tensor" else "HBM copy"),
+                "launches_per_step": c["launches"] / args.steps, "ms_per_launch": per_launch_ms,
+                "share_of_step": c["ms"] / args.steps / ms, "traffic": None}
+
+    kinds = {"shared_linear": "tensor", "window_attention": "tensor", "prepare_qkv": "hbm", "ada_rmsnorm": "hbm",
+             "text_pool": "hbm"}
+    dominant = max(kinds, key=lambda k: counters[k]["ms"])
+    result = {
+        "metric": "DiT tokens/sec/GPU (32-block step)", "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) tokens and "
+        "modulation, N(0,0.02) random-init weights)",
+        "config": {"workload": desc, "config": args.config, "video_tokens": nv, "text_tokens": TEXT,
+                   "blocks": BLOCKS, "hidden": D, "heads": HEADS, "mlp": F, "window": window,
+                   "window_mode": "target-count" if mode == 0 else "extent", "global_batch": world,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (5 GB of weights + 222 MB residual per step)"},
+        "roofline": roof(dominant, kinds[dominant]),
+        "window_attention": roof("window_attention", "tensor"),
+        "hbm_passes": {k: roof(k, "hbm") for k in ("prepare_qkv", "ada_rmsnorm", "text_pool")},
+        "e2e": {"value": world * M / (e2e_ms / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(M * D * 4 + 6 * D * 4), "d2h_bytes_per_step": int(M * D * 4),
+                "ms_per_step": e2e_ms, "entry_point": "s2_dit_forward_host"},
+        "gpu_launches": launches,
+        "clocks": clk,
+        "device_status": status,
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        dt, kind, cores = cpu_sample("reference")
+        v = cpu_tokens_per_s(dt, args.config)
+        result["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind,
+                                  "sample": "one 2x15x20 window + 58 text tokens through AWA and the 4 SharedLinear "
+                                            "projections of one block (fp32), extrapolated x32 blocks x windows",
+                                  "sample_seconds": dt}
+    if rank == 0:
+        print(json.dumps(result))
+    dit.close()
+    ctx.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

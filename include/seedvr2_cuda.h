@@ -65,6 +65,23 @@ int s2_version(void);
 /* Count of this library's kernel launches on ctx since creation. */
 uint64_t s2_launch_count(const s2_context* ctx);
 
+/* Per-kernel counters (the layers' "ncnn counters"): while enabled, every
+ * launch is bracketed by CUDA events on the context stream and credited with
+ * its algorithmic flops and HBM bytes.  Enabling resets the totals.
+ * s2_profile_read synchronises the stream and returns the totals of one
+ * kernel kind.  The reference has no counters (wall clock only,
+ * examples/seedvr2_blocks_main.cpp:135-149). */
+#define S2_KERNEL_SHARED_LINEAR 0
+#define S2_KERNEL_WINDOW_ATTENTION 1
+#define S2_KERNEL_PREPARE_QKV 2
+#define S2_KERNEL_ADA_RMSNORM 3
+#define S2_KERNEL_TEXT_POOL 4
+#define S2_KERNEL_OTHER 5
+#define S2_NUM_KERNEL_KINDS 6
+int s2_profile_enable(s2_context* ctx, int enable);
+int s2_profile_read(s2_context* ctx, int kind, int64_t* launches, double* milliseconds, double* flops,
+                    double* bytes);
+
 /* ---------------------------------------------------------------------------
  * Window plan.  Replaces build_adaptive_window_plan
  * (adaptive_window_attention.h:46-49, .cpp:565-655), bit-exact for

@@ -26,6 +26,14 @@ S2_DTYPE_BF16 = 1
 S2_WINDOW_TARGET = 0
 S2_WINDOW_EXTENT = 1
 
+S2_KERNEL_SHARED_LINEAR = 0
+S2_KERNEL_WINDOW_ATTENTION = 1
+S2_KERNEL_PREPARE_QKV = 2
+S2_KERNEL_ADA_RMSNORM = 3
+S2_KERNEL_TEXT_POOL = 4
+S2_KERNEL_OTHER = 5
+KERNEL_NAMES = ["shared_linear", "window_attention", "prepare_qkv", "ada_rmsnorm", "text_pool", "other"]
+
 S2_EPI_STORE = 0
 S2_EPI_GELU_TANH = 1
 S2_EPI_GATE_RESIDUAL = 2
@@ -33,6 +41,7 @@ S2_EPI_GATE_RESIDUAL = 2
 # Every symbol include/seedvr2_cuda.h declares.
 EXPORTED = [
     "s2_init", "s2_destroy", "s2_set_stream", "s2_status", "s2_error_string", "s2_version", "s2_launch_count",
+    "s2_profile_enable", "s2_profile_read",
     "s2_plan_build", "s2_plan_info", "s2_plan_copy", "s2_plan_free",
     "s2_awa_forward", "s2_shared_linear", "s2_ada_rmsnorm", "s2_convert_f32_bf16",
     "s2_dit_create", "s2_dit_free", "s2_dit_set_block_weights", "s2_dit_init_random", "s2_dit_forward",
@@ -92,6 +101,9 @@ def lib() -> C.CDLL:
     L.s2_version.argtypes = []
     L.s2_launch_count.argtypes = [vp]
     L.s2_launch_count.restype = C.c_uint64
+    L.s2_profile_enable.argtypes = [vp, ip]
+    L.s2_profile_read.argtypes = [vp, ip, C.POINTER(C.c_int64), C.POINTER(C.c_double), C.POINTER(C.c_double),
+                                  C.POINTER(C.c_double)]
     L.s2_plan_build.argtypes = [pint, ip, pint, ip, ip, C.POINTER(vp)]
     L.s2_plan_info.argtypes = [vp, pint, pint, pint]
     L.s2_plan_copy.argtypes = [vp, pint, pint, pint, pint, pint]
@@ -169,6 +181,19 @@ class Context:
 
     def launches(self) -> int:
         return int(lib().s2_launch_count(self.handle))
+
+    def profile(self, enable: bool) -> None:
+        check(lib().s2_profile_enable(self.handle, int(bool(enable))), "s2_profile_enable")
+
+    def counters(self) -> dict:
+        """{kernel name: {launches, ms, flops, bytes}} since profiling was enabled."""
+        out = {}
+        for k, name in enumerate(KERNEL_NAMES):
+            n, ms, fl, by = C.c_int64(), C.c_double(), C.c_double(), C.c_double()
+            check(lib().s2_profile_read(self.handle, k, C.byref(n), C.byref(ms), C.byref(fl), C.byref(by)),
+                  "s2_profile_read")
+            out[name] = {"launches": n.value, "ms": ms.value, "flops": fl.value, "bytes": by.value}
+        return out
 
 
 class Plan:

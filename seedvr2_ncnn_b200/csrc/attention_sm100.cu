@@ -417,6 +417,10 @@ int launch_window_attention(Context& ctx, const AttnSchedule& s, int heads, cons
         configured = true;
     }
     dim3 grid(s.num_items, heads);
+    const double video_rows = (double)s.packed_rows - s.partial_rows;
+    ProfileScope prof(ctx, K_ATTN, s.attn_flops_per_head * heads,
+                      (double)s.packed_rows * inner * 2.0 * 3.0 + video_rows * inner * (out_f32 ? 4.0 : 2.0) +
+                          (double)s.partial_rows * inner * 4.0);
     window_attention_kernel<<<grid, NUM_THREADS, SMEM_BYTES, ctx.stream>>>(mq, mk, mv, a);
     ctx.launches++;
     return cudaGetLastError() == cudaSuccess ? S2_OK : S2_ERR_CUDA;

@@ -276,6 +276,7 @@ int launch_prepare_qkv(Context& ctx, const AttnSchedule& s, int heads, int head_
         return S2_ERR_INVALID;
     if (s.packed_rows == 0) return S2_OK;
     const dim3 grid(s.packed_rows), block((heads * 16 + 31) & ~31);
+    ProfileScope prof(ctx, K_PREP, 0.0, (double)s.packed_rows * heads * head_dim * 3.0 * (esz + 2.0));
     if (in_bf16)
         prepare_qkv_kernel<__nv_bfloat16><<<grid, block, 0, ctx.stream>>>(
             s.row_src, s.row_pos, heads, head_dim, rope_pairs, eps, norms, freqs, (const __nv_bfloat16*)vq,
@@ -298,6 +299,8 @@ int launch_text_pool(Context& ctx, const AttnSchedule& s, int inner, const float
     if (inner % 4) return S2_ERR_INVALID;
     const int threads = 256;
     const dim3 grid(s.total_text, (inner / 4 + threads - 1) / threads);
+    ProfileScope prof(ctx, K_POOL, 0.0,
+                      (double)s.partial_rows * inner * 4.0 + (double)s.total_text * inner * (out_f32 ? 4.0 : 2.0));
     text_pool_kernel<<<grid, threads, 0, ctx.stream>>>(s.text_reduce, s.text_scale, inner, partial, out_f32,
                                                         text_out);
     return finish(ctx);
@@ -310,6 +313,7 @@ int launch_ada_rmsnorm(Context& ctx, int rows, int D, const float* x, float eps,
         return S2_ERR_INVALID;
     if (rows == 0) return S2_OK;
     const int warps = 8;
+    ProfileScope prof(ctx, K_NORM, 0.0, (double)rows * D * 6.0);
     ada_rmsnorm_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, ctx.stream>>>(rows, D, x, eps, shift, scale,
                                                                                 (__nv_bfloat16*)out);
     return finish(ctx);

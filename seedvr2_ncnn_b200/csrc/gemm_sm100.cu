@@ -389,6 +389,9 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
         configured = true;
     }
     const int grid = a.num_tiles < ctx.num_sms ? a.num_tiles : ctx.num_sms;
+    const double M = (double)M0 + M1;
+    const double out_bytes = epilogue == EPI_GATE_RESIDUAL ? 8.0 : (out_f32 ? 4.0 : 2.0);
+    ProfileScope prof(ctx, K_GEMM, 2.0 * M * N * K, (M * K + (double)N * K) * 2.0 + M * N * out_bytes);
     shared_linear_kernel<<<grid, NUM_THREADS, SMEM_BYTES, ctx.stream>>>(ta0, ta1, tw, a);
     ctx.launches++;
     return cudaGetLastError() == cudaSuccess ? S2_OK : S2_ERR_CUDA;

@@ -195,6 +195,7 @@ int build_schedule(const Plan& plan, const int* text_lengths, AttnSchedule& s, c
         }
         const int S = L + T;
         const int ntiles = (S + 127) / 128;
+        s.attn_flops_per_head += 4.0 * S * (double)S * 128.0;
         for (int q0 = 0; q0 < S; q0 += 128)
         {
             items.push_back(make_int2(w, q0));
@@ -332,6 +333,78 @@ void DeviceBuffer::release()
     if (ptr) cudaFree(ptr);
     ptr = nullptr;
     bytes = 0;
+}
+
+} // namespace s2
+
+// ---------------------------------------------------------------- counters
+namespace s2 {
+
+void Profiler::reset()
+{
+    collect();
+    for (int k = 0; k < K_NUM; k++)
+    {
+        launches[k] = 0;
+        ms[k] = flops[k] = bytes[k] = 0.0;
+    }
+}
+
+int Profiler::collect()
+{
+    int r = S2_OK;
+    for (Record& rec : pending)
+    {
+        float t = 0.f;
+        if (cudaEventSynchronize(rec.stop) != cudaSuccess || cudaEventElapsedTime(&t, rec.start, rec.stop) != cudaSuccess)
+            r = S2_ERR_CUDA;
+        launches[rec.kind] += 1;
+        ms[rec.kind] += t;
+        flops[rec.kind] += rec.flops;
+        bytes[rec.kind] += rec.bytes;
+        pool.push_back(rec.start);
+        pool.push_back(rec.stop);
+    }
+    pending.clear();
+    return r;
+}
+
+void Profiler::release()
+{
+    collect();
+    for (cudaEvent_t e : pool) cudaEventDestroy(e);
+    pool.clear();
+}
+
+static cudaEvent_t take_event(Profiler& p)
+{
+    if (!p.pool.empty())
+    {
+        cudaEvent_t e = p.pool.back();
+        p.pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+ProfileScope::ProfileScope(Context& c, int kind, double f, double b) : ctx(c), on(c.prof.on)
+{
+    if (!on) return;
+    rec.kind = kind;
+    rec.flops = f;
+    rec.bytes = b;
+    rec.start = take_event(c.prof);
+    rec.stop = take_event(c.prof);
+    cudaEventRecord(rec.start, c.stream);
+}
+
+ProfileScope::~ProfileScope()
+{
+    if (!on) return;
+    cudaEventRecord(rec.stop, ctx.stream);
+    ctx.prof.pending.push_back(rec);
 }
 
 } // namespace s2

@@ -102,6 +102,7 @@ void s2_destroy(s2_context* ctx)
     cudaSetDevice(ctx->c.device);
     cudaStreamSynchronize(ctx->c.stream);
     ctx->plan_cache.clear();
+    ctx->c.prof.release();
     for (auto& b : ctx->c.ws) b.release();
     if (ctx->c.status) cudaFree(ctx->c.status);
     delete ctx;
@@ -129,6 +130,25 @@ int s2_status(s2_context* ctx)
     if (h == s2::kStatusTimeout) return S2_ERR_TIMEOUT;
     if (h != 0) return S2_ERR_INVALID;
     return S2_OK;
+}
+
+int s2_profile_enable(s2_context* ctx, int enable)
+{
+    if (!ctx) return S2_ERR_INVALID;
+    ctx->c.prof.reset();
+    ctx->c.prof.on = enable != 0;
+    return S2_OK;
+}
+
+int s2_profile_read(s2_context* ctx, int kind, int64_t* launches, double* milliseconds, double* flops, double* bytes)
+{
+    if (!ctx || kind < 0 || kind >= S2_NUM_KERNEL_KINDS) return S2_ERR_INVALID;
+    const int r = ctx->c.prof.collect();
+    if (launches) *launches = ctx->c.prof.launches[kind];
+    if (milliseconds) *milliseconds = ctx->c.prof.ms[kind];
+    if (flops) *flops = ctx->c.prof.flops[kind];
+    if (bytes) *bytes = ctx->c.prof.bytes[kind];
+    return r;
 }
 
 // ------------------------------------------------------------------ plan

@@ -29,6 +29,38 @@ struct DeviceBuffer
     ~DeviceBuffer() { release(); }
 };
 
+// Per-kernel-class counters: CUDA-event time and algorithmic work.
+enum KernelKind
+{
+    K_GEMM = S2_KERNEL_SHARED_LINEAR,
+    K_ATTN = S2_KERNEL_WINDOW_ATTENTION,
+    K_PREP = S2_KERNEL_PREPARE_QKV,
+    K_NORM = S2_KERNEL_ADA_RMSNORM,
+    K_POOL = S2_KERNEL_TEXT_POOL,
+    K_OTHER = S2_KERNEL_OTHER,
+    K_NUM = S2_NUM_KERNEL_KINDS,
+};
+
+struct Profiler
+{
+    struct Record
+    {
+        int kind;
+        cudaEvent_t start, stop;
+        double flops, bytes;
+    };
+    bool on = false;
+    std::vector<cudaEvent_t> pool;
+    std::vector<Record> pending;
+    int64_t launches[K_NUM] = {};
+    double ms[K_NUM] = {};
+    double flops[K_NUM] = {};
+    double bytes[K_NUM] = {};
+    void reset();
+    int collect(); // waits for pending records and folds them in
+    void release();
+};
+
 struct Context
 {
     int device = 0;
@@ -36,8 +68,19 @@ struct Context
     int num_sms = 148;
     int* status = nullptr; // device status word
     uint64_t launches = 0;
+    Profiler prof;
     // workspace slots (see s2_api.cu for their use)
     DeviceBuffer ws[8];
+};
+
+// Brackets one launch with events when counters are on.
+struct ProfileScope
+{
+    Context& ctx;
+    bool on;
+    Profiler::Record rec;
+    ProfileScope(Context& c, int kind, double flops, double bytes);
+    ~ProfileScope();
 };
 
 // Host window plan (AdaptiveWindowPlan) plus its device-side attention
@@ -75,6 +118,7 @@ struct AttnSchedule
     int4* text_reduce = nullptr;  // [total_text] {first partial row, stride (T), count (nw_s), 0}
     float* text_scale = nullptr;  // [total_text] 1/nw_s
     int partial_rows = 0;         // sum over windows of T_s
+    double attn_flops_per_head = 0; // sum over windows of 4 * S^2 * 128 (QK^T + PV)
     void* block = nullptr;        // single device allocation backing the arrays
     ~AttnSchedule();
 };

@@ -1,0 +1,114 @@
+"""GPU parity of whole DiT blocks (s2_dit, through the C ABI) against the CPU
+oracle's fp32 block restatement on identical seeded inputs and weights.
+
+Gate per block (north star): cosine >= 0.9995 and
+max|gpu - ref| / max|ref| <= 2e-2 on the block output; the block's update
+(output - input) must also agree (cosine >= 0.999) so the residual stream
+cannot hide an error in the block itself.
+"""
+import numpy as np
+import pytest
+
+from tests.conftest import cosine, rel_maxabs
+
+pytestmark = pytest.mark.gpu
+
+
+def make_block_weights(rng, D, F, hd, pairs, bias=True):
+    n = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
+    ada = n(6, D) / np.sqrt(D)
+    ada[1] += 1.0
+    ada[4] += 1.0
+    return dict(ada=ada, w_qkv=0.02 * n(3 * D, D), b_qkv=(0.02 * n(3 * D)) if bias else None,
+                w_out=0.02 * n(D, D), b_out=(0.02 * n(D)) if bias else None, w_up=0.02 * n(F, D),
+                b_up=(0.02 * n(F)) if bias else None, w_down=0.02 * n(D, F), b_down=(0.02 * n(D)) if bias else None,
+                qk_norm=1 + 0.02 * n(4, hd), rope_freqs=(1.0 / 10000 ** (np.arange(pairs) * 2 / (2 * pairs))))
+
+
+def run_case(gpu_ctx, s2lib, port, *, D, heads, F, shape, T, window, mode, blocks, seed, bias=True):
+    import torch
+
+    hd, pairs = 128, 21
+    rng = np.random.default_rng(seed)
+    ws = [make_block_weights(rng, D, F, hd, pairs, bias) for _ in range(blocks)]
+    mod = rng.standard_normal((6, D)).astype(np.float32)
+    nv = int(np.prod(shape))
+    xv = rng.standard_normal((nv, D)).astype(np.float32)
+    xt = rng.standard_normal((T, D)).astype(np.float32)
+
+    dit = s2lib.Dit(gpu_ctx, num_blocks=blocks, hidden=D, heads=heads, head_dim=hd, mlp_hidden=F, rope_pairs=pairs,
+                    window=window, window_mode=mode, bias=bias)
+    for b, w in enumerate(ws):
+        dit.set_block_weights(b, w)
+    x = torch.from_numpy(np.concatenate([xv, xt])).cuda()
+    dit.forward(shape, T, x, torch.from_numpy(mod).cuda())
+    torch.cuda.synchronize()
+    assert gpu_ctx.status() == 0
+    got = x.cpu().numpy()
+
+    ref_v, ref_t = xv, xt
+    for b, w in enumerate(ws):
+        dims = [D, heads, hd, F, pairs, mode, window[0], window[1], window[2], b & 1]
+        wo = dict(w)
+        wo["freqs"] = wo.pop("rope_freqs")
+        prev = np.concatenate([ref_v, ref_t])
+        ref_v, ref_t = port.block_forward(dims=dims, eps_norm=1e-5, eps_qk=1e-5, weights=wo, modulation=mod[None],
+                                          shapes=[shape], text_lengths=[T], x_video=ref_v, x_text=ref_t)
+    ref = np.concatenate([ref_v, ref_t])
+    dit.close()
+    return got, ref, prev, np.concatenate([xv, xt])
+
+
+def check(got, ref, prev):
+    assert cosine(got, ref) >= 0.9995
+    assert rel_maxabs(got, ref) <= 2e-2
+    assert cosine(got - prev, ref - prev) >= 0.999
+
+
+def test_block_reduced_width_two_blocks(gpu_ctx, s2lib, port):
+    """Block 0 (unshifted) then block 1 (shifted) at D=512, ragged shifted windows."""
+    got, ref, prev, x0 = run_case(gpu_ctx, s2lib, port, D=512, heads=4, F=2048, shape=[2, 12, 20], T=58,
+                                  window=[1, 8, 8], mode=1, blocks=2, seed=3)
+    check(got, ref, prev)
+
+
+def test_block_full_width_one_block(gpu_ctx, s2lib, port):
+    """BASELINE widths (D=2560, 20x128 heads, MLP 10240), one 720p-shaped window slab."""
+    got, ref, prev, x0 = run_case(gpu_ctx, s2lib, port, D=2560, heads=20, F=10240, shape=[2, 15, 20], T=58,
+                                  window=[4, 3, 4], mode=0, blocks=1, seed=4)
+    check(got, ref, x0)
+
+
+def test_block_no_bias_target_windows(gpu_ctx, s2lib, port):
+    got, ref, prev, x0 = run_case(gpu_ctx, s2lib, port, D=256, heads=2, F=1024, shape=[3, 9, 14], T=7,
+                                  window=[2, 2, 3], mode=0, blocks=2, seed=5, bias=False)
+    check(got, ref, prev)
+
+
+def test_forward_host_matches_device(gpu_ctx, s2lib):
+    """s2_dit_forward_host (host buffers, 2 samples run one after another) == per-sample s2_dit_forward."""
+    import torch
+
+    D, heads, F = 256, 2, 1024
+    dit = s2lib.Dit(gpu_ctx, num_blocks=2, hidden=D, heads=heads, head_dim=128, mlp_hidden=F, window=[1, 4, 4],
+                    window_mode=1)
+    dit.init_random(9)
+    rng = np.random.default_rng(0)
+    shapes, tls = [[1, 6, 8], [2, 4, 4]], [5, 3]
+    nv = [48, 32]
+    video = rng.standard_normal((sum(nv), D)).astype(np.float32)
+    text = rng.standard_normal((sum(tls), D)).astype(np.float32)
+    mod = rng.standard_normal((6, 2, D)).astype(np.float32)
+    vo = np.zeros_like(video)
+    to = np.zeros_like(text)
+    dit.forward_host(shapes, tls, video, text, mod, vo, to)
+    voff = toff = 0
+    for s in range(2):
+        x = torch.from_numpy(np.concatenate([video[voff:voff + nv[s]], text[toff:toff + tls[s]]])).cuda()
+        dit.forward(shapes[s], tls[s], x, torch.from_numpy(np.ascontiguousarray(mod[:, s])).cuda())
+        x = x.cpu().numpy()
+        np.testing.assert_array_equal(x[:nv[s]], vo[voff:voff + nv[s]])
+        np.testing.assert_array_equal(x[nv[s]:], to[toff:toff + tls[s]])
+        voff += nv[s]
+        toff += tls[s]
+    dit.close()
