@@ -31,6 +31,7 @@ extern "C" {
 #define S2_ERR_CUDA (-3)
 #define S2_ERR_TIMEOUT (-4)
 #define S2_ERR_DEVICE (-5)
+#define S2_ERR_TOO_LARGE (-6) /* exceeds a fixed workspace (s2_awa_forward_static) */
 #define S2_ERR_ALLOC (-100)
 
 #define S2_DTYPE_F32 0
@@ -128,6 +129,29 @@ int s2_awa_forward(s2_context* ctx, const s2_awa_params* params, const s2_plan* 
                    const int* text_lengths, int batch, int in_dtype, const void* video_q, const void* video_k,
                    const void* video_v, int64_t video_ld, const void* text_q, const void* text_k,
                    const void* text_v, int64_t text_ld, int out_dtype, void* video_out, void* text_out);
+
+/* AdaptiveWindowAttention forward that allocates no memory, for callers that
+ * cannot call cudaMalloc: plugins whose host owns all device memory and only
+ * hands them inputs and outputs, processes under a hard device-memory cap,
+ * and loops that must not risk the device-wide synchronisation of
+ * cudaMalloc/cudaFree.  No counterpart in the reference (its layers allocate
+ * through ncnn's allocators).  Same arguments and results as s2_awa_forward
+ * minus the context and plan; `stream` is a cudaStream_t of the CURRENT
+ * device.  Scratch (schedule tables, packed bf16 q/k/v, text partials, a
+ * status word) is one static __device__ array of S2_AWA_STATIC_SCRATCH_BYTES
+ * that every GPU loading the library holds until exit; with 20 heads it fits
+ * about 4000 packed rows (video tokens + windows x text tokens), e.g. a
+ * 1x32x32 or 1x48x48 token video with 58 text tokens.  Larger inputs return
+ * S2_ERR_TOO_LARGE.  The first call on a device resolves the array's device
+ * address (cudaGetSymbolAddress) -- make it before any stream capture.  All
+ * calls share the array: calls whose GPU work overlaps race (serialise
+ * them on one stream).  Device-side wait timeouts are recorded in the
+ * scratch status word only. */
+#define S2_AWA_STATIC_SCRATCH_BYTES (64u << 20)
+int s2_awa_forward_static(const s2_awa_params* params, const int* video_shapes, const int* text_lengths, int batch,
+                          int in_dtype, const void* video_q, const void* video_k, const void* video_v,
+                          int64_t video_ld, const void* text_q, const void* text_k, const void* text_v,
+                          int64_t text_ld, int out_dtype, void* video_out, void* text_out, void* stream);
 
 /* ---------------------------------------------------------------------------
  * SharedLinear forward.  Replaces SharedLinear::forward (shared_linear.cpp:83-96,

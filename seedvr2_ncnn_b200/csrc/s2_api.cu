@@ -62,6 +62,7 @@ const char* s2_error_string(int code)
     case S2_ERR_CUDA: return "CUDA error";
     case S2_ERR_TIMEOUT: return "bounded device wait expired";
     case S2_ERR_DEVICE: return "unsupported device (needs sm_100)";
+    case S2_ERR_TOO_LARGE: return "input exceeds the fixed static workspace";
     case S2_ERR_ALLOC: return "allocation failure";
     default: return "unknown error";
     }
