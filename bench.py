@@ -186,6 +186,8 @@ def main():
     ap.add_argument("--config", default="c3", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer pass (profiling runs)")
+    ap.add_argument("--blocks", type=int, default=BLOCKS, help="fewer blocks for small profiling captures only")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -232,7 +234,7 @@ def main():
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     ctx = abi.Context(local_rank)
-    dit = abi.Dit(ctx, num_blocks=BLOCKS, hidden=D, heads=HEADS, head_dim=HD, mlp_hidden=F, rope_pairs=PAIRS,
+    dit = abi.Dit(ctx, num_blocks=args.blocks, hidden=D, heads=HEADS, head_dim=HD, mlp_hidden=F, rope_pairs=PAIRS,
                   window=window, window_mode=mode)
     dit.init_random(1234)
     g = torch.Generator(device="cuda").manual_seed(100 + rank)
@@ -282,6 +284,7 @@ def main():
     value = world * M / (ms / 1000.0)
 
     # end to end through the host-buffer entry point (pinned host memory)
+    e2e_ms = float("nan")
     hv = x0[:nv].cpu().pin_memory()
     ht = x0[nv:].cpu().pin_memory()
     hm = mod.reshape(6, 1, D).cpu().pin_memory()
@@ -291,15 +294,16 @@ def main():
     def e2e_step():
         dit.forward_host([shape], [TEXT], hv, ht, hm, ov, ot)
 
-    e2e_step()
-    barrier()
-    e2e_steps = max(1, min(args.steps, 5))
-    e0.record(stream)
-    for _ in range(e2e_steps):
+    if not args.no_e2e:
         e2e_step()
-    e1.record(stream)
-    barrier()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+        barrier()
+        e2e_steps = max(1, min(args.steps, 5))
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        barrier()
+        e2e_ms = e0.elapsed_time(e1) / e2e_steps
     if world > 1:
         t = torch.tensor([e2e_ms], device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -334,7 +338,7 @@ def main():
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) tokens and "
         "modulation, N(0,0.02) random-init weights)",
         "config": {"workload": desc, "config": args.config, "video_tokens": nv, "text_tokens": TEXT,
-                   "blocks": BLOCKS, "hidden": D, "heads": HEADS, "mlp": F, "window": window,
+                   "blocks": args.blocks, "hidden": D, "heads": HEADS, "mlp": F, "window": window,
                    "window_mode": "target-count" if mode == 0 else "extent", "global_batch": world,
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (5 GB of weights + 222 MB residual per step)"},
