@@ -6,18 +6,25 @@
 // L video rows followed by the sample's T text rows, packed contiguously
 // (window after window) in bf16 [rows][heads*128] by the prepare kernel.
 //
-// One CTA = (window q-tile of 128 rows, head).  Warp roles:
-//   warp 0     TMA: Q tile once, then K/V tiles into a 2-stage ring;
-//   warp 1     one thread issues tcgen05.mma: S = Q K^T (M=N=128, K=128) into
-//              one of two TMEM S buffers, O_j = P_j V_j into a TMEM O buffer;
-//   warps 2-5  softmax: one query row per thread (TMEM lane), fp32 online
-//              softmax with exp2, P written to shared memory in the 128-byte
-//              swizzled K-major layout the PV MMA reads, O accumulated in
-//              registers, then the epilogue: video rows stored straight to
-//              their source token (the scatter), text rows to a per-window
-//              fp32 partial that text_pool averages over the sample's windows.
-// Keys past the window's sequence length are masked; query rows past it are
-// computed but never stored.
+// One CTA = (window, pair of 128-row query tiles A and B, head).  K/V tiles
+// are loaded once for both query tiles.  Warp roles:
+//   warp 0     TMA: Q_A and Q_B once, then K/V tiles into a 2-stage ring;
+//   warp 1     one thread issues every tcgen05.mma, ping-ponging the tiles:
+//                S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...
+//              so the tensor core works on one tile while the other tile's
+//              softmax runs;
+//   warps 2-5  softmax of tile A, warps 6-9 softmax of tile B: one query row
+//              per thread (TMEM lane).  S is read from TMEM, P = exp2(S*c - m)
+//              is written back over S as packed bf16 and fed to the PV MMA as
+//              its TMEM A operand; O accumulates in TMEM across key tiles.
+//              The running max is only raised (and O, l rescaled in place)
+//              when it grows by more than 2^8, so most tiles skip the
+//              rescale.  S_X(j) is committed after PV_X(j-1), so O is stable
+//              whenever the softmax may rescale it.
+// Epilogue: O / l -- video rows stored straight to their source token (the
+// scatter), text rows to a per-window fp32 partial that text_pool averages
+// over the sample's windows.  Keys past the window's sequence are masked;
+// query rows past it are computed but never stored.
 #include "s2_common.cuh"
 #include "s2_internal.h"
 
@@ -25,21 +32,22 @@ namespace s2 {
 
 namespace {
 
-constexpr int HD = 128;           // head_dim
-constexpr int TILE = 128;         // q rows / keys per tile
-constexpr int CHUNK_BYTES = TILE * 128; // 128 rows x 64 bf16 (one swizzle row each)
-constexpr int TILE_BYTES = 2 * CHUNK_BYTES; // 128 x 128 bf16
-constexpr int NUM_THREADS = 192;
-constexpr int TMEM_COLS = 512; // S0 [0,128) S1 [128,256) O [256,384)
+constexpr int HD = 128;                      // head_dim
+constexpr int TILE = 128;                    // q rows / keys per tile
+constexpr int CHUNK_BYTES = TILE * 128;      // 128 rows x 64 bf16 (one swizzle row each)
+constexpr int TILE_BYTES = 2 * CHUNK_BYTES;  // 128 x 128 bf16
+constexpr int NUM_THREADS = 320;             // TMA, MMA, 2 x 4 softmax warps
+constexpr int TMEM_COLS = 512;               // S/P_A [0,128) S/P_B [128,256) O_A [256,384) O_B [384,512)
 constexpr uint32_t IDESC_S = umma_idesc_bf16(128, 128, 0, 0);
 constexpr uint32_t IDESC_O = umma_idesc_bf16(128, 128, 0, 1); // B (= V) MN-major
-constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;      // Q, K x2, V x2, P
+constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;       // Q_A, Q_B, K x2, V x2
+constexpr float RESCALE_THRESHOLD = 8.0f;                     // log2 units
 
 struct AttnArgs
 {
     const int4* win_info; // {seq_offset, L, T, partition_offset}
     const int* win_pool;  // partial row of the window's first text row
-    const int2* items;    // {window, q0}
+    const int2* items;    // {window, q0 of tile A}
     const int* video_indices;
     int inner;
     float scale_log2;
@@ -78,26 +86,84 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity)
         if (global_timer_ns() - t0 > kWaitLimitNs) break;
 }
 
+// Stores 32 output columns [col0, col0+32) of query row qi of the window.
+__device__ __forceinline__ void store_row(const AttnArgs& a, int item_window, int part_off, int L, int qi, int col0,
+                                          const float* o, float inv)
+{
+    if (qi < L)
+    {
+        const int src = a.video_indices[part_off + qi];
+        const size_t base = (size_t)src * a.inner + col0;
+        if (a.out_f32)
+        {
+            float* dst = reinterpret_cast<float*>(a.video_out) + base;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+            {
+                float4 w = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+                if (a.round_bf16)
+                {
+                    w.x = bf16_round_f32(w.x);
+                    w.y = bf16_round_f32(w.y);
+                    w.z = bf16_round_f32(w.z);
+                    w.w = bf16_round_f32(w.w);
+                }
+                *reinterpret_cast<float4*>(dst + i) = w;
+            }
+        }
+        else
+        {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.video_out) + base;
+#pragma unroll
+            for (int i = 0; i < 32; i += 8)
+            {
+                uint4 p;
+                p.x = pack_bf16x2(o[i] * inv, o[i + 1] * inv);
+                p.y = pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv);
+                p.z = pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv);
+                p.w = pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv);
+                *reinterpret_cast<uint4*>(dst + i) = p;
+            }
+        }
+    }
+    else
+    {
+        float* dst = a.text_partial + (size_t)(a.win_pool[item_window] + (qi - L)) * a.inner + col0;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+        {
+            float4 w = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+            if (a.round_bf16)
+            {
+                w.x = bf16_round_f32(w.x);
+                w.y = bf16_round_f32(w.y);
+                w.z = bf16_round_f32(w.z);
+                w.w = bf16_round_f32(w.w);
+            }
+            *reinterpret_cast<float4*>(dst + i) = w;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     window_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                             const __grid_constant__ CUtensorMap tv, const AttnArgs args)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem;
-    uint8_t* sK = sQ + TILE_BYTES;     // 2 stages
+    uint8_t* sQ = smem;                // Q_A, Q_B
+    uint8_t* sK = sQ + 2 * TILE_BYTES; // 2 stages
     uint8_t* sV = sK + 2 * TILE_BYTES; // 2 stages
-    uint8_t* sP = sV + 2 * TILE_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + TILE_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * TILE_BYTES);
     uint64_t* q_full = bars + 0;
-    uint64_t* k_full = bars + 1;  // [2]
-    uint64_t* v_full = bars + 3;  // [2]
+    uint64_t* k_full = bars + 1;   // [2]
+    uint64_t* v_full = bars + 3;   // [2]
     uint64_t* kv_empty = bars + 5; // [2]
-    uint64_t* s_full = bars + 7;  // [2]
-    uint64_t* p_full = bars + 9;
-    uint64_t* o_full = bars + 10;
-    uint64_t* drain = bars + 11;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    uint64_t* s_full = bars + 7;   // [2] per query tile
+    uint64_t* p_full = bars + 9;   // [2] per query tile
+    uint64_t* o_done = bars + 11;  // [2] per query tile
+    uint64_t* drain = bars + 13;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -108,6 +174,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int seq_off = wi.x, L = wi.y, T = wi.z, part_off = wi.w;
     const int S_len = L + T;
     const int q0 = item.y;
+    const bool has_b = q0 + TILE < S_len;
     const int nkv = (S_len + TILE - 1) / TILE;
 
     if (threadIdx.x == 0)
@@ -119,9 +186,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(&v_full[s], 1);
             mbar_init(&kv_empty[s], 1);
             mbar_init(&s_full[s], 1);
+            mbar_init(&p_full[s], 128);
+            mbar_init(&o_done[s], 1);
         }
-        mbar_init(p_full, 128);
-        mbar_init(o_full, 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbarrier_init();
@@ -136,14 +203,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     {
         if (lane == 0)
         {
+            // ---------------- TMA producer
             const int x0 = head * HD;
-            bool issued_q = false;
             int issued_stage[2] = {0, 0};
             uint32_t last_parity[2] = {0, 0};
-            mbar_arrive_expect_tx(q_full, TILE_BYTES);
+            mbar_arrive_expect_tx(q_full, has_b ? 2 * TILE_BYTES : TILE_BYTES);
             tma_load_2d(sQ, &tq, q_full, x0, seq_off + q0);
             tma_load_2d(sQ + CHUNK_BYTES, &tq, q_full, x0 + 64, seq_off + q0);
-            issued_q = true;
+            if (has_b)
+            {
+                tma_load_2d(sQ + TILE_BYTES, &tq, q_full, x0, seq_off + q0 + TILE);
+                tma_load_2d(sQ + TILE_BYTES + CHUNK_BYTES, &tq, q_full, x0 + 64, seq_off + q0 + TILE);
+            }
             for (int j = 0; j < nkv; j++)
             {
                 const int st = j & 1;
@@ -161,7 +232,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             if (*abort_flag)
             {
-                if (issued_q) drain_wait(q_full, 0);
+                drain_wait(q_full, 0);
                 for (int s = 0; s < 2; s++)
                     if (issued_stage[s])
                     {
@@ -175,13 +246,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     {
         if (lane == 0)
         {
+            // ---------------- MMA issuer
             bool any = false;
-            const uint32_t q_addr = smem_u32(sQ);
-            const uint32_t p_addr = smem_u32(sP);
-            auto issue_s = [&](int j) {
-                const int st = j & 1;
-                const uint32_t k_addr = smem_u32(sK + st * TILE_BYTES);
-                const uint32_t d = tmem + st * 128;
+            const int ntiles = has_b ? 2 : 1;
+            auto issue_s = [&](int x, int j) {
+                const uint32_t q_addr = smem_u32(sQ + x * TILE_BYTES);
+                const uint32_t k_addr = smem_u32(sK + (j & 1) * TILE_BYTES);
+                const uint32_t d = tmem + x * 128;
 #pragma unroll
                 for (int k = 0; k < HD / 16; k++)
                 {
@@ -189,39 +260,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     umma_bf16(d, umma_desc_sw128(q_addr + off, 16, 1024), umma_desc_sw128(k_addr + off, 16, 1024),
                               IDESC_S, k != 0);
                 }
-                umma_commit(&s_full[st]);
+                umma_commit(&s_full[x]);
+            };
+            auto issue_pv = [&](int x, int j) {
+                const uint32_t v_addr = smem_u32(sV + (j & 1) * TILE_BYTES);
+                const uint32_t p_tmem = tmem + x * 128; // P packed bf16x2 over S columns [0,64)
+                const uint32_t o_tmem = tmem + 256 + x * 128;
+#pragma unroll
+                for (int k = 0; k < TILE / 16; k++)
+                    umma_bf16_tmem_a(o_tmem, p_tmem + k * 8, umma_desc_sw128(v_addr + k * 16 * 128, CHUNK_BYTES, 1024),
+                                     IDESC_O, (j | k) != 0);
             };
             do
             {
                 if (!mbar_wait(q_full, 0, abort_flag, args.status)) break;
                 if (!mbar_wait(&k_full[0], 0, abort_flag, args.status)) break;
                 tc_fence_after();
-                issue_s(0);
+                for (int x = 0; x < ntiles; x++) issue_s(x, 0);
                 any = true;
-                for (int j = 0; j < nkv; j++)
+                bool ok = true;
+                for (int j = 0; j < nkv && ok; j++)
                 {
                     const int st = j & 1;
-                    const uint32_t par = (j >> 1) & 1;
-                    if (j + 1 < nkv)
+                    if (!mbar_wait(&v_full[st], (j >> 1) & 1, abort_flag, args.status)) break;
+                    const bool more = j + 1 < nkv;
+                    if (more && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, args.status)) break;
+                    for (int x = 0; x < ntiles; x++)
                     {
-                        if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, args.status)) break;
+                        if (!mbar_wait(&p_full[x], j & 1, abort_flag, args.status))
+                        {
+                            ok = false;
+                            break;
+                        }
                         tc_fence_after();
-                        issue_s(j + 1);
+                        issue_pv(x, j);
+                        if (!more) umma_commit(&o_done[x]);
+                        if (x == ntiles - 1) umma_commit(&kv_empty[st]);
+                        if (more) issue_s(x, j + 1);
                     }
-                    if (!mbar_wait(p_full, j & 1, abort_flag, args.status)) break;
-                    if (!mbar_wait(&v_full[st], par, abort_flag, args.status)) break;
-                    tc_fence_after();
-                    const uint32_t v_addr = smem_u32(sV + st * TILE_BYTES);
-#pragma unroll
-                    for (int k = 0; k < TILE / 16; k++)
-                    {
-                        const uint32_t a_off = (k >> 2) * CHUNK_BYTES + (k & 3) * 32;
-                        const uint32_t b_off = k * 16 * 128;
-                        umma_bf16(tmem + 256, umma_desc_sw128(p_addr + a_off, 16, 1024),
-                                  umma_desc_sw128(v_addr + b_off, CHUNK_BYTES, 1024), IDESC_O, k != 0);
-                    }
-                    umma_commit(o_full);
-                    umma_commit(&kv_empty[st]);
                 }
             } while (0);
             if (any)
@@ -233,146 +309,103 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     else
     {
-        // softmax + epilogue warps
+        // ---------------- softmax + epilogue (warps 2-5: tile A, 6-9: tile B)
+        const int x = (warp - 2) >> 2;
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-        float o_acc[HD];
-#pragma unroll
-        for (int i = 0; i < HD; i++) o_acc[i] = 0.f;
-        float m_run = -INFINITY;
-        float l_run = 0.f;
-        bool ok = true;
-        for (int j = 0; j < nkv && ok; j++)
+        const uint32_t s_addr = tmem + lane_base + x * 128;
+        const uint32_t o_addr = tmem + lane_base + 256 + x * 128;
+        const int qbase = q0 + x * TILE;
+        if (x == 0 || has_b)
         {
-            const int st = j & 1;
-            if (!warp_wait(&s_full[st], (j >> 1) & 1, abort_flag, args.status))
+            float m_used = -INFINITY;
+            float l_run = 0.f;
+            bool ok = true;
+            for (int j = 0; j < nkv; j++)
             {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const int valid = S_len - j * TILE; // >= 1
-            const uint32_t s_addr = tmem + lane_base + st * 128;
-            float mx = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < 4; c++)
-            {
-                uint32_t v[32];
-                tmem_ld32(s_addr + c * 32, v);
-                tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 32; i++)
-                    if (c * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(v[i]));
-            }
-            const float m_new = fmaxf(m_run, mx * args.scale_log2);
-            const float alpha = ex2(m_run - m_new); // m_run = -inf on the first tile -> 0
-            float rowsum = 0.f;
-#pragma unroll
-            for (int c = 0; c < 4; c++)
-            {
-                uint32_t v[32];
-                tmem_ld32(s_addr + c * 32, v);
-                tmem_ld_wait();
-                uint32_t packed[16];
-#pragma unroll
-                for (int i = 0; i < 32; i += 2)
+                if (!warp_wait(&s_full[x], j & 1, abort_flag, args.status))
                 {
-                    const float p0 = (c * 32 + i < valid) ? ex2(__uint_as_float(v[i]) * args.scale_log2 - m_new) : 0.f;
-                    const float p1 =
-                        (c * 32 + i + 1 < valid) ? ex2(__uint_as_float(v[i + 1]) * args.scale_log2 - m_new) : 0.f;
-                    rowsum += p0 + p1;
-                    packed[i >> 1] = pack_bf16x2(p0, p1);
+                    ok = false;
+                    break;
                 }
-                // columns c*32 .. c*32+31 = chunk c/2, 16-byte units (c%2)*4 .. +3
-                uint8_t* prow = sP + (c >> 1) * CHUNK_BYTES + row * 128;
+                tc_fence_after();
+                const int valid = S_len - j * TILE; // >= 1
+                float mx = -INFINITY;
 #pragma unroll
-                for (int u = 0; u < 4; u++)
+                for (int c = 0; c < 4; c++)
                 {
-                    const int unit = (c & 1) * 4 + u;
-                    *reinterpret_cast<uint4*>(prow + ((unit ^ (row & 7)) << 4)) =
-                        make_uint4(packed[u * 4], packed[u * 4 + 1], packed[u * 4 + 2], packed[u * 4 + 3]);
+                    uint32_t v[32];
+                    tmem_ld32(s_addr + c * 32, v);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; i++)
+                        if (c * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(v[i]));
                 }
-            }
-            l_run = l_run * alpha + rowsum;
-            m_run = m_new;
-            fence_proxy_async_smem();
-            tc_fence_before();
-            mbar_arrive(p_full);
-            if (!warp_wait(o_full, j & 1, abort_flag, args.status))
-            {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < 4; c++)
-            {
-                uint32_t v[32];
-                tmem_ld32(tmem + lane_base + 256 + c * 32, v);
-                tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 32; i++) o_acc[c * 32 + i] = o_acc[c * 32 + i] * alpha + __uint_as_float(v[i]);
-            }
-            tc_fence_before();
-        }
-        const int qi = q0 + row;
-        if (ok && qi < S_len)
-        {
-            const float inv = 1.f / l_run;
-            if (qi < L)
-            {
-                const int src = args.video_indices[part_off + qi];
-                const size_t base = (size_t)src * args.inner + head * HD;
-                if (args.out_f32)
+                const float mt = mx * args.scale_log2;
+                if (j == 0)
+                    m_used = mt;
+                else if (mt > m_used + RESCALE_THRESHOLD)
                 {
-                    float* o = reinterpret_cast<float*>(args.video_out) + base;
+                    // O is stable here: S_X(j) was committed after PV_X(j-1).
+                    const float alpha = ex2(m_used - mt);
 #pragma unroll
-                    for (int i = 0; i < HD; i += 4)
+                    for (int c = 0; c < 4; c++)
                     {
-                        float4 w = make_float4(o_acc[i] * inv, o_acc[i + 1] * inv, o_acc[i + 2] * inv,
-                                               o_acc[i + 3] * inv);
-                        if (args.round_bf16)
-                        {
-                            w.x = bf16_round_f32(w.x);
-                            w.y = bf16_round_f32(w.y);
-                            w.z = bf16_round_f32(w.z);
-                            w.w = bf16_round_f32(w.w);
-                        }
-                        *reinterpret_cast<float4*>(o + i) = w;
-                    }
-                }
-                else
-                {
-                    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(args.video_out) + base;
+                        uint32_t v[32];
+                        tmem_ld32(o_addr + c * 32, v);
+                        tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < HD; i += 8)
-                    {
-                        uint4 p;
-                        p.x = pack_bf16x2(o_acc[i] * inv, o_acc[i + 1] * inv);
-                        p.y = pack_bf16x2(o_acc[i + 2] * inv, o_acc[i + 3] * inv);
-                        p.z = pack_bf16x2(o_acc[i + 4] * inv, o_acc[i + 5] * inv);
-                        p.w = pack_bf16x2(o_acc[i + 6] * inv, o_acc[i + 7] * inv);
-                        *reinterpret_cast<uint4*>(o + i) = p;
+                        for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+                        tmem_st32(o_addr + c * 32, v);
                     }
+                    l_run *= alpha;
+                    m_used = mt;
                 }
+                float rowsum = 0.f;
+#pragma unroll
+                for (int c = 0; c < 4; c++)
+                {
+                    uint32_t v[32];
+                    tmem_ld32(s_addr + c * 32, v);
+                    tmem_ld_wait();
+                    uint32_t packed[16];
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2)
+                    {
+                        const float p0 =
+                            (c * 32 + i < valid) ? ex2(__uint_as_float(v[i]) * args.scale_log2 - m_used) : 0.f;
+                        const float p1 =
+                            (c * 32 + i + 1 < valid) ? ex2(__uint_as_float(v[i + 1]) * args.scale_log2 - m_used) : 0.f;
+                        rowsum += p0 + p1;
+                        packed[i >> 1] = pack_bf16x2(p0, p1);
+                    }
+                    // P columns [c*16, c*16+16): S columns already consumed.
+                    tmem_st16(s_addr + c * 16, packed);
+                }
+                l_run += rowsum;
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(&p_full[x]);
             }
-            else
+            if (ok && warp_wait(&o_done[x], 0, abort_flag, args.status))
             {
-                float* o = args.text_partial + (size_t)(args.win_pool[item.x] + (qi - L)) * args.inner + head * HD;
-#pragma unroll
-                for (int i = 0; i < HD; i += 4)
+                tc_fence_after();
+                const int qi = qbase + row;
+                const float inv = 1.f / l_run;
+#pragma unroll 1
+                for (int c = 0; c < 4; c++)
                 {
-                    float4 w = make_float4(o_acc[i] * inv, o_acc[i + 1] * inv, o_acc[i + 2] * inv,
-                                           o_acc[i + 3] * inv);
-                    if (args.round_bf16)
+                    uint32_t v[32];
+                    tmem_ld32(o_addr + c * 32, v);
+                    tmem_ld_wait();
+                    if (qi < S_len)
                     {
-                        w.x = bf16_round_f32(w.x);
-                        w.y = bf16_round_f32(w.y);
-                        w.z = bf16_round_f32(w.z);
-                        w.w = bf16_round_f32(w.w);
+                        float o[32];
+#pragma unroll
+                        for (int i = 0; i < 32; i++) o[i] = __uint_as_float(v[i]);
+                        store_row(args, item.x, part_off, L, qi, head * HD + c * 32, o, inv);
                     }
-                    *reinterpret_cast<float4*>(o + i) = w;
                 }
             }
         }

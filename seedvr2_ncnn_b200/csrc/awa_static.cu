@@ -211,7 +211,7 @@ int walk(const s2_awa_params* p, const int* shapes, const int* tl, int batch, La
                             T[L.o_pos + 3 * (size_t)row + 2] = j;
                         }
                     }
-                    ni += ceil_div(Lw + tl[s], 128);
+                    ni += ceil_div(Lw + tl[s], 256);
                     seq += Lw + tl[s];
                     pool += tl[s];
                     n += Lw;
@@ -254,7 +254,7 @@ int walk(const s2_awa_params* p, const int* shapes, const int* tl, int batch, La
         {
             const int S = T[L.o_win + 4 * w + 1] + T[L.o_win + 4 * w + 2];
             if (ceil_div(S, 128) != cost) continue;
-            for (int q0 = 0; q0 < S; q0 += 128, k++)
+            for (int q0 = 0; q0 < S; q0 += 256, k++)
             {
                 T[L.o_items + 2 * (size_t)k] = w;
                 T[L.o_items + 2 * (size_t)k + 1] = q0;

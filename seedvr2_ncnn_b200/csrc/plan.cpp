@@ -196,7 +196,7 @@ int build_schedule(const Plan& plan, const int* text_lengths, AttnSchedule& s, c
         const int S = L + T;
         const int ntiles = (S + 127) / 128;
         s.attn_flops_per_head += 4.0 * S * (double)S * 128.0;
-        for (int q0 = 0; q0 < S; q0 += 128)
+        for (int q0 = 0; q0 < S; q0 += 256) // one item = a pair of 128-row query tiles
         {
             items.push_back(make_int2(w, q0));
             item_cost.push_back(ntiles);

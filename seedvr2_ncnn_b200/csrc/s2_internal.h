@@ -105,7 +105,7 @@ struct AttnSchedule
 {
     int num_windows = 0;
     int packed_rows = 0;    // sum over windows of (L_w + T_s)
-    int num_items = 0;      // q-tiles (window, q0) in longest-first order
+    int num_items = 0;      // query-tile pairs (window, q0; 256 rows) in longest-first order
     int total_text = 0;
     int max_text = 0;
     // device arrays
@@ -113,7 +113,7 @@ struct AttnSchedule
     int* row_pos = nullptr;    // [packed_rows][3] rope positions
     int4* win_info = nullptr;  // [nw] {seq_offset, L, T, partition_offset}
     int* win_pool = nullptr;   // [nw] partial-row offset of the window's text rows
-    int2* items = nullptr;     // [num_items] {window, q0}
+    int2* items = nullptr;     // [num_items] {window, q0 of the first of two 128-row tiles}
     int* video_indices = nullptr; // [n]
     int4* text_reduce = nullptr;  // [total_text] {first partial row, stride (T), count (nw_s), 0}
     float* text_scale = nullptr;  // [total_text] 1/nw_s
