@@ -65,6 +65,144 @@ __device__ __forceinline__ float ex2(float x)
     return y;
 }
 
+// Packed fp32 pairs (sm_100 f32x2 FMA / ADD) and a 3-input max.
+__device__ __forceinline__ uint64_t pk2(uint32_t lo, uint32_t hi)
+{
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+
+__device__ __forceinline__ void upk2(uint64_t v, float& lo, float& hi)
+{
+    uint32_t a, b;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(a), "=r"(b) : "l"(v));
+    lo = __uint_as_float(a);
+    hi = __uint_as_float(b);
+}
+
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// 2^x on the FMA and integer pipes, for a share of the softmax exponentials
+// so the MUFU unit (ex2.approx) is not the only source: x = j + f with
+// j = round(x) (the 1.5*2^23 shift trick, f in [-1/2, 1/2]), 2^f from a cubic
+// fitted for this kernel (weighted least squares iterated toward minimum
+// relative error on [-1/2, 1/2]; max relative error 7.5e-5, far below the
+// 2^-9 of the bf16 P it feeds), and 2^j added into the exponent field.
+// x is clamped at -125 (2^-125 is 0 for softmax purposes) so the exponent
+// add stays in the normal range.
+constexpr uint64_t kMagic2 = 0x4B4000004B400000ull;    // 1.5*2^23 (x2)
+constexpr uint64_t kNegMagic2 = 0xCB400000CB400000ull; // -1.5*2^23
+constexpr uint64_t kNegOne2 = 0xBF800000BF800000ull;   // -1
+constexpr uint64_t kC0 = 0x3F7FFB4A3F7FFB4Aull;        // 0.99992812
+constexpr uint64_t kC1 = 0x3F31798D3F31798Dull;        // 0.69326097
+constexpr uint64_t kC2 = 0x3E786EE63E786EE6ull;        // 0.24261054
+constexpr uint64_t kC3 = 0x3D61FB533D61FB53ull;        // 0.05517132
+
+__device__ __forceinline__ void ex2_poly(uint64_t t2, float& p0, float& p1)
+{
+    float x0, x1;
+    upk2(t2, x0, x1);
+    const uint64_t x2 = pk2(__float_as_uint(fmaxf(x0, -125.f)), __float_as_uint(fmaxf(x1, -125.f)));
+    const uint64_t r2 = fadd2(x2, kMagic2);
+    const uint64_t f2 = ffma2(fadd2(r2, kNegMagic2), kNegOne2, x2);
+    uint64_t q2 = ffma2(f2, kC3, kC2);
+    q2 = ffma2(q2, f2, kC1);
+    q2 = ffma2(q2, f2, kC0);
+    float q0, q1, r0, r1;
+    upk2(q2, q0, q1);
+    upk2(r2, r0, r1);
+    p0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(r0) << 23));
+    p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(r1) << 23));
+}
+
+// Row max of the 128 raw scores of one key tile (FULL: no masked columns).
+template <bool FULL>
+__device__ __forceinline__ float row_max(const uint32_t (&v)[128], int valid)
+{
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 128; i += 2)
+    {
+        float a = __uint_as_float(v[i]), b = __uint_as_float(v[i + 1]);
+        if (!FULL)
+        {
+            a = i < valid ? a : -INFINITY;
+            b = i + 1 < valid ? b : -INFINITY;
+        }
+        mx = fmax3(mx, a, b);
+    }
+    return mx;
+}
+
+// P = exp2(S * c - m) for the row (masked columns -> 0), written over the
+// first 64 TMEM columns of the S tile as packed bf16 pairs; returns the fp32
+// row sum.  In full tiles 3 of every 8 pairs use the polynomial exp2.
+template <bool FULL>
+__device__ __forceinline__ float row_exp(const uint32_t (&v)[128], int valid, uint64_t c2, uint64_t negm2,
+                                         uint32_t s_addr)
+{
+    uint64_t sum2 = 0;
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+    {
+        uint32_t packed[16];
+#pragma unroll
+        for (int q = 0; q < 16; q++)
+        {
+            const int i = c * 32 + 2 * q;
+            const uint64_t t2 = ffma2(pk2(v[i], v[i + 1]), c2, negm2);
+            float p0, p1;
+            if (FULL && (q & 7) < 3)
+                ex2_poly(t2, p0, p1);
+            else
+            {
+                float t0, t1;
+                upk2(t2, t0, t1);
+                p0 = ex2(t0);
+                p1 = ex2(t1);
+                if (!FULL)
+                {
+                    p0 = i < valid ? p0 : 0.f;
+                    p1 = i + 1 < valid ? p1 : 0.f;
+                }
+            }
+            sum2 = fadd2(sum2, pk2(__float_as_uint(p0), __float_as_uint(p1)));
+            packed[q] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(s_addr + c * 16, packed);
+    }
+    float lo, hi;
+    upk2(sum2, lo, hi);
+    return lo + hi;
+}
+
+__device__ __forceinline__ void st_v8(void* p, const uint32_t (&r)[8])
+{
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(r[0]), "r"(r[1]), "r"(r[2]),
+                 "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+
 __device__ __forceinline__ float bf16_round_f32(float x)
 {
     return __bfloat162float(__float2bfloat16_rn(x));
@@ -86,62 +224,41 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity)
         if (global_timer_ns() - t0 > kWaitLimitNs) break;
 }
 
-// Stores 32 output columns [col0, col0+32) of query row qi of the window.
+// Stores 32 output columns [col0, col0+32) of query row qi of the window with
+// 32-byte (full-sector) stores: video rows to their source token, text rows
+// to the window's fp32 partial.
 __device__ __forceinline__ void store_row(const AttnArgs& a, int item_window, int part_off, int L, int qi, int col0,
                                           const float* o, float inv)
 {
-    if (qi < L)
+    const bool video = qi < L;
+    if (video && !a.out_f32)
     {
         const int src = a.video_indices[part_off + qi];
-        const size_t base = (size_t)src * a.inner + col0;
-        if (a.out_f32)
-        {
-            float* dst = reinterpret_cast<float*>(a.video_out) + base;
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.video_out) + (size_t)src * a.inner + col0;
 #pragma unroll
-            for (int i = 0; i < 32; i += 4)
-            {
-                float4 w = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
-                if (a.round_bf16)
-                {
-                    w.x = bf16_round_f32(w.x);
-                    w.y = bf16_round_f32(w.y);
-                    w.z = bf16_round_f32(w.z);
-                    w.w = bf16_round_f32(w.w);
-                }
-                *reinterpret_cast<float4*>(dst + i) = w;
-            }
-        }
-        else
+        for (int i = 0; i < 32; i += 16)
         {
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.video_out) + base;
+            uint32_t r[8];
 #pragma unroll
-            for (int i = 0; i < 32; i += 8)
-            {
-                uint4 p;
-                p.x = pack_bf16x2(o[i] * inv, o[i + 1] * inv);
-                p.y = pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv);
-                p.z = pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv);
-                p.w = pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv);
-                *reinterpret_cast<uint4*>(dst + i) = p;
-            }
+            for (int k = 0; k < 8; k++) r[k] = pack_bf16x2(o[i + 2 * k] * inv, o[i + 2 * k + 1] * inv);
+            st_v8(dst + i, r);
         }
+        return;
     }
-    else
-    {
-        float* dst = a.text_partial + (size_t)(a.win_pool[item_window] + (qi - L)) * a.inner + col0;
+    float* dst = video ? reinterpret_cast<float*>(a.video_out) + (size_t)a.video_indices[part_off + qi] * a.inner + col0
+                       : a.text_partial + (size_t)(a.win_pool[item_window] + (qi - L)) * a.inner + col0;
 #pragma unroll
-        for (int i = 0; i < 32; i += 4)
+    for (int i = 0; i < 32; i += 8)
+    {
+        uint32_t r[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++)
         {
-            float4 w = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
-            if (a.round_bf16)
-            {
-                w.x = bf16_round_f32(w.x);
-                w.y = bf16_round_f32(w.y);
-                w.z = bf16_round_f32(w.z);
-                w.w = bf16_round_f32(w.w);
-            }
-            *reinterpret_cast<float4*>(dst + i) = w;
+            float w = o[i + k] * inv;
+            if (a.round_bf16) w = bf16_round_f32(w);
+            r[k] = __float_as_uint(w);
         }
+        st_v8(dst + i, r);
     }
 }
 
@@ -331,17 +448,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 tc_fence_after();
                 const int valid = S_len - j * TILE; // >= 1
-                float mx = -INFINITY;
-#pragma unroll
-                for (int c = 0; c < 4; c++)
-                {
-                    uint32_t v[32];
-                    tmem_ld32(s_addr + c * 32, v);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int i = 0; i < 32; i++)
-                        if (c * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(v[i]));
-                }
+                const bool full = valid >= TILE;
+                uint32_t v[128];
+                tmem_ld128(s_addr, v);
+                tmem_ld_wait();
+                const float mx = full ? row_max<true>(v, valid) : row_max<false>(v, valid);
                 const float mt = mx * args.scale_log2;
                 if (j == 0)
                     m_used = mt;
@@ -352,37 +463,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                     for (int c = 0; c < 4; c++)
                     {
-                        uint32_t v[32];
-                        tmem_ld32(o_addr + c * 32, v);
+                        uint32_t o[32];
+                        tmem_ld32(o_addr + c * 32, o);
                         tmem_ld_wait();
 #pragma unroll
-                        for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-                        tmem_st32(o_addr + c * 32, v);
+                        for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_st32(o_addr + c * 32, o);
                     }
                     l_run *= alpha;
                     m_used = mt;
                 }
-                float rowsum = 0.f;
-#pragma unroll
-                for (int c = 0; c < 4; c++)
-                {
-                    uint32_t v[32];
-                    tmem_ld32(s_addr + c * 32, v);
-                    tmem_ld_wait();
-                    uint32_t packed[16];
-#pragma unroll
-                    for (int i = 0; i < 32; i += 2)
-                    {
-                        const float p0 =
-                            (c * 32 + i < valid) ? ex2(__uint_as_float(v[i]) * args.scale_log2 - m_used) : 0.f;
-                        const float p1 =
-                            (c * 32 + i + 1 < valid) ? ex2(__uint_as_float(v[i + 1]) * args.scale_log2 - m_used) : 0.f;
-                        rowsum += p0 + p1;
-                        packed[i >> 1] = pack_bf16x2(p0, p1);
-                    }
-                    // P columns [c*16, c*16+16): S columns already consumed.
-                    tmem_st16(s_addr + c * 16, packed);
-                }
+                const uint64_t c2 = pk2(__float_as_uint(args.scale_log2), __float_as_uint(args.scale_log2));
+                const uint64_t negm2 = pk2(__float_as_uint(-m_used), __float_as_uint(-m_used));
+                const float rowsum = full ? row_exp<true>(v, valid, c2, negm2, s_addr)
+                                          : row_exp<false>(v, valid, c2, negm2, s_addr);
                 l_run += rowsum;
                 tmem_st_wait();
                 tc_fence_before();
@@ -423,6 +517,9 @@ int launch_window_attention(Context& ctx, const AttnSchedule& s, int heads, cons
                             const void* v, int out_f32, int round_bf16, void* video_out, float* text_partial)
 {
     if (s.num_items <= 0) return S2_OK;
+    // The epilogue writes 32-byte vectors straight into the output rows.
+    if ((reinterpret_cast<uintptr_t>(video_out) & 31) || (reinterpret_cast<uintptr_t>(text_partial) & 31))
+        return S2_ERR_INVALID;
     const int inner = heads * HD;
     CUtensorMap mq, mk, mv;
     int r = make_tmap_bf16_2d(&mq, q, inner, s.packed_rows, (uint64_t)inner * 2, 64, TILE);

@@ -171,7 +171,9 @@ __global__ void text_pool_kernel(const int4* __restrict__ reduce, const float* _
 
 // ---------------------------------------------------------------- ada_rmsnorm
 // y = x * (1/sqrt(mean(x^2) + eps)) * scale + shift -> bf16; one warp per row,
-// 8 dims per lane per step.
+// 8 dims per lane per step.  G = D / 256 steps are held in registers so x is
+// read from HBM once (G = 0: generic two-pass form for other widths).
+template <int G>
 __global__ void ada_rmsnorm_kernel(int rows, int D, const float* __restrict__ x, float eps,
                                    const float* __restrict__ shift, const float* __restrict__ scale,
                                    __nv_bfloat16* __restrict__ y)
@@ -180,7 +182,34 @@ __global__ void ada_rmsnorm_kernel(int rows, int D, const float* __restrict__ x,
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
     const float* xr = x + (int64_t)row * D;
+    __nv_bfloat16* yr = y + (int64_t)row * D;
     float ss = 0.f;
+    if (G > 0)
+    {
+        float v[G > 0 ? G : 1][8];
+#pragma unroll
+        for (int g = 0; g < G; g++)
+        {
+            load8<float>(xr + g * 256 + lane * 8, v[g]);
+#pragma unroll
+            for (int i = 0; i < 8; i++) ss += v[g][i] * v[g][i];
+        }
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+        const float inv = 1.f / sqrtf(ss / D + eps);
+#pragma unroll
+        for (int g = 0; g < G; g++)
+        {
+            const int c = g * 256 + lane * 8;
+            float sc[8], sh[8];
+            load8<float>(scale + c, sc);
+            load8<float>(shift + c, sh);
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[g][i] = v[g][i] * inv * sc[i] + sh[i];
+            store8_bf16(yr + c, v[g]);
+        }
+        return;
+    }
     for (int c = lane * 8; c < D; c += 256)
     {
         float v[8];
@@ -191,7 +220,6 @@ __global__ void ada_rmsnorm_kernel(int rows, int D, const float* __restrict__ x,
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
     const float inv = 1.f / sqrtf(ss / D + eps);
-    __nv_bfloat16* yr = y + (int64_t)row * D;
     for (int c = lane * 8; c < D; c += 256)
     {
         float v[8], sc[8], sh[8];
@@ -314,8 +342,18 @@ int launch_ada_rmsnorm(Context& ctx, int rows, int D, const float* x, float eps,
     if (rows == 0) return S2_OK;
     const int warps = 8;
     ProfileScope prof(ctx, K_NORM, 0.0, (double)rows * D * 6.0);
-    ada_rmsnorm_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, ctx.stream>>>(rows, D, x, eps, shift, scale,
-                                                                                (__nv_bfloat16*)out);
+    const dim3 grid((rows + warps - 1) / warps), block(warps * 32);
+    __nv_bfloat16* y = (__nv_bfloat16*)out;
+    switch (D)
+    {
+    case 2560: ada_rmsnorm_kernel<10><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
+    case 3072: ada_rmsnorm_kernel<12><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
+    case 1536: ada_rmsnorm_kernel<6><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
+    case 1024: ada_rmsnorm_kernel<4><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
+    case 512: ada_rmsnorm_kernel<2><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
+    case 256: ada_rmsnorm_kernel<1><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
+    default: ada_rmsnorm_kernel<0><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
+    }
     return finish(ctx);
 }
 
