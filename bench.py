@@ -228,27 +228,50 @@ def main():
 
     torch.cuda.set_device(local_rank)
     if world > 1:
-        import torch.distributed as dist
-
         from datetime import timedelta
 
+        import torch.distributed as dist
+
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     ctx = abi.Context(local_rank)
+    sharded = world > 1
+    if sharded:
+        # NCCL communicator of the library (its own, next to torch's process group)
+        uid = [abi.dist_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        abi.dist_init(ctx, uid[0], rank, world, 120000)
     dit = abi.Dit(ctx, num_blocks=args.blocks, hidden=D, heads=HEADS, head_dim=HD, mlp_hidden=F, rope_pairs=PAIRS,
                   window=window, window_mode=mode)
     dit.init_random(1234)
-    g = torch.Generator(device="cuda").manual_seed(100 + rank)
-    x0 = torch.randn(M, D, device="cuda", generator=g)
+    g = torch.Generator(device="cuda").manual_seed(100)
+    x_global = torch.randn(M, D, device="cuda", generator=g)
     mod = torch.randn(6, D, device="cuda", generator=g)
+    if sharded:
+        sh = abi.shard(shape, TEXT, window, mode, rank, world)
+        local = torch.from_numpy(sh["local_tokens"].astype("int64")).cuda()
+        x0 = torch.cat([x_global[local], x_global[nv:]]).contiguous()
+        n_local = int(local.numel())
+    else:
+        x0 = x_global
+        n_local = nv
+    del x_global
     x = torch.empty_like(x0)
     stream = torch.cuda.current_stream()
 
+    def forward(buf):
+        if sharded:
+            dit.forward_sharded(shape, TEXT, buf, mod)
+        else:
+            dit.forward(shape, TEXT, buf, mod)
+
     def step():
         x.copy_(x0)
-        dit.forward(shape, TEXT, x, mod)
+        forward(x)
 
     def barrier():
-        if world > 1:
+        if sharded:
+            abi.dist_sync(ctx)  # bounded wait; aborts the communicator on expiry
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
@@ -277,24 +300,36 @@ def main():
     counters = ctx.counters()
     ctx.profile(False)
     clk = clocks.stop()
-    if world > 1:
+    if sharded:
         t = torch.tensor([ms], device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
-    value = world * M / (ms / 1000.0)
+    value = M / (ms / 1000.0)
 
-    # end to end through the host-buffer entry point (pinned host memory)
+    # end to end with host buffers (pinned): H2D of this rank's rows and the
+    # modulation, the forward, D2H of the result -- inside the timed region
     e2e_ms = float("nan")
-    hv = x0[:nv].cpu().pin_memory()
-    ht = x0[nv:].cpu().pin_memory()
-    hm = mod.reshape(6, 1, D).cpu().pin_memory()
-    ov = torch.empty_like(hv).pin_memory()
-    ot = torch.empty_like(ht).pin_memory()
-
-    def e2e_step():
-        dit.forward_host([shape], [TEXT], hv, ht, hm, ov, ot)
-
     if not args.no_e2e:
+        hx = x0.cpu().pin_memory()
+        hm = mod.cpu().pin_memory()
+        hout = torch.empty_like(hx).pin_memory()
+        if sharded:
+            dx = torch.empty_like(x0)
+            dm = torch.empty_like(mod)
+
+            def e2e_step():
+                dx.copy_(hx, non_blocking=True)
+                dm.copy_(hm, non_blocking=True)
+                forward(dx)
+                hout.copy_(dx, non_blocking=True)
+        else:
+            hv, ht = hx[:nv], hx[nv:]
+            ov, ot = hout[:nv], hout[nv:]
+            hm3 = hm.reshape(6, 1, D)
+
+            def e2e_step():
+                dit.forward_host([shape], [TEXT], hv, ht, hm3, ov, ot)
+
         e2e_step()
         barrier()
         e2e_steps = max(1, min(args.steps, 5))
@@ -304,10 +339,10 @@ def main():
         e1.record(stream)
         barrier()
         e2e_ms = e0.elapsed_time(e1) / e2e_steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+        if sharded:
+            t = torch.tensor([e2e_ms], device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            e2e_ms = float(t.item())
     status = ctx.status()
 
     peaks = load_peaks()
@@ -335,24 +370,27 @@ def main():
     result = {
         "metric": "DiT tokens/sec/GPU (32-block step)", "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) tokens and "
+        "scaling": "strong" if sharded else "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) tokens and "
         "modulation, N(0,0.02) random-init weights)",
         "config": {"workload": desc, "config": args.config, "video_tokens": nv, "text_tokens": TEXT,
                    "blocks": args.blocks, "hidden": D, "heads": HEADS, "mlp": F, "window": window,
-                   "window_mode": "target-count" if mode == 0 else "extent", "global_batch": world,
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "window_mode": "target-count" if mode == 0 else "extent", "global_batch": 1,
+                   "parallelism": (f"window sharding x{world} (rank 0 owns {n_local} video tokens; NCCL "
+                                   "send/recv of shifted-window qkv/context rows + text all-reduce)")
+                   if sharded else "single GPU",
                    "l2": "inputs larger than L2 (5 GB of weights + 222 MB residual per step)"},
         "roofline": roof(dominant, kinds[dominant]),
         "window_attention": roof("window_attention", "tensor"),
         "hbm_passes": {k: roof(k, "hbm") for k in ("prepare_qkv", "ada_rmsnorm", "text_pool")},
-        "e2e": {"value": world * M / (e2e_ms / 1000.0), "unit": "tokens/s",
-                "h2d_bytes_per_step": int(M * D * 4 + 6 * D * 4), "d2h_bytes_per_step": int(M * D * 4),
-                "ms_per_step": e2e_ms, "entry_point": "s2_dit_forward_host"},
+        "e2e": {"value": M / (e2e_ms / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": int((n_local + TEXT) * D * 4 + 6 * D * 4),
+                "d2h_bytes_per_step": int((n_local + TEXT) * D * 4), "ms_per_step": e2e_ms,
+                "entry_point": "s2_dit_forward_sharded + pinned H2D/D2H" if sharded else "s2_dit_forward_host"},
         "gpu_launches": launches,
         "clocks": clk,
         "device_status": status,
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         dt, kind, cores = cpu_sample("reference")
         v = cpu_tokens_per_s(dt, args.config)
         result["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind,
@@ -362,6 +400,8 @@ def main():
     if rank == 0:
         print(json.dumps(result))
     dit.close()
+    if sharded:
+        abi.dist_destroy(ctx)
     ctx.close()
     if world > 1:
         torch.distributed.destroy_process_group()

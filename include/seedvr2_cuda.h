@@ -49,6 +49,7 @@ extern "C" {
 typedef struct s2_context s2_context;
 typedef struct s2_plan s2_plan;
 typedef struct s2_dit s2_dit;
+typedef struct s2_shard s2_shard;
 
 /* ---------------------------------------------------------------------------
  * Context.  Replaces the Vulkan device / VkCompute / allocator set-up the
@@ -232,6 +233,43 @@ int s2_dit_forward(s2_dit* dit, const int* video_shape, int text_length, float* 
 int s2_dit_forward_host(s2_dit* dit, const int* video_shapes, const int* text_lengths, int batch,
                         const float* video, const float* text, const float* modulation, float* video_out,
                         float* text_out);
+
+/* ---------------------------------------------------------------------------
+ * Multi-GPU (one process per GPU, NCCL over NVLink).  The reference has no
+ * distributed path (seedvr2_main.cpp:89-100 forces --sp-size 1); this is the
+ * window sharding of the B200 build.
+ *
+ * Ownership of one sample over `world` ranks: rank r owns the video tokens of
+ * a contiguous, token-balanced run of the UNSHIFTED plan's windows, stored in
+ * plan order; text tokens are replicated.  Shifted (odd) blocks move the raw
+ * qkv rows of each shifted window's foreign tokens to the window's owner and
+ * the context rows back (grouped NCCL send/recv); the text pool is an NCCL
+ * all-reduce.  s2_shard_* expose the plan (host only, no GPU needed):
+ * local_tokens [n_local] global token ids in local row order; send_tokens /
+ * recv_tokens concatenated over peer ranks in rank order (counts from
+ * s2_shard_counts). */
+int s2_shard_build(const int* video_shape, int text_length, const int* window, int window_mode, int rank, int world,
+                   s2_shard** out);
+int s2_shard_counts(const s2_shard* shard, int* n_local, int* send_counts, int* recv_counts);
+int s2_shard_lists(const s2_shard* shard, int* local_tokens, int* send_tokens, int* recv_tokens);
+void s2_shard_free(s2_shard* shard);
+
+/* NCCL: rank 0 makes a 128-byte id and shares it out of band; every rank then
+ * calls s2_dist_init on its context.  The communicator is non-blocking and
+ * every host wait on it is bounded by timeout_ms: on expiry it is aborted and
+ * the call returns S2_ERR_TIMEOUT.  s2_dist_sync waits (bounded) for the
+ * context stream. */
+int s2_dist_unique_id(void* id128);
+int s2_dist_init(s2_context* ctx, const void* id128, int rank, int world, int timeout_ms);
+int s2_dist_sync(s2_context* ctx);
+int s2_dist_destroy(s2_context* ctx);
+
+/* Sharded forward of all blocks for ONE sample on this rank (collective: every
+ * rank calls it with the same shape).  x_local: fp32 [n_local + Nt][D] -- the
+ * rank's own video rows in s2_shard local order, then all text rows -- updated
+ * in place.  modulation: fp32 [6][D] device. */
+int s2_dit_forward_sharded(s2_dit* dit, const int* video_shape, int text_length, float* x_local,
+                           const float* modulation);
 
 #ifdef __cplusplus
 }

@@ -46,7 +46,8 @@ EXPORTED = [
     "s2_plan_build", "s2_plan_info", "s2_plan_copy", "s2_plan_free",
     "s2_awa_forward", "s2_awa_forward_static", "s2_shared_linear", "s2_ada_rmsnorm", "s2_convert_f32_bf16",
     "s2_dit_create", "s2_dit_free", "s2_dit_set_block_weights", "s2_dit_init_random", "s2_dit_forward",
-    "s2_dit_forward_host",
+    "s2_dit_forward_host", "s2_shard_build", "s2_shard_counts", "s2_shard_lists", "s2_shard_free",
+    "s2_dist_unique_id", "s2_dist_init", "s2_dist_sync", "s2_dist_destroy", "s2_dit_forward_sharded",
 ]
 
 
@@ -124,6 +125,16 @@ def lib() -> C.CDLL:
     L.s2_dit_init_random.argtypes = [vp, C.c_uint64]
     L.s2_dit_forward.argtypes = [vp, pint, ip, vp, vp]
     L.s2_dit_forward_host.argtypes = [vp, pint, pint, ip, vp, vp, vp, vp, vp]
+    L.s2_shard_build.argtypes = [pint, ip, pint, ip, ip, ip, C.POINTER(vp)]
+    L.s2_shard_counts.argtypes = [vp, pint, pint, pint]
+    L.s2_shard_lists.argtypes = [vp, pint, pint, pint]
+    L.s2_shard_free.argtypes = [vp]
+    L.s2_shard_free.restype = None
+    L.s2_dist_unique_id.argtypes = [vp]
+    L.s2_dist_init.argtypes = [vp, vp, ip, ip, ip]
+    L.s2_dist_sync.argtypes = [vp]
+    L.s2_dist_destroy.argtypes = [vp]
+    L.s2_dit_forward_sharded.argtypes = [vp, pint, ip, vp, vp]
     _lib = L
     return L
 
@@ -352,9 +363,56 @@ class Dit:
                                    modulation.data_ptr()), "s2_dit_forward")
         return x
 
+    def forward_sharded(self, video_shape, text_length, x_local, modulation):
+        """x_local: fp32 CUDA [n_local + Nt, D] (this rank's rows, see shard()), updated in place."""
+        check(lib().s2_dit_forward_sharded(self.handle, _ints(video_shape), int(text_length), x_local.data_ptr(),
+                                           modulation.data_ptr()), "s2_dit_forward_sharded")
+        return x_local
+
     def forward_host(self, video_shapes, text_lengths, video, text, modulation, video_out, text_out):
         """Host buffers (numpy or pinned torch CPU tensors, fp32)."""
         flat = [int(v) for s in video_shapes for v in s]
         check(lib().s2_dit_forward_host(self.handle, _ints(flat), _ints(text_lengths), len(video_shapes),
                                         ptr(video), ptr(text), ptr(modulation), ptr(video_out), ptr(text_out)),
               "s2_dit_forward_host")
+
+
+def shard(video_shape, text_length, window, window_mode, rank, world) -> dict:
+    """Token ownership of a sharded forward (host only): local tokens and the exchange lists."""
+    import numpy as np
+
+    h = C.c_void_p()
+    check(lib().s2_shard_build(_ints(video_shape), int(text_length), _ints(window), int(window_mode), int(rank),
+                               int(world), C.byref(h)), "s2_shard_build")
+    try:
+        n = C.c_int()
+        sc = np.zeros(world, np.int32)
+        rc = np.zeros(world, np.int32)
+        P = lambda a: a.ctypes.data_as(C.POINTER(C.c_int))  # noqa: E731
+        check(lib().s2_shard_counts(h, C.byref(n), P(sc), P(rc)), "s2_shard_counts")
+        local = np.zeros(n.value, np.int32)
+        st = np.zeros(int(sc.sum()), np.int32)
+        rt = np.zeros(int(rc.sum()), np.int32)
+        check(lib().s2_shard_lists(h, P(local), P(st), P(rt)), "s2_shard_lists")
+    finally:
+        lib().s2_shard_free(h)
+    return {"local_tokens": local, "send_counts": sc, "recv_counts": rc, "send_tokens": st, "recv_tokens": rt}
+
+
+def dist_unique_id() -> bytes:
+    buf = (C.c_char * 128)()
+    check(lib().s2_dist_unique_id(buf), "s2_dist_unique_id")
+    return bytes(buf)
+
+
+def dist_init(ctx: Context, uid: bytes, rank: int, world: int, timeout_ms: int = 60000) -> None:
+    buf = (C.c_char * 128).from_buffer_copy(uid)
+    check(lib().s2_dist_init(ctx.handle, buf, rank, world, timeout_ms), "s2_dist_init")
+
+
+def dist_sync(ctx: Context) -> None:
+    check(lib().s2_dist_sync(ctx.handle), "s2_dist_sync")
+
+
+def dist_destroy(ctx: Context) -> None:
+    check(lib().s2_dist_destroy(ctx.handle), "s2_dist_destroy")

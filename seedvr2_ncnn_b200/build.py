@@ -26,7 +26,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I" + os.path.join(ROOT, "include"),
           "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills", "-Wno-deprecated-gpu-targets"]
 
-SOURCES = ["s2_api.cu", "dit.cu", "gemm_sm100.cu", "attention_sm100.cu", "elementwise.cu", "plan.cpp", "awa_static.cu"]
+SOURCES = ["s2_api.cu", "dit.cu", "gemm_sm100.cu", "attention_sm100.cu", "elementwise.cu", "plan.cpp", "awa_static.cu", "dist.cpp"]
 
 
 def _headers_digest() -> str:
@@ -67,8 +67,7 @@ def build(verbose: bool = False, extra: list[str] | None = None) -> str:
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 2)) as ex:
         objs = list(ex.map(lambda s: _compile(s, extra, hdr), SOURCES))
     if not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-cudart", "static", "-lcuda" if False else ""]
-        cmd = [c for c in cmd if c]
+        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-cudart", "static", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -1,0 +1,317 @@
+// Multi-GPU plumbing: the token-ownership plan of a sharded DiT forward and a
+// NCCL binding (one process per GPU).
+//
+// Ownership.  The reference runs one device (seedvr2_main.cpp:89-100 forces
+// --sp-size 1); sharding is this library's addition.  Every token-wise op of
+// a block (norms, the four SharedLinear GEMMs) only needs the token's own row,
+// and attention only needs the rows of one window, so:
+//   * rank r owns the tokens of a contiguous, token-balanced run of the
+//     UNSHIFTED plan's windows (plan order), stored in plan (partition) order;
+//   * even blocks attend over unshifted windows -- all local, no exchange;
+//   * odd blocks attend over shifted windows: each shifted window belongs to
+//     the rank holding most of its tokens; that rank receives the raw qkv rows
+//     of the window's other tokens (one grouped send/recv exchange) and sends
+//     their context rows back (a second exchange);
+//   * text tokens are replicated on every rank; each rank pools the text rows
+//     of its own windows with the sample's global window count and the
+//     partial sums are all-reduced (sum), which reproduces the reference's
+//     mean over all windows (adaptive_window_attention.cpp:963-974).
+//
+// NCCL is loaded with dlopen (the copy torch already loaded, else the
+// system's), communicators are created non-blocking, and every host wait on
+// them is bounded: on expiry the communicator is aborted and S2_ERR_TIMEOUT
+// returned.
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstring>
+#include <numeric>
+#include <thread>
+
+#include "s2_dist.h"
+
+namespace s2 {
+
+// ---------------------------------------------------------------- ownership
+int build_shard(const int* shape, int text_length, const int* window, int window_mode, int rank, int world,
+                ShardPlan& sp)
+{
+    sp = ShardPlan();
+    if (!shape || text_length <= 0 || world <= 0 || rank < 0 || rank >= world) return S2_ERR_INVALID;
+    int r = build_plan(shape, 1, window, window_mode, 0, sp.plan0);
+    if (r == S2_OK) r = build_plan(shape, 1, window, window_mode, 1, sp.plan1);
+    if (r != S2_OK) return r;
+    sp.world = world;
+    sp.rank = rank;
+    sp.T = text_length;
+    const int Nv = static_cast<int>(sp.plan0.video_indices.size());
+    sp.Nv = Nv;
+    const int nw0 = static_cast<int>(sp.plan0.windows.size() / 9);
+    const int nw1 = static_cast<int>(sp.plan1.windows.size() / 9);
+
+    // Unshifted windows: contiguous token-balanced split (window midpoints).
+    sp.owner0.resize(nw0);
+    long long before = 0;
+    for (int w = 0; w < nw0; w++)
+    {
+        const int cnt = sp.plan0.windows[9 * w + 8];
+        const long long mid2 = 2 * before + cnt; // 2 x midpoint
+        sp.owner0[w] = std::min(world - 1, static_cast<int>((mid2 * world) / (2LL * Nv)));
+        before += cnt;
+    }
+    sp.token_owner.assign(Nv, -1);
+    sp.token_local.assign(Nv, -1);
+    sp.n_local.assign(world, 0);
+    for (int w = 0; w < nw0; w++)
+    {
+        const int o = sp.owner0[w], part = sp.plan0.windows[9 * w + 7], cnt = sp.plan0.windows[9 * w + 8];
+        for (int i = 0; i < cnt; i++)
+        {
+            const int g = sp.plan0.video_indices[part + i];
+            sp.token_owner[g] = o;
+            sp.token_local[g] = sp.n_local[o]++;
+        }
+        if (o == rank) sp.win0_mine.push_back(w);
+    }
+    sp.local_tokens.resize(sp.n_local[rank]);
+    for (int g = 0; g < Nv; g++)
+        if (sp.token_owner[g] == rank) sp.local_tokens[sp.token_local[g]] = g;
+
+    // Shifted windows: owner = rank holding most of the window's tokens.
+    sp.owner1.resize(nw1);
+    std::vector<int> votes(world);
+    for (int w = 0; w < nw1; w++)
+    {
+        std::fill(votes.begin(), votes.end(), 0);
+        const int part = sp.plan1.windows[9 * w + 7], cnt = sp.plan1.windows[9 * w + 8];
+        for (int i = 0; i < cnt; i++) votes[sp.token_owner[sp.plan1.video_indices[part + i]]]++;
+        sp.owner1[w] = static_cast<int>(std::max_element(votes.begin(), votes.end()) - votes.begin());
+    }
+
+    // Exchange lists (both sides walk the same order: destination's shifted
+    // windows in plan order, tokens in partition order).
+    sp.send_rows.assign(world, {});
+    sp.send_tokens.assign(world, {});
+    sp.recv_tokens.assign(world, {});
+    for (int w = 0; w < nw1; w++)
+    {
+        const int q = sp.owner1[w], part = sp.plan1.windows[9 * w + 7], cnt = sp.plan1.windows[9 * w + 8];
+        if (q == rank) sp.win1_mine.push_back(w);
+        for (int i = 0; i < cnt; i++)
+        {
+            const int g = sp.plan1.video_indices[part + i];
+            const int s = sp.token_owner[g];
+            if (s == q) continue;
+            if (s == rank)
+            {
+                sp.send_rows[q].push_back(sp.token_local[g]);
+                sp.send_tokens[q].push_back(g);
+            }
+            if (q == rank) sp.recv_tokens[s].push_back(g);
+        }
+    }
+    sp.recv_off.assign(world, 0);
+    sp.send_off.assign(world, 0);
+    int acc = 0, sacc = 0;
+    for (int s = 0; s < world; s++)
+    {
+        sp.recv_off[s] = acc;
+        acc += static_cast<int>(sp.recv_tokens[s].size());
+        sp.send_off[s] = sacc;
+        sacc += static_cast<int>(sp.send_rows[s].size());
+    }
+    sp.m_foreign = acc;
+    sp.m_send = sacc;
+
+    // Row maps into this rank's buffers: [local video | text | foreign video].
+    const int n = sp.n_local[rank];
+    sp.row0.assign(Nv, -1);
+    sp.row1.assign(Nv, -1);
+    for (int i = 0; i < n; i++)
+    {
+        sp.row0[sp.local_tokens[i]] = i;
+        sp.row1[sp.local_tokens[i]] = i;
+    }
+    for (int s = 0; s < world; s++)
+        for (size_t k = 0; k < sp.recv_tokens[s].size(); k++)
+            sp.row1[sp.recv_tokens[s][k]] = n + text_length + sp.recv_off[s] + static_cast<int>(k);
+    return S2_OK;
+}
+
+// ---------------------------------------------------------------- NCCL
+namespace {
+
+struct NcclApi
+{
+    void* handle = nullptr;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    bool ok = false;
+};
+
+NcclApi& api()
+{
+    static NcclApi a;
+    static bool tried = false;
+    if (tried) return a;
+    tried = true;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return a;
+    a.handle = h;
+#define S2_SYM(name, field) a.field = reinterpret_cast<decltype(a.field)>(dlsym(h, name))
+    S2_SYM("ncclGetUniqueId", GetUniqueId);
+    S2_SYM("ncclCommInitRankConfig", CommInitRankConfig);
+    S2_SYM("ncclCommDestroy", CommDestroy);
+    S2_SYM("ncclCommAbort", CommAbort);
+    S2_SYM("ncclCommGetAsyncError", CommGetAsyncError);
+    S2_SYM("ncclGroupStart", GroupStart);
+    S2_SYM("ncclGroupEnd", GroupEnd);
+    S2_SYM("ncclSend", Send);
+    S2_SYM("ncclRecv", Recv);
+    S2_SYM("ncclAllReduce", AllReduce);
+#undef S2_SYM
+    a.ok = a.GetUniqueId && a.CommInitRankConfig && a.CommDestroy && a.CommAbort && a.CommGetAsyncError &&
+           a.GroupStart && a.GroupEnd && a.Send && a.Recv && a.AllReduce;
+    return a;
+}
+
+} // namespace
+
+bool nccl_available()
+{
+    return api().ok;
+}
+
+int nccl_unique_id(void* out128)
+{
+    NcclApi& a = api();
+    if (!a.ok) return S2_ERR_DEVICE;
+    ncclUniqueId id;
+    if (a.GetUniqueId(&id) != ncclSuccess) return S2_ERR_CUDA;
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
+    std::memcpy(out128, &id, 128);
+    return S2_OK;
+}
+
+// Bounded wait for a non-blocking communicator to leave ncclInProgress.
+int Dist::wait_ready()
+{
+    NcclApi& a = api();
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true)
+    {
+        ncclResult_t st = ncclSuccess;
+        if (a.CommGetAsyncError(comm, &st) != ncclSuccess) return fail(S2_ERR_CUDA);
+        if (st == ncclSuccess) return S2_OK;
+        if (st != ncclInProgress) return fail(S2_ERR_CUDA);
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) return fail(S2_ERR_TIMEOUT);
+        std::this_thread::yield();
+    }
+}
+
+int Dist::fail(int code)
+{
+    if (comm && !aborted)
+    {
+        api().CommAbort(comm);
+        aborted = true;
+        comm = nullptr;
+    }
+    return code;
+}
+
+int Dist::init(const void* id128, int r, int w, int tmo)
+{
+    NcclApi& a = api();
+    if (!a.ok) return S2_ERR_DEVICE;
+    rank = r;
+    world = w;
+    timeout_ms = tmo > 0 ? tmo : 60000;
+    ncclUniqueId id;
+    std::memcpy(&id, id128, 128);
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    const ncclResult_t res = a.CommInitRankConfig(&comm, world, id, rank, &cfg);
+    if (res != ncclSuccess && res != ncclInProgress)
+    {
+        comm = nullptr;
+        return S2_ERR_CUDA;
+    }
+    return wait_ready();
+}
+
+void Dist::destroy()
+{
+    if (comm && !aborted) api().CommDestroy(comm);
+    comm = nullptr;
+}
+
+int Dist::all_reduce_sum_f32(float* buf, size_t count, cudaStream_t stream)
+{
+    if (!comm) return S2_ERR_INVALID;
+    NcclApi& a = api();
+    const ncclResult_t res = a.AllReduce(buf, buf, count, ncclFloat32, ncclSum, comm, stream);
+    if (res != ncclSuccess && res != ncclInProgress) return fail(S2_ERR_CUDA);
+    return wait_ready();
+}
+
+// Grouped point-to-point exchange of bf16 rows of `row_elems` elements:
+// send_counts[p] rows from send + send_off[p] rows, recv_counts[p] rows into
+// recv + recv_off[p] rows.
+int Dist::exchange_bf16(const void* send, const std::vector<int>& send_counts, const std::vector<int>& send_off,
+                        void* recv, const std::vector<int>& recv_counts, const std::vector<int>& recv_off,
+                        size_t row_elems, cudaStream_t stream)
+{
+    if (!comm) return S2_ERR_INVALID;
+    NcclApi& a = api();
+    const size_t rb = row_elems * 2;
+    if (a.GroupStart() != ncclSuccess) return fail(S2_ERR_CUDA);
+    for (int p = 0; p < world; p++)
+    {
+        if (p == rank) continue;
+        if (send_counts[p] > 0)
+            a.Send(static_cast<const uint8_t*>(send) + (size_t)send_off[p] * rb, (size_t)send_counts[p] * rb,
+                   ncclUint8, p, comm, stream);
+        if (recv_counts[p] > 0)
+            a.Recv(static_cast<uint8_t*>(recv) + (size_t)recv_off[p] * rb, (size_t)recv_counts[p] * rb, ncclUint8, p,
+                   comm, stream);
+    }
+    const ncclResult_t res = a.GroupEnd();
+    if (res != ncclSuccess && res != ncclInProgress) return fail(S2_ERR_CUDA);
+    return wait_ready();
+}
+
+// Waits (bounded) for the stream; on expiry the communicator is aborted so
+// the ranks' NCCL kernels return and the caller sees S2_ERR_TIMEOUT.
+int Dist::sync(cudaStream_t stream)
+{
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true)
+    {
+        const cudaError_t e = cudaStreamQuery(stream);
+        if (e == cudaSuccess) return S2_OK;
+        if (e != cudaErrorNotReady) return S2_ERR_CUDA;
+        if (comm)
+        {
+            ncclResult_t st = ncclSuccess;
+            api().CommGetAsyncError(comm, &st);
+            if (st != ncclSuccess && st != ncclInProgress) return fail(S2_ERR_CUDA);
+        }
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) return fail(S2_ERR_TIMEOUT);
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+} // namespace s2

@@ -45,6 +45,19 @@ struct s2_dit
     s2::DeviceBuffer act; // activations of one forward
     s2::DeviceBuffer mods; // [blocks][6][D]
     s2::DeviceBuffer host_x; // staging for s2_dit_forward_host
+    // multi-GPU: ownership plan and schedules per (shape, text, rank, world)
+    struct Shard
+    {
+        s2::ShardPlan sp;
+        s2::AttnSchedule sched[2];
+        int* d_send_rows = nullptr; // [m_send] own rows sent, concatenated over peers
+        std::vector<int> send_counts, recv_counts;
+        ~Shard()
+        {
+            if (d_send_rows) cudaFree(d_send_rows);
+        }
+    };
+    std::map<std::vector<int>, std::unique_ptr<Shard>> shards;
 };
 
 namespace {
@@ -127,6 +140,7 @@ void s2_dit_free(s2_dit* d)
     cudaSetDevice(d->ctx->c.device);
     cudaStreamSynchronize(d->ctx->c.stream);
     d->plans.clear();
+    d->shards.clear();
     if (d->weights) cudaFree(d->weights);
     delete d;
 }
@@ -267,6 +281,128 @@ int s2_dit_forward(s2_dit* d, const int* video_shape, int text_length, float* x,
             return r;
         if ((r = s2::launch_window_attention(c, S, H, Qp, Kp, Vp, 0, 0, ctxb, partial)) != S2_OK) return r;
         if ((r = s2::launch_text_pool(c, S, D, partial, 0, 0, ctxb + (size_t)Nv * D)) != S2_OK) return r;
+        if ((r = s2::launch_shared_linear(c, M, 0, D, D, ctxb, nullptr, bl.w_out, cfg.out_bias ? bl.b_out : nullptr,
+                                          s2::EPI_GATE_RESIDUAL, mb + 2 * D, 1, x, nullptr)) != S2_OK)
+            return r;
+        if ((r = s2::launch_ada_rmsnorm(c, M, D, x, cfg.norm_eps, mb + 3 * D, mb + 4 * D, h)) != S2_OK) return r;
+        if ((r = s2::launch_shared_linear(c, M, 0, F, D, h, nullptr, bl.w_up, cfg.mlp_bias ? bl.b_up : nullptr,
+                                          s2::EPI_GELU_TANH, nullptr, 0, u, nullptr)) != S2_OK)
+            return r;
+        if ((r = s2::launch_shared_linear(c, M, 0, D, F, u, nullptr, bl.w_down, cfg.mlp_bias ? bl.b_down : nullptr,
+                                          s2::EPI_GATE_RESIDUAL, mb + 5 * D, 1, x, nullptr)) != S2_OK)
+            return r;
+    }
+    return S2_OK;
+}
+
+int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, float* x, const float* modulation)
+{
+    if (!d || !video_shape || text_length <= 0 || !x || !modulation) return S2_ERR_INVALID;
+    s2::Context& c = d->ctx->c;
+    s2::Dist* dist = d->ctx->dist.get();
+    const int rank = dist ? dist->rank : 0, world = dist ? dist->world : 1;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    const s2_dit_config& cfg = d->cfg;
+    const int D = cfg.hidden, F = cfg.mlp_hidden, H = cfg.heads, T = text_length;
+    int r;
+    std::vector<int> key(video_shape, video_shape + 3);
+    key.push_back(T);
+    key.push_back(rank);
+    key.push_back(world);
+    std::unique_ptr<s2_dit::Shard>& slot = d->shards[key];
+    if (!slot)
+    {
+        std::unique_ptr<s2_dit::Shard> sh(new s2_dit::Shard);
+        r = s2::build_shard(video_shape, T, cfg.window, cfg.window_mode, rank, world, sh->sp);
+        if (r == S2_OK) r = s2::build_schedule_ex(sh->sp.plan0, &T, &sh->sp.win0_mine, &sh->sp.row0, sh->sched[0], c.stream);
+        if (r == S2_OK) r = s2::build_schedule_ex(sh->sp.plan1, &T, &sh->sp.win1_mine, &sh->sp.row1, sh->sched[1], c.stream);
+        if (r == S2_OK)
+        {
+            std::vector<int> rows;
+            for (int p = 0; p < world; p++)
+            {
+                rows.insert(rows.end(), sh->sp.send_rows[p].begin(), sh->sp.send_rows[p].end());
+                sh->send_counts.push_back(static_cast<int>(sh->sp.send_rows[p].size()));
+                sh->recv_counts.push_back(static_cast<int>(sh->sp.recv_tokens[p].size()));
+            }
+            if (!rows.empty())
+            {
+                if (cudaMalloc(&sh->d_send_rows, rows.size() * 4) != cudaSuccess) r = S2_ERR_ALLOC;
+                else if (cudaMemcpy(sh->d_send_rows, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+                    r = S2_ERR_CUDA;
+            }
+        }
+        if (r != S2_OK)
+        {
+            d->shards.erase(key);
+            return r;
+        }
+        slot = std::move(sh);
+    }
+    s2_dit::Shard& sh = *slot;
+    const s2::ShardPlan& sp = sh.sp;
+    const int n = sp.n_local[rank];
+    const int M = n + T;                 // rows of x / h / u
+    const int E = n + T + sp.m_foreign;  // rows of qkv / ctx (foreign rows after the text rows)
+    int max_packed = std::max(sh.sched[0].packed_rows, sh.sched[1].packed_rows);
+    int max_partial = std::max(sh.sched[0].partial_rows, sh.sched[1].partial_rows);
+    const size_t sz_h = align256((size_t)M * D * 2), sz_qkv = align256((size_t)E * 3 * D * 2),
+                 sz_pk = align256((size_t)std::max(max_packed, 1) * D * 2), sz_ctx = align256((size_t)E * D * 2),
+                 sz_part = align256((size_t)std::max(max_partial, 1) * D * 4), sz_u = align256((size_t)M * F * 2),
+                 sz_text = align256((size_t)T * D * 4), sz_send = align256((size_t)std::max(sp.m_send, 1) * 3 * D * 2);
+    if ((r = d->act.ensure(sz_h + sz_qkv + 3 * sz_pk + sz_ctx + sz_part + sz_u + sz_text + sz_send)) != S2_OK) return r;
+    if ((r = d->mods.ensure((size_t)cfg.num_blocks * 6 * D * 4)) != S2_OK) return r;
+    uint8_t* a = static_cast<uint8_t*>(d->act.ptr);
+    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(a);
+    __nv_bfloat16* qkv = reinterpret_cast<__nv_bfloat16*>(a + sz_h);
+    uint8_t* pk = a + sz_h + sz_qkv;
+    __nv_bfloat16* ctxb = reinterpret_cast<__nv_bfloat16*>(pk + 3 * sz_pk);
+    float* partial = reinterpret_cast<float*>(pk + 3 * sz_pk + sz_ctx);
+    __nv_bfloat16* u = reinterpret_cast<__nv_bfloat16*>(pk + 3 * sz_pk + sz_ctx + sz_part);
+    float* text32 = reinterpret_cast<float*>(pk + 3 * sz_pk + sz_ctx + sz_part + sz_u);
+    __nv_bfloat16* sendbuf = reinterpret_cast<__nv_bfloat16*>(pk + 3 * sz_pk + sz_ctx + sz_part + sz_u + sz_text);
+    float* mods = static_cast<float*>(d->mods.ptr);
+    if ((r = s2::launch_add_vectors(c, d->ada_all, modulation, mods, cfg.num_blocks * 6 * D, 6 * D)) != S2_OK)
+        return r;
+
+    for (int b = 0; b < cfg.num_blocks; b++)
+    {
+        const s2_dit::Block& bl = d->blocks[b];
+        const float* mb = mods + (size_t)b * 6 * D;
+        const int shf = b & 1;
+        const s2::AttnSchedule& S = sh.sched[shf];
+        if ((r = s2::launch_ada_rmsnorm(c, M, D, x, cfg.norm_eps, mb, mb + D, h)) != S2_OK) return r;
+        if ((r = s2::launch_shared_linear(c, M, 0, 3 * D, D, h, nullptr, bl.w_qkv, cfg.qkv_bias ? bl.b_qkv : nullptr,
+                                          s2::EPI_STORE, nullptr, 0, qkv, nullptr)) != S2_OK)
+            return r;
+        if (shf && world > 1)
+        {
+            // own qkv rows of tokens in other ranks' shifted windows -> their owners
+            if ((r = s2::launch_gather_rows_bf16(c, qkv, sh.d_send_rows, sp.m_send, 3 * D, sendbuf)) != S2_OK) return r;
+            if ((r = dist->exchange_bf16(sendbuf, sh.send_counts, sp.send_off, qkv + (size_t)(n + T) * 3 * D,
+                                         sh.recv_counts, sp.recv_off, (size_t)3 * D, c.stream)) != S2_OK)
+                return r;
+        }
+        __nv_bfloat16* Qp = reinterpret_cast<__nv_bfloat16*>(pk);
+        __nv_bfloat16* Kp = reinterpret_cast<__nv_bfloat16*>(pk + sz_pk);
+        __nv_bfloat16* Vp = reinterpret_cast<__nv_bfloat16*>(pk + 2 * sz_pk);
+        const __nv_bfloat16* tq = qkv + (size_t)n * 3 * D;
+        if ((r = s2::launch_prepare_qkv(c, S, H, cfg.head_dim, cfg.rope_pairs, cfg.qk_eps, bl.qk_norm, bl.freqs, 1, qkv,
+                                        qkv + D, qkv + 2 * D, 3 * D, tq, tq + D, tq + 2 * D, 3 * D, Qp, Kp, Vp)) !=
+            S2_OK)
+            return r;
+        if ((r = s2::launch_window_attention(c, S, H, Qp, Kp, Vp, 0, 0, ctxb, partial)) != S2_OK) return r;
+        if ((r = s2::launch_text_pool(c, S, D, partial, 1, 0, text32)) != S2_OK) return r;
+        if (world > 1 && (r = dist->all_reduce_sum_f32(text32, (size_t)T * D, c.stream)) != S2_OK) return r;
+        if ((r = s2::launch_convert_f32_bf16(c, text32, ctxb + (size_t)n * D, (int64_t)T * D)) != S2_OK) return r;
+        if (shf && world > 1)
+        {
+            // context rows of foreign tokens back to their owners
+            if ((r = dist->exchange_bf16(ctxb + (size_t)(n + T) * D, sh.recv_counts, sp.recv_off, sendbuf,
+                                         sh.send_counts, sp.send_off, (size_t)D, c.stream)) != S2_OK)
+                return r;
+            if ((r = s2::launch_scatter_rows_bf16(c, sendbuf, sh.d_send_rows, sp.m_send, D, ctxb)) != S2_OK) return r;
+        }
         if ((r = s2::launch_shared_linear(c, M, 0, D, D, ctxb, nullptr, bl.w_out, cfg.out_bias ? bl.b_out : nullptr,
                                           s2::EPI_GATE_RESIDUAL, mb + 2 * D, 1, x, nullptr)) != S2_OK)
             return r;

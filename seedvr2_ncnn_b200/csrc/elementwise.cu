@@ -3,6 +3,7 @@
 // modulation, and small utilities.  All are 16-byte vectorised, one warp (or
 // 16-lane group) per row, grids sized by rows.
 #include "s2_common.cuh"
+#include "s2_dist.h"
 #include "s2_internal.h"
 
 namespace s2 {
@@ -184,9 +185,9 @@ __global__ void ada_rmsnorm_kernel(int rows, int D, const float* __restrict__ x,
     const float* xr = x + (int64_t)row * D;
     __nv_bfloat16* yr = y + (int64_t)row * D;
     float ss = 0.f;
-    if (G > 0)
+    if constexpr (G > 0)
     {
-        float v[G > 0 ? G : 1][8];
+        float v[G][8];
 #pragma unroll
         for (int g = 0; g < G; g++)
         {
@@ -208,27 +209,29 @@ __global__ void ada_rmsnorm_kernel(int rows, int D, const float* __restrict__ x,
             for (int i = 0; i < 8; i++) v[g][i] = v[g][i] * inv * sc[i] + sh[i];
             store8_bf16(yr + c, v[g]);
         }
-        return;
     }
-    for (int c = lane * 8; c < D; c += 256)
+    else
     {
-        float v[8];
-        load8<float>(xr + c, v);
+        for (int c = lane * 8; c < D; c += 256)
+        {
+            float v[8];
+            load8<float>(xr + c, v);
 #pragma unroll
-        for (int i = 0; i < 8; i++) ss += v[i] * v[i];
-    }
+            for (int i = 0; i < 8; i++) ss += v[i] * v[i];
+        }
 #pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
-    const float inv = 1.f / sqrtf(ss / D + eps);
-    for (int c = lane * 8; c < D; c += 256)
-    {
-        float v[8], sc[8], sh[8];
-        load8<float>(xr + c, v);
-        load8<float>(scale + c, sc);
-        load8<float>(shift + c, sh);
+        for (int m = 16; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+        const float inv = 1.f / sqrtf(ss / D + eps);
+        for (int c = lane * 8; c < D; c += 256)
+        {
+            float v[8], sc[8], sh[8];
+            load8<float>(xr + c, v);
+            load8<float>(scale + c, sc);
+            load8<float>(shift + c, sh);
 #pragma unroll
-        for (int i = 0; i < 8; i++) v[i] = v[i] * inv * sc[i] + sh[i];
-        store8_bf16(yr + c, v);
+            for (int i = 0; i < 8; i++) v[i] = v[i] * inv * sc[i] + sh[i];
+            store8_bf16(yr + c, v);
+        }
     }
 }
 
@@ -276,6 +279,19 @@ __global__ void fill_normal_f32_kernel(float* out, int64_t count, uint64_t seed,
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride)
         out[i] = mean + stddev * normal_at(seed, i);
+}
+
+// Row gather / scatter (16-byte vectors); one warp per row.
+__global__ void gather_rows_kernel(const uint4* __restrict__ src, const int* __restrict__ idx, int count,
+                                   int row_vecs, uint4* __restrict__ dst, int scatter)
+{
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= count) return;
+    const int r = __ldg(idx + row);
+    const uint4* s = src + (int64_t)(scatter ? row : r) * row_vecs;
+    uint4* d = dst + (int64_t)(scatter ? r : row) * row_vecs;
+    for (int c = lane; c < row_vecs; c += 32) d[c] = __ldg(s + c);
 }
 
 inline int finish(Context& ctx)
@@ -355,6 +371,27 @@ int launch_ada_rmsnorm(Context& ctx, int rows, int D, const float* x, float eps,
     default: ada_rmsnorm_kernel<0><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
     }
     return finish(ctx);
+}
+
+static int launch_rows(Context& ctx, const void* src, const int* idx, int count, int row_elems, void* dst, int scatter)
+{
+    if (count <= 0) return S2_OK;
+    if (row_elems % 8 || !aligned16(src) || !aligned16(dst)) return S2_ERR_INVALID;
+    const int warps = 8;
+    ProfileScope prof(ctx, K_OTHER, 0.0, (double)count * row_elems * 4.0);
+    gather_rows_kernel<<<(count + warps - 1) / warps, warps * 32, 0, ctx.stream>>>(
+        static_cast<const uint4*>(src), idx, count, row_elems / 8, static_cast<uint4*>(dst), scatter);
+    return finish(ctx);
+}
+
+int launch_gather_rows_bf16(Context& ctx, const void* src, const int* idx, int count, int row_elems, void* dst)
+{
+    return launch_rows(ctx, src, idx, count, row_elems, dst, 0);
+}
+
+int launch_scatter_rows_bf16(Context& ctx, const void* src, const int* idx, int count, int row_elems, void* dst)
+{
+    return launch_rows(ctx, src, idx, count, row_elems, dst, 1);
 }
 
 int launch_convert_f32_bf16(Context& ctx, const float* in, void* out, int64_t count)

@@ -155,7 +155,28 @@ AttnSchedule::~AttnSchedule()
 
 int build_schedule(const Plan& plan, const int* text_lengths, AttnSchedule& s, cudaStream_t stream)
 {
-    const int nw = static_cast<int>(plan.windows.size() / 9);
+    return build_schedule_ex(plan, text_lengths, nullptr, nullptr, s, stream);
+}
+
+// Schedule over a subset of the plan's windows (nullptr = all), with video
+// tokens mapped to the rows of the caller's qkv / output buffers through
+// row_of_token (nullptr = identity).  Text rows are pooled with the
+// sample's GLOBAL window count, so per-rank partial sums add up to the mean
+// (adaptive_window_attention.cpp:963-974).
+int build_schedule_ex(const Plan& plan, const int* text_lengths, const std::vector<int>* windows_subset,
+                      const std::vector<int>* row_of_token, AttnSchedule& s, cudaStream_t stream)
+{
+    const int nw_all = static_cast<int>(plan.windows.size() / 9);
+    std::vector<int> wsel;
+    if (windows_subset)
+        wsel = *windows_subset;
+    else
+    {
+        wsel.resize(nw_all);
+        std::iota(wsel.begin(), wsel.end(), 0);
+    }
+    const int nw = static_cast<int>(wsel.size());
+    auto row_of = [&](int token) { return row_of_token ? (*row_of_token)[token] : token; };
     std::vector<int> text_offset(plan.batch, 0);
     int total_text = 0, max_text = 0;
     for (int b = 0; b < plan.batch; b++)
@@ -165,21 +186,30 @@ int build_schedule(const Plan& plan, const int* text_lengths, AttnSchedule& s, c
         total_text += text_lengths[b];
         max_text = std::max(max_text, text_lengths[b]);
     }
-    std::vector<int> row_src, row_pos;
+    std::vector<int> row_src, row_pos, vidx;
     std::vector<int4> win_info(nw);
     std::vector<int> win_pool(nw);
     std::vector<int2> items;
     std::vector<int> item_cost;
+    std::vector<int> sample_first(plan.batch, -1), sample_count(plan.batch, 0);
     int seq = 0, pool = 0;
-    for (int w = 0; w < nw; w++)
+    s.attn_flops_per_head = 0;
+    for (int k = 0; k < nw; k++)
     {
+        const int w = wsel[k];
+        if (w < 0 || w >= nw_all) return S2_ERR_INVALID;
         const int* rec = &plan.windows[9 * w];
         const int sample = rec[0], part = rec[7], L = rec[8], T = text_lengths[sample];
-        win_info[w] = make_int4(seq, L, T, part);
-        win_pool[w] = pool;
+        if (sample_first[sample] < 0) sample_first[sample] = k;
+        sample_count[sample]++;
+        win_info[k] = make_int4(seq, L, T, static_cast<int>(vidx.size()));
+        win_pool[k] = pool;
         for (int r = 0; r < L; r++)
         {
-            row_src.push_back(plan.video_indices[part + r]);
+            const int row = row_of(plan.video_indices[part + r]);
+            if (row < 0) return S2_ERR_PLAN;
+            row_src.push_back(row);
+            vidx.push_back(row);
             // video RoPE position: window-local (t + text_len, h, w) (:904-905)
             row_pos.push_back(plan.local_positions[3 * (part + r)] + T);
             row_pos.push_back(plan.local_positions[3 * (part + r) + 1]);
@@ -198,7 +228,7 @@ int build_schedule(const Plan& plan, const int* text_lengths, AttnSchedule& s, c
         s.attn_flops_per_head += 4.0 * S * (double)S * 128.0;
         for (int q0 = 0; q0 < S; q0 += 256) // one item = a pair of 128-row query tiles
         {
-            items.push_back(make_int2(w, q0));
+            items.push_back(make_int2(k, q0));
             item_cost.push_back(ntiles);
         }
         seq += S;
@@ -215,16 +245,16 @@ int build_schedule(const Plan& plan, const int* text_lengths, AttnSchedule& s, c
     std::vector<float> scale(total_text);
     for (int b = 0; b < plan.batch; b++)
     {
-        const int fw = plan.sample_first_window[b], cnt = plan.sample_window_count[b];
+        const int cnt = sample_count[b], total = plan.sample_window_count[b];
         for (int j = 0; j < text_lengths[b]; j++)
         {
-            reduce[text_offset[b] + j] = make_int4(cnt > 0 ? win_pool[fw] + j : 0, text_lengths[b], cnt, 0);
-            scale[text_offset[b] + j] = cnt > 0 ? 1.f / cnt : 0.f;
+            reduce[text_offset[b] + j] = make_int4(cnt > 0 ? win_pool[sample_first[b]] + j : 0, text_lengths[b], cnt, 0);
+            scale[text_offset[b] + j] = total > 0 ? 1.f / total : 0.f;
         }
     }
 
     // One device block for every table.
-    const size_t n_tok = plan.video_indices.size();
+    const size_t n_tok = vidx.size();
     size_t off = 0;
     auto take = [&](size_t bytes) {
         const size_t o = off;
@@ -249,7 +279,7 @@ int build_schedule(const Plan& plan, const int* text_lengths, AttnSchedule& s, c
     put(o_win, win_info.data(), nw * 16);
     put(o_pool, win_pool.data(), nw * 4);
     put(o_items, sorted.data(), sorted.size() * 8);
-    put(o_vi, plan.video_indices.data(), n_tok * 4);
+    put(o_vi, vidx.data(), n_tok * 4);
     put(o_red, reduce.data(), total_text * 16);
     put(o_scale, scale.data(), total_text * 4);
     if (cudaMemcpyAsync(s.block, host.data(), host.size(), cudaMemcpyHostToDevice, stream) != cudaSuccess ||

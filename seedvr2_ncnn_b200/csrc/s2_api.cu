@@ -103,6 +103,8 @@ void s2_destroy(s2_context* ctx)
     cudaSetDevice(ctx->c.device);
     cudaStreamSynchronize(ctx->c.stream);
     ctx->plan_cache.clear();
+    if (ctx->dist) ctx->dist->destroy();
+    ctx->dist.reset();
     ctx->c.prof.release();
     for (auto& b : ctx->c.ws) b.release();
     if (ctx->c.status) cudaFree(ctx->c.status);
@@ -294,6 +296,91 @@ int s2_convert_f32_bf16(s2_context* ctx, const float* in, void* out, int64_t cou
     if (!ctx || !in || !out) return S2_ERR_INVALID;
     if (cudaSetDevice(ctx->c.device) != cudaSuccess) return S2_ERR_CUDA;
     return s2::launch_convert_f32_bf16(ctx->c, in, out, count);
+}
+
+// ------------------------------------------------------------------ multi-GPU
+int s2_shard_build(const int* video_shape, int text_length, const int* window, int window_mode, int rank, int world,
+                   s2_shard** out)
+{
+    if (!out) return S2_ERR_INVALID;
+    *out = nullptr;
+    std::unique_ptr<s2_shard> sh(new s2_shard);
+    const int r = s2::build_shard(video_shape, text_length, window, window_mode, rank, world, sh->sp);
+    if (r != S2_OK) return r;
+    *out = sh.release();
+    return S2_OK;
+}
+
+int s2_shard_counts(const s2_shard* sh, int* n_local, int* send_counts, int* recv_counts)
+{
+    if (!sh) return S2_ERR_INVALID;
+    const s2::ShardPlan& sp = sh->sp;
+    if (n_local) *n_local = sp.n_local[sp.rank];
+    for (int p = 0; p < sp.world; p++)
+    {
+        if (send_counts) send_counts[p] = static_cast<int>(sp.send_rows[p].size());
+        if (recv_counts) recv_counts[p] = static_cast<int>(sp.recv_tokens[p].size());
+    }
+    return S2_OK;
+}
+
+int s2_shard_lists(const s2_shard* sh, int* local_tokens, int* send_tokens, int* recv_tokens)
+{
+    if (!sh) return S2_ERR_INVALID;
+    const s2::ShardPlan& sp = sh->sp;
+    if (local_tokens) std::memcpy(local_tokens, sp.local_tokens.data(), sp.local_tokens.size() * 4);
+    for (int p = 0; p < sp.world; p++)
+    {
+        if (send_tokens)
+        {
+            std::memcpy(send_tokens, sp.send_tokens[p].data(), sp.send_tokens[p].size() * 4);
+            send_tokens += sp.send_tokens[p].size();
+        }
+        if (recv_tokens)
+        {
+            std::memcpy(recv_tokens, sp.recv_tokens[p].data(), sp.recv_tokens[p].size() * 4);
+            recv_tokens += sp.recv_tokens[p].size();
+        }
+    }
+    return S2_OK;
+}
+
+void s2_shard_free(s2_shard* sh)
+{
+    delete sh;
+}
+
+int s2_dist_unique_id(void* id128)
+{
+    if (!id128) return S2_ERR_INVALID;
+    return s2::nccl_unique_id(id128);
+}
+
+int s2_dist_init(s2_context* ctx, const void* id128, int rank, int world, int timeout_ms)
+{
+    if (!ctx || !id128 || world <= 0 || rank < 0 || rank >= world) return S2_ERR_INVALID;
+    if (cudaSetDevice(ctx->c.device) != cudaSuccess) return S2_ERR_CUDA;
+    std::unique_ptr<s2::Dist> d(new s2::Dist);
+    const int r = d->init(id128, rank, world, timeout_ms);
+    if (r != S2_OK) return r;
+    if (ctx->dist) ctx->dist->destroy();
+    ctx->dist = std::move(d);
+    return S2_OK;
+}
+
+int s2_dist_sync(s2_context* ctx)
+{
+    if (!ctx) return S2_ERR_INVALID;
+    if (!ctx->dist) return cudaStreamSynchronize(ctx->c.stream) == cudaSuccess ? S2_OK : S2_ERR_CUDA;
+    return ctx->dist->sync(ctx->c.stream);
+}
+
+int s2_dist_destroy(s2_context* ctx)
+{
+    if (!ctx) return S2_ERR_INVALID;
+    if (ctx->dist) ctx->dist->destroy();
+    ctx->dist.reset();
+    return S2_OK;
 }
 
 } // extern "C"

@@ -124,6 +124,8 @@ struct AttnSchedule
 };
 
 int build_schedule(const Plan& plan, const int* text_lengths, AttnSchedule& sched, cudaStream_t stream);
+int build_schedule_ex(const Plan& plan, const int* text_lengths, const std::vector<int>* windows_subset,
+                      const std::vector<int>* row_of_token, AttnSchedule& sched, cudaStream_t stream);
 
 int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                       uint32_t box_inner, uint32_t box_outer);

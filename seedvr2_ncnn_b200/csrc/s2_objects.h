@@ -6,6 +6,7 @@
 #include <memory>
 #include <vector>
 
+#include "s2_dist.h"
 #include "s2_internal.h"
 
 struct s2_plan
@@ -23,6 +24,13 @@ struct s2_context
     // Plans built from shapes inside s2_awa_forward, kept for later calls
     // (their device schedules must outlive the kernels that read them).
     std::map<std::vector<int>, std::unique_ptr<s2_plan>> plan_cache;
+    // NCCL communicator of a multi-GPU job (s2_dist_init), or null.
+    std::unique_ptr<s2::Dist> dist;
+};
+
+struct s2_shard
+{
+    s2::ShardPlan sp;
 };
 
 namespace s2 {

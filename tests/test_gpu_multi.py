@@ -1,0 +1,121 @@
+"""Multi-GPU parity: the sharded forward (s2_dit_forward_sharded over NCCL,
+one process per GPU) reproduces the single-GPU forward.  Runs only where the
+box has at least 2 GPUs; NVLS is off (NCCL_NVLS_ENABLE=0) and the library's
+own kernels only read local memory.
+
+Rows are computed by the same kernels in both runs; only the text-pool sum
+order (all-reduce) differs, so the gate is tight: cosine >= 0.99999 and
+max|a-b|/max|b| <= 1e-3.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from tests.conftest import ROOT, cosine, rel_maxabs
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    # shape, window, mode, D, heads, F, blocks
+    ([2, 12, 20], [1, 8, 8], 1, 512, 4, 2048, 2),
+    ([6, 45, 80], [4, 3, 4], 0, 2560, 20, 10240, 2),
+]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import sys
+    from datetime import timedelta
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    sys.path.insert(0, ROOT)
+    import torch
+    import torch.distributed as dist
+
+    from seedvr2_ncnn_b200 import abi
+
+    try:
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=timedelta(seconds=60))
+        ctx = abi.Context(rank)
+        uid = [abi.dist_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        abi.dist_init(ctx, uid[0], rank, world, 60000)
+        results = []
+        for shape, window, mode, D, H, F, blocks in CASES:
+            T = 58
+            dit = abi.Dit(ctx, num_blocks=blocks, hidden=D, heads=H, head_dim=128, mlp_hidden=F, window=window,
+                          window_mode=mode)
+            dit.init_random(42)
+            nv = int(np.prod(shape))
+            g = torch.Generator().manual_seed(7)
+            xg = torch.randn(nv + T, D, generator=g)
+            mod = torch.randn(6, D, generator=g).cuda()
+            s = abi.shard(shape, T, window, mode, rank, world)
+            local = torch.from_numpy(s["local_tokens"].astype(np.int64))
+            x = torch.cat([xg[local], xg[nv:]]).cuda()
+            dit.forward_sharded(shape, T, x, mod)
+            abi.dist_sync(ctx)
+            out = x.cpu()
+            # every rank sends its rows to rank 0
+            gathered = [None] * world
+            dist.all_gather_object(gathered, (local.numpy(), out.numpy()))
+            if rank == 0:
+                full = torch.zeros(nv + T, D)
+                for loc, rows in gathered:
+                    full[torch.from_numpy(loc)] = torch.from_numpy(rows[:len(loc)])
+                full[nv:] = torch.from_numpy(gathered[0][1][len(gathered[0][0]):])
+                ref = xg.clone().cuda()
+                dit.forward(shape, T, ref, mod)
+                torch.cuda.synchronize()
+                ref = ref.cpu().numpy()
+                results.append((cosine(full.numpy(), ref), rel_maxabs(full.numpy(), ref)))
+                # text rows agree across ranks
+                for _, rows in gathered[1:]:
+                    t0 = gathered[0][1][len(gathered[0][0]):]
+                    t1 = rows[-T:]
+                    assert np.array_equal(t0, t1), "text rows differ between ranks"
+            dit.close()
+        assert ctx.status() == 0
+        dist.barrier()
+        abi.dist_destroy(ctx)
+        ctx.close()
+        dist.destroy_process_group()
+        q.put((rank, results))
+    except Exception as e:
+        q.put((rank, f"error: {e!r}"))
+
+
+def test_sharded_forward_matches_single_gpu():
+    import multiprocessing as mp
+
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    for _ in range(world):
+        r, msg = q.get(timeout=600)
+        out[r] = msg
+    for p in procs:
+        p.join(timeout=60)
+    assert all(not isinstance(v, str) for v in out.values()), out
+    for c, rel in out[0]:
+        assert c >= 0.99999 and rel <= 1e-3, (c, rel)
