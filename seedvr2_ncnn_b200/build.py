@@ -19,6 +19,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libseedvr2_cuda.so")
+LAYER_LIB = os.path.join(HERE, "libseedvr2_ncnn.so")
+LAYER_SOURCES = ["adaptive_window_attention.cpp", "shared_linear.cpp", "layer_capi.cpp"]
+CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 ROOT = os.path.dirname(HERE)
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
@@ -71,9 +74,29 @@ def build(verbose: bool = False, extra: list[str] | None = None) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    build_layers(verbose)
     if verbose:
         print(LIB)
     return LIB
+
+
+def build_layers(verbose: bool = False) -> str:
+    """The ncnn-surface layer classes (C++, host) over libseedvr2_cuda.so."""
+    srcs = [os.path.join(CSRC, "layers", f) for f in LAYER_SOURCES]
+    deps = srcs + [os.path.join(CSRC, "layers", f) for f in os.listdir(os.path.join(CSRC, "layers")) if f.endswith(".h")]
+    deps.append(os.path.join(ROOT, "include", "seedvr2_cuda.h"))
+    if os.path.exists(LAYER_LIB) and all(os.path.getmtime(d) <= os.path.getmtime(LAYER_LIB) for d in deps) and \
+            os.path.getmtime(LIB) <= os.path.getmtime(LAYER_LIB):
+        return LAYER_LIB
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-o", LAYER_LIB] + srcs + [
+        "-I" + os.path.join(CUDA_HOME, "include"), "-L" + HERE, "-lseedvr2_cuda", "-L" + os.path.join(CUDA_HOME, "lib64"),
+        "-lcudart", "-Wl,-rpath,$ORIGIN", "-Wl,-rpath," + os.path.join(CUDA_HOME, "lib64")]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"layer library build failed:\n{r.stdout}\n{r.stderr}")
+    if verbose:
+        print(LAYER_LIB)
+    return LAYER_LIB
 
 
 if __name__ == "__main__":
