@@ -74,13 +74,17 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
+                                          "-i", str(self.gpu), "-lms", "50"], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 5.0:  # sampler is up before the timed region starts
+            time.sleep(0.01)
+        self.skip = len(self.lines)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -98,7 +102,7 @@ class ClockSampler:
             self.thread.join(timeout=2)
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        for line in self.lines[getattr(self, "skip", 0):]:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 8:
                 continue
@@ -284,7 +288,6 @@ def main():
 
     clocks = ClockSampler(local_rank)
     clocks.start()
-    time.sleep(0.3)
     ctx.profile(True)
     launches0 = ctx.launches()
     barrier()

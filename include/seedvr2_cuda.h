@@ -239,19 +239,20 @@ int s2_dit_forward_host(s2_dit* dit, const int* video_shapes, const int* text_le
  * distributed path (seedvr2_main.cpp:89-100 forces --sp-size 1); this is the
  * window sharding of the B200 build.
  *
- * Ownership of one sample over `world` ranks: rank r owns the video tokens of
- * a contiguous, token-balanced run of the UNSHIFTED plan's windows, stored in
- * plan order; text tokens are replicated.  Shifted (odd) blocks move the raw
- * qkv rows of each shifted window's foreign tokens to the window's owner and
- * the context rows back (grouped NCCL send/recv); the text pool is an NCCL
- * all-reduce.  s2_shard_* expose the plan (host only, no GPU needed):
- * local_tokens [n_local] global token ids in local row order; send_tokens /
- * recv_tokens concatenated over peer ranks in rank order (counts from
- * s2_shard_counts). */
+ * Ownership of one sample over `world` ranks: rank r owns an equal contiguous
+ * range of the UNSHIFTED plan's token order (window after window); text
+ * tokens are replicated.  Each window of a block (unshifted in even blocks,
+ * shifted in odd blocks) belongs to the rank holding most of its tokens; the
+ * raw qkv rows of its foreign tokens move to that rank and their context
+ * rows back (grouped NCCL send/recv); the text pool is an NCCL all-reduce.
+ * s2_shard_* expose the plan (host only, no GPU needed): local_tokens
+ * [n_local] global token ids in local row order; for window plan `shifted`
+ * (0/1), send_tokens / recv_tokens concatenated over peer ranks in rank order
+ * (counts from s2_shard_counts). */
 int s2_shard_build(const int* video_shape, int text_length, const int* window, int window_mode, int rank, int world,
                    s2_shard** out);
-int s2_shard_counts(const s2_shard* shard, int* n_local, int* send_counts, int* recv_counts);
-int s2_shard_lists(const s2_shard* shard, int* local_tokens, int* send_tokens, int* recv_tokens);
+int s2_shard_counts(const s2_shard* shard, int shifted, int* n_local, int* send_counts, int* recv_counts);
+int s2_shard_lists(const s2_shard* shard, int shifted, int* local_tokens, int* send_tokens, int* recv_tokens);
 void s2_shard_free(s2_shard* shard);
 
 /* NCCL: rank 0 makes a 128-byte id and shares it out of band; every rank then

@@ -126,8 +126,8 @@ def lib() -> C.CDLL:
     L.s2_dit_forward.argtypes = [vp, pint, ip, vp, vp]
     L.s2_dit_forward_host.argtypes = [vp, pint, pint, ip, vp, vp, vp, vp, vp]
     L.s2_shard_build.argtypes = [pint, ip, pint, ip, ip, ip, C.POINTER(vp)]
-    L.s2_shard_counts.argtypes = [vp, pint, pint, pint]
-    L.s2_shard_lists.argtypes = [vp, pint, pint, pint]
+    L.s2_shard_counts.argtypes = [vp, ip, pint, pint, pint]
+    L.s2_shard_lists.argtypes = [vp, ip, pint, pint, pint]
     L.s2_shard_free.argtypes = [vp]
     L.s2_shard_free.restype = None
     L.s2_dist_unique_id.argtypes = [vp]
@@ -377,8 +377,9 @@ class Dit:
               "s2_dit_forward_host")
 
 
-def shard(video_shape, text_length, window, window_mode, rank, world) -> dict:
-    """Token ownership of a sharded forward (host only): local tokens and the exchange lists."""
+def shard(video_shape, text_length, window, window_mode, rank, world, shifted=1) -> dict:
+    """Token ownership of a sharded forward (host only): local tokens and the exchange lists of
+    window plan `shifted` (0 = unshifted blocks, 1 = shifted blocks)."""
     import numpy as np
 
     h = C.c_void_p()
@@ -389,11 +390,11 @@ def shard(video_shape, text_length, window, window_mode, rank, world) -> dict:
         sc = np.zeros(world, np.int32)
         rc = np.zeros(world, np.int32)
         P = lambda a: a.ctypes.data_as(C.POINTER(C.c_int))  # noqa: E731
-        check(lib().s2_shard_counts(h, C.byref(n), P(sc), P(rc)), "s2_shard_counts")
+        check(lib().s2_shard_counts(h, int(shifted), C.byref(n), P(sc), P(rc)), "s2_shard_counts")
         local = np.zeros(n.value, np.int32)
         st = np.zeros(int(sc.sum()), np.int32)
         rt = np.zeros(int(rc.sum()), np.int32)
-        check(lib().s2_shard_lists(h, P(local), P(st), P(rt)), "s2_shard_lists")
+        check(lib().s2_shard_lists(h, int(shifted), P(local), P(st), P(rt)), "s2_shard_lists")
     finally:
         lib().s2_shard_free(h)
     return {"local_tokens": local, "send_counts": sc, "recv_counts": rc, "send_tokens": st, "recv_tokens": rt}

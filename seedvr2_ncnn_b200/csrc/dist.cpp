@@ -5,13 +5,13 @@
 // --sp-size 1); sharding is this library's addition.  Every token-wise op of
 // a block (norms, the four SharedLinear GEMMs) only needs the token's own row,
 // and attention only needs the rows of one window, so:
-//   * rank r owns the tokens of a contiguous, token-balanced run of the
-//     UNSHIFTED plan's windows (plan order), stored in plan (partition) order;
-//   * even blocks attend over unshifted windows -- all local, no exchange;
-//   * odd blocks attend over shifted windows: each shifted window belongs to
-//     the rank holding most of its tokens; that rank receives the raw qkv rows
-//     of the window's other tokens (one grouped send/recv exchange) and sends
-//     their context rows back (a second exchange);
+//   * rank r owns an equal contiguous range of the UNSHIFTED plan's token
+//     order (window after window), so the GEMMs are balanced to one row;
+//   * every window (unshifted in even blocks, shifted in odd blocks) belongs
+//     to the rank holding most of its tokens; that rank receives the raw qkv
+//     rows of the window's other tokens (one grouped send/recv exchange) and
+//     sends their context rows back (a second exchange) -- in even blocks
+//     only the few windows cut by a range boundary exchange anything;
 //   * text tokens are replicated on every rank; each rank pools the text rows
 //     of its own windows with the sample's global window count and the
 //     partial sums are all-reduced (sum), which reproduces the reference's
@@ -39,103 +39,123 @@ int build_shard(const int* shape, int text_length, const int* window, int window
 {
     sp = ShardPlan();
     if (!shape || text_length <= 0 || world <= 0 || rank < 0 || rank >= world) return S2_ERR_INVALID;
-    int r = build_plan(shape, 1, window, window_mode, 0, sp.plan0);
-    if (r == S2_OK) r = build_plan(shape, 1, window, window_mode, 1, sp.plan1);
-    if (r != S2_OK) return r;
+    for (int p = 0; p < 2; p++)
+    {
+        const int r = build_plan(shape, 1, window, window_mode, p, sp.plan[p]);
+        if (r != S2_OK) return r;
+    }
     sp.world = world;
     sp.rank = rank;
     sp.T = text_length;
-    const int Nv = static_cast<int>(sp.plan0.video_indices.size());
+    const int Nv = static_cast<int>(sp.plan[0].video_indices.size());
     sp.Nv = Nv;
-    const int nw0 = static_cast<int>(sp.plan0.windows.size() / 9);
-    const int nw1 = static_cast<int>(sp.plan1.windows.size() / 9);
 
-    // Unshifted windows: contiguous token-balanced split (window midpoints).
-    sp.owner0.resize(nw0);
-    long long before = 0;
-    for (int w = 0; w < nw0; w++)
-    {
-        const int cnt = sp.plan0.windows[9 * w + 8];
-        const long long mid2 = 2 * before + cnt; // 2 x midpoint
-        sp.owner0[w] = std::min(world - 1, static_cast<int>((mid2 * world) / (2LL * Nv)));
-        before += cnt;
-    }
+    // Tokens: equal contiguous ranges of the unshifted plan's partition order
+    // (window after window), so every token-wise op is balanced to one row.
     sp.token_owner.assign(Nv, -1);
     sp.token_local.assign(Nv, -1);
     sp.n_local.assign(world, 0);
-    for (int w = 0; w < nw0; w++)
+    for (int i = 0; i < Nv; i++)
     {
-        const int o = sp.owner0[w], part = sp.plan0.windows[9 * w + 7], cnt = sp.plan0.windows[9 * w + 8];
-        for (int i = 0; i < cnt; i++)
-        {
-            const int g = sp.plan0.video_indices[part + i];
-            sp.token_owner[g] = o;
-            sp.token_local[g] = sp.n_local[o]++;
-        }
-        if (o == rank) sp.win0_mine.push_back(w);
+        const int o = static_cast<int>(((long long)i * world) / Nv);
+        const int g = sp.plan[0].video_indices[i];
+        sp.token_owner[g] = o;
+        sp.token_local[g] = sp.n_local[o]++;
     }
     sp.local_tokens.resize(sp.n_local[rank]);
     for (int g = 0; g < Nv; g++)
         if (sp.token_owner[g] == rank) sp.local_tokens[sp.token_local[g]] = g;
 
-    // Shifted windows: owner = rank holding most of the window's tokens.
-    sp.owner1.resize(nw1);
-    std::vector<int> votes(world);
-    for (int w = 0; w < nw1; w++)
-    {
-        std::fill(votes.begin(), votes.end(), 0);
-        const int part = sp.plan1.windows[9 * w + 7], cnt = sp.plan1.windows[9 * w + 8];
-        for (int i = 0; i < cnt; i++) votes[sp.token_owner[sp.plan1.video_indices[part + i]]]++;
-        sp.owner1[w] = static_cast<int>(std::max_element(votes.begin(), votes.end()) - votes.begin());
-    }
-
-    // Exchange lists (both sides walk the same order: destination's shifted
-    // windows in plan order, tokens in partition order).
-    sp.send_rows.assign(world, {});
-    sp.send_tokens.assign(world, {});
-    sp.recv_tokens.assign(world, {});
-    for (int w = 0; w < nw1; w++)
-    {
-        const int q = sp.owner1[w], part = sp.plan1.windows[9 * w + 7], cnt = sp.plan1.windows[9 * w + 8];
-        if (q == rank) sp.win1_mine.push_back(w);
-        for (int i = 0; i < cnt; i++)
-        {
-            const int g = sp.plan1.video_indices[part + i];
-            const int s = sp.token_owner[g];
-            if (s == q) continue;
-            if (s == rank)
-            {
-                sp.send_rows[q].push_back(sp.token_local[g]);
-                sp.send_tokens[q].push_back(g);
-            }
-            if (q == rank) sp.recv_tokens[s].push_back(g);
-        }
-    }
-    sp.recv_off.assign(world, 0);
-    sp.send_off.assign(world, 0);
-    int acc = 0, sacc = 0;
-    for (int s = 0; s < world; s++)
-    {
-        sp.recv_off[s] = acc;
-        acc += static_cast<int>(sp.recv_tokens[s].size());
-        sp.send_off[s] = sacc;
-        sacc += static_cast<int>(sp.send_rows[s].size());
-    }
-    sp.m_foreign = acc;
-    sp.m_send = sacc;
-
-    // Row maps into this rank's buffers: [local video | text | foreign video].
     const int n = sp.n_local[rank];
-    sp.row0.assign(Nv, -1);
-    sp.row1.assign(Nv, -1);
-    for (int i = 0; i < n; i++)
+    for (int p = 0; p < 2; p++)
     {
-        sp.row0[sp.local_tokens[i]] = i;
-        sp.row1[sp.local_tokens[i]] = i;
+        const Plan& pl = sp.plan[p];
+        const int nw = static_cast<int>(pl.windows.size() / 9);
+        // Window owners: the rank holding most of the window's tokens, then
+        // windows move from the most to the least loaded rank (attention cost
+        // (L+T)^2, preferring windows that rank already holds tokens of) until
+        // no rank carries more than 5 % above the mean.
+        sp.owner[p].assign(nw, 0);
+        std::vector<std::vector<int>> w_votes(nw, std::vector<int>(world, 0));
+        std::vector<double> load(world, 0.0);
+        auto cost = [&](int w) {
+            const double S = pl.windows[9 * w + 8] + text_length;
+            return S * S;
+        };
+        double total = 0.0;
+        for (int w = 0; w < nw; w++)
+        {
+            const int part = pl.windows[9 * w + 7], cnt = pl.windows[9 * w + 8];
+            for (int i = 0; i < cnt; i++) w_votes[w][sp.token_owner[pl.video_indices[part + i]]]++;
+            sp.owner[p][w] = static_cast<int>(std::max_element(w_votes[w].begin(), w_votes[w].end()) -
+                                              w_votes[w].begin());
+            load[sp.owner[p][w]] += cost(w);
+            total += cost(w);
+        }
+        const double mean = total / world;
+        for (int iter = 0; iter < 4 * nw; iter++)
+        {
+            const int hi = static_cast<int>(std::max_element(load.begin(), load.end()) - load.begin());
+            const int lo = static_cast<int>(std::min_element(load.begin(), load.end()) - load.begin());
+            if (load[hi] <= 1.05 * mean) break;
+            int pick = -1;
+            double pick_key = -1.0;
+            for (int w = 0; w < nw; w++)
+            {
+                if (sp.owner[p][w] != hi || load[lo] + cost(w) >= load[hi]) continue;
+                const double key = (double)w_votes[w][lo] / pl.windows[9 * w + 8] + 1e-9 * cost(w);
+                if (key > pick_key)
+                {
+                    pick = w;
+                    pick_key = key;
+                }
+            }
+            if (pick < 0) break;
+            sp.owner[p][pick] = lo;
+            load[hi] -= cost(pick);
+            load[lo] += cost(pick);
+        }
+        // Exchange lists: both sides walk the destination's windows in plan
+        // order and their tokens in partition order.
+        sp.send_rows[p].assign(world, {});
+        sp.send_tokens[p].assign(world, {});
+        sp.recv_tokens[p].assign(world, {});
+        for (int w = 0; w < nw; w++)
+        {
+            const int q = sp.owner[p][w], part = pl.windows[9 * w + 7], cnt = pl.windows[9 * w + 8];
+            if (q == rank) sp.win_mine[p].push_back(w);
+            for (int i = 0; i < cnt; i++)
+            {
+                const int g = pl.video_indices[part + i];
+                const int s = sp.token_owner[g];
+                if (s == q) continue;
+                if (s == rank)
+                {
+                    sp.send_rows[p][q].push_back(sp.token_local[g]);
+                    sp.send_tokens[p][q].push_back(g);
+                }
+                if (q == rank) sp.recv_tokens[p][s].push_back(g);
+            }
+        }
+        sp.recv_off[p].assign(world, 0);
+        sp.send_off[p].assign(world, 0);
+        int acc = 0, sacc = 0;
+        for (int s = 0; s < world; s++)
+        {
+            sp.recv_off[p][s] = acc;
+            acc += static_cast<int>(sp.recv_tokens[p][s].size());
+            sp.send_off[p][s] = sacc;
+            sacc += static_cast<int>(sp.send_rows[p][s].size());
+        }
+        sp.m_foreign[p] = acc;
+        sp.m_send[p] = sacc;
+        // Rows of this rank's buffers: [own video | text | foreign video].
+        sp.row[p].assign(Nv, -1);
+        for (int i = 0; i < n; i++) sp.row[p][sp.local_tokens[i]] = i;
+        for (int s = 0; s < world; s++)
+            for (size_t k = 0; k < sp.recv_tokens[p][s].size(); k++)
+                sp.row[p][sp.recv_tokens[p][s][k]] = n + text_length + sp.recv_off[p][s] + static_cast<int>(k);
     }
-    for (int s = 0; s < world; s++)
-        for (size_t k = 0; k < sp.recv_tokens[s].size(); k++)
-            sp.row1[sp.recv_tokens[s][k]] = n + text_length + sp.recv_off[s] + static_cast<int>(k);
     return S2_OK;
 }
 

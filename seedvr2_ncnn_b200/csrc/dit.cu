@@ -50,11 +50,12 @@ struct s2_dit
     {
         s2::ShardPlan sp;
         s2::AttnSchedule sched[2];
-        int* d_send_rows = nullptr; // [m_send] own rows sent, concatenated over peers
-        std::vector<int> send_counts, recv_counts;
+        int* d_send_rows[2] = {nullptr, nullptr}; // per plan: own rows sent, concatenated over peers
+        std::vector<int> send_counts[2], recv_counts[2];
         ~Shard()
         {
-            if (d_send_rows) cudaFree(d_send_rows);
+            for (int p = 0; p < 2; p++)
+                if (d_send_rows[p]) cudaFree(d_send_rows[p]);
         }
     };
     std::map<std::vector<int>, std::unique_ptr<Shard>> shards;
@@ -314,21 +315,23 @@ int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, f
     {
         std::unique_ptr<s2_dit::Shard> sh(new s2_dit::Shard);
         r = s2::build_shard(video_shape, T, cfg.window, cfg.window_mode, rank, world, sh->sp);
-        if (r == S2_OK) r = s2::build_schedule_ex(sh->sp.plan0, &T, &sh->sp.win0_mine, &sh->sp.row0, sh->sched[0], c.stream);
-        if (r == S2_OK) r = s2::build_schedule_ex(sh->sp.plan1, &T, &sh->sp.win1_mine, &sh->sp.row1, sh->sched[1], c.stream);
-        if (r == S2_OK)
+        for (int p = 0; p < 2 && r == S2_OK; p++)
         {
+            r = s2::build_schedule_ex(sh->sp.plan[p], &T, &sh->sp.win_mine[p], &sh->sp.row[p], sh->sched[p],
+                                      c.stream);
             std::vector<int> rows;
-            for (int p = 0; p < world; p++)
+            for (int q = 0; q < world && r == S2_OK; q++)
             {
-                rows.insert(rows.end(), sh->sp.send_rows[p].begin(), sh->sp.send_rows[p].end());
-                sh->send_counts.push_back(static_cast<int>(sh->sp.send_rows[p].size()));
-                sh->recv_counts.push_back(static_cast<int>(sh->sp.recv_tokens[p].size()));
+                rows.insert(rows.end(), sh->sp.send_rows[p][q].begin(), sh->sp.send_rows[p][q].end());
+                sh->send_counts[p].push_back(static_cast<int>(sh->sp.send_rows[p][q].size()));
+                sh->recv_counts[p].push_back(static_cast<int>(sh->sp.recv_tokens[p][q].size()));
             }
-            if (!rows.empty())
+            if (r == S2_OK && !rows.empty())
             {
-                if (cudaMalloc(&sh->d_send_rows, rows.size() * 4) != cudaSuccess) r = S2_ERR_ALLOC;
-                else if (cudaMemcpy(sh->d_send_rows, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+                if (cudaMalloc(&sh->d_send_rows[p], rows.size() * 4) != cudaSuccess)
+                    r = S2_ERR_ALLOC;
+                else if (cudaMemcpy(sh->d_send_rows[p], rows.data(), rows.size() * 4, cudaMemcpyHostToDevice) !=
+                         cudaSuccess)
                     r = S2_ERR_CUDA;
             }
         }
@@ -342,14 +345,14 @@ int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, f
     s2_dit::Shard& sh = *slot;
     const s2::ShardPlan& sp = sh.sp;
     const int n = sp.n_local[rank];
-    const int M = n + T;                 // rows of x / h / u
-    const int E = n + T + sp.m_foreign;  // rows of qkv / ctx (foreign rows after the text rows)
+    const int M = n + T; // rows of x / h / u
+    const int E = n + T + std::max(sp.m_foreign[0], sp.m_foreign[1]); // qkv / ctx rows (foreign after text)
     int max_packed = std::max(sh.sched[0].packed_rows, sh.sched[1].packed_rows);
     int max_partial = std::max(sh.sched[0].partial_rows, sh.sched[1].partial_rows);
     const size_t sz_h = align256((size_t)M * D * 2), sz_qkv = align256((size_t)E * 3 * D * 2),
                  sz_pk = align256((size_t)std::max(max_packed, 1) * D * 2), sz_ctx = align256((size_t)E * D * 2),
                  sz_part = align256((size_t)std::max(max_partial, 1) * D * 4), sz_u = align256((size_t)M * F * 2),
-                 sz_text = align256((size_t)T * D * 4), sz_send = align256((size_t)std::max(sp.m_send, 1) * 3 * D * 2);
+                 sz_text = align256((size_t)T * D * 4), sz_send = align256((size_t)std::max(std::max(sp.m_send[0], sp.m_send[1]), 1) * 3 * D * 2);
     if ((r = d->act.ensure(sz_h + sz_qkv + 3 * sz_pk + sz_ctx + sz_part + sz_u + sz_text + sz_send)) != S2_OK) return r;
     if ((r = d->mods.ensure((size_t)cfg.num_blocks * 6 * D * 4)) != S2_OK) return r;
     uint8_t* a = static_cast<uint8_t*>(d->act.ptr);
@@ -375,12 +378,15 @@ int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, f
         if ((r = s2::launch_shared_linear(c, M, 0, 3 * D, D, h, nullptr, bl.w_qkv, cfg.qkv_bias ? bl.b_qkv : nullptr,
                                           s2::EPI_STORE, nullptr, 0, qkv, nullptr)) != S2_OK)
             return r;
-        if (shf && world > 1)
+        const bool xchg = world > 1 && (sp.m_send[shf] > 0 || sp.m_foreign[shf] > 0);
+        if (xchg)
         {
-            // own qkv rows of tokens in other ranks' shifted windows -> their owners
-            if ((r = s2::launch_gather_rows_bf16(c, qkv, sh.d_send_rows, sp.m_send, 3 * D, sendbuf)) != S2_OK) return r;
-            if ((r = dist->exchange_bf16(sendbuf, sh.send_counts, sp.send_off, qkv + (size_t)(n + T) * 3 * D,
-                                         sh.recv_counts, sp.recv_off, (size_t)3 * D, c.stream)) != S2_OK)
+            // own qkv rows of tokens in other ranks' windows -> the window owners
+            if ((r = s2::launch_gather_rows_bf16(c, qkv, sh.d_send_rows[shf], sp.m_send[shf], 3 * D, sendbuf)) !=
+                S2_OK)
+                return r;
+            if ((r = dist->exchange_bf16(sendbuf, sh.send_counts[shf], sp.send_off[shf], qkv + (size_t)(n + T) * 3 * D,
+                                         sh.recv_counts[shf], sp.recv_off[shf], (size_t)3 * D, c.stream)) != S2_OK)
                 return r;
         }
         __nv_bfloat16* Qp = reinterpret_cast<__nv_bfloat16*>(pk);
@@ -395,13 +401,15 @@ int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, f
         if ((r = s2::launch_text_pool(c, S, D, partial, 1, 0, text32)) != S2_OK) return r;
         if (world > 1 && (r = dist->all_reduce_sum_f32(text32, (size_t)T * D, c.stream)) != S2_OK) return r;
         if ((r = s2::launch_convert_f32_bf16(c, text32, ctxb + (size_t)n * D, (int64_t)T * D)) != S2_OK) return r;
-        if (shf && world > 1)
+        if (xchg)
         {
             // context rows of foreign tokens back to their owners
-            if ((r = dist->exchange_bf16(ctxb + (size_t)(n + T) * D, sh.recv_counts, sp.recv_off, sendbuf,
-                                         sh.send_counts, sp.send_off, (size_t)D, c.stream)) != S2_OK)
+            if ((r = dist->exchange_bf16(ctxb + (size_t)(n + T) * D, sh.recv_counts[shf], sp.recv_off[shf], sendbuf,
+                                         sh.send_counts[shf], sp.send_off[shf], (size_t)D, c.stream)) != S2_OK)
                 return r;
-            if ((r = s2::launch_scatter_rows_bf16(c, sendbuf, sh.d_send_rows, sp.m_send, D, ctxb)) != S2_OK) return r;
+            if ((r = s2::launch_scatter_rows_bf16(c, sendbuf, sh.d_send_rows[shf], sp.m_send[shf], D, ctxb)) !=
+                S2_OK)
+                return r;
         }
         if ((r = s2::launch_shared_linear(c, M, 0, D, D, ctxb, nullptr, bl.w_out, cfg.out_bias ? bl.b_out : nullptr,
                                           s2::EPI_GATE_RESIDUAL, mb + 2 * D, 1, x, nullptr)) != S2_OK)

@@ -20,17 +20,23 @@ namespace s2 {
 namespace {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int BK = 64;
-constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int TMEM_COLS = 2 * BN;
 constexpr int GROUP_M = 16;
 constexpr int NUM_THREADS = 192; // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
-constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN, 0, 0);
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+
+// Tile width BN (256, or 128 when a problem has too few 256-wide tiles to
+// fill the SMs evenly): 192 KB of stages either way.
+template <int BN>
+struct Tile
+{
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN, 0, 0);
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
 
 struct GemmArgs
 {
@@ -45,6 +51,7 @@ struct GemmArgs
     int* status;
 };
 
+template <int BN>
 __device__ __forceinline__ void decode_tile(const GemmArgs& a, int t, int& stream, int& m0, int& n0)
 {
     const int mb_total = a.mblk0 + a.mblk1;
@@ -168,10 +175,15 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int stream, in
     }
 }
 
+template <int BN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     shared_linear_kernel(const __grid_constant__ CUtensorMap tmap_a0, const __grid_constant__ CUtensorMap tmap_a1,
                          const __grid_constant__ CUtensorMap tmap_w, const GemmArgs args)
 {
+    constexpr int STAGES = Tile<BN>::STAGES;
+    constexpr int STAGE_BYTES = Tile<BN>::STAGE_BYTES;
+    constexpr int TMEM_COLS = Tile<BN>::TMEM_COLS;
+    constexpr uint32_t IDESC = Tile<BN>::IDESC;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -223,7 +235,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x)
             {
                 int stream, m0, n0;
-                decode_tile(args, t, stream, m0, n0);
+                decode_tile<BN>(args, t, stream, m0, n0);
                 const CUtensorMap* ta = stream ? &tmap_a1 : &tmap_a0;
                 for (int kb = 0; kb < args.num_kb; kb++)
                 {
@@ -320,7 +332,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             __syncwarp();
             tc_fence_after();
             int stream, m0, n0;
-            decode_tile(args, t, stream, m0, n0);
+            decode_tile<BN>(args, t, stream, m0, n0);
             const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; c++)
@@ -359,7 +371,7 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
     CUtensorMap ta0, ta1, tw;
     int r = make_tmap_bf16_2d(&ta0, A0, K, M0 > 0 ? M0 : 1, (uint64_t)K * 2, BK, BM);
     if (r == 0) r = make_tmap_bf16_2d(&ta1, M1 > 0 ? A1 : A0, K, M1 > 0 ? M1 : (M0 > 0 ? M0 : 1), (uint64_t)K * 2, BK, BM);
-    if (r == 0) r = make_tmap_bf16_2d(&tw, W, K, N, (uint64_t)K * 2, BK, BN);
+    if (r == 0) r = make_tmap_bf16_2d(&tw, W, K, N, (uint64_t)K * 2, BK, 256);
     if (r != 0) return r;
 
     GemmArgs a;
@@ -369,8 +381,6 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
     a.K = K;
     a.mblk0 = (M0 + BM - 1) / BM;
     a.mblk1 = (M1 + BM - 1) / BM;
-    a.nblk = (N + BN - 1) / BN;
-    a.num_tiles = (a.mblk0 + a.mblk1) * a.nblk;
     a.num_kb = (K + BK - 1) / BK;
     a.epilogue = epilogue;
     a.out_f32 = out_f32;
@@ -380,19 +390,36 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
     a.out1 = out1;
     a.status = ctx.status;
 
-    static bool configured = false;
-    if (!configured)
+    // Tile width: 128 when it fills the SMs markedly more evenly than 256.
+    auto wave_eff = [&](int bn) {
+        const int tiles = (a.mblk0 + a.mblk1) * ((N + bn - 1) / bn);
+        const int waves = (tiles + ctx.num_sms - 1) / ctx.num_sms;
+        return (double)tiles / ((double)waves * ctx.num_sms);
+    };
+    const bool narrow = wave_eff(128) > 1.15 * wave_eff(256);
+    const int BNsel = narrow ? 128 : 256;
+    a.nblk = (N + BNsel - 1) / BNsel;
+    a.num_tiles = (a.mblk0 + a.mblk1) * a.nblk;
+    if (narrow && (r = make_tmap_bf16_2d(&tw, W, K, N, (uint64_t)K * 2, BK, 128)) != 0) return r;
+    static bool configured[2] = {false, false};
+    if (!configured[narrow])
     {
-        if (cudaFuncSetAttribute(shared_linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-            cudaSuccess)
-            return S2_ERR_CUDA;
-        configured = true;
+        const cudaError_t e =
+            narrow ? cudaFuncSetAttribute(shared_linear_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          Tile<128>::SMEM_BYTES)
+                   : cudaFuncSetAttribute(shared_linear_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          Tile<256>::SMEM_BYTES);
+        if (e != cudaSuccess) return S2_ERR_CUDA;
+        configured[narrow] = true;
     }
     const int grid = a.num_tiles < ctx.num_sms ? a.num_tiles : ctx.num_sms;
     const double M = (double)M0 + M1;
     const double out_bytes = epilogue == EPI_GATE_RESIDUAL ? 8.0 : (out_f32 ? 4.0 : 2.0);
     ProfileScope prof(ctx, K_GEMM, 2.0 * M * N * K, (M * K + (double)N * K) * 2.0 + M * N * out_bytes);
-    shared_linear_kernel<<<grid, NUM_THREADS, SMEM_BYTES, ctx.stream>>>(ta0, ta1, tw, a);
+    if (narrow)
+        shared_linear_kernel<128><<<grid, NUM_THREADS, Tile<128>::SMEM_BYTES, ctx.stream>>>(ta0, ta1, tw, a);
+    else
+        shared_linear_kernel<256><<<grid, NUM_THREADS, Tile<256>::SMEM_BYTES, ctx.stream>>>(ta0, ta1, tw, a);
     ctx.launches++;
     return cudaGetLastError() == cudaSuccess ? S2_OK : S2_ERR_CUDA;
 }

@@ -311,35 +311,37 @@ int s2_shard_build(const int* video_shape, int text_length, const int* window, i
     return S2_OK;
 }
 
-int s2_shard_counts(const s2_shard* sh, int* n_local, int* send_counts, int* recv_counts)
+int s2_shard_counts(const s2_shard* sh, int shifted, int* n_local, int* send_counts, int* recv_counts)
 {
-    if (!sh) return S2_ERR_INVALID;
+    if (!sh || shifted < 0 || shifted > 1) return S2_ERR_INVALID;
     const s2::ShardPlan& sp = sh->sp;
     if (n_local) *n_local = sp.n_local[sp.rank];
     for (int p = 0; p < sp.world; p++)
     {
-        if (send_counts) send_counts[p] = static_cast<int>(sp.send_rows[p].size());
-        if (recv_counts) recv_counts[p] = static_cast<int>(sp.recv_tokens[p].size());
+        if (send_counts) send_counts[p] = static_cast<int>(sp.send_rows[shifted][p].size());
+        if (recv_counts) recv_counts[p] = static_cast<int>(sp.recv_tokens[shifted][p].size());
     }
     return S2_OK;
 }
 
-int s2_shard_lists(const s2_shard* sh, int* local_tokens, int* send_tokens, int* recv_tokens)
+int s2_shard_lists(const s2_shard* sh, int shifted, int* local_tokens, int* send_tokens, int* recv_tokens)
 {
-    if (!sh) return S2_ERR_INVALID;
+    if (!sh || shifted < 0 || shifted > 1) return S2_ERR_INVALID;
     const s2::ShardPlan& sp = sh->sp;
     if (local_tokens) std::memcpy(local_tokens, sp.local_tokens.data(), sp.local_tokens.size() * 4);
     for (int p = 0; p < sp.world; p++)
     {
+        const std::vector<int>& st = sp.send_tokens[shifted][p];
+        const std::vector<int>& rt = sp.recv_tokens[shifted][p];
         if (send_tokens)
         {
-            std::memcpy(send_tokens, sp.send_tokens[p].data(), sp.send_tokens[p].size() * 4);
-            send_tokens += sp.send_tokens[p].size();
+            std::memcpy(send_tokens, st.data(), st.size() * 4);
+            send_tokens += st.size();
         }
         if (recv_tokens)
         {
-            std::memcpy(recv_tokens, sp.recv_tokens[p].data(), sp.recv_tokens[p].size() * 4);
-            recv_tokens += sp.recv_tokens[p].size();
+            std::memcpy(recv_tokens, rt.data(), rt.size() * 4);
+            recv_tokens += rt.size();
         }
     }
     return S2_OK;

@@ -10,25 +10,27 @@
 namespace s2 {
 
 // Token ownership of one sample for `world` ranks, seen from `rank`.
+// Per window plan p (0 = unshifted, 1 = shifted): each window has one owner
+// (the rank holding most of its tokens); foreign rows of its tokens travel to
+// it before attention and their context rows travel back.
 struct ShardPlan
 {
     int world = 1, rank = 0, Nv = 0, T = 0;
-    Plan plan0, plan1;                    // unshifted / shifted window plans
-    std::vector<int> owner0, owner1;      // window -> rank
-    std::vector<int> token_owner;         // [Nv] owning rank of each video token
-    std::vector<int> token_local;         // [Nv] row of the token at its owner
-    std::vector<int> n_local;             // [world] owned video tokens per rank
-    std::vector<int> local_tokens;        // this rank's tokens (global ids) in row order
-    std::vector<int> win0_mine, win1_mine; // this rank's unshifted / shifted windows
-    // Rows of this rank's buffers for each global token: row0 for unshifted
-    // blocks (own rows only), row1 for shifted blocks (own rows, then the
-    // foreign rows received after the text rows); -1 elsewhere.
-    std::vector<int> row0, row1;
-    std::vector<std::vector<int>> send_rows;   // [world] own rows sent to each rank (its order)
-    std::vector<std::vector<int>> send_tokens; // [world] the same rows as global token ids
-    std::vector<std::vector<int>> recv_tokens; // [world] foreign tokens received from each rank
-    std::vector<int> send_off, recv_off;       // [world] prefix offsets (rows)
-    int m_foreign = 0, m_send = 0;
+    Plan plan[2];                          // unshifted / shifted window plans
+    std::vector<int> token_owner;          // [Nv] owning rank of each video token
+    std::vector<int> token_local;          // [Nv] row of the token at its owner
+    std::vector<int> n_local;              // [world] owned video tokens per rank
+    std::vector<int> local_tokens;         // this rank's tokens (global ids) in row order
+    std::vector<int> owner[2];             // window -> rank
+    std::vector<int> win_mine[2];          // this rank's windows
+    // Rows of this rank's buffers for each global token: own rows first,
+    // then (after the text rows) the foreign rows received; -1 elsewhere.
+    std::vector<int> row[2];
+    std::vector<std::vector<int>> send_rows[2];   // [world] own rows sent to each rank (its order)
+    std::vector<std::vector<int>> send_tokens[2]; // [world] the same rows as global token ids
+    std::vector<std::vector<int>> recv_tokens[2]; // [world] foreign tokens received from each rank
+    std::vector<int> send_off[2], recv_off[2];    // [world] prefix offsets (rows)
+    int m_foreign[2] = {0, 0}, m_send[2] = {0, 0};
 };
 
 int build_shard(const int* shape, int text_length, const int* window, int window_mode, int rank, int world,

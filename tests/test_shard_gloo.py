@@ -41,7 +41,8 @@ def _worker(rank, world, port, T, q):
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                                 timeout=timedelta(seconds=30))
         for shape, window, mode in CASES:
-            _check_case(dist, torch, abi, rank, world, shape, window, mode, T)
+            for shifted in (0, 1):
+                _check_case(dist, torch, abi, rank, world, shape, window, mode, T, shifted)
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, "ok"))
@@ -49,8 +50,8 @@ def _worker(rank, world, port, T, q):
         q.put((rank, f"error: {e!r}"))
 
 
-def _check_case(dist, torch, abi, rank, world, shape, window, mode, T):
-    s = abi.shard(shape, T, window, mode, rank, world)
+def _check_case(dist, torch, abi, rank, world, shape, window, mode, T, shifted):
+    s = abi.shard(shape, T, window, mode, rank, world, shifted)
     nv = int(np.prod(shape))
     local = torch.from_numpy(s["local_tokens"].astype(np.int64))
     # 1. local tokens partition [0, nv)
@@ -63,6 +64,7 @@ def _check_case(dist, torch, abi, rank, world, shape, window, mode, T):
     dist.all_gather(allp, padded)
     every = torch.cat([a[a >= 0] for a in allp]).sort().values
     assert torch.equal(every, torch.arange(nv)), "local tokens do not partition the video tokens"
+    assert max(x.item() for x in sizes) - min(x.item() for x in sizes) <= 1, "token ranges are not balanced"
     # 2. send counts of s->q equal recv counts of q<-s
     sc = torch.from_numpy(s["send_counts"].astype(np.int64))
     rc = torch.from_numpy(s["recv_counts"].astype(np.int64))
