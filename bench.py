@@ -385,6 +385,10 @@ def main():
         "roofline": roof(dominant, kinds[dominant]),
         "window_attention": roof("window_attention", "tensor"),
         "hbm_passes": {k: roof(k, "hbm") for k in ("prepare_qkv", "ada_rmsnorm", "text_pool")},
+        "comm": {"nccl_ms_per_step": counters["comm"]["ms"] / args.steps,
+                 "nccl_bytes_per_step": counters["comm"]["bytes"] / args.steps,
+                 "host_wait_ms_per_step": counters["host_wait"]["ms"] / args.steps,
+                 "other_kernels_ms_per_step": counters["other"]["ms"] / args.steps},
         "e2e": {"value": M / (e2e_ms / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": int((n_local + TEXT) * D * 4 + 6 * D * 4),
                 "d2h_bytes_per_step": int((n_local + TEXT) * D * 4), "ms_per_step": e2e_ms,

@@ -79,7 +79,9 @@ uint64_t s2_launch_count(const s2_context* ctx);
 #define S2_KERNEL_ADA_RMSNORM 3
 #define S2_KERNEL_TEXT_POOL 4
 #define S2_KERNEL_OTHER 5
-#define S2_NUM_KERNEL_KINDS 6
+#define S2_KERNEL_COMM 6      /* NCCL exchanges / all-reduce (device time) */
+#define S2_KERNEL_HOST_WAIT 7 /* host time spent waiting on NCCL calls to be issued */
+#define S2_NUM_KERNEL_KINDS 8
 int s2_profile_enable(s2_context* ctx, int enable);
 int s2_profile_read(s2_context* ctx, int kind, int64_t* launches, double* milliseconds, double* flops,
                     double* bytes);

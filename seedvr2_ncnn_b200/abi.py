@@ -33,7 +33,10 @@ S2_KERNEL_PREPARE_QKV = 2
 S2_KERNEL_ADA_RMSNORM = 3
 S2_KERNEL_TEXT_POOL = 4
 S2_KERNEL_OTHER = 5
-KERNEL_NAMES = ["shared_linear", "window_attention", "prepare_qkv", "ada_rmsnorm", "text_pool", "other"]
+S2_KERNEL_COMM = 6
+S2_KERNEL_HOST_WAIT = 7
+KERNEL_NAMES = ["shared_linear", "window_attention", "prepare_qkv", "ada_rmsnorm", "text_pool", "other", "comm",
+                "host_wait"]
 
 S2_EPI_STORE = 0
 S2_EPI_GELU_TANH = 1

@@ -56,6 +56,10 @@ struct AttnArgs
     void* video_out;
     float* text_partial;
     int* status;
+    // peer output bases (multi-GPU): a video_indices entry with a non-zero
+    // peer field is stored into peer_out[peer - 1] over NVLink
+    void* peer_out[kMaxPeers];
+    int any_peer;
 };
 
 __device__ __forceinline__ float ex2(float x)
@@ -231,10 +235,21 @@ __device__ __forceinline__ void store_row(const AttnArgs& a, int item_window, in
                                           const float* o, float inv)
 {
     const bool video = qi < L;
+    int src = 0;
+    void* vbase = a.video_out;
+    if (video)
+    {
+        src = a.video_indices[part_off + qi];
+        const int peer = src >> kPeerShift;
+        if (peer)
+        {
+            vbase = a.peer_out[peer - 1];
+            src &= (1 << kPeerShift) - 1;
+        }
+    }
     if (video && !a.out_f32)
     {
-        const int src = a.video_indices[part_off + qi];
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.video_out) + (size_t)src * a.inner + col0;
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(vbase) + (size_t)src * a.inner + col0;
 #pragma unroll
         for (int i = 0; i < 32; i += 16)
         {
@@ -245,7 +260,7 @@ __device__ __forceinline__ void store_row(const AttnArgs& a, int item_window, in
         }
         return;
     }
-    float* dst = video ? reinterpret_cast<float*>(a.video_out) + (size_t)a.video_indices[part_off + qi] * a.inner + col0
+    float* dst = video ? reinterpret_cast<float*>(vbase) + (size_t)src * a.inner + col0
                        : a.text_partial + (size_t)(a.win_pool[item_window] + (qi - L)) * a.inner + col0;
 #pragma unroll
     for (int i = 0; i < 32; i += 8)
@@ -501,6 +516,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         store_row(args, item.x, part_off, L, qi, head * HD + c * 32, o, inv);
                     }
                 }
+                // rows stored into peer GPUs must be visible to them once this
+                // rank passes its next cross-GPU barrier
+                if (args.any_peer) __threadfence_system();
             }
         }
     }
@@ -514,8 +532,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 } // namespace
 
 int launch_window_attention(Context& ctx, const AttnSchedule& s, int heads, const void* q, const void* k,
-                            const void* v, int out_f32, int round_bf16, void* video_out, float* text_partial)
+                            const void* v, int out_f32, int round_bf16, void* video_out, float* text_partial,
+                            void* const* peer_out, int num_peers)
 {
+    if (num_peers < 0 || num_peers > kMaxPeers || (num_peers > 0 && !peer_out)) return S2_ERR_INVALID;
+    for (int i = 0; i < num_peers; i++)
+        if (reinterpret_cast<uintptr_t>(peer_out[i]) & 31) return S2_ERR_INVALID;
     if (s.num_items <= 0) return S2_OK;
     // The epilogue writes 32-byte vectors straight into the output rows.
     if ((reinterpret_cast<uintptr_t>(video_out) & 31) || (reinterpret_cast<uintptr_t>(text_partial) & 31))
@@ -538,6 +560,8 @@ int launch_window_attention(Context& ctx, const AttnSchedule& s, int heads, cons
     a.video_out = video_out;
     a.text_partial = text_partial;
     a.status = ctx.status;
+    for (int i = 0; i < kMaxPeers; i++) a.peer_out[i] = i < num_peers ? peer_out[i] : nullptr;
+    a.any_peer = num_peers > 0;
     static bool configured = false;
     if (!configured)
     {

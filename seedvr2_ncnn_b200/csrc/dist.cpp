@@ -149,6 +149,31 @@ int build_shard(const int* shape, int text_length, const int* window, int window
         }
         sp.m_foreign[p] = acc;
         sp.m_send[p] = sacc;
+        // Every rank's receive offsets (for direct stores into its buffer).
+        sp.recv_off_all[p].assign((size_t)world * world, 0);
+        sp.m_foreign_all[p].assign(world, 0);
+        {
+            std::vector<int> cnt((size_t)world * world, 0);
+            for (int w = 0; w < nw; w++)
+            {
+                const int q = sp.owner[p][w], part = pl.windows[9 * w + 7], c = pl.windows[9 * w + 8];
+                for (int i = 0; i < c; i++)
+                {
+                    const int s_ = sp.token_owner[pl.video_indices[part + i]];
+                    if (s_ != q) cnt[(size_t)q * world + s_]++;
+                }
+            }
+            for (int q = 0; q < world; q++)
+            {
+                int a2 = 0;
+                for (int s_ = 0; s_ < world; s_++)
+                {
+                    sp.recv_off_all[p][(size_t)q * world + s_] = a2;
+                    a2 += cnt[(size_t)q * world + s_];
+                }
+                sp.m_foreign_all[p][q] = a2;
+            }
+        }
         // Rows of this rank's buffers: [own video | text | foreign video].
         sp.row[p].assign(Nv, -1);
         for (int i = 0; i < n; i++) sp.row[p][sp.local_tokens[i]] = i;
@@ -176,6 +201,7 @@ struct NcclApi
     ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     bool ok = false;
 };
 
@@ -201,9 +227,10 @@ NcclApi& api()
     S2_SYM("ncclSend", Send);
     S2_SYM("ncclRecv", Recv);
     S2_SYM("ncclAllReduce", AllReduce);
+    S2_SYM("ncclAllGather", AllGather);
 #undef S2_SYM
     a.ok = a.GetUniqueId && a.CommInitRankConfig && a.CommDestroy && a.CommAbort && a.CommGetAsyncError &&
-           a.GroupStart && a.GroupEnd && a.Send && a.Recv && a.AllReduce;
+           a.GroupStart && a.GroupEnd && a.Send && a.Recv && a.AllReduce && a.AllGather;
     return a;
 }
 
@@ -226,7 +253,7 @@ int nccl_unique_id(void* out128)
 }
 
 // Bounded wait for a non-blocking communicator to leave ncclInProgress.
-int Dist::wait_ready()
+int Dist::wait_ready(Context* ctx)
 {
     NcclApi& a = api();
     const auto t0 = std::chrono::steady_clock::now();
@@ -234,7 +261,16 @@ int Dist::wait_ready()
     {
         ncclResult_t st = ncclSuccess;
         if (a.CommGetAsyncError(comm, &st) != ncclSuccess) return fail(S2_ERR_CUDA);
-        if (st == ncclSuccess) return S2_OK;
+        if (st == ncclSuccess)
+        {
+            if (ctx && ctx->prof.on)
+            {
+                ctx->prof.launches[K_HOST_WAIT] += 1;
+                ctx->prof.ms[K_HOST_WAIT] +=
+                    std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+            }
+            return S2_OK;
+        }
         if (st != ncclInProgress) return fail(S2_ERR_CUDA);
         if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) return fail(S2_ERR_TIMEOUT);
         std::this_thread::yield();
@@ -261,6 +297,8 @@ int Dist::init(const void* id128, int r, int w, int tmo)
     timeout_ms = tmo > 0 ? tmo : 60000;
     ncclUniqueId id;
     std::memcpy(&id, id128, 128);
+    // Creation is non-blocking so a peer that never joins is a bounded wait;
+    // data-path calls then enqueue without host polling (see exchange_bf16).
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.blocking = 0;
     const ncclResult_t res = a.CommInitRankConfig(&comm, world, id, rank, &cfg);
@@ -274,29 +312,81 @@ int Dist::init(const void* id128, int r, int w, int tmo)
 
 void Dist::destroy()
 {
+    for (void* p : opened) cudaIpcCloseMemHandle(p);
+    opened.clear();
     if (comm && !aborted) api().CommDestroy(comm);
     comm = nullptr;
 }
 
-int Dist::all_reduce_sum_f32(float* buf, size_t count, cudaStream_t stream)
+int Dist::share_buffer(Context& ctx, void* local, std::vector<void*>& peers)
+{
+    if (!comm) return S2_ERR_INVALID;
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "cudaIpcMemHandle_t size");
+    cudaIpcMemHandle_t mine;
+    if (cudaIpcGetMemHandle(&mine, local) != cudaSuccess) return S2_ERR_CUDA;
+    void* dev = nullptr;
+    if (cudaMalloc(&dev, (size_t)64 * (world + 1)) != cudaSuccess) return S2_ERR_ALLOC;
+    std::vector<uint8_t> all((size_t)64 * world);
+    int r = S2_OK;
+    if (cudaMemcpyAsync(dev, &mine, 64, cudaMemcpyHostToDevice, ctx.stream) != cudaSuccess) r = S2_ERR_CUDA;
+    if (r == S2_OK)
+    {
+        const ncclResult_t res =
+            api().AllGather(dev, static_cast<uint8_t*>(dev) + 64, 64, ncclUint8, comm, ctx.stream);
+        if (res != ncclSuccess && res != ncclInProgress) r = fail(S2_ERR_CUDA);
+        if (r == S2_OK) r = wait_ready(&ctx);
+    }
+    if (r == S2_OK) r = sync(ctx.stream);
+    if (r == S2_OK &&
+        cudaMemcpy(all.data(), static_cast<uint8_t*>(dev) + 64, all.size(), cudaMemcpyDeviceToHost) != cudaSuccess)
+        r = S2_ERR_CUDA;
+    cudaFree(dev);
+    if (r != S2_OK) return r;
+    peers.assign(world, nullptr);
+    for (int q = 0; q < world; q++)
+    {
+        if (q == rank)
+        {
+            peers[q] = local;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, all.data() + (size_t)64 * q, 64);
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return S2_ERR_CUDA;
+        opened.push_back(p);
+        peers[q] = p;
+    }
+    return S2_OK;
+}
+
+int Dist::all_reduce_sum_f32(Context& ctx, float* buf, size_t count)
 {
     if (!comm) return S2_ERR_INVALID;
     NcclApi& a = api();
-    const ncclResult_t res = a.AllReduce(buf, buf, count, ncclFloat32, ncclSum, comm, stream);
+    ncclResult_t res;
+    {
+        ProfileScope prof(ctx, K_COMM, 0.0, (double)count * 4.0 * 2.0);
+        res = a.AllReduce(buf, buf, count, ncclFloat32, ncclSum, comm, ctx.stream);
+    }
     if (res != ncclSuccess && res != ncclInProgress) return fail(S2_ERR_CUDA);
-    return wait_ready();
+    return wait_ready(&ctx);
 }
 
 // Grouped point-to-point exchange of bf16 rows of `row_elems` elements:
 // send_counts[p] rows from send + send_off[p] rows, recv_counts[p] rows into
 // recv + recv_off[p] rows.
-int Dist::exchange_bf16(const void* send, const std::vector<int>& send_counts, const std::vector<int>& send_off,
-                        void* recv, const std::vector<int>& recv_counts, const std::vector<int>& recv_off,
-                        size_t row_elems, cudaStream_t stream)
+int Dist::exchange_bf16(Context& ctx, const void* send, const std::vector<int>& send_counts,
+                        const std::vector<int>& send_off, void* recv, const std::vector<int>& recv_counts,
+                        const std::vector<int>& recv_off, size_t row_elems)
 {
     if (!comm) return S2_ERR_INVALID;
     NcclApi& a = api();
+    cudaStream_t stream = ctx.stream;
     const size_t rb = row_elems * 2;
+    double bytes = 0.0;
+    for (int p = 0; p < world; p++) bytes += (double)(send_counts[p] + recv_counts[p]) * rb;
+    ProfileScope prof(ctx, K_COMM, 0.0, bytes);
     if (a.GroupStart() != ncclSuccess) return fail(S2_ERR_CUDA);
     for (int p = 0; p < world; p++)
     {
@@ -310,7 +400,7 @@ int Dist::exchange_bf16(const void* send, const std::vector<int>& send_counts, c
     }
     const ncclResult_t res = a.GroupEnd();
     if (res != ncclSuccess && res != ncclInProgress) return fail(S2_ERR_CUDA);
-    return wait_ready();
+    return wait_ready(&ctx);
 }
 
 // Waits (bounded) for the stream; on expiry the communicator is aborted so

@@ -50,12 +50,23 @@ struct s2_dit
     {
         s2::ShardPlan sp;
         s2::AttnSchedule sched[2];
-        int* d_send_rows[2] = {nullptr, nullptr}; // per plan: own rows sent, concatenated over peers
-        std::vector<int> send_counts[2], recv_counts[2];
+        // Peer-visible exchange buffer (same layout on every rank):
+        // qkv [E][3D] bf16 | ctx [E][D] bf16 | text partial [2][T][D] f32 | flags.
+        // The text partial is double-buffered by block parity: a block without
+        // row pushes has no first barrier, so a rank may write block b+1's
+        // partial while a slower rank still sums block b's.
+        void* xbuf = nullptr;
+        size_t off_ctx = 0, off_text = 0, off_flags = 0;
+        std::vector<void*> base;                     // every rank's xbuf (mapped)
+        std::vector<void*> peer_qkv, peer_ctx, peer_text[2], peer_flags;
+        int4* d_push[2] = {nullptr, nullptr};        // {own row, rank, row there, 0}
+        int push_count[2] = {0, 0};
+        bool any_push[2] = {false, false};           // some rank pushes rows for this plan
         ~Shard()
         {
             for (int p = 0; p < 2; p++)
-                if (d_send_rows[p]) cudaFree(d_send_rows[p]);
+                if (d_push[p]) cudaFree(d_push[p]);
+            if (xbuf) cudaFree(xbuf);
         }
     };
     std::map<std::vector<int>, std::unique_ptr<Shard>> shards;
@@ -313,24 +324,61 @@ int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, f
     std::unique_ptr<s2_dit::Shard>& slot = d->shards[key];
     if (!slot)
     {
+        // Collective set-up (every rank builds the same shape): ownership,
+        // schedules, the exchange buffer and its IPC mapping on every peer.
         std::unique_ptr<s2_dit::Shard> sh(new s2_dit::Shard);
         r = s2::build_shard(video_shape, T, cfg.window, cfg.window_mode, rank, world, sh->sp);
+        const s2::ShardPlan& sp = sh->sp;
+        int E = 0;
+        for (int q = 0; q < world && r == S2_OK; q++)
+            E = std::max(E, sp.n_local[q] + T + std::max(sp.m_foreign_all[0][q], sp.m_foreign_all[1][q]));
+        sh->off_ctx = align256((size_t)E * 3 * D * 2);
+        sh->off_text = sh->off_ctx + align256((size_t)E * D * 2);
+        sh->off_flags = sh->off_text + 2 * align256((size_t)T * D * 4);
+        const size_t xbytes = sh->off_flags + 256;
+        if (r == S2_OK && cudaMalloc(&sh->xbuf, xbytes) != cudaSuccess) r = S2_ERR_ALLOC;
+        if (r == S2_OK && cudaMemset(sh->xbuf, 0, xbytes) != cudaSuccess) r = S2_ERR_CUDA;
+        if (r == S2_OK)
+        {
+            if (world > 1)
+                r = dist->share_buffer(c, sh->xbuf, sh->base);
+            else
+                sh->base.assign(1, sh->xbuf);
+        }
+        for (int q = 0; q < world && r == S2_OK; q++)
+        {
+            uint8_t* b = static_cast<uint8_t*>(sh->base[q]);
+            sh->peer_qkv.push_back(b);
+            sh->peer_ctx.push_back(b + sh->off_ctx);
+            sh->peer_text[0].push_back(b + sh->off_text);
+            sh->peer_text[1].push_back(b + sh->off_text + align256((size_t)T * D * 4));
+            sh->peer_flags.push_back(b + sh->off_flags);
+        }
         for (int p = 0; p < 2 && r == S2_OK; p++)
         {
-            r = s2::build_schedule_ex(sh->sp.plan[p], &T, &sh->sp.win_mine[p], &sh->sp.row[p], sh->sched[p],
-                                      c.stream);
-            std::vector<int> rows;
-            for (int q = 0; q < world && r == S2_OK; q++)
+            // context rows of foreign tokens go straight to their owner's buffer
+            std::vector<int> out(sp.Nv, -1);
+            for (int g = 0; g < sp.Nv; g++)
             {
-                rows.insert(rows.end(), sh->sp.send_rows[p][q].begin(), sh->sp.send_rows[p][q].end());
-                sh->send_counts[p].push_back(static_cast<int>(sh->sp.send_rows[p][q].size()));
-                sh->recv_counts[p].push_back(static_cast<int>(sh->sp.recv_tokens[p][q].size()));
+                if (sp.row[p][g] < 0) continue;
+                const int o = sp.token_owner[g];
+                out[g] = o == rank ? sp.token_local[g] : ((o + 1) << s2::kPeerShift) | sp.token_local[g];
             }
-            if (r == S2_OK && !rows.empty())
+            r = s2::build_schedule_ex(sp.plan[p], &T, &sp.win_mine[p], &sp.row[p], sh->sched[p], c.stream, &out);
+            std::vector<int4> push;
+            for (int q = 0; q < world; q++)
             {
-                if (cudaMalloc(&sh->d_send_rows[p], rows.size() * 4) != cudaSuccess)
+                const int base_row = sp.n_local[q] + T + sp.recv_off_all[p][(size_t)q * world + rank];
+                for (size_t k = 0; k < sp.send_tokens[p][q].size(); k++)
+                    push.push_back(make_int4(sp.token_local[sp.send_tokens[p][q][k]], q, base_row + (int)k, 0));
+            }
+            for (int q = 0; q < world; q++) sh->any_push[p] = sh->any_push[p] || sp.m_foreign_all[p][q] > 0;
+            sh->push_count[p] = static_cast<int>(push.size());
+            if (r == S2_OK && !push.empty())
+            {
+                if (cudaMalloc(&sh->d_push[p], push.size() * sizeof(int4)) != cudaSuccess)
                     r = S2_ERR_ALLOC;
-                else if (cudaMemcpy(sh->d_send_rows[p], rows.data(), rows.size() * 4, cudaMemcpyHostToDevice) !=
+                else if (cudaMemcpy(sh->d_push[p], push.data(), push.size() * sizeof(int4), cudaMemcpyHostToDevice) !=
                          cudaSuccess)
                     r = S2_ERR_CUDA;
             }
@@ -345,28 +393,31 @@ int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, f
     s2_dit::Shard& sh = *slot;
     const s2::ShardPlan& sp = sh.sp;
     const int n = sp.n_local[rank];
-    const int M = n + T; // rows of x / h / u
-    const int E = n + T + std::max(sp.m_foreign[0], sp.m_foreign[1]); // qkv / ctx rows (foreign after text)
-    int max_packed = std::max(sh.sched[0].packed_rows, sh.sched[1].packed_rows);
-    int max_partial = std::max(sh.sched[0].partial_rows, sh.sched[1].partial_rows);
-    const size_t sz_h = align256((size_t)M * D * 2), sz_qkv = align256((size_t)E * 3 * D * 2),
-                 sz_pk = align256((size_t)std::max(max_packed, 1) * D * 2), sz_ctx = align256((size_t)E * D * 2),
-                 sz_part = align256((size_t)std::max(max_partial, 1) * D * 4), sz_u = align256((size_t)M * F * 2),
-                 sz_text = align256((size_t)T * D * 4), sz_send = align256((size_t)std::max(std::max(sp.m_send[0], sp.m_send[1]), 1) * 3 * D * 2);
-    if ((r = d->act.ensure(sz_h + sz_qkv + 3 * sz_pk + sz_ctx + sz_part + sz_u + sz_text + sz_send)) != S2_OK) return r;
+    const int M = n + T; // rows of x / h / u (own video rows, then text)
+    const int max_packed = std::max(sh.sched[0].packed_rows, sh.sched[1].packed_rows);
+    const int max_partial = std::max(sh.sched[0].partial_rows, sh.sched[1].partial_rows);
+    const size_t sz_h = align256((size_t)M * D * 2), sz_pk = align256((size_t)std::max(max_packed, 1) * D * 2),
+                 sz_part = align256((size_t)std::max(max_partial, 1) * D * 4), sz_u = align256((size_t)M * F * 2);
+    if ((r = d->act.ensure(sz_h + 3 * sz_pk + sz_part + sz_u)) != S2_OK) return r;
     if ((r = d->mods.ensure((size_t)cfg.num_blocks * 6 * D * 4)) != S2_OK) return r;
     uint8_t* a = static_cast<uint8_t*>(d->act.ptr);
     __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(a);
-    __nv_bfloat16* qkv = reinterpret_cast<__nv_bfloat16*>(a + sz_h);
-    uint8_t* pk = a + sz_h + sz_qkv;
-    __nv_bfloat16* ctxb = reinterpret_cast<__nv_bfloat16*>(pk + 3 * sz_pk);
-    float* partial = reinterpret_cast<float*>(pk + 3 * sz_pk + sz_ctx);
-    __nv_bfloat16* u = reinterpret_cast<__nv_bfloat16*>(pk + 3 * sz_pk + sz_ctx + sz_part);
-    float* text32 = reinterpret_cast<float*>(pk + 3 * sz_pk + sz_ctx + sz_part + sz_u);
-    __nv_bfloat16* sendbuf = reinterpret_cast<__nv_bfloat16*>(pk + 3 * sz_pk + sz_ctx + sz_part + sz_u + sz_text);
+    uint8_t* pk = a + sz_h;
+    float* partial = reinterpret_cast<float*>(pk + 3 * sz_pk);
+    __nv_bfloat16* u = reinterpret_cast<__nv_bfloat16*>(pk + 3 * sz_pk + sz_part);
+    __nv_bfloat16* qkv = static_cast<__nv_bfloat16*>(sh.xbuf);
+    __nv_bfloat16* ctxb = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(sh.xbuf) + sh.off_ctx);
+    float* text32_buf[2] = {reinterpret_cast<float*>(static_cast<uint8_t*>(sh.xbuf) + sh.off_text),
+                            reinterpret_cast<float*>(static_cast<uint8_t*>(sh.xbuf) + sh.off_text +
+                                                     align256((size_t)T * D * 4))};
+    uint32_t* my_flags = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(sh.xbuf) + sh.off_flags);
     float* mods = static_cast<float*>(d->mods.ptr);
     if ((r = s2::launch_add_vectors(c, d->ada_all, modulation, mods, cfg.num_blocks * 6 * D, 6 * D)) != S2_OK)
         return r;
+    auto barrier = [&]() -> int {
+        if (world == 1) return S2_OK;
+        return s2::launch_peer_barrier(c, sh.peer_flags.data(), my_flags, rank, world, ++dist->epoch);
+    };
 
     for (int b = 0; b < cfg.num_blocks; b++)
     {
@@ -378,16 +429,13 @@ int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, f
         if ((r = s2::launch_shared_linear(c, M, 0, 3 * D, D, h, nullptr, bl.w_qkv, cfg.qkv_bias ? bl.b_qkv : nullptr,
                                           s2::EPI_STORE, nullptr, 0, qkv, nullptr)) != S2_OK)
             return r;
-        const bool xchg = world > 1 && (sp.m_send[shf] > 0 || sp.m_foreign[shf] > 0);
-        if (xchg)
+        if (world > 1 && sh.any_push[shf])
         {
-            // own qkv rows of tokens in other ranks' windows -> the window owners
-            if ((r = s2::launch_gather_rows_bf16(c, qkv, sh.d_send_rows[shf], sp.m_send[shf], 3 * D, sendbuf)) !=
-                S2_OK)
+            // own qkv rows of tokens in other ranks' windows -> straight into the owners' buffers
+            if ((r = s2::launch_push_rows(c, qkv, 3 * D, sh.d_push[shf], sh.push_count[shf], sh.peer_qkv.data(),
+                                          world)) != S2_OK)
                 return r;
-            if ((r = dist->exchange_bf16(sendbuf, sh.send_counts[shf], sp.send_off[shf], qkv + (size_t)(n + T) * 3 * D,
-                                         sh.recv_counts[shf], sp.recv_off[shf], (size_t)3 * D, c.stream)) != S2_OK)
-                return r;
+            if ((r = barrier()) != S2_OK) return r;
         }
         __nv_bfloat16* Qp = reinterpret_cast<__nv_bfloat16*>(pk);
         __nv_bfloat16* Kp = reinterpret_cast<__nv_bfloat16*>(pk + sz_pk);
@@ -397,18 +445,21 @@ int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, f
                                         qkv + D, qkv + 2 * D, 3 * D, tq, tq + D, tq + 2 * D, 3 * D, Qp, Kp, Vp)) !=
             S2_OK)
             return r;
-        if ((r = s2::launch_window_attention(c, S, H, Qp, Kp, Vp, 0, 0, ctxb, partial)) != S2_OK) return r;
-        if ((r = s2::launch_text_pool(c, S, D, partial, 1, 0, text32)) != S2_OK) return r;
-        if (world > 1 && (r = dist->all_reduce_sum_f32(text32, (size_t)T * D, c.stream)) != S2_OK) return r;
-        if ((r = s2::launch_convert_f32_bf16(c, text32, ctxb + (size_t)n * D, (int64_t)T * D)) != S2_OK) return r;
-        if (xchg)
+        // context rows of foreign tokens are stored into their owners' buffers by the epilogue
+        if ((r = s2::launch_window_attention(c, S, H, Qp, Kp, Vp, 0, 0, ctxb, partial, sh.peer_ctx.data(),
+                                             world > 1 ? world : 0)) != S2_OK)
+            return r;
+        if (world == 1)
         {
-            // context rows of foreign tokens back to their owners
-            if ((r = dist->exchange_bf16(ctxb + (size_t)(n + T) * D, sh.recv_counts[shf], sp.recv_off[shf], sendbuf,
-                                         sh.send_counts[shf], sp.send_off[shf], (size_t)D, c.stream)) != S2_OK)
-                return r;
-            if ((r = s2::launch_scatter_rows_bf16(c, sendbuf, sh.d_send_rows[shf], sp.m_send[shf], D, ctxb)) !=
-                S2_OK)
+            if ((r = s2::launch_text_pool(c, S, D, partial, 0, 0, ctxb + (size_t)n * D)) != S2_OK) return r;
+        }
+        else
+        {
+            if ((r = s2::launch_text_pool(c, S, D, partial, 1, 0, text32_buf[b & 1])) != S2_OK) return r;
+            if ((r = barrier()) != S2_OK) return r;
+            // text rows: sum of every rank's partial, read over NVLink in rank order
+            if ((r = s2::launch_text_reduce_peers(c, sh.peer_text[b & 1].data(), world, (int64_t)T * D,
+                                                  ctxb + (size_t)n * D)) != S2_OK)
                 return r;
         }
         if ((r = s2::launch_shared_linear(c, M, 0, D, D, ctxb, nullptr, bl.w_out, cfg.out_bias ? bl.b_out : nullptr,

@@ -155,7 +155,7 @@ AttnSchedule::~AttnSchedule()
 
 int build_schedule(const Plan& plan, const int* text_lengths, AttnSchedule& s, cudaStream_t stream)
 {
-    return build_schedule_ex(plan, text_lengths, nullptr, nullptr, s, stream);
+    return build_schedule_ex(plan, text_lengths, nullptr, nullptr, s, stream, nullptr);
 }
 
 // Schedule over a subset of the plan's windows (nullptr = all), with video
@@ -164,7 +164,8 @@ int build_schedule(const Plan& plan, const int* text_lengths, AttnSchedule& s, c
 // sample's GLOBAL window count, so per-rank partial sums add up to the mean
 // (adaptive_window_attention.cpp:963-974).
 int build_schedule_ex(const Plan& plan, const int* text_lengths, const std::vector<int>* windows_subset,
-                      const std::vector<int>* row_of_token, AttnSchedule& s, cudaStream_t stream)
+                      const std::vector<int>* row_of_token, AttnSchedule& s, cudaStream_t stream,
+                      const std::vector<int>* out_of_token)
 {
     const int nw_all = static_cast<int>(plan.windows.size() / 9);
     std::vector<int> wsel;
@@ -177,6 +178,8 @@ int build_schedule_ex(const Plan& plan, const int* text_lengths, const std::vect
     }
     const int nw = static_cast<int>(wsel.size());
     auto row_of = [&](int token) { return row_of_token ? (*row_of_token)[token] : token; };
+    // where the attention epilogue stores the token's context row (defaults to its input row)
+    auto out_of = [&](int token) { return out_of_token ? (*out_of_token)[token] : row_of(token); };
     std::vector<int> text_offset(plan.batch, 0);
     int total_text = 0, max_text = 0;
     for (int b = 0; b < plan.batch; b++)
@@ -206,10 +209,11 @@ int build_schedule_ex(const Plan& plan, const int* text_lengths, const std::vect
         win_pool[k] = pool;
         for (int r = 0; r < L; r++)
         {
-            const int row = row_of(plan.video_indices[part + r]);
-            if (row < 0) return S2_ERR_PLAN;
+            const int token = plan.video_indices[part + r];
+            const int row = row_of(token);
+            if (row < 0 || out_of(token) < 0) return S2_ERR_PLAN;
             row_src.push_back(row);
-            vidx.push_back(row);
+            vidx.push_back(out_of(token));
             // video RoPE position: window-local (t + text_len, h, w) (:904-905)
             row_pos.push_back(plan.local_positions[3 * (part + r)] + T);
             row_pos.push_back(plan.local_positions[3 * (part + r) + 1]);

@@ -31,6 +31,10 @@ struct ShardPlan
     std::vector<std::vector<int>> recv_tokens[2]; // [world] foreign tokens received from each rank
     std::vector<int> send_off[2], recv_off[2];    // [world] prefix offsets (rows)
     int m_foreign[2] = {0, 0}, m_send[2] = {0, 0};
+    // every rank's view: recv_off_all[p][q * world + s] = where rank q stores
+    // the rows it receives from rank s (after its own rows and text rows);
+    // m_foreign_all[p][q] = rows rank q receives
+    std::vector<int> recv_off_all[2], m_foreign_all[2];
 };
 
 int build_shard(const int* shape, int text_length, const int* window, int window_mode, int rank, int world,
@@ -47,14 +51,26 @@ struct Dist
     bool aborted = false;
     int init(const void* id128, int rank, int world, int timeout_ms);
     void destroy();
-    int wait_ready();
+    int wait_ready(Context* ctx = nullptr);
     int fail(int code);
-    int all_reduce_sum_f32(float* buf, size_t count, cudaStream_t stream);
-    int exchange_bf16(const void* send, const std::vector<int>& send_counts, const std::vector<int>& send_off,
-                      void* recv, const std::vector<int>& recv_counts, const std::vector<int>& recv_off,
-                      size_t row_elems, cudaStream_t stream);
+    int all_reduce_sum_f32(Context& ctx, float* buf, size_t count);
+    int exchange_bf16(Context& ctx, const void* send, const std::vector<int>& send_counts,
+                      const std::vector<int>& send_off, void* recv, const std::vector<int>& recv_counts,
+                      const std::vector<int>& recv_off, size_t row_elems);
     int sync(cudaStream_t stream);
+    // Maps every rank's `local` allocation into this process (CUDA IPC, handles
+    // all-gathered over NCCL); peers[r] is rank r's base (peers[rank] = local).
+    int share_buffer(Context& ctx, void* local, std::vector<void*>& peers);
+    std::vector<void*> opened; // IPC mappings to close on destroy
+    uint32_t epoch = 0;        // cross-GPU barrier generation
 };
+
+// NVLink peer-memory kernels (peer.cu)
+int launch_push_rows(Context& ctx, const void* src, int row_elems, const int4* table, int count, void* const* dst,
+                     int world);
+int launch_peer_barrier(Context& ctx, void* const* peer_flags, uint32_t* my_flags, int rank, int world,
+                        uint32_t epoch);
+int launch_text_reduce_peers(Context& ctx, void* const* parts, int world, int64_t count, void* out_bf16);
 
 // Row gather / scatter of bf16 rows (row_elems multiple of 8):
 //   gather:  dst[i] = src[idx[i]]     scatter: dst[idx[i]] = src[i]

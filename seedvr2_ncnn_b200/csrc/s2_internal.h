@@ -38,6 +38,8 @@ enum KernelKind
     K_NORM = S2_KERNEL_ADA_RMSNORM,
     K_POOL = S2_KERNEL_TEXT_POOL,
     K_OTHER = S2_KERNEL_OTHER,
+    K_COMM = S2_KERNEL_COMM,
+    K_HOST_WAIT = S2_KERNEL_HOST_WAIT,
     K_NUM = S2_NUM_KERNEL_KINDS,
 };
 
@@ -125,7 +127,14 @@ struct AttnSchedule
 
 int build_schedule(const Plan& plan, const int* text_lengths, AttnSchedule& sched, cudaStream_t stream);
 int build_schedule_ex(const Plan& plan, const int* text_lengths, const std::vector<int>* windows_subset,
-                      const std::vector<int>* row_of_token, AttnSchedule& sched, cudaStream_t stream);
+                      const std::vector<int>* row_of_token, AttnSchedule& sched, cudaStream_t stream,
+                      const std::vector<int>* out_of_token = nullptr);
+
+// Output rows of the attention epilogue may live on a peer GPU: an entry of
+// AttnSchedule::video_indices is row | (peer + 1) << kPeerShift, and the
+// launcher is given the peers' output bases (NVLink peer memory).
+constexpr int kPeerShift = 26;
+constexpr int kMaxPeers = 8;
 
 int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                       uint32_t box_inner, uint32_t box_outer);
@@ -140,7 +149,8 @@ int launch_prepare_qkv(Context& ctx, const AttnSchedule& s, int heads, int head_
                        void* q_out, void* k_out, void* v_out);
 
 int launch_window_attention(Context& ctx, const AttnSchedule& s, int heads, const void* q, const void* k,
-                            const void* v, int out_f32, int round_bf16, void* video_out, float* text_partial);
+                            const void* v, int out_f32, int round_bf16, void* video_out, float* text_partial,
+                            void* const* peer_out = nullptr, int num_peers = 0);
 
 int launch_text_pool(Context& ctx, const AttnSchedule& s, int inner, const float* partial, int out_f32,
                      int round_bf16, void* text_out);
