@@ -59,7 +59,6 @@ struct AttnArgs
     // peer output bases (multi-GPU): a video_indices entry with a non-zero
     // peer field is stored into peer_out[peer - 1] over NVLink
     void* peer_out[kMaxPeers];
-    int any_peer;
 };
 
 __device__ __forceinline__ float ex2(float x)
@@ -231,12 +230,14 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity)
 // Stores 32 output columns [col0, col0+32) of query row qi of the window with
 // 32-byte (full-sector) stores: video rows to their source token, text rows
 // to the window's fp32 partial.
-__device__ __forceinline__ void store_row(const AttnArgs& a, int item_window, int part_off, int L, int qi, int col0,
+// Returns true when the row went to a peer GPU.
+__device__ __forceinline__ bool store_row(const AttnArgs& a, int item_window, int part_off, int L, int qi, int col0,
                                           const float* o, float inv)
 {
     const bool video = qi < L;
     int src = 0;
     void* vbase = a.video_out;
+    bool remote = false;
     if (video)
     {
         src = a.video_indices[part_off + qi];
@@ -245,6 +246,7 @@ __device__ __forceinline__ void store_row(const AttnArgs& a, int item_window, in
         {
             vbase = a.peer_out[peer - 1];
             src &= (1 << kPeerShift) - 1;
+            remote = true;
         }
     }
     if (video && !a.out_f32)
@@ -258,7 +260,7 @@ __device__ __forceinline__ void store_row(const AttnArgs& a, int item_window, in
             for (int k = 0; k < 8; k++) r[k] = pack_bf16x2(o[i + 2 * k] * inv, o[i + 2 * k + 1] * inv);
             st_v8(dst + i, r);
         }
-        return;
+        return remote;
     }
     float* dst = video ? reinterpret_cast<float*>(vbase) + (size_t)src * a.inner + col0
                        : a.text_partial + (size_t)(a.win_pool[item_window] + (qi - L)) * a.inner + col0;
@@ -275,6 +277,7 @@ __device__ __forceinline__ void store_row(const AttnArgs& a, int item_window, in
         }
         st_v8(dst + i, r);
     }
+    return remote;
 }
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -502,6 +505,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tc_fence_after();
                 const int qi = qbase + row;
                 const float inv = 1.f / l_run;
+                bool remote = false;
 #pragma unroll 1
                 for (int c = 0; c < 4; c++)
                 {
@@ -513,12 +517,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         float o[32];
 #pragma unroll
                         for (int i = 0; i < 32; i++) o[i] = __uint_as_float(v[i]);
-                        store_row(args, item.x, part_off, L, qi, head * HD + c * 32, o, inv);
+                        remote |= store_row(args, item.x, part_off, L, qi, head * HD + c * 32, o, inv);
                     }
                 }
-                // rows stored into peer GPUs must be visible to them once this
+                // a row stored into a peer GPU must be visible there once this
                 // rank passes its next cross-GPU barrier
-                if (args.any_peer) __threadfence_system();
+                if (remote) __threadfence_system();
             }
         }
     }
@@ -561,7 +565,6 @@ int launch_window_attention(Context& ctx, const AttnSchedule& s, int heads, cons
     a.text_partial = text_partial;
     a.status = ctx.status;
     for (int i = 0; i < kMaxPeers; i++) a.peer_out[i] = i < num_peers ? peer_out[i] : nullptr;
-    a.any_peer = num_peers > 0;
     static bool configured = false;
     if (!configured)
     {

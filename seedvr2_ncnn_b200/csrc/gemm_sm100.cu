@@ -9,8 +9,10 @@
 //     one of two TMEM accumulators (2 x 256 columns), so the epilogue of tile
 //     i overlaps the MMAs of tile i+1;
 //   * four epilogue warps drain TMEM with tcgen05.ld (one accumulator row per
-//     thread) and apply bias and the fused epilogue (store, GELU-tanh, or
-//     gate * acc + fp32 residual);
+//     thread), apply bias and the fused epilogue (store, GELU-tanh, or
+//     gate * acc + fp32 residual), stage each 32-row x 128-byte box in
+//     128-byte-swizzled shared memory (two boxes per warp in flight) and
+//     write it with one TMA store, so global writes are whole lines;
 //   * every mbarrier wait is bounded (s2_common.cuh) and unwinds the CTA.
 #include "s2_common.cuh"
 #include "s2_internal.h"
@@ -26,16 +28,25 @@ constexpr int GROUP_M = 16;
 constexpr int NUM_THREADS = 192; // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 
 // Tile width BN (256, or 128 when a problem has too few 256-wide tiles to
-// fill the SMs evenly): 192 KB of stages either way.
-template <int BN>
+// fill the SMs evenly).  224 KB of shared memory is split between SKB KB of
+// operand stages and the epilogue's 4 KB boxes (R per epilogue warp):
+//   * SKB = 192: R = 2 (store double buffering; a gate-residual epilogue
+//     (GR) loads its residual box one box ahead);
+//   * SKB = 144, GR only: R = 5 or 6, so each warp keeps R-1 residual boxes
+//     in flight from HBM -- for short K, where the epilogue of a tile has
+//     little mainloop time to hide behind.
+template <int BN, int SKB, bool GR>
 struct Tile
 {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+    static constexpr int STAGES = (SKB * 1024) / STAGE_BYTES;
+    static constexpr int R = (224 * 1024 - STAGES * STAGE_BYTES) / (4 * 4096);
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN, 0, 0);
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int EPI_BYTES = 4 * R * 4096; // 4 warps x R boxes of 32 rows x 128 bytes
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 512;
+    static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
 struct GemmArgs
@@ -44,6 +55,7 @@ struct GemmArgs
     int mblk0, mblk1, nblk, num_tiles, num_kb;
     int epilogue;
     int out_f32;
+    int tma_out; // outputs written through tmap_o0 / tmap_o1
     const float* bias;
     const float* gate;
     void* out0;
@@ -175,23 +187,293 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int stream, in
     }
 }
 
+// Epilogue of one tile for one warp (accumulator rows quarter*32 .. +31)
+// through shared-memory staging and TMA stores: each 128-byte-wide box
+// (32 fp32 or 64 bf16 columns x 32 rows) is written by the lanes in the
+// 128-byte swizzle (16-byte unit u of row r at unit u ^ (r & 7), which is
+// free of bank conflicts) and stored by lane 0.  `stg` holds the warp's two
+// 4 KB boxes; `slot` alternates between them.
 template <int BN>
+__device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const CUtensorMap* tmap_out, uint8_t* stg, int& slot,
+                                                  uint32_t t_row, int stream, int m0, int n0, int quarter, int lane)
+{
+    const int M = stream ? a.M1 : a.M0;
+    const int N = a.N;
+    const int row = m0 + quarter * 32 + lane;
+    const bool live = row < M;
+    const bool box_live = m0 + quarter * 32 < M;
+    const int box_cols = a.out_f32 ? 32 : 64;
+    const float* res_row = reinterpret_cast<const float*>(stream ? a.out1 : a.out0) + (size_t)row * N;
+    const int sw = lane & 7;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN && n0 + c0 < N; c0 += box_cols)
+    {
+        if (lane == 0) bulk_wait_read<1>(); // this slot's previous store has read it
+        __syncwarp();
+        uint8_t* srow = stg + slot * 4096 + lane * 128;
+#pragma unroll 1
+        for (int k = 0; k < box_cols / 32; k++)
+        {
+            const int n = n0 + c0 + 32 * k;
+            const bool full = n + 32 <= N;
+            float4 r[8];
+            if (a.epilogue == EPI_GATE_RESIDUAL)
+            {
+                if (live && full)
+                {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) r[j] = *reinterpret_cast<const float4*>(res_row + n + 4 * j);
+                }
+                else
+                {
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                    {
+                        float e[4];
+#pragma unroll
+                        for (int q = 0; q < 4; q++) e[q] = (live && n + 4 * j + q < N) ? res_row[n + 4 * j + q] : 0.f;
+                        r[j] = make_float4(e[0], e[1], e[2], e[3]);
+                    }
+                }
+            }
+            uint32_t v[32];
+            tmem_ld32(t_row + c0 + 32 * k, v);
+            tmem_ld_wait();
+            float x[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++) x[j] = __uint_as_float(v[j]);
+            if (a.bias)
+            {
+                if (full)
+                {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                    {
+                        const float4 b = __ldg(reinterpret_cast<const float4*>(a.bias + n + j));
+                        x[j] += b.x;
+                        x[j + 1] += b.y;
+                        x[j + 2] += b.z;
+                        x[j + 3] += b.w;
+                    }
+                }
+                else
+                {
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (n + j < N) x[j] += __ldg(a.bias + n + j);
+                }
+            }
+            if (a.epilogue == EPI_GATE_RESIDUAL)
+            {
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                {
+                    float4 g;
+                    if (full)
+                        g = __ldg(reinterpret_cast<const float4*>(a.gate + n + 4 * j));
+                    else
+                    {
+                        g.x = n + 4 * j < N ? __ldg(a.gate + n + 4 * j) : 0.f;
+                        g.y = n + 4 * j + 1 < N ? __ldg(a.gate + n + 4 * j + 1) : 0.f;
+                        g.z = n + 4 * j + 2 < N ? __ldg(a.gate + n + 4 * j + 2) : 0.f;
+                        g.w = n + 4 * j + 3 < N ? __ldg(a.gate + n + 4 * j + 3) : 0.f;
+                    }
+                    x[4 * j] = r[j].x + x[4 * j] * g.x;
+                    x[4 * j + 1] = r[j].y + x[4 * j + 1] * g.y;
+                    x[4 * j + 2] = r[j].z + x[4 * j + 2] * g.z;
+                    x[4 * j + 3] = r[j].w + x[4 * j + 3] * g.w;
+                }
+            }
+            else if (a.epilogue == EPI_GELU_TANH)
+            {
+#pragma unroll
+                for (int j = 0; j < 32; j++) x[j] = gelu_tanh(x[j]);
+            }
+            if (a.out_f32)
+            {
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    *reinterpret_cast<float4*>(srow + ((j ^ sw) << 4)) =
+                        make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
+            }
+            else
+            {
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                {
+                    uint4 p;
+                    p.x = pack_bf16x2(x[8 * j], x[8 * j + 1]);
+                    p.y = pack_bf16x2(x[8 * j + 2], x[8 * j + 3]);
+                    p.z = pack_bf16x2(x[8 * j + 4], x[8 * j + 5]);
+                    p.w = pack_bf16x2(x[8 * j + 6], x[8 * j + 7]);
+                    *reinterpret_cast<uint4*>(srow + (((4 * k + j) ^ sw) << 4)) = p;
+                }
+            }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0)
+        {
+            if (box_live) tma_store_2d(tmap_out, stg + slot * 4096, n0 + c0, m0 + quarter * 32);
+            bulk_commit();
+        }
+        slot ^= 1;
+    }
+}
+
+// Gate-residual epilogue of one warp over all of the CTA's tiles, fp32
+// residual in place: out = out + (acc + bias) * gate.  Boxes (32 rows x 32
+// columns) run in a fixed sequence over the CTA's tiles; lane 0 TMA-loads the
+// residual box R-1 boxes ahead into one of the warp's R shared-memory boxes
+// (barrier rfull[slot]), the lanes combine it with the accumulator row in
+// place, and lane 0 TMA-stores it back.  A box is reloaded only after its
+// previous store has read it.  Returns false on a failed wait.
+template <int BN, int R>
+__device__ __forceinline__ bool epilogue_gate_residual(const GemmArgs& a, const CUtensorMap* tmap_o0,
+                                                       const CUtensorMap* tmap_o1, uint8_t* stg, uint64_t* rfull,
+                                                       uint64_t* tfull, uint64_t* tempty, uint32_t tmem_base,
+                                                       int quarter, int lane, volatile int* abort_flag)
+{
+    const int N = a.N;
+    const int sw = lane & 7;
+    // loader cursor (lane 0): next box to load
+    int lt = blockIdx.x, lc = 0, lq = 0;
+    auto issue_load = [&]() {
+        if (lt >= a.num_tiles) return;
+        int s_, m0_, n0_;
+        decode_tile<BN>(a, lt, s_, m0_, n0_);
+        const int slot = lq % R;
+        mbar_arrive_expect_tx(&rfull[slot], 4096);
+        tma_load_2d(stg + slot * 4096, s_ ? tmap_o1 : tmap_o0, &rfull[slot], n0_ + lc, m0_ + quarter * 32);
+        lq++;
+        lc += 32;
+        if (lc >= BN || n0_ + lc >= N)
+        {
+            lc = 0;
+            lt += gridDim.x;
+        }
+    };
+    if (lane == 0)
+        for (int i = 0; i < R - 1; i++) issue_load();
+    int q = 0; // boxes consumed
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < a.num_tiles && ok; t += gridDim.x)
+    {
+        int w = 0;
+        if (lane == 0) w = mbar_wait(&tfull[acc], acc_phase, abort_flag, a.status) ? 1 : 0;
+        w = __shfl_sync(0xffffffffu, w, 0);
+        if (!w)
+        {
+            ok = false;
+            break;
+        }
+        __syncwarp();
+        tc_fence_after();
+        int stream, m0, n0;
+        decode_tile<BN>(a, t, stream, m0, n0);
+        const int M = stream ? a.M1 : a.M0;
+        const bool box_live = m0 + quarter * 32 < M;
+        const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN && n0 + c0 < N; c0 += 32, q++)
+        {
+            const int slot = q % R;
+            int r = 0;
+            if (lane == 0) r = mbar_wait(&rfull[slot], (uint32_t)(q / R) & 1u, abort_flag, a.status) ? 1 : 0;
+            r = __shfl_sync(0xffffffffu, r, 0);
+            if (!r)
+            {
+                ok = false;
+                break;
+            }
+            uint8_t* srow = stg + slot * 4096 + lane * 128;
+            const int n = n0 + c0;
+            const bool full = n + 32 <= N;
+            uint32_t v[32];
+            tmem_ld32(t_row + c0, v);
+            float4 res[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) res[j] = *reinterpret_cast<const float4*>(srow + ((j ^ sw) << 4));
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+            {
+                float4 g, b = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (full)
+                {
+                    g = __ldg(reinterpret_cast<const float4*>(a.gate + n + 4 * j));
+                    if (a.bias) b = __ldg(reinterpret_cast<const float4*>(a.bias + n + 4 * j));
+                }
+                else
+                {
+                    float ge[4], be[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++)
+                    {
+                        const bool in = n + 4 * j + e < N;
+                        ge[e] = in ? __ldg(a.gate + n + 4 * j + e) : 0.f;
+                        be[e] = (in && a.bias) ? __ldg(a.bias + n + 4 * j + e) : 0.f;
+                    }
+                    g = make_float4(ge[0], ge[1], ge[2], ge[3]);
+                    b = make_float4(be[0], be[1], be[2], be[3]);
+                }
+                float4 o;
+                o.x = res[j].x + (__uint_as_float(v[4 * j]) + b.x) * g.x;
+                o.y = res[j].y + (__uint_as_float(v[4 * j + 1]) + b.y) * g.y;
+                o.z = res[j].z + (__uint_as_float(v[4 * j + 2]) + b.z) * g.z;
+                o.w = res[j].w + (__uint_as_float(v[4 * j + 3]) + b.w) * g.w;
+                *reinterpret_cast<float4*>(srow + ((j ^ sw) << 4)) = o;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0)
+            {
+                if (box_live) tma_store_2d(stream ? tmap_o1 : tmap_o0, stg + slot * 4096, n, m0 + quarter * 32);
+                bulk_commit();
+                bulk_wait_read<1>(); // the store of box q-1 has read box (q-1) % R
+                issue_load();        // box q+R-1 into it
+            }
+        }
+        if (!ok) break;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+    }
+    if (lane == 0)
+    {
+        // no TMA load may land after the CTA exits
+        for (int i = q; i < lq; i++) drain_wait(&rfull[i % R], (uint32_t)(i / R) & 1u);
+        bulk_wait<0>();
+    }
+    __syncwarp();
+    return ok;
+}
+
+template <int BN, int SKB, bool GR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     shared_linear_kernel(const __grid_constant__ CUtensorMap tmap_a0, const __grid_constant__ CUtensorMap tmap_a1,
-                         const __grid_constant__ CUtensorMap tmap_w, const GemmArgs args)
+                         const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_o0,
+                         const __grid_constant__ CUtensorMap tmap_o1, const GemmArgs args)
 {
-    constexpr int STAGES = Tile<BN>::STAGES;
-    constexpr int STAGE_BYTES = Tile<BN>::STAGE_BYTES;
-    constexpr int TMEM_COLS = Tile<BN>::TMEM_COLS;
-    constexpr uint32_t IDESC = Tile<BN>::IDESC;
+    using TL = Tile<BN, SKB, GR>;
+    constexpr int STAGES = TL::STAGES;
+    constexpr int STAGE_BYTES = TL::STAGE_BYTES;
+    constexpr int TMEM_COLS = TL::TMEM_COLS;
+    constexpr uint32_t IDESC = TL::IDESC;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint8_t* epi_stage = smem + STAGES * STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + TL::EPI_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* rfull = drain + 1; // [4 warps][R] residual boxes (GR)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rfull + 4 * TL::R);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -210,11 +492,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(&tempty[b], 4);
         }
         mbar_init(drain, 1);
+        if (GR)
+            for (int i = 0; i < 4 * TL::R; i++) mbar_init(&rfull[i], 1);
         *abort_flag = 0;
         fence_mbarrier_init();
         tma_prefetch_desc(&tmap_a0);
         tma_prefetch_desc(&tmap_a1);
         tma_prefetch_desc(&tmap_w);
+        if (args.tma_out)
+        {
+            tma_prefetch_desc(&tmap_o0);
+            tma_prefetch_desc(&tmap_o1);
+        }
     }
     if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
     tc_fence_before();
@@ -321,32 +610,53 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // ---------------- epilogue (warps 2..5)
         const int quarter = warp & 3;
         const int row_in_tile = quarter * 32 + lane;
-        int acc = 0;
-        uint32_t acc_phase = 0;
-        for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x)
+        uint8_t* stg = epi_stage + quarter * (TL::R * 4096);
+        if constexpr (GR)
         {
-            int ok = 0;
-            if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, args.status) ? 1 : 0;
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) break;
-            __syncwarp();
-            tc_fence_after();
-            int stream, m0, n0;
-            decode_tile<BN>(args, t, stream, m0, n0);
-            const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; c++)
+            epilogue_gate_residual<BN, TL::R>(args, &tmap_o0, &tmap_o1, stg, rfull + quarter * TL::R, tfull, tempty,
+                                              tmem_base, quarter, lane, abort_flag);
+        }
+        else
+        {
+            int slot = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x)
             {
-                uint32_t v[32];
-                tmem_ld32(t_row + c * 32, v);
-                tmem_ld_wait();
-                if (n0 + c * 32 < args.N) epilogue_chunk(args, stream, m0 + row_in_tile, n0 + c * 32, v);
+                int ok = 0;
+                if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, args.status) ? 1 : 0;
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                __syncwarp();
+                tc_fence_after();
+                int stream, m0, n0;
+                decode_tile<BN>(args, t, stream, m0, n0);
+                const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+                if (args.tma_out)
+                {
+                    epilogue_tile_tma<BN>(args, stream ? &tmap_o1 : &tmap_o0, stg, slot, t_row, stream, m0, n0,
+                                          quarter, lane);
+                }
+                else
+                {
+#pragma unroll 1
+                    for (int c = 0; c < BN / 32; c++)
+                    {
+                        uint32_t v[32];
+                        tmem_ld32(t_row + c * 32, v);
+                        tmem_ld_wait();
+                        if (n0 + c * 32 < args.N) epilogue_chunk(args, stream, m0 + row_in_tile, n0 + c * 32, v);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[acc]);
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1;
             }
-            tc_fence_before();
+            // every TMA store of this warp has completed before the CTA exits
+            if (lane == 0) bulk_wait<0>();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[acc]);
-            acc ^= 1;
-            if (acc == 0) acc_phase ^= 1;
         }
     }
 
@@ -354,6 +664,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+template <int BN, int SKB, bool GR>
+cudaError_t launch_variant(int grid, cudaStream_t stream, const CUtensorMap& ta0, const CUtensorMap& ta1,
+                           const CUtensorMap& tw, const CUtensorMap& to0, const CUtensorMap& to1, const GemmArgs& a)
+{
+    static bool configured = false; // per instantiation
+    if (!configured)
+    {
+        const cudaError_t e =
+            cudaFuncSetAttribute(shared_linear_kernel<BN, SKB, GR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Tile<BN, SKB, GR>::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    shared_linear_kernel<BN, SKB, GR>
+        <<<grid, NUM_THREADS, Tile<BN, SKB, GR>::SMEM_BYTES, stream>>>(ta0, ta1, tw, to0, to1, a);
+    return cudaGetLastError();
 }
 
 } // namespace
@@ -373,6 +701,18 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
     if (r == 0) r = make_tmap_bf16_2d(&ta1, M1 > 0 ? A1 : A0, K, M1 > 0 ? M1 : (M0 > 0 ? M0 : 1), (uint64_t)K * 2, BK, BM);
     if (r == 0) r = make_tmap_bf16_2d(&tw, W, K, N, (uint64_t)K * 2, BK, 256);
     if (r != 0) return r;
+    // TMA-store epilogue when both outputs admit a tensor map (16-byte aligned
+    // bases and row strides); the per-thread store path otherwise.
+    CUtensorMap to0, to1;
+    const uint32_t esz = out_f32 ? 4 : 2;
+    const uint32_t box_cols = 128 / esz;
+    int tma_out = (((uint64_t)N * esz) % 16 == 0) ? 1 : 0;
+    if (tma_out)
+        tma_out = make_tmap_2d(&to0, out0, out_f32, N, M0 > 0 ? M0 : 1, (uint64_t)N * esz, box_cols, 32) == S2_OK;
+    if (tma_out)
+        tma_out = make_tmap_2d(&to1, M1 > 0 ? out1 : out0, out_f32, N, M1 > 0 ? M1 : (M0 > 0 ? M0 : 1),
+                               (uint64_t)N * esz, box_cols, 32) == S2_OK;
+    if (!tma_out) to1 = to0 = tw;
 
     GemmArgs a;
     a.M0 = M0;
@@ -384,6 +724,7 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
     a.num_kb = (K + BK - 1) / BK;
     a.epilogue = epilogue;
     a.out_f32 = out_f32;
+    a.tma_out = tma_out;
     a.bias = bias;
     a.gate = gate;
     a.out0 = out0;
@@ -401,25 +742,22 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
     a.nblk = (N + BNsel - 1) / BNsel;
     a.num_tiles = (a.mblk0 + a.mblk1) * a.nblk;
     if (narrow && (r = make_tmap_bf16_2d(&tw, W, K, N, (uint64_t)K * 2, BK, 128)) != 0) return r;
-    static bool configured[2] = {false, false};
-    if (!configured[narrow])
-    {
-        const cudaError_t e =
-            narrow ? cudaFuncSetAttribute(shared_linear_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          Tile<128>::SMEM_BYTES)
-                   : cudaFuncSetAttribute(shared_linear_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          Tile<256>::SMEM_BYTES);
-        if (e != cudaSuccess) return S2_ERR_CUDA;
-        configured[narrow] = true;
-    }
+    const bool gr = tma_out && epilogue == EPI_GATE_RESIDUAL;
     const int grid = a.num_tiles < ctx.num_sms ? a.num_tiles : ctx.num_sms;
     const double M = (double)M0 + M1;
     const double out_bytes = epilogue == EPI_GATE_RESIDUAL ? 8.0 : (out_f32 ? 4.0 : 2.0);
     ProfileScope prof(ctx, K_GEMM, 2.0 * M * N * K, (M * K + (double)N * K) * 2.0 + M * N * out_bytes);
+    const bool deep = gr && K < 4096; // deep residual prefetch for short K
+    cudaError_t e;
     if (narrow)
-        shared_linear_kernel<128><<<grid, NUM_THREADS, Tile<128>::SMEM_BYTES, ctx.stream>>>(ta0, ta1, tw, a);
+        e = deep ? launch_variant<128, 144, true>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
+            : gr ? launch_variant<128, 192, true>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
+                 : launch_variant<128, 192, false>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a);
     else
-        shared_linear_kernel<256><<<grid, NUM_THREADS, Tile<256>::SMEM_BYTES, ctx.stream>>>(ta0, ta1, tw, a);
+        e = deep ? launch_variant<256, 144, true>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
+            : gr ? launch_variant<256, 192, true>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
+                 : launch_variant<256, 192, false>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a);
+    if (e != cudaSuccess) return S2_ERR_CUDA;
     ctx.launches++;
     return cudaGetLastError() == cudaSuccess ? S2_OK : S2_ERR_CUDA;
 }

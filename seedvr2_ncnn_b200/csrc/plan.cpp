@@ -330,21 +330,29 @@ EncodeTiledFn encode_fn()
 
 // 2-D bf16 tensor [outer][inner] with 128-byte swizzle; box = box_inner x
 // box_outer (box_inner * 2 bytes must be 128); out-of-range elements read 0.
-int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
-                      uint32_t box_inner, uint32_t box_outer)
+int make_tmap_2d(CUtensorMap* map, const void* base, int f32, uint64_t inner, uint64_t outer,
+                 uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer)
 {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return S2_ERR_DEVICE;
-    if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_stride_bytes & 15) || box_inner * 2 != 128)
+    const uint32_t esz = f32 ? 4 : 2;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_stride_bytes & 15) || box_inner * esz != 128)
         return S2_ERR_INVALID;
     const cuuint64_t dims[2] = {inner, outer};
     const cuuint64_t strides[1] = {row_stride_bytes};
     const cuuint32_t box[2] = {box_inner, box_outer};
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                          const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? S2_OK : S2_ERR_INVALID;
+}
+
+int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                      uint32_t box_inner, uint32_t box_outer)
+{
+    return make_tmap_2d(map, base, 0, inner, outer, row_stride_bytes, box_inner, box_outer);
 }
 
 // ---------------------------------------------------------------- buffers

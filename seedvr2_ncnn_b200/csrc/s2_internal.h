@@ -138,6 +138,10 @@ constexpr int kMaxPeers = 8;
 
 int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                       uint32_t box_inner, uint32_t box_outer);
+// bf16 (f32 = 0) or fp32 (f32 = 1) row-major 2D map, 128-byte swizzle, box
+// rows 128 bytes wide
+int make_tmap_2d(CUtensorMap* map, const void* base, int f32, uint64_t inner, uint64_t outer,
+                 uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
 
 // kernels (launchers return S2_* codes)
 int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void* A0, const void* A1, const void* W,

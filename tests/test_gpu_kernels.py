@@ -30,7 +30,7 @@ def _ref_linear(a, w, bias):
 
 
 @pytest.mark.parametrize("M0,M1,N,K", [(300, 0, 512, 256), (1, 0, 256, 64), (257, 58, 520, 136), (129, 3, 8, 72),
-                                       (1000, 0, 2560, 2560)])
+                                       (1000, 0, 2560, 2560), (5000, 333, 2600, 192)])
 @pytest.mark.parametrize("epi", ["store_bf16", "store_f32", "gelu", "gate_residual"])
 def test_shared_linear_vs_torch(gpu_ctx, s2lib, M0, M1, N, K, epi):
     import torch
