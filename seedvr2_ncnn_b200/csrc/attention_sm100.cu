@@ -6,9 +6,12 @@
 // L video rows followed by the sample's T text rows, packed contiguously
 // (window after window) in bf16 [rows][heads*128] by the prepare kernel.
 //
-// One CTA = (window, pair of 128-row query tiles A and B, head).  K/V tiles
-// are loaded once for both query tiles.  Warp roles:
-//   warp 0     TMA: Q_A and Q_B once, then K/V tiles into a 2-stage ring;
+// Work unit = (window, pair of 128-row query tiles A and B, head); a
+// persistent grid of one CTA per SM walks the units.  K/V tiles are loaded
+// once for both query tiles.  Warp roles:
+//   warp 0     TMA: Q_A and Q_B per unit, K tiles into a 3-stage ring and V
+//              tiles into a 2-stage ring (a K stage is released after its
+//              last S MMA, a V stage after its last PV MMA);
 //   warp 1     one thread issues every tcgen05.mma, ping-ponging the tiles:
 //                S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...
 //              so the tensor core works on one tile while the other tile's
@@ -38,9 +41,10 @@ constexpr int CHUNK_BYTES = TILE * 128;      // 128 rows x 64 bf16 (one swizzle 
 constexpr int TILE_BYTES = 2 * CHUNK_BYTES;  // 128 x 128 bf16
 constexpr int NUM_THREADS = 320;             // TMA, MMA, 2 x 4 softmax warps
 constexpr int TMEM_COLS = 512;               // S/P_A [0,128) S/P_B [128,256) O_A [256,384) O_B [384,512)
-constexpr uint32_t IDESC_S = umma_idesc_bf16(128, 128, 0, 0);
 constexpr uint32_t IDESC_O = umma_idesc_bf16(128, 128, 0, 1); // B (= V) MN-major
-constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;       // Q_A, Q_B, K x2, V x2
+constexpr int K_STAGES = 3;
+constexpr int V_STAGES = 2;
+constexpr int SMEM_BYTES = (2 + K_STAGES + V_STAGES) * TILE_BYTES + 1024 + 256; // Q_A, Q_B, K ring, V ring
 constexpr float RESCALE_THRESHOLD = 8.0f;                     // log2 units
 
 struct AttnArgs
@@ -56,6 +60,8 @@ struct AttnArgs
     void* video_out;
     float* text_partial;
     int* status;
+    int heads;
+    int num_work; // items x heads
     // peer output bases (multi-GPU): a video_indices entry with a non-zero
     // peer field is stored into peer_out[peer - 1] over NVLink
     void* peer_out[kMaxPeers];
@@ -105,66 +111,50 @@ __device__ __forceinline__ float fmax3(float a, float b, float c)
     return d;
 }
 
-// 2^x on the FMA and integer pipes, for a share of the softmax exponentials
-// so the MUFU unit (ex2.approx) is not the only source: x = j + f with
-// j = round(x) (the 1.5*2^23 shift trick, f in [-1/2, 1/2]), 2^f from a cubic
-// fitted for this kernel (weighted least squares iterated toward minimum
-// relative error on [-1/2, 1/2]; max relative error 7.5e-5, far below the
-// 2^-9 of the bf16 P it feeds), and 2^j added into the exponent field.
-// x is clamped at -125 (2^-125 is 0 for softmax purposes) so the exponent
-// add stays in the normal range.
-constexpr uint64_t kMagic2 = 0x4B4000004B400000ull;    // 1.5*2^23 (x2)
-constexpr uint64_t kNegMagic2 = 0xCB400000CB400000ull; // -1.5*2^23
-constexpr uint64_t kNegOne2 = 0xBF800000BF800000ull;   // -1
-constexpr uint64_t kC0 = 0x3F7FFB4A3F7FFB4Aull;        // 0.99992812
-constexpr uint64_t kC1 = 0x3F31798D3F31798Dull;        // 0.69326097
-constexpr uint64_t kC2 = 0x3E786EE63E786EE6ull;        // 0.24261054
-constexpr uint64_t kC3 = 0x3D61FB533D61FB53ull;        // 0.05517132
-
-__device__ __forceinline__ void ex2_poly(uint64_t t2, float& p0, float& p1)
+// 2^x of two packed bf16 values in one MUFU operation; the result is P's
+// bf16 pair as the PV MMA consumes it.  ex2(-inf) = +0.
+__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x)
 {
-    float x0, x1;
-    upk2(t2, x0, x1);
-    const uint64_t x2 = pk2(__float_as_uint(fmaxf(x0, -125.f)), __float_as_uint(fmaxf(x1, -125.f)));
-    const uint64_t r2 = fadd2(x2, kMagic2);
-    const uint64_t f2 = ffma2(fadd2(r2, kNegMagic2), kNegOne2, x2);
-    uint64_t q2 = ffma2(f2, kC3, kC2);
-    q2 = ffma2(q2, f2, kC1);
-    q2 = ffma2(q2, f2, kC0);
-    float q0, q1, r0, r1;
-    upk2(q2, q0, q1);
-    upk2(r2, r0, r1);
-    p0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(r0) << 23));
-    p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(r1) << 23));
+    uint32_t y;
+    asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
 }
 
-// Row max of the 128 raw scores of one key tile (FULL: no masked columns).
+// Row max of the 128 raw scores of one key tile (FULL: no masked columns);
+// four independent 3-input max chains keep the dependency depth at 16.
 template <bool FULL>
 __device__ __forceinline__ float row_max(const uint32_t (&v)[128], int valid)
 {
-    float mx = -INFINITY;
+    float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-    for (int i = 0; i < 128; i += 2)
+    for (int i = 0; i < 128; i += 8)
     {
-        float a = __uint_as_float(v[i]), b = __uint_as_float(v[i + 1]);
-        if (!FULL)
+#pragma unroll
+        for (int c = 0; c < 4; c++)
         {
-            a = i < valid ? a : -INFINITY;
-            b = i + 1 < valid ? b : -INFINITY;
+            float a = __uint_as_float(v[i + 2 * c]), b = __uint_as_float(v[i + 2 * c + 1]);
+            if (!FULL)
+            {
+                a = i + 2 * c < valid ? a : -INFINITY;
+                b = i + 2 * c + 1 < valid ? b : -INFINITY;
+            }
+            m[c] = fmax3(m[c], a, b);
         }
-        mx = fmax3(mx, a, b);
     }
-    return mx;
+    return fmax3(m[0], m[1], fmaxf(m[2], m[3]));
 }
 
 // P = exp2(S * c - m) for the row (masked columns -> 0), written over the
-// first 64 TMEM columns of the S tile as packed bf16 pairs; returns the fp32
-// row sum.  In full tiles 3 of every 8 pairs use the polynomial exp2.
+// first 64 TMEM columns of the S tile as packed bf16 pairs.  The exponent
+// t = S * c - m is formed in fp32 (packed pairs), rounded to bf16 and
+// exponentiated two at a time (ex2.approx.ftz.bf16x2), so P leaves the MUFU
+// already in its bf16 MMA format; the row sum adds exactly those bf16
+// values in fp32 (four independent packed partial sums).
 template <bool FULL>
 __device__ __forceinline__ float row_exp(const uint32_t (&v)[128], int valid, uint64_t c2, uint64_t negm2,
                                          uint32_t s_addr)
 {
-    uint64_t sum2 = 0;
+    uint64_t sum2[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int c = 0; c < 4; c++)
     {
@@ -174,28 +164,22 @@ __device__ __forceinline__ float row_exp(const uint32_t (&v)[128], int valid, ui
         {
             const int i = c * 32 + 2 * q;
             const uint64_t t2 = ffma2(pk2(v[i], v[i + 1]), c2, negm2);
-            float p0, p1;
-            if (FULL && (q & 7) < 3)
-                ex2_poly(t2, p0, p1);
-            else
+            float t0, t1;
+            upk2(t2, t0, t1);
+            if (!FULL)
             {
-                float t0, t1;
-                upk2(t2, t0, t1);
-                p0 = ex2(t0);
-                p1 = ex2(t1);
-                if (!FULL)
-                {
-                    p0 = i < valid ? p0 : 0.f;
-                    p1 = i + 1 < valid ? p1 : 0.f;
-                }
+                t0 = i < valid ? t0 : -INFINITY;
+                t1 = i + 1 < valid ? t1 : -INFINITY;
             }
-            sum2 = fadd2(sum2, pk2(__float_as_uint(p0), __float_as_uint(p1)));
-            packed[q] = pack_bf16x2(p0, p1);
+            const uint32_t p = ex2_bf16x2(pack_bf16x2(t0, t1));
+            packed[q] = p;
+            sum2[q & 3] = fadd2(sum2[q & 3], pk2(p << 16, p & 0xFFFF0000u));
         }
         tmem_st16(s_addr + c * 16, packed);
     }
+    const uint64_t s2 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
     float lo, hi;
-    upk2(sum2, lo, hi);
+    upk2(s2, lo, hi);
     return lo + hi;
 }
 
@@ -280,6 +264,35 @@ __device__ __forceinline__ bool store_row(const AttnArgs& a, int item_window, in
     return remote;
 }
 
+// One unit of work: (item, head); consecutive units share the item.
+struct Work
+{
+    int window, seq_off, L, part_off, S_len, q0, has_b, nkv, head;
+};
+
+__device__ __forceinline__ Work decode_work(const AttnArgs& a, int w)
+{
+    Work r;
+    const int it = w / a.heads;
+    r.head = w - it * a.heads;
+    const int2 item = a.items[it];
+    const int4 wi = a.win_info[item.x];
+    r.window = item.x;
+    r.seq_off = wi.x;
+    r.L = wi.y;
+    r.part_off = wi.w;
+    r.S_len = wi.y + wi.z;
+    r.q0 = item.y;
+    r.has_b = r.q0 + TILE < r.S_len;
+    r.nkv = (r.S_len + TILE - 1) / TILE;
+    return r;
+}
+
+// Persistent: CTA b processes units b, b + gridDim.x, ...  The K/V ring and
+// every barrier phase run on across units, so the next unit's K/V loads,
+// its first S MMA and the L2 prefetch of its Q overlap the current unit's
+// last tiles and epilogue.  Q is reloaded once the unit's last S MMA has
+// read it (q_empty).
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     window_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                             const __grid_constant__ CUtensorMap tv, const AttnArgs args)
@@ -287,41 +300,43 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;                // Q_A, Q_B
-    uint8_t* sK = sQ + 2 * TILE_BYTES; // 2 stages
-    uint8_t* sV = sK + 2 * TILE_BYTES; // 2 stages
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * TILE_BYTES);
+    uint8_t* sK = sQ + 2 * TILE_BYTES;        // K ring
+    uint8_t* sV = sK + K_STAGES * TILE_BYTES; // V ring
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + V_STAGES * TILE_BYTES);
     uint64_t* q_full = bars + 0;
-    uint64_t* k_full = bars + 1;   // [2]
-    uint64_t* v_full = bars + 3;   // [2]
-    uint64_t* kv_empty = bars + 5; // [2]
-    uint64_t* s_full = bars + 7;   // [2] per query tile
-    uint64_t* p_full = bars + 9;   // [2] per query tile
-    uint64_t* o_done = bars + 11;  // [2] per query tile
-    uint64_t* drain = bars + 13;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+    uint64_t* q_empty = bars + 1;
+    uint64_t* k_full = bars + 2;   // [K_STAGES]
+    uint64_t* k_empty = bars + 5;  // [K_STAGES]
+    uint64_t* v_full = bars + 8;   // [V_STAGES]
+    uint64_t* v_empty = bars + 10; // [V_STAGES]
+    uint64_t* s_full = bars + 12;  // [2] per query tile
+    uint64_t* p_full = bars + 14;  // [2] per query tile
+    uint64_t* o_done = bars + 16;  // [2] per query tile
+    uint64_t* drain = bars + 18;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int head = blockIdx.y;
-    const int2 item = args.items[blockIdx.x];
-    const int4 wi = args.win_info[item.x];
-    const int seq_off = wi.x, L = wi.y, T = wi.z, part_off = wi.w;
-    const int S_len = L + T;
-    const int q0 = item.y;
-    const bool has_b = q0 + TILE < S_len;
-    const int nkv = (S_len + TILE - 1) / TILE;
 
     if (threadIdx.x == 0)
     {
         mbar_init(q_full, 1);
-        for (int s = 0; s < 2; s++)
+        mbar_init(q_empty, 1);
+        for (int s = 0; s < K_STAGES; s++)
         {
             mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+        }
+        for (int s = 0; s < V_STAGES; s++)
+        {
             mbar_init(&v_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+            mbar_init(&v_empty[s], 1);
+        }
+        for (int s = 0; s < 2; s++)
+        {
             mbar_init(&s_full[s], 1);
-            mbar_init(&p_full[s], 128);
+            mbar_init(&p_full[s], 4); // one arrival per softmax warp
             mbar_init(&o_done[s], 1);
         }
         mbar_init(drain, 1);
@@ -339,41 +354,79 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0)
         {
             // ---------------- TMA producer
-            const int x0 = head * HD;
-            int issued_stage[2] = {0, 0};
-            uint32_t last_parity[2] = {0, 0};
-            mbar_arrive_expect_tx(q_full, has_b ? 2 * TILE_BYTES : TILE_BYTES);
-            tma_load_2d(sQ, &tq, q_full, x0, seq_off + q0);
-            tma_load_2d(sQ + CHUNK_BYTES, &tq, q_full, x0 + 64, seq_off + q0);
-            if (has_b)
+            int g = 0; // K/V tiles issued so far (ring position)
+            int it = 0;
+            bool q_out = false;
+            uint32_t q_par = 0;
+            int k_issued[K_STAGES] = {0, 0, 0}, v_issued[V_STAGES] = {0, 0};
+            uint32_t k_par[K_STAGES] = {0, 0, 0}, v_par[V_STAGES] = {0, 0};
+            for (int w = blockIdx.x; w < args.num_work && !*abort_flag; w += gridDim.x, it++)
             {
-                tma_load_2d(sQ + TILE_BYTES, &tq, q_full, x0, seq_off + q0 + TILE);
-                tma_load_2d(sQ + TILE_BYTES + CHUNK_BYTES, &tq, q_full, x0 + 64, seq_off + q0 + TILE);
-            }
-            for (int j = 0; j < nkv; j++)
-            {
-                const int st = j & 1;
-                const uint32_t par = (j >> 1) & 1;
-                if (!mbar_wait(&kv_empty[st], par ^ 1, abort_flag, args.status)) break;
-                const int y = seq_off + j * TILE;
-                mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
-                tma_load_2d(sK + st * TILE_BYTES, &tk, &k_full[st], x0, y);
-                tma_load_2d(sK + st * TILE_BYTES + CHUNK_BYTES, &tk, &k_full[st], x0 + 64, y);
-                mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
-                tma_load_2d(sV + st * TILE_BYTES, &tv, &v_full[st], x0, y);
-                tma_load_2d(sV + st * TILE_BYTES + CHUNK_BYTES, &tv, &v_full[st], x0 + 64, y);
-                issued_stage[st] = 1;
-                last_parity[st] = par;
+                const Work wk = decode_work(args, w);
+                const int x0 = wk.head * HD;
+                if (it > 0 && !mbar_wait(q_empty, (it - 1) & 1, abort_flag, args.status)) break;
+                mbar_arrive_expect_tx(q_full, wk.has_b ? 2 * TILE_BYTES : TILE_BYTES);
+                tma_load_2d(sQ, &tq, q_full, x0, wk.seq_off + wk.q0);
+                tma_load_2d(sQ + CHUNK_BYTES, &tq, q_full, x0 + 64, wk.seq_off + wk.q0);
+                if (wk.has_b)
+                {
+                    tma_load_2d(sQ + TILE_BYTES, &tq, q_full, x0, wk.seq_off + wk.q0 + TILE);
+                    tma_load_2d(sQ + TILE_BYTES + CHUNK_BYTES, &tq, q_full, x0 + 64, wk.seq_off + wk.q0 + TILE);
+                }
+                q_out = true;
+                q_par = it & 1;
+                if (w + (int)gridDim.x < args.num_work)
+                {
+                    const Work nx = decode_work(args, w + gridDim.x);
+                    const int ny = nx.seq_off + nx.q0;
+                    tma_prefetch_l2_2d(&tq, nx.head * HD, ny);
+                    tma_prefetch_l2_2d(&tq, nx.head * HD + 64, ny);
+                    if (nx.has_b)
+                    {
+                        tma_prefetch_l2_2d(&tq, nx.head * HD, ny + TILE);
+                        tma_prefetch_l2_2d(&tq, nx.head * HD + 64, ny + TILE);
+                    }
+                }
+                bool ok = true;
+                // K(j) then V(j): the order the MMA issuer consumes them
+                for (int j = 0; j < wk.nkv; j++, g++)
+                {
+                    const int y = wk.seq_off + j * TILE;
+                    const int ks = g % K_STAGES;
+                    const uint32_t kp = (uint32_t)(g / K_STAGES) & 1u;
+                    if (!mbar_wait(&k_empty[ks], kp ^ 1, abort_flag, args.status))
+                    {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&k_full[ks], TILE_BYTES);
+                    tma_load_2d(sK + ks * TILE_BYTES, &tk, &k_full[ks], x0, y);
+                    tma_load_2d(sK + ks * TILE_BYTES + CHUNK_BYTES, &tk, &k_full[ks], x0 + 64, y);
+                    k_issued[ks] = 1;
+                    k_par[ks] = kp;
+                    const int vs = g % V_STAGES;
+                    const uint32_t vp = (uint32_t)(g / V_STAGES) & 1u;
+                    if (!mbar_wait(&v_empty[vs], vp ^ 1, abort_flag, args.status))
+                    {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&v_full[vs], TILE_BYTES);
+                    tma_load_2d(sV + vs * TILE_BYTES, &tv, &v_full[vs], x0, y);
+                    tma_load_2d(sV + vs * TILE_BYTES + CHUNK_BYTES, &tv, &v_full[vs], x0 + 64, y);
+                    v_issued[vs] = 1;
+                    v_par[vs] = vp;
+                }
+                if (!ok) break;
             }
             if (*abort_flag)
             {
-                drain_wait(q_full, 0);
-                for (int s = 0; s < 2; s++)
-                    if (issued_stage[s])
-                    {
-                        drain_wait(&k_full[s], last_parity[s]);
-                        drain_wait(&v_full[s], last_parity[s]);
-                    }
+                // no TMA write may land after the CTA exits
+                if (q_out) drain_wait(q_full, q_par);
+                for (int s = 0; s < K_STAGES; s++)
+                    if (k_issued[s]) drain_wait(&k_full[s], k_par[s]);
+                for (int s = 0; s < V_STAGES; s++)
+                    if (v_issued[s]) drain_wait(&v_full[s], v_par[s]);
             }
         }
     }
@@ -383,58 +436,105 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         {
             // ---------------- MMA issuer
             bool any = false;
-            const int ntiles = has_b ? 2 : 1;
-            auto issue_s = [&](int x, int j) {
-                const uint32_t q_addr = smem_u32(sQ + x * TILE_BYTES);
-                const uint32_t k_addr = smem_u32(sK + (j & 1) * TILE_BYTES);
-                const uint32_t d = tmem + x * 128;
-#pragma unroll
-                for (int k = 0; k < HD / 16; k++)
-                {
-                    const uint32_t off = (k >> 2) * CHUNK_BYTES + (k & 3) * 32;
-                    umma_bf16(d, umma_desc_sw128(q_addr + off, 16, 1024), umma_desc_sw128(k_addr + off, 16, 1024),
-                              IDESC_S, k != 0);
-                }
-                umma_commit(&s_full[x]);
-            };
-            auto issue_pv = [&](int x, int j) {
-                const uint32_t v_addr = smem_u32(sV + (j & 1) * TILE_BYTES);
-                const uint32_t p_tmem = tmem + x * 128; // P packed bf16x2 over S columns [0,64)
-                const uint32_t o_tmem = tmem + 256 + x * 128;
-#pragma unroll
-                for (int k = 0; k < TILE / 16; k++)
-                    umma_bf16_tmem_a(o_tmem, p_tmem + k * 8, umma_desc_sw128(v_addr + k * 16 * 128, CHUNK_BYTES, 1024),
-                                     IDESC_O, (j | k) != 0);
-            };
-            do
+            bool ok = true;
+            int g = 0;
+            int it = 0;
+            uint32_t pcnt[2] = {0, 0};
+            // shared-memory matrix descriptors of the Q tiles and K / V stages
+            const uint64_t q_desc0 = umma_desc_sw128(smem_u32(sQ), 16, 1024);
+            const uint64_t k_desc0 = umma_desc_sw128(smem_u32(sK), 16, 1024);
+            const uint64_t v_desc0 = umma_desc_sw128(smem_u32(sV), CHUNK_BYTES, 1024);
+            constexpr uint32_t kTileDesc = TILE_BYTES >> 4; // descriptor step of one tile buffer
+            for (int w = blockIdx.x; w < args.num_work && ok; w += gridDim.x, it++)
             {
-                if (!mbar_wait(q_full, 0, abort_flag, args.status)) break;
-                if (!mbar_wait(&k_full[0], 0, abort_flag, args.status)) break;
-                tc_fence_after();
-                for (int x = 0; x < ntiles; x++) issue_s(x, 0);
-                any = true;
-                bool ok = true;
-                for (int j = 0; j < nkv && ok; j++)
+                const Work wk = decode_work(args, w);
+                const int ntiles = wk.has_b ? 2 : 1;
+                // S_x = Q_x K^T for key tile j (ring slot gj); a ragged last
+                // tile runs with N = its keys rounded up to 16
+                auto issue_s = [&](int x, int gj, int j) {
+                    const int valid = wk.S_len - j * TILE;
+                    const int n = valid >= TILE ? TILE : ((valid + 15) & ~15);
+                    const uint32_t idesc = umma_idesc_bf16(128, n, 0, 0);
+                    const uint64_t qd = q_desc0 + (x ? kTileDesc : 0u);
+                    const uint64_t kd = k_desc0 + (uint32_t)(gj % K_STAGES) * kTileDesc;
+                    const uint32_t d = tmem + x * 128;
+#pragma unroll
+                    for (int k = 0; k < HD / 16; k++)
+                    {
+                        // start address field (bits 0-13, address >> 4) advanced by the K offset
+                        const uint32_t off = ((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4;
+                        umma_bf16(d, qd + off, kd + off, idesc, k != 0);
+                    }
+                    umma_commit(&s_full[x]);
+                };
+                // O_x += P_x V over the tile's keys (16 per MMA; P is zero
+                // past the window's sequence)
+                auto issue_pv = [&](int x, int gj, int j) {
+                    const int valid = wk.S_len - j * TILE;
+                    const int ksteps = valid >= TILE ? TILE / 16 : (valid + 15) / 16;
+                    const uint64_t vd = v_desc0 + (uint32_t)(gj % V_STAGES) * kTileDesc;
+                    const uint32_t p_tmem = tmem + x * 128; // P packed bf16x2 over S columns [0,64)
+                    const uint32_t o_tmem = tmem + 256 + x * 128;
+                    for (int k = 0; k < ksteps; k++)
+                        umma_bf16_tmem_a(o_tmem, p_tmem + k * 8, vd + ((k * 16 * 128) >> 4), IDESC_O, (j | k) != 0);
+                };
+                auto wait_k = [&](int gk) {
+                    return mbar_wait(&k_full[gk % K_STAGES], (uint32_t)(gk / K_STAGES) & 1u, abort_flag, args.status);
+                };
+                if (!mbar_wait(q_full, it & 1, abort_flag, args.status) || !wait_k(g))
                 {
-                    const int st = j & 1;
-                    if (!mbar_wait(&v_full[st], (j >> 1) & 1, abort_flag, args.status)) break;
-                    const bool more = j + 1 < nkv;
-                    if (more && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, args.status)) break;
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int x = 0; x < ntiles; x++) issue_s(x, g, 0);
+                umma_commit(&k_empty[g % K_STAGES]); // K(0) is free once S(., 0) is done
+                any = true;
+                if (wk.nkv == 1) umma_commit(q_empty);
+                // per key tile j: PV_A(j) S_A(j+1) PV_B(j) S_B(j+1); a K stage is
+                // released after its last S, a V stage after its last PV
+                for (int j = 0; j < wk.nkv && ok; j++)
+                {
+                    const int gj = g + j;
+                    const int vs = gj % V_STAGES;
+                    if (!mbar_wait(&v_full[vs], (uint32_t)(gj / V_STAGES) & 1u, abort_flag, args.status))
+                    {
+                        ok = false;
+                        break;
+                    }
+                    const bool more = j + 1 < wk.nkv;
                     for (int x = 0; x < ntiles; x++)
                     {
-                        if (!mbar_wait(&p_full[x], j & 1, abort_flag, args.status))
+                        if (!mbar_wait(&p_full[x], pcnt[x] & 1, abort_flag, args.status))
                         {
                             ok = false;
                             break;
                         }
+                        pcnt[x]++;
                         tc_fence_after();
-                        issue_pv(x, j);
+                        issue_pv(x, gj, j);
                         if (!more) umma_commit(&o_done[x]);
-                        if (x == ntiles - 1) umma_commit(&kv_empty[st]);
-                        if (more) issue_s(x, j + 1);
+                        if (x == ntiles - 1) umma_commit(&v_empty[vs]);
+                        if (more)
+                        {
+                            if (x == 0)
+                            {
+                                if (!wait_k(gj + 1))
+                                {
+                                    ok = false;
+                                    break;
+                                }
+                                tc_fence_after();
+                            }
+                            issue_s(x, gj + 1, j + 1);
+                            if (x == ntiles - 1) umma_commit(&k_empty[(gj + 1) % K_STAGES]);
+                        }
                     }
+                    // the unit's last S MMA has been issued: Q may be replaced
+                    if (ok && j + 2 == wk.nkv) umma_commit(q_empty);
                 }
-            } while (0);
+                g += wk.nkv;
+            }
             if (any)
             {
                 umma_commit(drain);
@@ -451,33 +551,48 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         const uint32_t s_addr = tmem + lane_base + x * 128;
         const uint32_t o_addr = tmem + lane_base + 256 + x * 128;
-        const int qbase = q0 + x * TILE;
-        if (x == 0 || has_b)
+        const uint64_t c2 = pk2(__float_as_uint(args.scale_log2), __float_as_uint(args.scale_log2));
+        uint32_t scnt = 0, ocnt = 0;
+        bool ok = true;
+        for (int w = blockIdx.x; w < args.num_work && ok; w += gridDim.x)
         {
+            const Work wk = decode_work(args, w);
+            if (x == 1 && !wk.has_b) continue;
+            const int qbase = wk.q0 + x * TILE;
             float m_used = -INFINITY;
             float l_run = 0.f;
-            bool ok = true;
-            for (int j = 0; j < nkv; j++)
+            for (int j = 0; j < wk.nkv; j++)
             {
-                if (!warp_wait(&s_full[x], j & 1, abort_flag, args.status))
+                if (!warp_wait(&s_full[x], scnt & 1, abort_flag, args.status))
                 {
                     ok = false;
                     break;
                 }
+                scnt++;
                 tc_fence_after();
-                const int valid = S_len - j * TILE; // >= 1
+                const int valid = wk.S_len - j * TILE; // >= 1
                 const bool full = valid >= TILE;
                 uint32_t v[128];
                 tmem_ld128(s_addr, v);
                 tmem_ld_wait();
                 const float mx = full ? row_max<true>(v, valid) : row_max<false>(v, valid);
                 const float mt = mx * args.scale_log2;
+                float alpha = 1.f;
+                const bool rescale = j > 0 && mt > m_used + RESCALE_THRESHOLD;
                 if (j == 0)
                     m_used = mt;
-                else if (mt > m_used + RESCALE_THRESHOLD)
+                else if (rescale)
                 {
-                    // O is stable here: S_X(j) was committed after PV_X(j-1).
-                    const float alpha = ex2(m_used - mt);
+                    alpha = ex2(m_used - mt);
+                    m_used = mt;
+                }
+                const uint64_t negm2 = pk2(__float_as_uint(-m_used), __float_as_uint(-m_used));
+                const float rowsum = full ? row_exp<true>(v, valid, c2, negm2, s_addr)
+                                          : row_exp<false>(v, valid, c2, negm2, s_addr);
+                if (rescale)
+                {
+                    // O is stable here: S_X(j) was committed after PV_X(j-1),
+                    // and PV_X(j) waits for this thread's p_full arrival.
 #pragma unroll
                     for (int c = 0; c < 4; c++)
                     {
@@ -489,41 +604,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         tmem_st32(o_addr + c * 32, o);
                     }
                     l_run *= alpha;
-                    m_used = mt;
                 }
-                const uint64_t c2 = pk2(__float_as_uint(args.scale_log2), __float_as_uint(args.scale_log2));
-                const uint64_t negm2 = pk2(__float_as_uint(-m_used), __float_as_uint(-m_used));
-                const float rowsum = full ? row_exp<true>(v, valid, c2, negm2, s_addr)
-                                          : row_exp<false>(v, valid, c2, negm2, s_addr);
                 l_run += rowsum;
                 tmem_st_wait();
                 tc_fence_before();
-                mbar_arrive(&p_full[x]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[x]);
             }
-            if (ok && warp_wait(&o_done[x], 0, abort_flag, args.status))
+            if (!ok) break;
+            if (!warp_wait(&o_done[x], ocnt & 1, abort_flag, args.status))
             {
-                tc_fence_after();
-                const int qi = qbase + row;
-                const float inv = 1.f / l_run;
-                bool remote = false;
-#pragma unroll 1
-                for (int c = 0; c < 4; c++)
-                {
-                    uint32_t v[32];
-                    tmem_ld32(o_addr + c * 32, v);
-                    tmem_ld_wait();
-                    if (qi < S_len)
-                    {
-                        float o[32];
-#pragma unroll
-                        for (int i = 0; i < 32; i++) o[i] = __uint_as_float(v[i]);
-                        remote |= store_row(args, item.x, part_off, L, qi, head * HD + c * 32, o, inv);
-                    }
-                }
-                // a row stored into a peer GPU must be visible there once this
-                // rank passes its next cross-GPU barrier
-                if (remote) __threadfence_system();
+                ok = false;
+                break;
             }
+            ocnt++;
+            tc_fence_after();
+            const int qi = qbase + row;
+            const float inv = 1.f / l_run;
+            bool remote = false;
+#pragma unroll 1
+            for (int c = 0; c < 4; c++)
+            {
+                uint32_t v[32];
+                tmem_ld32(o_addr + c * 32, v);
+                tmem_ld_wait();
+                if (qi < wk.S_len)
+                {
+                    float o[32];
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[i] = __uint_as_float(v[i]);
+                    remote |= store_row(args, wk.window, wk.part_off, wk.L, qi, wk.head * HD + c * 32, o, inv);
+                }
+            }
+            // a row stored into a peer GPU must be visible there once this
+            // rank passes its next cross-GPU barrier
+            if (remote) __threadfence_system();
+            // O has been read: the next unit's first PV may overwrite it
+            // (ordered by this warp's next p_full arrival)
+            tc_fence_before();
         }
     }
 
@@ -573,7 +691,9 @@ int launch_window_attention(Context& ctx, const AttnSchedule& s, int heads, cons
             return S2_ERR_CUDA;
         configured = true;
     }
-    dim3 grid(s.num_items, heads);
+    a.heads = heads;
+    a.num_work = s.num_items * heads;
+    const int grid = a.num_work < ctx.num_sms ? a.num_work : ctx.num_sms;
     const double video_rows = (double)s.packed_rows - s.partial_rows;
     ProfileScope prof(ctx, K_ATTN, s.attn_flops_per_head * heads,
                       (double)s.packed_rows * inner * 2.0 * 3.0 + video_rows * inner * (out_f32 ? 4.0 : 2.0) +

@@ -109,6 +109,13 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* desc, ui
         : "memory");
 }
 
+// Tiled 2D prefetch of one box into L2 (no shared-memory destination).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* desc, int x, int y)
+{
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(desc), "r"(x), "r"(y)
+                 : "memory");
+}
+
 // Tiled 2D store shared -> global (bulk async-group completion).  Rows and
 // columns beyond the tensor map's extents are not written.
 __device__ __forceinline__ void tma_store_2d(const void* desc, const void* smem_src, int x, int y)
