@@ -378,20 +378,23 @@ def main():
         "config": {"workload": desc, "config": args.config, "video_tokens": nv, "text_tokens": TEXT,
                    "blocks": args.blocks, "hidden": D, "heads": HEADS, "mlp": F, "window": window,
                    "window_mode": "target-count" if mode == 0 else "extent", "global_batch": 1,
-                   "parallelism": (f"window sharding x{world} (rank 0 owns {n_local} video tokens; NCCL "
-                                   "send/recv of shifted-window qkv/context rows + text all-reduce)")
+                   "parallelism": (f"window sharding x{world} (rank 0 owns {n_local} video tokens; qkv rows "
+                                   "pushed to window owners and context rows stored back over NVLink peer memory, "
+                                   "text partials summed over peers; no NCCL in the block loop)")
                    if sharded else "single GPU",
                    "l2": "inputs larger than L2 (5 GB of weights + 222 MB residual per step)"},
         "roofline": roof(dominant, kinds[dominant]),
         "window_attention": roof("window_attention", "tensor"),
-        "hbm_passes": {k: roof(k, "hbm") for k in ("prepare_qkv", "ada_rmsnorm", "text_pool")},
+        # prepare_qkv runs only when the QKV projection cannot pack whole heads per tile
+        "hbm_passes": {k: roof(k, "hbm") for k in ("prepare_qkv", "ada_rmsnorm", "text_pool")
+                       if counters[k]["launches"]},
         "comm": {"nccl_ms_per_step": counters["comm"]["ms"] / args.steps,
                  "nccl_bytes_per_step": counters["comm"]["bytes"] / args.steps,
                  "host_wait_ms_per_step": counters["host_wait"]["ms"] / args.steps,
                  "other_kernels_ms_per_step": counters["other"]["ms"] / args.steps},
-        "e2e": {"value": M / (e2e_ms / 1000.0), "unit": "tokens/s",
+        "e2e": {"value": None if args.no_e2e else M / (e2e_ms / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": int((n_local + TEXT) * D * 4 + 6 * D * 4),
-                "d2h_bytes_per_step": int((n_local + TEXT) * D * 4), "ms_per_step": e2e_ms,
+                "d2h_bytes_per_step": int((n_local + TEXT) * D * 4), "ms_per_step": None if args.no_e2e else e2e_ms,
                 "entry_point": "s2_dit_forward_sharded + pinned H2D/D2H" if sharded else "s2_dit_forward_host"},
         "gpu_launches": launches,
         "clocks": clk,

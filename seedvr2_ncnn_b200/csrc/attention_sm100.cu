@@ -183,13 +183,6 @@ __device__ __forceinline__ float row_exp(const uint32_t (&v)[128], int valid, ui
     return lo + hi;
 }
 
-__device__ __forceinline__ void st_v8(void* p, const uint32_t (&r)[8])
-{
-    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(r[0]), "r"(r[1]), "r"(r[2]),
-                 "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-                 : "memory");
-}
-
 __device__ __forceinline__ float bf16_round_f32(float x)
 {
     return __bfloat162float(__float2bfloat16_rn(x));

@@ -45,6 +45,11 @@ struct s2_dit
     s2::DeviceBuffer act; // activations of one forward
     s2::DeviceBuffer mods; // [blocks][6][D]
     s2::DeviceBuffer host_x; // staging for s2_dit_forward_host
+    // RoPE rotation tables [blocks][rope_pos][pairs] (cos, sin), rebuilt when
+    // the weights change or a shape needs more positions
+    s2::DeviceBuffer rope;
+    int rope_pos = 0;
+    bool rope_stale = true;
     // multi-GPU: ownership plan and schedules per (shape, text, rank, world)
     struct Shard
     {
@@ -159,6 +164,7 @@ void s2_dit_free(s2_dit* d)
 
 int s2_dit_set_block_weights(s2_dit* d, int block, const s2_block_host_weights* w)
 {
+    if (d) d->rope_stale = true;
     if (!d || !w || block < 0 || block >= d->cfg.num_blocks || !w->ada || !w->w_qkv || !w->w_out || !w->w_up ||
         !w->w_down || !w->qk_norm || !w->rope_freqs)
         return S2_ERR_INVALID;
@@ -197,6 +203,7 @@ int s2_dit_set_block_weights(s2_dit* d, int block, const s2_block_host_weights* 
 
 int s2_dit_init_random(s2_dit* d, uint64_t seed)
 {
+    if (d) d->rope_stale = true;
     if (!d) return S2_ERR_INVALID;
     s2::Context& c = d->ctx->c;
     if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
@@ -227,6 +234,27 @@ int s2_dit_init_random(s2_dit* d, uint64_t seed)
     return r;
 }
 
+namespace {
+
+// RoPE rotation tables of every block for positions [0, max_pos).
+int ensure_rope_tables(s2_dit* d, int max_pos)
+{
+    if (!d->rope_stale && max_pos <= d->rope_pos) return S2_OK;
+    const int np = d->cfg.rope_pairs;
+    const int pos = std::max(max_pos, d->rope_pos);
+    const size_t per_block = (size_t)pos * np * 8;
+    int r = d->rope.ensure(per_block * d->cfg.num_blocks);
+    for (int b = 0; b < d->cfg.num_blocks && r == S2_OK; b++)
+        r = s2::launch_rope_table(d->ctx->c, d->blocks[b].freqs, np, pos,
+                                  static_cast<uint8_t*>(d->rope.ptr) + per_block * b);
+    if (r != S2_OK) return r;
+    d->rope_pos = pos;
+    d->rope_stale = false;
+    return S2_OK;
+}
+
+} // namespace
+
 int s2_dit_forward(s2_dit* d, const int* video_shape, int text_length, float* x, const float* modulation)
 {
     if (!d || !video_shape || text_length <= 0 || !x || !modulation) return S2_ERR_INVALID;
@@ -251,9 +279,15 @@ int s2_dit_forward(s2_dit* d, const int* video_shape, int text_length, float* x,
         max_packed = std::max(max_packed, sched[s]->packed_rows);
         max_partial = std::max(max_partial, sched[s]->partial_rows);
     }
-    // activations: h [M][D] bf16 | qkv [M][3D] bf16 | Q,K,V [R][D] bf16 | ctx [M][D] bf16 |
+    // The QKV projection's epilogue writes the packed windows directly when a
+    // 256-column tile holds whole heads (D % 256 == 0); otherwise qkv rows go
+    // through a buffer and the prepare kernel.
+    const bool fused_qkv = D % 256 == 0;
+    if (fused_qkv && (r = ensure_rope_tables(d, std::max(sched[0]->max_pos, sched[1]->max_pos))) != S2_OK) return r;
+    const size_t rope_block = (size_t)d->rope_pos * cfg.rope_pairs * 8;
+    // activations: h [M][D] bf16 | (qkv [M][3D] bf16) | Q,K,V [R][D] bf16 | ctx [M][D] bf16 |
     //              partial [P][D] f32 | u [M][F] bf16
-    const size_t sz_h = align256((size_t)M * D * 2), sz_qkv = align256((size_t)M * 3 * D * 2),
+    const size_t sz_h = align256((size_t)M * D * 2), sz_qkv = fused_qkv ? 0 : align256((size_t)M * 3 * D * 2),
                  sz_pk = align256((size_t)max_packed * D * 2), sz_ctx = sz_h,
                  sz_part = align256((size_t)max_partial * D * 4), sz_u = align256((size_t)M * F * 2);
     if ((r = d->act.ensure(sz_h + sz_qkv + 3 * sz_pk + sz_ctx + sz_part + sz_u)) != S2_OK) return r;
@@ -278,19 +312,30 @@ int s2_dit_forward(s2_dit* d, const int* video_shape, int text_length, float* x,
         const int sh = b & 1; // odd blocks use the half-shifted windows
         const s2::AttnSchedule& S = *sched[sh];
         if ((r = s2::launch_ada_rmsnorm(c, M, D, x, cfg.norm_eps, mb, mb + D, h)) != S2_OK) return r;
-        if ((r = s2::launch_shared_linear(c, M, 0, 3 * D, D, h, nullptr, bl.w_qkv, cfg.qkv_bias ? bl.b_qkv : nullptr,
-                                          s2::EPI_STORE, nullptr, 0, qkv, nullptr)) != S2_OK)
-            return r;
-        const size_t pk_elems = (size_t)S.packed_rows * D;
         __nv_bfloat16* Qp = reinterpret_cast<__nv_bfloat16*>(pk);
         __nv_bfloat16* Kp = reinterpret_cast<__nv_bfloat16*>(pk + sz_pk);
         __nv_bfloat16* Vp = reinterpret_cast<__nv_bfloat16*>(pk + 2 * sz_pk);
-        (void)pk_elems;
-        const __nv_bfloat16* tq = qkv + (size_t)Nv * 3 * D;
-        if ((r = s2::launch_prepare_qkv(c, S, H, cfg.head_dim, cfg.rope_pairs, cfg.qk_eps, bl.qk_norm, bl.freqs, 1, qkv,
-                                        qkv + D, qkv + 2 * D, 3 * D, tq, tq + D, tq + 2 * D, 3 * D, Qp, Kp, Vp)) !=
-            S2_OK)
-            return r;
+        if (fused_qkv)
+        {
+            // QKV projection + qk norm + RoPE + window packing in one kernel
+            if ((r = s2::launch_qkv_packed(c, S, Nv, Nt, D, h, h + (size_t)Nv * D, bl.w_qkv,
+                                           cfg.qkv_bias ? bl.b_qkv : nullptr, H, cfg.rope_pairs, cfg.qk_eps,
+                                           bl.qk_norm, static_cast<uint8_t*>(d->rope.ptr) + rope_block * b,
+                                           d->rope_pos, Qp, Kp, Vp)) != S2_OK)
+                return r;
+        }
+        else
+        {
+            if ((r = s2::launch_shared_linear(c, M, 0, 3 * D, D, h, nullptr, bl.w_qkv,
+                                              cfg.qkv_bias ? bl.b_qkv : nullptr, s2::EPI_STORE, nullptr, 0, qkv,
+                                              nullptr)) != S2_OK)
+                return r;
+            const __nv_bfloat16* tq = qkv + (size_t)Nv * 3 * D;
+            if ((r = s2::launch_prepare_qkv(c, S, H, cfg.head_dim, cfg.rope_pairs, cfg.qk_eps, bl.qk_norm, bl.freqs,
+                                            1, qkv, qkv + D, qkv + 2 * D, 3 * D, tq, tq + D, tq + 2 * D, 3 * D, Qp,
+                                            Kp, Vp)) != S2_OK)
+                return r;
+        }
         if ((r = s2::launch_window_attention(c, S, H, Qp, Kp, Vp, 0, 0, ctxb, partial)) != S2_OK) return r;
         if ((r = s2::launch_text_pool(c, S, D, partial, 0, 0, ctxb + (size_t)Nv * D)) != S2_OK) return r;
         if ((r = s2::launch_shared_linear(c, M, 0, D, D, ctxb, nullptr, bl.w_out, cfg.out_bias ? bl.b_out : nullptr,

@@ -403,6 +403,30 @@ int launch_convert_f32_bf16(Context& ctx, const float* in, void* out, int64_t co
     return finish(ctx);
 }
 
+namespace {
+// table[pos][pair] = (cos, sin)(pos * freqs[pair]), the RoPE rotation of the
+// prepare kernel (same expression, so the same values).
+__global__ void rope_table_kernel(const float* __restrict__ freqs, int pairs, int max_pos, float2* __restrict__ table)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= max_pos * pairs) return;
+    const int pos = i / pairs, pair = i - pos * pairs;
+    float s, c;
+    sincosf((float)pos * __ldg(freqs + pair), &s, &c);
+    table[i] = make_float2(c, s);
+}
+} // namespace
+
+int launch_rope_table(Context& ctx, const float* freqs, int pairs, int max_pos, void* table)
+{
+    if (pairs < 0 || max_pos < 0 || (pairs > 0 && (!freqs || !table))) return S2_ERR_INVALID;
+    const int n = pairs * max_pos;
+    if (n == 0) return S2_OK;
+    ProfileScope prof(ctx, K_OTHER, 0.0, (double)n * 8.0);
+    rope_table_kernel<<<(n + 255) / 256, 256, 0, ctx.stream>>>(freqs, pairs, max_pos, static_cast<float2*>(table));
+    return finish(ctx);
+}
+
 int launch_add_vectors(Context& ctx, const float* a, const float* b, float* out, int count, int period)
 {
     if (count <= 0) return S2_OK;

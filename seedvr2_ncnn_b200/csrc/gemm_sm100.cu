@@ -25,17 +25,29 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int GROUP_M = 16;
-constexpr int NUM_THREADS = 192; // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+// warp 0 TMA, warp 1 MMA, then the epilogue warps: 4 (one per TMEM lane
+// quarter), or 8 for the QKV packing epilogue (two per quarter, one head of
+// the tile each), whose per-row work needs two warps per SMSP to hide latency
+__host__ __device__ constexpr int epilogue_warps(int EK)
+{
+    return EK == 2 ? 8 : 4;
+}
+__host__ __device__ constexpr int num_threads(int EK)
+{
+    return 64 + 32 * epilogue_warps(EK);
+}
 
 // Tile width BN (256, or 128 when a problem has too few 256-wide tiles to
 // fill the SMs evenly).  224 KB of shared memory is split between SKB KB of
 // operand stages and the epilogue's 4 KB boxes (R per epilogue warp):
 //   * SKB = 192: R = 2 (store double buffering; a gate-residual epilogue
-//     (GR) loads its residual box one box ahead);
-//   * SKB = 144, GR only: R = 5 or 6, so each warp keeps R-1 residual boxes
-//     in flight from HBM -- for short K, where the epilogue of a tile has
-//     little mainloop time to hide behind.
-template <int BN, int SKB, bool GR>
+//     loads its residual box one box ahead);
+//   * SKB = 144, gate-residual only: R = 5 or 6, so each warp keeps R-1
+//     residual boxes in flight from HBM -- for short K, where the epilogue
+//     of a tile has little mainloop time to hide behind.
+// Epilogue kinds EK: 0 store / GELU (runtime), 1 gate-residual (fp32 in
+// place, TMA), 2 QKV packing (norm + RoPE, rows scattered to packed windows).
+template <int BN, int SKB, int EK>
 struct Tile
 {
     static constexpr int B_BYTES = BN * BK * 2;
@@ -47,6 +59,23 @@ struct Tile
     static constexpr int EPI_BYTES = 4 * R * 4096; // 4 warps x R boxes of 32 rows x 128 bytes
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 512;
     static_assert(SMEM_BYTES <= 232448, "shared memory");
+};
+
+// QKV packing epilogue (EK 2): see launch_qkv_packed.
+struct PackArgs
+{
+    int D;      // heads * 128 (columns of each of q, k, v)
+    int pairs;  // RoPE pairs per axis
+    float eps;
+    const int* dst0; // [dst0_rows] packed row of each stream-0 (video) row, -1: none
+    int dst0_rows;
+    const int* tdst_off; // [M1 + 1] CSR offsets of each stream-1 (text) row's packed rows
+    const int* tdst;
+    const int* row_pos;  // [packed rows][3] RoPE positions
+    const float* norms;  // [4][128]: q video, k video, q text, k text
+    const float2* rope;  // [positions][pairs] (cos, sin)
+    int rope_entries;    // positions * pairs; staged in shared memory when it fits
+    __nv_bfloat16* out[3]; // packed q, k, v [packed rows][D]
 };
 
 struct GemmArgs
@@ -61,6 +90,7 @@ struct GemmArgs
     void* out0;
     void* out1;
     int* status;
+    PackArgs pack;
 };
 
 template <int BN>
@@ -321,6 +351,170 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const CUten
     }
 }
 
+__device__ __forceinline__ float bf16_round(float x)
+{
+    return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// QKV packing epilogue of one tile for one warp (one accumulator row per
+// thread).  The tile's 128-column heads lie in one of q, k, v (D is a
+// multiple of BN).  Per head: x = bf16(acc + bias); for q and k,
+// x * rsqrt(mean(x^2) + eps) * w then 3D RoPE on adjacent pairs (axis a
+// covers head dims [2*pairs*a, 2*pairs*(a+1)), rotation (cos, sin) of
+// pos[a] * freqs[pair] from the precomputed table);
+// the bf16 row segment is stored to every packed row of the token (one for
+// a video row, one per window of the sample for a text row).  The same
+// arithmetic as prepare_qkv_kernel, which reads the rounded qkv rows back.
+template <int BN>
+__device__ __forceinline__ void epilogue_tile_pack(const GemmArgs& a, const float2* rope, uint32_t t_row, int stream,
+                                                   int m0, int n0, int quarter, int lane, int half)
+{
+    const PackArgs& p = a.pack;
+    const int M = stream ? a.M1 : a.M0;
+    const int row = m0 + quarter * 32 + lane;
+    const int part = n0 / p.D;
+    const int col0 = n0 - part * p.D;
+    __nv_bfloat16* const base = p.out[part];
+    int first = -1, cnt = 0;
+    const int* list = nullptr;
+    if (row < M)
+    {
+        if (stream == 0)
+        {
+            first = row < p.dst0_rows ? __ldg(p.dst0 + row) : -1;
+            cnt = first >= 0 ? 1 : 0;
+        }
+        else
+        {
+            const int o = __ldg(p.tdst_off + row);
+            cnt = __ldg(p.tdst_off + row + 1) - o;
+            list = p.tdst + o;
+            first = cnt > 0 ? __ldg(list) : -1;
+        }
+    }
+    const bool qk = part < 2;
+    const float* w = p.norms + (stream ? 256 : 0) + part * 128;
+    // rows of the rotation table for the three axes (text rows share their
+    // positions (i, i, i) across windows)
+    const float2* rp0 = rope;
+    const float2* rp1 = rope;
+    const float2* rp2 = rope;
+    if (qk && first >= 0)
+    {
+        rp0 = rope + __ldg(p.row_pos + 3 * first) * p.pairs;
+        rp1 = rope + __ldg(p.row_pos + 3 * first + 1) * p.pairs;
+        rp2 = rope + __ldg(p.row_pos + 3 * first + 2) * p.pairs;
+    }
+    const int aw = 2 * p.pairs;
+    const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    // head hh of the tile: the two warps of a lane quarter take one head each
+#pragma unroll 1
+    for (int hh = half; hh < BN / 128; hh += 2)
+    {
+        const uint32_t th = t_row + hh * 128;
+        const int nb = n0 + hh * 128; // GEMM column of the head's first element
+        float inv = 1.f;
+        if (qk)
+        {
+            float ss[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+            for (int c = 0; c < 4; c++)
+            {
+                // operands first: the TMEM load below orders all memory accesses
+                float4 b4[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    b4[j] = a.bias ? __ldg(reinterpret_cast<const float4*>(a.bias + nb + c * 32) + j) : zero4;
+                uint32_t v[32];
+                tmem_ld32(th + c * 32, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                {
+                    const float x0 = bf16_round(__uint_as_float(v[4 * j]) + b4[j].x);
+                    const float x1 = bf16_round(__uint_as_float(v[4 * j + 1]) + b4[j].y);
+                    const float x2 = bf16_round(__uint_as_float(v[4 * j + 2]) + b4[j].z);
+                    const float x3 = bf16_round(__uint_as_float(v[4 * j + 3]) + b4[j].w);
+                    ss[0] += x0 * x0;
+                    ss[1] += x1 * x1;
+                    ss[2] += x2 * x2;
+                    ss[3] += x3 * x3;
+                }
+            }
+            inv = 1.f / sqrtf(((ss[0] + ss[1]) + (ss[2] + ss[3])) / 128.f + p.eps);
+        }
+#pragma unroll 1
+        for (int c = 0; c < 4; c++)
+        {
+            float4 b4[8], w4[8];
+            float2 r2[16];
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+            {
+                b4[j] = a.bias ? __ldg(reinterpret_cast<const float4*>(a.bias + nb + c * 32) + j) : zero4;
+                w4[j] = qk ? __ldg(reinterpret_cast<const float4*>(w + c * 32) + j) : zero4;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+            {
+                const int d = c * 32 + 2 * j;
+                const int axis = d >= 2 * aw ? 2 : (d >= aw ? 1 : 0);
+                const float2* rp = axis == 0 ? rp0 : (axis == 1 ? rp1 : rp2);
+                // generic load: the table is in shared or global memory
+                r2[j] = (qk && d < 3 * aw) ? rp[(d - axis * aw) >> 1] : make_float2(1.f, 0.f);
+            }
+            uint32_t v[32];
+            tmem_ld32(th + c * 32, v);
+            tmem_ld_wait();
+            float x[32];
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+            {
+                x[4 * j] = bf16_round(__uint_as_float(v[4 * j]) + b4[j].x);
+                x[4 * j + 1] = bf16_round(__uint_as_float(v[4 * j + 1]) + b4[j].y);
+                x[4 * j + 2] = bf16_round(__uint_as_float(v[4 * j + 2]) + b4[j].z);
+                x[4 * j + 3] = bf16_round(__uint_as_float(v[4 * j + 3]) + b4[j].w);
+            }
+            if (qk)
+            {
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                {
+                    x[4 * j] = x[4 * j] * inv * w4[j].x;
+                    x[4 * j + 1] = x[4 * j + 1] * inv * w4[j].y;
+                    x[4 * j + 2] = x[4 * j + 2] * inv * w4[j].z;
+                    x[4 * j + 3] = x[4 * j + 3] * inv * w4[j].w;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                {
+                    // (cos, sin) = (1, 0) past the rotated dims
+                    const float cs = r2[j].x, sn = r2[j].y;
+                    const float x0 = x[2 * j], x1 = x[2 * j + 1];
+                    x[2 * j] = x0 * cs - x1 * sn;
+                    x[2 * j + 1] = x0 * sn + x1 * cs;
+                }
+            }
+            uint32_t u0[8], u1[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++)
+            {
+                u0[q] = pack_bf16x2(x[2 * q], x[2 * q + 1]);
+                u1[q] = pack_bf16x2(x[16 + 2 * q], x[16 + 2 * q + 1]);
+            }
+            const size_t coff = (size_t)col0 + hh * 128 + c * 32;
+            for (int i = 0; i < cnt; i++)
+            {
+                // two full 32-byte sectors of the packed row
+                const int r = stream == 0 ? first : __ldg(list + i);
+                __nv_bfloat16* dst = base + (size_t)r * p.D + coff;
+                st_v8(dst, u0);
+                st_v8(dst + 16, u1);
+            }
+        }
+    }
+}
+
 // Gate-residual epilogue of one warp over all of the CTA's tiles, fp32
 // residual in place: out = out + (acc + bias) * gate.  Boxes (32 rows x 32
 // columns) run in a fixed sequence over the CTA's tiles; lane 0 TMA-loads the
@@ -453,13 +647,14 @@ __device__ __forceinline__ bool epilogue_gate_residual(const GemmArgs& a, const 
     return ok;
 }
 
-template <int BN, int SKB, bool GR>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+template <int BN, int SKB, int EK>
+__global__ void __launch_bounds__(num_threads(EK), 1)
     shared_linear_kernel(const __grid_constant__ CUtensorMap tmap_a0, const __grid_constant__ CUtensorMap tmap_a1,
                          const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_o0,
                          const __grid_constant__ CUtensorMap tmap_o1, const GemmArgs args)
 {
-    using TL = Tile<BN, SKB, GR>;
+    using TL = Tile<BN, SKB, EK>;
+    constexpr bool GR = EK == 1;
     constexpr int STAGES = TL::STAGES;
     constexpr int STAGE_BYTES = TL::STAGE_BYTES;
     constexpr int TMEM_COLS = TL::TMEM_COLS;
@@ -489,7 +684,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int b = 0; b < 2; b++)
         {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 4);
+            mbar_init(&tempty[b], epilogue_warps(EK));
         }
         mbar_init(drain, 1);
         if (GR)
@@ -609,6 +804,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     {
         // ---------------- epilogue (warps 2..5)
         const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2; // second warp of the lane quarter (8 epilogue warps)
+        // QKV packing: the RoPE table goes into the (otherwise unused) epilogue
+        // staging memory when it fits
+        const float2* rope = args.pack.rope;
+        if constexpr (EK == 2)
+        {
+            if (args.pack.rope_entries > 0 && args.pack.rope_entries * 8 <= TL::EPI_BYTES)
+            {
+                float2* tab = reinterpret_cast<float2*>(epi_stage);
+                for (int i = threadIdx.x - 64; i < args.pack.rope_entries; i += 32 * epilogue_warps(EK))
+                    tab[i] = __ldg(args.pack.rope + i);
+                named_barrier_sync(1, 32 * epilogue_warps(EK));
+                rope = tab;
+            }
+        }
         const int row_in_tile = quarter * 32 + lane;
         uint8_t* stg = epi_stage + quarter * (TL::R * 4096);
         if constexpr (GR)
@@ -632,7 +842,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 int stream, m0, n0;
                 decode_tile<BN>(args, t, stream, m0, n0);
                 const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-                if (args.tma_out)
+                if constexpr (EK == 2)
+                {
+                    epilogue_tile_pack<BN>(args, rope, t_row, stream, m0, n0, quarter, lane, half);
+                }
+                else if (args.tma_out)
                 {
                     epilogue_tile_tma<BN>(args, stream ? &tmap_o1 : &tmap_o0, stg, slot, t_row, stream, m0, n0,
                                           quarter, lane);
@@ -666,7 +880,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
-template <int BN, int SKB, bool GR>
+template <int BN, int SKB, int EK>
 cudaError_t launch_variant(int grid, cudaStream_t stream, const CUtensorMap& ta0, const CUtensorMap& ta1,
                            const CUtensorMap& tw, const CUtensorMap& to0, const CUtensorMap& to1, const GemmArgs& a)
 {
@@ -674,14 +888,47 @@ cudaError_t launch_variant(int grid, cudaStream_t stream, const CUtensorMap& ta0
     if (!configured)
     {
         const cudaError_t e =
-            cudaFuncSetAttribute(shared_linear_kernel<BN, SKB, GR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 Tile<BN, SKB, GR>::SMEM_BYTES);
+            cudaFuncSetAttribute(shared_linear_kernel<BN, SKB, EK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Tile<BN, SKB, EK>::SMEM_BYTES);
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    shared_linear_kernel<BN, SKB, GR>
-        <<<grid, NUM_THREADS, Tile<BN, SKB, GR>::SMEM_BYTES, stream>>>(ta0, ta1, tw, to0, to1, a);
+    shared_linear_kernel<BN, SKB, EK>
+        <<<grid, num_threads(EK), Tile<BN, SKB, EK>::SMEM_BYTES, stream>>>(ta0, ta1, tw, to0, to1, a);
     return cudaGetLastError();
+}
+
+} // namespace
+
+namespace {
+
+// Operand tensor maps, tile count and tile width shared by the launchers.
+int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const void* A1, const void* W,
+               CUtensorMap& ta0, CUtensorMap& ta1, CUtensorMap& tw, GemmArgs& a, bool& narrow)
+{
+    int r = make_tmap_bf16_2d(&ta0, A0, K, M0 > 0 ? M0 : 1, (uint64_t)K * 2, BK, BM);
+    if (r == 0) r = make_tmap_bf16_2d(&ta1, M1 > 0 ? A1 : A0, K, M1 > 0 ? M1 : (M0 > 0 ? M0 : 1), (uint64_t)K * 2, BK, BM);
+    if (r != 0) return r;
+    a = GemmArgs{};
+    a.M0 = M0;
+    a.M1 = M1;
+    a.N = N;
+    a.K = K;
+    a.mblk0 = (M0 + BM - 1) / BM;
+    a.mblk1 = (M1 + BM - 1) / BM;
+    a.num_kb = (K + BK - 1) / BK;
+    a.status = ctx.status;
+    // Tile width: 128 when it fills the SMs markedly more evenly than 256.
+    auto wave_eff = [&](int bn) {
+        const int tiles = (a.mblk0 + a.mblk1) * ((N + bn - 1) / bn);
+        const int waves = (tiles + ctx.num_sms - 1) / ctx.num_sms;
+        return (double)tiles / ((double)waves * ctx.num_sms);
+    };
+    narrow = wave_eff(128) > 1.15 * wave_eff(256);
+    const int BNsel = narrow ? 128 : 256;
+    a.nblk = (N + BNsel - 1) / BNsel;
+    a.num_tiles = (a.mblk0 + a.mblk1) * a.nblk;
+    return make_tmap_bf16_2d(&tw, W, K, N, (uint64_t)K * 2, BK, BNsel);
 }
 
 } // namespace
@@ -697,9 +944,9 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
     if (epilogue < 0 || epilogue > EPI_GATE_RESIDUAL) return S2_ERR_INVALID;
 
     CUtensorMap ta0, ta1, tw;
-    int r = make_tmap_bf16_2d(&ta0, A0, K, M0 > 0 ? M0 : 1, (uint64_t)K * 2, BK, BM);
-    if (r == 0) r = make_tmap_bf16_2d(&ta1, M1 > 0 ? A1 : A0, K, M1 > 0 ? M1 : (M0 > 0 ? M0 : 1), (uint64_t)K * 2, BK, BM);
-    if (r == 0) r = make_tmap_bf16_2d(&tw, W, K, N, (uint64_t)K * 2, BK, 256);
+    GemmArgs a;
+    bool narrow = false;
+    int r = gemm_setup(ctx, M0, M1, N, K, A0, A1, W, ta0, ta1, tw, a, narrow);
     if (r != 0) return r;
     // TMA-store epilogue when both outputs admit a tensor map (16-byte aligned
     // bases and row strides); the per-thread store path otherwise.
@@ -713,15 +960,6 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
         tma_out = make_tmap_2d(&to1, M1 > 0 ? out1 : out0, out_f32, N, M1 > 0 ? M1 : (M0 > 0 ? M0 : 1),
                                (uint64_t)N * esz, box_cols, 32) == S2_OK;
     if (!tma_out) to1 = to0 = tw;
-
-    GemmArgs a;
-    a.M0 = M0;
-    a.M1 = M1;
-    a.N = N;
-    a.K = K;
-    a.mblk0 = (M0 + BM - 1) / BM;
-    a.mblk1 = (M1 + BM - 1) / BM;
-    a.num_kb = (K + BK - 1) / BK;
     a.epilogue = epilogue;
     a.out_f32 = out_f32;
     a.tma_out = tma_out;
@@ -729,19 +967,7 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
     a.gate = gate;
     a.out0 = out0;
     a.out1 = out1;
-    a.status = ctx.status;
 
-    // Tile width: 128 when it fills the SMs markedly more evenly than 256.
-    auto wave_eff = [&](int bn) {
-        const int tiles = (a.mblk0 + a.mblk1) * ((N + bn - 1) / bn);
-        const int waves = (tiles + ctx.num_sms - 1) / ctx.num_sms;
-        return (double)tiles / ((double)waves * ctx.num_sms);
-    };
-    const bool narrow = wave_eff(128) > 1.15 * wave_eff(256);
-    const int BNsel = narrow ? 128 : 256;
-    a.nblk = (N + BNsel - 1) / BNsel;
-    a.num_tiles = (a.mblk0 + a.mblk1) * a.nblk;
-    if (narrow && (r = make_tmap_bf16_2d(&tw, W, K, N, (uint64_t)K * 2, BK, 128)) != 0) return r;
     const bool gr = tma_out && epilogue == EPI_GATE_RESIDUAL;
     const int grid = a.num_tiles < ctx.num_sms ? a.num_tiles : ctx.num_sms;
     const double M = (double)M0 + M1;
@@ -750,16 +976,62 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
     const bool deep = gr && K < 4096; // deep residual prefetch for short K
     cudaError_t e;
     if (narrow)
-        e = deep ? launch_variant<128, 144, true>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
-            : gr ? launch_variant<128, 192, true>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
-                 : launch_variant<128, 192, false>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a);
+        e = deep ? launch_variant<128, 144, 1>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
+            : gr ? launch_variant<128, 192, 1>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
+                 : launch_variant<128, 192, 0>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a);
     else
-        e = deep ? launch_variant<256, 144, true>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
-            : gr ? launch_variant<256, 192, true>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
-                 : launch_variant<256, 192, false>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a);
+        e = deep ? launch_variant<256, 144, 1>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
+            : gr ? launch_variant<256, 192, 1>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
+                 : launch_variant<256, 192, 0>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a);
     if (e != cudaSuccess) return S2_ERR_CUDA;
     ctx.launches++;
-    return cudaGetLastError() == cudaSuccess ? S2_OK : S2_ERR_CUDA;
+    return S2_OK;
+}
+
+int launch_qkv_packed(Context& ctx, const AttnSchedule& s, int M0, int M1, int K, const void* A0, const void* A1,
+                      const void* W, const float* bias, int heads, int rope_pairs, float eps, const float* norms,
+                      const void* rope_table, int rope_positions, void* q_out, void* k_out, void* v_out)
+{
+    const int D = heads * 128;
+    if (heads <= 0 || D % 256 != 0 || M0 < 0 || M1 < 0 || M0 + M1 <= 0 || K <= 0 || K % 8 || !A0 || !W ||
+        (M1 > 0 && !A1) || M0 > s.pack_dst_rows || M1 > s.total_text || rope_pairs < 0 || 6 * rope_pairs > 128 ||
+        !norms || (rope_pairs > 0 && (!rope_table || rope_positions < s.max_pos)) || !q_out || !k_out || !v_out ||
+        (bias && (reinterpret_cast<uintptr_t>(bias) & 15)) || (reinterpret_cast<uintptr_t>(norms) & 15))
+        return S2_ERR_INVALID;
+    for (const void* o : {q_out, k_out, v_out})
+        if (reinterpret_cast<uintptr_t>(o) & 15) return S2_ERR_INVALID;
+    if (s.packed_rows == 0) return S2_OK;
+    const int N = 3 * D;
+    CUtensorMap ta0, ta1, tw;
+    GemmArgs a;
+    bool narrow = false;
+    int r = gemm_setup(ctx, M0, M1, N, K, A0, A1, W, ta0, ta1, tw, a, narrow);
+    if (r != 0) return r;
+    a.epilogue = EPI_STORE;
+    a.bias = bias;
+    a.pack.D = D;
+    a.pack.pairs = rope_pairs;
+    a.pack.eps = eps;
+    a.pack.dst0 = s.pack_dst;
+    a.pack.dst0_rows = s.pack_dst_rows;
+    a.pack.tdst_off = s.text_dst_off;
+    a.pack.tdst = s.text_dst;
+    a.pack.row_pos = s.row_pos;
+    a.pack.norms = norms;
+    a.pack.rope = static_cast<const float2*>(rope_table);
+    a.pack.rope_entries = s.max_pos * rope_pairs;
+    a.pack.out[0] = static_cast<__nv_bfloat16*>(q_out);
+    a.pack.out[1] = static_cast<__nv_bfloat16*>(k_out);
+    a.pack.out[2] = static_cast<__nv_bfloat16*>(v_out);
+    const int grid = a.num_tiles < ctx.num_sms ? a.num_tiles : ctx.num_sms;
+    const double M = (double)M0 + M1;
+    ProfileScope prof(ctx, K_GEMM, 2.0 * M * N * K,
+                      (M * K + (double)N * K) * 2.0 + (double)s.packed_rows * N * 2.0);
+    const cudaError_t e = narrow ? launch_variant<128, 192, 2>(grid, ctx.stream, ta0, ta1, tw, tw, tw, a)
+                                 : launch_variant<256, 192, 2>(grid, ctx.stream, ta0, ta1, tw, tw, tw, a);
+    if (e != cudaSuccess) return S2_ERR_CUDA;
+    ctx.launches++;
+    return S2_OK;
 }
 
 } // namespace s2

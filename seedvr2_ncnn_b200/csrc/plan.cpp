@@ -257,6 +257,27 @@ int build_schedule_ex(const Plan& plan, const int* text_lengths, const std::vect
         }
     }
 
+    // Inverse of row_src: packed row of each video row, and the packed rows
+    // (one per window) of each text row.
+    int max_row = -1;
+    for (int v : row_src) max_row = std::max(max_row, v);
+    std::vector<int> pack_dst(max_row + 1, -1);
+    std::vector<std::vector<int>> text_rows(total_text);
+    for (size_t r = 0; r < row_src.size(); r++)
+    {
+        if (row_src[r] >= 0)
+            pack_dst[row_src[r]] = static_cast<int>(r);
+        else
+            text_rows[-1 - row_src[r]].push_back(static_cast<int>(r));
+    }
+    std::vector<int> text_dst_off(total_text + 1, 0), text_dst;
+    for (int t = 0; t < total_text; t++)
+    {
+        text_dst_off[t] = static_cast<int>(text_dst.size());
+        text_dst.insert(text_dst.end(), text_rows[t].begin(), text_rows[t].end());
+    }
+    text_dst_off[total_text] = static_cast<int>(text_dst.size());
+
     // One device block for every table.
     const size_t n_tok = vidx.size();
     size_t off = 0;
@@ -267,7 +288,8 @@ int build_schedule_ex(const Plan& plan, const int* text_lengths, const std::vect
     };
     const size_t o_src = take(row_src.size() * 4), o_pos = take(row_pos.size() * 4), o_win = take(nw * 16),
                  o_pool = take(nw * 4), o_items = take(sorted.size() * 8), o_vi = take(n_tok * 4),
-                 o_red = take(total_text * 16), o_scale = take(total_text * 4);
+                 o_red = take(total_text * 16), o_scale = take(total_text * 4), o_pd = take(pack_dst.size() * 4),
+                 o_tdo = take(text_dst_off.size() * 4), o_td = take(text_dst.size() * 4);
     if (s.block)
     {
         cudaFree(s.block);
@@ -286,6 +308,9 @@ int build_schedule_ex(const Plan& plan, const int* text_lengths, const std::vect
     put(o_vi, vidx.data(), n_tok * 4);
     put(o_red, reduce.data(), total_text * 16);
     put(o_scale, scale.data(), total_text * 4);
+    put(o_pd, pack_dst.data(), pack_dst.size() * 4);
+    put(o_tdo, text_dst_off.data(), text_dst_off.size() * 4);
+    put(o_td, text_dst.data(), text_dst.size() * 4);
     if (cudaMemcpyAsync(s.block, host.data(), host.size(), cudaMemcpyHostToDevice, stream) != cudaSuccess ||
         cudaStreamSynchronize(stream) != cudaSuccess)
         return S2_ERR_CUDA;
@@ -298,6 +323,12 @@ int build_schedule_ex(const Plan& plan, const int* text_lengths, const std::vect
     s.video_indices = reinterpret_cast<int*>(base + o_vi);
     s.text_reduce = reinterpret_cast<int4*>(base + o_red);
     s.text_scale = reinterpret_cast<float*>(base + o_scale);
+    s.pack_dst = reinterpret_cast<int*>(base + o_pd);
+    s.pack_dst_rows = static_cast<int>(pack_dst.size());
+    s.max_pos = 0;
+    for (int v : row_pos) s.max_pos = std::max(s.max_pos, v + 1);
+    s.text_dst_off = reinterpret_cast<int*>(base + o_tdo);
+    s.text_dst = reinterpret_cast<int*>(base + o_td);
     s.num_windows = nw;
     s.packed_rows = seq;
     s.num_items = static_cast<int>(sorted.size());

@@ -307,6 +307,20 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi)
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// 32-byte (one full sector) global store; p 32-byte aligned.
+__device__ __forceinline__ void st_v8(void* p, const uint32_t (&r)[8])
+{
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(r[0]), "r"(r[1]), "r"(r[2]),
+                 "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+
+// Barrier over `count` threads (a multiple of 32) on hardware barrier `id` (1..15).
+__device__ __forceinline__ void named_barrier_sync(int id, int count)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v)
 {
     __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);

@@ -119,6 +119,12 @@ struct AttnSchedule
     int* video_indices = nullptr; // [n]
     int4* text_reduce = nullptr;  // [total_text] {first partial row, stride (T), count (nw_s), 0}
     float* text_scale = nullptr;  // [total_text] 1/nw_s
+    // inverse of row_src, for producers that write packed rows directly:
+    int* pack_dst = nullptr;      // [pack_dst_rows] packed row of each video row (-1: none)
+    int pack_dst_rows = 0;
+    int* text_dst_off = nullptr;  // [total_text + 1] CSR offsets into text_dst
+    int* text_dst = nullptr;      // packed rows of each text row (one per window of its sample)
+    int max_pos = 0;              // 1 + largest RoPE position in row_pos
     int partial_rows = 0;         // sum over windows of T_s
     double attn_flops_per_head = 0; // sum over windows of 4 * S^2 * 128 (QK^T + PV)
     void* block = nullptr;        // single device allocation backing the arrays
@@ -147,6 +153,17 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int f32, uint64_t inner, ui
 int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void* A0, const void* A1, const void* W,
                          const float* bias, int epilogue, const float* gate, int out_f32, void* out0, void* out1);
 
+// QKV projection whose epilogue does the work of launch_prepare_qkv: out =
+// A W^T + bias rounded to bf16, per-head RMSNorm (q, k; video / text
+// weights) and 3D RoPE, stored straight into the packed rows of `s`
+// (stream 0 = video rows indexed like row_src, stream 1 = text rows).
+// head_dim 128; heads * 128 a multiple of 256.  rope_table: launch_rope_table
+// output for at least s.max_pos positions.
+int launch_qkv_packed(Context& ctx, const AttnSchedule& s, int M0, int M1, int K, const void* A0, const void* A1,
+                      const void* W, const float* bias, int heads, int rope_pairs, float eps, const float* norms,
+                      const void* rope_table, int rope_positions, void* q_out, void* k_out, void* v_out);
+// [max_pos][pairs] float2 (cos, sin) of pos * freqs[pair]
+int launch_rope_table(Context& ctx, const float* freqs, int pairs, int max_pos, void* table);
 int launch_prepare_qkv(Context& ctx, const AttnSchedule& s, int heads, int head_dim, int rope_pairs, float eps,
                        const float* norms, const float* freqs, int in_bf16, const void* vq, const void* vk,
                        const void* vv, int64_t v_ld, const void* tq, const void* tk, const void* tv, int64_t t_ld,

@@ -85,6 +85,14 @@ def test_block_no_bias_target_windows(gpu_ctx, s2lib, port):
     check(got, ref, prev)
 
 
+def test_block_odd_head_count(gpu_ctx, s2lib, port):
+    """3 heads (D=384): the QKV projection cannot pack whole heads per 256-column tile, so the block runs the
+    projection into a buffer and the separate prepare kernel."""
+    got, ref, prev, x0 = run_case(gpu_ctx, s2lib, port, D=384, heads=3, F=1536, shape=[2, 8, 12], T=9,
+                                  window=[1, 4, 6], mode=1, blocks=2, seed=6)
+    check(got, ref, prev)
+
+
 def test_forward_host_matches_device(gpu_ctx, s2lib):
     """s2_dit_forward_host (host buffers, 2 samples run one after another) == per-sample s2_dit_forward."""
     import torch
