@@ -93,7 +93,9 @@ struct GemmArgs
     PackArgs pack;
 };
 
-template <int BN>
+// Tile t -> (stream, first row, first column); M blocks of BMT rows
+// (128, or 256 for a CTA pair), GROUP_M-row raster.
+template <int BN, int BMT = BM>
 __device__ __forceinline__ void decode_tile(const GemmArgs& a, int t, int& stream, int& m0, int& n0)
 {
     const int mb_total = a.mblk0 + a.mblk1;
@@ -105,9 +107,38 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& a, int t, int& strea
     const int mb = first_m + r % gm;
     const int nb = r / gm;
     stream = mb < a.mblk0 ? 0 : 1;
-    m0 = (stream ? mb - a.mblk0 : mb) * BM;
+    m0 = (stream ? mb - a.mblk0 : mb) * BMT;
     n0 = nb * BN;
 }
+
+// Tile walk of one CTA: a single CTA per tile, or a CTA pair (cluster of 2)
+// per 256-row tile, each CTA owning 128 of its rows.
+struct SingleWalk
+{
+    __device__ int first() const { return blockIdx.x; }
+    __device__ int step() const { return gridDim.x; }
+    template <int BN>
+    __device__ void decode(const GemmArgs& a, int t, int& stream, int& m0, int& n0) const
+    {
+        decode_tile<BN>(a, t, stream, m0, n0);
+    }
+    __device__ void arrive_tempty(uint64_t* bar) const { mbar_arrive(bar); }
+};
+
+struct PairWalk
+{
+    uint32_t rank; // 0 = leader (issues the MMAs)
+    __device__ int first() const { return blockIdx.x >> 1; }
+    __device__ int step() const { return gridDim.x >> 1; }
+    template <int BN>
+    __device__ void decode(const GemmArgs& a, int t, int& stream, int& m0, int& n0) const
+    {
+        decode_tile<BN, 2 * BM>(a, t, stream, m0, n0);
+        m0 += (int)rank * BM;
+    }
+    // accumulator release goes to the leader's barrier
+    __device__ void arrive_tempty(uint64_t* bar) const { mbar_arrive_cluster(mapa_shared(bar, 0)); }
+};
 
 // Wait for all in-flight work tracked by `bar` (phase `parity`) with a time
 // limit only; used on the unwind path so no async copy or MMA outlives the CTA.
@@ -522,8 +553,8 @@ __device__ __forceinline__ void epilogue_tile_pack(const GemmArgs& a, const floa
 // (barrier rfull[slot]), the lanes combine it with the accumulator row in
 // place, and lane 0 TMA-stores it back.  A box is reloaded only after its
 // previous store has read it.  Returns false on a failed wait.
-template <int BN, int R>
-__device__ __forceinline__ bool epilogue_gate_residual(const GemmArgs& a, const CUtensorMap* tmap_o0,
+template <int BN, int R, class Walk>
+__device__ __forceinline__ bool epilogue_gate_residual(const GemmArgs& a, const Walk& wk, const CUtensorMap* tmap_o0,
                                                        const CUtensorMap* tmap_o1, uint8_t* stg, uint64_t* rfull,
                                                        uint64_t* tfull, uint64_t* tempty, uint32_t tmem_base,
                                                        int quarter, int lane, volatile int* abort_flag)
@@ -531,11 +562,11 @@ __device__ __forceinline__ bool epilogue_gate_residual(const GemmArgs& a, const 
     const int N = a.N;
     const int sw = lane & 7;
     // loader cursor (lane 0): next box to load
-    int lt = blockIdx.x, lc = 0, lq = 0;
+    int lt = wk.first(), lc = 0, lq = 0;
     auto issue_load = [&]() {
         if (lt >= a.num_tiles) return;
         int s_, m0_, n0_;
-        decode_tile<BN>(a, lt, s_, m0_, n0_);
+        wk.template decode<BN>(a, lt, s_, m0_, n0_);
         const int slot = lq % R;
         mbar_arrive_expect_tx(&rfull[slot], 4096);
         tma_load_2d(stg + slot * 4096, s_ ? tmap_o1 : tmap_o0, &rfull[slot], n0_ + lc, m0_ + quarter * 32);
@@ -544,7 +575,7 @@ __device__ __forceinline__ bool epilogue_gate_residual(const GemmArgs& a, const 
         if (lc >= BN || n0_ + lc >= N)
         {
             lc = 0;
-            lt += gridDim.x;
+            lt += wk.step();
         }
     };
     if (lane == 0)
@@ -553,7 +584,7 @@ __device__ __forceinline__ bool epilogue_gate_residual(const GemmArgs& a, const 
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < a.num_tiles && ok; t += gridDim.x)
+    for (int t = wk.first(); t < a.num_tiles && ok; t += wk.step())
     {
         int w = 0;
         if (lane == 0) w = mbar_wait(&tfull[acc], acc_phase, abort_flag, a.status) ? 1 : 0;
@@ -566,7 +597,7 @@ __device__ __forceinline__ bool epilogue_gate_residual(const GemmArgs& a, const 
         __syncwarp();
         tc_fence_after();
         int stream, m0, n0;
-        decode_tile<BN>(a, t, stream, m0, n0);
+        wk.template decode<BN>(a, t, stream, m0, n0);
         const int M = stream ? a.M1 : a.M0;
         const bool box_live = m0 + quarter * 32 < M;
         const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
@@ -633,7 +664,7 @@ __device__ __forceinline__ bool epilogue_gate_residual(const GemmArgs& a, const 
         if (!ok) break;
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[acc]);
+        if (lane == 0) wk.arrive_tempty(&tempty[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
     }
@@ -823,7 +854,7 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
         uint8_t* stg = epi_stage + quarter * (TL::R * 4096);
         if constexpr (GR)
         {
-            epilogue_gate_residual<BN, TL::R>(args, &tmap_o0, &tmap_o1, stg, rfull + quarter * TL::R, tfull, tempty,
+            epilogue_gate_residual<BN, TL::R>(args, SingleWalk{}, &tmap_o0, &tmap_o1, stg, rfull + quarter * TL::R, tfull, tempty,
                                               tmem_base, quarter, lane, abort_flag);
         }
         else
@@ -880,6 +911,301 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
     if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
+// ---------------------------------------------------------------- CTA pairs
+// 256 x 256 output tile per cluster of two CTAs (tcgen05 .cta_group::2): each
+// CTA loads its 128 rows of A and its 128 rows of W (half of N) per K step --
+// 32 KB instead of the 48 KB a lone 128 x 256 tile needs -- and receives a
+// 128 x 256 fp32 accumulator in its own TMEM.  The leader (rank 0) issues the
+// M = 256 MMAs; its `full` barriers count both CTAs' TMA bytes, commits
+// arrive in both CTAs, and both CTAs' epilogue warps release an accumulator
+// on the leader's `tempty`.  Loads carry no multicast.
+template <int SKB, int EK>
+struct PairTile
+{
+    static constexpr int A_STAGE = BM * BK * 2;  // 128 rows of A
+    static constexpr int B_STAGE = 128 * BK * 2; // 128 rows of W
+    static constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+    static constexpr int STAGES = (SKB * 1024) / STAGE_BYTES;
+    static constexpr int R = (224 * 1024 - STAGES * STAGE_BYTES) / (4 * 4096);
+    static constexpr int TMEM_COLS = 512; // two 256-column accumulators
+    static constexpr uint32_t IDESC = umma_idesc_bf16(256, 256, 0, 0);
+    static constexpr int EPI_BYTES = 4 * R * 4096;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 512;
+    static_assert(SMEM_BYTES <= 232448, "shared memory");
+};
+
+template <int SKB, int EK>
+__global__ void __launch_bounds__(num_threads(EK), 1)
+    shared_linear_pair_kernel(const __grid_constant__ CUtensorMap tmap_a0, const __grid_constant__ CUtensorMap tmap_a1,
+                              const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_o0,
+                              const __grid_constant__ CUtensorMap tmap_o1, const GemmArgs args)
+{
+    constexpr int BN = 256;
+    using TL = PairTile<SKB, EK>;
+    constexpr bool GR = EK == 1;
+    constexpr int STAGES = TL::STAGES;
+    constexpr int STAGE_BYTES = TL::STAGE_BYTES;
+    constexpr int EW = epilogue_warps(EK);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* epi_stage = smem + STAGES * STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + TL::EPI_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint64_t* rfull = drain + 1; // [4 warps][R] residual boxes (GR)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rfull + 4 * TL::R);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const PairWalk walk{cluster_ctarank()};
+    const bool leader = walk.rank == 0;
+
+    if (threadIdx.x == 0)
+    {
+        for (int s = 0; s < STAGES; s++)
+        {
+            mbar_init(&full[s], 1);  // leader: its producer's expect_tx for both CTAs' bytes
+            mbar_init(&empty[s], 1); // the leader's commit, in both CTAs
+        }
+        for (int b = 0; b < 2; b++)
+        {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 2 * EW); // leader: epilogue warps of both CTAs
+        }
+        mbar_init(drain, 1);
+        if (GR)
+            for (int i = 0; i < 4 * TL::R; i++) mbar_init(&rfull[i], 1);
+        *abort_flag = 0;
+        *tmem_slot = 0;
+        fence_mbarrier_init();
+        tma_prefetch_desc(&tmap_a0);
+        tma_prefetch_desc(&tmap_a1);
+        tma_prefetch_desc(&tmap_w);
+        if (args.tma_out)
+        {
+            tma_prefetch_desc(&tmap_o0);
+            tma_prefetch_desc(&tmap_o1);
+        }
+    }
+    __syncthreads();
+    if (warp == 1) tmem_alloc_pair(tmem_slot, TL::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync(); // both CTAs' barriers exist before any remote arrival
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0)
+    {
+        if (lane == 0)
+        {
+            // ---------------- TMA producer (both CTAs; completion on the leader's barriers)
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued[STAGES];
+            uint32_t last_phase[STAGES];
+            for (int s = 0; s < STAGES; s++) issued[s] = 0, last_phase[s] = 0;
+            for (int t = walk.first(); t < args.num_tiles && !*abort_flag; t += walk.step())
+            {
+                int stream, m0, n0p;
+                decode_tile<BN, 2 * BM>(args, t, stream, m0, n0p);
+                m0 += (int)walk.rank * BM;
+                const int nb = n0p + (int)walk.rank * 128;
+                const CUtensorMap* ta = stream ? &tmap_a1 : &tmap_a0;
+                for (int kb = 0; kb < args.num_kb; kb++)
+                {
+                    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, args.status)) break;
+                    uint8_t* sa = smem + stage * STAGE_BYTES;
+                    uint8_t* sb = sa + TL::A_STAGE;
+                    if (leader) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
+                    const uint32_t fb = mapa_shared(&full[stage], 0);
+                    tma_load_2d_pair(sa, ta, fb, kb * BK, m0);
+                    tma_load_2d_pair(sb, &tmap_w, fb, kb * BK, nb);
+                    issued[stage] = 1;
+                    last_phase[stage] = phase;
+                    if (++stage == STAGES)
+                    {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            if (*abort_flag && leader)
+            {
+                // No TMA write may land after the CTAs exit (the peer's loads
+                // complete on these barriers too).
+                for (int s = 0; s < STAGES; s++)
+                    if (issued[s]) drain_wait(&full[s], last_phase[s]);
+            }
+        }
+    }
+    else if (warp == 1)
+    {
+        if (lane == 0 && leader)
+        {
+            // ---------------- MMA issuer (leader only)
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int t = walk.first(); t < args.num_tiles && !*abort_flag; t += walk.step())
+            {
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, args.status)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                bool ok = true;
+                for (int kb = 0; kb < args.num_kb; kb++)
+                {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, args.status))
+                    {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+                    const uint32_t b_addr = a_addr + TL::A_STAGE;
+#pragma unroll
+                    for (int k = 0; k < BK / 16; k++)
+                    {
+                        const uint64_t ad = umma_desc_sw128(a_addr + k * 32, 16, 1024);
+                        const uint64_t bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
+                        umma_bf16_pair(d_tmem, ad, bd, TL::IDESC, (kb | k) != 0);
+                    }
+                    umma_commit_pair(&empty[stage], 0x3);
+                    if (++stage == STAGES)
+                    {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                umma_commit_pair(&tfull[acc], 0x3);
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1;
+            }
+            // every MMA completes (in both CTAs) before TMEM is released
+            umma_commit_pair(drain, 0x3);
+        }
+        if (lane == 0) drain_wait(drain, 0);
+    }
+    else
+    {
+        // ---------------- epilogue (warps 2..): this CTA's 128 rows of the tile
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row_in_tile = quarter * 32 + lane;
+        uint8_t* stg = epi_stage + quarter * (TL::R * 4096);
+        const float2* rope = args.pack.rope;
+        if constexpr (EK == 2)
+        {
+            if (args.pack.rope_entries > 0 && args.pack.rope_entries * 8 <= TL::EPI_BYTES)
+            {
+                float2* tab = reinterpret_cast<float2*>(epi_stage);
+                for (int i = threadIdx.x - 64; i < args.pack.rope_entries; i += 32 * EW) tab[i] = __ldg(args.pack.rope + i);
+                named_barrier_sync(1, 32 * EW);
+                rope = tab;
+            }
+        }
+        if constexpr (GR)
+        {
+            epilogue_gate_residual<BN, TL::R>(args, walk, &tmap_o0, &tmap_o1, stg, rfull + quarter * TL::R, tfull,
+                                              tempty, tmem_base, quarter, lane, abort_flag);
+        }
+        else
+        {
+            int slot = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int t = walk.first(); t < args.num_tiles; t += walk.step())
+            {
+                int ok = 0;
+                if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, args.status) ? 1 : 0;
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                __syncwarp();
+                tc_fence_after();
+                int stream, m0, n0;
+                walk.decode<BN>(args, t, stream, m0, n0);
+                const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+                if constexpr (EK == 2)
+                {
+                    epilogue_tile_pack<BN>(args, rope, t_row, stream, m0, n0, quarter, lane, half);
+                }
+                else if (args.tma_out)
+                {
+                    epilogue_tile_tma<BN>(args, stream ? &tmap_o1 : &tmap_o0, stg, slot, t_row, stream, m0, n0,
+                                          quarter, lane);
+                }
+                else
+                {
+#pragma unroll 1
+                    for (int c = 0; c < BN / 32; c++)
+                    {
+                        uint32_t v[32];
+                        tmem_ld32(t_row + c * 32, v);
+                        tmem_ld_wait();
+                        if (n0 + c * 32 < args.N) epilogue_chunk(args, stream, m0 + row_in_tile, n0 + c * 32, v);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) walk.arrive_tempty(&tempty[acc]);
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1;
+            }
+            if (lane == 0) bulk_wait<0>();
+            __syncwarp();
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync(); // no remote arrival or MMA operand read outlives either CTA
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem_base, TL::TMEM_COLS);
+}
+
+// Persistent grid of CTA pairs: one pair per tile up to the number of pairs
+// that can be resident at once (cudaOccupancyMaxActiveClusters).
+template <int SKB, int EK>
+cudaError_t launch_pair_variant(cudaStream_t stream, const CUtensorMap& ta0, const CUtensorMap& ta1,
+                                const CUtensorMap& tw, const CUtensorMap& to0, const CUtensorMap& to1,
+                                const GemmArgs& a)
+{
+    static int max_clusters = 0; // per instantiation
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(num_threads(EK));
+    cfg.dynamicSmemBytes = PairTile<SKB, EK>::SMEM_BYTES;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (max_clusters == 0)
+    {
+        cudaError_t e = cudaFuncSetAttribute(shared_linear_pair_kernel<SKB, EK>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, PairTile<SKB, EK>::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        cfg.gridDim = dim3(2);
+        int n = 0;
+        e = cudaOccupancyMaxActiveClusters(&n, shared_linear_pair_kernel<SKB, EK>, &cfg);
+        if (e != cudaSuccess) return e;
+        if (n <= 0) return cudaErrorInvalidConfiguration;
+        max_clusters = n;
+    }
+    const int pairs = a.num_tiles < max_clusters ? a.num_tiles : max_clusters;
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(num_threads(EK));
+    cfg.dynamicSmemBytes = PairTile<SKB, EK>::SMEM_BYTES;
+    return cudaLaunchKernelEx(&cfg, shared_linear_pair_kernel<SKB, EK>, ta0, ta1, tw, to0, to1, a);
+}
+
 template <int BN, int SKB, int EK>
 cudaError_t launch_variant(int grid, cudaStream_t stream, const CUtensorMap& ta0, const CUtensorMap& ta1,
                            const CUtensorMap& tw, const CUtensorMap& to0, const CUtensorMap& to1, const GemmArgs& a)
@@ -902,9 +1228,18 @@ cudaError_t launch_variant(int grid, cudaStream_t stream, const CUtensorMap& ta0
 
 namespace {
 
-// Operand tensor maps, tile count and tile width shared by the launchers.
+enum TileMode
+{
+    TILE_256 = 0,  // one CTA per 128 x 256 tile
+    TILE_128 = 1,  // one CTA per 128 x 128 tile
+    TILE_PAIR = 2, // one CTA pair per 256 x 256 tile
+};
+
+// Operand tensor maps, tile count and tile shape shared by the launchers.
+// The pair tile needs fewer operand bytes per MMA; a narrower tile is taken
+// only when it fills the SMs markedly more evenly.
 int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const void* A1, const void* W,
-               CUtensorMap& ta0, CUtensorMap& ta1, CUtensorMap& tw, GemmArgs& a, bool& narrow)
+               CUtensorMap& ta0, CUtensorMap& ta1, CUtensorMap& tw, GemmArgs& a, int& mode)
 {
     int r = make_tmap_bf16_2d(&ta0, A0, K, M0 > 0 ? M0 : 1, (uint64_t)K * 2, BK, BM);
     if (r == 0) r = make_tmap_bf16_2d(&ta1, M1 > 0 ? A1 : A0, K, M1 > 0 ? M1 : (M0 > 0 ? M0 : 1), (uint64_t)K * 2, BK, BM);
@@ -918,17 +1253,36 @@ int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const
     a.mblk1 = (M1 + BM - 1) / BM;
     a.num_kb = (K + BK - 1) / BK;
     a.status = ctx.status;
-    // Tile width: 128 when it fills the SMs markedly more evenly than 256.
-    auto wave_eff = [&](int bn) {
-        const int tiles = (a.mblk0 + a.mblk1) * ((N + bn - 1) / bn);
-        const int waves = (tiles + ctx.num_sms - 1) / ctx.num_sms;
-        return (double)tiles / ((double)waves * ctx.num_sms);
+    auto wave_eff = [&](int tiles, int slots) {
+        const int waves = (tiles + slots - 1) / slots;
+        return (double)tiles / ((double)waves * slots);
     };
-    narrow = wave_eff(128) > 1.15 * wave_eff(256);
-    const int BNsel = narrow ? 128 : 256;
-    a.nblk = (N + BNsel - 1) / BNsel;
+    const int t256 = (a.mblk0 + a.mblk1) * ((N + 255) / 256);
+    const int t128 = (a.mblk0 + a.mblk1) * ((N + 127) / 128);
+    const int pm0 = (M0 + 2 * BM - 1) / (2 * BM), pm1 = (M1 + 2 * BM - 1) / (2 * BM);
+    const int tpair = (pm0 + pm1) * ((N + 255) / 256);
+    const int pairs = ctx.num_sms / 2;
+    const double e256 = wave_eff(t256, ctx.num_sms), e128 = wave_eff(t128, ctx.num_sms);
+    const double esingle = e128 > 1.15 * e256 ? e128 : e256;
+    if (tpair >= pairs && 1.1 * wave_eff(tpair, pairs) >= esingle)
+    {
+        mode = TILE_PAIR;
+        a.mblk0 = pm0;
+        a.mblk1 = pm1;
+        a.nblk = (N + 255) / 256;
+    }
+    else
+    {
+        mode = e128 > 1.15 * e256 ? TILE_128 : TILE_256;
+        a.nblk = (N + (mode == TILE_128 ? 127 : 255)) / (mode == TILE_128 ? 128 : 256);
+    }
     a.num_tiles = (a.mblk0 + a.mblk1) * a.nblk;
-    return make_tmap_bf16_2d(&tw, W, K, N, (uint64_t)K * 2, BK, BNsel);
+    return make_tmap_bf16_2d(&tw, W, K, N, (uint64_t)K * 2, BK, mode == TILE_256 ? 256 : 128);
+}
+
+int grid_of(const Context& ctx, const GemmArgs& a)
+{
+    return a.num_tiles < ctx.num_sms ? a.num_tiles : ctx.num_sms;
 }
 
 } // namespace
@@ -945,8 +1299,8 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
 
     CUtensorMap ta0, ta1, tw;
     GemmArgs a;
-    bool narrow = false;
-    int r = gemm_setup(ctx, M0, M1, N, K, A0, A1, W, ta0, ta1, tw, a, narrow);
+    int mode = TILE_256;
+    int r = gemm_setup(ctx, M0, M1, N, K, A0, A1, W, ta0, ta1, tw, a, mode);
     if (r != 0) return r;
     // TMA-store epilogue when both outputs admit a tensor map (16-byte aligned
     // bases and row strides); the per-thread store path otherwise.
@@ -969,13 +1323,17 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
     a.out1 = out1;
 
     const bool gr = tma_out && epilogue == EPI_GATE_RESIDUAL;
-    const int grid = a.num_tiles < ctx.num_sms ? a.num_tiles : ctx.num_sms;
+    const int grid = grid_of(ctx, a);
     const double M = (double)M0 + M1;
     const double out_bytes = epilogue == EPI_GATE_RESIDUAL ? 8.0 : (out_f32 ? 4.0 : 2.0);
     ProfileScope prof(ctx, K_GEMM, 2.0 * M * N * K, (M * K + (double)N * K) * 2.0 + M * N * out_bytes);
     const bool deep = gr && K < 4096; // deep residual prefetch for short K
     cudaError_t e;
-    if (narrow)
+    if (mode == TILE_PAIR)
+        e = deep ? launch_pair_variant<160, 1>(ctx.stream, ta0, ta1, tw, to0, to1, a)
+            : gr ? launch_pair_variant<192, 1>(ctx.stream, ta0, ta1, tw, to0, to1, a)
+                 : launch_pair_variant<192, 0>(ctx.stream, ta0, ta1, tw, to0, to1, a);
+    else if (mode == TILE_128)
         e = deep ? launch_variant<128, 144, 1>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
             : gr ? launch_variant<128, 192, 1>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
                  : launch_variant<128, 192, 0>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a);
@@ -1004,8 +1362,8 @@ int launch_qkv_packed(Context& ctx, const AttnSchedule& s, int M0, int M1, int K
     const int N = 3 * D;
     CUtensorMap ta0, ta1, tw;
     GemmArgs a;
-    bool narrow = false;
-    int r = gemm_setup(ctx, M0, M1, N, K, A0, A1, W, ta0, ta1, tw, a, narrow);
+    int mode = TILE_256;
+    int r = gemm_setup(ctx, M0, M1, N, K, A0, A1, W, ta0, ta1, tw, a, mode);
     if (r != 0) return r;
     a.epilogue = EPI_STORE;
     a.bias = bias;
@@ -1023,12 +1381,13 @@ int launch_qkv_packed(Context& ctx, const AttnSchedule& s, int M0, int M1, int K
     a.pack.out[0] = static_cast<__nv_bfloat16*>(q_out);
     a.pack.out[1] = static_cast<__nv_bfloat16*>(k_out);
     a.pack.out[2] = static_cast<__nv_bfloat16*>(v_out);
-    const int grid = a.num_tiles < ctx.num_sms ? a.num_tiles : ctx.num_sms;
+    const int grid = grid_of(ctx, a);
     const double M = (double)M0 + M1;
     ProfileScope prof(ctx, K_GEMM, 2.0 * M * N * K,
                       (M * K + (double)N * K) * 2.0 + (double)s.packed_rows * N * 2.0);
-    const cudaError_t e = narrow ? launch_variant<128, 192, 2>(grid, ctx.stream, ta0, ta1, tw, tw, tw, a)
-                                 : launch_variant<256, 192, 2>(grid, ctx.stream, ta0, ta1, tw, tw, tw, a);
+    const cudaError_t e = mode == TILE_PAIR ? launch_pair_variant<192, 2>(ctx.stream, ta0, ta1, tw, tw, tw, a)
+                          : mode == TILE_128 ? launch_variant<128, 192, 2>(grid, ctx.stream, ta0, ta1, tw, tw, tw, a)
+                                             : launch_variant<256, 192, 2>(grid, ctx.stream, ta0, ta1, tw, tw, tw, a);
     if (e != cudaSuccess) return S2_ERR_CUDA;
     ctx.launches++;
     return S2_OK;
