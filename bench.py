@@ -40,6 +40,17 @@ sys.path.insert(0, ROOT)
 D, HEADS, HD, F, TEXT, PAIRS, BLOCKS = 2560, 20, 128, 10240, 58, 21, 32
 
 # name -> (video shape t,h,w ; window tuple ; window mode 0=target count (reference) 1=extent ; description)
+# DRAM bytes per launch of each kernel class on the C3 workload (single GPU), from
+# `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum` over one 720p block; the command
+# and per-launch table are in profiles/traffic_c3_one_block.md.  shared_linear is the mean of the
+# block's four projections.
+NCU_TRAFFIC_C3 = {
+    "shared_linear": 1104.0e6,
+    "window_attention": 476.0e6,
+    "ada_rmsnorm": 302.6e6,
+    "text_pool": 21.4e6,
+}
+
 CONFIGS = {
     "c1": ([1, 32, 32], [1, 16, 16], 1, "BASELINE config 1 geometry: 1x32x32 tokens, windows 16x16"),
     "c2": ([1, 64, 64], [1, 16, 16], 1, "BASELINE config 2: 1024x1024 image, 64x64 tokens, windows 1x16x16"),
@@ -350,6 +361,14 @@ def main():
 
     peaks = load_peaks()
 
+    def traffic_of(name):
+        """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the committed ncu
+        capture of one 720p block (profiles/traffic_c3_one_block.md); the single-GPU C3 workload only."""
+        if args.config != "c3" or world != 1:
+            return None
+        t = NCU_TRAFFIC_C3.get(name)
+        return None if t is None else {"bytes_per_launch": t, "source": "profiles/traffic_c3_one_block.md"}
+
     def roof(name, bound):
         c = counters[name]
         per_launch_ms = c["ms"] / max(c["launches"], 1)
@@ -365,7 +384,7 @@ def main():
                 "frac": achieved / peak, "peak_source": f"{peaks['source']} "
                 + ("bf16 sustained (kernel timed inside a long step)" if bound == "tensor" else "HBM copy"),
                 "launches_per_step": c["launches"] / args.steps, "ms_per_launch": per_launch_ms,
-                "share_of_step": c["ms"] / args.steps / ms, "traffic": None}
+                "share_of_step": c["ms"] / args.steps / ms, "traffic": traffic_of(name)}
 
     kinds = {"shared_linear": "tensor", "window_attention": "tensor", "prepare_qkv": "hbm", "ada_rmsnorm": "hbm",
              "text_pool": "hbm"}
@@ -388,8 +407,9 @@ def main():
         # prepare_qkv runs only when the QKV projection cannot pack whole heads per tile
         "hbm_passes": {k: roof(k, "hbm") for k in ("prepare_qkv", "ada_rmsnorm", "text_pool")
                        if counters[k]["launches"]},
-        "comm": {"nccl_ms_per_step": counters["comm"]["ms"] / args.steps,
-                 "nccl_bytes_per_step": counters["comm"]["bytes"] / args.steps,
+        # cross-GPU kernels (NVLink peer pushes, flag barriers, text reduce)
+        "comm": {"peer_kernels_ms_per_step": counters["comm"]["ms"] / args.steps,
+                 "peer_bytes_per_step": counters["comm"]["bytes"] / args.steps,
                  "host_wait_ms_per_step": counters["host_wait"]["ms"] / args.steps,
                  "other_kernels_ms_per_step": counters["other"]["ms"] / args.steps},
         "e2e": {"value": None if args.no_e2e else M / (e2e_ms / 1000.0), "unit": "tokens/s",

@@ -24,7 +24,6 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int GROUP_M = 16;
 // warp 0 TMA, warp 1 MMA, then the epilogue warps: 4 (one per TMEM lane
 // quarter), or 8 for the QKV packing epilogue (two per quarter, one head of
 // the tile each), whose per-row work needs two warps per SMSP to hide latency
@@ -82,6 +81,7 @@ struct GemmArgs
 {
     int M0, M1, N, K;
     int mblk0, mblk1, nblk, num_tiles, num_kb;
+    int group_m; // M blocks per raster group (tiles walk M fastest inside a group)
     int epilogue;
     int out_f32;
     int tma_out; // outputs written through tmap_o0 / tmap_o1
@@ -94,15 +94,15 @@ struct GemmArgs
 };
 
 // Tile t -> (stream, first row, first column); M blocks of BMT rows
-// (128, or 256 for a CTA pair), GROUP_M-row raster.
+// (128, or 256 for a CTA pair), raster of group_m M blocks.
 template <int BN, int BMT = BM>
 __device__ __forceinline__ void decode_tile(const GemmArgs& a, int t, int& stream, int& m0, int& n0)
 {
     const int mb_total = a.mblk0 + a.mblk1;
-    const int per_group = GROUP_M * a.nblk;
+    const int per_group = a.group_m * a.nblk;
     const int g = t / per_group;
-    const int first_m = g * GROUP_M;
-    const int gm = min(GROUP_M, mb_total - first_m);
+    const int first_m = g * a.group_m;
+    const int gm = min(a.group_m, mb_total - first_m);
     const int r = t - g * per_group;
     const int mb = first_m + r % gm;
     const int nb = r / gm;
@@ -1277,6 +1277,10 @@ int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const
         a.nblk = (N + (mode == TILE_128 ? 127 : 255)) / (mode == TILE_128 ? 128 : 256);
     }
     a.num_tiles = (a.mblk0 + a.mblk1) * a.nblk;
+    // Raster group height: long-K operands (MLP down) keep fewer A blocks
+    // in L2, narrow-N short-K ones (attention out) a medium group; measured
+    // on the 720p shapes (differences of 2-4 %).
+    a.group_m = K >= 8192 ? 4 : (N <= 4096 ? 8 : 16);
     return make_tmap_bf16_2d(&tw, W, K, N, (uint64_t)K * 2, BK, mode == TILE_256 ? 256 : 128);
 }
 
