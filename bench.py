@@ -45,9 +45,9 @@ D, HEADS, HD, F, TEXT, PAIRS, BLOCKS = 2560, 20, 128, 10240, 58, 21, 32
 # and per-launch table are in profiles/traffic_c3_one_block.md.  shared_linear is the mean of the
 # block's four projections.
 NCU_TRAFFIC_C3 = {
-    "shared_linear": 1104.0e6,
-    "window_attention": 476.0e6,
-    "ada_rmsnorm": 302.6e6,
+    "shared_linear": 996.2e6,
+    "window_attention": 474.2e6,
+    "ada_rmsnorm": 302.0e6,
     "text_pool": 21.4e6,
 }
 
