@@ -171,13 +171,15 @@ __global__ void text_pool_kernel(const int4* __restrict__ reduce, const float* _
 }
 
 // ---------------------------------------------------------------- ada_rmsnorm
-// y = x * (1/sqrt(mean(x^2) + eps)) * scale + shift -> bf16; one warp per row,
-// 8 dims per lane per step.  G = D / 256 steps are held in registers so x is
-// read from HBM once (G = 0: generic two-pass form for other widths).
+// y = x * (1/sqrt(mean(x^2) + eps)) * scale + shift -> bf16; one warp per row.
+// For D = 256 G the row is held in registers (2G float4 per lane, each warp
+// access 512 contiguous bytes) so x is read from HBM once, and two 8-warp
+// blocks fit per SM (128 registers) to keep 16 rows in flight; G = 0 is the
+// generic two-pass form for other widths.
 template <int G>
-__global__ void ada_rmsnorm_kernel(int rows, int D, const float* __restrict__ x, float eps,
-                                   const float* __restrict__ shift, const float* __restrict__ scale,
-                                   __nv_bfloat16* __restrict__ y)
+__global__ void __launch_bounds__(256, 2)
+    ada_rmsnorm_kernel(int rows, int D, const float* __restrict__ x, float eps, const float* __restrict__ shift,
+                       const float* __restrict__ scale, __nv_bfloat16* __restrict__ y)
 {
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -187,27 +189,28 @@ __global__ void ada_rmsnorm_kernel(int rows, int D, const float* __restrict__ x,
     float ss = 0.f;
     if constexpr (G > 0)
     {
-        float v[G][8];
+        // 2G float4 per lane; each warp access covers 512 contiguous bytes
+        constexpr int Q = 2 * G;
+        float4 v[Q];
 #pragma unroll
-        for (int g = 0; g < G; g++)
+        for (int q = 0; q < Q; q++)
         {
-            load8<float>(xr + g * 256 + lane * 8, v[g]);
-#pragma unroll
-            for (int i = 0; i < 8; i++) ss += v[g][i] * v[g][i];
+            v[q] = __ldg(reinterpret_cast<const float4*>(xr + q * 128 + lane * 4));
+            ss += v[q].x * v[q].x + v[q].y * v[q].y + v[q].z * v[q].z + v[q].w * v[q].w;
         }
 #pragma unroll
         for (int m = 16; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
         const float inv = 1.f / sqrtf(ss / D + eps);
 #pragma unroll
-        for (int g = 0; g < G; g++)
+        for (int q = 0; q < Q; q++)
         {
-            const int c = g * 256 + lane * 8;
-            float sc[8], sh[8];
-            load8<float>(scale + c, sc);
-            load8<float>(shift + c, sh);
-#pragma unroll
-            for (int i = 0; i < 8; i++) v[g][i] = v[g][i] * inv * sc[i] + sh[i];
-            store8_bf16(yr + c, v[g]);
+            const int c = q * 128 + lane * 4;
+            const float4 sc = __ldg(reinterpret_cast<const float4*>(scale + c));
+            const float4 sh = __ldg(reinterpret_cast<const float4*>(shift + c));
+            uint2 u;
+            u.x = pack_bf16x2(v[q].x * inv * sc.x + sh.x, v[q].y * inv * sc.y + sh.y);
+            u.y = pack_bf16x2(v[q].z * inv * sc.z + sh.z, v[q].w * inv * sc.w + sh.w);
+            *reinterpret_cast<uint2*>(yr + c) = u;
         }
     }
     else
