@@ -56,12 +56,22 @@ struct s2_dit
         s2::ShardPlan sp;
         s2::AttnSchedule sched[2];
         // Peer-visible exchange buffer (same layout on every rank):
-        // qkv [E][3D] bf16 | ctx [E][D] bf16 | text partial [2][T][D] f32 | flags.
+        // fused QKV packing (D % 256 == 0): packed Q | K | V [R][D] bf16, written
+        //   by every rank's QKV projection for the windows this rank owns;
+        // otherwise qkv [E][3D] bf16 rows pushed to window owners;
+        // then ctx [E][D] bf16 | text partial [2][T][D] f32 | flags.
         // The text partial is double-buffered by block parity: a block without
         // row pushes has no first barrier, so a rank may write block b+1's
         // partial while a slower rank still sums block b's.
         void* xbuf = nullptr;
+        bool fused = false;
+        size_t off_q = 0, off_k = 0, off_v = 0; // packed Q/K/V (fused)
         size_t off_ctx = 0, off_text = 0, off_flags = 0;
+        std::vector<void*> peer_q, peer_k, peer_v;
+        // fused: per plan, own row -> packed row at the window owner (peer field)
+        // and its RoPE positions (window-local (t + T, h, w))
+        int* d_pack[2] = {nullptr, nullptr}; // [n] dst | [n][3] positions
+        int max_pos = 0;                     // 1 + largest RoPE position this rank uses
         std::vector<void*> base;                     // every rank's xbuf (mapped)
         std::vector<void*> peer_qkv, peer_ctx, peer_text[2], peer_flags;
         int4* d_push[2] = {nullptr, nullptr};        // {own row, rank, row there, 0}
@@ -70,7 +80,10 @@ struct s2_dit
         ~Shard()
         {
             for (int p = 0; p < 2; p++)
+            {
                 if (d_push[p]) cudaFree(d_push[p]);
+                if (d_pack[p]) cudaFree(d_pack[p]);
+            }
             if (xbuf) cudaFree(xbuf);
         }
     };
@@ -377,7 +390,54 @@ int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, f
         int E = 0;
         for (int q = 0; q < world && r == S2_OK; q++)
             E = std::max(E, sp.n_local[q] + T + std::max(sp.m_foreign_all[0][q], sp.m_foreign_all[1][q]));
-        sh->off_ctx = align256((size_t)E * 3 * D * 2);
+        // Fused packing: every window's rows land at its owner, windows in
+        // ascending order, each = its tokens (partition order) then T text
+        // rows -- the order build_schedule_ex packs the owner's windows in.
+        sh->fused = D % 256 == 0;
+        std::vector<int> pack_tab[2];
+        int R = 1;
+        for (int p = 0; p < 2 && r == S2_OK && sh->fused; p++)
+        {
+            const s2::Plan& pl = sp.plan[p];
+            const int nw = static_cast<int>(pl.windows.size() / 9);
+            std::vector<int> seq(world, 0), seq_off(nw, 0);
+            for (int w = 0; w < nw; w++)
+            {
+                const int q = sp.owner[p][w];
+                seq_off[w] = seq[q];
+                seq[q] += pl.windows[9 * w + 8] + T;
+            }
+            for (int q = 0; q < world; q++) R = std::max(R, seq[q]);
+            const int n = sp.n_local[rank];
+            pack_tab[p].assign((size_t)n * 4, -1);
+            for (int w = 0; w < nw; w++)
+            {
+                const int q = sp.owner[p][w], part = pl.windows[9 * w + 7], cnt = pl.windows[9 * w + 8];
+                for (int i = 0; i < cnt; i++)
+                {
+                    const int g = pl.video_indices[part + i];
+                    if (sp.token_owner[g] != rank) continue;
+                    const int row = sp.token_local[g];
+                    const int dst = seq_off[w] + i;
+                    pack_tab[p][row] = q == rank ? dst : ((q + 1) << s2::kPeerShift) | dst;
+                    pack_tab[p][n + 3 * row] = pl.local_positions[3 * (part + i)] + T;
+                    pack_tab[p][n + 3 * row + 1] = pl.local_positions[3 * (part + i) + 1];
+                    pack_tab[p][n + 3 * row + 2] = pl.local_positions[3 * (part + i) + 2];
+                }
+            }
+            for (size_t i = (size_t)n; i < pack_tab[p].size(); i++) sh->max_pos = std::max(sh->max_pos, pack_tab[p][i] + 1);
+            if (cudaMalloc(&sh->d_pack[p], std::max<size_t>(pack_tab[p].size(), 4) * 4) != cudaSuccess)
+                r = S2_ERR_ALLOC;
+            else if (!pack_tab[p].empty() &&
+                     cudaMemcpy(sh->d_pack[p], pack_tab[p].data(), pack_tab[p].size() * 4, cudaMemcpyHostToDevice) !=
+                         cudaSuccess)
+                r = S2_ERR_CUDA;
+        }
+        const size_t sz_pk = align256((size_t)R * D * 2);
+        sh->off_q = 0;
+        sh->off_k = sh->fused ? sz_pk : 0;
+        sh->off_v = sh->fused ? 2 * sz_pk : 0;
+        sh->off_ctx = sh->fused ? 3 * sz_pk : align256((size_t)E * 3 * D * 2);
         sh->off_text = sh->off_ctx + align256((size_t)E * D * 2);
         sh->off_flags = sh->off_text + 2 * align256((size_t)T * D * 4);
         const size_t xbytes = sh->off_flags + 256;
@@ -394,6 +454,9 @@ int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, f
         {
             uint8_t* b = static_cast<uint8_t*>(sh->base[q]);
             sh->peer_qkv.push_back(b);
+            sh->peer_q.push_back(b + sh->off_q);
+            sh->peer_k.push_back(b + sh->off_k);
+            sh->peer_v.push_back(b + sh->off_v);
             sh->peer_ctx.push_back(b + sh->off_ctx);
             sh->peer_text[0].push_back(b + sh->off_text);
             sh->peer_text[1].push_back(b + sh->off_text + align256((size_t)T * D * 4));
@@ -441,7 +504,13 @@ int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, f
     const int M = n + T; // rows of x / h / u (own video rows, then text)
     const int max_packed = std::max(sh.sched[0].packed_rows, sh.sched[1].packed_rows);
     const int max_partial = std::max(sh.sched[0].partial_rows, sh.sched[1].partial_rows);
-    const size_t sz_h = align256((size_t)M * D * 2), sz_pk = align256((size_t)std::max(max_packed, 1) * D * 2),
+    if (sh.fused &&
+        (r = ensure_rope_tables(d, std::max(sh.max_pos, std::max(sh.sched[0].max_pos, sh.sched[1].max_pos)))) !=
+            S2_OK)
+        return r;
+    const size_t rope_block = (size_t)d->rope_pos * cfg.rope_pairs * 8;
+    const size_t sz_h = align256((size_t)M * D * 2),
+                 sz_pk = sh.fused ? 0 : align256((size_t)std::max(max_packed, 1) * D * 2),
                  sz_part = align256((size_t)std::max(max_partial, 1) * D * 4), sz_u = align256((size_t)M * F * 2);
     if ((r = d->act.ensure(sz_h + 3 * sz_pk + sz_part + sz_u)) != S2_OK) return r;
     if ((r = d->mods.ensure((size_t)cfg.num_blocks * 6 * D * 4)) != S2_OK) return r;
@@ -471,25 +540,52 @@ int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, f
         const int shf = b & 1;
         const s2::AttnSchedule& S = sh.sched[shf];
         if ((r = s2::launch_ada_rmsnorm(c, M, D, x, cfg.norm_eps, mb, mb + D, h)) != S2_OK) return r;
-        if ((r = s2::launch_shared_linear(c, M, 0, 3 * D, D, h, nullptr, bl.w_qkv, cfg.qkv_bias ? bl.b_qkv : nullptr,
-                                          s2::EPI_STORE, nullptr, 0, qkv, nullptr)) != S2_OK)
-            return r;
-        if (world > 1 && sh.any_push[shf])
+        __nv_bfloat16 *Qp, *Kp, *Vp;
+        if (sh.fused)
         {
-            // own qkv rows of tokens in other ranks' windows -> straight into the owners' buffers
-            if ((r = s2::launch_push_rows(c, qkv, 3 * D, sh.d_push[shf], sh.push_count[shf], sh.peer_qkv.data(),
-                                          world)) != S2_OK)
+            // QKV projection + qk norm + RoPE, each row stored into the packed
+            // window of the GPU that owns it (NVLink peer stores)
+            Qp = static_cast<__nv_bfloat16*>(sh.peer_q[rank]);
+            Kp = static_cast<__nv_bfloat16*>(sh.peer_k[rank]);
+            Vp = static_cast<__nv_bfloat16*>(sh.peer_v[rank]);
+            s2::QkvPeers peers;
+            peers.dst0 = sh.d_pack[shf];
+            peers.dst0_rows = n;
+            peers.pos0 = sh.d_pack[shf] + n;
+            peers.q = sh.peer_q.data();
+            peers.k = sh.peer_k.data();
+            peers.v = sh.peer_v.data();
+            peers.num_peers = world;
+            if ((r = s2::launch_qkv_packed(c, S, n, T, D, h, h + (size_t)n * D, bl.w_qkv,
+                                           cfg.qkv_bias ? bl.b_qkv : nullptr, H, cfg.rope_pairs, cfg.qk_eps,
+                                           bl.qk_norm, static_cast<uint8_t*>(d->rope.ptr) + rope_block * b,
+                                           d->rope_pos, Qp, Kp, Vp, &peers)) != S2_OK)
                 return r;
-            if ((r = barrier()) != S2_OK) return r;
+            if (world > 1 && sh.any_push[shf] && (r = barrier()) != S2_OK) return r;
         }
-        __nv_bfloat16* Qp = reinterpret_cast<__nv_bfloat16*>(pk);
-        __nv_bfloat16* Kp = reinterpret_cast<__nv_bfloat16*>(pk + sz_pk);
-        __nv_bfloat16* Vp = reinterpret_cast<__nv_bfloat16*>(pk + 2 * sz_pk);
-        const __nv_bfloat16* tq = qkv + (size_t)n * 3 * D;
-        if ((r = s2::launch_prepare_qkv(c, S, H, cfg.head_dim, cfg.rope_pairs, cfg.qk_eps, bl.qk_norm, bl.freqs, 1, qkv,
-                                        qkv + D, qkv + 2 * D, 3 * D, tq, tq + D, tq + 2 * D, 3 * D, Qp, Kp, Vp)) !=
-            S2_OK)
-            return r;
+        else
+        {
+            if ((r = s2::launch_shared_linear(c, M, 0, 3 * D, D, h, nullptr, bl.w_qkv,
+                                              cfg.qkv_bias ? bl.b_qkv : nullptr, s2::EPI_STORE, nullptr, 0, qkv,
+                                              nullptr)) != S2_OK)
+                return r;
+            if (world > 1 && sh.any_push[shf])
+            {
+                // own qkv rows of tokens in other ranks' windows -> straight into the owners' buffers
+                if ((r = s2::launch_push_rows(c, qkv, 3 * D, sh.d_push[shf], sh.push_count[shf],
+                                              sh.peer_qkv.data(), world)) != S2_OK)
+                    return r;
+                if ((r = barrier()) != S2_OK) return r;
+            }
+            Qp = reinterpret_cast<__nv_bfloat16*>(pk);
+            Kp = reinterpret_cast<__nv_bfloat16*>(pk + sz_pk);
+            Vp = reinterpret_cast<__nv_bfloat16*>(pk + 2 * sz_pk);
+            const __nv_bfloat16* tq = qkv + (size_t)n * 3 * D;
+            if ((r = s2::launch_prepare_qkv(c, S, H, cfg.head_dim, cfg.rope_pairs, cfg.qk_eps, bl.qk_norm, bl.freqs,
+                                            1, qkv, qkv + D, qkv + 2 * D, 3 * D, tq, tq + D, tq + 2 * D, 3 * D, Qp,
+                                            Kp, Vp)) != S2_OK)
+                return r;
+        }
         // context rows of foreign tokens are stored into their owners' buffers by the epilogue
         if ((r = s2::launch_window_attention(c, S, H, Qp, Kp, Vp, 0, 0, ctxb, partial, sh.peer_ctx.data(),
                                              world > 1 ? world : 0)) != S2_OK)

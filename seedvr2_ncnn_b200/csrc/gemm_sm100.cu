@@ -66,8 +66,10 @@ struct PackArgs
     int D;      // heads * 128 (columns of each of q, k, v)
     int pairs;  // RoPE pairs per axis
     float eps;
-    const int* dst0; // [dst0_rows] packed row of each stream-0 (video) row, -1: none
+    const int* dst0; // [dst0_rows] packed row of each stream-0 (video) row, -1: none;
+                     // row | (peer + 1) << kPeerShift: the row lives on a peer GPU
     int dst0_rows;
+    const int* pos0; // [dst0_rows][3] RoPE positions of stream-0 rows (null: row_pos of the packed row)
     const int* tdst_off; // [M1 + 1] CSR offsets of each stream-1 (text) row's packed rows
     const int* tdst;
     const int* row_pos;  // [packed rows][3] RoPE positions
@@ -75,6 +77,7 @@ struct PackArgs
     const float2* rope;  // [positions][pairs] (cos, sin)
     int rope_entries;    // positions * pairs; staged in shared memory when it fits
     __nv_bfloat16* out[3]; // packed q, k, v [packed rows][D]
+    __nv_bfloat16* peer_out[3][kMaxPeers]; // the same buffers on peer GPUs (NVLink peer memory)
 };
 
 struct GemmArgs
@@ -405,7 +408,8 @@ __device__ __forceinline__ void epilogue_tile_pack(const GemmArgs& a, const floa
     const int row = m0 + quarter * 32 + lane;
     const int part = n0 / p.D;
     const int col0 = n0 - part * p.D;
-    __nv_bfloat16* const base = p.out[part];
+    __nv_bfloat16* base = p.out[part];
+    bool remote = false;
     int first = -1, cnt = 0;
     const int* list = nullptr;
     if (row < M)
@@ -414,6 +418,13 @@ __device__ __forceinline__ void epilogue_tile_pack(const GemmArgs& a, const floa
         {
             first = row < p.dst0_rows ? __ldg(p.dst0 + row) : -1;
             cnt = first >= 0 ? 1 : 0;
+            const int peer = first >= 0 ? first >> kPeerShift : 0;
+            if (peer)
+            {
+                base = p.peer_out[part][peer - 1];
+                first &= (1 << kPeerShift) - 1;
+                remote = true;
+            }
         }
         else
         {
@@ -432,9 +443,10 @@ __device__ __forceinline__ void epilogue_tile_pack(const GemmArgs& a, const floa
     const float2* rp2 = rope;
     if (qk && first >= 0)
     {
-        rp0 = rope + __ldg(p.row_pos + 3 * first) * p.pairs;
-        rp1 = rope + __ldg(p.row_pos + 3 * first + 1) * p.pairs;
-        rp2 = rope + __ldg(p.row_pos + 3 * first + 2) * p.pairs;
+        const int* pp = (stream == 0 && p.pos0) ? p.pos0 + 3 * row : p.row_pos + 3 * first;
+        rp0 = rope + __ldg(pp) * p.pairs;
+        rp1 = rope + __ldg(pp + 1) * p.pairs;
+        rp2 = rope + __ldg(pp + 2) * p.pairs;
     }
     const int aw = 2 * p.pairs;
     const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -544,6 +556,9 @@ __device__ __forceinline__ void epilogue_tile_pack(const GemmArgs& a, const floa
             }
         }
     }
+    // rows stored into a peer GPU must be visible there once this rank
+    // passes its next cross-GPU barrier
+    if (remote) __threadfence_system();
 }
 
 // Gate-residual epilogue of one warp over all of the CTA's tiles, fp32
@@ -1352,11 +1367,14 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
 
 int launch_qkv_packed(Context& ctx, const AttnSchedule& s, int M0, int M1, int K, const void* A0, const void* A1,
                       const void* W, const float* bias, int heads, int rope_pairs, float eps, const float* norms,
-                      const void* rope_table, int rope_positions, void* q_out, void* k_out, void* v_out)
+                      const void* rope_table, int rope_positions, void* q_out, void* k_out, void* v_out,
+                      const QkvPeers* peers)
 {
     const int D = heads * 128;
     if (heads <= 0 || D % 256 != 0 || M0 < 0 || M1 < 0 || M0 + M1 <= 0 || K <= 0 || K % 8 || !A0 || !W ||
-        (M1 > 0 && !A1) || M0 > s.pack_dst_rows || M1 > s.total_text || rope_pairs < 0 || 6 * rope_pairs > 128 ||
+        (M1 > 0 && !A1) || M0 > (peers ? peers->dst0_rows : s.pack_dst_rows) || M1 > s.total_text || rope_pairs < 0 ||
+        6 * rope_pairs > 128 || (peers && (!peers->dst0 || !peers->pos0 || peers->num_peers < 0 ||
+                                            peers->num_peers > kMaxPeers)) ||
         !norms || (rope_pairs > 0 && (!rope_table || rope_positions < s.max_pos)) || !q_out || !k_out || !v_out ||
         (bias && (reinterpret_cast<uintptr_t>(bias) & 15)) || (reinterpret_cast<uintptr_t>(norms) & 15))
         return S2_ERR_INVALID;
@@ -1374,8 +1392,16 @@ int launch_qkv_packed(Context& ctx, const AttnSchedule& s, int M0, int M1, int K
     a.pack.D = D;
     a.pack.pairs = rope_pairs;
     a.pack.eps = eps;
-    a.pack.dst0 = s.pack_dst;
-    a.pack.dst0_rows = s.pack_dst_rows;
+    a.pack.dst0 = peers ? peers->dst0 : s.pack_dst;
+    a.pack.dst0_rows = peers ? peers->dst0_rows : s.pack_dst_rows;
+    a.pack.pos0 = peers ? peers->pos0 : nullptr;
+    if (peers)
+        for (int i = 0; i < peers->num_peers; i++)
+        {
+            a.pack.peer_out[0][i] = static_cast<__nv_bfloat16*>(peers->q[i]);
+            a.pack.peer_out[1][i] = static_cast<__nv_bfloat16*>(peers->k[i]);
+            a.pack.peer_out[2][i] = static_cast<__nv_bfloat16*>(peers->v[i]);
+        }
     a.pack.tdst_off = s.text_dst_off;
     a.pack.tdst = s.text_dst;
     a.pack.row_pos = s.row_pos;

@@ -159,9 +159,23 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
 // (stream 0 = video rows indexed like row_src, stream 1 = text rows).
 // head_dim 128; heads * 128 a multiple of 256.  rope_table: launch_rope_table
 // output for at least s.max_pos positions.
+// Multi-GPU form: stream-0 rows are stored to the packed row dst0[row] of
+// the GPU named by its peer field (row | (peer + 1) << kPeerShift) with RoPE
+// positions pos0[row][3]; q/k/v[i] are peer i's packed buffers.
+struct QkvPeers
+{
+    const int* dst0;
+    int dst0_rows;
+    const int* pos0;
+    void* const* q;
+    void* const* k;
+    void* const* v;
+    int num_peers;
+};
 int launch_qkv_packed(Context& ctx, const AttnSchedule& s, int M0, int M1, int K, const void* A0, const void* A1,
                       const void* W, const float* bias, int heads, int rope_pairs, float eps, const float* norms,
-                      const void* rope_table, int rope_positions, void* q_out, void* k_out, void* v_out);
+                      const void* rope_table, int rope_positions, void* q_out, void* k_out, void* v_out,
+                      const QkvPeers* peers = nullptr);
 // [max_pos][pairs] float2 (cos, sin) of pos * freqs[pair]
 int launch_rope_table(Context& ctx, const float* freqs, int pairs, int max_pos, void* table);
 int launch_prepare_qkv(Context& ctx, const AttnSchedule& s, int heads, int head_dim, int rope_pairs, float eps,

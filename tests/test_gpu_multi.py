@@ -1,11 +1,14 @@
-"""Multi-GPU parity: the sharded forward (s2_dit_forward_sharded over NCCL,
-one process per GPU) reproduces the single-GPU forward.  Runs only where the
-box has at least 2 GPUs; NVLS is off (NCCL_NVLS_ENABLE=0) and the library's
-own kernels only read local memory.
+"""Multi-GPU parity: the sharded forward (s2_dit_forward_sharded, one
+process per GPU, rows exchanged over NVLink peer memory) reproduces the
+single-GPU forward.  Runs only where the box has at least 2 GPUs; NVLS is off
+(NCCL_NVLS_ENABLE=0; NCCL only sets up the communicator and the IPC handle
+exchange).  Cases with D % 256 == 0 take the fused path (the QKV projection
+stores rows into the window owners' packed buffers); D = 384 takes the qkv
+push + prepare path.
 
 Rows are computed by the same kernels in both runs; only the text-pool sum
-order (all-reduce) differs, which can flip the bf16 rounding of a text
-context element, so the gate is: cosine >= 0.99999 and
+order (partials summed over ranks) differs, which can flip the bf16 rounding
+of a text context element, so the gate is: cosine >= 0.99999 and
 max|a-b|/max|b| <= 5e-3 (the per-block gate of the north star is 2e-2).
 """
 import os
@@ -22,6 +25,7 @@ CASES = [
     # shape, window, mode, D, heads, F, blocks
     ([2, 12, 20], [1, 8, 8], 1, 512, 4, 2048, 2),
     ([6, 45, 80], [4, 3, 4], 0, 2560, 20, 10240, 2),
+    ([2, 8, 12], [1, 4, 6], 1, 384, 3, 1536, 2),
 ]
 
 
