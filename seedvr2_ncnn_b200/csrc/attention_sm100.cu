@@ -40,11 +40,11 @@ constexpr int TILE = 128;                    // q rows / keys per tile
 constexpr int CHUNK_BYTES = TILE * 128;      // 128 rows x 64 bf16 (one swizzle row each)
 constexpr int TILE_BYTES = 2 * CHUNK_BYTES;  // 128 x 128 bf16
 constexpr int NUM_THREADS = 320;             // TMA, MMA, 2 x 4 softmax warps
-constexpr int TMEM_COLS = 512;               // S/P_A [0,128) S/P_B [128,256) O_A [256,384) O_B [384,512)
-constexpr uint32_t IDESC_O = umma_idesc_bf16(128, 128, 0, 1); // B (= V) MN-major
-constexpr int K_STAGES = 3;
-constexpr int V_STAGES = 2;
-constexpr int SMEM_BYTES = (2 + K_STAGES + V_STAGES) * TILE_BYTES + 1024 + 256; // Q_A, Q_B, K ring, V ring
+constexpr int TMEM_COLS = 512;               // S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512)
+constexpr uint32_t IDESC_O = umma_idesc_bf16(128, 128, 0, 1); // A (= P) K-major, B (= V) MN-major
+constexpr int K_STAGES = 2;
+// Q_A, Q_B | K ring (2) | V (1) | P_A, P_B  = 7 x 32 KB
+constexpr int SMEM_BYTES = (2 + K_STAGES + 1 + 2) * TILE_BYTES + 1024 + 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;                     // log2 units
 
 struct AttnArgs
@@ -144,43 +144,46 @@ __device__ __forceinline__ float row_max(const uint32_t (&v)[128], int valid)
     return fmax3(m[0], m[1], fmaxf(m[2], m[3]));
 }
 
-// P = exp2(S * c - m) for the row (masked columns -> 0), written over the
-// first 64 TMEM columns of the S tile as packed bf16 pairs.  The exponent
-// t = S * c - m is formed in fp32 (packed pairs), rounded to bf16 and
-// exponentiated two at a time (ex2.approx.ftz.bf16x2), so P leaves the MUFU
-// already in its bf16 MMA format; the row sum adds exactly those bf16
-// values in fp32 (four independent packed partial sums).
-template <bool FULL>
-__device__ __forceinline__ float row_exp(const uint32_t (&v)[128], int valid, uint64_t c2, uint64_t negm2,
-                                         uint32_t s_addr)
+// P = exp2(S * c - m) for half H (64 columns) of the row (masked columns ->
+// 0) as 32 packed bf16 pairs.  The exponent t = S * c - m is formed in fp32
+// (packed pairs), rounded to bf16 and exponentiated two at a time
+// (ex2.approx.ftz.bf16x2), so P leaves the MUFU already in its bf16 MMA
+// format; the row sum adds exactly those bf16 values in fp32 (packed partial
+// sums in sum2).
+template <bool FULL, int H>
+__device__ __forceinline__ void row_exp_half(const uint32_t (&v)[128], int valid, uint64_t c2, uint64_t negm2,
+                                             uint32_t (&p)[32], uint64_t (&sum2)[4])
 {
-    uint64_t sum2[4] = {0, 0, 0, 0};
 #pragma unroll
-    for (int c = 0; c < 4; c++)
+    for (int q = 0; q < 32; q++)
     {
-        uint32_t packed[16];
-#pragma unroll
-        for (int q = 0; q < 16; q++)
+        const int i = 64 * H + 2 * q;
+        const uint64_t t2 = ffma2(pk2(v[i], v[i + 1]), c2, negm2);
+        float t0, t1;
+        upk2(t2, t0, t1);
+        if (!FULL)
         {
-            const int i = c * 32 + 2 * q;
-            const uint64_t t2 = ffma2(pk2(v[i], v[i + 1]), c2, negm2);
-            float t0, t1;
-            upk2(t2, t0, t1);
-            if (!FULL)
-            {
-                t0 = i < valid ? t0 : -INFINITY;
-                t1 = i + 1 < valid ? t1 : -INFINITY;
-            }
-            const uint32_t p = ex2_bf16x2(pack_bf16x2(t0, t1));
-            packed[q] = p;
-            sum2[q & 3] = fadd2(sum2[q & 3], pk2(p << 16, p & 0xFFFF0000u));
+            t0 = i < valid ? t0 : -INFINITY;
+            t1 = i + 1 < valid ? t1 : -INFINITY;
         }
-        tmem_st16(s_addr + c * 16, packed);
+        const uint32_t e = ex2_bf16x2(pack_bf16x2(t0, t1));
+        p[q] = e;
+        sum2[q & 3] = fadd2(sum2[q & 3], pk2(e << 16, e & 0xFFFF0000u));
     }
-    const uint64_t s2 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
-    float lo, hi;
-    upk2(s2, lo, hi);
-    return lo + hi;
+}
+
+// Half H (64 columns = one 128-byte chunk) of row `row` of a 128 x 128 bf16
+// tile in the 128-byte-swizzled K-major layout TMA gives Q and K (chunks of
+// 128 rows x 128 bytes; 16-byte unit u of row r at unit u ^ (r & 7)), so the
+// PV MMA reads P like Q.
+template <int H>
+__device__ __forceinline__ void store_p_half(uint8_t* tile, int row, const uint32_t (&p)[32])
+{
+    uint8_t* r0 = tile + H * CHUNK_BYTES + row * 128;
+    const int sw = row & 7;
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+        *reinterpret_cast<uint4*>(r0 + ((u ^ sw) << 4)) = make_uint4(p[4 * u], p[4 * u + 1], p[4 * u + 2], p[4 * u + 3]);
 }
 
 __device__ __forceinline__ float bf16_round_f32(float x)
@@ -281,30 +284,39 @@ __device__ __forceinline__ Work decode_work(const AttnArgs& a, int w)
     return r;
 }
 
-// Persistent: CTA b processes units b, b + gridDim.x, ...  The K/V ring and
-// every barrier phase run on across units, so the next unit's K/V loads,
-// its first S MMA and the L2 prefetch of its Q overlap the current unit's
-// last tiles and epilogue.  Q is reloaded once the unit's last S MMA has
-// read it (q_empty).
+// Persistent: CTA b processes units b, b + gridDim.x, ...  Barrier phases run
+// on across units, so the next unit's loads and first S MMAs overlap the
+// current unit's last tiles and epilogue; Q is reloaded once the unit's last
+// S MMA has read it (q_empty).
+//
+// P lives in shared memory, not over S in TMEM: as soon as a softmax warp
+// group has read S_x(j) into registers (s_free) the MMA thread issues
+// S_x(j+1) into the same TMEM columns, so the tensor core computes the next
+// scores while the exponentials of this tile run; PV_x(j) (shared-memory A =
+// P_x, B = V) follows once P_x(j) is stored (p_full).  A softmax group waits
+// for PV_x(j-1) (p_empty) before overwriting P_x or rescaling O_x.
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     window_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                             const __grid_constant__ CUtensorMap tv, const AttnArgs args)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem;                // Q_A, Q_B
+    uint8_t* sQ = smem;                       // Q_A, Q_B
     uint8_t* sK = sQ + 2 * TILE_BYTES;        // K ring
-    uint8_t* sV = sK + K_STAGES * TILE_BYTES; // V ring
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + V_STAGES * TILE_BYTES);
+    uint8_t* sV = sK + K_STAGES * TILE_BYTES; // V
+    uint8_t* sP = sV + TILE_BYTES;            // P_A, P_B
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * TILE_BYTES);
     uint64_t* q_full = bars + 0;
     uint64_t* q_empty = bars + 1;
-    uint64_t* k_full = bars + 2;   // [K_STAGES]
-    uint64_t* k_empty = bars + 5;  // [K_STAGES]
-    uint64_t* v_full = bars + 8;   // [V_STAGES]
-    uint64_t* v_empty = bars + 10; // [V_STAGES]
-    uint64_t* s_full = bars + 12;  // [2] per query tile
-    uint64_t* p_full = bars + 14;  // [2] per query tile
-    uint64_t* o_done = bars + 16;  // [2] per query tile
+    uint64_t* k_full = bars + 2;  // [K_STAGES]
+    uint64_t* k_empty = bars + 4; // [K_STAGES]
+    uint64_t* v_full = bars + 6;
+    uint64_t* v_empty = bars + 7;
+    uint64_t* s_full = bars + 8;   // [2] per query tile: S_x computed
+    uint64_t* s_free = bars + 10;  // [2] S_x read by the softmax warps (4 arrivals)
+    uint64_t* p_full = bars + 12;  // [2] P_x stored (4 arrivals)
+    uint64_t* p_empty = bars + 14; // [2] PV_x done (P_x and O_x free)
+    uint64_t* o_done = bars + 16;  // [2] last PV_x of the unit done
     uint64_t* drain = bars + 18;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -321,15 +333,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(&k_full[s], 1);
             mbar_init(&k_empty[s], 1);
         }
-        for (int s = 0; s < V_STAGES; s++)
-        {
-            mbar_init(&v_full[s], 1);
-            mbar_init(&v_empty[s], 1);
-        }
+        mbar_init(v_full, 1);
+        mbar_init(v_empty, 1);
         for (int s = 0; s < 2; s++)
         {
             mbar_init(&s_full[s], 1);
-            mbar_init(&p_full[s], 4); // one arrival per softmax warp
+            mbar_init(&s_free[s], 4);
+            mbar_init(&p_full[s], 4);
+            mbar_init(&p_empty[s], 1);
             mbar_init(&o_done[s], 1);
         }
         mbar_init(drain, 1);
@@ -346,13 +357,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     {
         if (lane == 0)
         {
-            // ---------------- TMA producer
-            int g = 0; // K/V tiles issued so far (ring position)
+            // ---------------- TMA producer: Q pair per unit, K tiles into the ring
+            int g = 0; // K tiles issued so far
             int it = 0;
             bool q_out = false;
             uint32_t q_par = 0;
-            int k_issued[K_STAGES] = {0, 0, 0}, v_issued[V_STAGES] = {0, 0};
-            uint32_t k_par[K_STAGES] = {0, 0, 0}, v_par[V_STAGES] = {0, 0};
+            int k_issued[K_STAGES] = {0, 0};
+            uint32_t k_par[K_STAGES] = {0, 0};
             for (int w = blockIdx.x; w < args.num_work && !*abort_flag; w += gridDim.x, it++)
             {
                 const Work wk = decode_work(args, w);
@@ -381,10 +392,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     }
                 }
                 bool ok = true;
-                // K(j) then V(j): the order the MMA issuer consumes them
                 for (int j = 0; j < wk.nkv; j++, g++)
                 {
-                    const int y = wk.seq_off + j * TILE;
                     const int ks = g % K_STAGES;
                     const uint32_t kp = (uint32_t)(g / K_STAGES) & 1u;
                     if (!mbar_wait(&k_empty[ks], kp ^ 1, abort_flag, args.status))
@@ -392,23 +401,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         ok = false;
                         break;
                     }
+                    const int y = wk.seq_off + j * TILE;
                     mbar_arrive_expect_tx(&k_full[ks], TILE_BYTES);
                     tma_load_2d(sK + ks * TILE_BYTES, &tk, &k_full[ks], x0, y);
                     tma_load_2d(sK + ks * TILE_BYTES + CHUNK_BYTES, &tk, &k_full[ks], x0 + 64, y);
                     k_issued[ks] = 1;
                     k_par[ks] = kp;
-                    const int vs = g % V_STAGES;
-                    const uint32_t vp = (uint32_t)(g / V_STAGES) & 1u;
-                    if (!mbar_wait(&v_empty[vs], vp ^ 1, abort_flag, args.status))
-                    {
-                        ok = false;
-                        break;
-                    }
-                    mbar_arrive_expect_tx(&v_full[vs], TILE_BYTES);
-                    tma_load_2d(sV + vs * TILE_BYTES, &tv, &v_full[vs], x0, y);
-                    tma_load_2d(sV + vs * TILE_BYTES + CHUNK_BYTES, &tv, &v_full[vs], x0 + 64, y);
-                    v_issued[vs] = 1;
-                    v_par[vs] = vp;
                 }
                 if (!ok) break;
             }
@@ -418,9 +416,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (q_out) drain_wait(q_full, q_par);
                 for (int s = 0; s < K_STAGES; s++)
                     if (k_issued[s]) drain_wait(&k_full[s], k_par[s]);
-                for (int s = 0; s < V_STAGES; s++)
-                    if (v_issued[s]) drain_wait(&v_full[s], v_par[s]);
             }
+        }
+        else if (lane == 1)
+        {
+            // ---------------- TMA producer: V tiles (one buffer; V(j) is needed
+            // only after the softmax of key tile j, so it reloads behind PV(j-1))
+            int g = 0;
+            bool issued = false;
+            uint32_t last = 0;
+            for (int w = blockIdx.x; w < args.num_work && !*abort_flag; w += gridDim.x)
+            {
+                const Work wk = decode_work(args, w);
+                const int x0 = wk.head * HD;
+                bool ok = true;
+                for (int j = 0; j < wk.nkv; j++, g++)
+                {
+                    const uint32_t vp = (uint32_t)g & 1u;
+                    if (!mbar_wait(v_empty, vp ^ 1, abort_flag, args.status))
+                    {
+                        ok = false;
+                        break;
+                    }
+                    const int y = wk.seq_off + j * TILE;
+                    mbar_arrive_expect_tx(v_full, TILE_BYTES);
+                    tma_load_2d(sV, &tv, v_full, x0, y);
+                    tma_load_2d(sV + CHUNK_BYTES, &tv, v_full, x0 + 64, y);
+                    issued = true;
+                    last = vp;
+                }
+                if (!ok) break;
+            }
+            if (*abort_flag && issued) drain_wait(v_full, last);
         }
     }
     else if (warp == 1)
@@ -430,103 +457,145 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // ---------------- MMA issuer
             bool any = false;
             bool ok = true;
-            int g = 0;
-            int it = 0;
-            uint32_t pcnt[2] = {0, 0};
-            // shared-memory matrix descriptors of the Q tiles and K / V stages
+            int gk = 0, gv = 0, it = 0;
+            uint32_t sfree[2] = {0, 0}, pfull[2] = {0, 0};
+            bool s_issued[2] = {false, false};
+            // shared-memory matrix descriptors; buffers are one tile (kTileDesc) apart
             const uint64_t q_desc0 = umma_desc_sw128(smem_u32(sQ), 16, 1024);
             const uint64_t k_desc0 = umma_desc_sw128(smem_u32(sK), 16, 1024);
             const uint64_t v_desc0 = umma_desc_sw128(smem_u32(sV), CHUNK_BYTES, 1024);
-            constexpr uint32_t kTileDesc = TILE_BYTES >> 4; // descriptor step of one tile buffer
+            const uint64_t p_desc0 = umma_desc_sw128(smem_u32(sP), 16, 1024);
+            constexpr uint32_t kTileDesc = TILE_BYTES >> 4;
             for (int w = blockIdx.x; w < args.num_work && ok; w += gridDim.x, it++)
             {
                 const Work wk = decode_work(args, w);
                 const int ntiles = wk.has_b ? 2 : 1;
-                // S_x = Q_x K^T for key tile j (ring slot gj); a ragged last
-                // tile runs with N = its keys rounded up to 16
-                auto issue_s = [&](int x, int gj, int j) {
+                // S_x = Q_x K^T for key tile j (ring slot of K tile gkk); a ragged
+                // last tile runs with N = its keys rounded up to 16.  Compile-time
+                // descriptor offsets keep the issue path MMAs only.
+                auto issue_s = [&](int x, int gkk, int j) {
                     const int valid = wk.S_len - j * TILE;
                     const int n = valid >= TILE ? TILE : ((valid + 15) & ~15);
                     const uint32_t idesc = umma_idesc_bf16(128, n, 0, 0);
                     const uint64_t qd = q_desc0 + (x ? kTileDesc : 0u);
-                    const uint64_t kd = k_desc0 + (uint32_t)(gj % K_STAGES) * kTileDesc;
+                    const uint64_t kd = k_desc0 + (uint32_t)(gkk % K_STAGES) * kTileDesc;
                     const uint32_t d = tmem + x * 128;
+                    umma_bf16_i<0>(d, qd, kd, idesc);
 #pragma unroll
-                    for (int k = 0; k < HD / 16; k++)
+                    for (int k = 1; k < HD / 16; k++)
                     {
-                        // start address field (bits 0-13, address >> 4) advanced by the K offset
                         const uint32_t off = ((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4;
-                        umma_bf16(d, qd + off, kd + off, idesc, k != 0);
+                        umma_bf16_i<1>(d, qd + off, kd + off, idesc);
                     }
                     umma_commit(&s_full[x]);
                 };
-                // O_x += P_x V over the tile's keys (16 per MMA; P is zero
-                // past the window's sequence)
-                auto issue_pv = [&](int x, int gj, int j) {
+                // O_x (+)= P_x V over the tile's keys (16 per MMA; P is zero past
+                // the window's sequence)
+                auto issue_pv = [&](int x, int j) {
                     const int valid = wk.S_len - j * TILE;
-                    const int ksteps = valid >= TILE ? TILE / 16 : (valid + 15) / 16;
-                    const uint64_t vd = v_desc0 + (uint32_t)(gj % V_STAGES) * kTileDesc;
-                    const uint32_t p_tmem = tmem + x * 128; // P packed bf16x2 over S columns [0,64)
+                    const uint64_t pd = p_desc0 + (x ? kTileDesc : 0u);
                     const uint32_t o_tmem = tmem + 256 + x * 128;
-                    for (int k = 0; k < ksteps; k++)
-                        umma_bf16_tmem_a(o_tmem, p_tmem + k * 8, vd + ((k * 16 * 128) >> 4), IDESC_O, (j | k) != 0);
+                    if (valid >= TILE)
+                    {
+                        if (j == 0)
+                            umma_bf16_i<0>(o_tmem, pd, v_desc0, IDESC_O);
+                        else
+                            umma_bf16_i<1>(o_tmem, pd, v_desc0, IDESC_O);
+#pragma unroll
+                        for (int k = 1; k < TILE / 16; k++)
+                        {
+                            const uint32_t aoff = ((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4;
+                            umma_bf16_i<1>(o_tmem, pd + aoff, v_desc0 + ((k * 16 * 128) >> 4), IDESC_O);
+                        }
+                    }
+                    else
+                    {
+                        const int ksteps = (valid + 15) / 16;
+                        for (int k = 0; k < ksteps; k++)
+                        {
+                            const uint32_t aoff = ((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4;
+                            umma_bf16(o_tmem, pd + aoff, v_desc0 + ((k * 16 * 128) >> 4), IDESC_O, (j | k) != 0);
+                        }
+                    }
+                    umma_commit(&p_empty[x]);
                 };
-                auto wait_k = [&](int gk) {
-                    return mbar_wait(&k_full[gk % K_STAGES], (uint32_t)(gk / K_STAGES) & 1u, abort_flag, args.status);
+                auto wait_k = [&](int g_) {
+                    return mbar_wait(&k_full[g_ % K_STAGES], (uint32_t)(g_ / K_STAGES) & 1u, abort_flag, args.status);
                 };
-                if (!mbar_wait(q_full, it & 1, abort_flag, args.status) || !wait_k(g))
+                // S_x(j) may overwrite S_x once the softmax has read the previous one
+                auto s_ready = [&](int x) {
+                    if (!s_issued[x]) return true;
+                    const bool r = mbar_wait(&s_free[x], sfree[x] & 1u, abort_flag, args.status);
+                    sfree[x]++;
+                    return r;
+                };
+                if (!mbar_wait(q_full, it & 1, abort_flag, args.status) || !wait_k(gk))
                 {
                     ok = false;
                     break;
                 }
-                tc_fence_after();
-                for (int x = 0; x < ntiles; x++) issue_s(x, g, 0);
-                umma_commit(&k_empty[g % K_STAGES]); // K(0) is free once S(., 0) is done
-                any = true;
-                if (wk.nkv == 1) umma_commit(q_empty);
-                // per key tile j: PV_A(j) S_A(j+1) PV_B(j) S_B(j+1); a K stage is
-                // released after its last S, a V stage after its last PV
-                for (int j = 0; j < wk.nkv && ok; j++)
+                for (int x = 0; x < ntiles && ok; x++)
                 {
-                    const int gj = g + j;
-                    const int vs = gj % V_STAGES;
-                    if (!mbar_wait(&v_full[vs], (uint32_t)(gj / V_STAGES) & 1u, abort_flag, args.status))
+                    if (!s_ready(x))
                     {
                         ok = false;
                         break;
                     }
-                    const bool more = j + 1 < wk.nkv;
-                    for (int x = 0; x < ntiles; x++)
+                    tc_fence_after();
+                    issue_s(x, gk, 0);
+                    s_issued[x] = true;
+                }
+                if (!ok) break;
+                umma_commit(&k_empty[gk % K_STAGES]);
+                gk++;
+                any = true;
+                if (wk.nkv == 1) umma_commit(q_empty);
+                for (int j = 0; j < wk.nkv && ok; j++)
+                {
+                    // next scores first: they only need the softmax to have read S(j)
+                    if (j + 1 < wk.nkv)
                     {
-                        if (!mbar_wait(&p_full[x], pcnt[x] & 1, abort_flag, args.status))
+                        if (!wait_k(gk))
                         {
                             ok = false;
                             break;
                         }
-                        pcnt[x]++;
-                        tc_fence_after();
-                        issue_pv(x, gj, j);
-                        if (!more) umma_commit(&o_done[x]);
-                        if (x == ntiles - 1) umma_commit(&v_empty[vs]);
-                        if (more)
+                        for (int x = 0; x < ntiles && ok; x++)
                         {
-                            if (x == 0)
+                            if (!s_ready(x))
                             {
-                                if (!wait_k(gj + 1))
-                                {
-                                    ok = false;
-                                    break;
-                                }
-                                tc_fence_after();
+                                ok = false;
+                                break;
                             }
-                            issue_s(x, gj + 1, j + 1);
-                            if (x == ntiles - 1) umma_commit(&k_empty[(gj + 1) % K_STAGES]);
+                            tc_fence_after();
+                            issue_s(x, gk, j + 1);
                         }
+                        if (!ok) break;
+                        umma_commit(&k_empty[gk % K_STAGES]);
+                        gk++;
+                        if (j + 2 == wk.nkv) umma_commit(q_empty); // the unit's last S MMA
                     }
-                    // the unit's last S MMA has been issued: Q may be replaced
-                    if (ok && j + 2 == wk.nkv) umma_commit(q_empty);
+                    if (!mbar_wait(v_full, (uint32_t)gv & 1u, abort_flag, args.status))
+                    {
+                        ok = false;
+                        break;
+                    }
+                    for (int x = 0; x < ntiles; x++)
+                    {
+                        if (!mbar_wait(&p_full[x], pfull[x] & 1u, abort_flag, args.status))
+                        {
+                            ok = false;
+                            break;
+                        }
+                        pfull[x]++;
+                        tc_fence_after();
+                        issue_pv(x, j);
+                        if (j + 1 == wk.nkv) umma_commit(&o_done[x]);
+                    }
+                    if (!ok) break;
+                    umma_commit(v_empty);
+                    gv++;
                 }
-                g += wk.nkv;
             }
             if (any)
             {
@@ -544,8 +613,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         const uint32_t s_addr = tmem + lane_base + x * 128;
         const uint32_t o_addr = tmem + lane_base + 256 + x * 128;
+        uint8_t* p_tile = sP + x * TILE_BYTES;
         const uint64_t c2 = pk2(__float_as_uint(args.scale_log2), __float_as_uint(args.scale_log2));
-        uint32_t scnt = 0, ocnt = 0;
+        uint32_t scnt = 0, pecnt = 0, ocnt = 0;
+        bool pv_before = false; // a PV_x has been issued (P_x / O_x may be in use)
         bool ok = true;
         for (int w = blockIdx.x; w < args.num_work && ok; w += gridDim.x)
         {
@@ -568,6 +639,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 uint32_t v[128];
                 tmem_ld128(s_addr, v);
                 tmem_ld_wait();
+                // S_x is in registers: the next S_x may be computed into TMEM
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_free[x]);
                 const float mx = full ? row_max<true>(v, valid) : row_max<false>(v, valid);
                 const float mt = mx * args.scale_log2;
                 float alpha = 1.f;
@@ -580,12 +655,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     m_used = mt;
                 }
                 const uint64_t negm2 = pk2(__float_as_uint(-m_used), __float_as_uint(-m_used));
-                const float rowsum = full ? row_exp<true>(v, valid, c2, negm2, s_addr)
-                                          : row_exp<false>(v, valid, c2, negm2, s_addr);
+                uint64_t sum2[4] = {0, 0, 0, 0};
+                uint32_t pk[32];
+                if (full)
+                    row_exp_half<true, 0>(v, valid, c2, negm2, pk, sum2);
+                else
+                    row_exp_half<false, 0>(v, valid, c2, negm2, pk, sum2);
+                // P_x and O_x are free once the previous PV_x has completed
+                if (pv_before)
+                {
+                    if (!warp_wait(&p_empty[x], pecnt & 1, abort_flag, args.status))
+                    {
+                        ok = false;
+                        break;
+                    }
+                    pecnt++;
+                    tc_fence_after();
+                }
+                store_p_half<0>(p_tile, row, pk);
+                if (full)
+                    row_exp_half<true, 1>(v, valid, c2, negm2, pk, sum2);
+                else
+                    row_exp_half<false, 1>(v, valid, c2, negm2, pk, sum2);
+                store_p_half<1>(p_tile, row, pk);
+                float rowsum;
+                {
+                    const uint64_t s2 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
+                    float lo, hi;
+                    upk2(s2, lo, hi);
+                    rowsum = lo + hi;
+                }
                 if (rescale)
                 {
-                    // O is stable here: S_X(j) was committed after PV_X(j-1),
-                    // and PV_X(j) waits for this thread's p_full arrival.
 #pragma unroll
                     for (int c = 0; c < 4; c++)
                     {
@@ -596,13 +697,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
                         tmem_st32(o_addr + c * 32, o);
                     }
+                    tmem_st_wait();
                     l_run *= alpha;
                 }
                 l_run += rowsum;
-                tmem_st_wait();
+                fence_proxy_async_smem(); // P is read by the tensor core (async proxy)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&p_full[x]);
+                pv_before = true;
             }
             if (!ok) break;
             if (!warp_wait(&o_done[x], ocnt & 1, abort_flag, args.status))
@@ -633,7 +736,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // rank passes its next cross-GPU barrier
             if (remote) __threadfence_system();
             // O has been read: the next unit's first PV may overwrite it
-            // (ordered by this warp's next p_full arrival)
+            // (ordered by this group's next p_full arrival)
             tc_fence_before();
         }
     }
