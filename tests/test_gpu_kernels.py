@@ -147,6 +147,10 @@ def test_awa_split_bf16_inputs(gpu_ctx, s2lib, golden):
     ([1, 64, 64], [1, 16, 16], 1, 2),     # config 2 shifted: 25 windows of 64..256 tokens
     ([2, 15, 20], [2, 15, 20], 0, 2),     # one 600-token window (720p window, 5 kv tiles + text)
     ([3, 7, 11], [2, 3, 4], 1, 3),        # odd extents, tiny shifted boundary windows
+    # BASELINE config 4 sweep of window lengths L (video tokens per window; + 58 text rows)
+    ([2, 16, 16], [1, 8, 8], 0, 2),       # L = 64: 8 windows of one query tile each
+    ([1, 32, 32], [1, 16, 16], 1, 2),     # L = 256 shifted: 9 windows of 64..256 tokens
+    ([1, 32, 64], [1, 32, 64], 0, 2),     # L = 2048: 17 key tiles, 9 query-tile pairs
 ])
 def test_awa_vs_oracle_explicit_windows(gpu_ctx, s2lib, port, shape, window, shifted, heads):
     from oracle import oracle
