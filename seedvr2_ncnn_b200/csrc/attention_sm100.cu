@@ -120,14 +120,14 @@ __device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x)
     return y;
 }
 
-// Row max of the 128 raw scores of one key tile (FULL: no masked columns);
-// four independent 3-input max chains keep the dependency depth at 16.
-template <bool FULL>
-__device__ __forceinline__ float row_max(const uint32_t (&v)[128], int valid)
+// Row max over NV raw scores (FULL: no masked columns; otherwise columns
+// >= valid are ignored); four independent 3-input max chains.
+template <bool FULL, int NV>
+__device__ __forceinline__ float row_max(const uint32_t (&v)[NV], int valid)
 {
     float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-    for (int i = 0; i < 128; i += 8)
+    for (int i = 0; i < NV; i += 8)
     {
 #pragma unroll
         for (int c = 0; c < 4; c++)
@@ -144,20 +144,20 @@ __device__ __forceinline__ float row_max(const uint32_t (&v)[128], int valid)
     return fmax3(m[0], m[1], fmaxf(m[2], m[3]));
 }
 
-// P = exp2(S * c - m) for half H (64 columns) of the row (masked columns ->
-// 0) as 32 packed bf16 pairs.  The exponent t = S * c - m is formed in fp32
+// P = exp2(S * c - m) for 64 columns of the row (columns >= valid -> 0) as
+// 32 packed bf16 pairs.  The exponent t = S * c - m is formed in fp32
 // (packed pairs), rounded to bf16 and exponentiated two at a time
 // (ex2.approx.ftz.bf16x2), so P leaves the MUFU already in its bf16 MMA
 // format; the row sum adds exactly those bf16 values in fp32 (packed partial
 // sums in sum2).
-template <bool FULL, int H>
-__device__ __forceinline__ void row_exp_half(const uint32_t (&v)[128], int valid, uint64_t c2, uint64_t negm2,
-                                             uint32_t (&p)[32], uint64_t (&sum2)[4])
+template <bool FULL>
+__device__ __forceinline__ void row_exp64(const uint32_t (&v)[64], int valid, uint64_t c2, uint64_t negm2,
+                                          uint32_t (&p)[32], uint64_t (&sum2)[4])
 {
 #pragma unroll
     for (int q = 0; q < 32; q++)
     {
-        const int i = 64 * H + 2 * q;
+        const int i = 2 * q;
         const uint64_t t2 = ffma2(pk2(v[i], v[i + 1]), c2, negm2);
         float t0, t1;
         upk2(t2, t0, t1);
@@ -636,14 +636,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tc_fence_after();
                 const int valid = wk.S_len - j * TILE; // >= 1
                 const bool full = valid >= TILE;
-                uint32_t v[128];
-                tmem_ld128(s_addr, v);
-                tmem_ld_wait();
-                // S_x is in registers: the next S_x may be computed into TMEM
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s_free[x]);
-                const float mx = full ? row_max<true>(v, valid) : row_max<false>(v, valid);
+                // Scores in two 64-column halves so only one half is live: the
+                // max reads the second half in 32-column pieces, the first
+                // half's exponentials run, then the second half is reloaded and
+                // S released (the next S_x is needed only at the next key tile).
+                uint32_t v[64];
+                tmem_ld64(s_addr, v);
+                float mo;
+                {
+                    uint32_t t[32];
+                    tmem_ld32(s_addr + 64, t);
+                    tmem_ld_wait();
+                    mo = full ? row_max<true, 32>(t, valid - 64) : row_max<false, 32>(t, valid - 64);
+                    tmem_ld32(s_addr + 96, t);
+                    tmem_ld_wait();
+                    mo = fmaxf(mo, full ? row_max<true, 32>(t, valid - 96) : row_max<false, 32>(t, valid - 96));
+                }
+                const float mx = fmaxf(mo, full ? row_max<true, 64>(v, valid) : row_max<false, 64>(v, valid));
                 const float mt = mx * args.scale_log2;
                 float alpha = 1.f;
                 const bool rescale = j > 0 && mt > m_used + RESCALE_THRESHOLD;
@@ -658,9 +667,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 uint64_t sum2[4] = {0, 0, 0, 0};
                 uint32_t pk[32];
                 if (full)
-                    row_exp_half<true, 0>(v, valid, c2, negm2, pk, sum2);
+                    row_exp64<true>(v, valid, c2, negm2, pk, sum2);
                 else
-                    row_exp_half<false, 0>(v, valid, c2, negm2, pk, sum2);
+                    row_exp64<false>(v, valid, c2, negm2, pk, sum2);
                 // P_x and O_x are free once the previous PV_x has completed
                 if (pv_before)
                 {
@@ -673,10 +682,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     tc_fence_after();
                 }
                 store_p_half<0>(p_tile, row, pk);
+                tmem_ld64(s_addr + 64, v);
+                tmem_ld_wait();
+                // S_x is in registers: the next S_x may be computed into TMEM
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_free[x]);
                 if (full)
-                    row_exp_half<true, 1>(v, valid, c2, negm2, pk, sum2);
+                    row_exp64<true>(v, valid - 64, c2, negm2, pk, sum2);
                 else
-                    row_exp_half<false, 1>(v, valid, c2, negm2, pk, sum2);
+                    row_exp64<false>(v, valid - 64, c2, negm2, pk, sum2);
                 store_p_half<1>(p_tile, row, pk);
                 float rowsum;
                 {

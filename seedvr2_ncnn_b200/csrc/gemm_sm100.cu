@@ -802,7 +802,6 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
             int acc = 0;
             uint32_t acc_phase = 0;
             bool any = false;
-            const uint64_t a_desc0 = umma_desc_sw128(smem_u32(smem), 16, 1024);
             for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x)
             {
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, args.status)) break;
@@ -817,15 +816,15 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                         break;
                     }
                     tc_fence_after();
-                    // descriptors: stage base + compile-time K-step offsets (32 B = 2 units)
-                    const uint64_t ad = a_desc0 + (uint32_t)stage * (STAGE_BYTES >> 4);
-                    const uint64_t bd = ad + (A_BYTES >> 4);
-                    if (kb == 0)
-                        umma_bf16_i<0>(d_tmem, ad, bd, IDESC);
-                    else
-                        umma_bf16_i<1>(d_tmem, ad, bd, IDESC);
+                    const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+                    const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
-                    for (int k = 1; k < BK / 16; k++) umma_bf16_i<1>(d_tmem, ad + 2 * k, bd + 2 * k, IDESC);
+                    for (int k = 0; k < BK / 16; k++)
+                    {
+                        const uint64_t ad = umma_desc_sw128(a_addr + k * 32, 16, 1024);
+                        const uint64_t bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
+                        umma_bf16(d_tmem, ad, bd, IDESC, (kb | k) != 0);
+                    }
                     umma_commit(&empty[stage]);
                     any = true;
                     if (++stage == STAGES)
@@ -1067,7 +1066,6 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
-            const uint64_t a_desc0 = umma_desc_sw128(smem_u32(smem), 16, 1024);
             for (int t = walk.first(); t < args.num_tiles && !*abort_flag; t += walk.step())
             {
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, args.status)) break;
@@ -1082,14 +1080,15 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t ad = a_desc0 + (uint32_t)stage * (STAGE_BYTES >> 4);
-                    const uint64_t bd = ad + (TL::A_STAGE >> 4);
-                    if (kb == 0)
-                        umma_bf16_pair_i<0>(d_tmem, ad, bd, TL::IDESC);
-                    else
-                        umma_bf16_pair_i<1>(d_tmem, ad, bd, TL::IDESC);
+                    const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+                    const uint32_t b_addr = a_addr + TL::A_STAGE;
 #pragma unroll
-                    for (int k = 1; k < BK / 16; k++) umma_bf16_pair_i<1>(d_tmem, ad + 2 * k, bd + 2 * k, TL::IDESC);
+                    for (int k = 0; k < BK / 16; k++)
+                    {
+                        const uint64_t ad = umma_desc_sw128(a_addr + k * 32, 16, 1024);
+                        const uint64_t bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
+                        umma_bf16_pair(d_tmem, ad, bd, TL::IDESC, (kb | k) != 0);
+                    }
                     umma_commit_pair(&empty[stage], 0x3);
                     if (++stage == STAGES)
                     {

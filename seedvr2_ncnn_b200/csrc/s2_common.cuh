@@ -288,14 +288,6 @@ __device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t a_desc,
         : "memory");
 }
 
-template <int ACC>
-__device__ __forceinline__ void umma_bf16_pair_i(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t idesc)
-{
-    asm volatile("tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, %4;" ::"r"(tmem_d), "l"(a_desc), "l"(b_desc),
-                 "r"(idesc), "n"(ACC)
-                 : "memory");
-}
-
 // Arrive on the mbarrier at this offset in every CTA of `mask` once all prior
 // tcgen05 ops of this thread complete.
 __device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t mask)
