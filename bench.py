@@ -210,6 +210,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer pass (profiling runs)")
     ap.add_argument("--blocks", type=int, default=BLOCKS, help="fewer blocks for small profiling captures only")
+    ap.add_argument("--no-dit-step", action="store_true", help="skip the whole-DiT pass (frontend, blocks, tail)")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -337,6 +338,8 @@ def main():
     ms_instr, _, counters = timed(True)
     clk = clocks.stop()
     value = M / (ms / 1000.0)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
 
     # end to end with host buffers (pinned): H2D of this rank's rows and the
     # modulation, the forward, D2H of the result -- inside the timed region
@@ -375,6 +378,55 @@ def main():
             t = torch.tensor([e2e_ms], device="cuda")
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             e2e_ms = float(t.item())
+    # The whole DiT (SeedVR2DiTBlocks::forward(DiTInputs)): 1x2x2-patchified
+    # latents of the same video (33 channels) + 58 text embeddings (5120) +
+    # one timestep -> frontend, the blocks, tail -> prediction (16 channels),
+    # on device buffers, then through the host-buffer entry point.
+    dit_step = None
+    if not sharded and not args.no_dit_step:
+        lat = [shape[0], 2 * shape[1], 2 * shape[2]]
+        ntok = lat[0] * lat[1] * lat[2]
+        gl = torch.Generator(device="cuda").manual_seed(7)
+        lv = torch.randn(ntok, abi.S2_LATENT_CHANNELS, device="cuda", generator=gl)
+        lt = torch.randn(TEXT, abi.S2_TEXT_CHANNELS, device="cuda", generator=gl)
+        pred = torch.empty(ntok, abi.S2_PRED_CHANNELS, device="cuda")
+        tout = torch.empty(TEXT, D, device="cuda")
+
+        def full_step():
+            dit.forward_step([lat], [TEXT], [500.0], lv, lt, pred, tout)
+
+        for _ in range(args.warmup):
+            full_step()
+        barrier()
+        launches0 = ctx.launches()
+        e0.record(stream)
+        for _ in range(args.steps):
+            full_step()
+        e1.record(stream)
+        barrier()
+        st_ms = e0.elapsed_time(e1) / args.steps
+        st_launches = ctx.launches() - launches0
+        hlv, hlt = lv.cpu().pin_memory(), lt.cpu().pin_memory()
+        hpred, htout = torch.empty_like(pred, device="cpu").pin_memory(), torch.empty_like(tout, device="cpu").pin_memory()
+        dit.forward_step_host([lat], [TEXT], [500.0], hlv, hlt, hpred, htout)
+        barrier()
+        st_e2e_steps = max(1, min(args.steps, 5))
+        e0.record(stream)
+        for _ in range(st_e2e_steps):
+            dit.forward_step_host([lat], [TEXT], [500.0], hlv, hlt, hpred, htout)
+        e1.record(stream)
+        barrier()
+        st_e2e_ms = e0.elapsed_time(e1) / st_e2e_steps
+        dit_step = {"value": M / (st_ms / 1000.0), "unit": "tokens/s", "ms_per_step": st_ms,
+                    "frontend_tail_ms_per_step": st_ms - ms, "gpu_launches": st_launches,
+                    "workload": f"latents {lat[0]}x{lat[1]}x{lat[2]}x33 + {TEXT}x5120 text + 1 timestep -> "
+                                f"prediction {lat[0]}x{lat[1]}x{lat[2]}x16 (frontend, {args.blocks} blocks, tail)",
+                    "entry_point": "s2_dit_forward_step",
+                    "e2e": {"value": M / (st_e2e_ms / 1000.0), "unit": "tokens/s", "ms_per_step": st_e2e_ms,
+                            "h2d_bytes_per_step": int(ntok * 33 * 4 + TEXT * 5120 * 4),
+                            "d2h_bytes_per_step": int(ntok * 16 * 4 + TEXT * D * 4),
+                            "entry_point": "s2_dit_forward_step_host"}}
+        del lv, lt, pred, tout, hlv, hlt, hpred, htout
     status = ctx.status()
 
     peaks = load_peaks()
@@ -442,6 +494,7 @@ def main():
                 "d2h_bytes_per_step": int((n_local + TEXT) * D * 4), "ms_per_step": None if args.no_e2e else e2e_ms,
                 "entry_point": "s2_dit_forward_sharded + pinned H2D/D2H" if sharded else "s2_dit_forward_host"},
         "gpu_launches": launches,
+        "dit_step": dit_step,
         "clocks": clk,
         "device_status": status,
     }

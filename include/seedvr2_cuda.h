@@ -237,16 +237,102 @@ int s2_dit_forward_host(s2_dit* dit, const int* video_shapes, const int* text_le
                         float* text_out);
 
 /* ---------------------------------------------------------------------------
- * Multi-GPU (one process per GPU, NCCL over NVLink).  The reference has no
+ * Token formats and the frontend / tail nets around the block stack
+ * (seedvr2_dit.cpp).  Widths fixed by the reference: 33 latent channels per
+ * token, 1x2x2 patches (132 features in, 64 = 4 x 16 prediction features
+ * out), 5120 text-embedding channels, a 256-wide sinusoidal timestep
+ * embedding.  shapes: latent (t, h, w) per sample, h and w even. */
+#define S2_LATENT_CHANNELS 33
+#define S2_PATCH_FEATURES 132
+#define S2_PRED_CHANNELS 16
+#define S2_PRED_FEATURES 64
+#define S2_TEXT_CHANNELS 5120
+#define S2_TIME_FEATURES 256
+
+/* patchify_video (seedvr2_dit.cpp:167-230): video fp32 [rows][33] (samples
+ * concatenated, rows = sum t*h*w) -> out fp32 [sum t*(h/2)*(w/2)][132];
+ * feature (y*2 + x)*33 + c of patch (f, py, px) = channel c of token
+ * (f, 2py + y, 2px + x).  -1 on an odd h/w, a non-positive extent or a row
+ * count that does not match the shapes. */
+int s2_patchify_video(s2_context* ctx, const float* video, int rows, const int* shapes, int batch, float* out);
+/* unpatchify_prediction (seedvr2_dit.cpp:255-326): pred fp32 [patches][64]
+ * -> out fp32 [tokens][16], the inverse ordering (16-byte aligned buffers). */
+int s2_unpatchify_prediction(s2_context* ctx, const float* pred, int rows, const int* shapes, int batch,
+                             float* out);
+/* make_timestep_embedding (seedvr2_dit.cpp:232-253): host timesteps[batch]
+ * -> out fp32 [batch][256] = sin(t f_i) | cos(t f_i), f_i = exp(-ln(1e4) i/128). */
+int s2_timestep_embedding(s2_context* ctx, const float* timesteps, int batch, float* out);
+
+/* Host fp32 weights of the frontend and tail nets (frontend.ncnn /
+ * tail.ncnn of SeedVR2DiTBlocks, seedvr2_dit.cpp:1183-1295, :1424-1494;
+ * the exported graphs are not in the reference tree, so this op sequence is
+ * the B200 build's assumption, restated by the CPU oracle):
+ *   video  = patches W_vid_in^T + b_vid_in                       [Np][D]
+ *   text   = text W_txt_in^T + b_txt_in                          [T][D]
+ *   e      = silu(temb W_emb0^T + b0); e = silu(e W_emb1^T + b1)
+ *   mod    = e W_emb2^T + b2 = six [D] chunks (out2..out7)       [6][D]
+ *   tail:  h = rmsnorm(video) * (mod[1] + tail_ada[1]) + (mod[0] + tail_ada[0])
+ *          pred = h W_out^T + b_out                              [Np][64]
+ * Shapes: w_vid_in [D][132], w_txt_in [D][5120], w_emb0 [D][256],
+ * w_emb1 [D][D], w_emb2 [6D][D], tail_ada [2][D], w_out [64][D]; biases
+ * [rows of W] or NULL. */
+typedef struct
+{
+    const float* w_vid_in;
+    const float* b_vid_in;
+    const float* w_txt_in;
+    const float* b_txt_in;
+    const float* w_emb0;
+    const float* b_emb0;
+    const float* w_emb1;
+    const float* b_emb1;
+    const float* w_emb2;
+    const float* b_emb2;
+    const float* tail_ada;
+    const float* w_out;
+    const float* b_out;
+} s2_dit_io_host_weights;
+
+/* Uploads the frontend / tail weights (bf16 on the device).  s2_dit_init_random
+ * also fills them (weights ~N(0,0.02), tail offsets like the blocks'). */
+int s2_dit_set_io_weights(s2_dit* dit, const s2_dit_io_host_weights* w);
+
+/* forward_frontend (seedvr2_dit.cpp:1183-1295): DiTInputs -> DiTBlockInputs.
+ * video fp32 [video_rows][33], text fp32 [text_rows][5120], host timesteps
+ * [batch]; video_out fp32 [patches][D], text_out fp32 [text_rows][D],
+ * modulation fp32 [6][batch][D].  Validation of split_dit_inputs_by_sample
+ * (:369-427) and patchify_video; -1 before the weights are set. */
+int s2_dit_forward_frontend(s2_dit* dit, const int* video_shapes, const int* text_lengths, const float* timesteps,
+                            int batch, const float* video, int video_rows, const float* text, int text_rows,
+                            float* video_out, float* text_out, float* modulation);
+/* The tail net + unpatchify_prediction: video fp32 [patches][D] (block
+ * output), modulation fp32 [6][batch][D] -> prediction fp32 [tokens][16]. */
+int s2_dit_forward_tail(s2_dit* dit, const int* video_shapes, int batch, const float* video, int video_rows,
+                        const float* modulation, float* prediction);
+/* The whole DiT (SeedVR2DiTBlocks::forward(DiTInputs), seedvr2_dit.cpp:1297-1536):
+ * frontend, all blocks, tail, per sample like the reference; prediction fp32
+ * [video_rows][16], text_out fp32 [text_rows][D] (block stack's text rows). */
+int s2_dit_forward_step(s2_dit* dit, const int* video_shapes, const int* text_lengths, const float* timesteps,
+                        int batch, const float* video, int video_rows, const float* text, int text_rows,
+                        float* prediction, float* text_out);
+/* Same, host buffers in and out (synchronises). */
+int s2_dit_forward_step_host(s2_dit* dit, const int* video_shapes, const int* text_lengths, const float* timesteps,
+                             int batch, const float* video, int video_rows, const float* text, int text_rows,
+                             float* prediction, float* text_out);
+
+/* ---------------------------------------------------------------------------
+ * Multi-GPU (one process per GPU over NVLink).  The reference has no
  * distributed path (seedvr2_main.cpp:89-100 forces --sp-size 1); this is the
  * window sharding of the B200 build.
  *
- * Ownership of one sample over `world` ranks: rank r owns an equal contiguous
- * range of the UNSHIFTED plan's token order (window after window); text
- * tokens are replicated.  Each window of a block (unshifted in even blocks,
- * shifted in odd blocks) belongs to the rank holding most of its tokens; the
- * raw qkv rows of its foreign tokens move to that rank and their context
- * rows back (grouped NCCL send/recv); the text pool is an NCCL all-reduce.
+ * Ownership of one sample over `world` ranks: rank r owns a token-balanced
+ * contiguous range of the UNSHIFTED plan's token order (window after window);
+ * text tokens are replicated.  Each window of a block (unshifted in even
+ * blocks, shifted in odd blocks) belongs to the rank holding most of its
+ * tokens; the QKV projection stores the packed q/k/v rows of foreign tokens
+ * straight into the owner's buffer and attention stores their context rows
+ * back (NVLink peer memory); every rank sums the text-pool partials of all
+ * peers.  NCCL only exchanges the ids and memory handles at setup.
  * s2_shard_* expose the plan (host only, no GPU needed): local_tokens
  * [n_local] global token ids in local row order; for window plan `shifted`
  * (0/1), send_tokens / recv_tokens concatenated over peer ranks in rank order

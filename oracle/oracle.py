@@ -9,6 +9,9 @@ baseline; the shipped package never imports it.
 * :class:`Ref` wraps ``oracle/_ref/libs2_ref.so`` -- the reference's OWN
   ``adaptive_window_attention.cpp`` / ``shared_linear.cpp`` compiled against
   the clean-room ncnn API shim (built only where the reference tree exists).
+* :class:`RefIO` wraps ``oracle/_ref/libs2_ref_dit_io.so`` -- the reference's
+  own ``patchify_video`` / ``make_timestep_embedding`` /
+  ``unpatchify_prediction`` (``src/seedvr2/seedvr2_dit.cpp:167-326``).
 """
 from __future__ import annotations
 
@@ -21,6 +24,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_SO = os.path.join(HERE, "libs2_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libs2_ref.so")
+REF_IO_SO = os.path.join(HERE, "_ref", "libs2_ref_dit_io.so")
 
 WINDOW_TARGET = 0
 WINDOW_EXTENT = 1
@@ -82,6 +86,9 @@ class Port:
         lib.s2o_linear.argtypes = [_f32p, C.c_int, C.c_int, _f32p, C.c_void_p, C.c_int, _f32p]
         lib.s2o_block_forward.argtypes = [_i32p, C.c_float, C.c_float, C.c_void_p, _f32p, _i32p, _i32p, C.c_int,
                                           _f32p, _f32p, C.c_int]
+        lib.s2o_patchify_video.argtypes = [C.c_void_p, C.c_int, _i32p, C.c_int, C.c_void_p]
+        lib.s2o_unpatchify_prediction.argtypes = [C.c_void_p, C.c_int, _i32p, C.c_int, C.c_void_p]
+        lib.s2o_timestep_embedding.argtypes = [_f32p, C.c_int, _f32p]
         self.lib = lib
 
     def plan(self, shapes, window, shifted, mode=WINDOW_TARGET) -> Plan:
@@ -168,6 +175,138 @@ class Port:
         if r != 0:
             raise ValueError(f"s2o_block_forward returned {r}")
         return xv, xt
+
+
+    # ---- token formats and the frontend / tail nets (seedvr2_dit.cpp) ----
+    def patchify_video(self, video, shapes, rows=None):
+        """[tokens, 33] -> [patches, 132]; raises ValueError(code) like the reference's return code."""
+        video = _f32(video)
+        shapes = _i32(shapes).reshape(-1, 3)
+        rows = video.shape[0] if rows is None else rows
+        patches = int(sum(max(t, 0) * (max(h, 0) // 2) * (max(w, 0) // 2) for t, h, w in shapes.tolist()))
+        out = np.zeros((max(patches, 1), 132), np.float32)
+        r = self.lib.s2o_patchify_video(video.ctypes.data, rows, shapes, len(shapes), out.ctypes.data)
+        if r != 0:
+            raise ValueError(r)
+        return out[:patches]
+
+    def unpatchify_prediction(self, pred, shapes, rows=None):
+        """[patches, 64] -> [tokens, 16] (latent shapes)."""
+        pred = _f32(pred)
+        shapes = _i32(shapes).reshape(-1, 3)
+        rows = pred.shape[0] if rows is None else rows
+        tokens = int(sum(max(t, 0) * max(h, 0) * max(w, 0) for t, h, w in shapes.tolist()))
+        out = np.zeros((max(tokens, 1), 16), np.float32)
+        r = self.lib.s2o_unpatchify_prediction(pred.ctypes.data, rows, shapes, len(shapes), out.ctypes.data)
+        if r != 0:
+            raise ValueError(r)
+        return out[:tokens]
+
+    def timestep_embedding(self, timesteps):
+        t = _f32(timesteps)
+        out = np.zeros((len(t), 256), np.float32)
+        r = self.lib.s2o_timestep_embedding(t, len(t), out)
+        if r != 0:
+            raise ValueError(r)
+        return out
+
+    def frontend_forward(self, io: dict, shapes, timesteps, video, text, emulate_bf16=False):
+        """The frontend net (in0..in2 -> out0..out7 of forward_frontend, seedvr2_dit.cpp:1183-1295) as this
+        build restates it (the exported graph is not in the reference tree):
+          video = patchify(latents) W_vid_in^T + b;  text = text W_txt_in^T + b
+          e = silu(temb W_emb0^T + b0); e = silu(e W_emb1^T + b1); modulation = e W_emb2^T + b2 -> [6][batch][D]
+        emulate_bf16 rounds the GEMM activations the device path stores in bf16 (patches, text)."""
+        rnd = self.round_bf16 if emulate_bf16 else _f32
+        p = self.patchify_video(video, shapes)
+        v = rnd(p) @ _f32(io["w_vid_in"]).T + _bias(io.get("b_vid_in"))
+        t = rnd(text) @ _f32(io["w_txt_in"]).T + _bias(io.get("b_txt_in"))
+        temb = self.timestep_embedding(timesteps).astype(np.float64)
+        e = _silu(temb @ _f64(io["w_emb0"]).T + _bias(io.get("b_emb0")))
+        e = _silu(e @ _f64(io["w_emb1"]).T + _bias(io.get("b_emb1")))
+        emb = e @ _f64(io["w_emb2"]).T + _bias(io.get("b_emb2"))
+        B = len(timesteps)
+        D = emb.shape[1] // 6
+        mod = emb.reshape(B, 6, D).transpose(1, 0, 2)
+        return _f32(v), _f32(t), _f32(mod)
+
+    def tail_forward(self, io: dict, shapes, video, modulation, eps=1e-5, emulate_bf16=False):
+        """The tail net + unpatchify: per sample h = rmsnorm(x) * (mod[1] + tail_ada[1]) + (mod[0] + tail_ada[0]),
+        prediction patches = h W_out^T + b_out [patches][64] -> tokens [tokens][16]."""
+        rnd = self.round_bf16 if emulate_bf16 else _f32
+        video = _f32(video)
+        mod = _f32(modulation)
+        ada = _f32(io["tail_ada"])
+        out = []
+        off = 0
+        for s, (t, h, w) in enumerate(_i32(shapes).reshape(-1, 3).tolist()):
+            n = t * (h // 2) * (w // 2)
+            x = video[off:off + n]
+            off += n
+            ss = np.concatenate([np.square(x[i:i + 4096], dtype=np.float64).mean(axis=1)
+                                 for i in range(0, len(x), 4096)])[:, None]
+            inv = (1.0 / np.sqrt(ss.astype(np.float32) + np.float32(eps))).astype(np.float32)
+            hh = x * inv * (mod[1, s] + ada[1]) + (mod[0, s] + ada[0])
+            pp = rnd(hh) @ _f32(io["w_out"]).T + _bias(io.get("b_out"))
+            out.append(self.unpatchify_prediction(_f32(pp), [[t, h, w]]))
+        return np.concatenate(out)
+
+
+def _f64(a) -> np.ndarray:
+    return np.asarray(a, dtype=np.float64)
+
+
+def _bias(b):
+    return 0.0 if b is None else np.asarray(b, dtype=np.float64)
+
+
+def _silu(x):
+    return x / (1.0 + np.exp(-x))
+
+
+class RefIO:
+    """The reference's own patchify_video / make_timestep_embedding / unpatchify_prediction
+    (oracle/_ref/libs2_ref_dit_io.so; seedvr2_dit.cpp:167-326 compiled unmodified)."""
+
+    def __init__(self, path: str = REF_IO_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        lib = C.CDLL(path)
+        lib.s2ref_patchify_video.argtypes = [C.c_void_p, C.c_int, _i32p, C.c_int, C.c_void_p, C.c_void_p]
+        lib.s2ref_unpatchify_prediction.argtypes = [C.c_void_p, C.c_int, _i32p, C.c_int, C.c_void_p]
+        lib.s2ref_timestep_embedding.argtypes = [_f32p, C.c_int, C.c_void_p]
+        self.lib = lib
+
+    def patchify_video(self, video, shapes, rows=None):
+        video = _f32(video)
+        shapes = _i32(shapes).reshape(-1, 3)
+        rows = video.shape[0] if rows is None else rows
+        patches = int(sum(max(t, 0) * (max(h, 0) // 2) * (max(w, 0) // 2) for t, h, w in shapes.tolist()))
+        out = np.zeros((max(patches, 1), 132), np.float32)
+        oshapes = np.zeros((max(len(shapes), 1), 3), np.int32)
+        r = self.lib.s2ref_patchify_video(video.ctypes.data, rows, shapes, len(shapes), out.ctypes.data,
+                                          oshapes.ctypes.data)
+        if r != 0:
+            raise ValueError(r)
+        return out[:patches]
+
+    def unpatchify_prediction(self, pred, shapes, rows=None):
+        pred = _f32(pred)
+        shapes = _i32(shapes).reshape(-1, 3)
+        rows = pred.shape[0] if rows is None else rows
+        tokens = int(sum(max(t, 0) * max(h, 0) * max(w, 0) for t, h, w in shapes.tolist()))
+        out = np.zeros((max(tokens, 1), 16), np.float32)
+        r = self.lib.s2ref_unpatchify_prediction(pred.ctypes.data, rows, shapes, len(shapes), out.ctypes.data)
+        if r != 0:
+            raise ValueError(r)
+        return out[:tokens]
+
+    def timestep_embedding(self, timesteps):
+        t = _f32(timesteps)
+        out = np.zeros((max(len(t), 1), 256), np.float32)
+        r = self.lib.s2ref_timestep_embedding(t if len(t) else np.zeros(1, np.float32), len(t), out.ctypes.data)
+        if r != 0:
+            raise ValueError(r)
+        return out[:len(t)]
 
 
 class Ref:

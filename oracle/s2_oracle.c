@@ -523,3 +523,118 @@ done:
     free(row_sample);
     return ret;
 }
+
+/* ---------------------------------------------------------------------------
+ * Token formats on either side of the block stack (src/seedvr2/seedvr2_dit.cpp).
+ * Latent tokens are rows of 33 channels in (frame, y, x) order per sample,
+ * samples concatenated; a 1x2x2 patch is a row of 132 = 4 * 33 features, the
+ * prediction patch a row of 64 = 4 * 16. */
+
+/* Row counts of a batch of latent shapes under patchify_video's checks
+ * (seedvr2_dit.cpp:178-189): -1 for a non-positive extent or an odd
+ * height/width. */
+int s2o_patch_rows(const int* shapes, int batch, long* tokens, long* patches)
+{
+    long nt = 0, np = 0;
+    if (batch < 0) return -1;
+    for (int s = 0; s < batch; s++)
+    {
+        const int t = shapes[3 * s], h = shapes[3 * s + 1], w = shapes[3 * s + 2];
+        if (t <= 0 || h <= 0 || w <= 0 || h % 2 != 0 || w % 2 != 0) return -1;
+        nt += (long)t * h * w;
+        np += (long)t * (h / 2) * (w / 2);
+    }
+    *tokens = nt;
+    *patches = np;
+    return 0;
+}
+
+/* patchify_video (seedvr2_dit.cpp:167-230): feature (y*2 + x)*33 + c of patch
+ * (frame, py, px) is channel c of token (frame, 2*py + y, 2*px + x), patches
+ * in (frame, py, px) order per sample.  -1: bad shape or rows != tokens;
+ * -100: empty output (the reference's failed Mat::create of zero rows). */
+int s2o_patchify_video(const float* src, int rows, const int* shapes, int batch, float* dst)
+{
+    long nt, np;
+    if (s2o_patch_rows(shapes, batch, &nt, &np) != 0 || nt != rows) return -1;
+    if (np == 0) return -100;
+    long in_off = 0, out_off = 0;
+    for (int s = 0; s < batch; s++)
+    {
+        const int T = shapes[3 * s], H = shapes[3 * s + 1], W = shapes[3 * s + 2];
+        for (int f = 0; f < T; f++)
+            for (int py = 0; py < H / 2; py++)
+                for (int px = 0; px < W / 2; px++)
+                {
+                    float* o = dst + (out_off++) * 132;
+                    for (int y = 0; y < 2; y++)
+                        for (int x = 0; x < 2; x++)
+                        {
+                            const long tok = in_off + ((long)f * H + 2 * py + y) * W + 2 * px + x;
+                            memcpy(o + (y * 2 + x) * 33, src + tok * 33, 33 * sizeof(float));
+                        }
+                }
+        in_off += (long)T * H * W;
+    }
+    return 0;
+}
+
+/* unpatchify_prediction (seedvr2_dit.cpp:255-326): channel c of token
+ * (frame, 2*py + y, 2*px + x) = feature (y*2 + x)*16 + c of patch (frame, py, px).
+ * shapes are the latent (unpatchified) shapes.  Its checks (:261-281) only ask
+ * for even h/w (patch shape * 2 == latent shape) and matching rows, so a
+ * zero-extent sample is accepted and adds no rows; negative extents are
+ * rejected here (-1).  -100: empty output. */
+int s2o_unpatchify_prediction(const float* src, int rows, const int* shapes, int batch, float* dst)
+{
+    long nt = 0, np = 0;
+    if (batch < 0) return -1;
+    for (int s = 0; s < batch; s++)
+    {
+        const int t = shapes[3 * s], h = shapes[3 * s + 1], w = shapes[3 * s + 2];
+        if (t < 0 || h < 0 || w < 0 || h % 2 != 0 || w % 2 != 0) return -1;
+        nt += (long)t * h * w;
+        np += (long)t * (h / 2) * (w / 2);
+    }
+    if (np != rows) return -1;
+    if (nt == 0) return -100;
+    long p_off = 0, out_off = 0;
+    for (int s = 0; s < batch; s++)
+    {
+        const int T = shapes[3 * s], H = shapes[3 * s + 1], W = shapes[3 * s + 2];
+        const int ph = H / 2, pw = W / 2;
+        for (int f = 0; f < T; f++)
+            for (int py = 0; py < ph; py++)
+                for (int px = 0; px < pw; px++)
+                {
+                    const float* in = src + (p_off + ((long)f * ph + py) * pw + px) * 64;
+                    for (int y = 0; y < 2; y++)
+                        for (int x = 0; x < 2; x++)
+                        {
+                            const long tok = out_off + ((long)f * H + 2 * py + y) * W + 2 * px + x;
+                            memcpy(dst + tok * 16, in + (y * 2 + x) * 16, 16 * sizeof(float));
+                        }
+                }
+        p_off += (long)T * ph * pw;
+        out_off += (long)T * H * W;
+    }
+    return 0;
+}
+
+/* make_timestep_embedding (seedvr2_dit.cpp:232-253): out[s][i] = sin(t_s * f_i),
+ * out[s][128 + i] = cos(t_s * f_i), f_i = exp(-log(10000) * i / 128), all in
+ * fp32 with the reference's operation order. */
+int s2o_timestep_embedding(const float* timesteps, int batch, float* out)
+{
+    if (batch <= 0) return -1;
+    const int half = 128;
+    for (int s = 0; s < batch; s++)
+        for (int i = 0; i < half; i++)
+        {
+            const float exponent = -logf(10000.f) * (float)i / (float)half;
+            const float phase = timesteps[s] * expf(exponent);
+            out[(size_t)s * 2 * half + i] = sinf(phase);
+            out[(size_t)s * 2 * half + i + half] = cosf(phase);
+        }
+    return 0;
+}

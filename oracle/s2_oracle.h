@@ -72,6 +72,16 @@ int s2o_block_forward(const int* dims, float eps_norm, float eps_qk, const s2o_b
                       const float* modulation /* [6][D] */, const int* shapes, const int* text_lengths,
                       int batch, float* x_video, float* x_text, int emulate_bf16);
 
+/* Token formats around the block stack (src/seedvr2/seedvr2_dit.cpp).
+ * shapes: latent (t, h, w) per sample.  Return 0 or -1 (bad shape / rows). */
+int s2o_patch_rows(const int* shapes, int batch, long* tokens, long* patches);
+/* [tokens][33] -> [patches][132] (patchify_video, :167-230) */
+int s2o_patchify_video(const float* src, int rows, const int* shapes, int batch, float* dst);
+/* [patches][64] -> [tokens][16] (unpatchify_prediction, :255-326) */
+int s2o_unpatchify_prediction(const float* src, int rows, const int* shapes, int batch, float* dst);
+/* [batch][256] sinusoidal embedding (make_timestep_embedding, :232-253) */
+int s2o_timestep_embedding(const float* timesteps, int batch, float* out);
+
 #ifdef __cplusplus
 }
 #endif

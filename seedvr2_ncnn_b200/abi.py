@@ -51,7 +51,17 @@ EXPORTED = [
     "s2_dit_create", "s2_dit_free", "s2_dit_set_block_weights", "s2_dit_init_random", "s2_dit_forward",
     "s2_dit_forward_host", "s2_shard_build", "s2_shard_counts", "s2_shard_lists", "s2_shard_free",
     "s2_dist_unique_id", "s2_dist_init", "s2_dist_sync", "s2_dist_destroy", "s2_dit_forward_sharded",
+    "s2_patchify_video", "s2_unpatchify_prediction", "s2_timestep_embedding", "s2_dit_set_io_weights",
+    "s2_dit_forward_frontend", "s2_dit_forward_tail", "s2_dit_forward_step", "s2_dit_forward_step_host",
 ]
+
+# Widths fixed by the reference's DiT input/output formats.
+S2_LATENT_CHANNELS = 33
+S2_PATCH_FEATURES = 132
+S2_PRED_CHANNELS = 16
+S2_PRED_FEATURES = 64
+S2_TEXT_CHANNELS = 5120
+S2_TIME_FEATURES = 256
 
 
 class S2Error(RuntimeError):
@@ -80,6 +90,11 @@ class DitConfig(C.Structure):
 class BlockHostWeights(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in ("ada", "w_qkv", "b_qkv", "w_out", "b_out", "w_up", "b_up", "w_down",
                                           "b_down", "qk_norm", "rope_freqs")]
+
+
+class IoHostWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("w_vid_in", "b_vid_in", "w_txt_in", "b_txt_in", "w_emb0", "b_emb0",
+                                          "w_emb1", "b_emb1", "w_emb2", "b_emb2", "tail_ada", "w_out", "b_out")]
 
 
 _lib = None
@@ -138,6 +153,14 @@ def lib() -> C.CDLL:
     L.s2_dist_sync.argtypes = [vp]
     L.s2_dist_destroy.argtypes = [vp]
     L.s2_dit_forward_sharded.argtypes = [vp, pint, ip, vp, vp]
+    L.s2_patchify_video.argtypes = [vp, vp, ip, pint, ip, vp]
+    L.s2_unpatchify_prediction.argtypes = [vp, vp, ip, pint, ip, vp]
+    L.s2_timestep_embedding.argtypes = [vp, C.POINTER(C.c_float), ip, vp]
+    L.s2_dit_set_io_weights.argtypes = [vp, C.POINTER(IoHostWeights)]
+    L.s2_dit_forward_frontend.argtypes = [vp, pint, pint, C.POINTER(C.c_float), ip, vp, ip, vp, ip, vp, vp, vp]
+    L.s2_dit_forward_tail.argtypes = [vp, pint, ip, vp, ip, vp, vp]
+    L.s2_dit_forward_step.argtypes = [vp, pint, pint, C.POINTER(C.c_float), ip, vp, ip, vp, ip, vp, vp]
+    L.s2_dit_forward_step_host.argtypes = [vp, pint, pint, C.POINTER(C.c_float), ip, vp, ip, vp, ip, vp, vp]
     _lib = L
     return L
 
@@ -319,8 +342,60 @@ def ada_rmsnorm(ctx: Context, x, eps, shift, scale, out=None):
     return out
 
 
+def _floats(values) -> C.Array:
+    values = [float(v) for v in values]
+    return (C.c_float * len(values))(*values)
+
+
+def _flat_shapes(shapes):
+    return [int(v) for s in shapes for v in s]
+
+
+def patch_rows(shapes) -> tuple[int, int]:
+    """(latent tokens, 1x2x2 patches) of a batch of latent shapes."""
+    tokens = sum(int(t) * int(h) * int(w) for t, h, w in shapes)
+    patches = sum(int(t) * (int(h) // 2) * (int(w) // 2) for t, h, w in shapes)
+    return tokens, patches
+
+
+def patchify_video(ctx: Context, video, shapes, rows=None, out=None):
+    """patchify_video: fp32 CUDA [tokens, 33] -> [patches, 132]."""
+    import torch
+
+    rows = video.shape[0] if rows is None else rows
+    if out is None:
+        out = torch.empty((max(patch_rows(shapes)[1], 1), S2_PATCH_FEATURES), dtype=torch.float32,
+                          device=video.device)
+    check(lib().s2_patchify_video(ctx.handle, video.data_ptr(), int(rows), _ints(_flat_shapes(shapes)), len(shapes),
+                                  out.data_ptr()), "s2_patchify_video")
+    return out
+
+
+def unpatchify_prediction(ctx: Context, pred, shapes, rows=None, out=None):
+    """unpatchify_prediction: fp32 CUDA [patches, 64] -> [tokens, 16]."""
+    import torch
+
+    rows = pred.shape[0] if rows is None else rows
+    if out is None:
+        out = torch.empty((max(patch_rows(shapes)[0], 1), S2_PRED_CHANNELS), dtype=torch.float32, device=pred.device)
+    check(lib().s2_unpatchify_prediction(ctx.handle, pred.data_ptr(), int(rows), _ints(_flat_shapes(shapes)),
+                                         len(shapes), out.data_ptr()), "s2_unpatchify_prediction")
+    return out
+
+
+def timestep_embedding(ctx: Context, timesteps, out=None, device="cuda"):
+    """make_timestep_embedding: host timesteps -> fp32 CUDA [batch, 256]."""
+    import torch
+
+    n = len(timesteps)
+    if out is None:
+        out = torch.empty((max(n, 1), S2_TIME_FEATURES), dtype=torch.float32, device=device)
+    check(lib().s2_timestep_embedding(ctx.handle, _floats(timesteps), n, out.data_ptr()), "s2_timestep_embedding")
+    return out
+
+
 class Dit:
-    """s2_dit: the block stack (SeedVR2DiTBlocks' block graph)."""
+    """s2_dit: the block stack (SeedVR2DiTBlocks' block graph) and its frontend / tail nets."""
 
     def __init__(self, ctx: Context, *, num_blocks=32, hidden=2560, heads=20, head_dim=128, mlp_hidden=10240,
                  rope_pairs=21, window=(4, 3, 3), window_mode=S2_WINDOW_TARGET, norm_eps=1e-5, qk_eps=1e-5,
@@ -378,6 +453,72 @@ class Dit:
         check(lib().s2_dit_forward_host(self.handle, _ints(flat), _ints(text_lengths), len(video_shapes),
                                         ptr(video), ptr(text), ptr(modulation), ptr(video_out), ptr(text_out)),
               "s2_dit_forward_host")
+
+
+    def set_io_weights(self, w: dict):
+        """w: dict of fp32 numpy arrays keyed like IoHostWeights (biases may be None)."""
+        import numpy as np
+
+        keep = {k: (np.ascontiguousarray(v, dtype=np.float32) if v is not None else None) for k, v in w.items()}
+        hw = IoHostWeights(*[(keep[n].ctypes.data if keep.get(n) is not None else None)
+                             for n, _ in IoHostWeights._fields_])
+        check(lib().s2_dit_set_io_weights(self.handle, C.byref(hw)), "s2_dit_set_io_weights")
+
+    def forward_frontend(self, video_shapes, text_lengths, timesteps, video, text, video_out=None, text_out=None,
+                         modulation=None):
+        """DiTInputs -> DiTBlockInputs on the device: returns (video [patches, D], text [T, D],
+        modulation [6, batch, D]), fp32 CUDA."""
+        import torch
+
+        D, B = self.cfg.hidden, len(video_shapes)
+        dev = video.device
+        _, np_ = patch_rows(video_shapes)
+        if video_out is None:
+            video_out = torch.empty((np_, D), dtype=torch.float32, device=dev)
+        if text_out is None:
+            text_out = torch.empty((text.shape[0], D), dtype=torch.float32, device=dev)
+        if modulation is None:
+            modulation = torch.empty((6, B, D), dtype=torch.float32, device=dev)
+        check(lib().s2_dit_forward_frontend(self.handle, _ints(_flat_shapes(video_shapes)), _ints(text_lengths),
+                                            _floats(timesteps), B, video.data_ptr(), video.shape[0], text.data_ptr(),
+                                            text.shape[0], video_out.data_ptr(), text_out.data_ptr(),
+                                            modulation.data_ptr()), "s2_dit_forward_frontend")
+        return video_out, text_out, modulation
+
+    def forward_tail(self, video_shapes, video, modulation, prediction=None):
+        """Block-stack video rows [patches, D] + modulation [6, batch, D] -> prediction [tokens, 16]."""
+        import torch
+
+        tokens, _ = patch_rows(video_shapes)
+        if prediction is None:
+            prediction = torch.empty((tokens, S2_PRED_CHANNELS), dtype=torch.float32, device=video.device)
+        check(lib().s2_dit_forward_tail(self.handle, _ints(_flat_shapes(video_shapes)), len(video_shapes),
+                                        video.data_ptr(), video.shape[0], modulation.data_ptr(),
+                                        prediction.data_ptr()), "s2_dit_forward_tail")
+        return prediction
+
+    def forward_step(self, video_shapes, text_lengths, timesteps, video, text, prediction=None, text_out=None):
+        """The whole DiT on device buffers: latents [tokens, 33] + text [T, 5120] -> (prediction [tokens, 16],
+        text [T, D])."""
+        import torch
+
+        dev = video.device
+        if prediction is None:
+            prediction = torch.empty((video.shape[0], S2_PRED_CHANNELS), dtype=torch.float32, device=dev)
+        if text_out is None:
+            text_out = torch.empty((text.shape[0], self.cfg.hidden), dtype=torch.float32, device=dev)
+        check(lib().s2_dit_forward_step(self.handle, _ints(_flat_shapes(video_shapes)), _ints(text_lengths),
+                                        _floats(timesteps), len(video_shapes), video.data_ptr(), video.shape[0],
+                                        text.data_ptr(), text.shape[0], prediction.data_ptr(), text_out.data_ptr()),
+              "s2_dit_forward_step")
+        return prediction, text_out
+
+    def forward_step_host(self, video_shapes, text_lengths, timesteps, video, text, prediction, text_out):
+        """Same, host buffers (numpy or pinned torch CPU tensors, fp32); synchronises."""
+        check(lib().s2_dit_forward_step_host(self.handle, _ints(_flat_shapes(video_shapes)), _ints(text_lengths),
+                                             _floats(timesteps), len(video_shapes), ptr(video), video.shape[0],
+                                             ptr(text), text.shape[0], ptr(prediction), ptr(text_out)),
+              "s2_dit_forward_step_host")
 
 
 def shard(video_shape, text_length, window, window_mode, rank, world, shifted=1) -> dict:

@@ -88,6 +88,17 @@ struct s2_dit
         }
     };
     std::map<std::vector<int>, std::unique_ptr<Shard>> shards;
+    // frontend / tail nets (s2_dit_set_io_weights, s2_dit_init_random); one
+    // allocation made on first use
+    struct Io
+    {
+        __nv_bfloat16 *w_vid_in, *w_txt_in, *w_emb0, *w_emb1, *w_emb2, *w_out;
+        float *b_vid_in, *b_txt_in, *b_emb0, *b_emb1, *b_emb2, *tail_ada, *b_out;
+    } io = {};
+    void* io_weights = nullptr;
+    bool io_loaded = false;
+    s2::DeviceBuffer io_ws;   // frontend / tail activations
+    s2::DeviceBuffer io_host; // staging of s2_dit_forward_step_host
 };
 
 namespace {
@@ -115,6 +126,137 @@ int get_plan(s2_dit* d, const int* shape, int shifted, s2_plan** out)
     }
     *out = slot.get();
     return S2_OK;
+}
+
+// ---------------------------------------------------------------- frontend / tail
+// Weights of the frontend and tail nets, one allocation: bf16 w_vid_in
+// [D][kPatchPitch] (zero columns 132..135) | w_txt_in [D][5120] | w_emb0
+// [D][256] | w_emb1 [D][D] | w_emb2 [6D][D] | w_out [64][D], then fp32
+// b_vid_in, b_txt_in, b_emb0, b_emb1 [D] | b_emb2 [6D] | tail_ada [2][D] | b_out [64].
+int ensure_io_weights(s2_dit* d)
+{
+    if (d->io_weights) return S2_OK;
+    const size_t D = d->cfg.hidden;
+    const size_t n_bf16 = D * s2::kPatchPitch + D * s2::kTextChannels + D * s2::kTimeFeatures + D * D + 6 * D * D +
+                          (size_t)s2::kPredFeatures * D;
+    const size_t n_f32 = 10 * D + 2 * D + s2::kPredFeatures;
+    const size_t bytes = align256(n_bf16 * 2) + align256(n_f32 * 4);
+    if (cudaMalloc(&d->io_weights, bytes) != cudaSuccess)
+    {
+        d->io_weights = nullptr;
+        return S2_ERR_ALLOC;
+    }
+    if (cudaMemset(d->io_weights, 0, bytes) != cudaSuccess) return S2_ERR_CUDA;
+    s2_dit::Io& io = d->io;
+    __nv_bfloat16* w = static_cast<__nv_bfloat16*>(d->io_weights);
+    io.w_vid_in = w, w += D * s2::kPatchPitch;
+    io.w_txt_in = w, w += D * s2::kTextChannels;
+    io.w_emb0 = w, w += D * s2::kTimeFeatures;
+    io.w_emb1 = w, w += D * D;
+    io.w_emb2 = w, w += 6 * D * D;
+    io.w_out = w;
+    float* f = reinterpret_cast<float*>(static_cast<uint8_t*>(d->io_weights) + align256(n_bf16 * 2));
+    io.b_vid_in = f, f += D;
+    io.b_txt_in = f, f += D;
+    io.b_emb0 = f, f += D;
+    io.b_emb1 = f, f += D;
+    io.b_emb2 = f, f += 6 * D;
+    io.tail_ada = f, f += 2 * D;
+    io.b_out = f;
+    return S2_OK;
+}
+
+// Seeded synthetic frontend / tail weights (streams disjoint from the blocks').
+int init_io_random(s2_dit* d, uint64_t seed)
+{
+    int r = ensure_io_weights(d);
+    if (r != S2_OK) return r;
+    s2::Context& c = d->ctx->c;
+    const int64_t D = d->cfg.hidden;
+    const s2_dit::Io& io = d->io;
+    const uint64_t s = seed * 1000003ull + (uint64_t)d->cfg.num_blocks * 64 + 7;
+    r = s2::launch_fill_normal_bf16(c, io.w_vid_in, D * s2::kPatchPitch, s + 1, 0.f, 0.02f);
+    if (r == S2_OK && cudaMemset2DAsync(io.w_vid_in + s2::kPatchFeatures, s2::kPatchPitch * 2, 0,
+                                        (s2::kPatchPitch - s2::kPatchFeatures) * 2, D, c.stream) != cudaSuccess)
+        r = S2_ERR_CUDA;
+    if (r == S2_OK) r = s2::launch_fill_normal_bf16(c, io.w_txt_in, D * s2::kTextChannels, s + 2, 0.f, 0.02f);
+    if (r == S2_OK) r = s2::launch_fill_normal_bf16(c, io.w_emb0, D * s2::kTimeFeatures, s + 3, 0.f, 0.02f);
+    if (r == S2_OK) r = s2::launch_fill_normal_bf16(c, io.w_emb1, D * D, s + 4, 0.f, 0.02f);
+    if (r == S2_OK) r = s2::launch_fill_normal_bf16(c, io.w_emb2, 6 * D * D, s + 5, 0.f, 0.02f);
+    if (r == S2_OK) r = s2::launch_fill_normal_bf16(c, io.w_out, s2::kPredFeatures * D, s + 6, 0.f, 0.02f);
+    if (r == S2_OK) r = s2::launch_fill_normal_f32(c, io.b_vid_in, 10 * D, s + 7, 0.f, 0.02f);
+    const float sd = 1.f / std::sqrt((float)D);
+    if (r == S2_OK) r = s2::launch_fill_normal_f32(c, io.tail_ada, D, s + 8, 0.f, sd);
+    if (r == S2_OK) r = s2::launch_fill_normal_f32(c, io.tail_ada + D, D, s + 9, 1.f, sd);
+    if (r == S2_OK) r = s2::launch_fill_normal_f32(c, io.b_out, s2::kPredFeatures, s + 10, 0.f, 0.02f);
+    if (r == S2_OK) d->io_loaded = true;
+    return r;
+}
+
+// split_dit_inputs_by_sample's checks (seedvr2_dit.cpp:369-427) plus
+// patchify_video's even h/w (:178-184).  Sums the rows per side.
+int check_dit_inputs(const int* shapes, const int* text_lengths, const float* timesteps, int batch, int video_rows,
+                     int text_rows, int64_t* patches_total)
+{
+    if (!shapes || !text_lengths || !timesteps || batch <= 0 || video_rows <= 0 || text_rows <= 0)
+        return S2_ERR_INVALID;
+    int64_t v = 0, t = 0, p = 0;
+    for (int s = 0; s < batch; s++)
+    {
+        const int* shp = shapes + 3 * s;
+        if (shp[0] <= 0 || shp[1] <= 0 || shp[2] <= 0 || text_lengths[s] <= 0 || !std::isfinite(timesteps[s]))
+            return S2_ERR_INVALID;
+        if ((shp[1] & 1) || (shp[2] & 1)) return S2_ERR_INVALID;
+        const int64_t tok = (int64_t)shp[0] * shp[1] * shp[2];
+        if (tok > 0x7fffffff) return S2_ERR_INVALID;
+        v += tok;
+        t += text_lengths[s];
+        p += tok / 4;
+    }
+    if (v != video_rows || t != text_rows) return S2_ERR_INVALID;
+    if (patches_total) *patches_total = p;
+    return S2_OK;
+}
+
+// Timestep embedding and the frontend's timestep MLP for `batch` samples:
+// temb [B][256] -> e0, e1 [B][D] -> modulation, stored [6][B][D] (ref_layout,
+// the frontend's out2..out7) or [B][6][D] (one [6][D] block per sample).
+int run_emb(s2_dit* d, const float* timesteps, int batch, float* temb, float* e0, float* e1, float* mod,
+            bool ref_layout)
+{
+    s2::Context& c = d->ctx->c;
+    const int D = d->cfg.hidden;
+    const s2_dit::Io& io = d->io;
+    int r = s2::launch_timestep_embedding(c, timesteps, batch, temb);
+    if (r == S2_OK)
+        r = s2::launch_gemv(c, io.w_emb0, io.b_emb0, D, s2::kTimeFeatures, temb, s2::kTimeFeatures, batch, 1, e0, D,
+                            0, D);
+    if (r == S2_OK) r = s2::launch_gemv(c, io.w_emb1, io.b_emb1, D, D, e0, D, batch, 1, e1, D, 0, D);
+    if (r == S2_OK)
+        r = ref_layout ? s2::launch_gemv(c, io.w_emb2, io.b_emb2, 6 * D, D, e1, D, batch, 0, mod, D, (int64_t)batch * D,
+                                         D)
+                       : s2::launch_gemv(c, io.w_emb2, io.b_emb2, 6 * D, D, e1, D, batch, 0, mod, 6 * D, 0, 6 * D);
+    return r;
+}
+
+// Tail net + unpatchify for one sample: x = its [patches][D] block output,
+// mod0 / mod1 = its shift / scale modulation rows.  h [patches][D] bf16,
+// pp [patches][64] fp32 and tm [2][D] fp32 are workspace.
+int run_tail(s2_dit* d, const int* shape, const float* x, const float* mod0, const float* mod1, float* pred,
+             __nv_bfloat16* h, float* pp, float* tm)
+{
+    s2::Context& c = d->ctx->c;
+    const int D = d->cfg.hidden;
+    const s2_dit::Io& io = d->io;
+    const int np = shape[0] * (shape[1] / 2) * (shape[2] / 2);
+    int r = s2::launch_add_vectors(c, io.tail_ada, mod0, tm, D, D);
+    if (r == S2_OK) r = s2::launch_add_vectors(c, io.tail_ada + D, mod1, tm + D, D, D);
+    if (r == S2_OK) r = s2::launch_ada_rmsnorm(c, np, D, x, d->cfg.norm_eps, tm, tm + D, h);
+    if (r == S2_OK)
+        r = s2::launch_shared_linear(c, np, 0, s2::kPredFeatures, D, h, nullptr, io.w_out, io.b_out, s2::EPI_STORE,
+                                     nullptr, 1, pp, nullptr);
+    if (r == S2_OK) r = s2::launch_unpatchify(c, pp, shape[0], shape[1], shape[2], pred);
+    return r;
 }
 
 } // namespace
@@ -172,6 +314,7 @@ void s2_dit_free(s2_dit* d)
     d->plans.clear();
     d->shards.clear();
     if (d->weights) cudaFree(d->weights);
+    if (d->io_weights) cudaFree(d->io_weights);
     delete d;
 }
 
@@ -243,6 +386,7 @@ int s2_dit_init_random(s2_dit* d, uint64_t seed)
         for (int k = 0; k < 6 && r == S2_OK; k++)
             r = s2::launch_fill_normal_f32(c, ada + (size_t)k * D, D, s + 10 + k, (k == 1 || k == 4) ? 1.f : 0.f, sd);
     }
+    if (r == S2_OK) r = init_io_random(d, seed);
     if (r == S2_OK && cudaStreamSynchronize(c.stream) != cudaSuccess) r = S2_ERR_CUDA;
     return r;
 }
@@ -657,6 +801,249 @@ int s2_dit_forward_host(s2_dit* d, const int* video_shapes, const int* text_leng
     }
     if (cudaStreamSynchronize(c.stream) != cudaSuccess) return S2_ERR_CUDA;
     return r;
+}
+
+// ---------------------------------------------------------------- frontend / tail
+int s2_dit_set_io_weights(s2_dit* d, const s2_dit_io_host_weights* w)
+{
+    if (!d || !w || !w->w_vid_in || !w->w_txt_in || !w->w_emb0 || !w->w_emb1 || !w->w_emb2 || !w->tail_ada ||
+        !w->w_out)
+        return S2_ERR_INVALID;
+    s2::Context& c = d->ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    int r = ensure_io_weights(d);
+    if (r != S2_OK) return r;
+    d->io_loaded = false;
+    const size_t D = d->cfg.hidden;
+    const s2_dit::Io& io = d->io;
+    s2::DeviceBuffer tmp;
+    if ((r = tmp.ensure(std::max<size_t>(6 * D * D, D * s2::kTextChannels) * 4)) != S2_OK) return r;
+    float* t = static_cast<float*>(tmp.ptr);
+    auto up_bf16 = [&](const float* src, __nv_bfloat16* dst, size_t n) -> int {
+        if (cudaMemcpyAsync(t, src, n * 4, cudaMemcpyHostToDevice, c.stream) != cudaSuccess) return S2_ERR_CUDA;
+        return s2::launch_convert_f32_bf16(c, t, dst, (int64_t)n);
+    };
+    auto up_f32 = [&](const float* src, float* dst, size_t n) -> int {
+        if (!src) return cudaMemsetAsync(dst, 0, n * 4, c.stream) == cudaSuccess ? S2_OK : S2_ERR_CUDA;
+        return cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyHostToDevice, c.stream) == cudaSuccess ? S2_OK
+                                                                                                 : S2_ERR_CUDA;
+    };
+    // video input projection: rows of 132 placed at a pitch of kPatchPitch, zero padded
+    if (cudaMemsetAsync(t, 0, D * s2::kPatchPitch * 4, c.stream) != cudaSuccess ||
+        cudaMemcpy2DAsync(t, s2::kPatchPitch * 4, w->w_vid_in, s2::kPatchFeatures * 4, s2::kPatchFeatures * 4, D,
+                          cudaMemcpyHostToDevice, c.stream) != cudaSuccess)
+        return S2_ERR_CUDA;
+    r = s2::launch_convert_f32_bf16(c, t, io.w_vid_in, (int64_t)D * s2::kPatchPitch);
+    // the staging buffer is reused below: order the conversion before the next upload
+    if (r == S2_OK && cudaStreamSynchronize(c.stream) != cudaSuccess) r = S2_ERR_CUDA;
+    const float* srcs[5] = {w->w_txt_in, w->w_emb0, w->w_emb1, w->w_emb2, w->w_out};
+    __nv_bfloat16* dsts[5] = {io.w_txt_in, io.w_emb0, io.w_emb1, io.w_emb2, io.w_out};
+    const size_t ns[5] = {D * s2::kTextChannels, D * s2::kTimeFeatures, D * D, 6 * D * D, s2::kPredFeatures * D};
+    for (int i = 0; i < 5 && r == S2_OK; i++) r = up_bf16(srcs[i], dsts[i], ns[i]);
+    if (r == S2_OK) r = up_f32(w->b_vid_in, io.b_vid_in, D);
+    if (r == S2_OK) r = up_f32(w->b_txt_in, io.b_txt_in, D);
+    if (r == S2_OK) r = up_f32(w->b_emb0, io.b_emb0, D);
+    if (r == S2_OK) r = up_f32(w->b_emb1, io.b_emb1, D);
+    if (r == S2_OK) r = up_f32(w->b_emb2, io.b_emb2, 6 * D);
+    if (r == S2_OK) r = up_f32(w->tail_ada, io.tail_ada, 2 * D);
+    if (r == S2_OK) r = up_f32(w->b_out, io.b_out, s2::kPredFeatures);
+    if (r == S2_OK && cudaStreamSynchronize(c.stream) != cudaSuccess) r = S2_ERR_CUDA;
+    if (r == S2_OK) d->io_loaded = true;
+    return r;
+}
+
+int s2_dit_forward_frontend(s2_dit* d, const int* video_shapes, const int* text_lengths, const float* timesteps,
+                            int batch, const float* video, int video_rows, const float* text, int text_rows,
+                            float* video_out, float* text_out, float* modulation)
+{
+    // forward_frontend returns -1 before the frontend net is loaded (seedvr2_dit.cpp:1186-1187)
+    if (!d || !d->io_loaded || !video || !text || !video_out || !text_out || !modulation) return S2_ERR_INVALID;
+    int64_t np = 0;
+    int r = check_dit_inputs(video_shapes, text_lengths, timesteps, batch, video_rows, text_rows, &np);
+    if (r != S2_OK) return r;
+    s2::Context& c = d->ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    const int D = d->cfg.hidden;
+    const s2_dit::Io& io = d->io;
+    // workspace: patches bf16 [np][136] | text bf16 [T][5120] | temb [B][256] | e0, e1 [B][D]
+    const size_t sz_p = align256((size_t)np * s2::kPatchPitch * 2),
+                 sz_t = align256((size_t)text_rows * s2::kTextChannels * 2),
+                 sz_e = align256((size_t)batch * (s2::kTimeFeatures + 2 * D) * 4);
+    if ((r = d->io_ws.ensure(sz_p + sz_t + sz_e)) != S2_OK) return r;
+    uint8_t* ws = static_cast<uint8_t*>(d->io_ws.ptr);
+    __nv_bfloat16* patches = reinterpret_cast<__nv_bfloat16*>(ws);
+    __nv_bfloat16* tb = reinterpret_cast<__nv_bfloat16*>(ws + sz_p);
+    float* temb = reinterpret_cast<float*>(ws + sz_p + sz_t);
+    float* e0 = temb + (size_t)batch * s2::kTimeFeatures;
+    float* e1 = e0 + (size_t)batch * D;
+    int64_t v_off = 0, p_off = 0;
+    for (int s = 0; s < batch && r == S2_OK; s++)
+    {
+        const int* shp = video_shapes + 3 * s;
+        r = s2::launch_patchify(c, video + v_off * s2::kLatentChannels, shp[0], shp[1], shp[2],
+                                patches + p_off * s2::kPatchPitch, 1);
+        v_off += (int64_t)shp[0] * shp[1] * shp[2];
+        p_off += (int64_t)shp[0] * (shp[1] / 2) * (shp[2] / 2);
+    }
+    // token-wise nets: every sample's rows in one launch each
+    if (r == S2_OK)
+        r = s2::launch_shared_linear(c, (int)np, 0, D, s2::kPatchPitch, patches, nullptr, io.w_vid_in, io.b_vid_in,
+                                     s2::EPI_STORE, nullptr, 1, video_out, nullptr);
+    if (r == S2_OK) r = s2::launch_convert_f32_bf16(c, text, tb, (int64_t)text_rows * s2::kTextChannels);
+    if (r == S2_OK)
+        r = s2::launch_shared_linear(c, text_rows, 0, D, s2::kTextChannels, tb, nullptr, io.w_txt_in, io.b_txt_in,
+                                     s2::EPI_STORE, nullptr, 1, text_out, nullptr);
+    if (r == S2_OK) r = run_emb(d, timesteps, batch, temb, e0, e1, modulation, true);
+    return r;
+}
+
+int s2_dit_forward_tail(s2_dit* d, const int* video_shapes, int batch, const float* video, int video_rows,
+                        const float* modulation, float* prediction)
+{
+    if (!d || !d->io_loaded || !video_shapes || batch <= 0 || !video || !modulation || !prediction)
+        return S2_ERR_INVALID;
+    int64_t np_max = 0, np_total = 0;
+    for (int s = 0; s < batch; s++)
+    {
+        const int* shp = video_shapes + 3 * s;
+        if (shp[0] <= 0 || shp[1] <= 0 || shp[2] <= 0 || (shp[1] & 1) || (shp[2] & 1)) return S2_ERR_INVALID;
+        const int64_t np = (int64_t)shp[0] * (shp[1] / 2) * (shp[2] / 2);
+        np_max = std::max(np_max, np);
+        np_total += np;
+    }
+    if (np_total != video_rows) return S2_ERR_INVALID;
+    s2::Context& c = d->ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    const int D = d->cfg.hidden;
+    const size_t sz_h = align256((size_t)np_max * D * 2), sz_pp = align256((size_t)np_max * s2::kPredFeatures * 4);
+    int r = d->io_ws.ensure(sz_h + sz_pp + align256((size_t)2 * D * 4));
+    if (r != S2_OK) return r;
+    uint8_t* ws = static_cast<uint8_t*>(d->io_ws.ptr);
+    int64_t p_off = 0, t_off = 0;
+    for (int s = 0; s < batch && r == S2_OK; s++)
+    {
+        const int* shp = video_shapes + 3 * s;
+        // modulation rows [0][s] (shift) and [1][s] (scale) of the [6][batch][D] frontend output
+        r = run_tail(d, shp, video + p_off * D, modulation + (size_t)s * D, modulation + ((size_t)batch + s) * D,
+                     prediction + t_off * s2::kPredChannels, reinterpret_cast<__nv_bfloat16*>(ws),
+                     reinterpret_cast<float*>(ws + sz_h), reinterpret_cast<float*>(ws + sz_h + sz_pp));
+        p_off += (int64_t)shp[0] * (shp[1] / 2) * (shp[2] / 2);
+        t_off += (int64_t)shp[0] * shp[1] * shp[2];
+    }
+    return r;
+}
+
+int s2_dit_forward_step(s2_dit* d, const int* video_shapes, const int* text_lengths, const float* timesteps,
+                        int batch, const float* video, int video_rows, const float* text, int text_rows,
+                        float* prediction, float* text_out)
+{
+    // SeedVR2DiTBlocks::forward(DiTInputs) returns -1 unless the frontend, the
+    // tail and the block graph are loaded (seedvr2_dit.cpp:1301-1302)
+    if (!d || !d->io_loaded || !video || !text || !prediction || !text_out) return S2_ERR_INVALID;
+    int r = check_dit_inputs(video_shapes, text_lengths, timesteps, batch, video_rows, text_rows, nullptr);
+    if (r != S2_OK) return r;
+    s2::Context& c = d->ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    const int D = d->cfg.hidden;
+    const s2_dit::Io& io = d->io;
+    int64_t np_max = 0, nt_max = 0;
+    for (int s = 0; s < batch; s++)
+    {
+        const int* shp = video_shapes + 3 * s;
+        np_max = std::max(np_max, (int64_t)shp[0] * (shp[1] / 2) * (shp[2] / 2));
+        nt_max = std::max(nt_max, (int64_t)text_lengths[s]);
+    }
+    // workspace: x [np + T][D] f32 | patches bf16 [np][136] | text bf16 [T][5120] |
+    //            h bf16 [np][D] | pp [np][64] f32 | tm [2][D] | temb [B][256] | e0, e1 [B][D] | emb [B][6][D]
+    const size_t sz_x = align256((size_t)(np_max + nt_max) * D * 4),
+                 sz_p = align256((size_t)np_max * s2::kPatchPitch * 2),
+                 sz_t = align256((size_t)nt_max * s2::kTextChannels * 2), sz_h = align256((size_t)np_max * D * 2),
+                 sz_pp = align256((size_t)np_max * s2::kPredFeatures * 4), sz_tm = align256((size_t)2 * D * 4),
+                 sz_e = align256((size_t)batch * (s2::kTimeFeatures + 2 * D) * 4),
+                 sz_m = align256((size_t)batch * 6 * D * 4);
+    if ((r = d->io_ws.ensure(sz_x + sz_p + sz_t + sz_h + sz_pp + sz_tm + sz_e + sz_m)) != S2_OK) return r;
+    uint8_t* ws = static_cast<uint8_t*>(d->io_ws.ptr);
+    float* x = reinterpret_cast<float*>(ws);
+    ws += sz_x;
+    __nv_bfloat16* patches = reinterpret_cast<__nv_bfloat16*>(ws);
+    ws += sz_p;
+    __nv_bfloat16* tb = reinterpret_cast<__nv_bfloat16*>(ws);
+    ws += sz_t;
+    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(ws);
+    ws += sz_h;
+    float* pp = reinterpret_cast<float*>(ws);
+    ws += sz_pp;
+    float* tm = reinterpret_cast<float*>(ws);
+    ws += sz_tm;
+    float* temb = reinterpret_cast<float*>(ws);
+    float* e0 = temb + (size_t)batch * s2::kTimeFeatures;
+    float* e1 = e0 + (size_t)batch * D;
+    ws += sz_e;
+    float* emb = reinterpret_cast<float*>(ws);
+
+    // timestep MLP of every sample at once; per sample [6][D]
+    if ((r = run_emb(d, timesteps, batch, temb, e0, e1, emb, false)) != S2_OK) return r;
+    int64_t v_off = 0, t_off = 0;
+    for (int s = 0; s < batch && r == S2_OK; s++)
+    {
+        const int* shp = video_shapes + 3 * s;
+        const int pshape[3] = {shp[0], shp[1] / 2, shp[2] / 2};
+        const int np = pshape[0] * pshape[1] * pshape[2], nt = text_lengths[s];
+        const float* mod = emb + (size_t)s * 6 * D;
+        // frontend: x = [video patches W_vid_in^T + b | text W_txt_in^T + b]
+        r = s2::launch_patchify(c, video + v_off * s2::kLatentChannels, shp[0], shp[1], shp[2], patches, 1);
+        if (r == S2_OK)
+            r = s2::launch_shared_linear(c, np, 0, D, s2::kPatchPitch, patches, nullptr, io.w_vid_in, io.b_vid_in,
+                                         s2::EPI_STORE, nullptr, 1, x, nullptr);
+        if (r == S2_OK)
+            r = s2::launch_convert_f32_bf16(c, text + t_off * s2::kTextChannels, tb, (int64_t)nt * s2::kTextChannels);
+        if (r == S2_OK)
+            r = s2::launch_shared_linear(c, nt, 0, D, s2::kTextChannels, tb, nullptr, io.w_txt_in, io.b_txt_in,
+                                         s2::EPI_STORE, nullptr, 1, x + (size_t)np * D, nullptr);
+        // all blocks, in place
+        if (r == S2_OK) r = s2_dit_forward(d, pshape, nt, x, mod);
+        // tail -> prediction tokens; text rows out
+        if (r == S2_OK) r = run_tail(d, shp, x, mod, mod + D, prediction + v_off * s2::kPredChannels, h, pp, tm);
+        if (r == S2_OK && cudaMemcpyAsync(text_out + t_off * D, x + (size_t)np * D, (size_t)nt * D * 4,
+                                          cudaMemcpyDeviceToDevice, c.stream) != cudaSuccess)
+            r = S2_ERR_CUDA;
+        v_off += (int64_t)shp[0] * shp[1] * shp[2];
+        t_off += nt;
+    }
+    return r;
+}
+
+int s2_dit_forward_step_host(s2_dit* d, const int* video_shapes, const int* text_lengths, const float* timesteps,
+                             int batch, const float* video, int video_rows, const float* text, int text_rows,
+                             float* prediction, float* text_out)
+{
+    if (!d || !d->io_loaded || !video || !text || !prediction || !text_out) return S2_ERR_INVALID;
+    int r = check_dit_inputs(video_shapes, text_lengths, timesteps, batch, video_rows, text_rows, nullptr);
+    if (r != S2_OK) return r;
+    s2::Context& c = d->ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    const int D = d->cfg.hidden;
+    const size_t bv = align256((size_t)video_rows * s2::kLatentChannels * 4),
+                 bt = align256((size_t)text_rows * s2::kTextChannels * 4),
+                 bp = align256((size_t)video_rows * s2::kPredChannels * 4), bo = align256((size_t)text_rows * D * 4);
+    if ((r = d->io_host.ensure(bv + bt + bp + bo)) != S2_OK) return r;
+    uint8_t* p = static_cast<uint8_t*>(d->io_host.ptr);
+    float* dv = reinterpret_cast<float*>(p);
+    float* dt = reinterpret_cast<float*>(p + bv);
+    float* dp = reinterpret_cast<float*>(p + bv + bt);
+    float* dto = reinterpret_cast<float*>(p + bv + bt + bp);
+    if (cudaMemcpyAsync(dv, video, (size_t)video_rows * s2::kLatentChannels * 4, cudaMemcpyHostToDevice, c.stream) !=
+            cudaSuccess ||
+        cudaMemcpyAsync(dt, text, (size_t)text_rows * s2::kTextChannels * 4, cudaMemcpyHostToDevice, c.stream) !=
+            cudaSuccess)
+        return S2_ERR_CUDA;
+    r = s2_dit_forward_step(d, video_shapes, text_lengths, timesteps, batch, dv, video_rows, dt, text_rows, dp, dto);
+    if (r != S2_OK) return r;
+    if (cudaMemcpyAsync(prediction, dp, (size_t)video_rows * s2::kPredChannels * 4, cudaMemcpyDeviceToHost,
+                        c.stream) != cudaSuccess ||
+        cudaMemcpyAsync(text_out, dto, (size_t)text_rows * D * 4, cudaMemcpyDeviceToHost, c.stream) != cudaSuccess)
+        return S2_ERR_CUDA;
+    return cudaStreamSynchronize(c.stream) == cudaSuccess ? S2_OK : S2_ERR_CUDA;
 }
 
 } // extern "C"

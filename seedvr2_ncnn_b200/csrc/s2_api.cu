@@ -298,6 +298,55 @@ int s2_convert_f32_bf16(s2_context* ctx, const float* in, void* out, int64_t cou
     return s2::launch_convert_f32_bf16(ctx->c, in, out, count);
 }
 
+// ------------------------------------------------------- token formats
+int s2_patchify_video(s2_context* ctx, const float* video, int rows, const int* shapes, int batch, float* out)
+{
+    if (!ctx) return S2_ERR_INVALID;
+    const int r = s2::patchify_rows(shapes, batch, rows, nullptr);
+    if (r != S2_OK) return r;
+    if (!video || !out) return S2_ERR_INVALID;
+    if (cudaSetDevice(ctx->c.device) != cudaSuccess) return S2_ERR_CUDA;
+    int64_t v_off = 0, p_off = 0;
+    for (int s = 0; s < batch; s++)
+    {
+        const int* shp = shapes + 3 * s;
+        const int e = s2::launch_patchify(ctx->c, video + v_off * s2::kLatentChannels, shp[0], shp[1], shp[2],
+                                          out + p_off * s2::kPatchFeatures, 0);
+        if (e != S2_OK) return e;
+        v_off += (int64_t)shp[0] * shp[1] * shp[2];
+        p_off += (int64_t)shp[0] * (shp[1] / 2) * (shp[2] / 2);
+    }
+    return S2_OK;
+}
+
+int s2_unpatchify_prediction(s2_context* ctx, const float* pred, int rows, const int* shapes, int batch, float* out)
+{
+    if (!ctx) return S2_ERR_INVALID;
+    const int r = s2::unpatchify_rows(shapes, batch, rows, nullptr);
+    if (r != S2_OK) return r;
+    if (!pred || !out) return S2_ERR_INVALID;
+    if (cudaSetDevice(ctx->c.device) != cudaSuccess) return S2_ERR_CUDA;
+    int64_t p_off = 0, t_off = 0;
+    for (int s = 0; s < batch; s++)
+    {
+        const int* shp = shapes + 3 * s;
+        const int e = s2::launch_unpatchify(ctx->c, pred + p_off * s2::kPredFeatures, shp[0], shp[1], shp[2],
+                                            out + t_off * s2::kPredChannels);
+        if (e != S2_OK) return e;
+        p_off += (int64_t)shp[0] * (shp[1] / 2) * (shp[2] / 2);
+        t_off += (int64_t)shp[0] * shp[1] * shp[2];
+    }
+    return S2_OK;
+}
+
+int s2_timestep_embedding(s2_context* ctx, const float* timesteps, int batch, float* out)
+{
+    // make_timestep_embedding returns -1 for an empty batch (seedvr2_dit.cpp:235-236)
+    if (!ctx || batch <= 0 || !timesteps || !out) return S2_ERR_INVALID;
+    if (cudaSetDevice(ctx->c.device) != cudaSuccess) return S2_ERR_CUDA;
+    return s2::launch_timestep_embedding(ctx->c, timesteps, batch, out);
+}
+
 // ------------------------------------------------------------------ multi-GPU
 int s2_shard_build(const int* video_shape, int text_length, const int* window, int window_mode, int rank, int world,
                    s2_shard** out)

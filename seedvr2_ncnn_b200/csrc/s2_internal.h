@@ -193,6 +193,34 @@ int launch_text_pool(Context& ctx, const AttnSchedule& s, int inner, const float
 int launch_ada_rmsnorm(Context& ctx, int rows, int D, const float* x, float eps, const float* shift,
                        const float* scale, void* out);
 
+// Token formats around the block stack (seedvr2_dit.cpp:167-326) and the
+// frontend / tail nets' dense passes.
+constexpr int kLatentChannels = S2_LATENT_CHANNELS;  // 33
+constexpr int kPatchFeatures = S2_PATCH_FEATURES;    // 132 = 4 x 33
+constexpr int kPatchPitch = 136;                     // bf16 GEMM row: 132 features + zeros (16-byte rows)
+constexpr int kPredChannels = S2_PRED_CHANNELS;      // 16
+constexpr int kPredFeatures = S2_PRED_FEATURES;      // 64 = 4 x 16
+constexpr int kTextChannels = S2_TEXT_CHANNELS;      // 5120
+constexpr int kTimeFeatures = S2_TIME_FEATURES;      // 256
+constexpr int kTimestepChunk = 64;                   // timesteps per embedding launch
+constexpr int kGemvRows = 8;                         // batch rows per matrix-vector launch
+// Host checks of patchify_video / unpatchify_prediction over a batch of
+// latent shapes (S2_OK, S2_ERR_INVALID, or S2_ERR_ALLOC for an empty output,
+// as the reference); the other side's row count is returned.
+int patchify_rows(const int* shapes, int batch, int rows, int64_t* patches);
+int unpatchify_rows(const int* shapes, int batch, int rows, int64_t* tokens);
+// [T][H][W][33] fp32 latent tokens of one sample -> patches: fp32 rows of 132
+// (bf16_out = 0) or bf16 rows of kPatchPitch with zero padding (bf16_out = 1)
+int launch_patchify(Context& ctx, const float* src, int T, int H, int W, void* dst, int bf16_out);
+// [patches][64] fp32 -> [T][H][W][16] fp32 (16-byte aligned buffers)
+int launch_unpatchify(Context& ctx, const float* src, int T, int H, int W, float* dst);
+// host timesteps -> [batch][256] fp32 device
+int launch_timestep_embedding(Context& ctx, const float* timesteps, int batch, float* out);
+// y(b, n) = act(bias[n] + W[n] . x[b]) (act 1 = SiLU), W bf16 [N][K], x fp32
+// [B][ldx]; y(b, n) stored at y[(n / chunk) * s_chunk + b * s_b + n % chunk]
+int launch_gemv(Context& ctx, const void* W, const float* bias, int N, int K, const float* x, int ldx, int B, int act,
+                float* y, int chunk, int64_t s_chunk, int64_t s_b);
+
 int launch_convert_f32_bf16(Context& ctx, const float* in, void* out, int64_t count);
 int launch_add_vectors(Context& ctx, const float* a, const float* b, float* out, int count, int period);
 int launch_fill_normal_bf16(Context& ctx, void* out, int64_t count, uint64_t seed, float mean, float stddev);

@@ -35,7 +35,17 @@ def ref():
 
 @pytest.fixture(scope="session")
 def golden():
-    return {name: np.load(os.path.join(GOLDEN, f"{name}.npz")) for name in ("plans", "awa", "linear")}
+    return {name: np.load(os.path.join(GOLDEN, f"{name}.npz")) for name in ("plans", "awa", "linear", "dit_io")}
+
+
+@pytest.fixture(scope="session")
+def refio():
+    """The reference's own patchify / timestep / unpatchify (built only where its tree is present)."""
+    from oracle import oracle
+
+    if not os.path.exists(oracle.REF_IO_SO):
+        pytest.skip("oracle/_ref/libs2_ref_dit_io.so not built (reference tree absent)")
+    return oracle.RefIO()
 
 
 @pytest.fixture(scope="session")

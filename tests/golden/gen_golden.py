@@ -15,6 +15,10 @@ Outputs:
   awa.npz     -- AdaptiveWindowAttention::forward (CPU) on a seeded 2-sample
                  batch, fused-QKV input, shifted/unshifted x bf16 on/off.
   linear.npz  -- SharedLinear::forward on seeded inputs, with and without bias.
+  dit_io.npz  -- patchify_video / unpatchify_prediction / make_timestep_embedding
+                 (oracle/_ref/libs2_ref_dit_io.so: src/seedvr2/seedvr2_dit.cpp:167-326
+                 compiled unmodified) on seeded inputs, plus the return codes of
+                 a set of invalid / empty calls.
 """
 from __future__ import annotations
 
@@ -120,6 +124,51 @@ def gen_linear(ref: oracle.Ref) -> None:
                         video_out_bias=vo_b, text_out_bias=to_b, video_out_nobias=vo_n, text_out_nobias=to_n)
 
 
+DIT_IO_CASES = [("one", [[2, 6, 8]]), ("batch2", [[1, 2, 2], [3, 4, 10]]), ("frames", [[3, 8, 10]])]
+# (function, shapes, rows): rows are the input blob's height
+DIT_IO_ERRORS = [
+    ("patchify", [[1, 3, 4]], 12), ("patchify", [[1, 4, 4]], 15), ("patchify", [], 0), ("patchify", [], 5),
+    ("patchify", [[0, 4, 4]], 0), ("patchify", [[-1, 4, 4]], 16), ("patchify", [[2, 4, 4]], 32),
+    ("unpatchify", [[1, 3, 4]], 3), ("unpatchify", [], 0), ("unpatchify", [], 3), ("unpatchify", [[0, 4, 4]], 0),
+    ("unpatchify", [[0, 4, 4], [1, 2, 2]], 1), ("unpatchify", [[2, 4, 4]], 7), ("unpatchify", [[2, 4, 4]], 8),
+]
+
+
+def _code(fn) -> int:
+    try:
+        fn()
+        return 0
+    except ValueError as e:
+        return int(e.args[0])
+
+
+def gen_dit_io(refio: oracle.RefIO) -> None:
+    rng = np.random.default_rng(4321)
+    out = {}
+    for name, shapes in DIT_IO_CASES:
+        tokens = sum(t * h * w for t, h, w in shapes)
+        video = rng.standard_normal((tokens, 33)).astype(np.float32)
+        patches = refio.patchify_video(video, shapes)
+        pred = rng.standard_normal((patches.shape[0], 64)).astype(np.float32)
+        out[f"{name}__shapes"] = np.asarray(shapes, np.int32)
+        out[f"{name}__video"] = video
+        out[f"{name}__patches"] = patches
+        out[f"{name}__pred"] = pred
+        out[f"{name}__unpatched"] = refio.unpatchify_prediction(pred, shapes)
+    t = np.asarray([0.0, 1.0, 0.5, 999.0, 1000.0, 437.25, -3.0, 1e-3, 250.0, 12345.5], np.float32)
+    out["timesteps"] = t
+    out["timestep_embedding"] = refio.timestep_embedding(t)
+    codes = []
+    for fn, shapes, rows in DIT_IO_ERRORS:
+        if fn == "patchify":
+            codes.append(_code(lambda: refio.patchify_video(np.zeros((max(rows, 1), 33), np.float32), shapes, rows)))
+        else:
+            codes.append(_code(lambda: refio.unpatchify_prediction(np.zeros((max(rows, 1), 64), np.float32), shapes,
+                                                                    rows)))
+    out["error_codes"] = np.asarray(codes, np.int32)
+    np.savez_compressed(os.path.join(OUT, "dit_io.npz"), **out)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-tree", default=os.environ.get("S2_REFERENCE_TREE", "/root/reference"))
@@ -129,7 +178,8 @@ def main() -> None:
     gen_plans(ref)
     gen_awa(ref)
     gen_linear(ref)
-    for f in ("plans.npz", "awa.npz", "linear.npz"):
+    gen_dit_io(oracle.RefIO())
+    for f in ("plans.npz", "awa.npz", "linear.npz", "dit_io.npz"):
         print(f, os.path.getsize(os.path.join(OUT, f)), "bytes")
 
 
