@@ -427,6 +427,30 @@ def main():
                             "d2h_bytes_per_step": int(ntok * 16 * 4 + TEXT * D * 4),
                             "entry_point": "s2_dit_forward_step_host"}}
         del lv, lt, pred, tout, hlv, hlt, hpred, htout
+
+        # SeedVR2Pipeline::denoise on the device: 2 Euler steps with
+        # classifier-free guidance (two whole-DiT passes per step + apply_cfg
+        # with rescale + the update), latent / condition as 16 channel planes.
+        planes = torch.randn(2, abi.S2_PRED_CHANNELS, ntok, device="cuda", generator=gl)
+        neg_text = torch.randn(TEXT, abi.S2_TEXT_CHANNELS, device="cuda", generator=gl)
+        pos_text = torch.randn(TEXT, abi.S2_TEXT_CHANNELS, device="cuda", generator=gl)
+        lat0 = planes[0].clone()
+
+        def denoise():
+            planes[0].copy_(lat0)
+            dit.denoise(lat, planes[0], planes[1], pos_text, neg_text, steps=2, cfg_scale=6.5, cfg_rescale=0.7)
+
+        denoise()
+        barrier()
+        e0.record(stream)
+        denoise()
+        e1.record(stream)
+        barrier()
+        dn_ms = e0.elapsed_time(e1)
+        dit_step["denoise"] = {"steps": 2, "cfg_scale": 6.5, "cfg_rescale": 0.7, "ms": dn_ms,
+                               "ms_per_dit_pass": dn_ms / 4, "entry_point": "s2_dit_denoise",
+                               "host_round_trips_between_steps": 0}
+        del planes, neg_text, pos_text, lat0
     status = ctx.status()
 
     peaks = load_peaks()

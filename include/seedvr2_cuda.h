@@ -321,6 +321,39 @@ int s2_dit_forward_step_host(s2_dit* dit, const int* video_shapes, const int* te
                              float* prediction, float* text_out);
 
 /* ---------------------------------------------------------------------------
+ * Denoise loop on the device (SeedVR2Pipeline::denoise + predict,
+ * seedvr2_pipeline.cpp:284-329, :536-588): `steps` Euler steps from
+ * t = 1000 down to 0, each a whole-DiT pass on [latent | condition | 1] tokens
+ * and, when cfg_scale != 1, a second pass on the negative text combined by
+ * apply_cfg (:171-210); no host round trip between steps.
+ * latent / condition: 16 fp32 channel planes of t*h*w values (plane stride
+ * *_cstep elements, >= t*h*w: the ncnn Mat layout); the latent is updated in
+ * place.  positive / negative text fp32 [rows][5120].  -1 for steps <= 0, an
+ * odd h/w, empty text, a missing negative text with cfg_scale != 1, or
+ * frontend / tail weights not loaded. */
+typedef struct
+{
+    int steps;         /* PipelineOptions::steps (>= 1) */
+    float cfg_scale;   /* 1 = no guidance */
+    float cfg_rescale; /* 0 = no rescale */
+} s2_denoise_options;
+
+int s2_dit_denoise(s2_dit* dit, const int* latent_shape, float* latent, int64_t latent_cstep, const float* condition,
+                   int64_t condition_cstep, const float* positive_text, int positive_rows, const float* negative_text,
+                   int negative_rows, const s2_denoise_options* options);
+/* Same, host buffers (synchronises). */
+int s2_dit_denoise_host(s2_dit* dit, const int* latent_shape, float* latent, int64_t latent_cstep,
+                        const float* condition, int64_t condition_cstep, const float* positive_text,
+                        int positive_rows, const float* negative_text, int negative_rows,
+                        const s2_denoise_options* options);
+/* apply_cfg (seedvr2_pipeline.cpp:171-210) on device arrays of `count` fp32:
+ * out = neg + scale (pos - neg), then with rescale != 0 multiplied by
+ * float(rescale std(pos) / std(out) + 1 - rescale) (sample standard
+ * deviations in double). */
+int s2_apply_cfg(s2_context* ctx, const float* pos, const float* neg, int64_t count, float scale, float rescale,
+                 float* out);
+
+/* ---------------------------------------------------------------------------
  * Multi-GPU (one process per GPU over NVLink).  The reference has no
  * distributed path (seedvr2_main.cpp:89-100 forces --sp-size 1); this is the
  * window sharding of the B200 build.

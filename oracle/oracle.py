@@ -89,6 +89,10 @@ class Port:
         lib.s2o_patchify_video.argtypes = [C.c_void_p, C.c_int, _i32p, C.c_int, C.c_void_p]
         lib.s2o_unpatchify_prediction.argtypes = [C.c_void_p, C.c_int, _i32p, C.c_int, C.c_void_p]
         lib.s2o_timestep_embedding.argtypes = [_f32p, C.c_int, _f32p]
+        lib.s2o_assemble_dit_input.argtypes = [_f32p, C.c_long, _f32p, C.c_long, C.c_long, _f32p]
+        lib.s2o_apply_cfg.argtypes = [_f32p, _f32p, C.c_long, C.c_float, C.c_float, _f32p]
+        lib.s2o_euler_update.argtypes = [_f32p, C.c_long, C.c_long, _f32p, C.c_float]
+        lib.s2o_denoise_schedule.argtypes = [C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_float)]
         self.lib = lib
 
     def plan(self, shapes, window, shifted, mode=WINDOW_TARGET) -> Plan:
@@ -251,6 +255,48 @@ class Port:
         return np.concatenate(out)
 
 
+    # ---- denoise loop (seedvr2_pipeline.cpp) ----
+    def assemble_dit_input(self, latent, condition):
+        """latent, condition: [16][tokens] planes -> [tokens][33] rows (predict, :296-318)."""
+        latent = _f32(latent)
+        condition = _f32(condition)
+        tokens = latent.shape[1]
+        out = np.zeros((tokens, 33), np.float32)
+        self.lib.s2o_assemble_dit_input(latent, tokens, condition, tokens, tokens, out)
+        return out
+
+    def apply_cfg(self, pos, neg, scale, rescale):
+        pos = _f32(pos)
+        out = np.zeros_like(pos)
+        self.lib.s2o_apply_cfg(pos, _f32(neg), pos.size, scale, rescale, out)
+        return out
+
+    def denoise_schedule(self, steps, step):
+        t, d = C.c_float(), C.c_float()
+        self.lib.s2o_denoise_schedule(steps, step, C.byref(t), C.byref(d))
+        return t.value, d.value
+
+    def euler_update(self, latent, pred, delta):
+        """latent [16][tokens] (returned updated copy), pred [tokens][16]."""
+        lat = _f32(latent).copy()
+        self.lib.s2o_euler_update(lat, lat.shape[1], lat.shape[1], _f32(pred), delta)
+        return lat
+
+    def denoise(self, predict, latent, condition, steps, cfg_scale=1.0, cfg_rescale=0.0):
+        """SeedVR2Pipeline::denoise (seedvr2_pipeline.cpp:536-588) with predict(video_rows [tokens][33],
+        timestep, positive: bool) -> prediction [tokens][16] supplied by the caller."""
+        lat = _f32(latent).copy()
+        for step in range(steps):
+            t, delta = self.denoise_schedule(steps, step)
+            rows = self.assemble_dit_input(lat, condition)
+            pred = predict(rows, t, True)
+            if cfg_scale != 1.0:
+                neg = predict(rows, t, False)
+                pred = self.apply_cfg(pred, neg, cfg_scale, cfg_rescale)
+            lat = self.euler_update(lat, pred, delta)
+        return lat
+
+
 def _f64(a) -> np.ndarray:
     return np.asarray(a, dtype=np.float64)
 
@@ -274,7 +320,15 @@ class RefIO:
         lib.s2ref_patchify_video.argtypes = [C.c_void_p, C.c_int, _i32p, C.c_int, C.c_void_p, C.c_void_p]
         lib.s2ref_unpatchify_prediction.argtypes = [C.c_void_p, C.c_int, _i32p, C.c_int, C.c_void_p]
         lib.s2ref_timestep_embedding.argtypes = [_f32p, C.c_int, C.c_void_p]
+        lib.s2ref_apply_cfg.argtypes = [_f32p, _f32p, C.c_int, C.c_int, C.c_float, C.c_float, _f32p]
         self.lib = lib
+
+    def apply_cfg(self, pos, neg, scale, rescale):
+        pos = _f32(pos)
+        out = np.zeros_like(pos)
+        w = pos.shape[-1] if pos.ndim > 1 else pos.size
+        self.lib.s2ref_apply_cfg(pos, _f32(neg), w, pos.size // w, scale, rescale, out)
+        return out
 
     def patchify_video(self, video, shapes, rows=None):
         video = _f32(video)

@@ -1,10 +1,12 @@
 // extern "C" wrapper around the reference's OWN token-format functions
 // patchify_video, make_timestep_embedding and unpatchify_prediction
-// (src/seedvr2/seedvr2_dit.cpp:167-326).  They sit in an anonymous namespace
-// of a file that needs the Vulkan runtime, so oracle/Makefile cuts exactly
-// that range, unmodified, out of the reference tree into the git-ignored
-// oracle/_ref/dit_io_extract.inc, and this file compiles it against the
-// clean-room ncnn Mat shim into oracle/_ref/libs2_ref_dit_io.so.
+// (src/seedvr2/seedvr2_dit.cpp:167-326) and the classifier-free guidance
+// combine apply_cfg (src/seedvr2/seedvr2_pipeline.cpp:171-210).  They sit in
+// anonymous namespaces of files that need the Vulkan runtime, so
+// oracle/Makefile cuts exactly those ranges, unmodified, out of the reference
+// tree into the git-ignored oracle/_ref/{dit_io,cfg}_extract.inc, and this
+// file compiles them against the clean-room ncnn Mat shim into
+// oracle/_ref/libs2_ref_dit_io.so.
 //
 // TEST INFRASTRUCTURE ONLY: the tests and the fixture generator load it as the
 // checker; the shipped library never links it.
@@ -18,6 +20,7 @@
 namespace seedvr2 {
 namespace {
 #include "dit_io_extract.inc"
+#include "cfg_extract.inc"
 } // namespace
 } // namespace seedvr2
 
@@ -73,6 +76,17 @@ int s2ref_timestep_embedding(const float* timesteps, int batch, float* out)
     const int r = seedvr2::make_timestep_embedding(t, e);
     if (r != 0) return r;
     std::memcpy(out, e.data, sizeof(float) * 256 * (size_t)batch);
+    return 0;
+}
+
+// cfg [count] = apply_cfg(pos, neg) on [rows][w] blobs
+int s2ref_apply_cfg(const float* pos, const float* neg, int w, int rows, float scale, float rescale, float* cfg)
+{
+    ncnn::Mat p(w, rows), n(w, rows), out;
+    std::memcpy(p.data, pos, sizeof(float) * (size_t)w * rows);
+    std::memcpy(n.data, neg, sizeof(float) * (size_t)w * rows);
+    seedvr2::apply_cfg(p, n, scale, rescale, out);
+    std::memcpy(cfg, out.data, sizeof(float) * (size_t)w * rows);
     return 0;
 }
 

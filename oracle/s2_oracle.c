@@ -638,3 +638,73 @@ int s2o_timestep_embedding(const float* timesteps, int batch, float* out)
         }
     return 0;
 }
+
+/* ---------------------------------------------------------------------------
+ * Denoise loop pieces (src/seedvr2/seedvr2_pipeline.cpp). Latents are 16
+ * channel planes of `tokens` values, plane stride cstep (ncnn Mat layout). */
+
+/* SeedVR2Pipeline::predict's DiT input (seedvr2_pipeline.cpp:296-318): row
+ * token = [latent channels 0..15 | condition channels 0..15 | 1.0]. */
+void s2o_assemble_dit_input(const float* latent, long latent_cstep, const float* condition, long condition_cstep,
+                            long tokens, float* out)
+{
+    for (long t = 0; t < tokens; t++)
+    {
+        float* row = out + t * 33;
+        for (int c = 0; c < 16; c++)
+        {
+            row[c] = latent[c * latent_cstep + t];
+            row[c + 16] = condition[c * condition_cstep + t];
+        }
+        row[32] = 1.f;
+    }
+}
+
+/* apply_cfg (seedvr2_pipeline.cpp:171-210): cfg = neg + scale * (pos - neg);
+ * with rescale != 0 (and count >= 2) every value is multiplied by
+ * float(rescale * std(pos) / std(cfg) + (1 - rescale)), means and sample
+ * standard deviations accumulated in double in index order. */
+void s2o_apply_cfg(const float* pos, const float* neg, long count, float scale, float rescale, float* cfg)
+{
+    for (long i = 0; i < count; i++) cfg[i] = neg[i] + scale * (pos[i] - neg[i]);
+    if (rescale == 0.f || count < 2) return;
+    double pos_mean = 0.0, cfg_mean = 0.0;
+    for (long i = 0; i < count; i++)
+    {
+        pos_mean += pos[i];
+        cfg_mean += cfg[i];
+    }
+    pos_mean /= count;
+    cfg_mean /= count;
+    double pos_var = 0.0, cfg_var = 0.0;
+    for (long i = 0; i < count; i++)
+    {
+        const double p = pos[i] - pos_mean;
+        const double c = cfg[i] - cfg_mean;
+        pos_var += p * p;
+        cfg_var += c * c;
+    }
+    const double pos_std = sqrt(pos_var / (count - 1));
+    const double cfg_std = sqrt(cfg_var / (count - 1));
+    if (cfg_std == 0.0) return;
+    const float factor = (float)(rescale * pos_std / cfg_std + (1.f - rescale));
+    for (long i = 0; i < count; i++) cfg[i] *= factor;
+}
+
+/* Euler update of SeedVR2Pipeline::denoise (seedvr2_pipeline.cpp:572-586):
+ * latent[c][t] += delta * pred[t][c]. */
+void s2o_euler_update(float* latent, long cstep, long tokens, const float* pred, float delta)
+{
+    for (long t = 0; t < tokens; t++)
+        for (int c = 0; c < 16; c++) latent[c * cstep + t] += delta * pred[t * 16 + c];
+}
+
+/* The denoise schedule (seedvr2_pipeline.cpp:542-545): timestep of step s of n
+ * and the Euler delta to the next one. */
+void s2o_denoise_schedule(int steps, int step, float* timestep, float* delta)
+{
+    const float t = 1000.f * (steps - step) / steps;
+    const float next = 1000.f * (steps - step - 1) / steps;
+    *timestep = t;
+    *delta = (next - t) / 1000.f;
+}

@@ -82,6 +82,14 @@ int s2o_unpatchify_prediction(const float* src, int rows, const int* shapes, int
 /* [batch][256] sinusoidal embedding (make_timestep_embedding, :232-253) */
 int s2o_timestep_embedding(const float* timesteps, int batch, float* out);
 
+/* Denoise loop pieces (src/seedvr2/seedvr2_pipeline.cpp); latents are 16
+ * channel planes of `tokens` values with plane stride cstep. */
+void s2o_assemble_dit_input(const float* latent, long latent_cstep, const float* condition, long condition_cstep,
+                            long tokens, float* out);
+void s2o_apply_cfg(const float* pos, const float* neg, long count, float scale, float rescale, float* cfg);
+void s2o_euler_update(float* latent, long cstep, long tokens, const float* pred, float delta);
+void s2o_denoise_schedule(int steps, int step, float* timestep, float* delta);
+
 #ifdef __cplusplus
 }
 #endif

@@ -53,6 +53,7 @@ EXPORTED = [
     "s2_dist_unique_id", "s2_dist_init", "s2_dist_sync", "s2_dist_destroy", "s2_dit_forward_sharded",
     "s2_patchify_video", "s2_unpatchify_prediction", "s2_timestep_embedding", "s2_dit_set_io_weights",
     "s2_dit_forward_frontend", "s2_dit_forward_tail", "s2_dit_forward_step", "s2_dit_forward_step_host",
+    "s2_dit_denoise", "s2_dit_denoise_host", "s2_apply_cfg",
 ]
 
 # Widths fixed by the reference's DiT input/output formats.
@@ -90,6 +91,10 @@ class DitConfig(C.Structure):
 class BlockHostWeights(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in ("ada", "w_qkv", "b_qkv", "w_out", "b_out", "w_up", "b_up", "w_down",
                                           "b_down", "qk_norm", "rope_freqs")]
+
+
+class DenoiseOptions(C.Structure):
+    _fields_ = [("steps", C.c_int), ("cfg_scale", C.c_float), ("cfg_rescale", C.c_float)]
 
 
 class IoHostWeights(C.Structure):
@@ -161,6 +166,9 @@ def lib() -> C.CDLL:
     L.s2_dit_forward_tail.argtypes = [vp, pint, ip, vp, ip, vp, vp]
     L.s2_dit_forward_step.argtypes = [vp, pint, pint, C.POINTER(C.c_float), ip, vp, ip, vp, ip, vp, vp]
     L.s2_dit_forward_step_host.argtypes = [vp, pint, pint, C.POINTER(C.c_float), ip, vp, ip, vp, ip, vp, vp]
+    L.s2_dit_denoise.argtypes = [vp, pint, vp, i64, vp, i64, vp, ip, vp, ip, C.POINTER(DenoiseOptions)]
+    L.s2_dit_denoise_host.argtypes = [vp, pint, vp, i64, vp, i64, vp, ip, vp, ip, C.POINTER(DenoiseOptions)]
+    L.s2_apply_cfg.argtypes = [vp, vp, vp, i64, C.c_float, C.c_float, vp]
     _lib = L
     return L
 
@@ -394,6 +402,17 @@ def timestep_embedding(ctx: Context, timesteps, out=None, device="cuda"):
     return out
 
 
+def apply_cfg(ctx: Context, pos, neg, scale, rescale, out=None):
+    """apply_cfg on fp32 CUDA tensors of the same shape."""
+    import torch
+
+    if out is None:
+        out = torch.empty_like(pos)
+    check(lib().s2_apply_cfg(ctx.handle, pos.data_ptr(), neg.data_ptr(), pos.numel(), float(scale), float(rescale),
+                             out.data_ptr()), "s2_apply_cfg")
+    return out
+
+
 class Dit:
     """s2_dit: the block stack (SeedVR2DiTBlocks' block graph) and its frontend / tail nets."""
 
@@ -519,6 +538,31 @@ class Dit:
                                              _floats(timesteps), len(video_shapes), ptr(video), video.shape[0],
                                              ptr(text), text.shape[0], ptr(prediction), ptr(text_out)),
               "s2_dit_forward_step_host")
+
+
+    def denoise(self, latent_shape, latent, condition, positive_text, negative_text=None, *, steps=1, cfg_scale=1.0,
+                cfg_rescale=0.0, latent_cstep=None, condition_cstep=None):
+        """SeedVR2Pipeline::denoise on the device: latent / condition fp32 CUDA [16, >= t*h*w] planes (latent
+        updated in place), texts fp32 CUDA [rows, 5120]."""
+        opt = DenoiseOptions(int(steps), float(cfg_scale), float(cfg_rescale))
+        check(lib().s2_dit_denoise(self.handle, _ints(latent_shape), latent.data_ptr(),
+                                   latent.stride(0) if latent_cstep is None else latent_cstep, condition.data_ptr(),
+                                   condition.stride(0) if condition_cstep is None else condition_cstep,
+                                   positive_text.data_ptr(), positive_text.shape[0], ptr(negative_text),
+                                   0 if negative_text is None else negative_text.shape[0], C.byref(opt)),
+              "s2_dit_denoise")
+        return latent
+
+    def denoise_host(self, latent_shape, latent, condition, positive_text, negative_text=None, *, steps=1,
+                     cfg_scale=1.0, cfg_rescale=0.0):
+        """Same with host numpy planes [16, cstep] (latent updated in place)."""
+        opt = DenoiseOptions(int(steps), float(cfg_scale), float(cfg_rescale))
+        check(lib().s2_dit_denoise_host(self.handle, _ints(latent_shape), ptr(latent), latent.shape[1],
+                                        ptr(condition), condition.shape[1], ptr(positive_text),
+                                        positive_text.shape[0], ptr(negative_text),
+                                        0 if negative_text is None else negative_text.shape[0], C.byref(opt)),
+              "s2_dit_denoise_host")
+        return latent
 
 
 def shard(video_shape, text_length, window, window_mode, rank, world, shifted=1) -> dict:

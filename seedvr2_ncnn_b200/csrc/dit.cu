@@ -259,6 +259,95 @@ int run_tail(s2_dit* d, const int* shape, const float* x, const float* mod0, con
     return r;
 }
 
+// Activations of one whole-DiT pass, carved out of io_ws: x [np + T][D] f32 |
+// patches bf16 [np][136] | text bf16 [T][5120] | h bf16 [np][D] | pp [np][64] |
+// tm [2][D] | temb [B][256] | e0, e1 [B][D] | emb [B][6][D] | `extra` bytes.
+struct StepWs
+{
+    float* x;
+    __nv_bfloat16 *patches, *tb, *h;
+    float *pp, *tm, *temb, *e0, *e1, *emb;
+    void* extra;
+};
+
+int step_workspace(s2_dit* d, int64_t np_max, int64_t nt_max, int batch, size_t extra, StepWs& w)
+{
+    const int D = d->cfg.hidden;
+    const size_t sz[11] = {align256((size_t)(np_max + nt_max) * D * 4),
+                           align256((size_t)np_max * s2::kPatchPitch * 2),
+                           align256((size_t)nt_max * s2::kTextChannels * 2),
+                           align256((size_t)np_max * D * 2),
+                           align256((size_t)np_max * s2::kPredFeatures * 4),
+                           align256((size_t)2 * D * 4),
+                           align256((size_t)batch * s2::kTimeFeatures * 4),
+                           align256((size_t)batch * D * 4),
+                           align256((size_t)batch * D * 4),
+                           align256((size_t)batch * 6 * D * 4),
+                           align256(extra)};
+    size_t total = 0;
+    for (size_t b : sz) total += b;
+    const int r = d->io_ws.ensure(total);
+    if (r != S2_OK) return r;
+    uint8_t* p = static_cast<uint8_t*>(d->io_ws.ptr);
+    void* at[11];
+    for (int i = 0; i < 11; i++) at[i] = p, p += sz[i];
+    w.x = static_cast<float*>(at[0]);
+    w.patches = static_cast<__nv_bfloat16*>(at[1]);
+    w.tb = static_cast<__nv_bfloat16*>(at[2]);
+    w.h = static_cast<__nv_bfloat16*>(at[3]);
+    w.pp = static_cast<float*>(at[4]);
+    w.tm = static_cast<float*>(at[5]);
+    w.temb = static_cast<float*>(at[6]);
+    w.e0 = static_cast<float*>(at[7]);
+    w.e1 = static_cast<float*>(at[8]);
+    w.emb = static_cast<float*>(at[9]);
+    w.extra = at[10];
+    return S2_OK;
+}
+
+// Where a sample's DiT video input comes from: [tokens][33] rows, or the
+// latent / condition planes SeedVR2Pipeline::predict assembles them from.
+struct PatchSrc
+{
+    const float* rows;
+    const float* latent;
+    int64_t latent_cstep;
+    const float* condition;
+    int64_t condition_cstep;
+};
+
+// One sample through frontend (token nets), all blocks and tail: shape = its
+// latent (t, h, w), mod = its [6][D] modulation; text_out may be null.
+int run_sample(s2_dit* d, const int* shp, const PatchSrc& src, const float* text, int nt, const float* mod,
+               float* prediction, float* text_out, const StepWs& w)
+{
+    s2::Context& c = d->ctx->c;
+    const int D = d->cfg.hidden;
+    const s2_dit::Io& io = d->io;
+    const int pshape[3] = {shp[0], shp[1] / 2, shp[2] / 2};
+    const int np = pshape[0] * pshape[1] * pshape[2];
+    // frontend: x = [video patches W_vid_in^T + b | text W_txt_in^T + b]
+    int r = src.rows ? s2::launch_patchify(c, src.rows, shp[0], shp[1], shp[2], w.patches, 1)
+                     : s2::launch_patchify_planar(c, src.latent, src.latent_cstep, src.condition, src.condition_cstep,
+                                                  shp[0], shp[1], shp[2], w.patches);
+    if (r == S2_OK)
+        r = s2::launch_shared_linear(c, np, 0, D, s2::kPatchPitch, w.patches, nullptr, io.w_vid_in, io.b_vid_in,
+                                     s2::EPI_STORE, nullptr, 1, w.x, nullptr);
+    if (r == S2_OK) r = s2::launch_convert_f32_bf16(c, text, w.tb, (int64_t)nt * s2::kTextChannels);
+    if (r == S2_OK)
+        r = s2::launch_shared_linear(c, nt, 0, D, s2::kTextChannels, w.tb, nullptr, io.w_txt_in, io.b_txt_in,
+                                     s2::EPI_STORE, nullptr, 1, w.x + (size_t)np * D, nullptr);
+    // all blocks, in place
+    if (r == S2_OK) r = s2_dit_forward(d, pshape, nt, w.x, mod);
+    // tail -> prediction tokens; text rows out
+    if (r == S2_OK) r = run_tail(d, shp, w.x, mod, mod + D, prediction, w.h, w.pp, w.tm);
+    if (r == S2_OK && text_out &&
+        cudaMemcpyAsync(text_out, w.x + (size_t)np * D, (size_t)nt * D * 4, cudaMemcpyDeviceToDevice, c.stream) !=
+            cudaSuccess)
+        r = S2_ERR_CUDA;
+    return r;
+}
+
 } // namespace
 
 extern "C" {
@@ -945,7 +1034,6 @@ int s2_dit_forward_step(s2_dit* d, const int* video_shapes, const int* text_leng
     s2::Context& c = d->ctx->c;
     if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
     const int D = d->cfg.hidden;
-    const s2_dit::Io& io = d->io;
     int64_t np_max = 0, nt_max = 0;
     for (int s = 0; s < batch; s++)
     {
@@ -953,62 +1041,19 @@ int s2_dit_forward_step(s2_dit* d, const int* video_shapes, const int* text_leng
         np_max = std::max(np_max, (int64_t)shp[0] * (shp[1] / 2) * (shp[2] / 2));
         nt_max = std::max(nt_max, (int64_t)text_lengths[s]);
     }
-    // workspace: x [np + T][D] f32 | patches bf16 [np][136] | text bf16 [T][5120] |
-    //            h bf16 [np][D] | pp [np][64] f32 | tm [2][D] | temb [B][256] | e0, e1 [B][D] | emb [B][6][D]
-    const size_t sz_x = align256((size_t)(np_max + nt_max) * D * 4),
-                 sz_p = align256((size_t)np_max * s2::kPatchPitch * 2),
-                 sz_t = align256((size_t)nt_max * s2::kTextChannels * 2), sz_h = align256((size_t)np_max * D * 2),
-                 sz_pp = align256((size_t)np_max * s2::kPredFeatures * 4), sz_tm = align256((size_t)2 * D * 4),
-                 sz_e = align256((size_t)batch * (s2::kTimeFeatures + 2 * D) * 4),
-                 sz_m = align256((size_t)batch * 6 * D * 4);
-    if ((r = d->io_ws.ensure(sz_x + sz_p + sz_t + sz_h + sz_pp + sz_tm + sz_e + sz_m)) != S2_OK) return r;
-    uint8_t* ws = static_cast<uint8_t*>(d->io_ws.ptr);
-    float* x = reinterpret_cast<float*>(ws);
-    ws += sz_x;
-    __nv_bfloat16* patches = reinterpret_cast<__nv_bfloat16*>(ws);
-    ws += sz_p;
-    __nv_bfloat16* tb = reinterpret_cast<__nv_bfloat16*>(ws);
-    ws += sz_t;
-    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(ws);
-    ws += sz_h;
-    float* pp = reinterpret_cast<float*>(ws);
-    ws += sz_pp;
-    float* tm = reinterpret_cast<float*>(ws);
-    ws += sz_tm;
-    float* temb = reinterpret_cast<float*>(ws);
-    float* e0 = temb + (size_t)batch * s2::kTimeFeatures;
-    float* e1 = e0 + (size_t)batch * D;
-    ws += sz_e;
-    float* emb = reinterpret_cast<float*>(ws);
-
+    StepWs w;
+    if ((r = step_workspace(d, np_max, nt_max, batch, 0, w)) != S2_OK) return r;
     // timestep MLP of every sample at once; per sample [6][D]
-    if ((r = run_emb(d, timesteps, batch, temb, e0, e1, emb, false)) != S2_OK) return r;
+    if ((r = run_emb(d, timesteps, batch, w.temb, w.e0, w.e1, w.emb, false)) != S2_OK) return r;
     int64_t v_off = 0, t_off = 0;
     for (int s = 0; s < batch && r == S2_OK; s++)
     {
         const int* shp = video_shapes + 3 * s;
-        const int pshape[3] = {shp[0], shp[1] / 2, shp[2] / 2};
-        const int np = pshape[0] * pshape[1] * pshape[2], nt = text_lengths[s];
-        const float* mod = emb + (size_t)s * 6 * D;
-        // frontend: x = [video patches W_vid_in^T + b | text W_txt_in^T + b]
-        r = s2::launch_patchify(c, video + v_off * s2::kLatentChannels, shp[0], shp[1], shp[2], patches, 1);
-        if (r == S2_OK)
-            r = s2::launch_shared_linear(c, np, 0, D, s2::kPatchPitch, patches, nullptr, io.w_vid_in, io.b_vid_in,
-                                         s2::EPI_STORE, nullptr, 1, x, nullptr);
-        if (r == S2_OK)
-            r = s2::launch_convert_f32_bf16(c, text + t_off * s2::kTextChannels, tb, (int64_t)nt * s2::kTextChannels);
-        if (r == S2_OK)
-            r = s2::launch_shared_linear(c, nt, 0, D, s2::kTextChannels, tb, nullptr, io.w_txt_in, io.b_txt_in,
-                                         s2::EPI_STORE, nullptr, 1, x + (size_t)np * D, nullptr);
-        // all blocks, in place
-        if (r == S2_OK) r = s2_dit_forward(d, pshape, nt, x, mod);
-        // tail -> prediction tokens; text rows out
-        if (r == S2_OK) r = run_tail(d, shp, x, mod, mod + D, prediction + v_off * s2::kPredChannels, h, pp, tm);
-        if (r == S2_OK && cudaMemcpyAsync(text_out + t_off * D, x + (size_t)np * D, (size_t)nt * D * 4,
-                                          cudaMemcpyDeviceToDevice, c.stream) != cudaSuccess)
-            r = S2_ERR_CUDA;
+        const PatchSrc src = {video + v_off * s2::kLatentChannels, nullptr, 0, nullptr, 0};
+        r = run_sample(d, shp, src, text + t_off * s2::kTextChannels, text_lengths[s], w.emb + (size_t)s * 6 * D,
+                       prediction + v_off * s2::kPredChannels, text_out + t_off * D, w);
         v_off += (int64_t)shp[0] * shp[1] * shp[2];
-        t_off += nt;
+        t_off += text_lengths[s];
     }
     return r;
 }
@@ -1042,6 +1087,114 @@ int s2_dit_forward_step_host(s2_dit* d, const int* video_shapes, const int* text
     if (cudaMemcpyAsync(prediction, dp, (size_t)video_rows * s2::kPredChannels * 4, cudaMemcpyDeviceToHost,
                         c.stream) != cudaSuccess ||
         cudaMemcpyAsync(text_out, dto, (size_t)text_rows * D * 4, cudaMemcpyDeviceToHost, c.stream) != cudaSuccess)
+        return S2_ERR_CUDA;
+    return cudaStreamSynchronize(c.stream) == cudaSuccess ? S2_OK : S2_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------- denoise loop
+int s2_apply_cfg(s2_context* ctx, const float* pos, const float* neg, int64_t count, float scale, float rescale,
+                 float* out)
+{
+    if (!ctx || !pos || !neg || !out || count <= 0) return S2_ERR_INVALID;
+    s2::Context& c = ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    s2::DeviceBuffer& scratch = c.ws[3];
+    int r = scratch.ensure(s2::cfg_scratch_bytes());
+    if (r != S2_OK) return r;
+    return s2::launch_apply_cfg(c, pos, neg, count, scale, rescale, out, scratch.ptr, 1, nullptr);
+}
+
+int s2_dit_denoise(s2_dit* d, const int* latent_shape, float* latent, int64_t latent_cstep, const float* condition,
+                   int64_t condition_cstep, const float* positive_text, int positive_rows, const float* negative_text,
+                   int negative_rows, const s2_denoise_options* opt)
+{
+    // restore()'s checks (seedvr2_pipeline.cpp:337-340) and predict()'s
+    // is_latent / is_text (:14-26, :289-292)
+    if (!d || !d->io_loaded || !latent_shape || !latent || !condition || !positive_text || !opt || opt->steps <= 0 ||
+        positive_rows <= 0)
+        return S2_ERR_INVALID;
+    const bool cfg = opt->cfg_scale != 1.f;
+    if (cfg && (!negative_text || negative_rows <= 0)) return S2_ERR_INVALID;
+    const int T = latent_shape[0], H = latent_shape[1], W = latent_shape[2];
+    if (T <= 0 || H <= 0 || W <= 0 || (H & 1) || (W & 1)) return S2_ERR_INVALID;
+    const int64_t tokens = (int64_t)T * H * W;
+    if (tokens > 0x7fffffff || latent_cstep < tokens || condition_cstep < tokens) return S2_ERR_INVALID;
+    s2::Context& c = d->ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    const int64_t n16 = tokens * s2::kPredChannels;
+    const size_t pred_bytes = align256((size_t)n16 * 4);
+    StepWs w;
+    int r = step_workspace(d, tokens / 4, std::max(positive_rows, cfg ? negative_rows : 0), 1,
+                           3 * pred_bytes + s2::cfg_scratch_bytes(), w);
+    if (r != S2_OK) return r;
+    float* pos = static_cast<float*>(w.extra);
+    float* neg = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(pos) + pred_bytes);
+    float* guided = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(neg) + pred_bytes);
+    void* scratch = reinterpret_cast<uint8_t*>(guided) + pred_bytes;
+    const PatchSrc src = {nullptr, latent, latent_cstep, condition, condition_cstep};
+    for (int step = 0; step < opt->steps && r == S2_OK; step++)
+    {
+        // the schedule of SeedVR2Pipeline::denoise (:542-545), same fp32 expressions
+        const float timestep = 1000.f * (opt->steps - step) / opt->steps;
+        const float next_timestep = 1000.f * (opt->steps - step - 1) / opt->steps;
+        const float delta = (next_timestep - timestep) / 1000.f;
+        r = run_emb(d, &timestep, 1, w.temb, w.e0, w.e1, w.emb, false);
+        if (r == S2_OK) r = run_sample(d, latent_shape, src, positive_text, positive_rows, w.emb, pos, nullptr, w);
+        const float* pred = pos;
+        const float* factor = nullptr;
+        if (r == S2_OK && cfg)
+        {
+            r = run_sample(d, latent_shape, src, negative_text, negative_rows, w.emb, neg, nullptr, w);
+            if (r == S2_OK)
+                r = s2::launch_apply_cfg(c, pos, neg, n16, opt->cfg_scale, opt->cfg_rescale, guided, scratch, 0,
+                                         &factor);
+            pred = guided;
+        }
+        if (r == S2_OK) r = s2::launch_euler(c, latent, latent_cstep, tokens, pred, factor, delta);
+    }
+    return r;
+}
+
+int s2_dit_denoise_host(s2_dit* d, const int* latent_shape, float* latent, int64_t latent_cstep,
+                        const float* condition, int64_t condition_cstep, const float* positive_text,
+                        int positive_rows, const float* negative_text, int negative_rows,
+                        const s2_denoise_options* opt)
+{
+    if (!d || !d->io_loaded || !latent_shape || !latent || !condition || !positive_text || !opt || opt->steps <= 0 ||
+        positive_rows <= 0)
+        return S2_ERR_INVALID;
+    const bool cfg = opt->cfg_scale != 1.f;
+    if (cfg && (!negative_text || negative_rows <= 0)) return S2_ERR_INVALID;
+    const int T = latent_shape[0], H = latent_shape[1], W = latent_shape[2];
+    if (T <= 0 || H <= 0 || W <= 0) return S2_ERR_INVALID;
+    const int64_t tokens = (int64_t)T * H * W;
+    if (latent_cstep < tokens || condition_cstep < tokens) return S2_ERR_INVALID;
+    s2::Context& c = d->ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    const size_t plane = (size_t)tokens * 4, planes = align256(plane * s2::kPredChannels);
+    const size_t bp = align256((size_t)positive_rows * s2::kTextChannels * 4),
+                 bn = cfg ? align256((size_t)negative_rows * s2::kTextChannels * 4) : 0;
+    int r = d->io_host.ensure(2 * planes + bp + bn);
+    if (r != S2_OK) return r;
+    uint8_t* p = static_cast<uint8_t*>(d->io_host.ptr);
+    float* dl = reinterpret_cast<float*>(p);
+    float* dc = reinterpret_cast<float*>(p + planes);
+    float* dp = reinterpret_cast<float*>(p + 2 * planes);
+    float* dn = cfg ? reinterpret_cast<float*>(p + 2 * planes + bp) : nullptr;
+    // 16 planes each, host plane stride cstep -> dense device planes
+    if (cudaMemcpy2DAsync(dl, plane, latent, (size_t)latent_cstep * 4, plane, s2::kPredChannels,
+                          cudaMemcpyHostToDevice, c.stream) != cudaSuccess ||
+        cudaMemcpy2DAsync(dc, plane, condition, (size_t)condition_cstep * 4, plane, s2::kPredChannels,
+                          cudaMemcpyHostToDevice, c.stream) != cudaSuccess ||
+        cudaMemcpyAsync(dp, positive_text, (size_t)positive_rows * s2::kTextChannels * 4, cudaMemcpyHostToDevice,
+                        c.stream) != cudaSuccess ||
+        (cfg && cudaMemcpyAsync(dn, negative_text, (size_t)negative_rows * s2::kTextChannels * 4,
+                                cudaMemcpyHostToDevice, c.stream) != cudaSuccess))
+        return S2_ERR_CUDA;
+    r = s2_dit_denoise(d, latent_shape, dl, tokens, dc, tokens, dp, positive_rows, dn, negative_rows, opt);
+    if (r != S2_OK) return r;
+    if (cudaMemcpy2DAsync(latent, (size_t)latent_cstep * 4, dl, plane, plane, s2::kPredChannels,
+                          cudaMemcpyDeviceToHost, c.stream) != cudaSuccess)
         return S2_ERR_CUDA;
     return cudaStreamSynchronize(c.stream) == cudaSuccess ? S2_OK : S2_ERR_CUDA;
 }

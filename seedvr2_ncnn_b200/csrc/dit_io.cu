@@ -32,9 +32,28 @@ inline int grid_for(const Context& ctx, int64_t items, int threads)
 // (frame, 2py + y, 2px + x) of src, 33 channels each, in (y, x) order.
 // BF16: rows of kPatchPitch bf16 with zeros after the 132 features (the GEMM
 // operand of the video input projection); otherwise rows of 132 fp32.
+// Token rows of the DiT video input: either [tokens][33] rows (rows != null)
+// or, fused with SeedVR2Pipeline::predict's assembly (seedvr2_pipeline.cpp:
+// 296-318), channel c < 16 of latent plane c, 16 <= c < 32 of condition plane
+// c - 16, and c = 32 the constant 1.
+struct PatchSource
+{
+    const float* rows;
+    const float* latent;
+    int64_t latent_cstep;
+    const float* condition;
+    int64_t condition_cstep;
+    __device__ __forceinline__ float at(int64_t tok, int c) const
+    {
+        if (rows) return __ldg(rows + tok * kLatentChannels + c);
+        if (c < kPredChannels) return __ldg(latent + c * latent_cstep + tok);
+        if (c < 2 * kPredChannels) return __ldg(condition + (c - kPredChannels) * condition_cstep + tok);
+        return 1.f;
+    }
+};
+
 template <bool BF16>
-__global__ void patchify_kernel(const float* __restrict__ src, int T, int H, int W, void* __restrict__ dst,
-                                int out_w)
+__global__ void patchify_kernel(const PatchSource src, int T, int H, int W, void* __restrict__ dst, int out_w)
 {
     const int ph = H >> 1, pw = W >> 1;
     const int64_t per_frame = (int64_t)ph * pw;
@@ -52,7 +71,7 @@ __global__ void patchify_kernel(const float* __restrict__ src, int T, int H, int
             const int rem = (int)(p - fr * per_frame);
             const int py = rem / pw, px = rem - py * pw;
             const int64_t tok = (fr * H + 2 * py + (q >> 1)) * (int64_t)W + 2 * px + (q & 1);
-            v = __ldg(src + tok * kLatentChannels + c);
+            v = src.at(tok, c);
         }
         if (BF16)
             static_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16_rn(v);
@@ -157,6 +176,119 @@ __global__ void __launch_bounds__(256) gemv_kernel(const __nv_bfloat16* __restri
     }
 }
 
+// apply_cfg (seedvr2_pipeline.cpp:171-210), deterministic two-level double
+// reductions (per-block partials in a fixed grid, summed in block order by one
+// block):
+//   combine: cfg = neg + scale * (pos - neg) (no contraction, as the reference),
+//            partial sums of pos and cfg;
+//   PASS 0 finish: means; deviations: partial sums of squared deviations;
+//   PASS 1 finish: factor = float(rescale * std(pos) / std(cfg) + (1 - rescale)),
+//            1 when std(cfg) == 0.
+constexpr int kCfgBlocks = 512;
+constexpr int kCfgThreads = 256;
+
+__device__ __forceinline__ double2 block_sum2(double a, double b)
+{
+    __shared__ double sa[kCfgThreads / 32], sb[kCfgThreads / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+    {
+        a += __shfl_xor_sync(0xffffffffu, a, o);
+        b += __shfl_xor_sync(0xffffffffu, b, o);
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) sa[w] = a, sb[w] = b;
+    __syncthreads();
+    double2 r = make_double2(0.0, 0.0);
+    if (threadIdx.x == 0)
+        for (int i = 0; i < kCfgThreads / 32; i++) r.x += sa[i], r.y += sb[i];
+    return r;
+}
+
+__global__ void __launch_bounds__(kCfgThreads) cfg_combine_kernel(const float* __restrict__ pos,
+                                                                  const float* __restrict__ neg, int64_t n,
+                                                                  float scale, float* __restrict__ out,
+                                                                  double2* __restrict__ partial)
+{
+    double sp = 0.0, sc = 0.0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    {
+        const float p = pos[i], q = neg[i];
+        const float c = __fadd_rn(q, __fmul_rn(scale, __fsub_rn(p, q)));
+        out[i] = c;
+        sp += (double)p;
+        sc += (double)c;
+    }
+    if (!partial) return;
+    const double2 r = block_sum2(sp, sc);
+    if (threadIdx.x == 0) partial[blockIdx.x] = r;
+}
+
+__global__ void __launch_bounds__(kCfgThreads) cfg_deviation_kernel(const float* __restrict__ pos,
+                                                                    const float* __restrict__ cfg, int64_t n,
+                                                                    const double* __restrict__ means,
+                                                                    double2* __restrict__ partial)
+{
+    const double pm = means[0], cm = means[1];
+    double vp = 0.0, vc = 0.0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    {
+        const double p = (double)pos[i] - pm, c = (double)cfg[i] - cm;
+        vp = __dadd_rn(vp, __dmul_rn(p, p));
+        vc = __dadd_rn(vc, __dmul_rn(c, c));
+    }
+    const double2 r = block_sum2(vp, vc);
+    if (threadIdx.x == 0) partial[blockIdx.x] = r;
+}
+
+template <int PASS>
+__global__ void __launch_bounds__(kCfgThreads) cfg_finish_kernel(const double2* __restrict__ partial, int blocks,
+                                                                 int64_t n, float rescale, double* __restrict__ means,
+                                                                 float* __restrict__ factor)
+{
+    double a = 0.0, b = 0.0;
+    for (int i = threadIdx.x; i < blocks; i += blockDim.x) a += partial[i].x, b += partial[i].y;
+    const double2 r = block_sum2(a, b);
+    if (threadIdx.x != 0) return;
+    if (PASS == 0)
+    {
+        means[0] = r.x / (double)n;
+        means[1] = r.y / (double)n;
+    }
+    else
+    {
+        const double pos_std = sqrt(r.x / (double)(n - 1));
+        const double cfg_std = sqrt(r.y / (double)(n - 1));
+        *factor = cfg_std == 0.0 ? 1.f : (float)((double)rescale * pos_std / cfg_std + (double)(1.f - rescale));
+    }
+}
+
+__global__ void scale_kernel(float* __restrict__ x, int64_t n, const float* __restrict__ factor)
+{
+    const float f = *factor;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        x[i] = __fmul_rn(x[i], f);
+}
+
+// Euler step of SeedVR2Pipeline::denoise (seedvr2_pipeline.cpp:572-586):
+// latent[c][t] += delta * (pred[t][c] * factor), factor from apply_cfg's
+// rescale (null: none); products and sums rounded separately, as the reference.
+__global__ void euler_kernel(float* __restrict__ latent, int64_t cstep, int64_t tokens,
+                             const float* __restrict__ pred, const float* __restrict__ factor, float delta)
+{
+    const float f = factor ? *factor : 1.f;
+    const int64_t n = tokens * kPredChannels;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    {
+        const int c = (int)(i / tokens);
+        const int64_t t = i - (int64_t)c * tokens;
+        float v = __ldg(pred + t * kPredChannels + c);
+        if (factor) v = __fmul_rn(v, f);
+        float* l = latent + c * cstep + t;
+        *l = __fadd_rn(*l, __fmul_rn(delta, v));
+    }
+}
+
 } // namespace
 
 int patchify_rows(const int* shapes, int batch, int rows, int64_t* patches)
@@ -205,10 +337,69 @@ int launch_patchify(Context& ctx, const float* src, int T, int H, int W, void* d
     const int64_t total = patches * out_w;
     ProfileScope prof(ctx, K_OTHER, 0.0, (double)patches * (kPatchFeatures * 4.0 + out_w * (bf16_out ? 2.0 : 4.0)));
     const int grid = grid_for(ctx, total, 256);
+    const PatchSource ps = {src, nullptr, 0, nullptr, 0};
     if (bf16_out)
-        patchify_kernel<true><<<grid, 256, 0, ctx.stream>>>(src, T, H, W, dst, out_w);
+        patchify_kernel<true><<<grid, 256, 0, ctx.stream>>>(ps, T, H, W, dst, out_w);
     else
-        patchify_kernel<false><<<grid, 256, 0, ctx.stream>>>(src, T, H, W, dst, out_w);
+        patchify_kernel<false><<<grid, 256, 0, ctx.stream>>>(ps, T, H, W, dst, out_w);
+    return launched(ctx);
+}
+
+int launch_patchify_planar(Context& ctx, const float* latent, int64_t latent_cstep, const float* condition,
+                           int64_t condition_cstep, int T, int H, int W, void* dst)
+{
+    if (T <= 0 || H <= 0 || W <= 0 || (H & 1) || (W & 1) || !latent || !condition || !dst) return S2_ERR_INVALID;
+    const int64_t tokens = (int64_t)T * H * W;
+    if (latent_cstep < tokens || condition_cstep < tokens) return S2_ERR_INVALID;
+    const int64_t patches = tokens / 4;
+    ProfileScope prof(ctx, K_OTHER, 0.0, (double)tokens * 32 * 4.0 + (double)patches * kPatchPitch * 2.0);
+    const int grid = grid_for(ctx, patches * kPatchPitch, 256);
+    const PatchSource ps = {nullptr, latent, latent_cstep, condition, condition_cstep};
+    patchify_kernel<true><<<grid, 256, 0, ctx.stream>>>(ps, T, H, W, dst, kPatchPitch);
+    return launched(ctx);
+}
+
+size_t cfg_scratch_bytes()
+{
+    return (size_t)kCfgBlocks * sizeof(double2) + 2 * sizeof(double) + 16;
+}
+
+int launch_apply_cfg(Context& ctx, const float* pos, const float* neg, int64_t n, float scale, float rescale,
+                     float* out, void* scratch, int apply_factor, const float** factor_out)
+{
+    if (n <= 0 || !pos || !neg || !out || !scratch) return S2_ERR_INVALID;
+    double2* partial = static_cast<double2*>(scratch);
+    double* means = reinterpret_cast<double*>(partial + kCfgBlocks);
+    float* factor = reinterpret_cast<float*>(means + 2);
+    const bool rescaled = rescale != 0.f && n >= 2;
+    if (factor_out) *factor_out = rescaled ? factor : nullptr;
+    int64_t b = (n + kCfgThreads - 1) / kCfgThreads;
+    const int blocks = (int)(b < kCfgBlocks ? b : kCfgBlocks);
+    ProfileScope prof(ctx, K_OTHER, 0.0, (double)n * (rescaled ? 24.0 : 12.0));
+    cfg_combine_kernel<<<blocks, kCfgThreads, 0, ctx.stream>>>(pos, neg, n, scale, out, rescaled ? partial : nullptr);
+    int r = launched(ctx);
+    if (r != S2_OK || !rescaled) return r;
+    cfg_finish_kernel<0><<<1, kCfgThreads, 0, ctx.stream>>>(partial, blocks, n, rescale, means, factor);
+    if ((r = launched(ctx)) != S2_OK) return r;
+    cfg_deviation_kernel<<<blocks, kCfgThreads, 0, ctx.stream>>>(pos, out, n, means, partial);
+    if ((r = launched(ctx)) != S2_OK) return r;
+    cfg_finish_kernel<1><<<1, kCfgThreads, 0, ctx.stream>>>(partial, blocks, n, rescale, means, factor);
+    if ((r = launched(ctx)) != S2_OK) return r;
+    if (apply_factor)
+    {
+        scale_kernel<<<grid_for(ctx, n, 256), 256, 0, ctx.stream>>>(out, n, factor);
+        r = launched(ctx);
+    }
+    return r;
+}
+
+int launch_euler(Context& ctx, float* latent, int64_t cstep, int64_t tokens, const float* pred, const float* factor,
+                 float delta)
+{
+    if (tokens <= 0 || cstep < tokens || !latent || !pred) return S2_ERR_INVALID;
+    ProfileScope prof(ctx, K_OTHER, 0.0, (double)tokens * kPredChannels * 12.0);
+    euler_kernel<<<grid_for(ctx, tokens * kPredChannels, 256), 256, 0, ctx.stream>>>(latent, cstep, tokens, pred,
+                                                                                      factor, delta);
     return launched(ctx);
 }
 

@@ -41,6 +41,7 @@ enum
     WS_QKV_PACKED = 0, // AWA: packed bf16 Q, K, V
     WS_TEXT_PARTIAL = 1,
     WS_DIT = 2, // DiT forward activations
+    WS_CFG = 3, // apply_cfg reduction scratch (s2_apply_cfg, dit.cu)
 };
 
 } // namespace

@@ -212,6 +212,19 @@ int unpatchify_rows(const int* shapes, int batch, int rows, int64_t* tokens);
 // [T][H][W][33] fp32 latent tokens of one sample -> patches: fp32 rows of 132
 // (bf16_out = 0) or bf16 rows of kPatchPitch with zero padding (bf16_out = 1)
 int launch_patchify(Context& ctx, const float* src, int T, int H, int W, void* dst, int bf16_out);
+// Fused SeedVR2Pipeline::predict assembly + patchify: 16 latent planes, 16
+// condition planes and a constant 1 per token -> bf16 patch rows of kPatchPitch
+int launch_patchify_planar(Context& ctx, const float* latent, int64_t latent_cstep, const float* condition,
+                           int64_t condition_cstep, int T, int H, int W, void* dst);
+// apply_cfg: out = neg + scale (pos - neg), and with rescale != 0 (n >= 2) the
+// rescale factor on the device (*factor_out; null when there is none), applied
+// to out when apply_factor.  scratch: cfg_scratch_bytes() device bytes.
+size_t cfg_scratch_bytes();
+int launch_apply_cfg(Context& ctx, const float* pos, const float* neg, int64_t n, float scale, float rescale,
+                     float* out, void* scratch, int apply_factor, const float** factor_out);
+// latent[c][t] += delta * pred[t][c] * (*factor, if given)
+int launch_euler(Context& ctx, float* latent, int64_t cstep, int64_t tokens, const float* pred, const float* factor,
+                 float delta);
 // [patches][64] fp32 -> [T][H][W][16] fp32 (16-byte aligned buffers)
 int launch_unpatchify(Context& ctx, const float* src, int T, int H, int W, float* dst);
 // host timesteps -> [batch][256] fp32 device

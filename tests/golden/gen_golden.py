@@ -134,6 +134,10 @@ DIT_IO_ERRORS = [
 ]
 
 
+# apply_cfg cases: (rows of 16, scale, rescale)
+CFG_CASES = [(96, 6.5, 0.0), (96, 6.5, 0.7), (1, 3.0, 1.0), (500, 1.5, 0.3)]
+
+
 def _code(fn) -> int:
     try:
         fn()
@@ -166,6 +170,13 @@ def gen_dit_io(refio: oracle.RefIO) -> None:
             codes.append(_code(lambda: refio.unpatchify_prediction(np.zeros((max(rows, 1), 64), np.float32), shapes,
                                                                     rows)))
     out["error_codes"] = np.asarray(codes, np.int32)
+    # apply_cfg (seedvr2_pipeline.cpp:171-210) on [tokens][16] predictions
+    for i, (rows, scale, rescale) in enumerate(CFG_CASES):
+        pos = rng.standard_normal((rows, 16)).astype(np.float32)
+        neg = (0.5 * pos + rng.standard_normal((rows, 16))).astype(np.float32)
+        out[f"cfg{i}__pos"] = pos
+        out[f"cfg{i}__neg"] = neg
+        out[f"cfg{i}__out"] = refio.apply_cfg(pos, neg, scale, rescale)
     np.savez_compressed(os.path.join(OUT, "dit_io.npz"), **out)
 
 

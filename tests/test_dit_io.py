@@ -100,3 +100,47 @@ def test_frontend_tail_restatement_shapes(port):
     bias = io["b_out"].reshape(4, 16)
     for q, tok in enumerate([0, 1, 6, 7]):
         assert np.allclose(pred[tok], bias[q])
+
+
+# ---- denoise loop pieces (src/seedvr2/seedvr2_pipeline.cpp) ----
+def test_port_apply_cfg_matches_golden(port, golden):
+    from tests.golden.gen_golden import CFG_CASES
+
+    g = golden["dit_io"]
+    for i, (_, scale, rescale) in enumerate(CFG_CASES):
+        got = port.apply_cfg(g[f"cfg{i}__pos"], g[f"cfg{i}__neg"], scale, rescale)
+        assert np.array_equal(_bits(got), _bits(g[f"cfg{i}__out"])), i
+
+
+def test_port_apply_cfg_vs_reference_random(port, refio):
+    rng = np.random.default_rng(12)
+    for _ in range(20):
+        rows = int(rng.integers(1, 300))
+        pos = rng.standard_normal((rows, 16)).astype(np.float32)
+        neg = rng.standard_normal((rows, 16)).astype(np.float32)
+        scale, rescale = float(rng.uniform(1, 8)), float(rng.choice([0.0, rng.uniform(0, 1)]))
+        assert np.array_equal(_bits(port.apply_cfg(pos, neg, scale, rescale)),
+                              _bits(refio.apply_cfg(pos, neg, scale, rescale)))
+    # a constant guided prediction (std 0) is left as is
+    one = np.ones((4, 16), np.float32)
+    assert np.array_equal(port.apply_cfg(one, one, 2.0, 0.5), one)
+
+
+def test_denoise_schedule_and_assembly(port):
+    """Timesteps 1000 * (n - s) / n in fp32 and deltas to the next one; the DiT input row is
+    [latent 16 | condition 16 | 1]."""
+    for n in (1, 3, 7, 50):
+        ts = [port.denoise_schedule(n, s) for s in range(n)]
+        assert ts[0][0] == 1000.0
+        assert all(np.float32(t) == np.float32(np.float32(1000.0) * np.float32(n - s) / np.float32(n))
+                   for s, (t, _) in enumerate(ts))
+        assert abs(sum(d for _, d in ts) + 1.0) < 1e-5
+    rng = np.random.default_rng(3)
+    lat = rng.standard_normal((16, 40)).astype(np.float32)
+    cond = rng.standard_normal((16, 40)).astype(np.float32)
+    rows = port.assemble_dit_input(lat, cond)
+    assert np.array_equal(rows[:, :16], lat.T) and np.array_equal(rows[:, 16:32], cond.T)
+    assert (rows[:, 32] == 1).all()
+    pred = rng.standard_normal((40, 16)).astype(np.float32)
+    upd = port.euler_update(lat, pred, np.float32(-0.25))
+    assert np.array_equal(upd, lat + np.float32(-0.25) * pred.T)

@@ -225,3 +225,113 @@ def test_dit_step_vs_oracle_chain(gpu_ctx, s2lib, port):
     assert cosine(got_p, ref_p) >= 0.9995 and rel_maxabs(got_p, ref_p) <= 2e-2
     assert cosine(got_t, ref_t) >= 0.9995 and rel_maxabs(got_t, ref_t) <= 2e-2
     dit.close()
+
+
+# ---- denoise loop (SeedVR2Pipeline::denoise / predict / apply_cfg) ----
+def test_apply_cfg_golden(gpu_ctx, s2lib, golden):
+    """The combine is bit-exact; with rescale the factor's double sums run in a different order than
+    the reference's sequential loop, so allow 2 ulp."""
+    import torch
+
+    from tests.golden.gen_golden import CFG_CASES
+
+    g = golden["dit_io"]
+    for i, (_, scale, rescale) in enumerate(CFG_CASES):
+        got = s2lib.apply_cfg(gpu_ctx, torch.from_numpy(g[f"cfg{i}__pos"]).cuda(),
+                              torch.from_numpy(g[f"cfg{i}__neg"]).cuda(), scale, rescale)
+        torch.cuda.synchronize()
+        got, ref = got.cpu().numpy(), g[f"cfg{i}__out"]
+        if rescale == 0.0:
+            assert np.array_equal(_bits(got), _bits(ref)), i
+        else:
+            assert (np.abs(got - ref) <= 2 * np.spacing(np.abs(ref))).all(), i
+
+
+def _oracle_predict(port, io, ws, shape, texts, D, heads, F, window):
+    def predict(rows, t, positive):
+        text = texts[0] if positive else texts[1]
+        rv, rt, rmod = port.frontend_forward(io, [shape], [t], rows, text)
+        pshape = [shape[0], shape[1] // 2, shape[2] // 2]
+        xv, xt = rv, rt
+        for b, w in enumerate(ws):
+            wo = dict(w)
+            wo["freqs"] = wo.pop("rope_freqs")
+            dims = [D, heads, 128, F, 21, 1, window[0], window[1], window[2], b & 1]
+            xv, xt = port.block_forward(dims=dims, eps_norm=1e-5, eps_qk=1e-5, weights=wo, modulation=rmod[:, 0][None],
+                                        shapes=[pshape], text_lengths=[text.shape[0]], x_video=xv, x_text=xt)
+        return port.tail_forward(io, [shape], xv, rmod)
+
+    return predict
+
+
+@pytest.mark.parametrize("steps,cfg_scale,cfg_rescale", [(2, 3.0, 0.5), (1, 1.0, 0.0)])
+def test_denoise_vs_oracle(gpu_ctx, s2lib, port, steps, cfg_scale, cfg_rescale):
+    """Whole denoise loop at reduced width (D = 256, 2 blocks) on padded channel planes (cstep > t*h*w,
+    the ncnn Mat layout): the latent update matches the oracle's loop (the block gate on the change),
+    the padding is untouched, and the host-buffer call matches the device call bit for bit."""
+    import torch
+
+    from tests.test_gpu_block import make_block_weights
+
+    D, heads, F, window = 256, 2, 1024, (1, 8, 8)
+    shape = [2, 16, 24]
+    tokens = int(np.prod(shape))
+    cstep = tokens + 8
+    rng = np.random.default_rng(41)
+    io = make_io_weights(rng, port, D)
+    ws = [make_block_weights(rng, D, F, 128, 21) for _ in range(2)]
+    dit = s2lib.Dit(gpu_ctx, num_blocks=2, hidden=D, heads=heads, head_dim=128, mlp_hidden=F, rope_pairs=21,
+                    window=window, window_mode=s2lib.S2_WINDOW_EXTENT)
+    dit.set_io_weights(io)
+    for b, w in enumerate(ws):
+        dit.set_block_weights(b, w)
+    latent = rng.standard_normal((16, cstep)).astype(np.float32)
+    cond = rng.standard_normal((16, cstep)).astype(np.float32)
+    ptext = rng.standard_normal((7, 5120)).astype(np.float32)
+    ntext = rng.standard_normal((5, 5120)).astype(np.float32)
+    use_neg = cfg_scale != 1.0
+    dl = torch.from_numpy(latent).cuda()
+    dit.denoise(shape, dl, torch.from_numpy(cond).cuda(), torch.from_numpy(ptext).cuda(),
+                torch.from_numpy(ntext).cuda() if use_neg else None, steps=steps, cfg_scale=cfg_scale,
+                cfg_rescale=cfg_rescale)
+    torch.cuda.synchronize()
+    assert gpu_ctx.status() == 0
+    got = dl.cpu().numpy()
+    host = latent.copy()
+    dit.denoise_host(shape, host, cond, ptext, ntext if use_neg else None, steps=steps, cfg_scale=cfg_scale,
+                     cfg_rescale=cfg_rescale)
+    assert np.array_equal(_bits(host), _bits(got))
+    assert np.array_equal(_bits(got[:, tokens:]), _bits(latent[:, tokens:]))
+
+    predict = _oracle_predict(port, io, ws, shape, (ptext, ntext), D, heads, F, window)
+    ref = port.denoise(predict, latent[:, :tokens], cond[:, :tokens], steps, cfg_scale, cfg_rescale)
+    d_got, d_ref = got[:, :tokens] - latent[:, :tokens], ref - latent[:, :tokens]
+    assert cosine(d_got, d_ref) >= 0.9995 and rel_maxabs(d_got, d_ref) <= 2e-2
+    dit.close()
+
+
+def test_denoise_rejects_bad_options(gpu_ctx, s2lib):
+    import torch
+
+    dit = s2lib.Dit(gpu_ctx, num_blocks=1, hidden=256, heads=2, head_dim=128, mlp_hidden=1024,
+                    window=(1, 8, 8), window_mode=s2lib.S2_WINDOW_EXTENT)
+    dit.init_random(5)
+    lat = torch.zeros((16, 64), device="cuda")
+    txt = torch.zeros((3, 5120), device="cuda")
+    L = s2lib.lib()
+
+    def call(shape, steps, scale, neg=None, cstep=64):
+        import ctypes
+
+        opt = s2lib.DenoiseOptions(steps, scale, 0.0)
+        return L.s2_dit_denoise(dit.handle, s2lib._ints(shape), lat.data_ptr(), cstep, lat.data_ptr(), cstep,
+                                txt.data_ptr(), 3, None if neg is None else neg.data_ptr(),
+                                0 if neg is None else 3, ctypes.byref(opt))
+
+    assert call([1, 8, 8], 0, 1.0) == -1          # steps <= 0 (restore)
+    assert call([1, 8, 8], 1, 2.0) == -1          # guidance without a negative text
+    assert call([1, 7, 8], 1, 1.0, cstep=56) == -1  # odd height (is_latent)
+    assert call([1, 8, 8], 1, 1.0, cstep=63) == -1  # plane stride below t*h*w
+    assert call([1, 8, 8], 1, 1.0) == 0
+    torch.cuda.synchronize()
+    dit.close()
