@@ -406,6 +406,26 @@ def main():
         barrier()
         st_ms = e0.elapsed_time(e1) / args.steps
         st_launches = ctx.launches() - launches0
+
+        # the frontend and the tail alone (same inputs), K calls each
+        fv = torch.empty(M - TEXT, D, device="cuda")
+        ft = torch.empty(TEXT, D, device="cuda")
+        fm = torch.empty(6, 1, D, device="cuda")
+        dit.forward_frontend([lat], [TEXT], [500.0], lv, lt, fv, ft, fm)
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            dit.forward_frontend([lat], [TEXT], [500.0], lv, lt, fv, ft, fm)
+        e1.record(stream)
+        barrier()
+        fe_ms = e0.elapsed_time(e1) / args.steps
+        e0.record(stream)
+        for _ in range(args.steps):
+            dit.forward_tail([lat], fv, fm, pred)
+        e1.record(stream)
+        barrier()
+        tail_ms = e0.elapsed_time(e1) / args.steps
+        del fv, ft, fm
         hlv, hlt = lv.cpu().pin_memory(), lt.cpu().pin_memory()
         hpred, htout = torch.empty_like(pred, device="cpu").pin_memory(), torch.empty_like(tout, device="cpu").pin_memory()
         dit.forward_step_host([lat], [TEXT], [500.0], hlv, hlt, hpred, htout)
@@ -418,7 +438,7 @@ def main():
         barrier()
         st_e2e_ms = e0.elapsed_time(e1) / st_e2e_steps
         dit_step = {"value": M / (st_ms / 1000.0), "unit": "tokens/s", "ms_per_step": st_ms,
-                    "frontend_tail_ms_per_step": st_ms - ms, "gpu_launches": st_launches,
+                    "frontend_ms": fe_ms, "tail_ms": tail_ms, "gpu_launches": st_launches,
                     "workload": f"latents {lat[0]}x{lat[1]}x{lat[2]}x33 + {TEXT}x5120 text + 1 timestep -> "
                                 f"prediction {lat[0]}x{lat[1]}x{lat[2]}x16 (frontend, {args.blocks} blocks, tail)",
                     "entry_point": "s2_dit_forward_step",

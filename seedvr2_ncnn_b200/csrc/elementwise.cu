@@ -175,15 +175,18 @@ __global__ void text_pool_kernel(const int4* __restrict__ reduce, const float* _
 // For D = 256 G the row is held in registers (2G float4 per lane, each warp
 // access 512 contiguous bytes) so x is read from HBM once, and two 8-warp
 // blocks fit per SM (128 registers) to keep 16 rows in flight; G = 0 is the
-// generic two-pass form for other widths.
+// generic two-pass form for other widths.  Rows are taken last first: x was
+// just written by a GEMM epilogue whose final tiles hold the highest rows, so
+// those are still in L2 when this pass starts, and the rows it writes last
+// (the lowest) are the ones the next GEMM reads first.
 template <int G>
 __global__ void __launch_bounds__(256, 2)
     ada_rmsnorm_kernel(int rows, int D, const float* __restrict__ x, float eps, const float* __restrict__ shift,
                        const float* __restrict__ scale, __nv_bfloat16* __restrict__ y)
 {
-    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int row = rows - 1 - (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5));
     const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
+    if (row < 0) return;
     const float* xr = x + (int64_t)row * D;
     __nv_bfloat16* yr = y + (int64_t)row * D;
     float ss = 0.f;
