@@ -602,7 +602,7 @@ __device__ __forceinline__ bool epilogue_gate_residual(const GemmArgs& a, const 
     for (int t = wk.first(); t < a.num_tiles && ok; t += wk.step())
     {
         int w = 0;
-        if (lane == 0) w = mbar_wait(&tfull[acc], acc_phase, abort_flag, a.status) ? 1 : 0;
+        if (lane == 0) w = mbar_wait<true>(&tfull[acc], acc_phase, abort_flag, a.status) ? 1 : 0;
         w = __shfl_sync(0xffffffffu, w, 0);
         if (!w)
         {
@@ -621,7 +621,7 @@ __device__ __forceinline__ bool epilogue_gate_residual(const GemmArgs& a, const 
         {
             const int slot = q % R;
             int r = 0;
-            if (lane == 0) r = mbar_wait(&rfull[slot], (uint32_t)(q / R) & 1u, abort_flag, a.status) ? 1 : 0;
+            if (lane == 0) r = mbar_wait<true>(&rfull[slot], (uint32_t)(q / R) & 1u, abort_flag, a.status) ? 1 : 0;
             r = __shfl_sync(0xffffffffu, r, 0);
             if (!r)
             {
@@ -769,7 +769,7 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                 const CUtensorMap* ta = stream ? &tmap_a1 : &tmap_a0;
                 for (int kb = 0; kb < args.num_kb; kb++)
                 {
-                    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, args.status)) break;
+                    if (!mbar_wait<true>(&empty[stage], phase ^ 1, abort_flag, args.status)) break;
                     uint8_t* sa = smem + stage * STAGE_BYTES;
                     uint8_t* sb = sa + A_BYTES;
                     mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
@@ -804,13 +804,13 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
             bool any = false;
             for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x)
             {
-                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, args.status)) break;
+                if (!mbar_wait<true>(&tempty[acc], acc_phase ^ 1, abort_flag, args.status)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
                 bool ok = true;
                 for (int kb = 0; kb < args.num_kb; kb++)
                 {
-                    if (!mbar_wait(&full[stage], phase, abort_flag, args.status))
+                    if (!mbar_wait<true>(&full[stage], phase, abort_flag, args.status))
                     {
                         ok = false;
                         break;
@@ -880,7 +880,7 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
             for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x)
             {
                 int ok = 0;
-                if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, args.status) ? 1 : 0;
+                if (lane == 0) ok = mbar_wait<true>(&tfull[acc], acc_phase, abort_flag, args.status) ? 1 : 0;
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
                 __syncwarp();
@@ -1032,7 +1032,7 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                 const CUtensorMap* ta = stream ? &tmap_a1 : &tmap_a0;
                 for (int kb = 0; kb < args.num_kb; kb++)
                 {
-                    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, args.status)) break;
+                    if (!mbar_wait<true>(&empty[stage], phase ^ 1, abort_flag, args.status)) break;
                     uint8_t* sa = smem + stage * STAGE_BYTES;
                     uint8_t* sb = sa + TL::A_STAGE;
                     if (leader) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
@@ -1068,13 +1068,13 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
             uint32_t acc_phase = 0;
             for (int t = walk.first(); t < args.num_tiles && !*abort_flag; t += walk.step())
             {
-                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, args.status)) break;
+                if (!mbar_wait<true>(&tempty[acc], acc_phase ^ 1, abort_flag, args.status)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
                 bool ok = true;
                 for (int kb = 0; kb < args.num_kb; kb++)
                 {
-                    if (!mbar_wait(&full[stage], phase, abort_flag, args.status))
+                    if (!mbar_wait<true>(&full[stage], phase, abort_flag, args.status))
                     {
                         ok = false;
                         break;
@@ -1137,7 +1137,7 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
             for (int t = walk.first(); t < args.num_tiles; t += walk.step())
             {
                 int ok = 0;
-                if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, args.status) ? 1 : 0;
+                if (lane == 0) ok = mbar_wait<true>(&tfull[acc], acc_phase, abort_flag, args.status) ? 1 : 0;
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
                 __syncwarp();
