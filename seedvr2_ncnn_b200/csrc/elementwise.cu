@@ -151,14 +151,25 @@ __global__ void text_pool_kernel(const int4* __restrict__ reduce, const float* _
     const int4 rd = reduce[t];
     const float sc = scale_of[t];
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int i = 0; i < rd.z; i++)
-    {
-        const float4 p = __ldg(reinterpret_cast<const float4*>(partial + (int64_t)(rd.x + i * rd.y) * inner + c));
+    const float* base = partial + (int64_t)rd.x * inner + c;
+    const int64_t step = (int64_t)rd.y * inner;
+    auto add = [&](const float4 p) {
         acc.x += p.x * sc;
         acc.y += p.y * sc;
         acc.z += p.z * sc;
         acc.w += p.w * sc;
+    };
+    // eight loads in flight, summed in window order
+    int i = 0;
+    for (; i + 8 <= rd.z; i += 8)
+    {
+        float4 p[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) p[k] = __ldg(reinterpret_cast<const float4*>(base + (i + k) * step));
+#pragma unroll
+        for (int k = 0; k < 8; k++) add(p[k]);
     }
+    for (; i < rd.z; i++) add(__ldg(reinterpret_cast<const float4*>(base + i * step)));
     if (out_f32)
         *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (int64_t)t * inner + c) = acc;
     else
