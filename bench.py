@@ -471,6 +471,43 @@ def main():
                                "ms_per_dit_pass": dn_ms / 4, "entry_point": "s2_dit_denoise",
                                "host_round_trips_between_steps": 0}
         del planes, neg_text, pos_text, lat0
+
+    # VAE DecomposedConv3D (implicit GEMM on the tensor cores) on the shapes the
+    # 720p decoder runs: 512 -> 512 channels at the latent size (6 frames of
+    # 90 x 160) and 128 -> 128 at full resolution (720 x 1280), 3 x 3 x 3
+    # causal kernels (two head frames).
+    vae_conv = None
+    if not sharded and not args.no_dit_step:
+        vae_conv = []
+        gv = torch.Generator(device="cpu").manual_seed(11)
+        for ci, frames, hh, ww in ((512, 6, 90, 160), (128, 6, 720, 1280)):
+            cfg = [ci, ci, 3, 3, 3, 1, 1, 2, 1, 1, 1, 1, 1, 1, 1, 1]
+            wts = (0.02 * torch.randn(3, ci, ci, 3, 3, generator=gv)).numpy()
+            bias = (0.02 * torch.randn(ci, generator=gv)).numpy()
+            layer = abi.Conv3d(ctx, cfg, bias, wts)
+            xin = torch.randn(ci, frames, hh, ww, device="cuda")
+            yout = layer.forward(xin, abi.S2_VAE_MEMORY_DISABLED)
+            barrier()
+            ctx.profile(True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                layer.forward(xin, abi.S2_VAE_MEMORY_DISABLED, out=yout)
+            e1.record(stream)
+            barrier()
+            cc = ctx.counters()
+            ctx.profile(False)
+            call_ms = e0.elapsed_time(e1) / args.steps
+            flops = 2.0 * frames * hh * ww * ci * 27 * ci
+            gemm = cc["shared_linear"]
+            vae_conv.append({"shape": f"{ci}->{ci} ch, {frames}x{hh}x{ww}, 3x3x3", "ms_per_call": call_ms,
+                             "tflops_per_call": flops / call_ms / 1e9,
+                             "conv_kernel_ms": gemm["ms"] / gemm["launches"],
+                             "conv_kernel_tflops": flops / (gemm["ms"] / gemm["launches"]) / 1e9,
+                             "conv_kernel_frac_of_burst_peak": flops / (gemm["ms"] / gemm["launches"]) / 1e9
+                             / load_peaks()["bf16_tflops"],
+                             "pack_ms": cc["other"]["ms"] / max(cc["other"]["launches"], 1)})
+            layer.close()
+            del xin, yout
     status = ctx.status()
 
     peaks = load_peaks()
@@ -539,6 +576,7 @@ def main():
                 "entry_point": "s2_dit_forward_sharded + pinned H2D/D2H" if sharded else "s2_dit_forward_host"},
         "gpu_launches": launches,
         "dit_step": dit_step,
+        "vae_conv": vae_conv,
         "clocks": clk,
         "device_status": status,
     }

@@ -354,6 +354,35 @@ int s2_apply_cfg(s2_context* ctx, const float* pos, const float* neg, int64_t co
                  float* out);
 
 /* ---------------------------------------------------------------------------
+ * VAE DecomposedConv3D (decomposed_conv3d.h:30-90, forward :605-765): a causal
+ * 3-D convolution of a [c][d][h][w] blob, computed here as one implicit GEMM
+ * on the tensor cores (bf16 operands, fp32 accumulation).
+ * cfg: the layer's 16-value config blob in its load_model order (num_output,
+ * num_input, kernel_w, kernel_h, kernel_t, stride_t, dilation_t, head_frames,
+ * stride_w, stride_h, dilation_w, dilation_h, pad_w, pad_h, groups,
+ * bias_term); bias: host fp32 [num_output] (bias_term) or NULL; weights: host
+ * fp32 kernel_t x [num_output][num_input][kernel_h][kernel_w].  This build
+ * supports groups = 1 and stride_w = 1 (-1 otherwise).
+ * memory_state: the VAE's temporal-memory state (seedvr2::MemoryState): with
+ * ACTIVE the head frames are the previous chunk's cached frames, otherwise
+ * head_frames copies of frame 0; any state but DISABLED caches the last
+ * kernel_t - stride_t padded input frames for the next call. */
+#define S2_VAE_MEMORY_DISABLED 0
+#define S2_VAE_MEMORY_INITIALIZING 1
+#define S2_VAE_MEMORY_ACTIVE 2
+typedef struct s2_conv3d s2_conv3d;
+int s2_conv3d_create(s2_context* ctx, const int* cfg, const float* bias, const float* weights, s2_conv3d** out);
+/* Output extents (w, h, d, c) of a forward on a w x h x d input, or -1. */
+int s2_conv3d_output_shape(const s2_conv3d* layer, int w, int h, int d, int memory_state, int* out_whdc);
+/* in: device fp32 [c][plane stride in_cstep >= d*h*w]; out: device fp32
+ * [num_output][plane stride out_cstep >= output d*h*w].  -1 on a channel
+ * count other than num_input, too few padded frames, or cached frames of
+ * another size (as the reference). */
+int s2_conv3d_forward(s2_conv3d* layer, const float* in, int64_t in_cstep, int w, int h, int d, int c,
+                      int memory_state, float* out, int64_t out_cstep);
+void s2_conv3d_free(s2_conv3d* layer);
+
+/* ---------------------------------------------------------------------------
  * Multi-GPU (one process per GPU over NVLink).  The reference has no
  * distributed path (seedvr2_main.cpp:89-100 forces --sp-size 1); this is the
  * window sharding of the B200 build.

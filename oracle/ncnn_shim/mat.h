@@ -1,12 +1,14 @@
 // Clean-room restatement of the subset of the ncnn::Mat API that the
-// reference's CPU layer code (src/seedvr2/adaptive_window_attention.cpp and
-// src/seedvr2/shared_linear.cpp, compiled with NCNN_VULKAN=0) calls.
+// reference's CPU layer code (src/seedvr2/adaptive_window_attention.cpp,
+// src/seedvr2/shared_linear.cpp and src/seedvr2/decomposed_conv3d.cpp,
+// compiled with NCNN_VULKAN=0) calls.
 //
 // TEST INFRASTRUCTURE ONLY.  This header exists so that the reference's own
 // layer sources compile unmodified into oracle/_ref; it is never part of the
 // shipped library.  Semantics follow the public ncnn documentation:
 //   * dims/w/h/c/elemsize/elempack describe the blob;
-//   * 3-D blobs store each channel at a 16-byte aligned stride (cstep);
+//   * 3-D and 4-D blobs store each channel (w x h, or w x h x d) at a
+//     16-byte aligned stride (cstep); n is the batch count (always 1 here);
 //   * storage is reference counted and shared by copies and views.
 #ifndef S2_ORACLE_NCNN_SHIM_MAT_H
 #define S2_ORACLE_NCNN_SHIM_MAT_H
@@ -34,6 +36,17 @@ public:
     explicit Mat(int _w, size_t _elemsize = 4u, Allocator* a = 0) { init_empty(); create(_w, _elemsize, a); }
     Mat(int _w, int _h, size_t _elemsize = 4u, Allocator* a = 0) { init_empty(); create(_w, _h, _elemsize, a); }
     Mat(int _w, int _h, int _c, size_t _elemsize = 4u, Allocator* a = 0) { init_empty(); create(_w, _h, _c, _elemsize, a); }
+    Mat(int _w, int _h, int _c, size_t _elemsize, int _elempack, Allocator* a)
+    {
+        init_empty();
+        create(_w, _h, _c, _elemsize, a);
+        elempack = _elempack;
+    }
+    Mat(int _w, int _h, int _d, int _c, size_t _elemsize, int _elempack, int _n, Allocator* a = 0)
+    {
+        init_empty();
+        create(_w, _h, _d, _c, _elemsize, _elempack, _n, a);
+    }
     // External-data 1-D view (not owned).
     Mat(int _w, void* _data, size_t _elemsize = 4u, Allocator* a = 0)
     {
@@ -48,7 +61,7 @@ public:
         cstep = (size_t)w;
     }
     Mat(const Mat& m) : data(m.data), refcount(m.refcount), elemsize(m.elemsize), elempack(m.elempack),
-                        allocator(m.allocator), dims(m.dims), w(m.w), h(m.h), d(m.d), c(m.c), cstep(m.cstep)
+                        allocator(m.allocator), dims(m.dims), w(m.w), h(m.h), d(m.d), c(m.c), n(m.n), cstep(m.cstep)
     {
         if (refcount) ++*refcount;
     }
@@ -69,6 +82,7 @@ public:
         h = m.h;
         d = m.d;
         c = m.c;
+        n = m.n;
         cstep = m.cstep;
         return *this;
     }
@@ -110,6 +124,24 @@ public:
         d = 1;
         c = _c;
         const size_t bytes = (size_t)w * h * elemsize;
+        cstep = ((bytes + 15) & ~(size_t)15) / elemsize;
+        allocate();
+    }
+
+    // 4-D: w x h x d per channel (d frames), 16-byte aligned channel stride
+    void create(int _w, int _h, int _d, int _c, size_t _elemsize, int _elempack, int _n, Allocator* a = 0)
+    {
+        release();
+        elemsize = _elemsize;
+        elempack = _elempack;
+        allocator = a;
+        dims = 4;
+        w = _w;
+        h = _h;
+        d = _d;
+        c = _c;
+        n = _n;
+        const size_t bytes = (size_t)w * h * d * elemsize;
         cstep = ((bytes + 15) & ~(size_t)15) / elemsize;
         allocate();
     }
@@ -161,14 +193,28 @@ public:
     bool empty() const { return data == 0 || total() == 0; }
     size_t total() const { return cstep * c; }
 
+    // channel _c: a w x h view (3-D blob) or a w x h x d view (4-D blob)
     Mat channel(int _c)
     {
         Mat m(w, h, (unsigned char*)data + cstep * _c * elemsize, elemsize);
+        if (dims == 4) m.set_depth(d);
         return m;
     }
     const Mat channel(int _c) const
     {
         Mat m(w, h, (unsigned char*)data + cstep * _c * elemsize, elemsize);
+        if (dims == 4) m.set_depth(d);
+        return m;
+    }
+    // frame z of a w x h x d channel view: a w x h view
+    Mat depth(int z)
+    {
+        Mat m(w, h, (unsigned char*)data + (size_t)w * h * z * elemsize, elemsize);
+        return m;
+    }
+    const Mat depth(int z) const
+    {
+        Mat m(w, h, (unsigned char*)data + (size_t)w * h * z * elemsize, elemsize);
         return m;
     }
 
@@ -199,6 +245,7 @@ public:
         refcount = 0;
         dims = 0;
         w = h = d = c = 0;
+        n = 1;
         cstep = 0;
         elemsize = 0;
         elempack = 0;
@@ -214,9 +261,16 @@ public:
     int h;
     int d;
     int c;
+    int n;
     size_t cstep;
 
 private:
+    void set_depth(int _d)
+    {
+        dims = 3;
+        d = _d;
+        cstep = (size_t)w * h * d;
+    }
     // 2-D external view used by channel()/row_range().
     Mat(int _w, int _h, void* _data, size_t _elemsize)
     {
@@ -239,6 +293,7 @@ private:
         allocator = 0;
         dims = 0;
         w = h = d = c = 0;
+        n = 1;
         cstep = 0;
     }
     void allocate()

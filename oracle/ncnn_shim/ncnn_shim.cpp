@@ -16,7 +16,15 @@
 //           broadcast_type_C 4 = per-output row vector, -1 = no C)
 //          out[m][n] = sum_k A[m][k] * B[n][k] + C[n], fp32.
 //
-// Both loops parallelise with OpenMP over independent outputs, so results do
+//   Convolution (configured in decomposed_conv3d.cpp:480-497: 0 num_output,
+//           1/11 kernel w/h, 2/12 dilation, 3/13 stride, 4/15/14/16 pad
+//           left/right/top/bottom, 5 bias_term, 6 weight_data_size; weights
+//           [num_output][num_input][kernel_h][kernel_w])
+//          out[p][y][x] = bias[p] + sum_{q, ky, kx} w[p][q][ky][kx] *
+//                         in[q][y*sh + ky*dh - pt][x*sw + kx*dw - pl]
+//          with zeros outside the input, fp32, summed in (q, ky, kx) order.
+//
+// All loops parallelise with OpenMP over independent outputs, so results do
 // not depend on the thread count.
 #include <cmath>
 #include <cstring>
@@ -208,11 +216,108 @@ private:
 
 } // namespace
 
+namespace {
+
+class ShimConvolution : public Layer
+{
+public:
+    ShimConvolution()
+        : num_output(0), kernel_w(0), kernel_h(0), dilation_w(1), dilation_h(1), stride_w(1), stride_h(1),
+          pad_left(0), pad_right(0), pad_top(0), pad_bottom(0), bias_term(0), weight_data_size(0)
+    {
+        one_blob_only = true;
+        support_inplace = false;
+    }
+
+    virtual int load_param(const ParamDict& pd)
+    {
+        num_output = pd.get(0, 0);
+        kernel_w = pd.get(1, 0);
+        kernel_h = pd.get(11, kernel_w);
+        dilation_w = pd.get(2, 1);
+        dilation_h = pd.get(12, dilation_w);
+        stride_w = pd.get(3, 1);
+        stride_h = pd.get(13, stride_w);
+        pad_left = pd.get(4, 0);
+        pad_right = pd.get(15, pad_left);
+        pad_top = pd.get(14, pad_left);
+        pad_bottom = pd.get(16, pad_top);
+        bias_term = pd.get(5, 0);
+        weight_data_size = pd.get(6, 0);
+        // negative pads are ncnn's "same" modes, not used by the reference layer
+        if (num_output <= 0 || kernel_w <= 0 || kernel_h <= 0 || pad_left < 0 || pad_right < 0 || pad_top < 0 ||
+            pad_bottom < 0)
+            return -1;
+        return 0;
+    }
+
+    virtual int load_model(const ModelBin& mb)
+    {
+        weight_data = mb.load(weight_data_size, 0);
+        if (weight_data.empty()) return -100;
+        if (bias_term)
+        {
+            bias_data = mb.load(num_output, 1);
+            if (bias_data.empty()) return -100;
+        }
+        return 0;
+    }
+
+    virtual int forward(const Mat& bottom, Mat& top, const Option& opt) const
+    {
+        const int w = bottom.w, h = bottom.h, inch = bottom.c;
+        if (inch <= 0 || weight_data_size != num_output * inch * kernel_w * kernel_h) return -1;
+        const int ew = dilation_w * (kernel_w - 1) + 1, eh = dilation_h * (kernel_h - 1) + 1;
+        const int outw = (w + pad_left + pad_right - ew) / stride_w + 1;
+        const int outh = (h + pad_top + pad_bottom - eh) / stride_h + 1;
+        if (outw <= 0 || outh <= 0) return -1;
+        top.create(outw, outh, num_output, 4u, opt.blob_allocator);
+        if (top.empty()) return -100;
+        const float* wt = weight_data;
+#pragma omp parallel for schedule(static)
+        for (int p = 0; p < num_output; p++)
+        {
+            float* out = top.channel(p);
+            for (int y = 0; y < outh; y++)
+                for (int x = 0; x < outw; x++)
+                {
+                    float sum = bias_term ? ((const float*)bias_data)[p] : 0.f;
+                    for (int q = 0; q < inch; q++)
+                    {
+                        const float* in = bottom.channel(q);
+                        const float* kq = wt + ((size_t)p * inch + q) * kernel_h * kernel_w;
+                        for (int ky = 0; ky < kernel_h; ky++)
+                        {
+                            const int iy = y * stride_h + ky * dilation_h - pad_top;
+                            if (iy < 0 || iy >= h) continue;
+                            for (int kx = 0; kx < kernel_w; kx++)
+                            {
+                                const int ix = x * stride_w + kx * dilation_w - pad_left;
+                                if (ix < 0 || ix >= w) continue;
+                                sum += in[(size_t)iy * w + ix] * kq[ky * kernel_w + kx];
+                            }
+                        }
+                    }
+                    out[(size_t)y * outw + x] = sum;
+                }
+        }
+        return 0;
+    }
+
+private:
+    int num_output, kernel_w, kernel_h, dilation_w, dilation_h, stride_w, stride_h;
+    int pad_left, pad_right, pad_top, pad_bottom, bias_term, weight_data_size;
+    Mat weight_data, bias_data;
+};
+
+} // namespace
+
 Layer* create_layer(const char* type)
 {
     const std::string t(type ? type : "");
     if (t == "SDPA") return new ShimSDPA;
     if (t == "Gemm") return new ShimGemm;
+    if (t == "Convolution") return new ShimConvolution;
     return 0;
 }
 

@@ -25,6 +25,12 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_SO = os.path.join(HERE, "libs2_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libs2_ref.so")
 REF_IO_SO = os.path.join(HERE, "_ref", "libs2_ref_dit_io.so")
+REF_VAE_SO = os.path.join(HERE, "_ref", "libs2_ref_vae.so")
+
+# DecomposedConv3D memory states (seedvr2::MemoryState)
+VAE_MEMORY_DISABLED = 0
+VAE_MEMORY_INITIALIZING = 1
+VAE_MEMORY_ACTIVE = 2
 
 WINDOW_TARGET = 0
 WINDOW_EXTENT = 1
@@ -93,6 +99,9 @@ class Port:
         lib.s2o_apply_cfg.argtypes = [_f32p, _f32p, C.c_long, C.c_float, C.c_float, _f32p]
         lib.s2o_euler_update.argtypes = [_f32p, C.c_long, C.c_long, _f32p, C.c_float]
         lib.s2o_denoise_schedule.argtypes = [C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_float)]
+        lib.s2o_conv3d_dims.argtypes = [_i32p, C.c_int, C.c_int, C.c_int, C.c_int, _i32p]
+        lib.s2o_conv3d_forward.argtypes = [_i32p, C.c_void_p, _f32p, _f32p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                           C.c_int, _f32p, C.c_void_p]
         self.lib = lib
 
     def plan(self, shapes, window, shifted, mode=WINDOW_TARGET) -> Plan:
@@ -297,6 +306,30 @@ class Port:
         return lat
 
 
+    # ---- VAE DecomposedConv3D (decomposed_conv3d.cpp) ----
+    def conv3d_forward(self, cfg, bias, weights, x, mem=None, keep_memory=True):
+        """x [c][d][h][w]; mem [c][m][h][w] cached frames or None (head = copies of frame 0).
+        Returns (out [co][t][oh][ow], next memory [c][kernel_t - stride_t][h][w] or None)."""
+        cfg = _i32(cfg)
+        x = _f32(x)
+        c, d, h, w = x.shape
+        m = 0 if mem is None else mem.shape[1]
+        dims = np.zeros(4, np.int32)
+        if self.lib.s2o_conv3d_dims(cfg, w, h, d, m if m else int(cfg[7]), dims) != 0:
+            raise ValueError(-1)
+        out = np.zeros((dims[3], dims[2], dims[1], dims[0]), np.float32)
+        cache = int(cfg[4] - cfg[5])
+        nm = np.zeros((c, cache, h, w), np.float32) if (keep_memory and cache > 0) else None
+        b = _f32(bias) if bias is not None else None
+        memf = _f32(mem) if mem is not None else None
+        r = self.lib.s2o_conv3d_forward(cfg, b.ctypes.data if b is not None else None, _f32(weights), x, w, h, d,
+                                        memf.ctypes.data if memf is not None else None, m, out,
+                                        nm.ctypes.data if nm is not None else None)
+        if r != 0:
+            raise ValueError(r)
+        return out, nm
+
+
 def _f64(a) -> np.ndarray:
     return np.asarray(a, dtype=np.float64)
 
@@ -361,6 +394,45 @@ class RefIO:
         if r != 0:
             raise ValueError(r)
         return out[:len(t)]
+
+
+class RefConv3d:
+    """The reference's own DecomposedConv3D layer (oracle/_ref/libs2_ref_vae.so), one layer instance
+    with its temporal memory."""
+
+    def __init__(self, cfg, bias, weights, path: str = REF_VAE_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        lib = C.CDLL(path)
+        lib.s2ref_conv3d_create.argtypes = [_f32p, _f32p, C.c_size_t]
+        lib.s2ref_conv3d_create.restype = C.c_void_p
+        lib.s2ref_conv3d_forward.argtypes = [C.c_void_p, C.c_int, _f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p,
+                                             C.c_size_t, _i32p]
+        lib.s2ref_conv3d_free.argtypes = [C.c_void_p]
+        self.lib = lib
+        self.cfg = _i32(cfg)
+        parts = ([] if bias is None else [_f32(bias).ravel()]) + [_f32(weights).ravel()]
+        blob = np.concatenate(parts).astype(np.float32)
+        self.handle = lib.s2ref_conv3d_create(_f32(self.cfg.astype(np.float32)), blob, blob.size)
+        if not self.handle:
+            raise ValueError("DecomposedConv3D load failed")
+
+    def forward(self, x, memory_state):
+        x = _f32(x)
+        c, d, h, w = x.shape
+        cap = int(self.cfg[0]) * (d + 64) * (h + 2 * int(self.cfg[13]) + 8) * (w + 2 * int(self.cfg[12]) + 8)
+        out = np.zeros(cap, np.float32)
+        dims = np.zeros(4, np.int32)
+        r = self.lib.s2ref_conv3d_forward(self.handle, memory_state, x, w, h, d, c, out, cap, dims)
+        if r != 0:
+            raise ValueError(r)
+        ow, oh, od, oc = dims.tolist()
+        return out[:ow * oh * od * oc].reshape(oc, od, oh, ow).copy()
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            self.lib.s2ref_conv3d_free(self.handle)
+            self.handle = None
 
 
 class Ref:

@@ -1,0 +1,76 @@
+// extern "C" wrapper around the reference's OWN DecomposedConv3D layer
+// (src/seedvr2/decomposed_conv3d.cpp, compiled unmodified with NCNN_VULKAN=0
+// against the clean-room ncnn shim, whose "Convolution" restates ncnn's
+// spatial convolution).  Built by oracle/Makefile into
+// oracle/_ref/libs2_ref_vae.so.
+//
+// TEST INFRASTRUCTURE ONLY: the tests and the fixture generator load it as the
+// checker; the shipped library never links it.
+#include <cstring>
+#include <vector>
+
+#include "decomposed_conv3d.h"
+#include "modelbin.h"
+
+using seedvr2::DecomposedConv3D;
+
+extern "C" {
+
+// cfg[16]: the layer's config blob in load_model order (num_output, num_input,
+// kernel_w, kernel_h, kernel_t, stride_t, dilation_t, head_frames, stride_w,
+// stride_h, dilation_w, dilation_h, pad_w, pad_h, groups, bias_term);
+// weights: bias [num_output] when bias_term, then kernel_t spatial kernels
+// [num_output][num_input][kernel_h][kernel_w].  Returns a layer handle or 0.
+void* s2ref_conv3d_create(const float* cfg, const float* weights, size_t count)
+{
+    DecomposedConv3D* layer = new DecomposedConv3D;
+    ncnn::ParamDict pd;
+    for (int i = 0; i < 16; i++) pd.set(i, (int)cfg[i]);
+    if (layer->load_param(pd) != 0)
+    {
+        delete layer;
+        return 0;
+    }
+    std::vector<float> blob(cfg, cfg + 16);
+    blob.insert(blob.end(), weights, weights + count);
+    ncnn::ModelBinFromFloats mb(blob.data(), blob.size());
+    ncnn::Option opt;
+    if (layer->load_model(mb) != 0 || layer->create_pipeline(opt) != 0)
+    {
+        delete layer;
+        return 0;
+    }
+    return layer;
+}
+
+// One forward: in dense [c][d][h][w] fp32 under the given memory state
+// (0 disabled, 1 initializing, 2 active); out dense [c][d][h][w] of at most
+// out_capacity floats, out_dims = (w, h, d, c).  Returns the layer's code.
+int s2ref_conv3d_forward(void* handle, int memory_state, const float* in, int w, int h, int d, int c, float* out,
+                         size_t out_capacity, int* out_dims)
+{
+    const DecomposedConv3D* layer = static_cast<const DecomposedConv3D*>(handle);
+    seedvr2::set_vae_memory_state(static_cast<seedvr2::MemoryState>(memory_state));
+    ncnn::Mat bottom(w, h, d, c, 4u, 1, 1);
+    const size_t plane = (size_t)w * h * d;
+    for (int ch = 0; ch < c; ch++) std::memcpy(bottom.channel(ch).data, in + plane * ch, plane * sizeof(float));
+    ncnn::Mat top;
+    ncnn::Option opt;
+    const int r = layer->forward(bottom, top, opt);
+    if (r != 0) return r;
+    out_dims[0] = top.w;
+    out_dims[1] = top.h;
+    out_dims[2] = top.d;
+    out_dims[3] = top.c;
+    const size_t oplane = (size_t)top.w * top.h * top.d;
+    if (oplane * top.c > out_capacity) return -1;
+    for (int ch = 0; ch < top.c; ch++) std::memcpy(out + oplane * ch, top.channel(ch).data, oplane * sizeof(float));
+    return 0;
+}
+
+void s2ref_conv3d_free(void* handle)
+{
+    delete static_cast<DecomposedConv3D*>(handle);
+}
+
+} // extern "C"

@@ -708,3 +708,111 @@ void s2o_denoise_schedule(int steps, int step, float* timestep, float* delta)
     *timestep = t;
     *delta = (next - t) / 1000.f;
 }
+
+/* ---------------------------------------------------------------------------
+ * VAE DecomposedConv3D (src/seedvr2/decomposed_conv3d.cpp:399-765).
+ * cfg: the layer's 16 config values (num_output, num_input, kernel_w,
+ * kernel_h, kernel_t, stride_t, dilation_t, head_frames, stride_w, stride_h,
+ * dilation_w, dilation_h, pad_w, pad_h, groups, bias_term). */
+
+/* ncnn Convolution of one frame as the reference configures it (:480-497):
+ * out[p][y][x] = bias[p] (tap 0 only) + sum_{q,ky,kx} w[p][q][ky][kx] in[q][..],
+ * zero padding pad_w / pad_h on both sides, summed in (q, ky, kx) order. */
+static void conv2d_frame(const int* cfg, const float* bias, const float* wt, const float* in, long in_cstep, int w,
+                         int h, float* out, long out_cstep, int ow, int oh, int accumulate)
+{
+    const int co = cfg[0], ci = cfg[1], kw = cfg[2], kh = cfg[3], sw = cfg[8], sh = cfg[9], dw = cfg[10],
+              dh = cfg[11], pw = cfg[12], ph = cfg[13];
+#pragma omp parallel for schedule(static)
+    for (int p = 0; p < co; p++)
+        for (int y = 0; y < oh; y++)
+            for (int x = 0; x < ow; x++)
+            {
+                float sum = bias ? bias[p] : 0.f;
+                for (int q = 0; q < ci; q++)
+                {
+                    const float* src = in + q * in_cstep;
+                    const float* kq = wt + ((long)p * ci + q) * kh * kw;
+                    for (int ky = 0; ky < kh; ky++)
+                    {
+                        const int iy = y * sh + ky * dh - ph;
+                        if (iy < 0 || iy >= h) continue;
+                        for (int kx = 0; kx < kw; kx++)
+                        {
+                            const int ix = x * sw + kx * dw - pw;
+                            if (ix < 0 || ix >= w) continue;
+                            sum += src[(long)iy * w + ix] * kq[ky * kw + kx];
+                        }
+                    }
+                }
+                float* o = out + p * out_cstep + (long)y * ow + x;
+                *o = accumulate ? *o + sum : 0.f + sum;
+            }
+}
+
+int s2o_conv3d_dims(const int* cfg, int w, int h, int d, int prefix, int* out_dims)
+{
+    const int kw = cfg[2], kh = cfg[3], kt = cfg[4], st = cfg[5], dt = cfg[6], sw = cfg[8], sh = cfg[9], dw = cfg[10],
+              dh = cfg[11], pw = cfg[12], ph = cfg[13];
+    const int padded = d + prefix, extent = dt * (kt - 1) + 1;
+    if (padded < extent) return -1;
+    const int ow = (w + 2 * pw - (dw * (kw - 1) + 1)) / sw + 1, oh = (h + 2 * ph - (dh * (kh - 1) + 1)) / sh + 1;
+    if (ow <= 0 || oh <= 0) return -1;
+    out_dims[0] = ow;
+    out_dims[1] = oh;
+    out_dims[2] = (padded - extent) / st + 1;
+    out_dims[3] = cfg[0];
+    return 0;
+}
+
+/* DecomposedConv3D::forward (:605-765) without the layer state: in [c][d][h][w]
+ * dense; mem [c][mem_frames][h][w] the cached frames (mem_frames 0: none, the
+ * head is head_frames copies of frame 0); out [co][t][oh][ow] dense; next_mem
+ * (when not NULL) receives the last kernel_t - stride_t frames of the padded
+ * input [c][cache][h][w]. */
+int s2o_conv3d_forward(const int* cfg, const float* bias, const float* weights, const float* in, int w, int h, int d,
+                       const float* mem, int mem_frames, float* out, float* next_mem)
+{
+    const int co = cfg[0], ci = cfg[1], kw = cfg[2], kh = cfg[3], kt = cfg[4], st = cfg[5], dt = cfg[6];
+    const int prefix = mem_frames > 0 ? mem_frames : cfg[7];
+    int od[4];
+    if (s2o_conv3d_dims(cfg, w, h, d, prefix, od) != 0) return -1;
+    const long plane = (long)w * h, in_cstep = plane * d, mem_cstep = plane * (mem_frames > 0 ? mem_frames : 1);
+    const long oplane = (long)od[0] * od[1], out_cstep = oplane * od[2];
+    float* frame = (float*)malloc(sizeof(float) * plane * ci);
+    if (!frame) return -100;
+    const long wsize = (long)co * ci * kh * kw;
+    /* frame source of padded index i: the cached frames, frame 0 (head), or the input */
+    for (int t = 0; t < od[2]; t++)
+        for (int k = 0; k < kt; k++)
+        {
+            const int pi = t * st + k * dt;
+            for (int q = 0; q < ci; q++)
+            {
+                const float* src = pi < prefix ? (mem_frames > 0 ? mem + q * mem_cstep + (long)pi * plane
+                                                                 : in + q * in_cstep)
+                                               : in + q * in_cstep + (long)(pi - prefix) * plane;
+                memcpy(frame + q * plane, src, sizeof(float) * plane);
+            }
+            conv2d_frame(cfg, (k == 0 && cfg[15]) ? bias : NULL, weights + k * wsize, frame, plane, w, h,
+                         out + (long)t * oplane, out_cstep, od[0], od[1], k > 0);
+        }
+    free(frame);
+    const int cache = kt - st;
+    if (next_mem && cache > 0)
+    {
+        const int padded = d + prefix;
+        for (int f = 0; f < cache; f++)
+        {
+            const int pi = padded - cache + f;
+            for (int q = 0; q < ci; q++)
+            {
+                const float* src = pi < prefix ? (mem_frames > 0 ? mem + q * mem_cstep + (long)pi * plane
+                                                                 : in + q * in_cstep)
+                                               : in + q * in_cstep + (long)(pi - prefix) * plane;
+                memcpy(next_mem + (q * (long)cache + f) * plane, src, sizeof(float) * plane);
+            }
+        }
+    }
+    return 0;
+}

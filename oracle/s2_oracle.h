@@ -90,6 +90,12 @@ void s2o_apply_cfg(const float* pos, const float* neg, long count, float scale, 
 void s2o_euler_update(float* latent, long cstep, long tokens, const float* pred, float delta);
 void s2o_denoise_schedule(int steps, int step, float* timestep, float* delta);
 
+/* VAE DecomposedConv3D (src/seedvr2/decomposed_conv3d.cpp:399-765); cfg is
+ * the layer's 16-value config blob.  out_dims = (ow, oh, t_out, co). */
+int s2o_conv3d_dims(const int* cfg, int w, int h, int d, int prefix, int* out_dims);
+int s2o_conv3d_forward(const int* cfg, const float* bias, const float* weights, const float* in, int w, int h, int d,
+                       const float* mem, int mem_frames, float* out, float* next_mem);
+
 #ifdef __cplusplus
 }
 #endif

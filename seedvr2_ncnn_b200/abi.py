@@ -54,7 +54,12 @@ EXPORTED = [
     "s2_patchify_video", "s2_unpatchify_prediction", "s2_timestep_embedding", "s2_dit_set_io_weights",
     "s2_dit_forward_frontend", "s2_dit_forward_tail", "s2_dit_forward_step", "s2_dit_forward_step_host",
     "s2_dit_denoise", "s2_dit_denoise_host", "s2_apply_cfg",
+    "s2_conv3d_create", "s2_conv3d_output_shape", "s2_conv3d_forward", "s2_conv3d_free",
 ]
+
+S2_VAE_MEMORY_DISABLED = 0
+S2_VAE_MEMORY_INITIALIZING = 1
+S2_VAE_MEMORY_ACTIVE = 2
 
 # Widths fixed by the reference's DiT input/output formats.
 S2_LATENT_CHANNELS = 33
@@ -169,6 +174,10 @@ def lib() -> C.CDLL:
     L.s2_dit_denoise.argtypes = [vp, pint, vp, i64, vp, i64, vp, ip, vp, ip, C.POINTER(DenoiseOptions)]
     L.s2_dit_denoise_host.argtypes = [vp, pint, vp, i64, vp, i64, vp, ip, vp, ip, C.POINTER(DenoiseOptions)]
     L.s2_apply_cfg.argtypes = [vp, vp, vp, i64, C.c_float, C.c_float, vp]
+    L.s2_conv3d_create.argtypes = [vp, pint, vp, vp, C.POINTER(vp)]
+    L.s2_conv3d_output_shape.argtypes = [vp, ip, ip, ip, ip, pint]
+    L.s2_conv3d_forward.argtypes = [vp, vp, i64, ip, ip, ip, ip, ip, vp, i64]
+    L.s2_conv3d_free.argtypes = [vp]
     _lib = L
     return L
 
@@ -563,6 +572,50 @@ class Dit:
                                         0 if negative_text is None else negative_text.shape[0], C.byref(opt)),
               "s2_dit_denoise_host")
         return latent
+
+
+class Conv3d:
+    """s2_conv3d: the VAE's DecomposedConv3D layer (cfg = its 16-value config blob; host fp32 bias and
+    kernel_t x [co][ci][kh][kw] weights)."""
+
+    def __init__(self, ctx: Context, cfg, bias, weights):
+        import numpy as np
+
+        self.ctx = ctx
+        self.cfg = [int(v) for v in cfg]
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        w = np.ascontiguousarray(weights, dtype=np.float32)
+        h = C.c_void_p()
+        check(lib().s2_conv3d_create(ctx.handle, _ints(self.cfg), ptr(b), ptr(w), C.byref(h)), "s2_conv3d_create")
+        self.handle = h
+
+    def output_shape(self, w, h, d, memory_state):
+        out = (C.c_int * 4)()
+        check(lib().s2_conv3d_output_shape(self.handle, w, h, d, memory_state, out), "s2_conv3d_output_shape")
+        return list(out)
+
+    def forward(self, x, memory_state=S2_VAE_MEMORY_DISABLED, out=None):
+        """x: fp32 CUDA [c, d, h, w] -> fp32 CUDA [co, t, oh, ow]."""
+        import torch
+
+        c, d, h, w = x.shape
+        ow, oh, od, oc = self.output_shape(w, h, d, memory_state)
+        if out is None:
+            out = torch.empty((oc, od, oh, ow), dtype=torch.float32, device=x.device)
+        check(lib().s2_conv3d_forward(self.handle, x.data_ptr(), d * h * w, w, h, d, c, memory_state,
+                                      out.data_ptr(), od * oh * ow), "s2_conv3d_forward")
+        return out
+
+    def close(self):
+        if self.handle:
+            lib().s2_conv3d_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def shard(video_shape, text_length, window, window_mode, rank, world, shifted=1) -> dict:

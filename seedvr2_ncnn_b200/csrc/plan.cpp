@@ -386,6 +386,24 @@ int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64
     return make_tmap_2d(map, base, 0, inner, outer, row_stride_bytes, box_inner, box_outer);
 }
 
+int make_tmap_bf16_4d(CUtensorMap* map, const void* base, const uint64_t* dims, const uint64_t* stride_bytes,
+                      const uint32_t* box)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return S2_ERR_DEVICE;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || box[0] * 2 != 128) return S2_ERR_INVALID;
+    for (int i = 0; i < 3; i++)
+        if (stride_bytes[i] & 15) return S2_ERR_INVALID;
+    const cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+    const cuuint64_t st[3] = {stride_bytes[0], stride_bytes[1], stride_bytes[2]};
+    const cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), d, st, bx, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? S2_OK : S2_ERR_INVALID;
+}
+
 // ---------------------------------------------------------------- buffers
 int DeviceBuffer::ensure(size_t want)
 {

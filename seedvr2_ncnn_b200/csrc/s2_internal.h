@@ -149,6 +149,11 @@ int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64
 int make_tmap_2d(CUtensorMap* map, const void* base, int f32, uint64_t inner, uint64_t outer,
                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
 
+// bf16 4-D tensor (dims[0] innermost, 16-byte aligned strides of dims 1..3 in
+// bytes), 128-byte swizzle, box[0] * 2 = 128 bytes; out-of-range elements read 0.
+int make_tmap_bf16_4d(CUtensorMap* map, const void* base, const uint64_t* dims, const uint64_t* stride_bytes,
+                      const uint32_t* box);
+
 // kernels (launchers return S2_* codes)
 int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void* A0, const void* A1, const void* W,
                          const float* bias, int epilogue, const float* gate, int out_f32, void* out0, void* out1);
@@ -233,6 +238,22 @@ int launch_timestep_embedding(Context& ctx, const float* timesteps, int batch, f
 // [B][ldx]; y(b, n) stored at y[(n / chunk) * s_chunk + b * s_b + n % chunk]
 int launch_gemv(Context& ctx, const void* W, const float* bias, int N, int K, const float* x, int ldx, int B, int act,
                 float* y, int chunk, int64_t s_chunk, int64_t s_b);
+
+// VAE DecomposedConv3D as one implicit GEMM (conv_sm100.cu).  X: the padded
+// input, channels-last bf16 [frames][H][W][Cp]; weights bf16
+// [Co][kt][kh][kw][cpad64]; out planar fp32 [Co][out_cstep], element
+// (t, y, x) at (t * Ho + y) * Wo + x.
+struct Conv3dGeometry
+{
+    int Ci, Cp, cpad64, Co;
+    int H, W;
+    int kt, kh, kw, st, dt, sh, dh, dw, ph, pw;
+    int Tout, Ho, Wo;
+};
+int conv3d_pack(Context& ctx, const float* in, int64_t in_cstep, int C, int Cp, int HW, int frame0, int frames,
+                int prefix, void* X);
+int conv3d_gemm(Context& ctx, const Conv3dGeometry& g, const void* X, int frames_x, const void* Wt, const float* bias,
+                float* out, int64_t out_cstep);
 
 int launch_convert_f32_bf16(Context& ctx, const float* in, void* out, int64_t count);
 int launch_add_vectors(Context& ctx, const float* a, const float* b, float* out, int count, int period);

@@ -35,7 +35,7 @@ def ref():
 
 @pytest.fixture(scope="session")
 def golden():
-    return {name: np.load(os.path.join(GOLDEN, f"{name}.npz")) for name in ("plans", "awa", "linear", "dit_io")}
+    return {name: np.load(os.path.join(GOLDEN, f"{name}.npz")) for name in ("plans", "awa", "linear", "dit_io", "vae_conv")}
 
 
 @pytest.fixture(scope="session")

@@ -15,6 +15,10 @@ Outputs:
   awa.npz     -- AdaptiveWindowAttention::forward (CPU) on a seeded 2-sample
                  batch, fused-QKV input, shifted/unshifted x bf16 on/off.
   linear.npz  -- SharedLinear::forward on seeded inputs, with and without bias.
+  vae_conv.npz -- DecomposedConv3D::forward (oracle/_ref/libs2_ref_vae.so:
+                 src/seedvr2/decomposed_conv3d.cpp compiled unmodified) on seeded
+                 inputs: memory disabled, and three chunks with the temporal
+                 memory (initializing, then active).
   dit_io.npz  -- patchify_video / unpatchify_prediction / make_timestep_embedding
                  (oracle/_ref/libs2_ref_dit_io.so: src/seedvr2/seedvr2_dit.cpp:167-326
                  compiled unmodified) on seeded inputs, plus the return codes of
@@ -180,6 +184,43 @@ def gen_dit_io(refio: oracle.RefIO) -> None:
     np.savez_compressed(os.path.join(OUT, "dit_io.npz"), **out)
 
 
+# DecomposedConv3D cases: (name, cfg (16 values), input (c, d, h, w), chunks)
+CONV_CASES = [
+    ("k333", [16, 8, 3, 3, 3, 1, 1, 2, 1, 1, 1, 1, 1, 1, 1, 1], (8, 5, 10, 12), 1),
+    ("k333_mem", [16, 8, 3, 3, 3, 1, 1, 2, 1, 1, 1, 1, 1, 1, 1, 1], (8, 4, 10, 12), 3),
+    ("st2_nobias", [7, 5, 3, 3, 3, 2, 1, 2, 1, 1, 1, 1, 1, 1, 1, 0], (5, 5, 8, 9), 2),
+    ("k111", [6, 4, 1, 1, 1, 1, 1, 0, 1, 1, 1, 1, 0, 0, 1, 1], (4, 3, 6, 6), 1),
+    ("dil2", [6, 4, 3, 3, 3, 1, 2, 4, 1, 1, 2, 2, 2, 2, 1, 1], (4, 3, 7, 11), 2),
+]
+
+
+def conv_weights(rng, cfg):
+    co, ci, kw, kh, kt = cfg[0], cfg[1], cfg[2], cfg[3], cfg[4]
+    w = (0.1 * rng.standard_normal((kt, co, ci, kh, kw))).astype(np.float32)
+    b = (0.1 * rng.standard_normal(co)).astype(np.float32) if cfg[15] else None
+    return b, w
+
+
+def gen_vae_conv() -> None:
+    rng = np.random.default_rng(777)
+    out = {}
+    for name, cfg, (c, d, h, w), chunks in CONV_CASES:
+        b, wt = conv_weights(rng, cfg)
+        layer = oracle.RefConv3d(cfg, b, wt)
+        out[f"{name}__cfg"] = np.asarray(cfg, np.int32)
+        out[f"{name}__w"] = wt
+        if b is not None:
+            out[f"{name}__b"] = b
+        for i in range(chunks):
+            x = rng.standard_normal((c, d, h, w)).astype(np.float32)
+            state = (oracle.VAE_MEMORY_DISABLED if chunks == 1 else
+                     oracle.VAE_MEMORY_INITIALIZING if i == 0 else oracle.VAE_MEMORY_ACTIVE)
+            out[f"{name}__x{i}"] = x
+            out[f"{name}__state{i}"] = np.asarray(state, np.int32)
+            out[f"{name}__y{i}"] = layer.forward(x, state)
+    np.savez_compressed(os.path.join(OUT, "vae_conv.npz"), **out)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-tree", default=os.environ.get("S2_REFERENCE_TREE", "/root/reference"))
@@ -190,7 +231,8 @@ def main() -> None:
     gen_awa(ref)
     gen_linear(ref)
     gen_dit_io(oracle.RefIO())
-    for f in ("plans.npz", "awa.npz", "linear.npz", "dit_io.npz"):
+    gen_vae_conv()
+    for f in ("plans.npz", "awa.npz", "linear.npz", "dit_io.npz", "vae_conv.npz"):
         print(f, os.path.getsize(os.path.join(OUT, f)), "bytes")
 
 
