@@ -362,7 +362,7 @@ int s2_apply_cfg(s2_context* ctx, const float* pos, const float* neg, int64_t co
  * stride_w, stride_h, dilation_w, dilation_h, pad_w, pad_h, groups,
  * bias_term); bias: host fp32 [num_output] (bias_term) or NULL; weights: host
  * fp32 kernel_t x [num_output][num_input][kernel_h][kernel_w].  This build
- * supports groups = 1 and stride_w = 1 (-1 otherwise).
+ * supports groups = 1 and stride_w <= 2 (-1 otherwise).
  * memory_state: the VAE's temporal-memory state (seedvr2::MemoryState): with
  * ACTIVE the head frames are the previous chunk's cached frames, otherwise
  * head_frames copies of frame 0; any state but DISABLED caches the last
@@ -381,6 +381,27 @@ int s2_conv3d_output_shape(const s2_conv3d* layer, int w, int h, int d, int memo
 int s2_conv3d_forward(s2_conv3d* layer, const float* in, int64_t in_cstep, int w, int h, int d, int c,
                       int memory_state, float* out, int64_t out_cstep);
 void s2_conv3d_free(s2_conv3d* layer);
+
+/* VAE resampling layers, built from the weight-blob sequence their
+ * load_model reads:
+ *   S2_VAE_DOWNSAMPLE  VAEDownsample3D (vae_downsample3d.cpp:98-173): blob =
+ *     channels, pad_right, pad_bottom, then one DecomposedConv3D (16 config
+ *     values, bias when bias_term, kernels); zero padding on the right /
+ *     bottom, then the convolution.
+ *   S2_VAE_UPSAMPLE    VAEUpsample3D (vae_upsample3d.cpp:191-320): blob =
+ *     channels, temporal_ratio, spatial_ratio, remove_temporal_head, then the
+ *     post and the upscale DecomposedConv3D; upscale conv, pixel / temporal
+ *     shuffle (frame 1 dropped unless the memory is ACTIVE when the temporal
+ *     ratio is 2), post conv.
+ * Same shapes, memory states and -1 cases as the reference layers. */
+#define S2_VAE_DOWNSAMPLE 0
+#define S2_VAE_UPSAMPLE 1
+typedef struct s2_vae_resample s2_vae_resample;
+int s2_vae_resample_create(s2_context* ctx, int kind, const float* blob, size_t count, s2_vae_resample** out);
+int s2_vae_resample_output_shape(const s2_vae_resample* layer, int w, int h, int d, int memory_state, int* out_whdc);
+int s2_vae_resample_forward(s2_vae_resample* layer, const float* in, int64_t in_cstep, int w, int h, int d, int c,
+                            int memory_state, float* out, int64_t out_cstep);
+void s2_vae_resample_free(s2_vae_resample* layer);
 
 /* ---------------------------------------------------------------------------
  * Multi-GPU (one process per GPU over NVLink).  The reference has no

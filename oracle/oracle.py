@@ -330,6 +330,129 @@ class Port:
         return out, nm
 
 
+class PortConv3dLayer:
+    """DecomposedConv3D with its temporal memory (decomposed_conv3d.cpp:605-765) on top of the stateless
+    C restatement Port.conv3d_forward."""
+
+    def __init__(self, port: Port, cfg, bias, weights, emulate_bf16=False):
+        self.port, self.cfg, self.bias = port, list(cfg), bias
+        self.emulate = emulate_bf16
+        self.weights = port.round_bf16(weights) if emulate_bf16 else weights
+        self.memory = None
+
+    def forward(self, x, state):
+        if state != VAE_MEMORY_ACTIVE:
+            self.memory = None
+        x = self.port.round_bf16(x) if self.emulate else _f32(x)
+        mem = self.memory if (state == VAE_MEMORY_ACTIVE and self.memory is not None) else None
+        if mem is not None and mem.shape[2:] != x.shape[2:]:
+            raise ValueError(-1)
+        y, nm = self.port.conv3d_forward(self.cfg, self.bias, self.weights, x, mem,
+                                         keep_memory=state != VAE_MEMORY_DISABLED)
+        if state != VAE_MEMORY_DISABLED and nm is not None:
+            self.memory = nm
+        return y
+
+
+def split_conv_blob(blob, offset=0):
+    """(cfg, bias, weights, next offset) of one DecomposedConv3D in a weight blob (its load_model order)."""
+    cfg = [int(v) for v in blob[offset:offset + 16]]
+    co, ci, kw, kh, kt = cfg[:5]
+    o = offset + 16
+    bias = None
+    if cfg[15]:
+        bias = _f32(blob[o:o + co])
+        o += co
+    n = kt * co * ci * kh * kw
+    w = _f32(blob[o:o + n]).reshape(kt, co, ci, kh, kw)
+    return cfg, bias, w, o + n
+
+
+class PortDownsample:
+    """VAEDownsample3D::forward (vae_downsample3d.cpp:145-173): zero padding on the right / bottom, then
+    its DecomposedConv3D.  blob: its load_model sequence (channels, pad_right, pad_bottom, conv blob)."""
+
+    def __init__(self, port: Port, blob, emulate_bf16=False):
+        blob = _f32(blob)
+        self.channels, self.pad_right, self.pad_bottom = (int(v) for v in blob[:3])
+        cfg, b, w, _ = split_conv_blob(blob, 3)
+        self.conv = PortConv3dLayer(port, cfg, b, w, emulate_bf16)
+
+    def forward(self, x, state):
+        x = _f32(x)
+        c, d, h, w = x.shape
+        if c != self.channels:
+            raise ValueError(-1)
+        padded = np.zeros((c, d, h + self.pad_bottom, w + self.pad_right), np.float32)
+        padded[:, :, :h, :w] = x
+        return self.conv.forward(padded, state)
+
+
+class PortUpsample:
+    """VAEUpsample3D::forward (vae_upsample3d.cpp:258-320): upscale conv to channels * tr * sr^2, the
+    pixel / temporal shuffle (dropping frame 1 unless the memory is active, when tr = 2), then the post
+    conv.  blob: config (channels, temporal_ratio, spatial_ratio, remove_temporal_head), post conv blob,
+    upscale conv blob."""
+
+    def __init__(self, port: Port, blob, emulate_bf16=False):
+        blob = _f32(blob)
+        self.channels, self.tr, self.sr, self.remove_head = (int(v) for v in blob[:4])
+        cfg, b, w, o = split_conv_blob(blob, 4)
+        self.post = PortConv3dLayer(port, cfg, b, w, emulate_bf16)
+        cfg, b, w, _ = split_conv_blob(blob, o)
+        self.upscale = PortConv3dLayer(port, cfg, b, w, emulate_bf16)
+
+    def forward(self, x, state):
+        x = _f32(x)
+        if x.shape[0] != self.channels:
+            raise ValueError(-1)
+        packed = self.upscale.forward(x, state)
+        ch, tr, sr = self.channels, self.tr, self.sr
+        _, pd, ph, pw = packed.shape
+        # packed channel ((yo * sr + xo) * tr + z) * ch + c -> frame * tr + z, pixel (y * sr + yo, x * sr + xo)
+        p = packed.reshape(sr, sr, tr, ch, pd, ph, pw)
+        sh = np.transpose(p, (3, 4, 2, 5, 0, 6, 1)).reshape(ch, pd * tr, ph * sr, pw * sr)
+        if self.remove_head and state != VAE_MEMORY_ACTIVE:
+            sh = np.concatenate([sh[:, :1], sh[:, 2:]], axis=1)
+        return self.post.forward(np.ascontiguousarray(sh), state)
+
+
+class RefResample:
+    """The reference's own VAEDownsample3D (kind 0) / VAEUpsample3D (kind 1) (oracle/_ref/libs2_ref_vae.so)."""
+
+    def __init__(self, kind, blob, path: str = REF_VAE_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        lib = C.CDLL(path)
+        lib.s2ref_resample_create.argtypes = [C.c_int, _f32p, C.c_size_t]
+        lib.s2ref_resample_create.restype = C.c_void_p
+        lib.s2ref_resample_forward.argtypes = [C.c_void_p, C.c_int, _f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p,
+                                               C.c_size_t, _i32p]
+        lib.s2ref_resample_free.argtypes = [C.c_void_p]
+        self.lib = lib
+        blob = _f32(blob)
+        self.handle = lib.s2ref_resample_create(kind, blob, blob.size)
+        if not self.handle:
+            raise ValueError("load failed")
+
+    def forward(self, x, memory_state):
+        x = _f32(x)
+        c, d, h, w = x.shape
+        cap = 64 * max(c, 8) * (2 * d + 8) * (2 * h + 8) * (2 * w + 8)
+        out = np.zeros(cap, np.float32)
+        dims = np.zeros(4, np.int32)
+        r = self.lib.s2ref_resample_forward(self.handle, memory_state, x, w, h, d, c, out, cap, dims)
+        if r != 0:
+            raise ValueError(r)
+        ow, oh, od, oc = dims.tolist()
+        return out[:ow * oh * od * oc].reshape(oc, od, oh, ow).copy()
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            self.lib.s2ref_resample_free(self.handle)
+            self.handle = None
+
+
 def _f64(a) -> np.ndarray:
     return np.asarray(a, dtype=np.float64)
 

@@ -1,7 +1,8 @@
-// extern "C" wrapper around the reference's OWN DecomposedConv3D layer
-// (src/seedvr2/decomposed_conv3d.cpp, compiled unmodified with NCNN_VULKAN=0
-// against the clean-room ncnn shim, whose "Convolution" restates ncnn's
-// spatial convolution).  Built by oracle/Makefile into
+// extern "C" wrapper around the reference's OWN VAE layers DecomposedConv3D,
+// VAEDownsample3D and VAEUpsample3D (src/seedvr2/decomposed_conv3d.cpp,
+// vae_downsample3d.cpp, vae_upsample3d.cpp, compiled unmodified with
+// NCNN_VULKAN=0 against the clean-room ncnn shim, whose "Convolution"
+// restates ncnn's spatial convolution).  Built by oracle/Makefile into
 // oracle/_ref/libs2_ref_vae.so.
 //
 // TEST INFRASTRUCTURE ONLY: the tests and the fixture generator load it as the
@@ -11,6 +12,8 @@
 
 #include "decomposed_conv3d.h"
 #include "modelbin.h"
+#include "vae_downsample3d.h"
+#include "vae_upsample3d.h"
 
 using seedvr2::DecomposedConv3D;
 
@@ -71,6 +74,50 @@ int s2ref_conv3d_forward(void* handle, int memory_state, const float* in, int w,
 void s2ref_conv3d_free(void* handle)
 {
     delete static_cast<DecomposedConv3D*>(handle);
+}
+
+// VAEDownsample3D (kind 0) or VAEUpsample3D (kind 1) from the weight blob
+// sequence its load_model reads (config values, then each DecomposedConv3D's
+// config, bias and kernels).  Returns a layer handle or 0.
+void* s2ref_resample_create(int kind, const float* blob, size_t count)
+{
+    ncnn::Layer* layer = kind == 0 ? static_cast<ncnn::Layer*>(new seedvr2::VAEDownsample3D)
+                                   : static_cast<ncnn::Layer*>(new seedvr2::VAEUpsample3D);
+    ncnn::ModelBinFromFloats mb(blob, count);
+    ncnn::Option opt;
+    if (layer->load_model(mb) != 0 || layer->create_pipeline(opt) != 0)
+    {
+        delete layer;
+        return 0;
+    }
+    return layer;
+}
+
+int s2ref_resample_forward(void* handle, int memory_state, const float* in, int w, int h, int d, int c, float* out,
+                           size_t out_capacity, int* out_dims)
+{
+    const ncnn::Layer* layer = static_cast<const ncnn::Layer*>(handle);
+    seedvr2::set_vae_memory_state(static_cast<seedvr2::MemoryState>(memory_state));
+    ncnn::Mat bottom(w, h, d, c, 4u, 1, 1);
+    const size_t plane = (size_t)w * h * d;
+    for (int ch = 0; ch < c; ch++) std::memcpy(bottom.channel(ch).data, in + plane * ch, plane * sizeof(float));
+    ncnn::Mat top;
+    ncnn::Option opt;
+    const int r = layer->forward(bottom, top, opt);
+    if (r != 0) return r;
+    out_dims[0] = top.w;
+    out_dims[1] = top.h;
+    out_dims[2] = top.d;
+    out_dims[3] = top.c;
+    const size_t oplane = (size_t)top.w * top.h * top.d;
+    if (oplane * top.c > out_capacity) return -1;
+    for (int ch = 0; ch < top.c; ch++) std::memcpy(out + oplane * ch, top.channel(ch).data, oplane * sizeof(float));
+    return 0;
+}
+
+void s2ref_resample_free(void* handle)
+{
+    delete static_cast<ncnn::Layer*>(handle);
 }
 
 } // extern "C"

@@ -55,7 +55,11 @@ EXPORTED = [
     "s2_dit_forward_frontend", "s2_dit_forward_tail", "s2_dit_forward_step", "s2_dit_forward_step_host",
     "s2_dit_denoise", "s2_dit_denoise_host", "s2_apply_cfg",
     "s2_conv3d_create", "s2_conv3d_output_shape", "s2_conv3d_forward", "s2_conv3d_free",
+    "s2_vae_resample_create", "s2_vae_resample_output_shape", "s2_vae_resample_forward", "s2_vae_resample_free",
 ]
+
+S2_VAE_DOWNSAMPLE = 0
+S2_VAE_UPSAMPLE = 1
 
 S2_VAE_MEMORY_DISABLED = 0
 S2_VAE_MEMORY_INITIALIZING = 1
@@ -178,6 +182,10 @@ def lib() -> C.CDLL:
     L.s2_conv3d_output_shape.argtypes = [vp, ip, ip, ip, ip, pint]
     L.s2_conv3d_forward.argtypes = [vp, vp, i64, ip, ip, ip, ip, ip, vp, i64]
     L.s2_conv3d_free.argtypes = [vp]
+    L.s2_vae_resample_create.argtypes = [vp, ip, vp, C.c_size_t, C.POINTER(vp)]
+    L.s2_vae_resample_output_shape.argtypes = [vp, ip, ip, ip, ip, pint]
+    L.s2_vae_resample_forward.argtypes = [vp, vp, i64, ip, ip, ip, ip, ip, vp, i64]
+    L.s2_vae_resample_free.argtypes = [vp]
     _lib = L
     return L
 
@@ -609,6 +617,50 @@ class Conv3d:
     def close(self):
         if self.handle:
             lib().s2_conv3d_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class VaeResample:
+    """s2_vae_resample: VAEDownsample3D (kind S2_VAE_DOWNSAMPLE) or VAEUpsample3D (S2_VAE_UPSAMPLE) from the
+    weight-blob sequence its load_model reads (host fp32)."""
+
+    def __init__(self, ctx: Context, kind, blob):
+        import numpy as np
+
+        self.ctx = ctx
+        b = np.ascontiguousarray(blob, dtype=np.float32)
+        h = C.c_void_p()
+        check(lib().s2_vae_resample_create(ctx.handle, int(kind), ptr(b), b.size, C.byref(h)),
+              "s2_vae_resample_create")
+        self.handle = h
+
+    def output_shape(self, w, h, d, memory_state):
+        out = (C.c_int * 4)()
+        check(lib().s2_vae_resample_output_shape(self.handle, w, h, d, memory_state, out),
+              "s2_vae_resample_output_shape")
+        return list(out)
+
+    def forward(self, x, memory_state=S2_VAE_MEMORY_DISABLED, out=None):
+        """x: fp32 CUDA [c, d, h, w] -> fp32 CUDA [c', t, oh, ow]."""
+        import torch
+
+        c, d, h, w = x.shape
+        ow, oh, od, oc = self.output_shape(w, h, d, memory_state)
+        if out is None:
+            out = torch.empty((oc, od, oh, ow), dtype=torch.float32, device=x.device)
+        check(lib().s2_vae_resample_forward(self.handle, x.data_ptr(), d * h * w, w, h, d, c, memory_state,
+                                            out.data_ptr(), od * oh * ow), "s2_vae_resample_forward")
+        return out
+
+    def close(self):
+        if self.handle:
+            lib().s2_vae_resample_free(self.handle)
             self.handle = None
 
     def __del__(self):

@@ -4,7 +4,7 @@
 // accumulation.
 //
 //   out[co][t][y][x] = bias[co] + sum_{kt, ky, kx, ci} W[co][kt][ky][kx][ci] *
-//                      X[t*st + kt*dt][y*sh + ky*dh - ph][x + kx*dw - pw][ci]
+//                      X[t*st + kt*dt][y*sh + ky*dh - ph][x*sw + kx*dw - pw][ci]
 //
 // X is the layer input with its head frames materialised (the cached frames
 // of the previous chunk, or copies of frame 0), stored channels-last in bf16
@@ -12,8 +12,9 @@
 // A tile is 128 output pixels of one output row times 128 output channels;
 // its K loop walks the taps (kt, ky, kx) and 64-channel blocks.  Warp 0 TMA-
 // loads the A box straight out of X with a 4-D tensor map at the tap's
-// shifted coordinates (zero padding comes from the out-of-range fill) and the
-// matching 128 x 64 weight box; warp 1 issues tcgen05.mma (128 x 128 x 16,
+// shifted coordinates (zero padding comes from the out-of-range fill; a
+// spatial stride sw is the box's traversal stride along x) and the matching
+// 128 x 64 weight box; warp 1 issues tcgen05.mma (128 x 128 x 16,
 // bf16 -> fp32) into one of two TMEM accumulators; warps 2-5 add the bias and
 // store the tile into the planar fp32 output (ncnn's [c][d][h][w] blob: for
 // each output channel a warp writes 32 consecutive pixels, 128 bytes).
@@ -41,7 +42,7 @@ struct ConvArgs
 {
     int Tout, Ho, Wo, Co;
     int xblocks, nblocks, num_tiles;
-    int kh, kw, st, dt, sh, dh, dw, ph, pw;
+    int kh, kw, st, dt, sh, sw, dh, dw, ph, pw;
     int cblocks, num_kb, cpad64;
     const float* bias;
     float* out;
@@ -133,7 +134,7 @@ __global__ void __launch_bounds__(C_THREADS, 1)
                     const int k_y = rem / args.kw, k_x = rem - k_y * args.kw;
                     uint8_t* sa = smem + stage * C_STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[stage], C_STAGE_BYTES);
-                    tma_load_4d(sa, &tmap_x, &full[stage], cb * CBK, x0 + k_x * args.dw - args.pw,
+                    tma_load_4d(sa, &tmap_x, &full[stage], cb * CBK, x0 * args.sw + k_x * args.dw - args.pw,
                                 y * args.sh + k_y * args.dh - args.ph, to * args.st + k_t * args.dt);
                     tma_load_2d(sa + C_A_BYTES, &tmap_w, &full[stage], tap * args.cpad64 + cb * CBK, n0);
                     issued[stage] = 1;
@@ -302,6 +303,34 @@ __global__ void __launch_bounds__(256) conv_pack_kernel(const float* __restrict_
     }
 }
 
+// VAEUpsample3D's shuffle (vae_upsample3d.cpp:274-318): output channel c,
+// frame t, pixel (Y, X) of [ch][out_t][ph*sr][pw*sr] takes packed channel
+// ((Y % sr * sr + X % sr) * tr + z) * ch + c, frame s / tr, pixel (Y / sr,
+// X / sr), where s = t, or t + 1 past frame 0 when frame 1 is dropped
+// (remove_head).  One output element per thread, writes coalesced.
+__global__ void upsample_shuffle_kernel(const float* __restrict__ packed, int64_t pcstep, int ch, int tr, int sr,
+                                        int pd, int ph, int pw, int out_t, int remove_head, float* __restrict__ out,
+                                        int64_t ocstep)
+{
+    const int OW = pw * sr, OH = ph * sr;
+    const int64_t per_c = (int64_t)out_t * OH * OW;
+    const int64_t total = per_c * ch;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+    {
+        const int c = (int)(i / per_c);
+        int64_t r = i - (int64_t)c * per_c;
+        const int t = (int)(r / ((int64_t)OH * OW));
+        r -= (int64_t)t * OH * OW;
+        const int Y = (int)(r / OW), X = (int)(r - (int64_t)Y * OW);
+        const int s = (remove_head && t >= 1) ? t + 1 : t;
+        const int frame = s / tr, z = s - frame * tr;
+        const int pc = (((Y % sr) * sr + X % sr) * tr + z) * ch + c;
+        out[(int64_t)c * ocstep + r + (int64_t)t * OH * OW] =
+            __ldg(packed + (int64_t)pc * pcstep + ((int64_t)frame * ph + Y / sr) * pw + X / sr);
+        (void)pd;
+    }
+}
+
 } // namespace
 
 int conv3d_pack(Context& ctx, const float* in, int64_t in_cstep, int C, int Cp, int HW, int frame0, int frames,
@@ -324,8 +353,11 @@ int conv3d_gemm(Context& ctx, const Conv3dGeometry& g, const void* X, int frames
     CUtensorMap tx, tw;
     const uint64_t xd[4] = {(uint64_t)g.Cp, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)frames_x};
     const uint64_t xs[3] = {(uint64_t)g.Cp * 2, (uint64_t)g.W * g.Cp * 2, (uint64_t)g.H * g.W * g.Cp * 2};
-    const uint32_t xb[4] = {CBK, CBM, 1, 1};
-    int r = make_tmap_bf16_4d(&tx, X, xd, xs, xb);
+    // a spatial stride sw reads every sw-th pixel of a box sw * 128 pixels wide
+    const uint32_t xb[4] = {CBK, (uint32_t)(CBM * g.sw), 1, 1};
+    const uint32_t xe[4] = {1, (uint32_t)g.sw, 1, 1};
+    if (g.sw < 1 || CBM * g.sw > 256) return S2_ERR_INVALID;
+    int r = make_tmap_bf16_4d(&tx, X, xd, xs, xb, xe);
     // B: weights [Co][taps * cpad64] bf16, boxes of 64 x 128
     const int taps = g.kt * g.kh * g.kw;
     if (r == S2_OK)
@@ -345,6 +377,7 @@ int conv3d_gemm(Context& ctx, const Conv3dGeometry& g, const void* X, int frames
     a.st = g.st;
     a.dt = g.dt;
     a.sh = g.sh;
+    a.sw = g.sw;
     a.dh = g.dh;
     a.dw = g.dw;
     a.ph = g.ph;
@@ -391,6 +424,10 @@ struct s2_conv3d
     s2::DeviceBuffer x;     // padded input, channels-last bf16
     s2::DeviceBuffer mem;   // cached frames of the previous chunk, same layout
     int mem_frames = 0, mem_w = 0, mem_h = 0;
+    // zero columns / rows appended on the right / bottom of every frame
+    // (VAEDownsample3D's padding, vae_downsample3d.cpp:154-168); they are the
+    // tensor map's out-of-range fill, never stored
+    int pad_right = 0, pad_bottom = 0;
     ~s2_conv3d()
     {
         if (wt) cudaFree(wt);
@@ -408,9 +445,12 @@ int conv3d_shape(const s2_conv3d* l, int w, int h, int d, int prefix, int& Tout,
     const int padded = d + prefix, extent = g.dt * (g.kt - 1) + 1;
     if (w <= 0 || h <= 0 || d <= 0 || padded < extent) return S2_ERR_INVALID;
     Tout = (padded - extent) / g.st + 1;
-    Wo = (w + 2 * g.pw - (g.dw * (g.kw - 1) + 1)) + 1;
-    Ho = (h + 2 * g.ph - (g.dh * (g.kh - 1) + 1)) / g.sh + 1;
-    return (Wo > 0 && Ho > 0) ? S2_OK : S2_ERR_INVALID;
+    const int ew = w + l->pad_right + 2 * g.pw - (g.dw * (g.kw - 1) + 1);
+    const int eh = h + l->pad_bottom + 2 * g.ph - (g.dh * (g.kh - 1) + 1);
+    if (ew < 0 || eh < 0) return S2_ERR_INVALID;
+    Wo = ew / g.sw + 1;
+    Ho = eh / g.sh + 1;
+    return S2_OK;
 }
 
 int conv3d_prefix(const s2_conv3d* l, int w, int h, int memory_state, bool& use_memory)
@@ -433,7 +473,7 @@ int s2_conv3d_create(s2_context* ctx, const int* cfg, const float* bias, const f
     if (co <= 0 || ci <= 0 || kw <= 0 || kh <= 0 || kt <= 0 || cfg[5] <= 0 || cfg[6] <= 0 || cfg[8] <= 0 ||
         cfg[9] <= 0 || cfg[10] <= 0 || cfg[11] <= 0 || cfg[14] <= 0 || ci % cfg[14] || co % cfg[14] || cfg[7] < 0)
         return S2_ERR_INVALID;
-    if (cfg[14] != 1 || cfg[8] != 1 || cfg[12] < 0 || cfg[13] < 0 || (cfg[15] && !bias)) return S2_ERR_INVALID;
+    if (cfg[14] != 1 || cfg[8] > 2 || cfg[12] < 0 || cfg[13] < 0 || (cfg[15] && !bias)) return S2_ERR_INVALID;
     s2::Context& c = ctx->c;
     if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
     std::unique_ptr<s2_conv3d> l(new s2_conv3d);
@@ -450,6 +490,7 @@ int s2_conv3d_create(s2_context* ctx, const int* cfg, const float* bias, const f
     g.st = cfg[5];
     g.dt = cfg[6];
     g.sh = cfg[9];
+    g.sw = cfg[8];
     g.dw = cfg[10];
     g.dh = cfg[11];
     g.pw = cfg[12];
@@ -548,6 +589,164 @@ int s2_conv3d_forward(s2_conv3d* l, const float* in, int64_t in_cstep, int w, in
 }
 
 void s2_conv3d_free(s2_conv3d* l)
+{
+    if (!l) return;
+    cudaSetDevice(l->ctx->c.device);
+    cudaStreamSynchronize(l->ctx->c.stream);
+    delete l;
+}
+
+} // extern "C"
+
+// ---------------------------------------------------------------- VAE resampling layers
+struct s2_vae_resample
+{
+    s2_context* ctx = nullptr;
+    int kind = 0;
+    int channels = 0;
+    int pad_right = 0, pad_bottom = 0;                   // downsample
+    int tr = 1, sr = 1, remove_head = 0;                 // upsample
+    s2_conv3d* conv = nullptr;                           // downsample conv / upsample post conv
+    s2_conv3d* upscale = nullptr;                        // upsample
+    s2::DeviceBuffer packed, shuffled;
+    ~s2_vae_resample()
+    {
+        delete conv;
+        delete upscale;
+    }
+};
+
+namespace {
+
+// One DecomposedConv3D out of a load_model blob: config (16), bias, kernels.
+int conv_from_blob(s2_context* ctx, const float* blob, size_t count, size_t& off, s2_conv3d** out)
+{
+    if (off + 16 > count) return S2_ERR_INVALID;
+    int cfg[16];
+    for (int i = 0; i < 16; i++) cfg[i] = (int)blob[off + i];
+    const size_t co = cfg[0] > 0 ? cfg[0] : 0, ci = cfg[1] > 0 ? cfg[1] : 0, kw = cfg[2] > 0 ? cfg[2] : 0,
+                 kh = cfg[3] > 0 ? cfg[3] : 0, kt = cfg[4] > 0 ? cfg[4] : 0;
+    size_t o = off + 16;
+    const float* bias = nullptr;
+    if (cfg[15])
+    {
+        bias = blob + o;
+        o += co;
+    }
+    const size_t nw = kt * co * ci * kh * kw;
+    if (o + nw > count) return S2_ERR_INVALID;
+    const int r = s2_conv3d_create(ctx, cfg, bias, blob + o, out);
+    off = o + nw;
+    return r;
+}
+
+// upsample: output frames of the shuffle for `pd` packed frames
+int shuffled_frames(const s2_vae_resample* l, int pd, int memory_state)
+{
+    const bool rm = l->remove_head && memory_state != S2_VAE_MEMORY_ACTIVE;
+    return pd * l->tr - (rm ? 1 : 0);
+}
+
+} // namespace
+
+extern "C" {
+
+int s2_vae_resample_create(s2_context* ctx, int kind, const float* blob, size_t count, s2_vae_resample** out)
+{
+    if (!ctx || !blob || !out || (kind != S2_VAE_DOWNSAMPLE && kind != S2_VAE_UPSAMPLE)) return S2_ERR_INVALID;
+    *out = nullptr;
+    std::unique_ptr<s2_vae_resample> l(new s2_vae_resample);
+    l->ctx = ctx;
+    l->kind = kind;
+    size_t off = 0;
+    int r;
+    if (kind == S2_VAE_DOWNSAMPLE)
+    {
+        // VAEDownsample3D::load_model (vae_downsample3d.cpp:98-112)
+        if (count < 3) return S2_ERR_INVALID;
+        l->channels = (int)blob[0];
+        l->pad_right = (int)blob[1];
+        l->pad_bottom = (int)blob[2];
+        if (l->channels <= 0 || l->pad_right < 0 || l->pad_bottom < 0 || (l->pad_right == 0 && l->pad_bottom == 0))
+            return S2_ERR_INVALID;
+        off = 3;
+        if ((r = conv_from_blob(ctx, blob, count, off, &l->conv)) != S2_OK) return r;
+        l->conv->pad_right = l->pad_right;
+        l->conv->pad_bottom = l->pad_bottom;
+    }
+    else
+    {
+        // VAEUpsample3D::load_model (vae_upsample3d.cpp:191-213): config, post conv, upscale conv
+        if (count < 4) return S2_ERR_INVALID;
+        l->channels = (int)blob[0];
+        l->tr = (int)blob[1];
+        l->sr = (int)blob[2];
+        l->remove_head = (int)blob[3] != 0;
+        if (l->channels <= 0 || (l->tr != 1 && l->tr != 2) || (l->sr != 1 && l->sr != 2) ||
+            (l->remove_head != 0) != (l->tr == 2))
+            return S2_ERR_INVALID;
+        off = 4;
+        if ((r = conv_from_blob(ctx, blob, count, off, &l->conv)) != S2_OK) return r;
+        if ((r = conv_from_blob(ctx, blob, count, off, &l->upscale)) != S2_OK) return r;
+    }
+    *out = l.release();
+    return S2_OK;
+}
+
+int s2_vae_resample_output_shape(const s2_vae_resample* l, int w, int h, int d, int memory_state, int* out_whdc)
+{
+    if (!l || !out_whdc) return S2_ERR_INVALID;
+    if (l->kind == S2_VAE_DOWNSAMPLE) return s2_conv3d_output_shape(l->conv, w, h, d, memory_state, out_whdc);
+    int p[4];
+    int r = s2_conv3d_output_shape(l->upscale, w, h, d, memory_state, p);
+    if (r != S2_OK) return r;
+    const int t = shuffled_frames(l, p[2], memory_state);
+    if (t <= 0) return S2_ERR_INVALID;
+    return s2_conv3d_output_shape(l->conv, p[0] * l->sr, p[1] * l->sr, t, memory_state, out_whdc);
+}
+
+int s2_vae_resample_forward(s2_vae_resample* l, const float* in, int64_t in_cstep, int w, int h, int d, int c,
+                            int memory_state, float* out, int64_t out_cstep)
+{
+    if (!l || !in || !out) return S2_ERR_INVALID;
+    if (c != l->channels) return S2_ERR_INVALID;
+    if (l->kind == S2_VAE_DOWNSAMPLE)
+        return s2_conv3d_forward(l->conv, in, in_cstep, w, h, d, c, memory_state, out, out_cstep);
+    s2::Context& ctx = l->ctx->c;
+    if (cudaSetDevice(ctx.device) != cudaSuccess) return S2_ERR_CUDA;
+    int p[4];
+    int r = s2_conv3d_output_shape(l->upscale, w, h, d, memory_state, p);
+    if (r != S2_OK) return r;
+    const int ratio = l->tr * l->sr * l->sr;
+    if (p[3] != l->channels * ratio) return S2_ERR_INVALID; // vae_upsample3d.cpp:270-272
+    const int64_t pplane = (int64_t)p[0] * p[1] * p[2];
+    if ((r = l->packed.ensure((size_t)pplane * p[3] * 4)) != S2_OK) return r;
+    float* packed = static_cast<float*>(l->packed.ptr);
+    if ((r = s2_conv3d_forward(l->upscale, in, in_cstep, w, h, d, c, memory_state, packed, pplane)) != S2_OK)
+        return r;
+    const int ot = shuffled_frames(l, p[2], memory_state);
+    if (ot <= 0) return S2_ERR_INVALID;
+    const int OW = p[0] * l->sr, OH = p[1] * l->sr;
+    const int64_t splane = (int64_t)OW * OH * ot;
+    if ((r = l->shuffled.ensure((size_t)splane * l->channels * 4)) != S2_OK) return r;
+    float* sh = static_cast<float*>(l->shuffled.ptr);
+    {
+        const int64_t total = splane * l->channels;
+        int64_t blocks = (total + 255) / 256;
+        if (blocks > (int64_t)ctx.num_sms * 16) blocks = (int64_t)ctx.num_sms * 16;
+        s2::ProfileScope prof(ctx, s2::K_OTHER, 0.0, (double)total * 8.0);
+        s2::upsample_shuffle_kernel<<<(int)blocks, 256, 0, ctx.stream>>>(packed, pplane, l->channels, l->tr, l->sr,
+                                                                        p[2], p[1], p[0], ot,
+                                                                        l->remove_head && memory_state !=
+                                                                                              S2_VAE_MEMORY_ACTIVE,
+                                                                        sh, splane);
+        ctx.launches++;
+        if (cudaGetLastError() != cudaSuccess) return S2_ERR_CUDA;
+    }
+    return s2_conv3d_forward(l->conv, sh, splane, OW, OH, ot, l->channels, memory_state, out, out_cstep);
+}
+
+void s2_vae_resample_free(s2_vae_resample* l)
 {
     if (!l) return;
     cudaSetDevice(l->ctx->c.device);

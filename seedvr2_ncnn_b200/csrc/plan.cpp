@@ -387,7 +387,7 @@ int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64
 }
 
 int make_tmap_bf16_4d(CUtensorMap* map, const void* base, const uint64_t* dims, const uint64_t* stride_bytes,
-                      const uint32_t* box)
+                      const uint32_t* box, const uint32_t* element_strides)
 {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return S2_ERR_DEVICE;
@@ -397,7 +397,8 @@ int make_tmap_bf16_4d(CUtensorMap* map, const void* base, const uint64_t* dims, 
     const cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
     const cuuint64_t st[3] = {stride_bytes[0], stride_bytes[1], stride_bytes[2]};
     const cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
-    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const cuuint32_t estr[4] = {element_strides[0], element_strides[1], element_strides[2], element_strides[3]};
+    if (estr[0] != 1) return S2_ERR_INVALID;
     const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), d, st, bx, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

@@ -150,9 +150,11 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int f32, uint64_t inner, ui
                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
 
 // bf16 4-D tensor (dims[0] innermost, 16-byte aligned strides of dims 1..3 in
-// bytes), 128-byte swizzle, box[0] * 2 = 128 bytes; out-of-range elements read 0.
+// bytes), 128-byte swizzle, box[0] * 2 = 128 bytes; out-of-range elements read
+// 0.  element_strides[i]: traversal stride (the box holds box[i] /
+// element_strides[i] elements along dim i); element_strides[0] must be 1.
 int make_tmap_bf16_4d(CUtensorMap* map, const void* base, const uint64_t* dims, const uint64_t* stride_bytes,
-                      const uint32_t* box);
+                      const uint32_t* box, const uint32_t* element_strides);
 
 // kernels (launchers return S2_* codes)
 int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void* A0, const void* A1, const void* W,
@@ -247,7 +249,7 @@ struct Conv3dGeometry
 {
     int Ci, Cp, cpad64, Co;
     int H, W;
-    int kt, kh, kw, st, dt, sh, dh, dw, ph, pw;
+    int kt, kh, kw, st, dt, sh, sw, dh, dw, ph, pw;
     int Tout, Ho, Wo;
 };
 int conv3d_pack(Context& ctx, const float* in, int64_t in_cstep, int C, int Cp, int HW, int frame0, int frames,

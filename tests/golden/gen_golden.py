@@ -194,6 +194,35 @@ CONV_CASES = [
 ]
 
 
+def conv_blob(rng, co, ci, k, kt, st, head, sw, pad, bias):
+    """One DecomposedConv3D's load_model blob: config, bias, kernels."""
+    cfg = [co, ci, k, k, kt, st, 1, head, sw, sw, 1, 1, pad, pad, 1, int(bias)]
+    parts = [np.asarray(cfg, np.float32)]
+    if bias:
+        parts.append((0.1 * rng.standard_normal(co)).astype(np.float32))
+    parts.append((0.1 * rng.standard_normal(kt * co * ci * k * k)).astype(np.float32))
+    return np.concatenate(parts)
+
+
+def resample_blob(rng, kind, head):
+    """VAEDownsample3D (0): 8 channels, pad right / bottom 1, 3x3 spatial stride 2 over 3 frames.
+    VAEUpsample3D (1): 4 channels, temporal and spatial ratio 2 (head frame removed), 3x3x3 post and
+    upscale convs."""
+    if kind == 0:
+        return np.concatenate([np.asarray([8, 1, 1], np.float32), conv_blob(rng, 8, 8, 3, 3, 1, head, 2, 0, True)])
+    return np.concatenate([np.asarray([4, 2, 2, 1], np.float32), conv_blob(rng, 4, 4, 3, 3, 1, head, 1, 1, True),
+                           conv_blob(rng, 32, 4, 3, 3, 1, head, 1, 1, True)])
+
+
+# (name, kind, head frames, input (c, d, h, w), memory states per chunk)
+RESAMPLE_CASES = [
+    ("down", 0, 2, (8, 3, 9, 12), [1, 2, 2]),
+    ("down_off", 0, 2, (8, 4, 10, 10), [0]),
+    ("up", 1, 2, (4, 2, 5, 6), [1, 2, 2]),
+    ("up_off", 1, 2, (4, 3, 4, 4), [0]),
+]
+
+
 def conv_weights(rng, cfg):
     co, ci, kw, kh, kt = cfg[0], cfg[1], cfg[2], cfg[3], cfg[4]
     w = (0.1 * rng.standard_normal((kt, co, ci, kh, kw))).astype(np.float32)
@@ -218,6 +247,16 @@ def gen_vae_conv() -> None:
             out[f"{name}__x{i}"] = x
             out[f"{name}__state{i}"] = np.asarray(state, np.int32)
             out[f"{name}__y{i}"] = layer.forward(x, state)
+    for name, kind, head, (c, d, h, w), states in RESAMPLE_CASES:
+        blob = resample_blob(rng, kind, head)
+        layer = oracle.RefResample(kind, blob)
+        out[f"{name}__blob"] = blob
+        out[f"{name}__kind"] = np.asarray(kind, np.int32)
+        for i, st in enumerate(states):
+            x = rng.standard_normal((c, d, h, w)).astype(np.float32)
+            out[f"{name}__x{i}"] = x
+            out[f"{name}__state{i}"] = np.asarray(st, np.int32)
+            out[f"{name}__y{i}"] = layer.forward(x, st)
     np.savez_compressed(os.path.join(OUT, "vae_conv.npz"), **out)
 
 

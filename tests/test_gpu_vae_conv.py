@@ -102,10 +102,69 @@ def test_conv3d_rejects_like_the_reference(gpu_ctx, s2lib):
     assert fwd(8, 4, 1) == 0           # initializing: caches the last two frames
     assert fwd(8, 1, 2) == 0           # active: two cached frames + one new frame -> one output frame
     assert fwd(8, 1, 2, hw=5) == -1    # cached frames of another size
-    # groups and spatial strides this build does not implement are refused at creation
-    bad = list(cfg)
-    bad[8] = 2
-    with pytest.raises(s2lib.S2Error):
-        s2lib.Conv3d(gpu_ctx, bad, b, w)
+    # grouped convolutions and spatial strides above 2, which this build does not implement, are refused
+    for i, v in ((14, 2), (8, 3)):
+        bad = list(cfg)
+        bad[i] = v
+        with pytest.raises(s2lib.S2Error):
+            s2lib.Conv3d(gpu_ctx, bad, b, w)
     torch.cuda.synchronize()
     layer.close()
+
+
+# ---- VAE resampling layers (VAEDownsample3D / VAEUpsample3D) ----
+def _resample_cases():
+    from tests.golden.gen_golden import RESAMPLE_CASES
+
+    return [c[0] for c in RESAMPLE_CASES]
+
+
+@pytest.mark.parametrize("name", _resample_cases())
+def test_resample_golden(gpu_ctx, s2lib, port, golden, name):
+    """Against the reference's own layers (golden, fp32): the DiT gate.  The downsample (one conv, spatial
+    stride 2 through the tensor map's traversal stride) also against the oracle fed bf16-rounded inputs and
+    weights: rel <= 1e-3; the upsample chains two convs around a shuffle, so its bf16-emulated comparison
+    allows 5e-3 (a bf16 rounding of the intermediate can flip)."""
+    import torch
+
+    from oracle import oracle
+
+    g = golden["vae_conv"]
+    kind = int(g[f"{name}__kind"])
+    blob = g[f"{name}__blob"]
+    layer = s2lib.VaeResample(gpu_ctx, kind, blob)
+    emu = (oracle.PortDownsample if kind == 0 else oracle.PortUpsample)(port, blob, emulate_bf16=True)
+    i = 0
+    while f"{name}__x{i}" in g:
+        x, st = g[f"{name}__x{i}"], int(g[f"{name}__state{i}"])
+        got = layer.forward(torch.from_numpy(x).cuda(), st).cpu().numpy()
+        ref = g[f"{name}__y{i}"]
+        assert got.shape == ref.shape, (name, i)
+        assert cosine(got, ref) >= 0.9995 and rel_maxabs(got, ref) <= 2e-2, (name, i)
+        assert rel_maxabs(got, emu.forward(x, st)) <= (1e-3 if kind == 0 else 5e-3), (name, i)
+        i += 1
+    torch.cuda.synchronize()
+    assert gpu_ctx.status() == 0
+    layer.close()
+
+
+def test_resample_decoder_shapes(gpu_ctx, s2lib, port):
+    """A 2x spatial downsample of 128 channels on 3 frames of 64 x 96 and a 2x / 2x upsample of 64 channels
+    on 2 frames of 24 x 40, against the oracle in fp32 (the DiT gate)."""
+    import torch
+
+    from oracle import oracle
+    from tests.golden.gen_golden import conv_blob
+
+    rng = np.random.default_rng(99)
+    down = np.concatenate([np.asarray([128, 1, 1], np.float32), conv_blob(rng, 128, 128, 3, 3, 1, 2, 2, 0, True)])
+    up = np.concatenate([np.asarray([64, 2, 2, 1], np.float32), conv_blob(rng, 64, 64, 3, 3, 1, 2, 1, 1, True),
+                         conv_blob(rng, 512, 64, 3, 3, 1, 2, 1, 1, True)])
+    for kind, blob, shape in ((0, down, (128, 3, 64, 96)), (1, up, (64, 2, 24, 40))):
+        x = rng.standard_normal(shape).astype(np.float32)
+        layer = s2lib.VaeResample(gpu_ctx, kind, blob)
+        got = layer.forward(torch.from_numpy(x).cuda(), s2lib.S2_VAE_MEMORY_DISABLED).cpu().numpy()
+        ref = (oracle.PortDownsample if kind == 0 else oracle.PortUpsample)(port, blob).forward(x, 0)
+        assert got.shape == ref.shape
+        assert cosine(got, ref) >= 0.9995 and rel_maxabs(got, ref) <= 2e-2, kind
+        layer.close()

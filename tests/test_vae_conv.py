@@ -62,3 +62,19 @@ def test_port_conv3d_vs_reference_random(port):
             except ValueError:
                 break  # too few padded frames for this chunk: both sides reject it
             assert np.array_equal(_bits(got[i]), _bits(want)), (cfg, i)
+
+
+@pytest.mark.parametrize("name", [c[0] for c in __import__("tests.golden.gen_golden", fromlist=["x"]).RESAMPLE_CASES])
+def test_port_resample_matches_golden(port, golden, name):
+    """VAEDownsample3D / VAEUpsample3D restated (pad / shuffle in numpy around the C conv) against the
+    reference's own layers (golden)."""
+    from oracle import oracle
+
+    g = golden["vae_conv"]
+    kind = int(g[f"{name}__kind"])
+    layer = (oracle.PortDownsample if kind == 0 else oracle.PortUpsample)(port, g[f"{name}__blob"])
+    i = 0
+    while f"{name}__x{i}" in g:
+        y = layer.forward(g[f"{name}__x{i}"], int(g[f"{name}__state{i}"]))
+        assert np.array_equal(_bits(y), _bits(g[f"{name}__y{i}"])), (name, i)
+        i += 1
