@@ -508,6 +508,24 @@ def main():
                              "pack_ms": cc["other"]["ms"] / max(cc["other"]["launches"], 1)})
             layer.close()
             del xin, yout
+        # VAEChunkedMHA at the mid block: one 512-wide head over a 90 x 160 latent frame
+        E, T = 512, 90 * 160
+        mw = (0.02 * torch.randn(4 * (E * E + E), generator=gv)).numpy()
+        mha = abi.VaeMha(ctx, E, 1, 1.0 / E ** 0.5, mw)
+        xin = torch.randn(T, E, device="cuda")
+        yout = mha.forward(xin)
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            mha.forward(xin, out=yout)
+        e1.record(stream)
+        barrier()
+        mha_ms = e0.elapsed_time(e1) / args.steps
+        mha_flops = 2.0 * T * E * E * 4 + 4.0 * T * T * E
+        vae_conv.append({"shape": f"VAEChunkedMHA, {T} tokens x {E}, one head", "ms_per_call": mha_ms,
+                         "tflops_per_call": mha_flops / mha_ms / 1e9})
+        mha.close()
+        del xin, yout
     status = ctx.status()
 
     peaks = load_peaks()

@@ -403,6 +403,18 @@ int s2_vae_resample_forward(s2_vae_resample* layer, const float* in, int64_t in_
                             int memory_state, float* out, int64_t out_cstep);
 void s2_vae_resample_free(s2_vae_resample* layer);
 
+/* VAEChunkedMHA (vae_chunked_mha.h, load_param / load_model :109-135, CPU
+ * forward :197-217): self-attention of x [tokens][embed_dim]; weights host
+ * fp32 in load_model order (q w [E][E], q b [E], k w, k b, v w, v b, out w,
+ * out b); scale as param 6 (the reference's default 1/sqrt(E / heads)).
+ * This build: one head (the VAE's), embed_dim a multiple of 8.  x and out are
+ * device fp32 [tokens][embed_dim]. */
+typedef struct s2_vae_mha s2_vae_mha;
+int s2_vae_mha_create(s2_context* ctx, int embed_dim, int num_heads, float scale, const float* weights,
+                      s2_vae_mha** out);
+int s2_vae_mha_forward(s2_vae_mha* layer, const float* x, int tokens, float* out);
+void s2_vae_mha_free(s2_vae_mha* layer);
+
 /* ---------------------------------------------------------------------------
  * Multi-GPU (one process per GPU over NVLink).  The reference has no
  * distributed path (seedvr2_main.cpp:89-100 forces --sp-size 1); this is the

@@ -24,8 +24,17 @@
 //                         in[q][y*sh + ky*dh - pt][x*sw + kx*dw - pl]
 //          with zeros outside the input, fp32, summed in (q, ky, kx) order.
 //
+//   MultiHeadAttention (configured in vae_chunked_mha.cpp:144-162 with one
+//           input blob [tokens][qdim]: 0 embed_dim, 1 num_heads, 2
+//           weight_data_size, 3 kdim, 4 vdim, 5 attn_mask = 0, 6 scale;
+//           weights q, k, v [embed_dim][in] + bias, out [qdim][embed_dim] +
+//           bias)
+//          q/k/v = x W^T + b; per head softmax(scale q k^T) v (fp32,
+//          max-subtracted, normalised after the sum); out = o Wout^T + b.
+//
 // All loops parallelise with OpenMP over independent outputs, so results do
 // not depend on the thread count.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -310,6 +319,114 @@ private:
     Mat weight_data, bias_data;
 };
 
+// y[t][o] = b[o] + sum_i x[t][i] w[o][i], fp32 in i order
+void shim_linear(const float* x, int tokens, int in, const float* w, const float* b, int out, float* y)
+{
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < tokens; t++)
+        for (int o = 0; o < out; o++)
+        {
+            float sum = b[o];
+            const float* xr = x + (size_t)t * in;
+            const float* wr = w + (size_t)o * in;
+            for (int i = 0; i < in; i++) sum += xr[i] * wr[i];
+            y[(size_t)t * out + o] = sum;
+        }
+}
+
+class ShimMultiHeadAttention : public Layer
+{
+public:
+    ShimMultiHeadAttention() : embed_dim(0), num_heads(1), weight_data_size(0), kdim(0), vdim(0), attn_mask(0), scale(1.f)
+    {
+        one_blob_only = false;
+        support_inplace = false;
+    }
+
+    virtual int load_param(const ParamDict& pd)
+    {
+        embed_dim = pd.get(0, 0);
+        num_heads = pd.get(1, 1);
+        weight_data_size = pd.get(2, 0);
+        kdim = pd.get(3, embed_dim);
+        vdim = pd.get(4, embed_dim);
+        attn_mask = pd.get(5, 0);
+        scale = pd.get(6, 1.f);
+        if (embed_dim <= 0 || num_heads <= 0 || embed_dim % num_heads || attn_mask != 0) return -1;
+        return 0;
+    }
+
+    virtual int load_model(const ModelBin& mb)
+    {
+        const int qdim = weight_data_size / embed_dim;
+        for (int i = 0; i < 8; i++)
+        {
+            const int n = i == 0 ? embed_dim * qdim : i == 2 ? embed_dim * kdim : i == 4 ? embed_dim * vdim
+                          : i == 6 ? qdim * embed_dim : (i == 7 ? qdim : embed_dim);
+            w[i] = mb.load(n, i % 2 ? 1 : 0);
+            if (w[i].empty()) return -100;
+        }
+        return 0;
+    }
+
+    virtual int forward(const std::vector<Mat>& bottom, std::vector<Mat>& top, const Option& opt) const
+    {
+        // one input blob: self-attention (q, k and v read it)
+        if (bottom.size() != 1 || top.size() != 1) return -1;
+        const Mat& x = bottom[0];
+        const int qdim = weight_data_size / embed_dim;
+        const int T = x.h;
+        if (x.w != qdim || kdim != qdim || vdim != qdim) return -1;
+        const int E = embed_dim, hd = E / num_heads;
+        std::vector<float> q((size_t)T * E), k((size_t)T * E), v((size_t)T * E), o((size_t)T * E);
+        shim_linear((const float*)x.data, T, qdim, w[0], w[1], E, q.data());
+        shim_linear((const float*)x.data, T, kdim, w[2], w[3], E, k.data());
+        shim_linear((const float*)x.data, T, vdim, w[4], w[5], E, v.data());
+#pragma omp parallel for schedule(static)
+        for (int t = 0; t < T; t++)
+        {
+            std::vector<float> s((size_t)T);
+            for (int h = 0; h < num_heads; h++)
+            {
+                const float* qr = q.data() + (size_t)t * E + h * hd;
+                float m = -INFINITY;
+                for (int j = 0; j < T; j++)
+                {
+                    const float* kr = k.data() + (size_t)j * E + h * hd;
+                    float d = 0.f;
+                    for (int i = 0; i < hd; i++) d += qr[i] * kr[i];
+                    s[j] = d * scale;
+                    m = std::max(m, s[j]);
+                }
+                float sum = 0.f;
+                for (int j = 0; j < T; j++)
+                {
+                    s[j] = std::exp(s[j] - m);
+                    sum += s[j];
+                }
+                float* orow = o.data() + (size_t)t * E + h * hd;
+                for (int i = 0; i < hd; i++) orow[i] = 0.f;
+                for (int j = 0; j < T; j++)
+                {
+                    const float p = s[j] / sum;
+                    const float* vr = v.data() + (size_t)j * E + h * hd;
+                    for (int i = 0; i < hd; i++) orow[i] += p * vr[i];
+                }
+            }
+        }
+        Mat& y = top[0];
+        y.create(qdim, T, 4u, opt.blob_allocator);
+        if (y.empty()) return -100;
+        shim_linear(o.data(), T, E, w[6], w[7], qdim, (float*)y.data);
+        return 0;
+    }
+
+private:
+    int embed_dim, num_heads, weight_data_size, kdim, vdim, attn_mask;
+    float scale;
+    Mat w[8];
+};
+
 } // namespace
 
 Layer* create_layer(const char* type)
@@ -318,6 +435,7 @@ Layer* create_layer(const char* type)
     if (t == "SDPA") return new ShimSDPA;
     if (t == "Gemm") return new ShimGemm;
     if (t == "Convolution") return new ShimConvolution;
+    if (t == "MultiHeadAttention") return new ShimMultiHeadAttention;
     return 0;
 }
 

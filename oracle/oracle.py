@@ -102,7 +102,17 @@ class Port:
         lib.s2o_conv3d_dims.argtypes = [_i32p, C.c_int, C.c_int, C.c_int, C.c_int, _i32p]
         lib.s2o_conv3d_forward.argtypes = [_i32p, C.c_void_p, _f32p, _f32p, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                            C.c_int, _f32p, C.c_void_p]
+        lib.s2o_mha_forward.argtypes = [C.c_int, C.c_int, C.c_float, _f32p, _f32p, C.c_int, _f32p]
         self.lib = lib
+
+    def mha_forward(self, E, heads, scale, weights, x):
+        """VAEChunkedMHA's CPU path: x [T][E] -> [T][E] (weights in load_model order, flat)."""
+        x = _f32(x)
+        out = np.zeros_like(x)
+        r = self.lib.s2o_mha_forward(E, heads, scale, _f32(weights), x, x.shape[0], out)
+        if r != 0:
+            raise ValueError(r)
+        return out
 
     def plan(self, shapes, window, shifted, mode=WINDOW_TARGET) -> Plan:
         shapes = _i32(shapes).reshape(-1, 3)
@@ -415,6 +425,19 @@ class PortUpsample:
         if self.remove_head and state != VAE_MEMORY_ACTIVE:
             sh = np.concatenate([sh[:, :1], sh[:, 2:]], axis=1)
         return self.post.forward(np.ascontiguousarray(sh), state)
+
+
+def ref_mha_forward(E, heads, scale, weights, x, chunk=128, path: str = REF_VAE_SO):
+    """The reference's own VAEChunkedMHA (oracle/_ref/libs2_ref_vae.so) on its CPU path."""
+    lib = C.CDLL(path)
+    lib.s2ref_mha_forward.argtypes = [_i32p, C.c_float, _f32p, C.c_size_t, _f32p, C.c_int, _f32p]
+    x = _f32(x)
+    w = _f32(weights)
+    out = np.zeros_like(x)
+    r = lib.s2ref_mha_forward(_i32([E, heads, E * E, E, E, chunk]), scale, w, w.size, x, x.shape[0], out)
+    if r != 0:
+        raise ValueError(r)
+    return out
 
 
 class RefResample:

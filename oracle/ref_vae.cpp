@@ -1,6 +1,7 @@
 // extern "C" wrapper around the reference's OWN VAE layers DecomposedConv3D,
-// VAEDownsample3D and VAEUpsample3D (src/seedvr2/decomposed_conv3d.cpp,
-// vae_downsample3d.cpp, vae_upsample3d.cpp, compiled unmodified with
+// VAEDownsample3D, VAEUpsample3D and VAEChunkedMHA
+// (src/seedvr2/decomposed_conv3d.cpp, vae_downsample3d.cpp,
+// vae_upsample3d.cpp, vae_chunked_mha.cpp, compiled unmodified with
 // NCNN_VULKAN=0 against the clean-room ncnn shim, whose "Convolution"
 // restates ncnn's spatial convolution).  Built by oracle/Makefile into
 // oracle/_ref/libs2_ref_vae.so.
@@ -12,6 +13,7 @@
 
 #include "decomposed_conv3d.h"
 #include "modelbin.h"
+#include "vae_chunked_mha.h"
 #include "vae_downsample3d.h"
 #include "vae_upsample3d.h"
 
@@ -118,6 +120,37 @@ int s2ref_resample_forward(void* handle, int memory_state, const float* in, int 
 void s2ref_resample_free(void* handle)
 {
     delete static_cast<ncnn::Layer*>(handle);
+}
+
+// VAEChunkedMHA: params (embed_dim, num_heads, weight_data_size, kdim, vdim,
+// scale, chunk_size), weights in load_model order (q w, q b, k w, k b, v w,
+// v b, out w, out b).  x [tokens][qdim] -> out [tokens][qdim].
+int s2ref_mha_forward(const int* ip, float scale, const float* weights, size_t count, const float* x, int tokens,
+                      float* out)
+{
+    seedvr2::VAEChunkedMHA layer;
+    ncnn::ParamDict pd;
+    pd.set(0, ip[0]);
+    pd.set(1, ip[1]);
+    pd.set(2, ip[2]);
+    pd.set(3, ip[3]);
+    pd.set(4, ip[4]);
+    pd.set(6, scale);
+    pd.set(20, ip[5]);
+    int r = layer.load_param(pd);
+    ncnn::ModelBinFromFloats mb(weights, count);
+    ncnn::Option opt;
+    if (r == 0) r = layer.load_model(mb);
+    if (r == 0) r = layer.create_pipeline(opt);
+    if (r != 0) return r;
+    const int qdim = ip[2] / ip[0];
+    ncnn::Mat bottom(qdim, tokens);
+    std::memcpy(bottom.data, x, sizeof(float) * (size_t)qdim * tokens);
+    ncnn::Mat top;
+    r = layer.forward(bottom, top, opt);
+    if (r != 0) return r;
+    std::memcpy(out, top.data, sizeof(float) * (size_t)qdim * tokens);
+    return 0;
 }
 
 } // extern "C"

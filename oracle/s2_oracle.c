@@ -816,3 +816,80 @@ int s2o_conv3d_forward(const int* cfg, const float* bias, const float* weights, 
     }
     return 0;
 }
+
+/* ---------------------------------------------------------------------------
+ * VAEChunkedMHA on its CPU path (src/seedvr2/vae_chunked_mha.cpp:197-217):
+ * ncnn MultiHeadAttention over one input blob x [tokens][E] (q, k and v all
+ * read it): q/k/v = x W^T + b, per head softmax(scale q k^T) v with the max
+ * subtracted and the probabilities normalised as p_j / sum, out = o Wout^T +
+ * b.  w: q w [E][E], q b, k w, k b, v w, v b, out w [E][E], out b. */
+static void mha_linear(const float* x, int T, int in, const float* w, const float* b, int out, float* y)
+{
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < T; t++)
+        for (int o = 0; o < out; o++)
+        {
+            float sum = b[o];
+            const float* xr = x + (long)t * in;
+            const float* wr = w + (long)o * in;
+            for (int i = 0; i < in; i++) sum += xr[i] * wr[i];
+            y[(long)t * out + o] = sum;
+        }
+}
+
+int s2o_mha_forward(int E, int heads, float scale, const float* w, const float* x, int T, float* out)
+{
+    if (E <= 0 || heads <= 0 || E % heads || T <= 0) return -1;
+    const long EE = (long)E * E;
+    const float *wq = w, *bq = wq + EE, *wk = bq + E, *bk = wk + EE, *wv = bk + E, *bv = wv + EE, *wo = bv + E,
+                *bo = wo + EE;
+    const int hd = E / heads;
+    float* q = (float*)malloc(sizeof(float) * (size_t)T * E * 4);
+    if (!q) return -100;
+    float *k = q + (long)T * E, *v = k + (long)T * E, *o = v + (long)T * E;
+    mha_linear(x, T, E, wq, bq, E, q);
+    mha_linear(x, T, E, wk, bk, E, k);
+    mha_linear(x, T, E, wv, bv, E, v);
+    int failed = 0;
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < T; t++)
+    {
+        float* s = (float*)malloc(sizeof(float) * (size_t)T);
+        if (!s)
+        {
+            failed = 1;
+            continue;
+        }
+        for (int h = 0; h < heads; h++)
+        {
+            const float* qr = q + (long)t * E + h * hd;
+            float m = -INFINITY;
+            for (int j = 0; j < T; j++)
+            {
+                const float* kr = k + (long)j * E + h * hd;
+                float d = 0.f;
+                for (int i = 0; i < hd; i++) d += qr[i] * kr[i];
+                s[j] = d * scale;
+                m = m > s[j] ? m : s[j];
+            }
+            float sum = 0.f;
+            for (int j = 0; j < T; j++)
+            {
+                s[j] = expf(s[j] - m);
+                sum += s[j];
+            }
+            float* orow = o + (long)t * E + h * hd;
+            for (int i = 0; i < hd; i++) orow[i] = 0.f;
+            for (int j = 0; j < T; j++)
+            {
+                const float p = s[j] / sum;
+                const float* vr = v + (long)j * E + h * hd;
+                for (int i = 0; i < hd; i++) orow[i] += p * vr[i];
+            }
+        }
+        free(s);
+    }
+    if (!failed) mha_linear(o, T, E, wo, bo, E, out);
+    free(q);
+    return failed ? -100 : 0;
+}

@@ -96,6 +96,11 @@ int s2o_conv3d_dims(const int* cfg, int w, int h, int d, int prefix, int* out_di
 int s2o_conv3d_forward(const int* cfg, const float* bias, const float* weights, const float* in, int w, int h, int d,
                        const float* mem, int mem_frames, float* out, float* next_mem);
 
+/* VAEChunkedMHA's CPU path (vae_chunked_mha.cpp:197-217): ncnn
+ * MultiHeadAttention, self-attention over x [T][E]; w = q w, q b, k w, k b,
+ * v w, v b, out w, out b (weights [E][E], out = in features last). */
+int s2o_mha_forward(int E, int heads, float scale, const float* w, const float* x, int T, float* out);
+
 #ifdef __cplusplus
 }
 #endif

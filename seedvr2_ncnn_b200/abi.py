@@ -56,6 +56,7 @@ EXPORTED = [
     "s2_dit_denoise", "s2_dit_denoise_host", "s2_apply_cfg",
     "s2_conv3d_create", "s2_conv3d_output_shape", "s2_conv3d_forward", "s2_conv3d_free",
     "s2_vae_resample_create", "s2_vae_resample_output_shape", "s2_vae_resample_forward", "s2_vae_resample_free",
+    "s2_vae_mha_create", "s2_vae_mha_forward", "s2_vae_mha_free",
 ]
 
 S2_VAE_DOWNSAMPLE = 0
@@ -186,6 +187,9 @@ def lib() -> C.CDLL:
     L.s2_vae_resample_output_shape.argtypes = [vp, ip, ip, ip, ip, pint]
     L.s2_vae_resample_forward.argtypes = [vp, vp, i64, ip, ip, ip, ip, ip, vp, i64]
     L.s2_vae_resample_free.argtypes = [vp]
+    L.s2_vae_mha_create.argtypes = [vp, ip, ip, C.c_float, vp, C.POINTER(vp)]
+    L.s2_vae_mha_forward.argtypes = [vp, vp, ip, vp]
+    L.s2_vae_mha_free.argtypes = [vp]
     _lib = L
     return L
 
@@ -661,6 +665,40 @@ class VaeResample:
     def close(self):
         if self.handle:
             lib().s2_vae_resample_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class VaeMha:
+    """s2_vae_mha: VAEChunkedMHA (one head); weights host fp32 in load_model order."""
+
+    def __init__(self, ctx: Context, embed_dim, num_heads, scale, weights):
+        import numpy as np
+
+        self.ctx = ctx
+        w = np.ascontiguousarray(weights, dtype=np.float32)
+        h = C.c_void_p()
+        check(lib().s2_vae_mha_create(ctx.handle, int(embed_dim), int(num_heads), float(scale), ptr(w), C.byref(h)),
+              "s2_vae_mha_create")
+        self.handle = h
+
+    def forward(self, x, out=None):
+        """x: fp32 CUDA [tokens, E] -> fp32 CUDA [tokens, E]."""
+        import torch
+
+        if out is None:
+            out = torch.empty_like(x)
+        check(lib().s2_vae_mha_forward(self.handle, x.data_ptr(), x.shape[0], out.data_ptr()), "s2_vae_mha_forward")
+        return out
+
+    def close(self):
+        if self.handle:
+            lib().s2_vae_mha_free(self.handle)
             self.handle = None
 
     def __del__(self):

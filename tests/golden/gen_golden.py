@@ -214,6 +214,16 @@ def resample_blob(rng, kind, head):
                            conv_blob(rng, 32, 4, 3, 3, 1, head, 1, 1, True)])
 
 
+# VAEChunkedMHA cases: (name, embed_dim, tokens), one head
+MHA_CASES = [("mha16", 16, 20), ("mha64", 64, 100)]
+
+
+def mha_weights(rng, E):
+    """q w, q b, k w, k b, v w, v b, out w, out b (load_model order), flat fp32."""
+    sizes = [E * E, E] * 4
+    return np.concatenate([(0.1 * rng.standard_normal(n)).astype(np.float32) for n in sizes])
+
+
 # (name, kind, head frames, input (c, d, h, w), memory states per chunk)
 RESAMPLE_CASES = [
     ("down", 0, 2, (8, 3, 9, 12), [1, 2, 2]),
@@ -257,6 +267,13 @@ def gen_vae_conv() -> None:
             out[f"{name}__x{i}"] = x
             out[f"{name}__state{i}"] = np.asarray(st, np.int32)
             out[f"{name}__y{i}"] = layer.forward(x, st)
+    # VAEChunkedMHA on its CPU path
+    for name, E, T in MHA_CASES:
+        w = mha_weights(rng, E)
+        x = rng.standard_normal((T, E)).astype(np.float32)
+        out[f"{name}__w"] = w
+        out[f"{name}__x"] = x
+        out[f"{name}__y"] = oracle.ref_mha_forward(E, 1, float(1.0 / np.sqrt(E)), w, x)
     np.savez_compressed(os.path.join(OUT, "vae_conv.npz"), **out)
 
 

@@ -168,3 +168,31 @@ def test_resample_decoder_shapes(gpu_ctx, s2lib, port):
         assert got.shape == ref.shape
         assert cosine(got, ref) >= 0.9995 and rel_maxabs(got, ref) <= 2e-2, kind
         layer.close()
+
+
+# ---- VAEChunkedMHA ----
+@pytest.mark.parametrize("E,T", [(16, 20), (64, 100), (512, 1440), (64, 9000)])
+def test_vae_mha_vs_oracle(gpu_ctx, s2lib, port, golden, E, T):
+    """Against the oracle's restatement of the reference's CPU path (fp32): the DiT gate.  (16, 20) and
+    (64, 100) are the golden cases; 512 x 1440 is a VAE mid-block width; 9000 tokens run in two query
+    chunks."""
+    import torch
+
+    from tests.golden.gen_golden import mha_weights
+
+    g = golden["vae_conv"]
+    name = f"mha{E}"
+    if (E, T) in ((16, 20), (64, 100)):
+        w, x = g[f"{name}__w"], g[f"{name}__x"]
+        ref = g[f"{name}__y"]
+    else:
+        rng = np.random.default_rng(E + T)
+        w = mha_weights(rng, E) * (0.5 if E == 512 else 1.0)
+        x = rng.standard_normal((T, E)).astype(np.float32)
+        ref = port.mha_forward(E, 1, float(1.0 / np.sqrt(E)), w, x)
+    layer = s2lib.VaeMha(gpu_ctx, E, 1, float(1.0 / np.sqrt(E)), w)
+    got = layer.forward(torch.from_numpy(np.ascontiguousarray(x)).cuda()).cpu().numpy()
+    torch.cuda.synchronize()
+    assert gpu_ctx.status() == 0
+    assert cosine(got, ref) >= 0.9995 and rel_maxabs(got, ref) <= 2e-2, (E, T)
+    layer.close()

@@ -78,3 +78,22 @@ def test_port_resample_matches_golden(port, golden, name):
         y = layer.forward(g[f"{name}__x{i}"], int(g[f"{name}__state{i}"]))
         assert np.array_equal(_bits(y), _bits(g[f"{name}__y{i}"])), (name, i)
         i += 1
+
+
+def test_port_mha_matches_golden_and_reference(port, golden):
+    """VAEChunkedMHA's CPU path (ncnn MultiHeadAttention, restated) -- port vs the reference's layer."""
+    from oracle import oracle
+    from tests.golden.gen_golden import MHA_CASES
+
+    g = golden["vae_conv"]
+    for name, E, T in MHA_CASES:
+        y = port.mha_forward(E, 1, float(1.0 / np.sqrt(E)), g[f"{name}__w"], g[f"{name}__x"])
+        assert np.array_equal(_bits(y), _bits(g[f"{name}__y"])), name
+    if __import__("os").path.exists(oracle.REF_VAE_SO):
+        rng = np.random.default_rng(8)
+        for E, H, T in ((32, 2, 41), (24, 1, 9)):
+            w = np.concatenate([(0.1 * rng.standard_normal(n)).astype(np.float32) for n in [E * E, E] * 4])
+            x = rng.standard_normal((T, E)).astype(np.float32)
+            sc = float(1.0 / np.sqrt(E // H))
+            assert np.array_equal(_bits(port.mha_forward(E, H, sc, w, x)),
+                                  _bits(oracle.ref_mha_forward(E, H, sc, w, x)))
