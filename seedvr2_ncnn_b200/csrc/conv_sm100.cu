@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(256) conv_pack_kernel(const float* __restrict_
 // X / sr), where s = t, or t + 1 past frame 0 when frame 1 is dropped
 // (remove_head).  One output element per thread, writes coalesced.
 __global__ void upsample_shuffle_kernel(const float* __restrict__ packed, int64_t pcstep, int ch, int tr, int sr,
-                                        int pd, int ph, int pw, int out_t, int remove_head, float* __restrict__ out,
+                                        int ph, int pw, int out_t, int remove_head, float* __restrict__ out,
                                         int64_t ocstep)
 {
     const int OW = pw * sr, OH = ph * sr;
@@ -327,7 +327,6 @@ __global__ void upsample_shuffle_kernel(const float* __restrict__ packed, int64_
         const int pc = (((Y % sr) * sr + X % sr) * tr + z) * ch + c;
         out[(int64_t)c * ocstep + r + (int64_t)t * OH * OW] =
             __ldg(packed + (int64_t)pc * pcstep + ((int64_t)frame * ph + Y / sr) * pw + X / sr);
-        (void)pd;
     }
 }
 
@@ -736,7 +735,7 @@ int s2_vae_resample_forward(s2_vae_resample* l, const float* in, int64_t in_cste
         if (blocks > (int64_t)ctx.num_sms * 16) blocks = (int64_t)ctx.num_sms * 16;
         s2::ProfileScope prof(ctx, s2::K_OTHER, 0.0, (double)total * 8.0);
         s2::upsample_shuffle_kernel<<<(int)blocks, 256, 0, ctx.stream>>>(packed, pplane, l->channels, l->tr, l->sr,
-                                                                        p[2], p[1], p[0], ot,
+                                                                        p[1], p[0], ot,
                                                                         l->remove_head && memory_state !=
                                                                                               S2_VAE_MEMORY_ACTIVE,
                                                                         sh, splane);
