@@ -786,14 +786,11 @@ int launch_window_attention(Context& ctx, const AttnSchedule& s, int heads, cons
     a.text_partial = text_partial;
     a.status = ctx.status;
     for (int i = 0; i < kMaxPeers; i++) a.peer_out[i] = i < num_peers ? peer_out[i] : nullptr;
-    static bool configured = false;
-    if (!configured)
-    {
-        if (cudaFuncSetAttribute(window_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+    static std::atomic<uint64_t> configured{0};
+    if (first_on_device(configured) &&
+        cudaFuncSetAttribute(window_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
             cudaSuccess)
-            return S2_ERR_CUDA;
-        configured = true;
-    }
+        return S2_ERR_CUDA;
     a.heads = heads;
     a.num_work = s.num_items * heads;
     const int grid = a.num_work < ctx.num_sms ? a.num_work : ctx.num_sms;

@@ -389,13 +389,10 @@ int conv3d_gemm(Context& ctx, const Conv3dGeometry& g, const void* X, int frames
     a.out_cstep = out_cstep;
     a.status = ctx.status;
     if (a.num_tiles <= 0) return S2_OK;
-    static bool configured = false;
-    if (!configured)
-    {
-        if (cudaFuncSetAttribute(conv3d_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C_SMEM) != cudaSuccess)
-            return S2_ERR_CUDA;
-        configured = true;
-    }
+    static std::atomic<uint64_t> configured{0};
+    if (first_on_device(configured) &&
+        cudaFuncSetAttribute(conv3d_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C_SMEM) != cudaSuccess)
+        return S2_ERR_CUDA;
     const int grid = a.num_tiles < ctx.num_sms ? a.num_tiles : ctx.num_sms;
     const double flops = 2.0 * g.Tout * g.Ho * g.Wo * (double)g.Co * taps * g.Ci;
     ProfileScope prof(ctx, K_GEMM, flops,

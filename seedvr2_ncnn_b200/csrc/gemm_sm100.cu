@@ -1190,7 +1190,8 @@ cudaError_t launch_pair_variant(cudaStream_t stream, const CUtensorMap& ta0, con
                                 const CUtensorMap& tw, const CUtensorMap& to0, const CUtensorMap& to1,
                                 const GemmArgs& a)
 {
-    static int max_clusters = 0; // per instantiation
+    static std::atomic<uint64_t> configured{0}; // per instantiation and device
+    static std::atomic<int> max_clusters{0};     // the same on every B200
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1202,19 +1203,24 @@ cudaError_t launch_pair_variant(cudaStream_t stream, const CUtensorMap& ta0, con
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (max_clusters == 0)
+    if (first_on_device(configured))
     {
-        cudaError_t e = cudaFuncSetAttribute(shared_linear_pair_kernel<SKB, EK>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, PairTile<SKB, EK>::SMEM_BYTES);
+        const cudaError_t e = cudaFuncSetAttribute(shared_linear_pair_kernel<SKB, EK>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   PairTile<SKB, EK>::SMEM_BYTES);
         if (e != cudaSuccess) return e;
+    }
+    if (max_clusters.load() == 0)
+    {
         cfg.gridDim = dim3(2);
         int n = 0;
-        e = cudaOccupancyMaxActiveClusters(&n, shared_linear_pair_kernel<SKB, EK>, &cfg);
+        const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, shared_linear_pair_kernel<SKB, EK>, &cfg);
         if (e != cudaSuccess) return e;
         if (n <= 0) return cudaErrorInvalidConfiguration;
-        max_clusters = n;
+        max_clusters.store(n);
     }
-    const int pairs = a.num_tiles < max_clusters ? a.num_tiles : max_clusters;
+    const int mc = max_clusters.load();
+    const int pairs = a.num_tiles < mc ? a.num_tiles : mc;
     cfg.gridDim = dim3(2 * pairs);
     cfg.blockDim = dim3(num_threads(EK));
     cfg.dynamicSmemBytes = PairTile<SKB, EK>::SMEM_BYTES;
@@ -1225,14 +1231,13 @@ template <int BN, int SKB, int EK>
 cudaError_t launch_variant(int grid, cudaStream_t stream, const CUtensorMap& ta0, const CUtensorMap& ta1,
                            const CUtensorMap& tw, const CUtensorMap& to0, const CUtensorMap& to1, const GemmArgs& a)
 {
-    static bool configured = false; // per instantiation
-    if (!configured)
+    static std::atomic<uint64_t> configured{0}; // per instantiation and device
+    if (first_on_device(configured))
     {
         const cudaError_t e =
             cudaFuncSetAttribute(shared_linear_kernel<BN, SKB, EK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  Tile<BN, SKB, EK>::SMEM_BYTES);
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     shared_linear_kernel<BN, SKB, EK>
         <<<grid, num_threads(EK), Tile<BN, SKB, EK>::SMEM_BYTES, stream>>>(ta0, ta1, tw, to0, to1, a);

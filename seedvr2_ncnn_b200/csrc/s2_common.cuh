@@ -7,7 +7,21 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace s2 {
+
+// Host: true the first time it is called for the current device (one bit
+// per device), so per-function attributes such as the dynamic shared-memory
+// limit are set once on every device a process launches on; safe to call
+// from several host threads (setting an attribute twice is harmless).
+inline bool first_on_device(std::atomic<uint64_t>& seen)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return true;
+    const uint64_t bit = 1ull << dev;
+    return (seen.fetch_or(bit) & bit) == 0;
+}
 
 // Device status word codes (first error wins).
 enum : int
