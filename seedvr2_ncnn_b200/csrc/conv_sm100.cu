@@ -9,7 +9,8 @@
 // X is the layer input with its head frames materialised (the cached frames
 // of the previous chunk, or copies of frame 0), stored channels-last in bf16
 // ([frames][H][W][Cp], Cp = channels rounded up to 8) by conv_pack_kernel.
-// A tile is 128 output pixels of one output row times 128 output channels;
+// A tile is 128 output pixels (a 128 x 1, 64 x 2 or 32 x 4 block of one
+// output frame, whichever pads the frame least) times 128 output channels;
 // its K loop walks the taps (kt, ky, kx) and 64-channel blocks.  Warp 0 TMA-
 // loads the A box straight out of X with a 4-D tensor map at the tap's
 // shifted coordinates (zero padding comes from the out-of-range fill; a
@@ -26,7 +27,7 @@ namespace s2 {
 
 namespace {
 
-constexpr int CBM = 128;                          // output pixels per tile (one output row segment)
+constexpr int CBM = 128;                          // output pixels per tile: bx x by, bx * by = 128
 constexpr int CBN = 128;                          // output channels per tile
 constexpr int CBK = 64;                           // input channels per K block (one 128-byte swizzle row)
 constexpr int C_A_BYTES = CBM * CBK * 2;
@@ -41,7 +42,8 @@ constexpr int kPackTiles = 4; // 32-pixel tiles per conv_pack_kernel block
 struct ConvArgs
 {
     int Tout, Ho, Wo, Co;
-    int xblocks, nblocks, num_tiles;
+    int bx, by;                    // tile extent in output pixels (x, y), bx * by = CBM
+    int xblocks, yblocks, nblocks, num_tiles;
     int kh, kw, st, dt, sh, sw, dh, dw, ph, pw;
     int cblocks, num_kb, cpad64;
     const float* bias;
@@ -50,17 +52,18 @@ struct ConvArgs
     int* status;
 };
 
-// tile -> (output frame, output row, first pixel, first channel); channel
-// blocks run fastest so the tiles of one row segment reuse its input in L2
-__device__ __forceinline__ void conv_decode(const ConvArgs& a, int t, int& to, int& y, int& x0, int& n0)
+// tile -> (output frame, first row, first pixel, first channel); channel
+// blocks run fastest so the tiles of one pixel block reuse its input in L2
+__device__ __forceinline__ void conv_decode(const ConvArgs& a, int t, int& to, int& y0, int& x0, int& n0)
 {
     const int nb = t % a.nblocks;
     int r = t / a.nblocks;
     const int xb = r % a.xblocks;
     r /= a.xblocks;
-    y = r % a.Ho;
-    to = r / a.Ho;
-    x0 = xb * CBM;
+    const int yb = r % a.yblocks;
+    to = r / a.yblocks;
+    x0 = xb * a.bx;
+    y0 = yb * a.by;
     n0 = nb * CBN;
 }
 
@@ -124,8 +127,8 @@ __global__ void __launch_bounds__(C_THREADS, 1)
             for (int s = 0; s < C_STAGES; s++) issued[s] = 0, last_phase[s] = 0;
             for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x)
             {
-                int to, y, x0, n0;
-                conv_decode(args, t, to, y, x0, n0);
+                int to, y0, x0, n0;
+                conv_decode(args, t, to, y0, x0, n0);
                 int tap = 0, cb = 0;
                 for (int kb = 0; kb < args.num_kb; kb++)
                 {
@@ -135,7 +138,7 @@ __global__ void __launch_bounds__(C_THREADS, 1)
                     uint8_t* sa = smem + stage * C_STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[stage], C_STAGE_BYTES);
                     tma_load_4d(sa, &tmap_x, &full[stage], cb * CBK, x0 * args.sw + k_x * args.dw - args.pw,
-                                y * args.sh + k_y * args.dh - args.ph, to * args.st + k_t * args.dt);
+                                y0 * args.sh + k_y * args.dh - args.ph, to * args.st + k_t * args.dt);
                     tma_load_2d(sa + C_A_BYTES, &tmap_w, &full[stage], tap * args.cpad64 + cb * CBK, n0);
                     issued[stage] = 1;
                     last_phase[stage] = phase;
@@ -224,10 +227,12 @@ __global__ void __launch_bounds__(C_THREADS, 1)
             if (!ok) break;
             __syncwarp();
             tc_fence_after();
-            int to, y, x0, n0;
-            conv_decode(args, t, to, y, x0, n0);
-            const int x = x0 + row;
-            const bool live = x < args.Wo;
+            int to, y0, x0, n0;
+            conv_decode(args, t, to, y0, x0, n0);
+            // accumulator row = the box's (y, x) order; a warp's 32 rows are 32
+            // consecutive pixels of one output row (bx >= 32)
+            const int y = y0 + row / args.bx, x = x0 + row % args.bx;
+            const bool live = x < args.Wo && y < args.Ho;
             float* dst = args.out + ((int64_t)to * args.Ho + y) * args.Wo + x;
             const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * CBN;
 #pragma unroll 1
@@ -348,14 +353,34 @@ int conv3d_pack(Context& ctx, const float* in, int64_t in_cstep, int C, int Cp, 
 int conv3d_gemm(Context& ctx, const Conv3dGeometry& g, const void* X, int frames_x, const void* Wt, const float* bias,
                 float* out, int64_t out_cstep)
 {
-    // A: X [frames][H][W][Cp] bf16, boxes of 64 channels x 128 pixels of one row
+    // Output tile of bx x by = 128 pixels, the shape among 128 x 1, 64 x 2 and
+    // 32 x 4 that leaves the fewest padding pixels on this frame (a 160-pixel
+    // row takes five 32-wide tiles instead of two 128-wide ones).
+    int bx = CBM, by = 1;
+    {
+        double best = 0.0;
+        for (int cx = CBM; cx >= 32; cx /= 2)
+        {
+            const int cy = CBM / cx;
+            const double used = (double)g.Wo * g.Ho /
+                                ((double)((g.Wo + cx - 1) / cx) * cx * (double)((g.Ho + cy - 1) / cy) * cy);
+            if (used > best + 1e-9)
+            {
+                best = used;
+                bx = cx;
+                by = cy;
+            }
+        }
+    }
+    // A: X [frames][H][W][Cp] bf16, boxes of 64 channels x bx pixels x by rows;
+    // spatial strides are the box's traversal strides (sw * bx pixels wide,
+    // sh * by rows high, every sw-th / sh-th one read)
     CUtensorMap tx, tw;
     const uint64_t xd[4] = {(uint64_t)g.Cp, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)frames_x};
     const uint64_t xs[3] = {(uint64_t)g.Cp * 2, (uint64_t)g.W * g.Cp * 2, (uint64_t)g.H * g.W * g.Cp * 2};
-    // a spatial stride sw reads every sw-th pixel of a box sw * 128 pixels wide
-    const uint32_t xb[4] = {CBK, (uint32_t)(CBM * g.sw), 1, 1};
-    const uint32_t xe[4] = {1, (uint32_t)g.sw, 1, 1};
-    if (g.sw < 1 || CBM * g.sw > 256) return S2_ERR_INVALID;
+    if (g.sw < 1 || g.sh < 1 || bx * g.sw > 256 || by * g.sh > 256 || g.sw > 8 || g.sh > 8) return S2_ERR_INVALID;
+    const uint32_t xb[4] = {CBK, (uint32_t)(bx * g.sw), (uint32_t)(by * g.sh), 1};
+    const uint32_t xe[4] = {1, (uint32_t)g.sw, (uint32_t)g.sh, 1};
     int r = make_tmap_bf16_4d(&tx, X, xd, xs, xb, xe);
     // B: weights [Co][taps * cpad64] bf16, boxes of 64 x 128
     const int taps = g.kt * g.kh * g.kw;
@@ -368,9 +393,12 @@ int conv3d_gemm(Context& ctx, const Conv3dGeometry& g, const void* X, int frames
     a.Ho = g.Ho;
     a.Wo = g.Wo;
     a.Co = g.Co;
-    a.xblocks = (g.Wo + CBM - 1) / CBM;
+    a.bx = bx;
+    a.by = by;
+    a.xblocks = (g.Wo + bx - 1) / bx;
+    a.yblocks = (g.Ho + by - 1) / by;
     a.nblocks = (g.Co + CBN - 1) / CBN;
-    a.num_tiles = g.Tout * g.Ho * a.xblocks * a.nblocks;
+    a.num_tiles = g.Tout * a.yblocks * a.xblocks * a.nblocks;
     a.kh = g.kh;
     a.kw = g.kw;
     a.st = g.st;
