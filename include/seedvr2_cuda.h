@@ -380,6 +380,9 @@ int s2_conv3d_output_shape(const s2_conv3d* layer, int w, int h, int d, int memo
  * another size (as the reference). */
 int s2_conv3d_forward(s2_conv3d* layer, const float* in, int64_t in_cstep, int w, int h, int d, int c,
                       int memory_state, float* out, int64_t out_cstep);
+/* Drops the cached frames (DecomposedConv3D::reset_temporal_memory,
+ * decomposed_conv3d.cpp:596-603); host state only, no device work. */
+void s2_conv3d_reset_memory(s2_conv3d* layer);
 void s2_conv3d_free(s2_conv3d* layer);
 
 /* VAE resampling layers, built from the weight-blob sequence their
@@ -401,6 +404,9 @@ int s2_vae_resample_create(s2_context* ctx, int kind, const float* blob, size_t 
 int s2_vae_resample_output_shape(const s2_vae_resample* layer, int w, int h, int d, int memory_state, int* out_whdc);
 int s2_vae_resample_forward(s2_vae_resample* layer, const float* in, int64_t in_cstep, int w, int h, int d, int c,
                             int memory_state, float* out, int64_t out_cstep);
+/* reset_temporal_memory of every convolution inside (vae_downsample3d.cpp:139-143,
+ * vae_upsample3d.cpp:250-256). */
+void s2_vae_resample_reset_memory(s2_vae_resample* layer);
 void s2_vae_resample_free(s2_vae_resample* layer);
 
 /* VAEChunkedMHA (vae_chunked_mha.h, load_param / load_model :109-135, CPU

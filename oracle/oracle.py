@@ -440,6 +440,28 @@ def ref_mha_forward(E, heads, scale, weights, x, chunk=128, path: str = REF_VAE_
     return out
 
 
+def ref_vae_load(kind, blob, path: str = REF_VAE_SO) -> int:
+    """Load-time code (first nonzero of load_param / load_model / create_pipeline) of the reference's own
+    DecomposedConv3D (kind 0; the blob's 16 config values also go through load_param), VAEDownsample3D (1)
+    or VAEUpsample3D (2) given the floats its load_model reads."""
+    lib = C.CDLL(path)
+    lib.s2ref_vae_load.argtypes = [C.c_int, _f32p, C.c_size_t]
+    n = len(blob)
+    return int(lib.s2ref_vae_load(kind, _f32(blob) if n else np.zeros(1, np.float32), n))
+
+
+def ref_mha_code(ip, scale, weights, x, path: str = REF_VAE_SO) -> int:
+    """Return code of the reference's own VAEChunkedMHA built from params ip = (embed_dim, num_heads,
+    weight_data_size, kdim, vdim, chunk_size) and scale, then run on x [tokens][weight_data_size / embed_dim]
+    when it loaded."""
+    lib = C.CDLL(path)
+    lib.s2ref_mha_forward.argtypes = [_i32p, C.c_float, _f32p, C.c_size_t, _f32p, C.c_int, _f32p]
+    x = _f32(x)
+    w = _f32(weights) if len(weights) else np.zeros(1, np.float32)
+    out = np.zeros_like(x)
+    return int(lib.s2ref_mha_forward(_i32(ip), scale, w, len(weights), x, x.shape[0], out))
+
+
 class RefResample:
     """The reference's own VAEDownsample3D (kind 0) / VAEUpsample3D (kind 1) (oracle/_ref/libs2_ref_vae.so)."""
 

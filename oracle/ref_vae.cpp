@@ -122,6 +122,31 @@ void s2ref_resample_free(void* handle)
     delete static_cast<ncnn::Layer*>(handle);
 }
 
+// The load-time codes of one layer, built the way ncnn's Net builds it: kind 0
+// DecomposedConv3D (its 16 config values also go through load_param ids
+// 0-15), 1 VAEDownsample3D, 2 VAEUpsample3D; blob = the floats load_model
+// reads.  Returns the first nonzero code of load_param / load_model /
+// create_pipeline, else 0.
+int s2ref_vae_load(int kind, const float* blob, size_t count)
+{
+    ncnn::Layer* layer = kind == 0   ? static_cast<ncnn::Layer*>(new DecomposedConv3D)
+                         : kind == 1 ? static_cast<ncnn::Layer*>(new seedvr2::VAEDownsample3D)
+                                     : static_cast<ncnn::Layer*>(new seedvr2::VAEUpsample3D);
+    int r = 0;
+    if (kind == 0 && count >= 16)
+    {
+        ncnn::ParamDict pd;
+        for (int i = 0; i < 16; i++) pd.set(i, (int)blob[i]);
+        r = layer->load_param(pd);
+    }
+    ncnn::ModelBinFromFloats mb(blob, count);
+    ncnn::Option opt;
+    if (r == 0) r = layer->load_model(mb);
+    if (r == 0) r = layer->create_pipeline(opt);
+    delete layer;
+    return r;
+}
+
 // VAEChunkedMHA: params (embed_dim, num_heads, weight_data_size, kdim, vdim,
 // scale, chunk_size), weights in load_model order (q w, q b, k w, k b, v w,
 // v b, out w, out b).  x [tokens][qdim] -> out [tokens][qdim].

@@ -54,8 +54,9 @@ EXPORTED = [
     "s2_patchify_video", "s2_unpatchify_prediction", "s2_timestep_embedding", "s2_dit_set_io_weights",
     "s2_dit_forward_frontend", "s2_dit_forward_tail", "s2_dit_forward_step", "s2_dit_forward_step_host",
     "s2_dit_denoise", "s2_dit_denoise_host", "s2_apply_cfg",
-    "s2_conv3d_create", "s2_conv3d_output_shape", "s2_conv3d_forward", "s2_conv3d_free",
-    "s2_vae_resample_create", "s2_vae_resample_output_shape", "s2_vae_resample_forward", "s2_vae_resample_free",
+    "s2_conv3d_create", "s2_conv3d_output_shape", "s2_conv3d_forward", "s2_conv3d_reset_memory", "s2_conv3d_free",
+    "s2_vae_resample_create", "s2_vae_resample_output_shape", "s2_vae_resample_forward",
+    "s2_vae_resample_reset_memory", "s2_vae_resample_free",
     "s2_vae_mha_create", "s2_vae_mha_forward", "s2_vae_mha_free",
 ]
 
@@ -183,10 +184,14 @@ def lib() -> C.CDLL:
     L.s2_conv3d_output_shape.argtypes = [vp, ip, ip, ip, ip, pint]
     L.s2_conv3d_forward.argtypes = [vp, vp, i64, ip, ip, ip, ip, ip, vp, i64]
     L.s2_conv3d_free.argtypes = [vp]
+    L.s2_conv3d_reset_memory.argtypes = [vp]
+    L.s2_conv3d_reset_memory.restype = None
     L.s2_vae_resample_create.argtypes = [vp, ip, vp, C.c_size_t, C.POINTER(vp)]
     L.s2_vae_resample_output_shape.argtypes = [vp, ip, ip, ip, ip, pint]
     L.s2_vae_resample_forward.argtypes = [vp, vp, i64, ip, ip, ip, ip, ip, vp, i64]
     L.s2_vae_resample_free.argtypes = [vp]
+    L.s2_vae_resample_reset_memory.argtypes = [vp]
+    L.s2_vae_resample_reset_memory.restype = None
     L.s2_vae_mha_create.argtypes = [vp, ip, ip, C.c_float, vp, C.POINTER(vp)]
     L.s2_vae_mha_forward.argtypes = [vp, vp, ip, vp]
     L.s2_vae_mha_free.argtypes = [vp]
@@ -618,6 +623,9 @@ class Conv3d:
                                       out.data_ptr(), od * oh * ow), "s2_conv3d_forward")
         return out
 
+    def reset_temporal_memory(self):
+        lib().s2_conv3d_reset_memory(self.handle)
+
     def close(self):
         if self.handle:
             lib().s2_conv3d_free(self.handle)
@@ -661,6 +669,9 @@ class VaeResample:
         check(lib().s2_vae_resample_forward(self.handle, x.data_ptr(), d * h * w, w, h, d, c, memory_state,
                                             out.data_ptr(), od * oh * ow), "s2_vae_resample_forward")
         return out
+
+    def reset_temporal_memory(self):
+        lib().s2_vae_resample_reset_memory(self.handle)
 
     def close(self):
         if self.handle:

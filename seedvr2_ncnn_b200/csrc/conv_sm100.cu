@@ -612,6 +612,11 @@ int s2_conv3d_forward(s2_conv3d* l, const float* in, int64_t in_cstep, int w, in
     return S2_OK;
 }
 
+void s2_conv3d_reset_memory(s2_conv3d* l)
+{
+    if (l) l->mem_frames = 0;
+}
+
 void s2_conv3d_free(s2_conv3d* l)
 {
     if (!l) return;
@@ -738,16 +743,20 @@ int s2_vae_resample_forward(s2_vae_resample* l, const float* in, int64_t in_cste
         return s2_conv3d_forward(l->conv, in, in_cstep, w, h, d, c, memory_state, out, out_cstep);
     s2::Context& ctx = l->ctx->c;
     if (cudaSetDevice(ctx.device) != cudaSuccess) return S2_ERR_CUDA;
+    // the upscale conv drops its cached frames first, whatever fails later
+    // (decomposed_conv3d.cpp:609-611)
+    if (memory_state != S2_VAE_MEMORY_ACTIVE) s2_conv3d_reset_memory(l->upscale);
     int p[4];
     int r = s2_conv3d_output_shape(l->upscale, w, h, d, memory_state, p);
     if (r != S2_OK) return r;
-    const int ratio = l->tr * l->sr * l->sr;
-    if (p[3] != l->channels * ratio) return S2_ERR_INVALID; // vae_upsample3d.cpp:270-272
     const int64_t pplane = (int64_t)p[0] * p[1] * p[2];
     if ((r = l->packed.ensure((size_t)pplane * p[3] * 4)) != S2_OK) return r;
     float* packed = static_cast<float*>(l->packed.ptr);
     if ((r = s2_conv3d_forward(l->upscale, in, in_cstep, w, h, d, c, memory_state, packed, pplane)) != S2_OK)
         return r;
+    // checked after the upscale conv ran, as vae_upsample3d.cpp:268-272 does
+    const int ratio = l->tr * l->sr * l->sr;
+    if (p[3] != l->channels * ratio) return S2_ERR_INVALID;
     const int ot = shuffled_frames(l, p[2], memory_state);
     if (ot <= 0) return S2_ERR_INVALID;
     const int OW = p[0] * l->sr, OH = p[1] * l->sr;
@@ -768,6 +777,13 @@ int s2_vae_resample_forward(s2_vae_resample* l, const float* in, int64_t in_cste
         if (cudaGetLastError() != cudaSuccess) return S2_ERR_CUDA;
     }
     return s2_conv3d_forward(l->conv, sh, splane, OW, OH, ot, l->channels, memory_state, out, out_cstep);
+}
+
+void s2_vae_resample_reset_memory(s2_vae_resample* l)
+{
+    if (!l) return;
+    s2_conv3d_reset_memory(l->conv);
+    s2_conv3d_reset_memory(l->upscale);
 }
 
 void s2_vae_resample_free(s2_vae_resample* l)

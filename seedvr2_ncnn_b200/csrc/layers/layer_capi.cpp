@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "shared_linear.h"
+#include "vae_layers.h"
 
 using seedvr2::AdaptiveWindowAttention;
 
@@ -17,6 +18,36 @@ ncnn::Mat vec(const float* p, int n)
 {
     ncnn::Mat m(n);
     std::memcpy(m.data, p, (size_t)n * 4);
+    return m;
+}
+
+// ModelBin over one flat fp32 array, as ncnn's reads a .bin: load(w, type)
+// hands out the next w values, or an empty Mat when fewer are left.  Both
+// types read raw fp32 (type 0's tag word is not part of these arrays).
+class FloatModelBin : public ncnn::ModelBin
+{
+public:
+    FloatModelBin(const float* data, size_t count) : data(data), count(count) {}
+    virtual ncnn::Mat load(int w, int type) const
+    {
+        if ((type != 0 && type != 1) || w <= 0 || cursor + (size_t)w > count) return ncnn::Mat();
+        ncnn::Mat m = vec(data + cursor, w);
+        cursor += (size_t)w;
+        return m;
+    }
+
+private:
+    const float* data;
+    size_t count;
+    mutable size_t cursor = 0;
+};
+
+// [c][d][h][w] dense floats <-> a 4-D Mat (channel steps padded to 16 bytes)
+ncnn::Mat blob_4d(const float* p, int w, int h, int d, int c)
+{
+    ncnn::Mat m(w, h, d, c);
+    const size_t plane = (size_t)w * h * d;
+    for (int ch = 0; ch < c; ch++) std::memcpy((float*)m.data + m.cstep * ch, p + plane * ch, plane * 4);
     return m;
 }
 
@@ -133,6 +164,129 @@ int s2layer_shared_linear_forward(int num_output, int num_input, int bias_term, 
     }
     delete layer;
     return ret;
+}
+
+// VAE layers, built the way ncnn's Net builds them: kind 0 DecomposedConv3D
+// (its 16 config values also go through load_param ids 0-15), 1
+// VAEDownsample3D, 2 VAEUpsample3D; blob = the floats the layer's load_model
+// reads.  Returns the first nonzero code of load_param / load_model /
+// create_pipeline, else 0 with the layer in *out.
+int s2layer_vae_create(int kind, const float* blob, size_t count, void** out)
+{
+    *out = nullptr;
+    ncnn::Layer* layer = kind == 0   ? seedvr2::decomposed_conv3d_layer_creator(nullptr)
+                         : kind == 1 ? seedvr2::vae_downsample3d_layer_creator(nullptr)
+                         : kind == 2 ? seedvr2::vae_upsample3d_layer_creator(nullptr)
+                                     : nullptr;
+    if (!layer) return -1;
+    int ret = 0;
+    if (kind == 0 && count >= 16)
+    {
+        ncnn::ParamDict pd;
+        for (int i = 0; i < 16; i++) pd.set(i, (int)blob[i]);
+        ret = layer->load_param(pd);
+    }
+    if (ret == 0) ret = layer->load_model(FloatModelBin(blob, count));
+    ncnn::Option opt;
+    if (ret == 0) ret = layer->create_pipeline(opt);
+    if (ret != 0)
+    {
+        delete layer;
+        return ret;
+    }
+    *out = layer;
+    return 0;
+}
+
+// One forward under the given memory state (0 disabled, 1 initializing, 2
+// active): in dense [c][d][h][w] fp32, out dense [c][d][h][w] of at most
+// out_capacity floats, out_dims = (w, h, d, c).  Returns the layer's code.
+int s2layer_vae_forward(void* handle, int memory_state, const float* in, int w, int h, int d, int c, float* out,
+                        size_t out_capacity, int* out_dims)
+{
+    const ncnn::Layer* layer = static_cast<const ncnn::Layer*>(handle);
+    seedvr2::set_vae_memory_state(static_cast<seedvr2::MemoryState>(memory_state));
+    ncnn::Mat top;
+    ncnn::Option opt;
+    const int r = layer->forward(blob_4d(in, w, h, d, c), top, opt);
+    if (r != 0) return r;
+    out_dims[0] = top.w;
+    out_dims[1] = top.h;
+    out_dims[2] = top.d;
+    out_dims[3] = top.c;
+    const size_t plane = (size_t)top.w * top.h * top.d;
+    if (plane * top.c > out_capacity) return -1;
+    for (int ch = 0; ch < top.c; ch++) std::memcpy(out + plane * ch, (const float*)top.data + top.cstep * ch, plane * 4);
+    return 0;
+}
+
+// Output extents (w, h, d, c) of a forward on a w x h x d input under the
+// given memory state (uploads the weights on first use).
+int s2layer_vae_output_shape(void* handle, int memory_state, int w, int h, int d, int* out_whdc)
+{
+    const ncnn::Layer* layer = static_cast<const ncnn::Layer*>(handle);
+    seedvr2::set_vae_memory_state(static_cast<seedvr2::MemoryState>(memory_state));
+    if (auto* l = dynamic_cast<const seedvr2::DecomposedConv3D*>(layer)) return l->output_shape(w, h, d, out_whdc);
+    if (auto* l = dynamic_cast<const seedvr2::VAEDownsample3D*>(layer)) return l->output_shape(w, h, d, out_whdc);
+    if (auto* l = dynamic_cast<const seedvr2::VAEUpsample3D*>(layer)) return l->output_shape(w, h, d, out_whdc);
+    return -1;
+}
+
+// reset_temporal_memory of a layer from s2layer_vae_create.
+void s2layer_vae_reset(void* handle)
+{
+    const ncnn::Layer* layer = static_cast<const ncnn::Layer*>(handle);
+    if (auto* l = dynamic_cast<const seedvr2::DecomposedConv3D*>(layer)) l->reset_temporal_memory();
+    if (auto* l = dynamic_cast<const seedvr2::VAEDownsample3D*>(layer)) l->reset_temporal_memory();
+    if (auto* l = dynamic_cast<const seedvr2::VAEUpsample3D*>(layer)) l->reset_temporal_memory();
+}
+
+void s2layer_vae_free(void* handle)
+{
+    delete static_cast<ncnn::Layer*>(handle);
+}
+
+// VAEChunkedMHA: ip = embed_dim, num_heads, weight_data_size, kdim, vdim,
+// chunk_size (param ids 0-4 and 20), scale = param 6; weights in load_model
+// order (q w, q b, k w, k b, v w, v b, out w, out b).  Same return
+// convention as s2layer_vae_create.
+int s2layer_mha_create(const int* ip, float scale, const float* weights, size_t count, void** out)
+{
+    *out = nullptr;
+    ncnn::Layer* layer = seedvr2::vae_chunked_mha_layer_creator(nullptr);
+    ncnn::ParamDict pd;
+    pd.set(0, ip[0]);
+    pd.set(1, ip[1]);
+    pd.set(2, ip[2]);
+    pd.set(3, ip[3]);
+    pd.set(4, ip[4]);
+    pd.set(6, scale);
+    pd.set(20, ip[5]);
+    int ret = layer->load_param(pd);
+    if (ret == 0) ret = layer->load_model(FloatModelBin(weights, count));
+    ncnn::Option opt;
+    if (ret == 0) ret = layer->create_pipeline(opt);
+    if (ret != 0)
+    {
+        delete layer;
+        return ret;
+    }
+    *out = layer;
+    return 0;
+}
+
+// x [tokens][qdim] -> out [tokens][qdim] through forward(Mat).
+int s2layer_mha_forward(void* handle, const float* x, int tokens, int qdim, float* out)
+{
+    const ncnn::Layer* layer = static_cast<const ncnn::Layer*>(handle);
+    ncnn::Mat bottom(qdim, tokens);
+    std::memcpy(bottom.data, x, (size_t)qdim * tokens * 4);
+    ncnn::Mat top;
+    ncnn::Option opt;
+    const int r = layer->forward(bottom, top, opt);
+    if (r != 0) return r;
+    std::memcpy(out, top.data, (size_t)top.w * top.h * 4);
+    return 0;
 }
 
 } // extern "C"

@@ -4,8 +4,9 @@
 // only lets the layer classes build and run where ncnn is not installed.
 //
 // Semantics follow ncnn's public API: Mat is a reference-counted host blob of
-// dims/w/h/c with 16-byte aligned channel steps; ModelBin::load(w, 1) reads
-// w raw fp32 values; ParamDict maps integer ids to int/float values.
+// dims/w/h/d/c (n = 1: one sample) whose 3-D and 4-D channel steps are
+// rounded up to 16 bytes; ModelBin::load(w, 1) reads w raw fp32 values;
+// ParamDict maps integer ids to int/float values.
 #pragma once
 
 #ifdef S2_WITH_NCNN
@@ -35,6 +36,7 @@ public:
     Mat(int w, size_t es = 4u) { create(w, es); }
     Mat(int w, int h, size_t es = 4u) { create(w, h, es); }
     Mat(int w, int h, int c, size_t es = 4u) { create(w, h, c, es); }
+    Mat(int w, int h, int d, int c, size_t es = 4u) { create(w, h, d, c, es); }
     Mat(const Mat& m) { assign(m); }
     Mat& operator=(const Mat& m)
     {
@@ -47,9 +49,10 @@ public:
     }
     ~Mat() { release(); }
 
-    void create(int _w, size_t es = 4u, Allocator* = 0) { shape(1, _w, 1, 1, es); }
-    void create(int _w, int _h, size_t es = 4u, Allocator* = 0) { shape(2, _w, _h, 1, es); }
-    void create(int _w, int _h, int _c, size_t es = 4u, Allocator* = 0) { shape(3, _w, _h, _c, es); }
+    void create(int _w, size_t es = 4u, Allocator* = 0) { shape(1, _w, 1, 1, 1, es); }
+    void create(int _w, int _h, size_t es = 4u, Allocator* = 0) { shape(2, _w, _h, 1, 1, es); }
+    void create(int _w, int _h, int _c, size_t es = 4u, Allocator* = 0) { shape(3, _w, _h, 1, _c, es); }
+    void create(int _w, int _h, int _d, int _c, size_t es = 4u, Allocator* = 0) { shape(4, _w, _h, _d, _c, es); }
     bool empty() const { return data == 0 || total() == 0; }
     size_t total() const { return cstep * c; }
     float* row(int y) { return (float*)((unsigned char*)data + (size_t)w * y * elemsize); }
@@ -63,10 +66,11 @@ public:
     Mat reshape(int _w, int _h) const
     {
         Mat m(*this);
-        if ((size_t)_w * _h != (size_t)w * h * c) return Mat();
+        if ((size_t)_w * _h != (size_t)w * h * d * c) return Mat();
         m.dims = 2;
         m.w = _w;
         m.h = _h;
+        m.d = 1;
         m.c = 1;
         m.cstep = (size_t)_w * _h;
         return m;
@@ -77,21 +81,22 @@ public:
     size_t elemsize = 0;
     int elempack = 0;
     Allocator* allocator = 0;
-    int dims = 0, w = 0, h = 0, d = 1, c = 0;
+    int dims = 0, w = 0, h = 0, d = 1, c = 0, n = 1;
     size_t cstep = 0;
 
 private:
-    void shape(int _dims, int _w, int _h, int _c, size_t es)
+    void shape(int _dims, int _w, int _h, int _d, int _c, size_t es)
     {
         release();
         dims = _dims;
         w = _w;
         h = _h;
+        d = _d;
         c = _c;
         elemsize = es;
         elempack = 1;
-        const size_t plane = (size_t)w * h * es;
-        cstep = (dims == 3 ? ((plane + 15) & ~(size_t)15) : plane) / es;
+        const size_t plane = (size_t)w * h * d * es;
+        cstep = (dims >= 3 ? ((plane + 15) & ~(size_t)15) : plane) / es;
         const size_t bytes = total() * es;
         if (!bytes) return;
         data = std::malloc(bytes + 64);
@@ -110,6 +115,7 @@ private:
         h = m.h;
         d = m.d;
         c = m.c;
+        n = m.n;
         cstep = m.cstep;
     }
     void release()
@@ -122,6 +128,7 @@ private:
         data = 0;
         refcount = 0;
         dims = w = h = c = 0;
+        d = n = 1;
         cstep = 0;
     }
 };
@@ -187,6 +194,7 @@ public:
     virtual int create_pipeline(const Option&) { return 0; }
     virtual int destroy_pipeline(const Option&) { return 0; }
     virtual int forward(const std::vector<Mat>&, std::vector<Mat>&, const Option&) const { return -1; }
+    virtual int forward(const Mat&, Mat&, const Option&) const { return -1; }
     bool one_blob_only = false;
     bool support_inplace = false;
     void* userdata = 0;

@@ -1,9 +1,10 @@
 """ctypes driver of the ncnn-surface layer classes (libseedvr2_ncnn.so).
 
-The C++ classes ``seedvr2::AdaptiveWindowAttention`` and
-``seedvr2::SharedLinear`` keep the reference's ncnn custom-layer surface
-(creator, ParamDict ids, ModelBin weight order, blob arity, error codes);
-their ``forward`` runs on libseedvr2_cuda.  This module drives them through
+The C++ classes ``seedvr2::AdaptiveWindowAttention``, ``seedvr2::SharedLinear``
+and the VAE's ``DecomposedConv3D``, ``VAEDownsample3D``, ``VAEUpsample3D`` and
+``VAEChunkedMHA`` keep the reference's ncnn custom-layer surface (creator,
+ParamDict ids, ModelBin weight order, blob arity, error codes); their
+``forward`` runs on libseedvr2_cuda.  This module drives them through
 the library's small extern "C" driver with host fp32 arrays, the way ncnn's
 Net would: create -> load_param -> load_model -> forward.
 """
@@ -32,6 +33,16 @@ def lib() -> C.CDLL:
                                           C.c_int, C.c_void_p, C.c_void_p, C.c_int, f32p, f32p]
         L.s2layer_shared_linear_forward.argtypes = [C.c_int, C.c_int, C.c_int, f32p, f32p, C.c_int, f32p, C.c_int,
                                                     f32p, f32p]
+        L.s2layer_vae_create.argtypes = [C.c_int, f32p, C.c_size_t, C.POINTER(C.c_void_p)]
+        L.s2layer_vae_output_shape.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, i32p]
+        L.s2layer_vae_forward.argtypes = [C.c_void_p, C.c_int, f32p, C.c_int, C.c_int, C.c_int, C.c_int, f32p,
+                                          C.c_size_t, i32p]
+        L.s2layer_vae_reset.argtypes = [C.c_void_p]
+        L.s2layer_vae_free.argtypes = [C.c_void_p]
+        L.s2layer_mha_create.argtypes = [i32p, C.c_float, f32p, C.c_size_t, C.POINTER(C.c_void_p)]
+        L.s2layer_mha_forward.argtypes = [C.c_void_p, f32p, C.c_int, C.c_int, f32p]
+        L.s2layer_vae_free.restype = None
+        L.s2layer_vae_reset.restype = None
         _lib = L
     return _lib
 
@@ -77,3 +88,130 @@ def shared_linear(video, text, weight, bias=None):
     r = lib().s2layer_shared_linear_forward(n, k, int(bias is not None), _f32(flat), video, video.shape[0], text,
                                             text.shape[0], vo, to)
     return r, vo, to
+
+
+class LayerError(RuntimeError):
+    """A layer call returned a nonzero code (the reference's codes: -1 invalid, -100 allocation; plus the
+    library's -3 CUDA, -5 no device)."""
+
+    def __init__(self, what, code):
+        super().__init__(f"{what} returned {code}")
+        self.code = code
+
+
+# VAE layer kinds of s2layer_vae_create
+DECOMPOSED_CONV3D, VAE_DOWNSAMPLE3D, VAE_UPSAMPLE3D = 0, 1, 2
+
+
+def _blob(a):
+    a = _f32(np.asarray(a).ravel())
+    return (a if a.size else np.zeros(1, np.float32)), int(a.size)
+
+
+def vae_load_code(kind, blob):
+    """First nonzero code of load_param / load_model / create_pipeline for a VAE layer, else 0."""
+    arr, n = _blob(blob)
+    h = C.c_void_p()
+    r = lib().s2layer_vae_create(kind, arr, n, C.byref(h))
+    if r == 0:
+        lib().s2layer_vae_free(h)
+    return r
+
+
+class VaeLayer:
+    """DecomposedConv3D / VAEDownsample3D / VAEUpsample3D through the layer surface, built from the floats
+    its load_model reads (for DecomposedConv3D the 16 config values also go through load_param)."""
+
+    def __init__(self, kind, blob):
+        arr, n = _blob(blob)
+        self.handle = C.c_void_p()
+        r = lib().s2layer_vae_create(kind, arr, n, C.byref(self.handle))
+        if r != 0:
+            self.handle = None
+            raise LayerError("load", r)
+
+    def output_shape(self, w, h, d, memory_state):
+        dims = np.zeros(4, np.int32)
+        r = lib().s2layer_vae_output_shape(self.handle, memory_state, w, h, d, dims)
+        if r != 0:
+            raise LayerError("output_shape", r)
+        return dims.tolist()
+
+    def forward(self, x, memory_state):
+        """x [c][d][h][w] fp32 (host) under the VAE memory state -> [c'][d'][h'][w']."""
+        x = _f32(x)
+        c, d, h, w = x.shape
+        try:
+            ow, oh, od, oc = self.output_shape(w, h, d, memory_state)
+            cap = ow * oh * od * oc
+        except LayerError:
+            cap = 1  # forward reports the same rejection (and drops the cached frames as it does)
+        out = np.zeros(max(cap, 1), np.float32)
+        dims = np.zeros(4, np.int32)
+        r = lib().s2layer_vae_forward(self.handle, memory_state, x, w, h, d, c, out, out.size, dims)
+        if r != 0:
+            raise LayerError("forward", r)
+        ow, oh, od, oc = dims.tolist()
+        return out[:ow * oh * od * oc].reshape(oc, od, oh, ow).copy()
+
+    def reset_temporal_memory(self):
+        lib().s2layer_vae_reset(self.handle)
+
+    def close(self):
+        if self.handle:
+            lib().s2layer_vae_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _mha_params(E, heads, wds, kdim, vdim, chunk):
+    return np.asarray([E, heads, E * E if wds is None else wds, E if kdim is None else kdim,
+                       E if vdim is None else vdim, chunk], np.int32)
+
+
+def mha_load_code(E, heads, scale, weights, *, wds=None, kdim=None, vdim=None, chunk=128):
+    """First nonzero code of VAEChunkedMHA's load_param / load_model / create_pipeline, else 0."""
+    arr, n = _blob(weights)
+    h = C.c_void_p()
+    r = lib().s2layer_mha_create(_mha_params(E, heads, wds, kdim, vdim, chunk), scale, arr, n, C.byref(h))
+    if r == 0:
+        lib().s2layer_vae_free(h)
+    return r
+
+
+class VaeMhaLayer:
+    """VAEChunkedMHA through the layer surface: x [tokens][E] (host) -> [tokens][E]."""
+
+    def __init__(self, E, heads, scale, weights, chunk=128):
+        arr, n = _blob(weights)
+        self.E = E
+        self.handle = C.c_void_p()
+        r = lib().s2layer_mha_create(_mha_params(E, heads, None, None, None, chunk), scale, arr, n,
+                                     C.byref(self.handle))
+        if r != 0:
+            self.handle = None
+            raise LayerError("load", r)
+
+    def forward(self, x):
+        x = _f32(x)
+        out = np.zeros_like(x)
+        r = lib().s2layer_mha_forward(self.handle, x, x.shape[0], x.shape[1], out)
+        if r != 0:
+            raise LayerError("forward", r)
+        return out
+
+    def close(self):
+        if self.handle:
+            lib().s2layer_vae_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
