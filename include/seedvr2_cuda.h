@@ -176,6 +176,10 @@ int s2_ada_rmsnorm(s2_context* ctx, int rows, int D, const float* x, float eps, 
                    const float* scale, void* out_bf16);
 /* fp32 -> bf16 (round to nearest even). */
 int s2_convert_f32_bf16(s2_context* ctx, const float* in, void* out, int64_t count);
+/* Number of NaN / Inf values among `count` device elements of dtype
+ * S2_DTYPE_F32 or S2_DTYPE_BF16 (the reference's finite-check shader,
+ * seedvr2_dit.cpp:33-54, as a count); synchronises. */
+int s2_count_nonfinite(s2_context* ctx, const void* data, int64_t count, int dtype, int64_t* nonfinite);
 
 /* ---------------------------------------------------------------------------
  * DiT block stack.  Replaces SeedVR2DiTBlocks' block graph
@@ -225,6 +229,18 @@ int s2_dit_set_block_weights(s2_dit* dit, int block, const s2_block_host_weights
  * ada offsets ~N(0,1)/sqrt(D) (+1 on the scale rows), qk norms ~N(1,0.02),
  * rope freqs 1/10000^(2i/(2*pairs))). */
 int s2_dit_init_random(s2_dit* dit, uint64_t seed);
+/* Finite checks (the reference's SEEDVR2_DIT_CHECK_FINITE,
+ * seedvr2_dit.cpp:651-716 and :843-1071).  With enable != 0, every
+ * s2_dit_forward (and the step / denoise calls built on it; one GPU) counts
+ * the NaN / Inf values of the video and text rows at the block stack's input
+ * (the frontend's output) and after every block, on the device, reads the
+ * counters once at the end and returns -1, as the reference does, when any
+ * is non-zero.  s2_dit_nonfinite_report then gives the first non-finite point
+ * of the last checked forward: block -1 = the input, b = block b's output,
+ * num_blocks = all finite; and the counts there (-1 before any checked
+ * forward). */
+int s2_dit_set_check_finite(s2_dit* dit, int enable);
+int s2_dit_nonfinite_report(const s2_dit* dit, int* block, int64_t* video_count, int64_t* text_count);
 /* Device-resident forward of all blocks for ONE sample:
  * x: fp32 [Nv + Nt][D] (video rows then text rows), updated in place;
  * modulation: fp32 [6][D] device (frontend outputs out2..out7). */

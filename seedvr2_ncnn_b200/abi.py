@@ -48,7 +48,9 @@ EXPORTED = [
     "s2_profile_enable", "s2_profile_read",
     "s2_plan_build", "s2_plan_info", "s2_plan_copy", "s2_plan_free",
     "s2_awa_forward", "s2_awa_forward_static", "s2_shared_linear", "s2_ada_rmsnorm", "s2_convert_f32_bf16",
+    "s2_count_nonfinite",
     "s2_dit_create", "s2_dit_free", "s2_dit_set_block_weights", "s2_dit_init_random", "s2_dit_forward",
+    "s2_dit_set_check_finite", "s2_dit_nonfinite_report",
     "s2_dit_forward_host", "s2_shard_build", "s2_shard_counts", "s2_shard_lists", "s2_shard_free",
     "s2_dist_unique_id", "s2_dist_init", "s2_dist_sync", "s2_dist_destroy", "s2_dit_forward_sharded",
     "s2_patchify_video", "s2_unpatchify_prediction", "s2_timestep_embedding", "s2_dit_set_io_weights",
@@ -157,6 +159,9 @@ def lib() -> C.CDLL:
     L.s2_dit_free.restype = None
     L.s2_dit_set_block_weights.argtypes = [vp, ip, C.POINTER(BlockHostWeights)]
     L.s2_dit_init_random.argtypes = [vp, C.c_uint64]
+    L.s2_count_nonfinite.argtypes = [vp, vp, i64, C.c_int, C.POINTER(C.c_int64)]
+    L.s2_dit_set_check_finite.argtypes = [vp, C.c_int]
+    L.s2_dit_nonfinite_report.argtypes = [vp, C.POINTER(C.c_int), C.POINTER(C.c_int64), C.POINTER(C.c_int64)]
     L.s2_dit_forward.argtypes = [vp, pint, ip, vp, vp]
     L.s2_dit_forward_host.argtypes = [vp, pint, pint, ip, vp, vp, vp, vp, vp]
     L.s2_shard_build.argtypes = [pint, ip, pint, ip, ip, ip, C.POINTER(vp)]
@@ -209,6 +214,16 @@ def error_string(code: int) -> str:
 def check(code: int, what: str) -> None:
     if code != S2_OK:
         raise S2Error(code, what)
+
+
+def count_nonfinite(ctx, t) -> int:
+    """NaN / Inf elements of a contiguous fp32 or bf16 CUDA tensor (s2_count_nonfinite; synchronises)."""
+    import torch
+
+    dtype = {torch.float32: S2_DTYPE_F32, torch.bfloat16: S2_DTYPE_BF16}[t.dtype]
+    n = C.c_int64()
+    check(lib().s2_count_nonfinite(ctx.handle, t.data_ptr(), t.numel(), dtype, C.byref(n)), "s2_count_nonfinite")
+    return n.value
 
 
 def _ints(values) -> C.Array:
@@ -470,6 +485,19 @@ class Dit:
 
     def init_random(self, seed: int):
         check(lib().s2_dit_init_random(self.handle, seed), "s2_dit_init_random")
+
+    def set_check_finite(self, enable: bool = True):
+        """Count the NaN / Inf values of the video and text rows at the block stack's input and after every
+        block; a forward that finds any fails with code -1 (see nonfinite_report)."""
+        check(lib().s2_dit_set_check_finite(self.handle, int(bool(enable))), "s2_dit_set_check_finite")
+
+    def nonfinite_report(self):
+        """(block, video_count, text_count) of the last checked forward's first non-finite point: block -1 =
+        the input, b = block b's output, num_blocks = all finite."""
+        b, v, t = C.c_int(), C.c_int64(), C.c_int64()
+        check(lib().s2_dit_nonfinite_report(self.handle, C.byref(b), C.byref(v), C.byref(t)),
+              "s2_dit_nonfinite_report")
+        return b.value, v.value, t.value
 
     def set_block_weights(self, block: int, w: dict):
         """w: dict of contiguous fp32 numpy arrays (keys of BlockHostWeights; biases may be None)."""

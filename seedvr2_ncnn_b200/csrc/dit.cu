@@ -99,6 +99,14 @@ struct s2_dit
     bool io_loaded = false;
     s2::DeviceBuffer io_ws;   // frontend / tail activations
     s2::DeviceBuffer io_host; // staging of s2_dit_forward_step_host
+    // finite checks (s2_dit_set_check_finite): NaN / Inf counters of the
+    // video and text rows at the block stack's input and after every block,
+    // [blocks + 1][2]; the last checked forward's first non-finite point
+    bool check_finite = false;
+    s2::DeviceBuffer finite;
+    bool finite_checked = false;
+    int nonfinite_block = 0;
+    int64_t nonfinite_video = 0, nonfinite_text = 0;
 };
 
 namespace {
@@ -106,6 +114,15 @@ namespace {
 size_t align256(size_t b)
 {
     return (b + 255) & ~size_t(255);
+}
+
+// NaN / Inf counts of the residual's video rows [Nv][D] and text rows
+// [Nt][D] into counters[0] / counters[1].
+int count_rows_nonfinite(s2::Context& c, const float* x, int Nv, int Nt, int D, unsigned long long* counters)
+{
+    const int r = s2::launch_count_nonfinite(c, x, (int64_t)Nv * D, S2_DTYPE_F32, counters);
+    if (r != S2_OK) return r;
+    return s2::launch_count_nonfinite(c, x + (size_t)Nv * D, (int64_t)Nt * D, S2_DTYPE_F32, counters + 1);
 }
 
 int get_plan(s2_dit* d, const int* shape, int shifted, s2_plan** out)
@@ -446,6 +463,22 @@ int s2_dit_set_block_weights(s2_dit* d, int block, const s2_block_host_weights* 
     return r;
 }
 
+int s2_dit_set_check_finite(s2_dit* d, int enable)
+{
+    if (!d) return S2_ERR_INVALID;
+    d->check_finite = enable != 0;
+    return S2_OK;
+}
+
+int s2_dit_nonfinite_report(const s2_dit* d, int* block, int64_t* video_count, int64_t* text_count)
+{
+    if (!d || !d->finite_checked) return S2_ERR_INVALID;
+    if (block) *block = d->nonfinite_block;
+    if (video_count) *video_count = d->nonfinite_video;
+    if (text_count) *text_count = d->nonfinite_text;
+    return S2_OK;
+}
+
 int s2_dit_init_random(s2_dit* d, uint64_t seed)
 {
     if (d) d->rope_stale = true;
@@ -551,6 +584,18 @@ int s2_dit_forward(s2_dit* d, const int* video_shape, int text_length, float* x,
     if ((r = s2::launch_add_vectors(c, d->ada_all, modulation, mods, cfg.num_blocks * 6 * D, 6 * D)) != S2_OK)
         return r;
 
+    // finite checks: the block stack's input (the frontend's output), then
+    // every block's output, counted on the device; read once at the end
+    unsigned long long* fin = nullptr;
+    const size_t nfin = 2 * (size_t)(cfg.num_blocks + 1);
+    if (d->check_finite)
+    {
+        if ((r = d->finite.ensure(nfin * sizeof(unsigned long long))) != S2_OK) return r;
+        fin = static_cast<unsigned long long*>(d->finite.ptr);
+        if (cudaMemsetAsync(fin, 0, nfin * sizeof(unsigned long long), c.stream) != cudaSuccess) return S2_ERR_CUDA;
+        if ((r = count_rows_nonfinite(c, x, Nv, Nt, D, fin)) != S2_OK) return r;
+    }
+
     for (int b = 0; b < cfg.num_blocks; b++)
     {
         const s2_dit::Block& bl = d->blocks[b];
@@ -594,6 +639,30 @@ int s2_dit_forward(s2_dit* d, const int* video_shape, int text_length, float* x,
         if ((r = s2::launch_shared_linear(c, M, 0, D, F, u, nullptr, bl.w_down, cfg.mlp_bias ? bl.b_down : nullptr,
                                           s2::EPI_GATE_RESIDUAL, mb + 5 * D, 1, x, nullptr)) != S2_OK)
             return r;
+        if (fin && (r = count_rows_nonfinite(c, x, Nv, Nt, D, fin + 2 * (b + 1))) != S2_OK) return r;
+    }
+    if (fin)
+    {
+        // -1 as the reference returns when its frontend or block-graph output
+        // is non-finite (seedvr2_dit.cpp:700-716, :1068-1071); counting every
+        // block's output as well names the first block that produced one (the
+        // blocks after it have run)
+        std::vector<unsigned long long> h(nfin);
+        if (cudaMemcpyAsync(h.data(), fin, nfin * sizeof(unsigned long long), cudaMemcpyDeviceToHost, c.stream) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(c.stream) != cudaSuccess)
+            return S2_ERR_CUDA;
+        d->finite_checked = true;
+        d->nonfinite_block = cfg.num_blocks;
+        d->nonfinite_video = d->nonfinite_text = 0;
+        for (int i = 0; i <= cfg.num_blocks; i++)
+            if (h[2 * i] || h[2 * i + 1])
+            {
+                d->nonfinite_block = i - 1;
+                d->nonfinite_video = (int64_t)h[2 * i];
+                d->nonfinite_text = (int64_t)h[2 * i + 1];
+                return S2_ERR_INVALID;
+            }
     }
     return S2_OK;
 }

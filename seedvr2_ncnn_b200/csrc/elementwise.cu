@@ -444,6 +444,72 @@ int launch_rope_table(Context& ctx, const float* freqs, int pairs, int max_pos, 
     return finish(ctx);
 }
 
+namespace {
+// *count += number of NaN / Inf elements of x[0, n): the reference's finite
+// check (seedvr2_dit.cpp:33-54 sets a flag per blob; a count says the same
+// and how much).  An element is non-finite when its exponent bits are all
+// ones.  16-byte loads (4 fp32 or 8 bf16) over the aligned body, scalar head
+// and tail, one atomic per warp.
+template <bool BF16>
+__global__ void __launch_bounds__(256) count_nonfinite_kernel(const void* __restrict__ x, int64_t n,
+                                                              unsigned long long* __restrict__ count)
+{
+    constexpr int kPer = BF16 ? 8 : 4; // elements per 16 bytes
+    const uintptr_t base = reinterpret_cast<uintptr_t>(x);
+    const int esz = BF16 ? 2 : 4;
+    // elements before the first 16-byte boundary (the pointer is element aligned)
+    int64_t head = (int64_t)(((16 - (base & 15)) & 15) / esz);
+    if (head > n) head = n;
+    const int64_t vecs = (n - head) / kPer;
+    const int64_t tail0 = head + vecs * kPer;
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, nthreads = (int64_t)gridDim.x * blockDim.x;
+    unsigned int bad = 0;
+    const uint4* v = reinterpret_cast<const uint4*>(base + head * esz);
+    for (int64_t i = tid; i < vecs; i += nthreads)
+    {
+        const uint4 u = __ldg(v + i);
+        const unsigned int w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+        {
+            if (BF16)
+                bad += ((w[j] & 0x7f80u) == 0x7f80u) + ((w[j] & 0x7f800000u) == 0x7f800000u);
+            else
+                bad += (w[j] & 0x7f800000u) == 0x7f800000u;
+        }
+    }
+    // head and tail elements (fewer than 16 bytes each)
+    if (tid < head + (n - tail0))
+    {
+        const int64_t e = tid < head ? tid : tail0 + (tid - head);
+        if (BF16)
+            bad += (__ldg(reinterpret_cast<const unsigned short*>(x) + e) & 0x7f80u) == 0x7f80u;
+        else
+            bad += (__ldg(reinterpret_cast<const unsigned int*>(x) + e) & 0x7f800000u) == 0x7f800000u;
+    }
+    bad = __reduce_add_sync(0xffffffffu, bad);
+    if ((threadIdx.x & 31) == 0 && bad) atomicAdd(count, (unsigned long long)bad);
+}
+} // namespace
+
+int launch_count_nonfinite(Context& ctx, const void* x, int64_t n, int dtype, unsigned long long* count)
+{
+    if (n < 0 || !count || (dtype != S2_DTYPE_F32 && dtype != S2_DTYPE_BF16)) return S2_ERR_INVALID;
+    if (n == 0) return S2_OK;
+    const int esz = dtype == S2_DTYPE_BF16 ? 2 : 4;
+    if (!x || (reinterpret_cast<uintptr_t>(x) % esz)) return S2_ERR_INVALID;
+    ProfileScope prof(ctx, K_OTHER, 0.0, (double)n * esz);
+    // one 16-byte load per thread per pass; the head / tail (< 8 + 8 elements) fit in the first block
+    int64_t blocks = (n * esz / 16 + 255) / 256;
+    if (blocks < 1) blocks = 1;
+    if (blocks > ctx.num_sms * 8) blocks = ctx.num_sms * 8;
+    if (dtype == S2_DTYPE_BF16)
+        count_nonfinite_kernel<true><<<(int)blocks, 256, 0, ctx.stream>>>(x, n, count);
+    else
+        count_nonfinite_kernel<false><<<(int)blocks, 256, 0, ctx.stream>>>(x, n, count);
+    return finish(ctx);
+}
+
 int launch_add_vectors(Context& ctx, const float* a, const float* b, float* out, int count, int period)
 {
     if (count <= 0) return S2_OK;

@@ -41,7 +41,8 @@ enum
     WS_QKV_PACKED = 0, // AWA: packed bf16 Q, K, V
     WS_TEXT_PARTIAL = 1,
     WS_DIT = 2, // DiT forward activations
-    WS_CFG = 3, // apply_cfg reduction scratch (s2_apply_cfg, dit.cu)
+    WS_CFG = 3,    // apply_cfg reduction scratch (s2_apply_cfg, dit.cu)
+    WS_FINITE = 4, // s2_count_nonfinite's counter
 };
 
 } // namespace
@@ -297,6 +298,26 @@ int s2_convert_f32_bf16(s2_context* ctx, const float* in, void* out, int64_t cou
     if (!ctx || !in || !out) return S2_ERR_INVALID;
     if (cudaSetDevice(ctx->c.device) != cudaSuccess) return S2_ERR_CUDA;
     return s2::launch_convert_f32_bf16(ctx->c, in, out, count);
+}
+
+int s2_count_nonfinite(s2_context* ctx, const void* data, int64_t count, int dtype, int64_t* nonfinite)
+{
+    if (!ctx || !nonfinite || count < 0) return S2_ERR_INVALID;
+    *nonfinite = 0;
+    if (count == 0) return S2_OK;
+    s2::Context& c = ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    int r = c.ws[WS_FINITE].ensure(sizeof(unsigned long long));
+    if (r != S2_OK) return r;
+    unsigned long long* d = static_cast<unsigned long long*>(c.ws[WS_FINITE].ptr);
+    if (cudaMemsetAsync(d, 0, sizeof(*d), c.stream) != cudaSuccess) return S2_ERR_CUDA;
+    if ((r = s2::launch_count_nonfinite(c, data, count, dtype, d)) != S2_OK) return r;
+    unsigned long long h = 0;
+    if (cudaMemcpyAsync(&h, d, sizeof(h), cudaMemcpyDeviceToHost, c.stream) != cudaSuccess ||
+        cudaStreamSynchronize(c.stream) != cudaSuccess)
+        return S2_ERR_CUDA;
+    *nonfinite = (int64_t)h;
+    return S2_OK;
 }
 
 // ------------------------------------------------------- token formats

@@ -259,6 +259,8 @@ int conv3d_gemm(Context& ctx, const Conv3dGeometry& g, const void* X, int frames
 
 int launch_convert_f32_bf16(Context& ctx, const float* in, void* out, int64_t count);
 int launch_add_vectors(Context& ctx, const float* a, const float* b, float* out, int count, int period);
+// *count += NaN / Inf elements of x[0, n) (dtype S2_DTYPE_F32 or S2_DTYPE_BF16)
+int launch_count_nonfinite(Context& ctx, const void* x, int64_t n, int dtype, unsigned long long* count);
 int launch_fill_normal_bf16(Context& ctx, void* out, int64_t count, uint64_t seed, float mean, float stddev);
 int launch_fill_normal_f32(Context& ctx, float* out, int64_t count, uint64_t seed, float mean, float stddev);
 
