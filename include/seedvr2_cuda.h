@@ -240,6 +240,15 @@ int s2_dit_init_random(s2_dit* dit, uint64_t seed);
  * num_blocks = all finite; and the counts there (-1 before any checked
  * forward). */
 int s2_dit_set_check_finite(s2_dit* dit, int enable);
+/* Block checkpoints (the checkpoint_blocks of SeedVR2DiTBlocks::record_blocks,
+ * seedvr2_dit.cpp:644-649, :817-831, :1073-1089, behind the reference's
+ * SEEDVR2_DIT_DUMP_BLOCKS dumps): after block blocks[i] of every following
+ * forward (one GPU), the block's video rows are copied to video[i] and its
+ * text rows to text[i] (device fp32 [Nv][D] and [Nt][D] of the forward's
+ * shape; s2_dit_forward_host writes sample s at its rows, as in its outputs).
+ * A block outside [0, num_blocks) is -1, as the reference's range check.
+ * count 0 clears them.  The pointers are kept, not copied. */
+int s2_dit_set_checkpoints(s2_dit* dit, const int* blocks, int count, float* const* video, float* const* text);
 int s2_dit_nonfinite_report(const s2_dit* dit, int* block, int64_t* video_count, int64_t* text_count);
 /* Device-resident forward of all blocks for ONE sample:
  * x: fp32 [Nv + Nt][D] (video rows then text rows), updated in place;

@@ -50,7 +50,7 @@ EXPORTED = [
     "s2_awa_forward", "s2_awa_forward_static", "s2_shared_linear", "s2_ada_rmsnorm", "s2_convert_f32_bf16",
     "s2_count_nonfinite",
     "s2_dit_create", "s2_dit_free", "s2_dit_set_block_weights", "s2_dit_init_random", "s2_dit_forward",
-    "s2_dit_set_check_finite", "s2_dit_nonfinite_report",
+    "s2_dit_set_check_finite", "s2_dit_nonfinite_report", "s2_dit_set_checkpoints",
     "s2_dit_forward_host", "s2_shard_build", "s2_shard_counts", "s2_shard_lists", "s2_shard_free",
     "s2_dist_unique_id", "s2_dist_init", "s2_dist_sync", "s2_dist_destroy", "s2_dit_forward_sharded",
     "s2_patchify_video", "s2_unpatchify_prediction", "s2_timestep_embedding", "s2_dit_set_io_weights",
@@ -161,6 +161,7 @@ def lib() -> C.CDLL:
     L.s2_dit_init_random.argtypes = [vp, C.c_uint64]
     L.s2_count_nonfinite.argtypes = [vp, vp, i64, C.c_int, C.POINTER(C.c_int64)]
     L.s2_dit_set_check_finite.argtypes = [vp, C.c_int]
+    L.s2_dit_set_checkpoints.argtypes = [vp, vp, C.c_int, vp, vp]
     L.s2_dit_nonfinite_report.argtypes = [vp, C.POINTER(C.c_int), C.POINTER(C.c_int64), C.POINTER(C.c_int64)]
     L.s2_dit_forward.argtypes = [vp, pint, ip, vp, vp]
     L.s2_dit_forward_host.argtypes = [vp, pint, pint, ip, vp, vp, vp, vp, vp]
@@ -490,6 +491,16 @@ class Dit:
         """Count the NaN / Inf values of the video and text rows at the block stack's input and after every
         block; a forward that finds any fails with code -1 (see nonfinite_report)."""
         check(lib().s2_dit_set_check_finite(self.handle, int(bool(enable))), "s2_dit_set_check_finite")
+
+    def set_checkpoints(self, blocks, videos, texts):
+        """After block blocks[i] of every following forward, copy its video rows into videos[i] and its text
+        rows into texts[i] (contiguous fp32 CUDA tensors kept alive by this object); [] clears them."""
+        n = len(blocks)
+        bl = _ints(blocks)
+        vp_ = (C.c_void_p * max(n, 1))(*[v.data_ptr() for v in videos])
+        tp_ = (C.c_void_p * max(n, 1))(*[t.data_ptr() for t in texts])
+        check(lib().s2_dit_set_checkpoints(self.handle, bl, n, vp_, tp_), "s2_dit_set_checkpoints")
+        self._checkpoints = (list(videos), list(texts))  # the library keeps the pointers
 
     def nonfinite_report(self):
         """(block, video_count, text_count) of the last checked forward's first non-finite point: block -1 =

@@ -107,6 +107,17 @@ struct s2_dit
     bool finite_checked = false;
     int nonfinite_block = 0;
     int64_t nonfinite_video = 0, nonfinite_text = 0;
+    // block checkpoints (s2_dit_set_checkpoints): caller-owned device
+    // destinations of chosen blocks' outputs; s2_dit_forward_host sets the
+    // row offsets of the sample it runs
+    struct Checkpoint
+    {
+        int block;
+        float* video;
+        float* text;
+    };
+    std::vector<Checkpoint> checkpoints;
+    size_t cp_video_row = 0, cp_text_row = 0;
 };
 
 namespace {
@@ -470,6 +481,20 @@ int s2_dit_set_check_finite(s2_dit* d, int enable)
     return S2_OK;
 }
 
+int s2_dit_set_checkpoints(s2_dit* d, const int* blocks, int count, float* const* video, float* const* text)
+{
+    if (!d || count < 0 || (count > 0 && (!blocks || !video || !text))) return S2_ERR_INVALID;
+    std::vector<s2_dit::Checkpoint> cps;
+    for (int i = 0; i < count; i++)
+    {
+        // record_blocks' range check (seedvr2_dit.cpp:820-825)
+        if (blocks[i] < 0 || blocks[i] >= d->cfg.num_blocks || !video[i] || !text[i]) return S2_ERR_INVALID;
+        cps.push_back({blocks[i], video[i], text[i]});
+    }
+    d->checkpoints.swap(cps);
+    return S2_OK;
+}
+
 int s2_dit_nonfinite_report(const s2_dit* d, int* block, int64_t* video_count, int64_t* text_count)
 {
     if (!d || !d->finite_checked) return S2_ERR_INVALID;
@@ -640,6 +665,13 @@ int s2_dit_forward(s2_dit* d, const int* video_shape, int text_length, float* x,
                                           s2::EPI_GATE_RESIDUAL, mb + 5 * D, 1, x, nullptr)) != S2_OK)
             return r;
         if (fin && (r = count_rows_nonfinite(c, x, Nv, Nt, D, fin + 2 * (b + 1))) != S2_OK) return r;
+        for (const s2_dit::Checkpoint& cp : d->checkpoints)
+            if (cp.block == b &&
+                (cudaMemcpyAsync(cp.video + d->cp_video_row * D, x, (size_t)Nv * D * 4, cudaMemcpyDeviceToDevice,
+                                 c.stream) != cudaSuccess ||
+                 cudaMemcpyAsync(cp.text + d->cp_text_row * D, x + (size_t)Nv * D, (size_t)Nt * D * 4,
+                                 cudaMemcpyDeviceToDevice, c.stream) != cudaSuccess))
+                return S2_ERR_CUDA;
     }
     if (fin)
     {
@@ -948,7 +980,11 @@ int s2_dit_forward_host(s2_dit* d, const int* video_shapes, const int* text_leng
             if (cudaMemcpyAsync(mod + (size_t)k * D, modulation + ((size_t)k * batch + s) * D, (size_t)D * 4,
                                 cudaMemcpyHostToDevice, c.stream) != cudaSuccess)
                 return S2_ERR_CUDA;
+        // checkpoints land at this sample's rows, like its outputs
+        d->cp_video_row = v_off;
+        d->cp_text_row = t_off;
         r = s2_dit_forward(d, shp, text_lengths[s], x, mod);
+        d->cp_video_row = d->cp_text_row = 0;
         if (r != S2_OK) return r;
         if (cudaMemcpyAsync(video_out + v_off * D, x, nv * D * 4, cudaMemcpyDeviceToHost, c.stream) != cudaSuccess ||
             cudaMemcpyAsync(text_out + t_off * D, x + nv * D, nt * D * 4, cudaMemcpyDeviceToHost, c.stream) !=

@@ -120,3 +120,66 @@ def test_forward_host_matches_device(gpu_ctx, s2lib):
         voff += nv[s]
         toff += tls[s]
     dit.close()
+
+
+def test_block_checkpoints(gpu_ctx, s2lib):
+    """s2_dit_set_checkpoints: block 0's copy equals a one-block stack's output bit for bit, the last block's
+    equals the final rows, s2_dit_forward_host writes each sample at its rows, and a block outside the stack
+    is -1 (the reference's range check)."""
+    import torch
+
+    D, heads, F = 256, 2, 1024
+    rng = np.random.default_rng(21)
+    ws = [make_block_weights(rng, D, F, 128, 21) for _ in range(2)]
+
+    def stack(n):
+        dit = s2lib.Dit(gpu_ctx, num_blocks=n, hidden=D, heads=heads, head_dim=128, mlp_hidden=F, window=[1, 4, 4],
+                        window_mode=1)
+        for b in range(n):
+            dit.set_block_weights(b, ws[b])
+        return dit
+
+    # one sample on the device
+    shape, T = [2, 6, 8], 5
+    nv = int(np.prod(shape))
+    x0 = rng.standard_normal((nv + T, D)).astype(np.float32)
+    mod = rng.standard_normal((6, D)).astype(np.float32)
+    two, one = stack(2), stack(1)
+    cv = [torch.empty((nv, D), device="cuda") for _ in range(2)]
+    ct = [torch.empty((T, D), device="cuda") for _ in range(2)]
+    two.set_checkpoints([0, 1], cv, ct)
+    x = torch.from_numpy(x0).cuda()
+    two.forward(shape, T, x, torch.from_numpy(mod).cuda())
+    y = torch.from_numpy(x0).cuda()
+    one.forward(shape, T, y, torch.from_numpy(mod).cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(cv[0], y[:nv]) and torch.equal(ct[0], y[nv:])
+    assert torch.equal(cv[1], x[:nv]) and torch.equal(ct[1], x[nv:])
+
+    # two samples through the host entry point: checkpoints at the samples' rows
+    shapes, tls = [[1, 6, 8], [2, 4, 4]], [5, 3]
+    nvs = [48, 32]
+    video = rng.standard_normal((sum(nvs), D)).astype(np.float32)
+    text = rng.standard_normal((sum(tls), D)).astype(np.float32)
+    mods = rng.standard_normal((6, 2, D)).astype(np.float32)
+    cv = [torch.full((sum(nvs), D), float("nan"), device="cuda") for _ in range(2)]
+    ct = [torch.full((sum(tls), D), float("nan"), device="cuda") for _ in range(2)]
+    two.set_checkpoints([1, 0], [cv[1], cv[0]], [ct[1], ct[0]])
+    vo, to = np.zeros_like(video), np.zeros_like(text)
+    two.forward_host(shapes, tls, video, text, mods, vo, to)
+    v1, t1 = np.zeros_like(video), np.zeros_like(text)
+    one.forward_host(shapes, tls, video, text, mods, v1, t1)
+    np.testing.assert_array_equal(cv[1].cpu().numpy(), vo)
+    np.testing.assert_array_equal(ct[1].cpu().numpy(), to)
+    np.testing.assert_array_equal(cv[0].cpu().numpy(), v1)
+    np.testing.assert_array_equal(ct[0].cpu().numpy(), t1)
+
+    for bad in ([2], [-1]):
+        with pytest.raises(s2lib.S2Error) as e:
+            two.set_checkpoints(bad, cv[:1], ct[:1])
+        assert e.value.code == -1
+    two.set_checkpoints([], [], [])
+    torch.cuda.synchronize()
+    assert gpu_ctx.status() == 0
+    two.close()
+    one.close()
