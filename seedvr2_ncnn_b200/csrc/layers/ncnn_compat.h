@@ -53,6 +53,8 @@ public:
     void create(int _w, int _h, size_t es = 4u, Allocator* = 0) { shape(2, _w, _h, 1, 1, es); }
     void create(int _w, int _h, int _c, size_t es = 4u, Allocator* = 0) { shape(3, _w, _h, 1, _c, es); }
     void create(int _w, int _h, int _d, int _c, size_t es = 4u, Allocator* = 0) { shape(4, _w, _h, _d, _c, es); }
+    // the batched form of the pinned ncnn (elempack 1, n 1 here)
+    void create(int _w, int _h, int _d, int _c, size_t es, int, int, Allocator* = 0) { shape(4, _w, _h, _d, _c, es); }
     bool empty() const { return data == 0 || total() == 0; }
     size_t total() const { return cstep * c; }
     float* row(int y) { return (float*)((unsigned char*)data + (size_t)w * y * elemsize); }

@@ -267,7 +267,7 @@ int DecomposedConv3D::forward(const ncnn::Mat& bottom_blob, ncnn::Mat& top_blob,
     int whdc[4];
     if ((r = s2_conv3d_output_shape(device_layer, bottom_blob.w, bottom_blob.h, bottom_blob.d, st, whdc)) != 0)
         return r;
-    top_blob.create(whdc[0], whdc[1], whdc[2], whdc[3], 4u, opt.blob_allocator);
+    top_blob.create(whdc[0], whdc[1], whdc[2], whdc[3], 4u, 1, 1, opt.blob_allocator);
     if (top_blob.empty()) return -100;
     return run_on_device(bottom_blob, top_blob, [&](const float* in, int64_t ic, float* out, int64_t oc) {
         return s2_conv3d_forward(device_layer, in, ic, bottom_blob.w, bottom_blob.h, bottom_blob.d, bottom_blob.c, st,
@@ -294,7 +294,7 @@ int resample_forward(s2_vae_resample* layer, const ncnn::Mat& bottom_blob, ncnn:
         if (st != S2_VAE_MEMORY_ACTIVE) s2_vae_resample_reset_memory(layer);
         return r;
     }
-    top_blob.create(whdc[0], whdc[1], whdc[2], whdc[3], 4u, opt.blob_allocator);
+    top_blob.create(whdc[0], whdc[1], whdc[2], whdc[3], 4u, 1, 1, opt.blob_allocator);
     if (top_blob.empty()) return -100;
     return run_on_device(bottom_blob, top_blob, [&](const float* in, int64_t ic, float* out, int64_t oc) {
         return s2_vae_resample_forward(layer, in, ic, bottom_blob.w, bottom_blob.h, bottom_blob.d, bottom_blob.c, st,

@@ -107,3 +107,19 @@ def test_shared_linear_layer_vs_golden(layers, golden):
         assert code == 0
         for a, key in ((vo, vk), (to, tk)):
             assert cosine(a, g[key]) >= 0.9995 and rel_maxabs(a, g[key]) <= 2e-2
+
+
+@pytest.mark.parametrize("src", ["adaptive_window_attention.cpp", "shared_linear.cpp", "vae_layers.cpp"])
+def test_layer_sources_compile_against_ncnn_headers(src):
+    """With -DS2_WITH_NCNN the layer sources include ncnn's own layer.h / modelbin.h / paramdict.h; checked
+    here against the oracle shim's copies of that API (the subset the reference's layers use)."""
+    import os
+    import subprocess
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-DS2_WITH_NCNN",
+                        "-I" + os.path.join(root, "oracle", "ncnn_shim"), "-I" + os.path.join(cuda, "include"),
+                        os.path.join(root, "seedvr2_ncnn_b200", "csrc", "layers", src)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
