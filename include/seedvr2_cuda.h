@@ -148,13 +148,21 @@ int s2_awa_forward(s2_context* ctx, const s2_awa_params* params, const s2_plan* 
  * S2_ERR_TOO_LARGE.  The first call on a device resolves the array's device
  * address (cudaGetSymbolAddress) -- make it before any stream capture.  All
  * calls share the array: calls whose GPU work overlaps race (serialise
- * them on one stream).  Device-side wait timeouts are recorded in the
- * scratch status word only. */
+ * them on one stream).  The call only enqueues: a bounded device wait that
+ * runs out, or a bad table index, is recorded in the scratch's status word,
+ * which s2_awa_static_status reads back. */
 #define S2_AWA_STATIC_SCRATCH_BYTES (64u << 20)
 int s2_awa_forward_static(const s2_awa_params* params, const int* video_shapes, const int* text_lengths, int batch,
                           int in_dtype, const void* video_q, const void* video_k, const void* video_v,
                           int64_t video_ld, const void* text_q, const void* text_k, const void* text_v,
                           int64_t text_ld, int out_dtype, void* video_out, void* text_out, void* stream);
+/* Status of the last s2_awa_forward_static call on the CURRENT device:
+ * synchronises `stream` (the call's stream), then returns and clears the
+ * scratch's status word -- S2_ERR_TIMEOUT for an expired device wait,
+ * S2_ERR_INVALID for a bad index, S2_OK otherwise (also before any call).
+ * Every static call clears the word on entry, so read it before the next
+ * call.  Allocates nothing.  No counterpart in the reference. */
+int s2_awa_static_status(void* stream);
 
 /* ---------------------------------------------------------------------------
  * SharedLinear forward.  Replaces SharedLinear::forward (shared_linear.cpp:83-96,
@@ -245,9 +253,13 @@ int s2_dit_set_check_finite(s2_dit* dit, int enable);
  * SEEDVR2_DIT_DUMP_BLOCKS dumps): after block blocks[i] of every following
  * forward (one GPU), the block's video rows are copied to video[i] and its
  * text rows to text[i] (device fp32 [Nv][D] and [Nt][D] of the forward's
- * shape; s2_dit_forward_host writes sample s at its rows, as in its outputs).
- * A block outside [0, num_blocks) is -1, as the reference's range check.
- * count 0 clears them.  The pointers are kept, not copied. */
+ * shape; s2_dit_forward_host writes sample s at its rows, as in its outputs;
+ * s2_dit_forward_step at its block-stack rows -- patches, then text rows --
+ * samples one after another; the denoise loop's buffers hold its last DiT
+ * pass).  A block outside [0, num_blocks) is -1, as the reference's range
+ * check.  count 0 clears them.  The pointers are kept, not copied.
+ * s2_dit_forward_sharded returns -1 while checkpoints are set (a rank holds
+ * only its own rows). */
 int s2_dit_set_checkpoints(s2_dit* dit, const int* blocks, int count, float* const* video, float* const* text);
 int s2_dit_nonfinite_report(const s2_dit* dit, int* block, int64_t* video_count, int64_t* text_count);
 /* Device-resident forward of all blocks for ONE sample:

@@ -39,11 +39,22 @@ _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 
 
+def reference_tree() -> str | None:
+    """The reference checkout (Chisato623/seedvr2_ncnn) to build the checkers from: $S2_REFERENCE_TREE, else a
+    checkout named `reference` beside this repository's directory; None when neither holds its sources (as on
+    a GPU box, which uses the checkers built beforehand)."""
+    repo_parent = os.path.dirname(os.path.dirname(HERE))
+    for tree in (os.environ.get("S2_REFERENCE_TREE"), os.path.join(repo_parent, "reference")):
+        if tree and os.path.isdir(os.path.join(tree, "src", "seedvr2")):
+            return tree
+    return None
+
+
 def build(ref_tree: str | None = None) -> None:
     """Compile the port (always) and the reference build (when its tree exists)."""
     subprocess.run(["make", "-s", "-C", HERE, "port"], check=True)
-    tree = ref_tree or os.environ.get("S2_REFERENCE_TREE", "/root/reference")
-    if os.path.isdir(os.path.join(tree, "src", "seedvr2")):
+    tree = ref_tree or reference_tree()
+    if tree and os.path.isdir(os.path.join(tree, "src", "seedvr2")):
         subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={tree}"], check=True)
 
 

@@ -47,7 +47,7 @@ EXPORTED = [
     "s2_init", "s2_destroy", "s2_set_stream", "s2_status", "s2_error_string", "s2_version", "s2_launch_count",
     "s2_profile_enable", "s2_profile_read",
     "s2_plan_build", "s2_plan_info", "s2_plan_copy", "s2_plan_free",
-    "s2_awa_forward", "s2_awa_forward_static", "s2_shared_linear", "s2_ada_rmsnorm", "s2_convert_f32_bf16",
+    "s2_awa_forward", "s2_awa_forward_static", "s2_awa_static_status", "s2_shared_linear", "s2_ada_rmsnorm", "s2_convert_f32_bf16",
     "s2_count_nonfinite",
     "s2_dit_create", "s2_dit_free", "s2_dit_set_block_weights", "s2_dit_init_random", "s2_dit_forward",
     "s2_dit_set_check_finite", "s2_dit_nonfinite_report", "s2_dit_set_checkpoints",
@@ -151,6 +151,7 @@ def lib() -> C.CDLL:
                                  ip, vp, vp]
     L.s2_awa_forward_static.argtypes = [C.POINTER(AwaParams), pint, pint, ip, ip, vp, vp, vp, i64, vp, vp, vp, i64,
                                         ip, vp, vp, vp]
+    L.s2_awa_static_status.argtypes = [vp]
     L.s2_shared_linear.argtypes = [vp, ip, ip, ip, ip, vp, vp, vp, vp, ip, vp, ip, vp, vp]
     L.s2_ada_rmsnorm.argtypes = [vp, ip, ip, vp, C.c_float, vp, vp, vp]
     L.s2_convert_f32_bf16.argtypes = [vp, vp, vp, i64]

@@ -23,6 +23,11 @@
 // other byte a call reads is written earlier by the same call.  Calls whose
 // GPU work overlaps (different streams, or several host threads) race on the
 // array; the host-side part is serialised by a mutex.
+//
+// A bounded device wait that runs out (or a bad table index) is recorded in
+// the scratch's status word, not returned by the call, which only enqueues;
+// s2_awa_static_status reads it back (after the stream's work) and clears it.
+// Each call clears the word on entry, so read it before the next call.
 #include <math.h>
 
 #include <algorithm>
@@ -260,7 +265,11 @@ int walk(const s2_awa_params* p, const int* shapes, const int* tl, int batch, La
                 T[L.o_items + 2 * (size_t)k + 1] = q0;
             }
         }
-    // coverage check on the host table space past the tables
+    // coverage check on the host table space past the tables: the windows
+    // hold exactly the samples' t*h*w tokens, each once (plan.cpp's check)
+    long long total = 0;
+    for (int s = 0; s < batch; s++) total += (long long)shapes[3 * s] * shapes[3 * s + 1] * shapes[3 * s + 2];
+    if (total != L.n) return S2_ERR_PLAN;
     int* inv = T + L.total_ints;
     for (int i = 0; i < L.n; i++) inv[i] = -1;
     for (int i = 0; i < L.n; i++)
@@ -365,4 +374,24 @@ extern "C" int s2_awa_forward_static(const s2_awa_params* prm, const int* video_
                                     partial);
     if (r != S2_OK) return r;
     return s2::launch_text_pool(c, s, inner, partial, out_f32, prm->official_bf16_attention, text_out);
+}
+
+extern "C" int s2_awa_static_status(void* stream)
+{
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return S2_ERR_CUDA;
+    if (device < 0 || device >= kMaxDevices) return S2_ERR_DEVICE;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    // no call has run on this device yet: nothing can have been recorded
+    if (!g_scratch_ptr[device]) return S2_OK;
+    int* status = static_cast<int*>(g_scratch_ptr[device]);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int h = 0;
+    if (cudaMemcpyAsync(&h, status, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return S2_ERR_CUDA;
+    if (h != 0 && (cudaMemsetAsync(status, 0, sizeof(int), st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess))
+        return S2_ERR_CUDA;
+    if (h == s2::kStatusTimeout) return S2_ERR_TIMEOUT;
+    return h != 0 ? S2_ERR_INVALID : S2_OK;
 }

@@ -702,6 +702,8 @@ int s2_dit_forward(s2_dit* d, const int* video_shape, int text_length, float* x,
 int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, float* x, const float* modulation)
 {
     if (!d || !video_shape || text_length <= 0 || !x || !modulation) return S2_ERR_INVALID;
+    // block checkpoints are a one-GPU feature: a rank holds only its own rows
+    if (!d->checkpoints.empty()) return S2_ERR_INVALID;
     s2::Context& c = d->ctx->c;
     s2::Dist* dist = d->ctx->dist.get();
     const int rank = dist ? dist->rank : 0, world = dist ? dist->world : 1;
@@ -1150,16 +1152,22 @@ int s2_dit_forward_step(s2_dit* d, const int* video_shapes, const int* text_leng
     if ((r = step_workspace(d, np_max, nt_max, batch, 0, w)) != S2_OK) return r;
     // timestep MLP of every sample at once; per sample [6][D]
     if ((r = run_emb(d, timesteps, batch, w.temb, w.e0, w.e1, w.emb, false)) != S2_OK) return r;
-    int64_t v_off = 0, t_off = 0;
+    int64_t v_off = 0, t_off = 0, p_off = 0;
     for (int s = 0; s < batch && r == S2_OK; s++)
     {
         const int* shp = video_shapes + 3 * s;
         const PatchSrc src = {video + v_off * s2::kLatentChannels, nullptr, 0, nullptr, 0};
+        // block checkpoints land at this sample's block-stack rows (patches,
+        // then text rows), samples one after another
+        d->cp_video_row = (size_t)p_off;
+        d->cp_text_row = (size_t)t_off;
         r = run_sample(d, shp, src, text + t_off * s2::kTextChannels, text_lengths[s], w.emb + (size_t)s * 6 * D,
                        prediction + v_off * s2::kPredChannels, text_out + t_off * D, w);
         v_off += (int64_t)shp[0] * shp[1] * shp[2];
+        p_off += (int64_t)shp[0] * (shp[1] / 2) * (shp[2] / 2);
         t_off += text_lengths[s];
     }
+    d->cp_video_row = d->cp_text_row = 0;
     return r;
 }
 

@@ -279,8 +279,11 @@ def gen_vae_conv() -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-tree", default=os.environ.get("S2_REFERENCE_TREE", "/root/reference"))
+    ap.add_argument("--reference-tree", default=oracle.reference_tree(),
+                    help="reference checkout (default: $S2_REFERENCE_TREE or ../reference beside the repository)")
     args = ap.parse_args()
+    if not args.reference_tree:
+        ap.error("the reference checkout was not found: pass --reference-tree or set S2_REFERENCE_TREE")
     oracle.build(args.reference_tree)
     ref = oracle.Ref()
     gen_plans(ref)

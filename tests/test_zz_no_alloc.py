@@ -21,6 +21,8 @@ from tests.conftest import cosine, rel_maxabs
 
 pytestmark = pytest.mark.gpu
 
+S2_STATIC_BYTES = 64 << 20  # S2_AWA_STATIC_SCRATCH_BYTES
+
 
 def _case(rng, heads, shape, T):
     inner = heads * 128
@@ -84,6 +86,8 @@ def test_static_scratch_entry_matches_allocating_entry():
         free_before = torch.cuda.mem_get_info()[0]
         r = _static_call(abi, prm, cs["shapes"], cs["tls"], vq, tq, inner, cs["out"], vo, to, stream)
         assert r == abi.S2_OK, abi.error_string(r)
+        # the call only enqueues: device-side failures are read back here
+        assert abi.lib().s2_awa_static_status(stream) == abi.S2_OK
         torch.cuda.synchronize()
         if call > 0:
             # the first call may load the library's module (and with it the
@@ -104,4 +108,60 @@ def test_static_scratch_entry_matches_allocating_entry():
         big.data_ptr(), big.data_ptr(), 3 * 2560, big.data_ptr(), big.data_ptr(), big.data_ptr(), 3 * 2560,
         abi.S2_DTYPE_F32, big.data_ptr(), big.data_ptr(), stream)
     assert r == abi.S2_ERR_TOO_LARGE
+    ctx.close()
+
+
+def test_static_planner_matches_allocating_planner(golden):
+    """The static entry point builds its window plan with its own heap-free walk.  On every golden plan
+    shape that fits the fixed scratch (the reference's target-count windows, shifted and unshifted, ragged
+    and 2-sample cases), its outputs must equal the allocating entry point's bit for bit: both run the
+    same kernels, so any difference in a window, a token's position or its RoPE coordinates would show."""
+    import torch
+
+    from seedvr2_ncnn_b200 import abi
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.cuda.set_device(0)
+    ctx = abi.Context(0)
+    stream = torch.cuda.current_stream().cuda_stream
+    g = golden["plans"]
+    rng = np.random.default_rng(5)
+    heads, inner, T = 1, 128, 7
+    freqs = torch.from_numpy((1.0 / 10000 ** (np.arange(21) * 2 / 42)).astype(np.float32)).cuda()
+    norms = torch.from_numpy((1 + 0.02 * rng.standard_normal((4, 128))).astype(np.float32)).cuda()
+    checked = 0
+    for case in sorted({k.split("__")[0] for k in g.files}):
+        shapes = g[f"{case}__shapes"].tolist()
+        target = g[f"{case}__target"].tolist()
+        shifted = int(case.endswith("_s1"))
+        nv = sum(int(np.prod(s)) for s in shapes)
+        nw = int(g[f"{case}__windows"].shape[0])
+        if (nv + nw * T) * inner * 2 * 3 + nw * T * inner * 4 > (S2_STATIC_BYTES * 3) // 4:
+            continue
+        tls = [T] * len(shapes)
+        vq = torch.from_numpy(rng.standard_normal((nv, 3 * inner)).astype(np.float32)).cuda().to(torch.bfloat16)
+        tq = torch.from_numpy(rng.standard_normal((T * len(shapes), 3 * inner)).astype(np.float32)).cuda().to(
+            torch.bfloat16)
+        ref_v, ref_t = abi.awa_forward(ctx, heads=heads, head_dim=128, window=target,
+                                       window_mode=abi.S2_WINDOW_TARGET, shifted=shifted, eps=1e-5, rope_pairs=21,
+                                       norms=norms, freqs=freqs, shapes=shapes, text_lengths=tls, video_qkv=vq,
+                                       text_qkv=tq, out_dtype=abi.S2_DTYPE_F32)
+        prm = abi.AwaParams()
+        prm.heads, prm.head_dim = heads, 128
+        prm.window[:] = target
+        prm.window_mode, prm.shifted, prm.epsilon, prm.rope_pairs = abi.S2_WINDOW_TARGET, shifted, 1e-5, 21
+        prm.official_bf16_attention = 0
+        prm.norm_weights, prm.rope_freqs = norms.data_ptr(), freqs.data_ptr()
+        vo = torch.full_like(ref_v, float("nan"))
+        to = torch.full_like(ref_t, float("nan"))
+        torch.cuda.synchronize()
+        r = _static_call(abi, prm, shapes, tls, vq, tq, inner, abi.S2_DTYPE_F32, vo, to, stream)
+        assert r == abi.S2_OK, (case, abi.error_string(r))
+        assert abi.lib().s2_awa_static_status(stream) == abi.S2_OK, case
+        assert torch.equal(vo, ref_v), case
+        assert torch.equal(to, ref_t), case
+        checked += 1
+    assert checked >= 8
+    assert ctx.status() == 0
     ctx.close()
