@@ -4,30 +4,54 @@
 // AdaptiveWindowAttention::forward (adaptive_window_attention.cpp:873-975 CPU,
 // :1172-1268 Vulkan, scatter shader :353-409).  Each window's sequence is its
 // L video rows followed by the sample's T text rows, packed contiguously
-// (window after window) in bf16 [rows][heads*128] by the prepare kernel.
+// (window after window) in bf16 [rows][heads*128]; every row attends to the
+// whole sequence (no mask), softmax(Q K^T / sqrt(128)) V.
 //
-// Work unit = (window, pair of 128-row query tiles A and B, head); a
+// Work unit = (pair of 128-row query tiles 0 and 1 of one window, head); a
 // persistent grid of one CTA per SM walks the units.  K/V tiles are loaded
-// once for both query tiles.  Warp roles:
-//   warp 0     TMA: Q_A and Q_B per unit, K tiles into a 3-stage ring and V
-//              tiles into a 2-stage ring (a K stage is released after its
-//              last S MMA, a V stage after its last PV MMA);
-//   warp 1     one thread issues every tcgen05.mma, ping-ponging the tiles:
-//                S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...
-//              so the tensor core works on one tile while the other tile's
-//              softmax runs;
-//   warps 2-5  softmax of tile A, warps 6-9 softmax of tile B: one query row
-//              per thread (TMEM lane).  S is read from TMEM, P = exp2(S*c - m)
-//              is written back over S as packed bf16 and fed to the PV MMA as
-//              its TMEM A operand; O accumulates in TMEM across key tiles.
-//              The running max is only raised (and O, l rescaled in place)
-//              when it grows by more than 2^8, so most tiles skip the
-//              rescale.  S_X(j) is committed after PV_X(j-1), so O is stable
-//              whenever the softmax may rescale it.
+// once for both query tiles.  384 threads, three warpgroups:
+//   warps 0-3   softmax + epilogue of query tile 0   (200 registers each)
+//   warps 4-7   softmax + epilogue of query tile 1   (200 registers each)
+//   warp 8      TMA: Q pair per unit, K tiles into a 3-slot ring
+//   warp 9      MMA: one thread issues every tcgen05.mma
+//   warp 10     TMA: V tiles into a 2-slot ring
+//   warp 11     idle (the warpgroup gives its registers to the softmax)
+// `setmaxnreg` moves registers from the TMA / MMA warpgroup (104 each) to the
+// two softmax warpgroups (200 each), so a thread holds its whole 128-column
+// score row in registers.
+//
+// Tensor memory (512 columns): S_0 [0,128) S_1 [128,256) O_0 [256,384)
+// O_1 [384,512).  A softmax thread owns one query row (one TMEM lane): it
+// loads the row of S_x(j) into registers, forms P = exp2(S*c - m) and stores
+// P as packed bf16 back into the first 64 columns of S_x; the PV MMA reads P
+// from tensor memory (A operand) and V from shared memory, so the tensor
+// core reads only Q, K and V from shared memory.  The MMA thread issues, per
+// key tile j,
+//     PV_0(j)  S_0(j+1)  PV_1(j)  S_1(j+1)
+// so S_x(j+1) overwrites P_x(j) only after PV_x(j) has read it (tcgen05 MMAs
+// of one thread run in issue order), and while the softmax of tile 0 runs
+// the tensor core works on tile 1 and the other way round.  The s_full_x
+// commit after S_x(j+1) also covers PV_x(j), so when the softmax sees S_x(j)
+// the accumulator O_x is stable and it may rescale it in place: the running
+// max is raised (and O, l rescaled) only when it grows by more than 2^8.
+//
+// Exponentials: a fixed share of each row's column pairs is exponentiated on
+// the FMA pipe (2^t = 2^n * 2^f, n = round(t), f in [-1/2, 1/2], a cubic for
+// 2^f) and the rest on the MUFU (ex2.approx): with head_dim 128 a 128 x 128
+// tile's 16,384 exponentials alone would take the MUFU as long as the tile's
+// two MMAs take the tensor core.
+//
 // Epilogue: O / l -- video rows stored straight to their source token (the
-// scatter), text rows to a per-window fp32 partial that text_pool averages
-// over the sample's windows.  Keys past the window's sequence are masked;
-// query rows past it are computed but never stored.
+// scatter; peer GPUs' rows over NVLink), text rows to a per-window fp32
+// partial that text_pool averages over the sample's windows.  Keys past the
+// window's sequence are masked; query rows past it are computed but never
+// stored.  The ragged last key tile loads, exponentiates and stores only its
+// 32-column chunks that hold keys, and its MMAs run with N (S) or K (PV)
+// rounded up to 16.
+//
+// Every mbarrier wait is bounded: on expiry the kernel records a timeout in
+// the status word, drains its own TMA / MMA work (bounded), frees TMEM and
+// returns.
 #include "s2_common.cuh"
 #include "s2_internal.h"
 
@@ -39,19 +63,31 @@ constexpr int HD = 128;                      // head_dim
 constexpr int TILE = 128;                    // q rows / keys per tile
 constexpr int CHUNK_BYTES = TILE * 128;      // 128 rows x 64 bf16 (one swizzle row each)
 constexpr int TILE_BYTES = 2 * CHUNK_BYTES;  // 128 x 128 bf16
-constexpr int NUM_THREADS = 320;             // TMA, MMA, 2 x 4 softmax warps
-constexpr int TMEM_COLS = 512;               // S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512)
-constexpr uint32_t IDESC_O = umma_idesc_bf16(128, 128, 0, 1); // A (= P) K-major, B (= V) MN-major
-constexpr int K_STAGES = 2;
-// Q_A, Q_B | K ring (2) | V (1) | P_A, P_B  = 7 x 32 KB
-constexpr int SMEM_BYTES = (2 + K_STAGES + 1 + 2) * TILE_BYTES + 1024 + 256;
-constexpr float RESCALE_THRESHOLD = 8.0f;                     // log2 units
+constexpr int NUM_THREADS = 384;
+constexpr int TMEM_COLS = 512;               // S_0 S_1 O_0 O_1
+constexpr uint32_t IDESC_O = umma_idesc_bf16(128, 128, 0, 1); // A (= P, tensor memory) K-major, B (= V) MN-major
+constexpr int K_STAGES = 3;
+constexpr int V_STAGES = 2;
+// Q_0, Q_1 | K ring | V ring
+constexpr int SMEM_BYTES = (2 + K_STAGES + V_STAGES) * TILE_BYTES + 1024 + 256;
+constexpr float RESCALE_THRESHOLD = 8.0f; // log2 units
+// Register split (setmaxnreg): the kernel is launched with LAUNCH_REGS per
+// thread; the TMA / MMA warpgroup drops to SUPPORT_REGS and the two softmax
+// warpgroups rise to SOFTMAX_REGS.  The shares must add up to the launch's
+// total exactly (an increase that the freed registers cannot cover waits
+// forever), and the launcher checks the compiled register count first.
+constexpr int LAUNCH_REGS = 168;
+constexpr int SUPPORT_REGS = 104;
+constexpr int SOFTMAX_REGS = 200;
+static_assert(2 * 128 * SOFTMAX_REGS + 128 * SUPPORT_REGS == NUM_THREADS * LAUNCH_REGS, "register split");
+// Column pairs of each 32-column chunk (16 pairs) exponentiated on the FMA pipe.
+constexpr int POLY_PAIRS = 4;
 
 struct AttnArgs
 {
     const int4* win_info; // {seq_offset, L, T, partition_offset}
     const int* win_pool;  // partial row of the window's first text row
-    const int2* items;    // {window, q0 of tile A}
+    const int2* items;    // {window, q0 of tile 0}
     const int* video_indices;
     int inner;
     float scale_log2;
@@ -66,6 +102,18 @@ struct AttnArgs
     // peer field is stored into peer_out[peer - 1] over NVLink
     void* peer_out[kMaxPeers];
 };
+
+template <int N>
+__device__ __forceinline__ void regs_increase()
+{
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+template <int N>
+__device__ __forceinline__ void regs_decrease()
+{
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
 
 __device__ __forceinline__ float ex2(float x)
 {
@@ -111,71 +159,113 @@ __device__ __forceinline__ float fmax3(float a, float b, float c)
     return d;
 }
 
-// Row max over NV raw scores (FULL: no masked columns; otherwise columns
-// >= valid are ignored); four independent 3-input max chains.
-template <bool FULL, int NV>
-__device__ __forceinline__ float row_max(const uint32_t (&v)[NV], int valid)
+__device__ __forceinline__ uint64_t f2(float v)
 {
-    float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    return pk2(__float_as_uint(v), __float_as_uint(v));
+}
+
+// 2^t for a pair on the FMA pipe.  Range reduction (Cody-Waite with one
+// constant, exact here): n = round(t) by adding and subtracting 1.5 * 2^23
+// (the sum's low mantissa bits then hold n in two's complement), f = t - n in
+// [-1/2, 1/2]; 2^f by a cubic fitted for this kernel (Remez exchange,
+// minimax relative error on [-1/2, 1/2], 7.5e-5 -- far below the 2^-9 of the
+// bf16 P it feeds); 2^n by adding n to the result's exponent field.  t is
+// clamped to -126 so the exponent never leaves the normal range (2^-126 is
+// zero for every practical purpose in a softmax).
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t t2)
+{
+    constexpr float kRound = 12582912.0f; // 1.5 * 2^23
+    constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261113f, c3 = 0.05517167f;
+    float a, b;
+    upk2(t2, a, b);
+    t2 = pk2(__float_as_uint(fmaxf(a, -126.f)), __float_as_uint(fmaxf(b, -126.f)));
+    const uint64_t y = fadd2(t2, f2(kRound));
+    const uint64_t n = fadd2(y, f2(-kRound));
+    const uint64_t f = ffma2(n, f2(-1.f), t2);
+    uint64_t p = ffma2(f, f2(c3), f2(c2));
+    p = ffma2(p, f, f2(c1));
+    p = ffma2(p, f, f2(c0));
+    uint32_t ylo, yhi, plo, phi;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(ylo), "=r"(yhi) : "l"(y));
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(plo), "=r"(phi) : "l"(p));
+    return pk2(plo + (ylo << 23), phi + (yhi << 23));
+}
+
+// 32 lanes x 32 consecutive 32-bit columns -> r[B, B + 32) of the row's
+// register array (compile-time indices keep it in registers).
+template <int B, int N>
+__device__ __forceinline__ void tmem_ld32_at(uint32_t taddr, uint32_t (&r)[N])
+{
+    static_assert(B + 32 <= N, "register window");
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                 "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                 : "=r"(r[B + 0]), "=r"(r[B + 1]), "=r"(r[B + 2]), "=r"(r[B + 3]), "=r"(r[B + 4]), "=r"(r[B + 5]),
+                   "=r"(r[B + 6]), "=r"(r[B + 7]), "=r"(r[B + 8]), "=r"(r[B + 9]), "=r"(r[B + 10]), "=r"(r[B + 11]),
+                   "=r"(r[B + 12]), "=r"(r[B + 13]), "=r"(r[B + 14]), "=r"(r[B + 15]), "=r"(r[B + 16]),
+                   "=r"(r[B + 17]), "=r"(r[B + 18]), "=r"(r[B + 19]), "=r"(r[B + 20]), "=r"(r[B + 21]),
+                   "=r"(r[B + 22]), "=r"(r[B + 23]), "=r"(r[B + 24]), "=r"(r[B + 25]), "=r"(r[B + 26]),
+                   "=r"(r[B + 27]), "=r"(r[B + 28]), "=r"(r[B + 29]), "=r"(r[B + 30]), "=r"(r[B + 31])
+                 : "r"(taddr));
+}
+
+// Max over chunk C (32 columns) of the row into four independent chains;
+// with MASKED, only the chunk's first `rem` columns count.
+template <int C, bool MASKED>
+__device__ __forceinline__ void chunk_max(const uint32_t (&v)[128], int rem, float (&m)[4])
+{
 #pragma unroll
-    for (int i = 0; i < NV; i += 8)
+    for (int i = 0; i < 32; i += 8)
     {
 #pragma unroll
         for (int c = 0; c < 4; c++)
         {
-            float a = __uint_as_float(v[i + 2 * c]), b = __uint_as_float(v[i + 2 * c + 1]);
-            if (!FULL)
+            const int k = i + 2 * c;
+            float a = __uint_as_float(v[C * 32 + k]), b = __uint_as_float(v[C * 32 + k + 1]);
+            if (MASKED)
             {
-                a = i + 2 * c < valid ? a : -INFINITY;
-                b = i + 2 * c + 1 < valid ? b : -INFINITY;
+                a = k < rem ? a : -INFINITY;
+                b = k + 1 < rem ? b : -INFINITY;
             }
             m[c] = fmax3(m[c], a, b);
         }
     }
-    return fmax3(m[0], m[1], fmaxf(m[2], m[3]));
 }
 
-// P = exp2(S * c - m) for 64 columns of the row (columns >= valid -> 0) as
-// 32 packed bf16 pairs.  The exponent t = S * c - m is formed in fp32
-// (packed pairs) and exponentiated in fp32 (ex2.approx.ftz.f32); the row sum
-// adds those fp32 values (packed partial sums in sum2) and P is rounded to
-// bf16 for the PV MMA.  Against exponentiating bf16 pairs in one MUFU
-// operation, this issues fewer instructions per pair (no unpacking for the
-// sum) for one more MUFU operation: measured 4.5-6.4 % faster per launch.
-template <bool FULL>
-__device__ __forceinline__ void row_exp64(const uint32_t (&v)[64], int valid, uint64_t c2, uint64_t negm2,
-                                          uint32_t (&p)[32], uint64_t (&sum2)[4])
+// P for chunk C of the row: t = S * c - m in packed pairs, the first
+// POLY_PAIRS pairs exponentiated on the FMA pipe, the rest on the MUFU; with
+// MASKED, columns >= rem of the chunk give 0.  Sums the fp32 values into
+// sum2 and stores the chunk's 16 packed bf16 pairs into tensor memory at
+// p_addr (over the chunk's half-width slot of S).
+template <int C, bool MASKED>
+__device__ __forceinline__ void chunk_exp(const uint32_t (&v)[128], int rem, uint64_t c2, uint64_t negm2,
+                                          uint64_t (&sum2)[4], uint32_t p_addr)
 {
+    uint32_t p[16];
 #pragma unroll
-    for (int q = 0; q < 32; q++)
+    for (int q = 0; q < 16; q++)
     {
-        const int i = 2 * q;
-        const uint64_t t2 = ffma2(pk2(v[i], v[i + 1]), c2, negm2);
-        float t0, t1;
-        upk2(t2, t0, t1);
-        if (!FULL)
+        const int k = 2 * q;
+        const uint64_t t2 = ffma2(pk2(v[C * 32 + k], v[C * 32 + k + 1]), c2, negm2);
+        float e0, e1;
+        if (q < POLY_PAIRS)
+            upk2(exp2_poly2(t2), e0, e1);
+        else
         {
-            t0 = i < valid ? t0 : -INFINITY;
-            t1 = i + 1 < valid ? t1 : -INFINITY;
+            float t0, t1;
+            upk2(t2, t0, t1);
+            e0 = ex2(t0);
+            e1 = ex2(t1);
         }
-        const float e0 = ex2(t0), e1 = ex2(t1);
+        if (MASKED)
+        {
+            e0 = k < rem ? e0 : 0.f;
+            e1 = k + 1 < rem ? e1 : 0.f;
+        }
         p[q] = pack_bf16x2(e0, e1);
         sum2[q & 3] = fadd2(sum2[q & 3], pk2(__float_as_uint(e0), __float_as_uint(e1)));
     }
-}
-
-// Half H (64 columns = one 128-byte chunk) of row `row` of a 128 x 128 bf16
-// tile in the 128-byte-swizzled K-major layout TMA gives Q and K (chunks of
-// 128 rows x 128 bytes; 16-byte unit u of row r at unit u ^ (r & 7)), so the
-// PV MMA reads P like Q.
-template <int H>
-__device__ __forceinline__ void store_p_half(uint8_t* tile, int row, const uint32_t (&p)[32])
-{
-    uint8_t* r0 = tile + H * CHUNK_BYTES + row * 128;
-    const int sw = row & 7;
-#pragma unroll
-    for (int u = 0; u < 8; u++)
-        *reinterpret_cast<uint4*>(r0 + ((u ^ sw) << 4)) = make_uint4(p[4 * u], p[4 * u + 1], p[4 * u + 2], p[4 * u + 3]);
+    tmem_st16(p_addr + C * 16, p);
 }
 
 __device__ __forceinline__ float bf16_round_f32(float x)
@@ -276,41 +366,108 @@ __device__ __forceinline__ Work decode_work(const AttnArgs& a, int w)
     return r;
 }
 
+// Softmax of one key tile for one query row: S_x(j) -> registers, running
+// max, P into the first 64 columns of S_x, the row sum into l; when the max
+// grows past the threshold, O_x is rescaled in place after P is stored (the
+// row's registers are free by then; O_x is stable: PV_x(j-1) completed
+// before S_x(j) was signalled, and PV_x(j) waits for this tile's p_full).
+// FULL: all 128 keys valid; otherwise `valid` (1..127) keys: chunks wholly
+// past them are skipped and only the partial chunk is masked.
+template <bool FULL>
+__device__ __forceinline__ void softmax_tile(uint32_t s_addr, uint32_t o_addr, int valid, bool first,
+                                             float scale_log2, float& m_used, float& l)
+{
+    const int nfull = FULL ? 4 : valid >> 5;      // chunks with every key valid
+    const int rem = FULL ? 0 : valid & 31;        // keys of the partial chunk (0: none)
+    // all four chunks are loaded (a conditional load leaves part of the row
+    // maybe-undefined, which costs the register allocator dearly); columns
+    // past the keys hold stale values that the max and exponentials skip
+    uint32_t v[128];
+    tmem_ld32_at<0>(s_addr, v);
+    tmem_ld32_at<32>(s_addr + 32, v);
+    tmem_ld32_at<64>(s_addr + 64, v);
+    tmem_ld32_at<96>(s_addr + 96, v);
+    tmem_ld_wait();
+    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#define S2_CHUNK_MAX(C)                                                                                        \
+    if (FULL || nfull > C)                                                                                     \
+        chunk_max<C, false>(v, 32, m4);                                                                        \
+    else if (nfull == C && rem)                                                                                \
+        chunk_max<C, true>(v, rem, m4);
+    S2_CHUNK_MAX(0)
+    S2_CHUNK_MAX(1)
+    S2_CHUNK_MAX(2)
+    S2_CHUNK_MAX(3)
+#undef S2_CHUNK_MAX
+    const float mt = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * scale_log2;
+    float alpha = 1.f;
+    bool rescale = false;
+    if (first)
+        m_used = mt;
+    else if (mt > m_used + RESCALE_THRESHOLD)
+    {
+        alpha = ex2(m_used - mt);
+        m_used = mt;
+        rescale = true;
+    }
+    const uint64_t c2 = f2(scale_log2);
+    const uint64_t negm2 = f2(-m_used);
+    uint64_t sum2[4] = {0, 0, 0, 0};
+#define S2_CHUNK_EXP(C)                                                                                        \
+    if (FULL || nfull > C)                                                                                     \
+        chunk_exp<C, false>(v, 32, c2, negm2, sum2, s_addr);                                                   \
+    else if (nfull == C && rem)                                                                                \
+        chunk_exp<C, true>(v, rem, c2, negm2, sum2, s_addr);
+    S2_CHUNK_EXP(0)
+    S2_CHUNK_EXP(1)
+    S2_CHUNK_EXP(2)
+    S2_CHUNK_EXP(3)
+#undef S2_CHUNK_EXP
+    const uint64_t s2 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
+    float lo, hi;
+    upk2(s2, lo, hi);
+    if (rescale)
+    {
+#pragma unroll 1
+        for (int c = 0; c < 4; c++)
+        {
+            uint32_t o[32];
+            tmem_ld32(o_addr + c * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(o_addr + c * 32, o);
+        }
+        l *= alpha;
+    }
+    l += lo + hi;
+}
+
 // Persistent: CTA b processes units b, b + gridDim.x, ...  Barrier phases run
 // on across units, so the next unit's loads and first S MMAs overlap the
-// current unit's last tiles and epilogue; Q is reloaded once the unit's last
-// S MMA has read it (q_empty).
-//
-// P lives in shared memory, not over S in TMEM: as soon as a softmax warp
-// group has read S_x(j) into registers (s_free) the MMA thread issues
-// S_x(j+1) into the same TMEM columns, so the tensor core computes the next
-// scores while the exponentials of this tile run; PV_x(j) (shared-memory A =
-// P_x, B = V) follows once P_x(j) is stored (p_full).  A softmax group waits
-// for PV_x(j-1) (p_empty) before overwriting P_x or rescaling O_x.
+// current unit's last tiles and epilogue; the Q pair is reloaded once the
+// unit's last S MMA has read it (q_empty).
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     window_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                             const __grid_constant__ CUtensorMap tv, const AttnArgs args)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem;                       // Q_A, Q_B
+    uint8_t* sQ = smem;                       // Q_0, Q_1
     uint8_t* sK = sQ + 2 * TILE_BYTES;        // K ring
-    uint8_t* sV = sK + K_STAGES * TILE_BYTES; // V
-    uint8_t* sP = sV + TILE_BYTES;            // P_A, P_B
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * TILE_BYTES);
+    uint8_t* sV = sK + K_STAGES * TILE_BYTES; // V ring
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + V_STAGES * TILE_BYTES);
     uint64_t* q_full = bars + 0;
     uint64_t* q_empty = bars + 1;
-    uint64_t* k_full = bars + 2;  // [K_STAGES]
-    uint64_t* k_empty = bars + 4; // [K_STAGES]
-    uint64_t* v_full = bars + 6;
-    uint64_t* v_empty = bars + 7;
-    uint64_t* s_full = bars + 8;   // [2] per query tile: S_x computed
-    uint64_t* s_free = bars + 10;  // [2] S_x read by the softmax warps (4 arrivals)
-    uint64_t* p_full = bars + 12;  // [2] P_x stored (4 arrivals)
-    uint64_t* p_empty = bars + 14; // [2] PV_x done (P_x and O_x free)
-    uint64_t* o_done = bars + 16;  // [2] last PV_x of the unit done
-    uint64_t* drain = bars + 18;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+    uint64_t* k_full = bars + 2;                  // [K_STAGES]
+    uint64_t* k_empty = k_full + K_STAGES;        // [K_STAGES]
+    uint64_t* v_full = k_empty + K_STAGES;        // [V_STAGES]
+    uint64_t* v_empty = v_full + V_STAGES;        // [V_STAGES]
+    uint64_t* s_full = v_empty + V_STAGES;        // [2] S_x computed (and PV_x before it done)
+    uint64_t* p_full = s_full + 2;                // [2] P_x stored (4 warp arrivals)
+    uint64_t* o_done = p_full + 2;                // [2] last PV_x of the unit done
+    uint64_t* drain = o_done + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -325,42 +482,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(&k_full[s], 1);
             mbar_init(&k_empty[s], 1);
         }
-        mbar_init(v_full, 1);
-        mbar_init(v_empty, 1);
+        for (int s = 0; s < V_STAGES; s++)
+        {
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
+        }
         for (int s = 0; s < 2; s++)
         {
             mbar_init(&s_full[s], 1);
-            mbar_init(&s_free[s], 4);
             mbar_init(&p_full[s], 4);
-            mbar_init(&p_empty[s], 1);
             mbar_init(&o_done[s], 1);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbarrier_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+    if (warp == 9) tmem_alloc(tmem_slot, TMEM_COLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0)
+    if (warp >= 8)
     {
-        if (lane == 0)
+        regs_decrease<SUPPORT_REGS>();
+        if (warp == 8 && lane == 0)
         {
-            // ---------------- TMA producer: Q pair per unit, K tiles into the ring
+            // ---------------- TMA: Q pair per unit, K tiles into the ring
             int g = 0; // K tiles issued so far
             int it = 0;
             bool q_out = false;
             uint32_t q_par = 0;
-            int k_issued[K_STAGES] = {0, 0};
-            uint32_t k_par[K_STAGES] = {0, 0};
+            int k_issued[K_STAGES] = {};
+            uint32_t k_par[K_STAGES] = {};
             for (int w = blockIdx.x; w < args.num_work && !*abort_flag; w += gridDim.x, it++)
             {
                 const Work wk = decode_work(args, w);
                 const int x0 = wk.head * HD;
-                if (it > 0 && !mbar_wait(q_empty, (it - 1) & 1, abort_flag, args.status)) break;
+                if (it > 0 && !mbar_wait<true>(q_empty, (it - 1) & 1, abort_flag, args.status)) break;
                 mbar_arrive_expect_tx(q_full, wk.has_b ? 2 * TILE_BYTES : TILE_BYTES);
                 tma_load_2d(sQ, &tq, q_full, x0, wk.seq_off + wk.q0);
                 tma_load_2d(sQ + CHUNK_BYTES, &tq, q_full, x0 + 64, wk.seq_off + wk.q0);
@@ -388,7 +547,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 {
                     const int ks = g % K_STAGES;
                     const uint32_t kp = (uint32_t)(g / K_STAGES) & 1u;
-                    if (!mbar_wait(&k_empty[ks], kp ^ 1, abort_flag, args.status))
+                    if (!mbar_wait<true>(&k_empty[ks], kp ^ 1, abort_flag, args.status))
                     {
                         ok = false;
                         break;
@@ -410,13 +569,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     if (k_issued[s]) drain_wait(&k_full[s], k_par[s]);
             }
         }
-        else if (lane == 1)
+        else if (warp == 10 && lane == 0)
         {
-            // ---------------- TMA producer: V tiles (one buffer; V(j) is needed
-            // only after the softmax of key tile j, so it reloads behind PV(j-1))
+            // ---------------- TMA: V tiles into the ring
             int g = 0;
-            bool issued = false;
-            uint32_t last = 0;
+            int v_issued[V_STAGES] = {};
+            uint32_t v_par[V_STAGES] = {};
             for (int w = blockIdx.x; w < args.num_work && !*abort_flag; w += gridDim.x)
             {
                 const Work wk = decode_work(args, w);
@@ -424,47 +582,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 bool ok = true;
                 for (int j = 0; j < wk.nkv; j++, g++)
                 {
-                    const uint32_t vp = (uint32_t)g & 1u;
-                    if (!mbar_wait(v_empty, vp ^ 1, abort_flag, args.status))
+                    const int vs = g % V_STAGES;
+                    const uint32_t vp = (uint32_t)(g / V_STAGES) & 1u;
+                    if (!mbar_wait<true>(&v_empty[vs], vp ^ 1, abort_flag, args.status))
                     {
                         ok = false;
                         break;
                     }
                     const int y = wk.seq_off + j * TILE;
-                    mbar_arrive_expect_tx(v_full, TILE_BYTES);
-                    tma_load_2d(sV, &tv, v_full, x0, y);
-                    tma_load_2d(sV + CHUNK_BYTES, &tv, v_full, x0 + 64, y);
-                    issued = true;
-                    last = vp;
+                    mbar_arrive_expect_tx(&v_full[vs], TILE_BYTES);
+                    tma_load_2d(sV + vs * TILE_BYTES, &tv, &v_full[vs], x0, y);
+                    tma_load_2d(sV + vs * TILE_BYTES + CHUNK_BYTES, &tv, &v_full[vs], x0 + 64, y);
+                    v_issued[vs] = 1;
+                    v_par[vs] = vp;
                 }
                 if (!ok) break;
             }
-            if (*abort_flag && issued) drain_wait(v_full, last);
+            if (*abort_flag)
+                for (int s = 0; s < V_STAGES; s++)
+                    if (v_issued[s]) drain_wait(&v_full[s], v_par[s]);
         }
-    }
-    else if (warp == 1)
-    {
-        if (lane == 0)
+        else if (warp == 9 && lane == 0)
         {
             // ---------------- MMA issuer
             bool any = false;
             bool ok = true;
             int gk = 0, gv = 0, it = 0;
-            uint32_t sfree[2] = {0, 0}, pfull[2] = {0, 0};
-            bool s_issued[2] = {false, false};
-            // shared-memory matrix descriptors; buffers are one tile (kTileDesc) apart
+            uint32_t pfull[2] = {0, 0};
+            // shared-memory matrix descriptors; ring slots are one tile (kTileDesc) apart
             const uint64_t q_desc0 = umma_desc_sw128(smem_u32(sQ), 16, 1024);
             const uint64_t k_desc0 = umma_desc_sw128(smem_u32(sK), 16, 1024);
             const uint64_t v_desc0 = umma_desc_sw128(smem_u32(sV), CHUNK_BYTES, 1024);
-            const uint64_t p_desc0 = umma_desc_sw128(smem_u32(sP), 16, 1024);
             constexpr uint32_t kTileDesc = TILE_BYTES >> 4;
             for (int w = blockIdx.x; w < args.num_work && ok; w += gridDim.x, it++)
             {
                 const Work wk = decode_work(args, w);
                 const int ntiles = wk.has_b ? 2 : 1;
                 // S_x = Q_x K^T for key tile j (ring slot of K tile gkk); a ragged
-                // last tile runs with N = its keys rounded up to 16.  Compile-time
-                // descriptor offsets keep the issue path MMAs only.
+                // last tile runs with N = its keys rounded up to 16.
                 auto issue_s = [&](int x, int gkk, int j) {
                     const int valid = wk.S_len - j * TILE;
                     const int n = valid >= TILE ? TILE : ((valid + 15) & ~15);
@@ -479,95 +634,60 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         const uint32_t off = ((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4;
                         umma_bf16_i<1>(d, qd + off, kd + off, idesc);
                     }
-                    umma_commit(&s_full[x]);
                 };
-                // O_x (+)= P_x V over the tile's keys (16 per MMA; P is zero past
-                // the window's sequence)
-                auto issue_pv = [&](int x, int j) {
+                // O_x (+)= P_x V(j): P from tensor memory (packed bf16 over the
+                // first 64 columns of S_x), 16 keys per MMA
+                auto issue_pv = [&](int x, int j, int vslot) {
                     const int valid = wk.S_len - j * TILE;
-                    const uint64_t pd = p_desc0 + (x ? kTileDesc : 0u);
+                    const uint32_t p_tmem = tmem + x * 128;
                     const uint32_t o_tmem = tmem + 256 + x * 128;
+                    const uint64_t vd = v_desc0 + (uint32_t)vslot * kTileDesc;
                     if (valid >= TILE)
                     {
                         if (j == 0)
-                            umma_bf16_i<0>(o_tmem, pd, v_desc0, IDESC_O);
+                            umma_bf16_tmem_a_i<0>(o_tmem, p_tmem, vd, IDESC_O);
                         else
-                            umma_bf16_i<1>(o_tmem, pd, v_desc0, IDESC_O);
+                            umma_bf16_tmem_a_i<1>(o_tmem, p_tmem, vd, IDESC_O);
 #pragma unroll
                         for (int k = 1; k < TILE / 16; k++)
-                        {
-                            const uint32_t aoff = ((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4;
-                            umma_bf16_i<1>(o_tmem, pd + aoff, v_desc0 + ((k * 16 * 128) >> 4), IDESC_O);
-                        }
+                            umma_bf16_tmem_a_i<1>(o_tmem, p_tmem + k * 8, vd + ((k * 16 * 128) >> 4), IDESC_O);
                     }
                     else
                     {
                         const int ksteps = (valid + 15) / 16;
                         for (int k = 0; k < ksteps; k++)
-                        {
-                            const uint32_t aoff = ((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4;
-                            umma_bf16(o_tmem, pd + aoff, v_desc0 + ((k * 16 * 128) >> 4), IDESC_O, (j | k) != 0);
-                        }
+                            umma_bf16_tmem_a(o_tmem, p_tmem + k * 8, vd + ((k * 16 * 128) >> 4), IDESC_O,
+                                             (j | k) != 0);
                     }
-                    umma_commit(&p_empty[x]);
                 };
                 auto wait_k = [&](int g_) {
                     return mbar_wait(&k_full[g_ % K_STAGES], (uint32_t)(g_ / K_STAGES) & 1u, abort_flag, args.status);
-                };
-                // S_x(j) may overwrite S_x once the softmax has read the previous one
-                auto s_ready = [&](int x) {
-                    if (!s_issued[x]) return true;
-                    const bool r = mbar_wait(&s_free[x], sfree[x] & 1u, abort_flag, args.status);
-                    sfree[x]++;
-                    return r;
                 };
                 if (!mbar_wait(q_full, it & 1, abort_flag, args.status) || !wait_k(gk))
                 {
                     ok = false;
                     break;
                 }
-                for (int x = 0; x < ntiles && ok; x++)
+                tc_fence_after();
+                for (int x = 0; x < ntiles; x++)
                 {
-                    if (!s_ready(x))
+                    issue_s(x, gk, 0);
+                    umma_commit(&s_full[x]);
+                }
+                any = true;
+                umma_commit(&k_empty[gk % K_STAGES]);
+                gk++;
+                if (wk.nkv == 1) umma_commit(q_empty);
+                for (int j = 0; j < wk.nkv && ok; j++)
+                {
+                    const int vs = gv % V_STAGES;
+                    if (!mbar_wait(&v_full[vs], (uint32_t)(gv / V_STAGES) & 1u, abort_flag, args.status))
                     {
                         ok = false;
                         break;
                     }
-                    tc_fence_after();
-                    issue_s(x, gk, 0);
-                    s_issued[x] = true;
-                }
-                if (!ok) break;
-                umma_commit(&k_empty[gk % K_STAGES]);
-                gk++;
-                any = true;
-                if (wk.nkv == 1) umma_commit(q_empty);
-                for (int j = 0; j < wk.nkv && ok; j++)
-                {
-                    // next scores first: they only need the softmax to have read S(j)
-                    if (j + 1 < wk.nkv)
-                    {
-                        if (!wait_k(gk))
-                        {
-                            ok = false;
-                            break;
-                        }
-                        for (int x = 0; x < ntiles && ok; x++)
-                        {
-                            if (!s_ready(x))
-                            {
-                                ok = false;
-                                break;
-                            }
-                            tc_fence_after();
-                            issue_s(x, gk, j + 1);
-                        }
-                        if (!ok) break;
-                        umma_commit(&k_empty[gk % K_STAGES]);
-                        gk++;
-                        if (j + 2 == wk.nkv) umma_commit(q_empty); // the unit's last S MMA
-                    }
-                    if (!mbar_wait(v_full, (uint32_t)gv & 1u, abort_flag, args.status))
+                    const bool more = j + 1 < wk.nkv;
+                    if (more && !wait_k(gk))
                     {
                         ok = false;
                         break;
@@ -581,12 +701,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         }
                         pfull[x]++;
                         tc_fence_after();
-                        issue_pv(x, j);
-                        if (j + 1 == wk.nkv) umma_commit(&o_done[x]);
+                        issue_pv(x, j, vs);
+                        if (x == ntiles - 1) umma_commit(&v_empty[vs]);
+                        if (more)
+                        {
+                            issue_s(x, gk, j + 1);
+                            umma_commit(&s_full[x]);
+                        }
+                        else
+                            umma_commit(&o_done[x]);
                     }
                     if (!ok) break;
-                    umma_commit(v_empty);
                     gv++;
+                    if (more)
+                    {
+                        umma_commit(&k_empty[gk % K_STAGES]);
+                        gk++;
+                        if (j + 2 == wk.nkv) umma_commit(q_empty); // the unit's last S MMAs
+                    }
                 }
             }
             if (any)
@@ -598,17 +730,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     else
     {
-        // ---------------- softmax + epilogue (warps 2-5: tile A, 6-9: tile B)
-        const int x = (warp - 2) >> 2;
+        // ---------------- softmax + epilogue (warps 0-3: tile 0, 4-7: tile 1)
+        regs_increase<SOFTMAX_REGS>();
+        const int x = warp >> 2;
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         const uint32_t s_addr = tmem + lane_base + x * 128;
         const uint32_t o_addr = tmem + lane_base + 256 + x * 128;
-        uint8_t* p_tile = sP + x * TILE_BYTES;
-        const uint64_t c2 = pk2(__float_as_uint(args.scale_log2), __float_as_uint(args.scale_log2));
-        uint32_t scnt = 0, pecnt = 0, ocnt = 0;
-        bool pv_before = false; // a PV_x has been issued (P_x / O_x may be in use)
+        uint32_t scnt = 0, ocnt = 0;
         bool ok = true;
         for (int w = blockIdx.x; w < args.num_work && ok; w += gridDim.x)
         {
@@ -617,104 +747,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int qbase = wk.q0 + x * TILE;
             float m_used = -INFINITY;
             float l_run = 0.f;
-            for (int j = 0; j < wk.nkv; j++)
+            // only the last key tile can be ragged; it runs after the loop so
+            // the two forms of the softmax never share a register allocation
+            const int last_valid = wk.S_len - (wk.nkv - 1) * TILE;
+            const int nfull = last_valid == TILE ? wk.nkv : wk.nkv - 1;
+            auto wait_s = [&]() {
+                if (!warp_wait(&s_full[x], scnt & 1, abort_flag, args.status)) return false;
+                scnt++;
+                tc_fence_after();
+                return true;
+            };
+            // P_x (and any rescaled O_x) written: the PV MMA may read them
+            auto release_p = [&]() {
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[x]);
+            };
+            for (int j = 0; j < nfull; j++)
             {
-                if (!warp_wait(&s_full[x], scnt & 1, abort_flag, args.status))
+                if (!wait_s())
                 {
                     ok = false;
                     break;
                 }
-                scnt++;
-                tc_fence_after();
-                const int valid = wk.S_len - j * TILE; // >= 1
-                const bool full = valid >= TILE;
-                // Scores in two 64-column halves so only one half is live: the
-                // max reads the second half in 32-column pieces, the first
-                // half's exponentials run, then the second half is reloaded and
-                // S released (the next S_x is needed only at the next key tile).
-                uint32_t v[64];
-                tmem_ld64(s_addr, v);
-                float mo;
-                {
-                    uint32_t t[32];
-                    tmem_ld32(s_addr + 64, t);
-                    tmem_ld_wait();
-                    mo = full ? row_max<true, 32>(t, valid - 64) : row_max<false, 32>(t, valid - 64);
-                    tmem_ld32(s_addr + 96, t);
-                    tmem_ld_wait();
-                    mo = fmaxf(mo, full ? row_max<true, 32>(t, valid - 96) : row_max<false, 32>(t, valid - 96));
-                }
-                const float mx = fmaxf(mo, full ? row_max<true, 64>(v, valid) : row_max<false, 64>(v, valid));
-                const float mt = mx * args.scale_log2;
-                float alpha = 1.f;
-                const bool rescale = j > 0 && mt > m_used + RESCALE_THRESHOLD;
-                if (j == 0)
-                    m_used = mt;
-                else if (rescale)
-                {
-                    alpha = ex2(m_used - mt);
-                    m_used = mt;
-                }
-                const uint64_t negm2 = pk2(__float_as_uint(-m_used), __float_as_uint(-m_used));
-                uint64_t sum2[4] = {0, 0, 0, 0};
-                uint32_t pk[32];
-                if (full)
-                    row_exp64<true>(v, valid, c2, negm2, pk, sum2);
-                else
-                    row_exp64<false>(v, valid, c2, negm2, pk, sum2);
-                // P_x and O_x are free once the previous PV_x has completed
-                if (pv_before)
-                {
-                    if (!warp_wait(&p_empty[x], pecnt & 1, abort_flag, args.status))
-                    {
-                        ok = false;
-                        break;
-                    }
-                    pecnt++;
-                    tc_fence_after();
-                }
-                store_p_half<0>(p_tile, row, pk);
-                tmem_ld64(s_addr + 64, v);
-                tmem_ld_wait();
-                // S_x is in registers: the next S_x may be computed into TMEM
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s_free[x]);
-                if (full)
-                    row_exp64<true>(v, valid - 64, c2, negm2, pk, sum2);
-                else
-                    row_exp64<false>(v, valid - 64, c2, negm2, pk, sum2);
-                store_p_half<1>(p_tile, row, pk);
-                float rowsum;
-                {
-                    const uint64_t s2 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
-                    float lo, hi;
-                    upk2(s2, lo, hi);
-                    rowsum = lo + hi;
-                }
-                if (rescale)
-                {
-#pragma unroll
-                    for (int c = 0; c < 4; c++)
-                    {
-                        uint32_t o[32];
-                        tmem_ld32(o_addr + c * 32, o);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                        tmem_st32(o_addr + c * 32, o);
-                    }
-                    tmem_st_wait();
-                    l_run *= alpha;
-                }
-                l_run += rowsum;
-                fence_proxy_async_smem(); // P is read by the tensor core (async proxy)
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&p_full[x]);
-                pv_before = true;
+                softmax_tile<true>(s_addr, o_addr, TILE, j == 0, args.scale_log2, m_used, l_run);
+                release_p();
             }
             if (!ok) break;
+            if (nfull < wk.nkv)
+            {
+                if (!wait_s())
+                {
+                    ok = false;
+                    break;
+                }
+                softmax_tile<false>(s_addr, o_addr, last_valid, nfull == 0, args.scale_log2, m_used, l_run);
+                release_p();
+            }
             if (!warp_wait(&o_done[x], ocnt & 1, abort_flag, args.status))
             {
                 ok = false;
@@ -751,7 +821,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+    if (warp == 9) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 } // namespace
@@ -787,10 +857,17 @@ int launch_window_attention(Context& ctx, const AttnSchedule& s, int heads, cons
     a.status = ctx.status;
     for (int i = 0; i < kMaxPeers; i++) a.peer_out[i] = i < num_peers ? peer_out[i] : nullptr;
     static std::atomic<uint64_t> configured{0};
-    if (first_on_device(configured) &&
-        cudaFuncSetAttribute(window_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+    if (first_on_device(configured))
+    {
+        // The register split assumes exactly LAUNCH_REGS per thread at launch
+        // (a different count would leave the softmax warps' increase waiting).
+        cudaFuncAttributes fa;
+        if (cudaFuncGetAttributes(&fa, window_attention_kernel) != cudaSuccess || fa.numRegs != LAUNCH_REGS)
+            return S2_ERR_CUDA;
+        if (cudaFuncSetAttribute(window_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
             cudaSuccess)
-        return S2_ERR_CUDA;
+            return S2_ERR_CUDA;
+    }
     a.heads = heads;
     a.num_work = s.num_items * heads;
     const int grid = a.num_work < ctx.num_sms ? a.num_work : ctx.num_sms;
