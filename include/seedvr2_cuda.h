@@ -100,6 +100,20 @@ int s2_plan_info(const s2_plan* plan, int* num_windows, int* num_tokens, int* ma
 int s2_plan_copy(const s2_plan* plan, int* windows, int* sample_window_count, int* video_indices,
                  int* inverse_video_indices, int* local_positions);
 void s2_plan_free(s2_plan* plan);
+/* The plan's attention schedule as the kernels read it, copied back from the
+ * device (built for these text lengths first if needed), so the device-side
+ * window indexing can be checked bit for bit against the plan's
+ * video_indices / inverse_video_indices / local_positions
+ * (adaptive_window_attention.cpp:446-473, :954-961).  sizes[4] (host, always
+ * written): packed rows R, windows nw, tokens n, pack_dst rows.  Then, for
+ * any non-NULL host array: row_src [R] (video token of each packed row, or
+ * -1 - text row), row_pos [R][3] (RoPE position: window-local (t + T, h, w)
+ * for video rows, (j, j, j) for text row j), win_info [nw][4] (packed row of
+ * the window's first row, L, T, partition offset), video_indices [n] (source
+ * token of each partition slot), pack_dst [rows] (packed row of each video
+ * token).  Synchronous. */
+int s2_plan_schedule_copy(s2_context* ctx, s2_plan* plan, const int* text_lengths, int* sizes, int* row_src,
+                          int* row_pos, int* win_info, int* video_indices, int* pack_dst);
 
 /* ---------------------------------------------------------------------------
  * AdaptiveWindowAttention forward.  Replaces
@@ -490,6 +504,16 @@ int s2_dist_unique_id(void* id128);
 int s2_dist_init(s2_context* ctx, const void* id128, int rank, int world, int timeout_ms);
 int s2_dist_sync(s2_context* ctx);
 int s2_dist_destroy(s2_context* ctx);
+
+/* The cross-GPU barrier of the sharded forward (no counterpart in the
+ * reference, whose layers never span GPUs): one warp stores `epoch` into
+ * slot `rank` of every rank's flag array (peer_flags[i], device or peer
+ * memory, 4-byte aligned, world <= 8) and waits until every slot of its own
+ * flags (my_flags[0..world)) holds at least `epoch`.  The wait is bounded
+ * (2 s of device time): on expiry the kernel records a timeout and returns,
+ * and s2_status reports S2_ERR_TIMEOUT -- the context stays usable. */
+int s2_peer_barrier(s2_context* ctx, void* const* peer_flags, uint32_t* my_flags, int rank, int world,
+                    uint32_t epoch);
 
 /* Sharded forward of all blocks for ONE sample on this rank (collective: every
  * rank calls it with the same shape).  x_local: fp32 [n_local + Nt][D] -- the

@@ -46,13 +46,14 @@ S2_EPI_GATE_RESIDUAL = 2
 EXPORTED = [
     "s2_init", "s2_destroy", "s2_set_stream", "s2_status", "s2_error_string", "s2_version", "s2_launch_count",
     "s2_profile_enable", "s2_profile_read",
-    "s2_plan_build", "s2_plan_info", "s2_plan_copy", "s2_plan_free",
+    "s2_plan_build", "s2_plan_info", "s2_plan_copy", "s2_plan_free", "s2_plan_schedule_copy",
     "s2_awa_forward", "s2_awa_forward_static", "s2_awa_static_status", "s2_shared_linear", "s2_ada_rmsnorm", "s2_convert_f32_bf16",
     "s2_count_nonfinite",
     "s2_dit_create", "s2_dit_free", "s2_dit_set_block_weights", "s2_dit_init_random", "s2_dit_forward",
     "s2_dit_set_check_finite", "s2_dit_nonfinite_report", "s2_dit_set_checkpoints",
     "s2_dit_forward_host", "s2_shard_build", "s2_shard_counts", "s2_shard_lists", "s2_shard_free",
-    "s2_dist_unique_id", "s2_dist_init", "s2_dist_sync", "s2_dist_destroy", "s2_dit_forward_sharded",
+    "s2_dist_unique_id", "s2_dist_init", "s2_dist_sync", "s2_dist_destroy", "s2_peer_barrier",
+    "s2_dit_forward_sharded",
     "s2_patchify_video", "s2_unpatchify_prediction", "s2_timestep_embedding", "s2_dit_set_io_weights",
     "s2_dit_forward_frontend", "s2_dit_forward_tail", "s2_dit_forward_step", "s2_dit_forward_step_host",
     "s2_dit_denoise", "s2_dit_denoise_host", "s2_apply_cfg",
@@ -147,6 +148,7 @@ def lib() -> C.CDLL:
     L.s2_plan_copy.argtypes = [vp, pint, pint, pint, pint, pint]
     L.s2_plan_free.argtypes = [vp]
     L.s2_plan_free.restype = None
+    L.s2_plan_schedule_copy.argtypes = [vp, vp, pint, pint, vp, vp, vp, vp, vp]
     L.s2_awa_forward.argtypes = [vp, C.POINTER(AwaParams), vp, pint, pint, ip, ip, vp, vp, vp, i64, vp, vp, vp, i64,
                                  ip, vp, vp]
     L.s2_awa_forward_static.argtypes = [C.POINTER(AwaParams), pint, pint, ip, ip, vp, vp, vp, i64, vp, vp, vp, i64,
@@ -176,6 +178,7 @@ def lib() -> C.CDLL:
     L.s2_dist_sync.argtypes = [vp]
     L.s2_dist_destroy.argtypes = [vp]
     L.s2_dit_forward_sharded.argtypes = [vp, pint, ip, vp, vp]
+    L.s2_peer_barrier.argtypes = [vp, vp, vp, ip, ip, C.c_uint32]
     L.s2_patchify_video.argtypes = [vp, vp, ip, pint, ip, vp]
     L.s2_unpatchify_prediction.argtypes = [vp, vp, ip, pint, ip, vp]
     L.s2_timestep_embedding.argtypes = [vp, C.POINTER(C.c_float), ip, vp]
@@ -320,6 +323,24 @@ class Plan:
         check(lib().s2_plan_copy(self.handle, P(windows), P(swc), P(vi), P(inv), P(pos)), "s2_plan_copy")
         return {"windows": windows, "sample_window_count": swc, "video_indices": vi,
                 "inverse_video_indices": inv, "local_positions": pos, "max_window_tokens": mx.value}
+
+    def schedule(self, ctx, text_lengths) -> dict:
+        """The attention schedule tables as they sit on the device (s2_plan_schedule_copy)."""
+        import numpy as np
+
+        tl = _ints(text_lengths)
+        sizes = (C.c_int * 4)()
+        check(lib().s2_plan_schedule_copy(ctx.handle, self.handle, tl, sizes, None, None, None, None, None),
+              "s2_plan_schedule_copy")
+        R, nw, n, npd = list(sizes)
+        out = {"row_src": np.zeros(R, np.int32), "row_pos": np.zeros((R, 3), np.int32),
+               "win_info": np.zeros((nw, 4), np.int32), "video_indices": np.zeros(n, np.int32),
+               "pack_dst": np.zeros(npd, np.int32)}
+        check(lib().s2_plan_schedule_copy(ctx.handle, self.handle, tl, sizes,
+                                          *[out[k].ctypes.data for k in ("row_src", "row_pos", "win_info",
+                                                                         "video_indices", "pack_dst")]),
+              "s2_plan_schedule_copy")
+        return out
 
 
 def awa_forward(ctx: Context, *, heads, head_dim, window, window_mode, shifted, eps, rope_pairs, norms, freqs,

@@ -195,6 +195,32 @@ int s2_plan_copy(const s2_plan* p, int* windows, int* sample_window_count, int* 
     return S2_OK;
 }
 
+int s2_plan_schedule_copy(s2_context* ctx, s2_plan* p, const int* text_lengths, int* sizes, int* row_src,
+                          int* row_pos, int* win_info, int* video_indices, int* pack_dst)
+{
+    if (!ctx || !p || !text_lengths || !sizes) return S2_ERR_INVALID;
+    s2::Context& c = ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    const s2::AttnSchedule* s = nullptr;
+    int r = s2::ensure_schedule(p, text_lengths, c, &s);
+    if (r != S2_OK) return r;
+    const int tokens = static_cast<int>(p->plan.video_indices.size());
+    sizes[0] = s->packed_rows;
+    sizes[1] = s->num_windows;
+    sizes[2] = tokens;
+    sizes[3] = s->pack_dst_rows;
+    // the tables as the kernels read them: copied back from the device
+    auto get = [&](int* dst, const void* src, size_t bytes) {
+        return !dst || !bytes || cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost) == cudaSuccess;
+    };
+    if (!get(row_src, s->row_src, (size_t)s->packed_rows * 4) || !get(row_pos, s->row_pos, (size_t)s->packed_rows * 12) ||
+        !get(win_info, s->win_info, (size_t)s->num_windows * 16) ||
+        !get(video_indices, s->video_indices, (size_t)tokens * 4) ||
+        !get(pack_dst, s->pack_dst, (size_t)s->pack_dst_rows * 4))
+        return S2_ERR_CUDA;
+    return S2_OK;
+}
+
 void s2_plan_free(s2_plan* p)
 {
     delete p;
@@ -454,6 +480,18 @@ int s2_dist_destroy(s2_context* ctx)
     if (ctx->dist) ctx->dist->destroy();
     ctx->dist.reset();
     return S2_OK;
+}
+
+int s2_peer_barrier(s2_context* ctx, void* const* peer_flags, uint32_t* my_flags, int rank, int world,
+                    uint32_t epoch)
+{
+    if (!ctx || !peer_flags || !my_flags || world <= 0 || world > s2::kMaxPeers || rank < 0 || rank >= world)
+        return S2_ERR_INVALID;
+    for (int i = 0; i < world; i++)
+        if (!peer_flags[i] || (reinterpret_cast<uintptr_t>(peer_flags[i]) & 3)) return S2_ERR_INVALID;
+    if (reinterpret_cast<uintptr_t>(my_flags) & 3) return S2_ERR_INVALID;
+    if (cudaSetDevice(ctx->c.device) != cudaSuccess) return S2_ERR_CUDA;
+    return s2::launch_peer_barrier(ctx->c, peer_flags, my_flags, rank, world, epoch);
 }
 
 } // extern "C"
