@@ -196,6 +196,12 @@ int s2_shared_linear(s2_context* ctx, int M0, int M1, int N, int K, const void* 
  * x fp32 [rows][D], shift/scale fp32 [D]. */
 int s2_ada_rmsnorm(s2_context* ctx, int rows, int D, const float* x, float eps, const float* shift,
                    const float* scale, void* out_bf16);
+/* The LayerNorm form of the same pass (BASELINE's block description names
+ * "RMS/LayerNorm"; which one the exported graph uses is not in the tree):
+ * out[r] (bf16) = (x[r] - mean(x[r])) * rsqrt(var(x[r]) + eps) * scale + shift,
+ * var the biased variance, no affine of its own. */
+int s2_ada_layernorm(s2_context* ctx, int rows, int D, const float* x, float eps, const float* shift,
+                     const float* scale, void* out_bf16);
 /* fp32 -> bf16 (round to nearest even). */
 int s2_convert_f32_bf16(s2_context* ctx, const float* in, void* out, int64_t count);
 /* Number of NaN / Inf values among `count` device elements of dtype
@@ -247,6 +253,12 @@ typedef struct
 int s2_dit_create(s2_context* ctx, const s2_dit_config* cfg, s2_dit** out);
 void s2_dit_free(s2_dit* dit);
 int s2_dit_set_block_weights(s2_dit* dit, int block, const s2_block_host_weights* w);
+/* The norm of a block's two AdaLN passes (both forms without affine, then
+ * the modulation's scale and shift): S2_NORM_RMS (the default) or
+ * S2_NORM_LAYER, chosen per block. */
+#define S2_NORM_RMS 0
+#define S2_NORM_LAYER 1
+int s2_dit_set_block_norm(s2_dit* dit, int block, int norm_type);
 /* Seeded synthetic weights generated on the device (weights ~N(0,0.02),
  * ada offsets ~N(0,1)/sqrt(D) (+1 on the scale rows), qk norms ~N(1,0.02),
  * rope freqs 1/10000^(2i/(2*pairs))). */

@@ -192,7 +192,8 @@ class Port:
 
     def block_forward(self, *, dims, eps_norm, eps_qk, weights: dict, modulation, shapes, text_lengths,
                       x_video, x_text, emulate_bf16=False):
-        """weights: dict of fp32 arrays keyed like s2o_block_weights; returns updated (xv, xt)."""
+        """weights: dict of fp32 arrays keyed like s2o_block_weights; returns updated (xv, xt).
+        dims: D, heads, head_dim, F, rope_pairs, window_mode, window0..2, shifted[, norm: 0 RMS, 1 Layer]."""
 
         class W(C.Structure):
             _fields_ = [(n, C.c_void_p) for n in
@@ -204,6 +205,7 @@ class Port:
         xv = _f32(x_video).copy()
         xt = _f32(x_text).copy()
         shapes = _i32(shapes).reshape(-1, 3)
+        dims = list(dims) + [0] * (11 - len(dims))  # norm type defaults to RMSNorm
         r = self.lib.s2o_block_forward(_i32(dims), eps_norm, eps_qk, C.addressof(w), _f32(modulation).reshape(-1),
                                        shapes, _i32(text_lengths), len(shapes), xv, xt, int(emulate_bf16))
         if r != 0:

@@ -402,11 +402,14 @@ static float maybe_bf16(float v, int on)
     return on ? s2o_round_bf16(v) : v;
 }
 
-/* Block-level RMSNorm (no affine) followed by AdaSingle-style modulation:
- * y = x * rsqrt(mean(x^2) + eps) * scale + shift, with the shift/scale rows
- * of each row's sample (mods: [batch][6][D], k0 = index of the shift row). */
+/* Block-level norm (no affine) followed by AdaSingle-style modulation, with
+ * the shift/scale rows of each row's sample (mods: [batch][6][D], k0 = index
+ * of the shift row):
+ *   RMSNorm   (layer = 0): y = x * rsqrt(mean(x^2) + eps) * scale + shift
+ *   LayerNorm (layer = 1): y = (x - mean(x)) * rsqrt(var(x) + eps) * scale + shift
+ * (var the biased variance, mean and variance in double). */
 static void ada_norm(const float* x, int rows, int D, float eps, const float* mods, const int* row_sample, int k0,
-                     float* y, int bf16)
+                     float* y, int bf16, int layer)
 {
 #pragma omp parallel for schedule(static)
     for (int r = 0; r < rows; r++)
@@ -414,10 +417,18 @@ static void ada_norm(const float* x, int rows, int D, float eps, const float* mo
         const float* xr = x + (size_t)r * D;
         const float* shift = mods + ((size_t)row_sample[r] * 6 + k0) * D;
         const float* scale = shift + D;
+        double mean = 0.0;
+        if (layer)
+        {
+            for (int i = 0; i < D; i++) mean += xr[i];
+            mean /= D;
+        }
         double ss = 0.0;
-        for (int i = 0; i < D; i++) ss += (double)xr[i] * xr[i];
+        for (int i = 0; i < D; i++) ss += ((double)xr[i] - mean) * ((double)xr[i] - mean);
         const float inv = 1.f / sqrtf((float)(ss / D) + eps);
-        for (int i = 0; i < D; i++) y[(size_t)r * D + i] = maybe_bf16(xr[i] * inv * scale[i] + shift[i], bf16);
+        const float m = (float)mean;
+        for (int i = 0; i < D; i++)
+            y[(size_t)r * D + i] = maybe_bf16((xr[i] - m) * inv * scale[i] + shift[i], bf16);
     }
 }
 
@@ -434,13 +445,16 @@ static float gelu_tanh(float x)
  * the published SeedVR2 block design):
  *
  *   mod_k = modulation[k] + ada[k], k = attn shift/scale/gate, mlp shift/scale/gate
- *   h   = rmsnorm(x) * scale_a + shift_a
+ *   h   = norm(x) * scale_a + shift_a
  *   qkv = SharedLinear_qkv(h);  (cv, ct) = AWA(qkv_v, qkv_t)
  *   x  += SharedLinear_out(c) * gate_a
- *   h   = rmsnorm(x) * scale_m + shift_m
+ *   h   = norm(x) * scale_m + shift_m
  *   x  += SharedLinear_down(gelu_tanh(SharedLinear_up(h))) * gate_m
  *
- * dims: D, heads, head_dim, F, rope_pairs, window_mode, window0..2, shifted.
+ * norm = RMSNorm or LayerNorm (both without affine; BASELINE names
+ * "RMS/LayerNorm" and the exported graph is not in the tree).
+ * dims: D, heads, head_dim, F, rope_pairs, window_mode, window0..2, shifted,
+ * norm (0 RMSNorm, 1 LayerNorm).
  * modulation: [batch][6][D].  emulate_bf16 rounds the activations the GPU
  * path stores in bf16 (h, qkv, attention q/k/v/context, u). */
 int s2o_block_forward(const int* dims, float eps_norm, float eps_qk, const s2o_block_weights* W,
@@ -448,8 +462,8 @@ int s2o_block_forward(const int* dims, float eps_norm, float eps_qk, const s2o_b
                       float* xt, int bf16)
 {
     const int D = dims[0], heads = dims[1], hd = dims[2], F = dims[3], pairs = dims[4], mode = dims[5];
-    const int shifted = dims[9];
-    if (heads * hd != D) return -1;
+    const int shifted = dims[9], layer = dims[10];
+    if (heads * hd != D || layer < 0 || layer > 1) return -1;
     int Nv = 0, Nt = 0;
     for (int s = 0; s < batch; s++)
     {
@@ -481,7 +495,7 @@ int s2o_block_forward(const int* dims, float eps_norm, float eps_qk, const s2o_b
 
     int ret = 0;
     /* attention half */
-    ada_norm(x, M, D, eps_norm, mods, row_sample, 0, h, bf16);
+    ada_norm(x, M, D, eps_norm, mods, row_sample, 0, h, bf16, layer);
     s2o_linear(h, M, D, W->w_qkv, W->b_qkv, 3 * D, qkv);
     if (bf16)
         for (size_t i = 0; i < (size_t)M * 3 * D; i++) qkv[i] = s2o_round_bf16(qkv[i]);
@@ -501,7 +515,7 @@ int s2o_block_forward(const int* dims, float eps_norm, float eps_qk, const s2o_b
         for (int i = 0; i < D; i++) x[(size_t)r * D + i] += o[(size_t)r * D + i] * g[i];
     }
     /* mlp half */
-    ada_norm(x, M, D, eps_norm, mods, row_sample, 3, h, bf16);
+    ada_norm(x, M, D, eps_norm, mods, row_sample, 3, h, bf16, layer);
     s2o_linear(h, M, D, W->w_up, W->b_up, F, u);
     for (size_t i = 0; i < (size_t)M * F; i++) u[i] = maybe_bf16(gelu_tanh(u[i]), bf16);
     s2o_linear(u, M, F, W->w_down, W->b_down, D, o);

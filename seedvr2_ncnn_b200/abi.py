@@ -47,9 +47,11 @@ EXPORTED = [
     "s2_init", "s2_destroy", "s2_set_stream", "s2_status", "s2_error_string", "s2_version", "s2_launch_count",
     "s2_profile_enable", "s2_profile_read",
     "s2_plan_build", "s2_plan_info", "s2_plan_copy", "s2_plan_free", "s2_plan_schedule_copy",
-    "s2_awa_forward", "s2_awa_forward_static", "s2_awa_static_status", "s2_shared_linear", "s2_ada_rmsnorm", "s2_convert_f32_bf16",
+    "s2_awa_forward", "s2_awa_forward_static", "s2_awa_static_status", "s2_shared_linear", "s2_ada_rmsnorm", "s2_ada_layernorm",
+    "s2_convert_f32_bf16",
     "s2_count_nonfinite",
-    "s2_dit_create", "s2_dit_free", "s2_dit_set_block_weights", "s2_dit_init_random", "s2_dit_forward",
+    "s2_dit_create", "s2_dit_free", "s2_dit_set_block_weights", "s2_dit_set_block_norm", "s2_dit_init_random",
+    "s2_dit_forward",
     "s2_dit_set_check_finite", "s2_dit_nonfinite_report", "s2_dit_set_checkpoints",
     "s2_dit_forward_host", "s2_shard_build", "s2_shard_counts", "s2_shard_lists", "s2_shard_free",
     "s2_dist_unique_id", "s2_dist_init", "s2_dist_sync", "s2_dist_destroy", "s2_peer_barrier",
@@ -156,6 +158,8 @@ def lib() -> C.CDLL:
     L.s2_awa_static_status.argtypes = [vp]
     L.s2_shared_linear.argtypes = [vp, ip, ip, ip, ip, vp, vp, vp, vp, ip, vp, ip, vp, vp]
     L.s2_ada_rmsnorm.argtypes = [vp, ip, ip, vp, C.c_float, vp, vp, vp]
+    L.s2_ada_layernorm.argtypes = [vp, ip, ip, vp, C.c_float, vp, vp, vp]
+    L.s2_dit_set_block_norm.argtypes = [vp, ip, ip]
     L.s2_convert_f32_bf16.argtypes = [vp, vp, vp, i64]
     L.s2_dit_create.argtypes = [vp, C.POINTER(DitConfig), C.POINTER(vp)]
     L.s2_dit_free.argtypes = [vp]
@@ -414,6 +418,17 @@ def ada_rmsnorm(ctx: Context, x, eps, shift, scale, out=None):
     return out
 
 
+def ada_layernorm(ctx: Context, x, eps, shift, scale, out=None):
+    import torch
+
+    rows, D = x.shape
+    if out is None:
+        out = torch.empty((rows, D), dtype=torch.bfloat16, device=x.device)
+    check(lib().s2_ada_layernorm(ctx.handle, rows, D, x.data_ptr(), float(eps), shift.data_ptr(), scale.data_ptr(),
+                                 out.data_ptr()), "s2_ada_layernorm")
+    return out
+
+
 def _floats(values) -> C.Array:
     values = [float(v) for v in values]
     return (C.c_float * len(values))(*values)
@@ -513,6 +528,10 @@ class Dit:
         """Count the NaN / Inf values of the video and text rows at the block stack's input and after every
         block; a forward that finds any fails with code -1 (see nonfinite_report)."""
         check(lib().s2_dit_set_check_finite(self.handle, int(bool(enable))), "s2_dit_set_check_finite")
+
+    def set_block_norm(self, block: int, layer: bool):
+        """The block's AdaLN norms: LayerNorm (layer=True) or RMSNorm (the default)."""
+        check(lib().s2_dit_set_block_norm(self.handle, block, 1 if layer else 0), "s2_dit_set_block_norm")
 
     def set_checkpoints(self, blocks, videos, texts):
         """After block blocks[i] of every following forward, copy its video rows into videos[i] and its text

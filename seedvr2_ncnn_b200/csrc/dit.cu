@@ -35,6 +35,7 @@ struct s2_dit
         float *b_qkv, *b_out, *b_up, *b_down;
         float* qk_norm;
         float* freqs;
+        int norm_layer = 0; // the block's two AdaLN norms: 0 RMSNorm, 1 LayerNorm
     };
     std::vector<Block> blocks;
     float* ada_all = nullptr; // [blocks][6][D]
@@ -481,6 +482,14 @@ int s2_dit_set_check_finite(s2_dit* d, int enable)
     return S2_OK;
 }
 
+int s2_dit_set_block_norm(s2_dit* d, int block, int norm_type)
+{
+    if (!d || block < 0 || block >= d->cfg.num_blocks || (norm_type != S2_NORM_RMS && norm_type != S2_NORM_LAYER))
+        return S2_ERR_INVALID;
+    d->blocks[block].norm_layer = norm_type == S2_NORM_LAYER;
+    return S2_OK;
+}
+
 int s2_dit_set_checkpoints(s2_dit* d, const int* blocks, int count, float* const* video, float* const* text)
 {
     if (!d || count < 0 || (count > 0 && (!blocks || !video || !text))) return S2_ERR_INVALID;
@@ -627,7 +636,7 @@ int s2_dit_forward(s2_dit* d, const int* video_shape, int text_length, float* x,
         const float* mb = mods + (size_t)b * 6 * D;
         const int sh = b & 1; // odd blocks use the half-shifted windows
         const s2::AttnSchedule& S = *sched[sh];
-        if ((r = s2::launch_ada_rmsnorm(c, M, D, x, cfg.norm_eps, mb, mb + D, h)) != S2_OK) return r;
+        if ((r = s2::launch_ada_norm(c, M, D, x, cfg.norm_eps, mb, mb + D, h, bl.norm_layer)) != S2_OK) return r;
         __nv_bfloat16* Qp = reinterpret_cast<__nv_bfloat16*>(pk);
         __nv_bfloat16* Kp = reinterpret_cast<__nv_bfloat16*>(pk + sz_pk);
         __nv_bfloat16* Vp = reinterpret_cast<__nv_bfloat16*>(pk + 2 * sz_pk);
@@ -657,7 +666,7 @@ int s2_dit_forward(s2_dit* d, const int* video_shape, int text_length, float* x,
         if ((r = s2::launch_shared_linear(c, M, 0, D, D, ctxb, nullptr, bl.w_out, cfg.out_bias ? bl.b_out : nullptr,
                                           s2::EPI_GATE_RESIDUAL, mb + 2 * D, 1, x, nullptr)) != S2_OK)
             return r;
-        if ((r = s2::launch_ada_rmsnorm(c, M, D, x, cfg.norm_eps, mb + 3 * D, mb + 4 * D, h)) != S2_OK) return r;
+        if ((r = s2::launch_ada_norm(c, M, D, x, cfg.norm_eps, mb + 3 * D, mb + 4 * D, h, bl.norm_layer)) != S2_OK) return r;
         if ((r = s2::launch_shared_linear(c, M, 0, F, D, h, nullptr, bl.w_up, cfg.mlp_bias ? bl.b_up : nullptr,
                                           s2::EPI_GELU_TANH, nullptr, 0, u, nullptr)) != S2_OK)
             return r;
@@ -875,7 +884,7 @@ int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, f
         const float* mb = mods + (size_t)b * 6 * D;
         const int shf = b & 1;
         const s2::AttnSchedule& S = sh.sched[shf];
-        if ((r = s2::launch_ada_rmsnorm(c, M, D, x, cfg.norm_eps, mb, mb + D, h)) != S2_OK) return r;
+        if ((r = s2::launch_ada_norm(c, M, D, x, cfg.norm_eps, mb, mb + D, h, bl.norm_layer)) != S2_OK) return r;
         __nv_bfloat16 *Qp, *Kp, *Vp;
         if (sh.fused)
         {
@@ -942,7 +951,7 @@ int s2_dit_forward_sharded(s2_dit* d, const int* video_shape, int text_length, f
         if ((r = s2::launch_shared_linear(c, M, 0, D, D, ctxb, nullptr, bl.w_out, cfg.out_bias ? bl.b_out : nullptr,
                                           s2::EPI_GATE_RESIDUAL, mb + 2 * D, 1, x, nullptr)) != S2_OK)
             return r;
-        if ((r = s2::launch_ada_rmsnorm(c, M, D, x, cfg.norm_eps, mb + 3 * D, mb + 4 * D, h)) != S2_OK) return r;
+        if ((r = s2::launch_ada_norm(c, M, D, x, cfg.norm_eps, mb + 3 * D, mb + 4 * D, h, bl.norm_layer)) != S2_OK) return r;
         if ((r = s2::launch_shared_linear(c, M, 0, F, D, h, nullptr, bl.w_up, cfg.mlp_bias ? bl.b_up : nullptr,
                                           s2::EPI_GELU_TANH, nullptr, 0, u, nullptr)) != S2_OK)
             return r;

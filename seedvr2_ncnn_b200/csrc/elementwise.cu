@@ -181,40 +181,62 @@ __global__ void text_pool_kernel(const int4* __restrict__ reduce, const float* _
     }
 }
 
-// ---------------------------------------------------------------- ada_rmsnorm
-// y = x * (1/sqrt(mean(x^2) + eps)) * scale + shift -> bf16; one warp per row.
-// For D = 256 G the row is held in registers (2G float4 per lane, each warp
-// access 512 contiguous bytes) so x is read from HBM once, and two 8-warp
-// blocks fit per SM (128 registers) to keep 16 rows in flight; G = 0 is the
-// generic two-pass form for other widths.  Rows are taken last first: x was
-// just written by a GEMM epilogue whose final tiles hold the highest rows, so
-// those are still in L2 when this pass starts, and the rows it writes last
-// (the lowest) are the ones the next GEMM reads first.
-template <int G>
+// ---------------------------------------------------------------- ada_rmsnorm / ada_layernorm
+// RMSNorm:   y = x * (1/sqrt(mean(x^2) + eps)) * scale + shift
+// LayerNorm: y = (x - mean(x)) * (1/sqrt(var(x) + eps)) * scale + shift
+// (no affine of their own; var the biased variance from the centred values)
+// -> bf16; one warp per row.  For D = 256 G the row is held in registers (2G
+// float4 per lane, each warp access 512 contiguous bytes) so x is read from
+// HBM once -- LayerNorm adds one warp reduction for the mean -- and two
+// 8-warp blocks fit per SM (128 registers) to keep 16 rows in flight; G = 0
+// is the generic form for other widths (it re-reads the row).  Rows are taken
+// last first: x was just written by a GEMM epilogue whose final tiles hold
+// the highest rows, so those are still in L2 when this pass starts, and the
+// rows it writes last (the lowest) are the ones the next GEMM reads first.
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    return v;
+}
+
+template <int G, bool LAYER>
 __global__ void __launch_bounds__(256, 2)
-    ada_rmsnorm_kernel(int rows, int D, const float* __restrict__ x, float eps, const float* __restrict__ shift,
-                       const float* __restrict__ scale, __nv_bfloat16* __restrict__ y)
+    ada_norm_kernel(int rows, int D, const float* __restrict__ x, float eps, const float* __restrict__ shift,
+                    const float* __restrict__ scale, __nv_bfloat16* __restrict__ y)
 {
     const int row = rows - 1 - (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5));
     const int lane = threadIdx.x & 31;
     if (row < 0) return;
     const float* xr = x + (int64_t)row * D;
     __nv_bfloat16* yr = y + (int64_t)row * D;
-    float ss = 0.f;
+    float mean = 0.f;
     if constexpr (G > 0)
     {
         // 2G float4 per lane; each warp access covers 512 contiguous bytes
         constexpr int Q = 2 * G;
         float4 v[Q];
 #pragma unroll
-        for (int q = 0; q < Q; q++)
+        for (int q = 0; q < Q; q++) v[q] = __ldg(reinterpret_cast<const float4*>(xr + q * 128 + lane * 4));
+        if (LAYER)
         {
-            v[q] = __ldg(reinterpret_cast<const float4*>(xr + q * 128 + lane * 4));
-            ss += v[q].x * v[q].x + v[q].y * v[q].y + v[q].z * v[q].z + v[q].w * v[q].w;
-        }
+            float s = 0.f;
 #pragma unroll
-        for (int m = 16; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
-        const float inv = 1.f / sqrtf(ss / D + eps);
+            for (int q = 0; q < Q; q++) s += (v[q].x + v[q].y) + (v[q].z + v[q].w);
+            mean = warp_sum(s) / D;
+#pragma unroll
+            for (int q = 0; q < Q; q++)
+            {
+                v[q].x -= mean;
+                v[q].y -= mean;
+                v[q].z -= mean;
+                v[q].w -= mean;
+            }
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int q = 0; q < Q; q++) ss += v[q].x * v[q].x + v[q].y * v[q].y + v[q].z * v[q].z + v[q].w * v[q].w;
+        const float inv = 1.f / sqrtf(warp_sum(ss) / D + eps);
 #pragma unroll
         for (int q = 0; q < Q; q++)
         {
@@ -229,16 +251,27 @@ __global__ void __launch_bounds__(256, 2)
     }
     else
     {
+        if (LAYER)
+        {
+            float s = 0.f;
+            for (int c = lane * 8; c < D; c += 256)
+            {
+                float v[8];
+                load8<float>(xr + c, v);
+#pragma unroll
+                for (int i = 0; i < 8; i++) s += v[i];
+            }
+            mean = warp_sum(s) / D;
+        }
+        float ss = 0.f;
         for (int c = lane * 8; c < D; c += 256)
         {
             float v[8];
             load8<float>(xr + c, v);
 #pragma unroll
-            for (int i = 0; i < 8; i++) ss += v[i] * v[i];
+            for (int i = 0; i < 8; i++) ss += (v[i] - mean) * (v[i] - mean);
         }
-#pragma unroll
-        for (int m = 16; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
-        const float inv = 1.f / sqrtf(ss / D + eps);
+        const float inv = 1.f / sqrtf(warp_sum(ss) / D + eps);
         for (int c = lane * 8; c < D; c += 256)
         {
             float v[8], sc[8], sh[8];
@@ -246,7 +279,7 @@ __global__ void __launch_bounds__(256, 2)
             load8<float>(scale + c, sc);
             load8<float>(shift + c, sh);
 #pragma unroll
-            for (int i = 0; i < 8; i++) v[i] = v[i] * inv * sc[i] + sh[i];
+            for (int i = 0; i < 8; i++) v[i] = (v[i] - mean) * inv * sc[i] + sh[i];
             store8_bf16(yr + c, v);
         }
     }
@@ -367,27 +400,44 @@ int launch_text_pool(Context& ctx, const AttnSchedule& s, int inner, const float
     return finish(ctx);
 }
 
+template <bool LAYER>
+static void norm_launch(Context& ctx, int rows, int D, const float* x, float eps, const float* shift,
+                        const float* scale, __nv_bfloat16* y)
+{
+    const int warps = 8;
+    const dim3 grid((rows + warps - 1) / warps), block(warps * 32);
+    switch (D)
+    {
+    case 2560: ada_norm_kernel<10, LAYER><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
+    case 3072: ada_norm_kernel<12, LAYER><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
+    case 1536: ada_norm_kernel<6, LAYER><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
+    case 1024: ada_norm_kernel<4, LAYER><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
+    case 512: ada_norm_kernel<2, LAYER><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
+    case 256: ada_norm_kernel<1, LAYER><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
+    default: ada_norm_kernel<0, LAYER><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
+    }
+}
+
+int launch_ada_norm(Context& ctx, int rows, int D, const float* x, float eps, const float* shift, const float* scale,
+                    void* out, int layer)
+{
+    if (rows < 0 || D <= 0 || D % 8 || !aligned16(x) || !aligned16(shift) || !aligned16(scale) || !aligned16(out) ||
+        (layer != 0 && layer != 1))
+        return S2_ERR_INVALID;
+    if (rows == 0) return S2_OK;
+    ProfileScope prof(ctx, K_NORM, 0.0, (double)rows * D * 6.0);
+    __nv_bfloat16* y = (__nv_bfloat16*)out;
+    if (layer)
+        norm_launch<true>(ctx, rows, D, x, eps, shift, scale, y);
+    else
+        norm_launch<false>(ctx, rows, D, x, eps, shift, scale, y);
+    return finish(ctx);
+}
+
 int launch_ada_rmsnorm(Context& ctx, int rows, int D, const float* x, float eps, const float* shift,
                        const float* scale, void* out)
 {
-    if (rows < 0 || D <= 0 || D % 8 || !aligned16(x) || !aligned16(shift) || !aligned16(scale) || !aligned16(out))
-        return S2_ERR_INVALID;
-    if (rows == 0) return S2_OK;
-    const int warps = 8;
-    ProfileScope prof(ctx, K_NORM, 0.0, (double)rows * D * 6.0);
-    const dim3 grid((rows + warps - 1) / warps), block(warps * 32);
-    __nv_bfloat16* y = (__nv_bfloat16*)out;
-    switch (D)
-    {
-    case 2560: ada_rmsnorm_kernel<10><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
-    case 3072: ada_rmsnorm_kernel<12><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
-    case 1536: ada_rmsnorm_kernel<6><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
-    case 1024: ada_rmsnorm_kernel<4><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
-    case 512: ada_rmsnorm_kernel<2><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
-    case 256: ada_rmsnorm_kernel<1><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
-    default: ada_rmsnorm_kernel<0><<<grid, block, 0, ctx.stream>>>(rows, D, x, eps, shift, scale, y); break;
-    }
-    return finish(ctx);
+    return launch_ada_norm(ctx, rows, D, x, eps, shift, scale, out, 0);
 }
 
 static int launch_rows(Context& ctx, const void* src, const int* idx, int count, int row_elems, void* dst, int scatter)

@@ -319,6 +319,14 @@ int s2_ada_rmsnorm(s2_context* ctx, int rows, int D, const float* x, float eps, 
     return s2::launch_ada_rmsnorm(ctx->c, rows, D, x, eps, shift, scale, out_bf16);
 }
 
+int s2_ada_layernorm(s2_context* ctx, int rows, int D, const float* x, float eps, const float* shift,
+                     const float* scale, void* out_bf16)
+{
+    if (!ctx || !x || !shift || !scale || !out_bf16) return S2_ERR_INVALID;
+    if (cudaSetDevice(ctx->c.device) != cudaSuccess) return S2_ERR_CUDA;
+    return s2::launch_ada_norm(ctx->c, rows, D, x, eps, shift, scale, out_bf16, 1);
+}
+
 int s2_convert_f32_bf16(s2_context* ctx, const float* in, void* out, int64_t count)
 {
     if (!ctx || !in || !out) return S2_ERR_INVALID;

@@ -199,6 +199,9 @@ int launch_text_pool(Context& ctx, const AttnSchedule& s, int inner, const float
 
 int launch_ada_rmsnorm(Context& ctx, int rows, int D, const float* x, float eps, const float* shift,
                        const float* scale, void* out);
+// layer = 0: RMSNorm, 1: LayerNorm (both without affine), then * scale + shift -> bf16
+int launch_ada_norm(Context& ctx, int rows, int D, const float* x, float eps, const float* shift, const float* scale,
+                    void* out, int layer);
 
 // Token formats around the block stack (seedvr2_dit.cpp:167-326) and the
 // frontend / tail nets' dense passes.

@@ -25,7 +25,7 @@ def make_block_weights(rng, D, F, hd, pairs, bias=True):
                 qk_norm=1 + 0.02 * n(4, hd), rope_freqs=(1.0 / 10000 ** (np.arange(pairs) * 2 / (2 * pairs))))
 
 
-def run_case(gpu_ctx, s2lib, port, *, D, heads, F, shape, T, window, mode, blocks, seed, bias=True):
+def run_case(gpu_ctx, s2lib, port, *, D, heads, F, shape, T, window, mode, blocks, seed, bias=True, layer=()):
     import torch
 
     hd, pairs = 128, 21
@@ -40,6 +40,8 @@ def run_case(gpu_ctx, s2lib, port, *, D, heads, F, shape, T, window, mode, block
                     window=window, window_mode=mode, bias=bias)
     for b, w in enumerate(ws):
         dit.set_block_weights(b, w)
+        if b in layer:
+            dit.set_block_norm(b, True)
     x = torch.from_numpy(np.concatenate([xv, xt])).cuda()
     dit.forward(shape, T, x, torch.from_numpy(mod).cuda())
     torch.cuda.synchronize()
@@ -48,7 +50,7 @@ def run_case(gpu_ctx, s2lib, port, *, D, heads, F, shape, T, window, mode, block
 
     ref_v, ref_t = xv, xt
     for b, w in enumerate(ws):
-        dims = [D, heads, hd, F, pairs, mode, window[0], window[1], window[2], b & 1]
+        dims = [D, heads, hd, F, pairs, mode, window[0], window[1], window[2], b & 1, int(b in layer)]
         wo = dict(w)
         wo["freqs"] = wo.pop("rope_freqs")
         prev = np.concatenate([ref_v, ref_t])
@@ -77,6 +79,13 @@ def test_block_full_width_one_block(gpu_ctx, s2lib, port):
     got, ref, prev, x0 = run_case(gpu_ctx, s2lib, port, D=2560, heads=20, F=10240, shape=[2, 15, 20], T=58,
                                   window=[4, 3, 4], mode=0, blocks=1, seed=4)
     check(got, ref, x0)
+
+
+def test_block_layernorm_then_rmsnorm(gpu_ctx, s2lib, port):
+    """Per-block norm choice: block 0 with LayerNorm AdaLN passes, block 1 with RMSNorm, at D=512."""
+    got, ref, prev, x0 = run_case(gpu_ctx, s2lib, port, D=512, heads=4, F=2048, shape=[2, 12, 20], T=58,
+                                  window=[1, 8, 8], mode=1, blocks=2, seed=8, layer=(0,))
+    check(got, ref, prev)
 
 
 def test_block_no_bias_target_windows(gpu_ctx, s2lib, port):

@@ -99,6 +99,22 @@ def test_ada_rmsnorm_vs_torch(gpu_ctx, s2lib):
         np.testing.assert_allclose(y.float().cpu().numpy(), ref.cpu().numpy(), rtol=1e-2, atol=2e-2)
 
 
+def test_ada_layernorm_vs_torch(gpu_ctx, s2lib):
+    """The LayerNorm form of the AdaLN pass against torch's fp32 layer_norm (no affine), then scale + shift;
+    rows with a large common offset check that the variance is taken about the mean."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(3)
+    for rows, D in ((1, 8), (333, 2560), (58, 512), (17, 2000)):
+        x = 3 * torch.randn(rows, D, device="cuda", generator=g) + 20 * torch.randn(rows, 1, device="cuda",
+                                                                                 generator=g)
+        shift = torch.randn(D, device="cuda", generator=g)
+        scale = torch.randn(D, device="cuda", generator=g)
+        y = s2lib.ada_layernorm(gpu_ctx, x, 1e-5, shift, scale)
+        ref = torch.nn.functional.layer_norm(x, (D,), eps=1e-5) * scale + shift
+        np.testing.assert_allclose(y.float().cpu().numpy(), ref.cpu().numpy(), rtol=1e-2, atol=2e-2)
+
+
 def _awa_kwargs(g):
     return dict(heads=int(g["heads"]), head_dim=int(g["head_dim"]), window=[int(v) for v in g["target"]],
                 window_mode=0, eps=float(g["eps"]), rope_pairs=int(g["rope_pairs"]),

@@ -173,3 +173,44 @@ def test_block_oracle_bf16_emulation_close(port):
     for x, y in zip(b, a):
         assert cosine(x, y) >= 0.9995
         assert rel_maxabs(x, y) <= 2e-2
+
+
+@pytest.mark.parametrize("layer", [0, 1])
+def test_block_oracle_norm_forms_vs_numpy(port, layer):
+    """The block restatement's two AdaLN forms (RMSNorm, LayerNorm; no affine) against numpy glue in float64
+    around the restatement's own attention: h = norm(x) * scale + shift, QKV, AWA, out + gate residual,
+    norm, up, GELU-tanh, down + gate residual."""
+    rng = np.random.default_rng(11 + layer)
+    D, heads, hd, F, pairs = 256, 2, 128, 512, 21
+    shapes, tl = [[1, 6, 8]], [5]
+    w = dict(ada=(rng.standard_normal((6, D)) / np.sqrt(D) + np.array([0, 1, 0, 0, 1, 0])[:, None]),
+             w_qkv=0.02 * rng.standard_normal((3 * D, D)), b_qkv=0.02 * rng.standard_normal(3 * D),
+             w_out=0.02 * rng.standard_normal((D, D)), b_out=0.02 * rng.standard_normal(D),
+             w_up=0.02 * rng.standard_normal((F, D)), b_up=0.02 * rng.standard_normal(F),
+             w_down=0.02 * rng.standard_normal((D, F)), b_down=0.02 * rng.standard_normal(D),
+             qk_norm=1 + 0.02 * rng.standard_normal((4, hd)),
+             freqs=1.0 / 10000 ** (np.arange(pairs) * 2 / (2 * pairs)))
+    mod = rng.standard_normal((1, 6, D))
+    xv = rng.standard_normal((48, D)) + 3.0 * rng.standard_normal((48, 1))  # row offsets: mean matters
+    xt = rng.standard_normal((5, D))
+    dims = [D, heads, hd, F, pairs, oracle.WINDOW_EXTENT, 1, 3, 4, 1, layer]
+    gv, gt = port.block_forward(dims=dims, eps_norm=1e-5, eps_qk=1e-5, weights=w, modulation=mod, shapes=shapes,
+                                text_lengths=tl, x_video=xv, x_text=xt)
+
+    m = mod[0] + w["ada"]
+    x = np.concatenate([xv, xt]).astype(np.float64)
+
+    def norm(x, k):
+        c = x - x.mean(1, keepdims=True) if layer else x
+        return c / np.sqrt((c * c).mean(1, keepdims=True) + 1e-5) * m[k + 1] + m[k]
+
+    h = norm(x, 0)
+    qkv = h @ w["w_qkv"].T + w["b_qkv"]
+    cv, ct = port.awa_forward(heads=heads, head_dim=hd, window=[1, 3, 4], shifted=1, eps=1e-5, rope_pairs=pairs,
+                              norms=w["qk_norm"], freqs=w["freqs"], shapes=shapes, text_lengths=tl,
+                              video_qkv=qkv[:48], text_qkv=qkv[48:], mode=oracle.WINDOW_EXTENT)
+    x = x + (np.concatenate([cv, ct]) @ w["w_out"].T + w["b_out"]) * m[2]
+    u = norm(x, 3) @ w["w_up"].T + w["b_up"]
+    u = 0.5 * u * (1 + np.tanh(0.7978845608028654 * (u + 0.044715 * u ** 3)))
+    x = x + (u @ w["w_down"].T + w["b_down"]) * m[5]
+    np.testing.assert_allclose(np.concatenate([gv, gt]), x, rtol=2e-4, atol=2e-4)
