@@ -202,6 +202,24 @@ int s2_ada_rmsnorm(s2_context* ctx, int rows, int D, const float* x, float eps, 
  * var the biased variance, no affine of its own. */
 int s2_ada_layernorm(s2_context* ctx, int rows, int D, const float* x, float eps, const float* shift,
                      const float* scale, void* out_bf16);
+/* ncnn built-in layers a DiT block graph places between the custom layers
+ * (ncnn's BinaryOp, RMSNorm, LayerNorm and GELU; used by the graph executor
+ * of the ncnn-surface library), on fp32 row-major device blobs.
+ * s2_binary_op: out[r][c] = a[r][c] op b[r][c], or b[0][c] for every row when
+ * b_rows == 1 (ncnn's broadcast of a [1][cols] blob); op = ncnn's op_type
+ * 0 add, 1 sub, 2 mul, 3 div; cols % 4 == 0, 16-byte aligned pointers.
+ * s2_norm_f32: layer = 0 RMSNorm, 1 LayerNorm over each row of D values,
+ * then * gamma[c] and + beta[c] when given (NULL = none).
+ * s2_gelu_f32: fast = 1 the tanh approximation, 0 the erf form. */
+#define S2_BINARY_ADD 0
+#define S2_BINARY_SUB 1
+#define S2_BINARY_MUL 2
+#define S2_BINARY_DIV 3
+int s2_binary_op(s2_context* ctx, int op, int rows, int cols, const float* a, const float* b, int b_rows, float* out);
+int s2_norm_f32(s2_context* ctx, int layer, int rows, int D, const float* x, float eps, const float* gamma,
+                const float* beta, float* out);
+int s2_gelu_f32(s2_context* ctx, int fast, int64_t count, const float* x, float* out);
+
 /* fp32 -> bf16 (round to nearest even). */
 int s2_convert_f32_bf16(s2_context* ctx, const float* in, void* out, int64_t count);
 /* Number of NaN / Inf values among `count` device elements of dtype

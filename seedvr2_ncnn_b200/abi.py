@@ -49,7 +49,7 @@ EXPORTED = [
     "s2_plan_build", "s2_plan_info", "s2_plan_copy", "s2_plan_free", "s2_plan_schedule_copy",
     "s2_awa_forward", "s2_awa_forward_static", "s2_awa_static_status", "s2_shared_linear", "s2_ada_rmsnorm", "s2_ada_layernorm",
     "s2_convert_f32_bf16",
-    "s2_count_nonfinite",
+    "s2_count_nonfinite", "s2_binary_op", "s2_norm_f32", "s2_gelu_f32",
     "s2_dit_create", "s2_dit_free", "s2_dit_set_block_weights", "s2_dit_set_block_norm", "s2_dit_init_random",
     "s2_dit_forward",
     "s2_dit_set_check_finite", "s2_dit_nonfinite_report", "s2_dit_set_checkpoints",
@@ -159,6 +159,9 @@ def lib() -> C.CDLL:
     L.s2_shared_linear.argtypes = [vp, ip, ip, ip, ip, vp, vp, vp, vp, ip, vp, ip, vp, vp]
     L.s2_ada_rmsnorm.argtypes = [vp, ip, ip, vp, C.c_float, vp, vp, vp]
     L.s2_ada_layernorm.argtypes = [vp, ip, ip, vp, C.c_float, vp, vp, vp]
+    L.s2_binary_op.argtypes = [vp, ip, ip, ip, vp, vp, ip, vp]
+    L.s2_norm_f32.argtypes = [vp, ip, ip, ip, vp, C.c_float, vp, vp, vp]
+    L.s2_gelu_f32.argtypes = [vp, ip, i64, vp, vp]
     L.s2_dit_set_block_norm.argtypes = [vp, ip, ip]
     L.s2_convert_f32_bf16.argtypes = [vp, vp, vp, i64]
     L.s2_dit_create.argtypes = [vp, C.POINTER(DitConfig), C.POINTER(vp)]

@@ -261,6 +261,11 @@ int conv3d_gemm(Context& ctx, const Conv3dGeometry& g, const void* X, int frames
                 float* out, int64_t out_cstep);
 
 int launch_convert_f32_bf16(Context& ctx, const float* in, void* out, int64_t count);
+// ncnn built-ins of a block graph (graph_ops.cu), fp32 [rows][cols]
+int launch_binary_op(Context& ctx, int op, int rows, int cols, const float* a, const float* b, int b_rows, float* out);
+int launch_norm_f32(Context& ctx, int layer, int rows, int D, const float* x, float eps, const float* gamma,
+                    const float* beta, float* y);
+int launch_gelu_f32(Context& ctx, int fast, int64_t count, const float* x, float* y);
 int launch_add_vectors(Context& ctx, const float* a, const float* b, float* out, int count, int period);
 // *count += NaN / Inf elements of x[0, n) (dtype S2_DTYPE_F32 or S2_DTYPE_BF16)
 int launch_count_nonfinite(Context& ctx, const void* x, int64_t n, int dtype, unsigned long long* count);
