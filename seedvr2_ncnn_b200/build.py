@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libseedvr2_cuda.so")
 LAYER_LIB = os.path.join(HERE, "libseedvr2_ncnn.so")
-LAYER_SOURCES = ["adaptive_window_attention.cpp", "shared_linear.cpp", "vae_layers.cpp", "layer_capi.cpp"]
+LAYER_SOURCES = ["adaptive_window_attention.cpp", "shared_linear.cpp", "vae_layers.cpp", "net.cpp", "layer_capi.cpp"]
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 ROOT = os.path.dirname(HERE)
 

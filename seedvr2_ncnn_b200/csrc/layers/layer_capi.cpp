@@ -4,9 +4,12 @@
 // without a C++ toolchain (ctypes, tests) can exercise the same layer surface
 // the reference's block graph uses.  Argument order matches the oracle's
 // reference driver, so parity tests call both the same way.
+#include <cuda_runtime.h>
+
 #include <cstring>
 #include <vector>
 
+#include "net.h"
 #include "shared_linear.h"
 #include "vae_layers.h"
 
@@ -286,6 +289,95 @@ int s2layer_mha_forward(void* handle, const float* x, int tokens, int qdim, floa
     const int r = layer->forward(bottom, top, opt);
     if (r != 0) return r;
     std::memcpy(out, top.data, (size_t)top.w * top.h * 4);
+    return 0;
+}
+
+// ---------------------------------------------------------------- graph
+// A block graph read from ncnn .param / .bin files with SeedVR2's two custom
+// layers registered the way seedvr2_dit.cpp:614-618 registers them
+// (AdaptiveWindowAttention with the caller-mutated runtime state as its
+// userdata, SharedLinear), run on device blobs by name.
+struct S2Net
+{
+    seedvr2::Net net;
+    seedvr2::AdaptiveWindowRuntimeState state;
+};
+
+void* s2net_create(void)
+{
+    S2Net* h = new S2Net;
+    h->net.register_custom_layer("AdaptiveWindowAttention", seedvr2::adaptive_window_attention_layer_creator, 0,
+                                 &h->state);
+    h->net.register_custom_layer("SharedLinear", seedvr2::shared_linear_layer_creator);
+    return h;
+}
+
+void s2net_destroy(void* h)
+{
+    delete static_cast<S2Net*>(h);
+}
+
+int s2net_load(void* h, const char* param_path, const char* bin_path)
+{
+    if (!h) return -1;
+    S2Net* n = static_cast<S2Net*>(h);
+    const int r = n->net.load_param(param_path);
+    return r != 0 ? r : n->net.load_model(bin_path);
+}
+
+int s2net_info(void* h, int* layers, int* blobs)
+{
+    if (!h || !layers || !blobs) return -1;
+    S2Net* n = static_cast<S2Net*>(h);
+    *layers = n->net.layer_count();
+    *blobs = n->net.blob_count();
+    return 0;
+}
+
+// The runtime state read by the attention layers at the next extract
+// (seedvr2_dit.cpp:724-725 sets it before each extract).
+int s2net_set_runtime(void* h, const int* shapes, const int* text_lengths, int batch)
+{
+    if (!h || !shapes || !text_lengths || batch <= 0) return -1;
+    S2Net* n = static_cast<S2Net*>(h);
+    n->state.video_shapes.assign(batch, {0, 0, 0});
+    n->state.text_lengths.assign(text_lengths, text_lengths + batch);
+    for (int b = 0; b < batch; b++)
+        n->state.video_shapes[b] = {shapes[3 * b], shapes[3 * b + 1], shapes[3 * b + 2]};
+    return 0;
+}
+
+// Inputs: fp32 device blobs [rows][cols] by name; outputs: each named blob
+// is computed and copied into the caller's fp32 device buffer of the given
+// shape (-1 on a shape mismatch).  Synchronous.
+int s2net_extract_cuda(void* h, int n_in, const char* const* in_names, void* const* in_ptrs, const int* in_rows,
+                       const int* in_cols, int n_out, const char* const* out_names, void* const* out_ptrs,
+                       const int* out_rows, const int* out_cols)
+{
+    if (!h || n_in < 0 || n_out <= 0) return -1;
+    S2Net* n = static_cast<S2Net*>(h);
+    seedvr2::Extractor ex = n->net.create_extractor();
+    for (int i = 0; i < n_in; i++)
+    {
+        seedvr2::CudaBlob b;
+        b.data = in_ptrs[i];
+        b.w = in_cols[i];
+        b.h = in_rows[i];
+        b.ld = in_cols[i];
+        b.dtype = S2_DTYPE_F32;
+        const int r = ex.input_cuda(in_names[i], b);
+        if (r != 0) return r;
+    }
+    for (int i = 0; i < n_out; i++)
+    {
+        seedvr2::CudaBlob b;
+        int r = ex.extract_cuda(out_names[i], b);
+        if (r != 0) return r;
+        if (b.w != out_cols[i] || b.h != out_rows[i]) return -1;
+        if ((r = s2_status(seedvr2::layer_context())) != 0) return r;
+        if (cudaMemcpy(out_ptrs[i], b.data, (size_t)b.w * b.h * 4, cudaMemcpyDeviceToDevice) != cudaSuccess)
+            return S2_ERR_CUDA;
+    }
     return 0;
 }
 

@@ -42,6 +42,16 @@ def lib() -> C.CDLL:
         L.s2layer_mha_create.argtypes = [i32p, C.c_float, f32p, C.c_size_t, C.POINTER(C.c_void_p)]
         L.s2layer_mha_forward.argtypes = [C.c_void_p, f32p, C.c_int, C.c_int, f32p]
         L.s2layer_vae_free.restype = None
+        vp = C.c_void_p
+        L.s2net_create.restype = vp
+        L.s2net_create.argtypes = []
+        L.s2net_destroy.argtypes = [vp]
+        L.s2net_destroy.restype = None
+        L.s2net_load.argtypes = [vp, C.c_char_p, C.c_char_p]
+        L.s2net_info.argtypes = [vp, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.s2net_set_runtime.argtypes = [vp, i32p, i32p, C.c_int]
+        L.s2net_extract_cuda.argtypes = [vp, C.c_int, C.POINTER(C.c_char_p), C.POINTER(vp), i32p, i32p, C.c_int,
+                                         C.POINTER(C.c_char_p), C.POINTER(vp), i32p, i32p]
         L.s2layer_vae_reset.restype = None
         _lib = L
     return _lib
@@ -208,6 +218,54 @@ class VaeMhaLayer:
     def close(self):
         if self.handle:
             lib().s2layer_vae_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Net:
+    """A block graph from ncnn .param / .bin files (seedvr2::Net) with SeedVR2's AdaptiveWindowAttention and
+    SharedLinear registered; blobs by name on the device."""
+
+    def __init__(self, param_path, bin_path):
+        self.handle = C.c_void_p(lib().s2net_create())
+        r = lib().s2net_load(self.handle, str(param_path).encode(), str(bin_path).encode())
+        if r != 0:
+            self.close()
+            raise LayerError("Net load", r)
+
+    def info(self):
+        n, b = C.c_int(), C.c_int()
+        lib().s2net_info(self.handle, C.byref(n), C.byref(b))
+        return n.value, b.value
+
+    def set_runtime(self, shapes, text_lengths):
+        sh = np.ascontiguousarray(np.asarray(shapes, np.int32).reshape(-1, 3))
+        tl = np.ascontiguousarray(np.asarray(text_lengths, np.int32))
+        r = lib().s2net_set_runtime(self.handle, sh, tl, len(tl))
+        if r != 0:
+            raise LayerError("Net set_runtime", r)
+
+    def extract(self, inputs: dict, outputs: dict):
+        """inputs / outputs: name -> contiguous fp32 CUDA tensor [rows][cols] (outputs are written)."""
+        def arr(d):
+            names = (C.c_char_p * len(d))(*[k.encode() for k in d])
+            ptrs = (C.c_void_p * len(d))(*[t.data_ptr() for t in d.values()])
+            rows = np.ascontiguousarray([t.shape[0] for t in d.values()], np.int32)
+            cols = np.ascontiguousarray([t.shape[1] for t in d.values()], np.int32)
+            return names, ptrs, rows, cols
+        i, o = arr(inputs), arr(outputs)
+        r = lib().s2net_extract_cuda(self.handle, len(inputs), *i, len(outputs), *o)
+        if r != 0:
+            raise LayerError("Net extract", r)
+
+    def close(self):
+        if self.handle:
+            lib().s2net_destroy(self.handle)
             self.handle = None
 
     def __del__(self):
