@@ -6,6 +6,7 @@
 #include <cstdio>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <sstream>
 
 #include "shared_linear.h"
@@ -109,17 +110,44 @@ bool read_file(const char* path, std::vector<unsigned char>& out)
     return ok;
 }
 
-std::shared_ptr<void> device_alloc(size_t bytes)
-{
-    void* p = nullptr;
-    if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) return nullptr;
-    return std::shared_ptr<void>(p, [](void* q) { cudaFree(q); });
-}
-
 } // namespace
 
 // ---------------------------------------------------------------- Net
-Net::Net() {}
+// Freed blocks are kept by size and handed out again for requests of up to
+// their size (and at least half of it); everything is released with the Net.
+struct Net::Pool
+{
+    std::mutex m;
+    std::multimap<size_t, void*> free_blocks;
+    ~Pool()
+    {
+        for (auto& kv : free_blocks) cudaFree(kv.second);
+    }
+};
+
+std::shared_ptr<void> Net::blob_alloc(size_t bytes) const
+{
+    bytes = (bytes + 255) & ~size_t(255);
+    std::shared_ptr<Pool> p = pool;
+    void* ptr = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(p->m);
+        auto it = p->free_blocks.lower_bound(bytes);
+        if (it != p->free_blocks.end() && it->first <= 2 * bytes)
+        {
+            ptr = it->second;
+            bytes = it->first;
+            p->free_blocks.erase(it);
+        }
+    }
+    if (!ptr && cudaMalloc(&ptr, bytes ? bytes : 256) != cudaSuccess) return nullptr;
+    return std::shared_ptr<void>(ptr, [p, bytes](void* q) {
+        std::lock_guard<std::mutex> lock(p->m);
+        p->free_blocks.emplace(bytes, q);
+    });
+}
+
+Net::Net() : pool(std::make_shared<Pool>()) {}
 
 Net::~Net()
 {
@@ -368,7 +396,7 @@ Extractor::~Extractor() {}
 
 int Extractor::alloc(Slot& s, int w, int h)
 {
-    std::shared_ptr<void> p = device_alloc((size_t)w * h * 4);
+    std::shared_ptr<void> p = net->blob_alloc((size_t)w * h * 4);
     if (!p) return -100;
     const size_t idx = &s - slots.data();
     mem[idx] = p;
@@ -490,7 +518,7 @@ int Extractor::run_layer(int li, int depth)
         if (e.with_scalar)
         {
             std::vector<float> v((size_t)a.w, e.scalar);
-            scalar_mem = device_alloc((size_t)a.w * 4);
+            scalar_mem = net->blob_alloc((size_t)a.w * 4);
             if (!scalar_mem) return -100;
             if (cudaMemcpy(scalar_mem.get(), v.data(), v.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
             b.data = scalar_mem.get();
@@ -532,7 +560,7 @@ int Extractor::run_layer(int li, int depth)
         for (int k = 0; k < 2; k++)
         {
             const CudaBlob& x = in(k);
-            tmp[k] = device_alloc((size_t)x.w * x.h * 2);
+            tmp[k] = net->blob_alloc((size_t)x.w * x.h * 2);
             if (!tmp[k]) return -100;
             if ((r = s2_convert_f32_bf16(ctx, static_cast<const float*>(x.data), tmp[k].get(), (int64_t)x.w * x.h)) != 0)
                 return r;

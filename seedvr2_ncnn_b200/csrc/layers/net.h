@@ -85,6 +85,12 @@ private:
     int load_weights(const ncnn::ModelBin& mb);
     int upload(const Entry& e) const;
 
+    // device memory of the blobs: a caching pool (ncnn's PoolAllocator
+    // role) so repeated extractions allocate nothing once warm
+    std::shared_ptr<void> blob_alloc(size_t bytes) const;
+    struct Pool;
+    std::shared_ptr<Pool> pool;
+
     std::vector<Custom> customs;
     std::vector<Entry> layers;
     std::vector<std::string> blob_names;

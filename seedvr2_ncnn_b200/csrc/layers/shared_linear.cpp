@@ -7,6 +7,28 @@
 
 namespace seedvr2 {
 
+namespace {
+
+// Grow-only device staging of the host-blob forward (one per host thread):
+// repeated calls of the same or smaller size allocate nothing.
+struct Staging
+{
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    void* get(size_t want)
+    {
+        if (want <= bytes) return ptr;
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+        if (cudaMalloc(&ptr, want) != cudaSuccess) return nullptr;
+        bytes = want;
+        return ptr;
+    }
+};
+
+} // namespace
+
 SharedLinear::SharedLinear()
     : num_output(0), num_input(0), bias_term(false), d_weight(nullptr), d_bias(nullptr)
 {
@@ -95,11 +117,12 @@ int SharedLinear::forward(const std::vector<ncnn::Mat>& bottom_blobs, std::vecto
     top_blobs[0].create(num_output, m0, 4u, opt.blob_allocator);
     top_blobs[1].create(num_output, m1, 4u, opt.blob_allocator);
     if (top_blobs[0].empty() || top_blobs[1].empty()) return -100;
-    // staging: fp32 inputs, bf16 inputs, fp32 outputs
+    // staging: fp32 inputs, bf16 inputs, fp32 outputs (grow-only, per host thread)
     const size_t K = num_input, N = num_output, M = (size_t)m0 + m1;
-    uint8_t* buf = nullptr;
     const size_t b_in32 = (M * K * 4 + 255) & ~size_t(255), b_in16 = (M * K * 2 + 255) & ~size_t(255);
-    if (cudaMalloc(&buf, b_in32 + b_in16 + M * N * 4 + 256) != cudaSuccess) return -100;
+    static thread_local Staging staging;
+    uint8_t* buf = static_cast<uint8_t*>(staging.get(b_in32 + b_in16 + M * N * 4 + 256));
+    if (!buf) return -100;
     float* in32 = reinterpret_cast<float*>(buf);
     uint8_t* in16 = buf + b_in32;
     float* out = reinterpret_cast<float*>(buf + b_in32 + b_in16);
@@ -119,7 +142,6 @@ int SharedLinear::forward(const std::vector<ncnn::Mat>& bottom_blobs, std::vecto
          cudaMemcpy(top_blobs[1].data, out + (size_t)m0 * N, (size_t)m1 * N * 4, cudaMemcpyDeviceToHost) !=
              cudaSuccess))
         r = S2_ERR_CUDA;
-    cudaFree(buf);
     return r;
 }
 
