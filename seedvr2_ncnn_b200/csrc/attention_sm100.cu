@@ -13,8 +13,8 @@
 //   warps 0-3   softmax + epilogue of query tile 0   (200 registers each)
 //   warps 4-7   softmax + epilogue of query tile 1   (200 registers each)
 //   warp 8      TMA: Q pair per unit, K tiles into a 3-slot ring
-//   warp 9      MMA: the warp runs the issue loop, one elected lane issues
-//               every tcgen05.mma
+//   warp 9      MMA: the warp runs the issue loop, lane 0 issues every
+//               tcgen05.mma
 //   warp 10     TMA: V tiles into a 2-slot ring
 //   warp 11     idle (the warpgroup gives its registers to the softmax)
 // `setmaxnreg` moves registers from the TMA / MMA warpgroup (104 each) to the
@@ -267,15 +267,6 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&v)[128], int rem, uin
         sum2[q & 3] = fadd2(sum2[q & 3], pk2(__float_as_uint(e0), __float_as_uint(e1)));
     }
     tmem_st16(p_addr + C * 16, p);
-}
-
-// One lane of the (fully active) warp, the same on every call.
-__device__ __forceinline__ bool elect_one()
-{
-    uint32_t p;
-    asm volatile(
-        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\tselp.u32 %0, 1, 0, e;\n\t}" : "=r"(p));
-    return p != 0;
 }
 
 __device__ __forceinline__ float bf16_round_f32(float x)
@@ -616,11 +607,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         {
             // ---------------- MMA issuer.  The whole warp runs the loop, the
             // waits and the descriptor arithmetic (warp-uniform values, which
-            // the compiler keeps in uniform registers), and one elected lane
-            // issues each tcgen05.mma / commit: issued from a lone lane with
-            // per-thread descriptors, an MMA costs ~160 cycles of issue, more
-            // than the 64 cycles a 128 x 128 x 16 MMA takes to execute.
-            const bool leader = elect_one();
+            // the compiler keeps in uniform registers), and lane 0 issues each
+            // tcgen05.mma / commit: issued from a lone lane with per-thread
+            // descriptors, an MMA costs ~160 cycles of issue, more than the
+            // 64 cycles a 128 x 128 x 16 MMA takes to execute.
+            const bool leader = lane == 0;
             bool any = false;
             bool ok = true;
             int gk = 0, gv = 0, it = 0;
