@@ -13,8 +13,7 @@
 //   warps 0-3   softmax + epilogue of query tile 0   (200 registers each)
 //   warps 4-7   softmax + epilogue of query tile 1   (200 registers each)
 //   warp 8      TMA: Q pair per unit, K tiles into a 3-slot ring
-//   warp 9      MMA: the warp runs the issue loop, lane 0 issues every
-//               tcgen05.mma
+//   warp 9      MMA: one thread issues every tcgen05.mma
 //   warp 10     TMA: V tiles into a 2-slot ring
 //   warp 11     idle (the warpgroup gives its registers to the softmax)
 // `setmaxnreg` moves registers from the TMA / MMA warpgroup (104 each) to the
@@ -603,15 +602,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int s = 0; s < V_STAGES; s++)
                     if (v_issued[s]) drain_wait(&v_full[s], v_par[s]);
         }
-        else if (warp == 9)
+        else if (warp == 9 && lane == 0)
         {
-            // ---------------- MMA issuer.  The whole warp runs the loop, the
-            // waits and the descriptor arithmetic (warp-uniform values, which
-            // the compiler keeps in uniform registers), and lane 0 issues each
-            // tcgen05.mma / commit: issued from a lone lane with per-thread
-            // descriptors, an MMA costs ~160 cycles of issue, more than the
-            // 64 cycles a 128 x 128 x 16 MMA takes to execute.
-            const bool leader = lane == 0;
+            // ---------------- MMA issuer
             bool any = false;
             bool ok = true;
             int gk = 0, gv = 0, it = 0;
@@ -621,35 +614,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint64_t k_desc0 = umma_desc_sw128(smem_u32(sK), 16, 1024);
             const uint64_t v_desc0 = umma_desc_sw128(smem_u32(sV), CHUNK_BYTES, 1024);
             constexpr uint32_t kTileDesc = TILE_BYTES >> 4;
-            auto wwait = [&](uint64_t* bar, uint32_t parity) { return warp_wait(bar, parity, abort_flag, args.status); };
-            auto commit = [&](uint64_t* bar) {
-                if (leader) umma_commit(bar);
-                __syncwarp();
-            };
             for (int w = blockIdx.x; w < args.num_work && ok; w += gridDim.x, it++)
             {
                 const Work wk = decode_work(args, w);
                 const int ntiles = wk.has_b ? 2 : 1;
-                // S_x = Q_x K^T for key tile j (K ring slot ks); a ragged last
-                // tile runs with N = its keys rounded up to 16.
-                auto issue_s = [&](int x, int ks, int j) {
+                // S_x = Q_x K^T for key tile j (ring slot of K tile gkk); a ragged
+                // last tile runs with N = its keys rounded up to 16.
+                auto issue_s = [&](int x, int gkk, int j) {
                     const int valid = wk.S_len - j * TILE;
                     const int n = valid >= TILE ? TILE : ((valid + 15) & ~15);
                     const uint32_t idesc = umma_idesc_bf16(128, n, 0, 0);
                     const uint64_t qd = q_desc0 + (x ? kTileDesc : 0u);
-                    const uint64_t kd = k_desc0 + (uint32_t)ks * kTileDesc;
+                    const uint64_t kd = k_desc0 + (uint32_t)(gkk % K_STAGES) * kTileDesc;
                     const uint32_t d = tmem + x * 128;
-                    if (leader)
-                    {
-                        umma_bf16_i<0>(d, qd, kd, idesc);
+                    umma_bf16_i<0>(d, qd, kd, idesc);
 #pragma unroll
-                        for (int k = 1; k < HD / 16; k++)
-                        {
-                            const uint32_t off = ((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4;
-                            umma_bf16_i<1>(d, qd + off, kd + off, idesc);
-                        }
+                    for (int k = 1; k < HD / 16; k++)
+                    {
+                        const uint32_t off = ((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4;
+                        umma_bf16_i<1>(d, qd + off, kd + off, idesc);
                     }
-                    __syncwarp();
                 };
                 // O_x (+)= P_x V(j): P from tensor memory (packed bf16 over the
                 // first 64 columns of S_x), 16 keys per MMA
@@ -658,31 +642,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t p_tmem = tmem + x * 128;
                     const uint32_t o_tmem = tmem + 256 + x * 128;
                     const uint64_t vd = v_desc0 + (uint32_t)vslot * kTileDesc;
-                    if (leader)
+                    if (valid >= TILE)
                     {
-                        if (valid >= TILE)
-                        {
-                            if (j == 0)
-                                umma_bf16_tmem_a_i<0>(o_tmem, p_tmem, vd, IDESC_O);
-                            else
-                                umma_bf16_tmem_a_i<1>(o_tmem, p_tmem, vd, IDESC_O);
-#pragma unroll
-                            for (int k = 1; k < TILE / 16; k++)
-                                umma_bf16_tmem_a_i<1>(o_tmem, p_tmem + k * 8, vd + ((k * 16 * 128) >> 4), IDESC_O);
-                        }
+                        if (j == 0)
+                            umma_bf16_tmem_a_i<0>(o_tmem, p_tmem, vd, IDESC_O);
                         else
-                        {
-                            const int ksteps = (valid + 15) / 16;
-                            for (int k = 0; k < ksteps; k++)
-                                umma_bf16_tmem_a(o_tmem, p_tmem + k * 8, vd + ((k * 16 * 128) >> 4), IDESC_O,
-                                                 (j | k) != 0);
-                        }
+                            umma_bf16_tmem_a_i<1>(o_tmem, p_tmem, vd, IDESC_O);
+#pragma unroll
+                        for (int k = 1; k < TILE / 16; k++)
+                            umma_bf16_tmem_a_i<1>(o_tmem, p_tmem + k * 8, vd + ((k * 16 * 128) >> 4), IDESC_O);
                     }
-                    __syncwarp();
+                    else
+                    {
+                        const int ksteps = (valid + 15) / 16;
+                        for (int k = 0; k < ksteps; k++)
+                            umma_bf16_tmem_a(o_tmem, p_tmem + k * 8, vd + ((k * 16 * 128) >> 4), IDESC_O,
+                                             (j | k) != 0);
+                    }
                 };
-                int ks = gk % K_STAGES;
-                uint32_t kpar = (uint32_t)(gk / K_STAGES) & 1u;
-                if (!wwait(q_full, it & 1) || !wwait(&k_full[ks], kpar))
+                auto wait_k = [&](int g_) {
+                    return mbar_wait(&k_full[g_ % K_STAGES], (uint32_t)(g_ / K_STAGES) & 1u, abort_flag, args.status);
+                };
+                if (!mbar_wait(q_full, it & 1, abort_flag, args.status) || !wait_k(gk))
                 {
                     ok = false;
                     break;
@@ -690,32 +671,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tc_fence_after();
                 for (int x = 0; x < ntiles; x++)
                 {
-                    issue_s(x, ks, 0);
-                    commit(&s_full[x]);
+                    issue_s(x, gk, 0);
+                    umma_commit(&s_full[x]);
                 }
                 any = true;
-                commit(&k_empty[ks]);
+                umma_commit(&k_empty[gk % K_STAGES]);
                 gk++;
-                if (wk.nkv == 1) commit(q_empty);
+                if (wk.nkv == 1) umma_commit(q_empty);
                 for (int j = 0; j < wk.nkv && ok; j++)
                 {
                     const int vs = gv % V_STAGES;
-                    if (!wwait(&v_full[vs], (uint32_t)(gv / V_STAGES) & 1u))
+                    if (!mbar_wait(&v_full[vs], (uint32_t)(gv / V_STAGES) & 1u, abort_flag, args.status))
                     {
                         ok = false;
                         break;
                     }
                     const bool more = j + 1 < wk.nkv;
-                    ks = gk % K_STAGES;
-                    kpar = (uint32_t)(gk / K_STAGES) & 1u;
-                    if (more && !wwait(&k_full[ks], kpar))
+                    if (more && !wait_k(gk))
                     {
                         ok = false;
                         break;
                     }
                     for (int x = 0; x < ntiles; x++)
                     {
-                        if (!wwait(&p_full[x], pfull[x] & 1u))
+                        if (!mbar_wait(&p_full[x], pfull[x] & 1u, abort_flag, args.status))
                         {
                             ok = false;
                             break;
@@ -723,30 +702,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         pfull[x]++;
                         tc_fence_after();
                         issue_pv(x, j, vs);
-                        if (x == ntiles - 1) commit(&v_empty[vs]);
+                        if (x == ntiles - 1) umma_commit(&v_empty[vs]);
                         if (more)
                         {
-                            issue_s(x, ks, j + 1);
-                            commit(&s_full[x]);
+                            issue_s(x, gk, j + 1);
+                            umma_commit(&s_full[x]);
                         }
                         else
-                            commit(&o_done[x]);
+                            umma_commit(&o_done[x]);
                     }
                     if (!ok) break;
                     gv++;
                     if (more)
                     {
-                        commit(&k_empty[ks]);
+                        umma_commit(&k_empty[gk % K_STAGES]);
                         gk++;
-                        if (j + 2 == wk.nkv) commit(q_empty); // the unit's last S MMAs
+                        if (j + 2 == wk.nkv) umma_commit(q_empty); // the unit's last S MMAs
                     }
                 }
             }
             if (any)
             {
-                commit(drain);
-                if (lane == 0) drain_wait(drain, 0);
-                __syncwarp();
+                umma_commit(drain);
+                drain_wait(drain, 0);
             }
         }
     }

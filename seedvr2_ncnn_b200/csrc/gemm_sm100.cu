@@ -85,7 +85,6 @@ struct GemmArgs
     int M0, M1, N, K;
     int mblk0, mblk1, nblk, num_tiles, num_kb;
     int group_m; // M blocks per raster group (tiles walk M fastest inside a group)
-    int a_evict_first; // A rows are streamed once (long K): load them with an L2 evict-first policy
     int epilogue;
     int out_f32;
     int tma_out; // outputs written through tmap_o0 / tmap_o1
@@ -763,10 +762,6 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
             int issued[STAGES];
             uint32_t last_phase[STAGES];
             for (int s = 0; s < STAGES; s++) issued[s] = 0, last_phase[s] = 0;
-            // the weight is read by every M block: keep it in L2 ahead of the
-            // activation rows that stream past it
-            const uint64_t pol_w = l2_policy_evict_last();
-            const uint64_t pol_a = l2_policy_evict_first();
             for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x)
             {
                 int stream, m0, n0;
@@ -778,11 +773,8 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                     uint8_t* sa = smem + stage * STAGE_BYTES;
                     uint8_t* sb = sa + A_BYTES;
                     mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-                    if (args.a_evict_first)
-                        tma_load_2d_hint(sa, ta, &full[stage], kb * BK, m0, pol_a);
-                    else
-                        tma_load_2d(sa, ta, &full[stage], kb * BK, m0);
-                    tma_load_2d_hint(sb, &tmap_w, &full[stage], kb * BK, n0, pol_w);
+                    tma_load_2d(sa, ta, &full[stage], kb * BK, m0);
+                    tma_load_2d(sb, &tmap_w, &full[stage], kb * BK, n0);
                     issued[stage] = 1;
                     last_phase[stage] = phase;
                     if (++stage == STAGES)
@@ -1031,8 +1023,6 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
             int issued[STAGES];
             uint32_t last_phase[STAGES];
             for (int s = 0; s < STAGES; s++) issued[s] = 0, last_phase[s] = 0;
-            const uint64_t pol_w = l2_policy_evict_last();
-            const uint64_t pol_a = l2_policy_evict_first();
             for (int t = walk.first(); t < args.num_tiles && !*abort_flag; t += walk.step())
             {
                 int stream, m0, n0p;
@@ -1047,11 +1037,8 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                     uint8_t* sb = sa + TL::A_STAGE;
                     if (leader) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
                     const uint32_t fb = mapa_shared(&full[stage], 0);
-                    if (args.a_evict_first)
-                        tma_load_2d_pair_hint(sa, ta, fb, kb * BK, m0, pol_a);
-                    else
-                        tma_load_2d_pair(sa, ta, fb, kb * BK, m0);
-                    tma_load_2d_pair_hint(sb, &tmap_w, fb, kb * BK, nb, pol_w);
+                    tma_load_2d_pair(sa, ta, fb, kb * BK, m0);
+                    tma_load_2d_pair(sb, &tmap_w, fb, kb * BK, nb);
                     issued[stage] = 1;
                     last_phase[stage] = phase;
                     if (++stage == STAGES)
@@ -1315,9 +1302,6 @@ int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const
     // short-K ones (attention out) a medium group; measured on the 720p
     // shapes (differences of 2-4 %).
     a.group_m = K >= 8192 ? 1 : (N <= 4096 ? 8 : 16);
-    // and the long-K activation is streamed once: it goes first from L2, so
-    // the weight (kept with evict-last on every load) stays resident
-    a.a_evict_first = K >= 8192;
     return make_tmap_bf16_2d(&tw, W, K, N, (uint64_t)K * 2, BK, mode == TILE_256 ? 256 : 128);
 }
 

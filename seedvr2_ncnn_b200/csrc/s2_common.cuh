@@ -154,33 +154,6 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* desc, ui
         : "memory");
 }
 
-// L2 eviction priority of a load (createpolicy): operands read again by
-// other tiles (a GEMM's weight) are kept (evict_last); operands streamed once
-// (a long-K GEMM's activation rows) go first (evict_first).
-__device__ __forceinline__ uint64_t l2_policy_evict_last()
-{
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
-
-__device__ __forceinline__ uint64_t l2_policy_evict_first()
-{
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
-
-__device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const void* desc, uint64_t* bar, int x, int y,
-                                                 uint64_t policy)
-{
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
-        "%3}], [%4], %5;" ::"r"(smem_u32(smem_dst)),
-        "l"(desc), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
-        : "memory");
-}
-
 // Tiled 2D prefetch of one box into L2 (no shared-memory destination).
 __device__ __forceinline__ void tma_prefetch_l2_2d(const void* desc, int x, int y)
 {
@@ -343,17 +316,6 @@ __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* des
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.cta_group::2 [%0], [%1, {%2, "
         "%3}], [%4];" ::"r"(smem_u32(smem_dst)),
         "l"(desc), "r"(x), "r"(y), "r"(bar_cluster)
-        : "memory");
-}
-
-// The same with an L2 eviction policy.
-__device__ __forceinline__ void tma_load_2d_pair_hint(void* smem_dst, const void* desc, uint32_t bar_cluster, int x,
-                                                      int y, uint64_t policy)
-{
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.cta_group::2.L2::cache_hint "
-        "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(smem_dst)),
-        "l"(desc), "r"(x), "r"(y), "r"(bar_cluster), "l"(policy)
         : "memory");
 }
 
