@@ -81,7 +81,7 @@ constexpr int SUPPORT_REGS = 104;
 constexpr int SOFTMAX_REGS = 200;
 static_assert(2 * 128 * SOFTMAX_REGS + 128 * SUPPORT_REGS == NUM_THREADS * LAUNCH_REGS, "register split");
 // Column pairs of each 32-column chunk (16 pairs) exponentiated on the FMA pipe.
-constexpr int POLY_PAIRS = 4;
+constexpr int POLY_PAIRS = 0;
 
 struct AttnArgs
 {
@@ -237,8 +237,8 @@ __device__ __forceinline__ void chunk_max(const uint32_t (&v)[128], int rem, flo
 // MASKED, columns >= rem of the chunk give 0.  Sums the fp32 values into
 // sum2 and stores the chunk's 16 packed bf16 pairs into tensor memory at
 // p_addr (over the chunk's half-width slot of S).
-template <int C, bool MASKED>
-__device__ __forceinline__ void chunk_exp(const uint32_t (&v)[128], int rem, uint64_t c2, uint64_t negm2,
+template <int C, bool MASKED, int N>
+__device__ __forceinline__ void chunk_exp(const uint32_t (&v)[N], int rem, uint64_t c2, uint64_t negm2,
                                           uint64_t (&sum2)[4], uint32_t p_addr)
 {
     uint32_t p[16];
@@ -366,39 +366,47 @@ __device__ __forceinline__ Work decode_work(const AttnArgs& a, int w)
     return r;
 }
 
-// Softmax of one key tile for one query row: S_x(j) -> registers, running
-// max, P into the first 64 columns of S_x, the row sum into l; when the max
-// grows past the threshold, O_x is rescaled in place after P is stored (the
-// row's registers are free by then; O_x is stable: PV_x(j-1) completed
+// Softmax of one key tile for one query row: the running max from S_x(j)
+// (pass 1), then S_x(j) re-read in 64-column pairs of chunks, P = exp2(S*c -
+// m) stored as packed bf16 over the first 64 columns of S_x and the row sum
+// added to l (pass 2); when the max grows past the threshold, O_x is
+// rescaled in place after P is stored (O_x is stable: PV_x(j-1) completed
 // before S_x(j) was signalled, and PV_x(j) waits for this tile's p_full).
+// Re-reading is safe: the P of chunk c lands on columns [16c, 16c + 16),
+// which pass 2 has already read.  Pass 2 is a loop, not unrolled: a fully
+// unrolled 128-column softmax is big enough to evict the MMA warp's issue
+// code from the instruction cache, which measured 4-6x slower MMA issue.
 // FULL: all 128 keys valid; otherwise `valid` (1..127) keys: chunks wholly
 // past them are skipped and only the partial chunk is masked.
 template <bool FULL>
 __device__ __forceinline__ void softmax_tile(uint32_t s_addr, uint32_t o_addr, int valid, bool first,
                                              float scale_log2, float& m_used, float& l)
 {
-    const int nfull = FULL ? 4 : valid >> 5;      // chunks with every key valid
-    const int rem = FULL ? 0 : valid & 31;        // keys of the partial chunk (0: none)
-    // all four chunks are loaded (a conditional load leaves part of the row
-    // maybe-undefined, which costs the register allocator dearly); columns
-    // past the keys hold stale values that the max and exponentials skip
-    uint32_t v[128];
-    tmem_ld32_at<0>(s_addr, v);
-    tmem_ld32_at<32>(s_addr + 32, v);
-    tmem_ld32_at<64>(s_addr + 64, v);
-    tmem_ld32_at<96>(s_addr + 96, v);
-    tmem_ld_wait();
+    const int nfull = FULL ? 4 : valid >> 5; // chunks with every key valid
+    const int rem = FULL ? 0 : valid & 31;   // keys of the partial chunk (0: none)
+    const int nchunks = nfull + (rem ? 1 : 0);
     float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    {
+        // pass 1: the row max (all four chunks are loaded -- a conditional load
+        // leaves part of the row maybe-undefined, which costs the register
+        // allocator dearly; columns past the keys are skipped or masked)
+        uint32_t v[128];
+        tmem_ld32_at<0>(s_addr, v);
+        tmem_ld32_at<32>(s_addr + 32, v);
+        tmem_ld32_at<64>(s_addr + 64, v);
+        tmem_ld32_at<96>(s_addr + 96, v);
+        tmem_ld_wait();
 #define S2_CHUNK_MAX(C)                                                                                        \
     if (FULL || nfull > C)                                                                                     \
         chunk_max<C, false>(v, 32, m4);                                                                        \
     else if (nfull == C && rem)                                                                                \
         chunk_max<C, true>(v, rem, m4);
-    S2_CHUNK_MAX(0)
-    S2_CHUNK_MAX(1)
-    S2_CHUNK_MAX(2)
-    S2_CHUNK_MAX(3)
+        S2_CHUNK_MAX(0)
+        S2_CHUNK_MAX(1)
+        S2_CHUNK_MAX(2)
+        S2_CHUNK_MAX(3)
 #undef S2_CHUNK_MAX
+    }
     const float mt = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * scale_log2;
     float alpha = 1.f;
     bool rescale = false;
@@ -413,16 +421,28 @@ __device__ __forceinline__ void softmax_tile(uint32_t s_addr, uint32_t o_addr, i
     const uint64_t c2 = f2(scale_log2);
     const uint64_t negm2 = f2(-m_used);
     uint64_t sum2[4] = {0, 0, 0, 0};
-#define S2_CHUNK_EXP(C)                                                                                        \
-    if (FULL || nfull > C)                                                                                     \
-        chunk_exp<C, false>(v, 32, c2, negm2, sum2, s_addr);                                                   \
-    else if (nfull == C && rem)                                                                                \
-        chunk_exp<C, true>(v, rem, c2, negm2, sum2, s_addr);
-    S2_CHUNK_EXP(0)
-    S2_CHUNK_EXP(1)
-    S2_CHUNK_EXP(2)
-    S2_CHUNK_EXP(3)
-#undef S2_CHUNK_EXP
+    // pass 2: two chunks per iteration (both loads in flight before the wait)
+#pragma unroll 1
+    for (int c = 0; c < nchunks; c += 2)
+    {
+        uint32_t v[64];
+        const bool two = c + 1 < nchunks;
+        tmem_ld32_at<0>(s_addr + c * 32, v);
+        if (two) tmem_ld32_at<32>(s_addr + c * 32 + 32, v);
+        tmem_ld_wait();
+        const uint32_t p_addr = s_addr + c * 16;
+        if (FULL || c < nfull)
+            chunk_exp<0, false>(v, 32, c2, negm2, sum2, p_addr);
+        else
+            chunk_exp<0, true>(v, rem, c2, negm2, sum2, p_addr);
+        if (two)
+        {
+            if (FULL || c + 1 < nfull)
+                chunk_exp<1, false>(v, 32, c2, negm2, sum2, p_addr);
+            else
+                chunk_exp<1, true>(v, rem, c2, negm2, sum2, p_addr);
+        }
+    }
     const uint64_t s2 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
     float lo, hi;
     upk2(s2, lo, hi);
