@@ -12,7 +12,7 @@
 // once for both query tiles.  384 threads, three warpgroups:
 //   warps 0-3   softmax + epilogue of query tile 0   (200 registers each)
 //   warps 4-7   softmax + epilogue of query tile 1   (200 registers each)
-//   warp 8      TMA: Q pair per unit, K tiles into a 3-slot ring
+//   warp 8      TMA: Q pair per unit, K tiles into a 2-slot ring
 //   warp 9      MMA: one thread issues every tcgen05.mma
 //   warp 10     TMA: V tiles into a 2-slot ring
 //   warp 11     idle (the warpgroup gives its registers to the softmax)
@@ -35,15 +35,19 @@
 // the accumulator O_x is stable and it may rescale it in place: the running
 // max is raised (and O, l rescaled) only when it grows by more than 2^8.
 //
-// Exponentials: a fixed share of each row's column pairs is exponentiated on
-// the FMA pipe (2^t = 2^n * 2^f, n = round(t), f in [-1/2, 1/2], a cubic for
+// Exponentials: a quarter of each row's column pairs is exponentiated on the
+// FMA pipe (2^t = 2^n * 2^f, n = round(t), f in [-1/2, 1/2], a cubic for
 // 2^f) and the rest on the MUFU (ex2.approx): with head_dim 128 a 128 x 128
 // tile's 16,384 exponentials alone would take the MUFU as long as the tile's
-// two MMAs take the tensor core.
+// two MMAs take the tensor core.  (Measured: a quarter beats none, a half
+// and three quarters.)
 //
 // Epilogue: O / l -- video rows stored straight to their source token (the
 // scatter; peer GPUs' rows over NVLink), text rows to a per-window fp32
-// partial that text_pool averages over the sample's windows.  Keys past the
+// partial that text_pool averages over the sample's windows.  Each row's
+// destination is read when its unit starts and every role decodes the next
+// unit's descriptor one unit ahead, so no dependent global load sits between
+// two units.  Keys past the
 // window's sequence are masked; query rows past it are computed but never
 // stored.  The ragged last key tile loads, exponentiates and stores only its
 // 32-column chunks that hold keys, and its MMAs run with N (S) or K (PV)
@@ -66,7 +70,7 @@ constexpr int TILE_BYTES = 2 * CHUNK_BYTES;  // 128 x 128 bf16
 constexpr int NUM_THREADS = 384;
 constexpr int TMEM_COLS = 512;               // S_0 S_1 O_0 O_1
 constexpr uint32_t IDESC_O = umma_idesc_bf16(128, 128, 0, 1); // A (= P, tensor memory) K-major, B (= V) MN-major
-constexpr int K_STAGES = 3;
+constexpr int K_STAGES = 2;
 constexpr int V_STAGES = 2;
 // Q_0, Q_1 | K ring | V ring
 constexpr int SMEM_BYTES = (2 + K_STAGES + V_STAGES) * TILE_BYTES + 1024 + 256;
@@ -81,7 +85,7 @@ constexpr int SUPPORT_REGS = 104;
 constexpr int SOFTMAX_REGS = 200;
 static_assert(2 * 128 * SOFTMAX_REGS + 128 * SUPPORT_REGS == NUM_THREADS * LAUNCH_REGS, "register split");
 // Column pairs of each 32-column chunk (16 pairs) exponentiated on the FMA pipe.
-constexpr int POLY_PAIRS = 0;
+constexpr int POLY_PAIRS = 4;
 
 struct AttnArgs
 {
@@ -289,20 +293,28 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity)
         if (global_timer_ns() - t0 > kWaitLimitNs) break;
 }
 
-// Stores 32 output columns [col0, col0+32) of query row qi of the window with
-// 32-byte (full-sector) stores: video rows to their source token, text rows
-// to the window's fp32 partial.
-// Returns true when the row went to a peer GPU.
-__device__ __forceinline__ bool store_row(const AttnArgs& a, int item_window, int part_off, int L, int qi, int col0,
-                                          const float* o, float inv)
+// Where query row qi of a unit goes, read once at the start of the unit so
+// the epilogue issues no dependent global load: a video row's source token
+// (with the peer GPU in the high bits), a text row's row of the window's
+// fp32 partial.  -1 for a padding row past the window.
+__device__ __forceinline__ int row_target(const AttnArgs& a, int window, int part_off, int L, int S_len, int qi)
 {
-    const bool video = qi < L;
-    int src = 0;
+    if (qi >= S_len) return -1;
+    return qi < L ? a.video_indices[part_off + qi] : a.win_pool[window] + (qi - L);
+}
+
+// Stores 32 output columns [col0, col0+32) of one query row with 32-byte
+// (full-sector) stores: a video row to its source token, a text row to the
+// window's fp32 partial.  `target` comes from row_target.
+// Returns true when the row went to a peer GPU.
+__device__ __forceinline__ bool store_row(const AttnArgs& a, bool video, int target, int col0, const float* o,
+                                          float inv)
+{
+    int src = target;
     void* vbase = a.video_out;
     bool remote = false;
     if (video)
     {
-        src = a.video_indices[part_off + qi];
         const int peer = src >> kPeerShift;
         if (peer)
         {
@@ -325,7 +337,7 @@ __device__ __forceinline__ bool store_row(const AttnArgs& a, int item_window, in
         return remote;
     }
     float* dst = video ? reinterpret_cast<float*>(vbase) + (size_t)src * a.inner + col0
-                       : a.text_partial + (size_t)(a.win_pool[item_window] + (qi - L)) * a.inner + col0;
+                       : a.text_partial + (size_t)target * a.inner + col0;
 #pragma unroll
     for (int i = 0; i < 32; i += 8)
     {
@@ -535,9 +547,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t q_par = 0;
             int k_issued[K_STAGES] = {};
             uint32_t k_par[K_STAGES] = {};
+            Work nwk = decode_work(args, blockIdx.x < args.num_work ? blockIdx.x : 0);
             for (int w = blockIdx.x; w < args.num_work && !*abort_flag; w += gridDim.x, it++)
             {
-                const Work wk = decode_work(args, w);
+                const Work wk = nwk;
+                const bool has_next = w + (int)gridDim.x < args.num_work;
+                if (has_next) nwk = decode_work(args, w + gridDim.x);
                 const int x0 = wk.head * HD;
                 if (it > 0 && !mbar_wait<true>(q_empty, (it - 1) & 1, abort_flag, args.status)) break;
                 mbar_arrive_expect_tx(q_full, wk.has_b ? 2 * TILE_BYTES : TILE_BYTES);
@@ -550,16 +565,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 q_out = true;
                 q_par = it & 1;
-                if (w + (int)gridDim.x < args.num_work)
+                if (has_next)
                 {
-                    const Work nx = decode_work(args, w + gridDim.x);
-                    const int ny = nx.seq_off + nx.q0;
-                    tma_prefetch_l2_2d(&tq, nx.head * HD, ny);
-                    tma_prefetch_l2_2d(&tq, nx.head * HD + 64, ny);
-                    if (nx.has_b)
+                    const int ny = nwk.seq_off + nwk.q0;
+                    tma_prefetch_l2_2d(&tq, nwk.head * HD, ny);
+                    tma_prefetch_l2_2d(&tq, nwk.head * HD + 64, ny);
+                    if (nwk.has_b)
                     {
-                        tma_prefetch_l2_2d(&tq, nx.head * HD, ny + TILE);
-                        tma_prefetch_l2_2d(&tq, nx.head * HD + 64, ny + TILE);
+                        tma_prefetch_l2_2d(&tq, nwk.head * HD, ny + TILE);
+                        tma_prefetch_l2_2d(&tq, nwk.head * HD + 64, ny + TILE);
                     }
                 }
                 bool ok = true;
@@ -595,9 +609,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             int g = 0;
             int v_issued[V_STAGES] = {};
             uint32_t v_par[V_STAGES] = {};
+            Work nwk = decode_work(args, blockIdx.x < args.num_work ? blockIdx.x : 0);
             for (int w = blockIdx.x; w < args.num_work && !*abort_flag; w += gridDim.x)
             {
-                const Work wk = decode_work(args, w);
+                const Work wk = nwk;
+                if (w + (int)gridDim.x < args.num_work) nwk = decode_work(args, w + gridDim.x);
                 const int x0 = wk.head * HD;
                 bool ok = true;
                 for (int j = 0; j < wk.nkv; j++, g++)
@@ -634,9 +650,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint64_t k_desc0 = umma_desc_sw128(smem_u32(sK), 16, 1024);
             const uint64_t v_desc0 = umma_desc_sw128(smem_u32(sV), CHUNK_BYTES, 1024);
             constexpr uint32_t kTileDesc = TILE_BYTES >> 4;
+            Work nwk = decode_work(args, blockIdx.x < args.num_work ? blockIdx.x : 0);
             for (int w = blockIdx.x; w < args.num_work && ok; w += gridDim.x, it++)
             {
-                const Work wk = decode_work(args, w);
+                const Work wk = nwk;
+                if (w + (int)gridDim.x < args.num_work) nwk = decode_work(args, w + gridDim.x);
                 const int ntiles = wk.has_b ? 2 : 1;
                 // S_x = Q_x K^T for key tile j (ring slot of K tile gkk); a ragged
                 // last tile runs with N = its keys rounded up to 16.
@@ -760,11 +778,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t o_addr = tmem + lane_base + 256 + x * 128;
         uint32_t scnt = 0, ocnt = 0;
         bool ok = true;
+        // each unit's descriptor is read one unit ahead (its loads are in
+        // flight while the current unit runs)
+        Work nwk = decode_work(args, blockIdx.x < args.num_work ? blockIdx.x : 0);
         for (int w = blockIdx.x; w < args.num_work && ok; w += gridDim.x)
         {
-            const Work wk = decode_work(args, w);
+            const Work wk = nwk;
+            if (w + (int)gridDim.x < args.num_work) nwk = decode_work(args, w + gridDim.x);
             if (x == 1 && !wk.has_b) continue;
             const int qbase = wk.q0 + x * TILE;
+            const int qi = qbase + row;
+            const int target = row_target(args, wk.window, wk.part_off, wk.L, wk.S_len, qi);
             float m_used = -INFINITY;
             float l_run = 0.f;
             // only the last key tile can be ragged; it runs after the loop so
@@ -812,21 +836,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             ocnt++;
             tc_fence_after();
-            const int qi = qbase + row;
             const float inv = 1.f / l_run;
             bool remote = false;
-#pragma unroll 1
-            for (int c = 0; c < 4; c++)
             {
-                uint32_t v[32];
-                tmem_ld32(o_addr + c * 32, v);
+                // the whole O row in one batch of tensor-memory loads
+                uint32_t v[128];
+                tmem_ld32_at<0>(o_addr, v);
+                tmem_ld32_at<32>(o_addr + 32, v);
+                tmem_ld32_at<64>(o_addr + 64, v);
+                tmem_ld32_at<96>(o_addr + 96, v);
                 tmem_ld_wait();
-                if (qi < wk.S_len)
+                if (target >= 0)
                 {
-                    float o[32];
+                    const bool video = qi < wk.L;
 #pragma unroll
-                    for (int i = 0; i < 32; i++) o[i] = __uint_as_float(v[i]);
-                    remote |= store_row(args, wk.window, wk.part_off, wk.L, qi, wk.head * HD + c * 32, o, inv);
+                    for (int c = 0; c < 4; c++)
+                        remote |= store_row(args, video, target, wk.head * HD + c * 32,
+                                            reinterpret_cast<const float*>(v) + c * 32, inv);
                 }
             }
             // a row stored into a peer GPU must be visible there once this
