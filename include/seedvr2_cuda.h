@@ -523,6 +523,11 @@ int s2_shard_build(const int* video_shape, int text_length, const int* window, i
                    s2_shard** out);
 int s2_shard_counts(const s2_shard* shard, int shifted, int* n_local, int* send_counts, int* recv_counts);
 int s2_shard_lists(const s2_shard* shard, int shifted, int* local_tokens, int* send_tokens, int* recv_tokens);
+/* The windows of plan `shifted` whose attention this rank computes, as plan
+ * window indices in ascending order: *count always, windows[] when non-null.
+ * Owners are balanced by the attention kernel's work per window (sharding
+ * is this library's addition; the reference runs one device). */
+int s2_shard_windows(const s2_shard* shard, int shifted, int* count, int* windows);
 void s2_shard_free(s2_shard* shard);
 
 /* NCCL: rank 0 makes a 128-byte id and shares it out of band; every rank then

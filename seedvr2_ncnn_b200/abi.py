@@ -53,7 +53,7 @@ EXPORTED = [
     "s2_dit_create", "s2_dit_free", "s2_dit_set_block_weights", "s2_dit_set_block_norm", "s2_dit_init_random",
     "s2_dit_forward",
     "s2_dit_set_check_finite", "s2_dit_nonfinite_report", "s2_dit_set_checkpoints",
-    "s2_dit_forward_host", "s2_shard_build", "s2_shard_counts", "s2_shard_lists", "s2_shard_free",
+    "s2_dit_forward_host", "s2_shard_build", "s2_shard_counts", "s2_shard_lists", "s2_shard_windows", "s2_shard_free",
     "s2_dist_unique_id", "s2_dist_init", "s2_dist_sync", "s2_dist_destroy", "s2_peer_barrier",
     "s2_dit_forward_sharded",
     "s2_patchify_video", "s2_unpatchify_prediction", "s2_timestep_embedding", "s2_dit_set_io_weights",
@@ -178,6 +178,7 @@ def lib() -> C.CDLL:
     L.s2_shard_build.argtypes = [pint, ip, pint, ip, ip, ip, C.POINTER(vp)]
     L.s2_shard_counts.argtypes = [vp, ip, pint, pint, pint]
     L.s2_shard_lists.argtypes = [vp, ip, pint, pint, pint]
+    L.s2_shard_windows.argtypes = [vp, ip, pint, pint]
     L.s2_shard_free.argtypes = [vp]
     L.s2_shard_free.restype = None
     L.s2_dist_unique_id.argtypes = [vp]
@@ -803,8 +804,8 @@ class VaeMha:
 
 
 def shard(video_shape, text_length, window, window_mode, rank, world, shifted=1) -> dict:
-    """Token ownership of a sharded forward (host only): local tokens and the exchange lists of
-    window plan `shifted` (0 = unshifted blocks, 1 = shifted blocks)."""
+    """Token ownership of a sharded forward (host only): local tokens, the exchange lists and the
+    owned windows (plan window indices) of window plan `shifted` (0 = unshifted, 1 = shifted)."""
     import numpy as np
 
     h = C.c_void_p()
@@ -820,9 +821,14 @@ def shard(video_shape, text_length, window, window_mode, rank, world, shifted=1)
         st = np.zeros(int(sc.sum()), np.int32)
         rt = np.zeros(int(rc.sum()), np.int32)
         check(lib().s2_shard_lists(h, int(shifted), P(local), P(st), P(rt)), "s2_shard_lists")
+        nw = C.c_int()
+        check(lib().s2_shard_windows(h, int(shifted), C.byref(nw), None), "s2_shard_windows")
+        wins = np.zeros(nw.value, np.int32)
+        check(lib().s2_shard_windows(h, int(shifted), C.byref(nw), P(wins)), "s2_shard_windows")
     finally:
         lib().s2_shard_free(h)
-    return {"local_tokens": local, "send_counts": sc, "recv_counts": rc, "send_tokens": st, "recv_tokens": rt}
+    return {"local_tokens": local, "send_counts": sc, "recv_counts": rc, "send_tokens": st, "recv_tokens": rt,
+            "windows": wins}
 
 
 def dist_unique_id() -> bytes:

@@ -72,15 +72,21 @@ int build_shard(const int* shape, int text_length, const int* window, int window
         const Plan& pl = sp.plan[p];
         const int nw = static_cast<int>(pl.windows.size() / 9);
         // Window owners: the rank holding most of the window's tokens, then
-        // windows move from the most to the least loaded rank (attention cost
-        // (L+T)^2, preferring windows that rank already holds tokens of) until
-        // no rank carries more than 5 % above the mean.
+        // windows move from the most to the least loaded rank (preferring
+        // windows that rank already holds tokens of) while a move lowers the
+        // larger of the two loads.  A window's load is the attention kernel's
+        // work for it: per head, ceil(S/256) units (pairs of 128-row query
+        // tiles), each walking ceil(S/128) key tiles plus about one key
+        // tile's worth of unit set-up and epilogue.  (S^2 undercounts the
+        // small boundary windows of the shifted plan, whose every head still
+        // costs a whole unit: with it the slowest rank's shifted attention ran
+        // 3-7 % longer at 2, 4 and 8 GPUs on the 720p and 1080p plans.)
         sp.owner[p].assign(nw, 0);
         std::vector<std::vector<int>> w_votes(nw, std::vector<int>(world, 0));
         std::vector<double> load(world, 0.0);
         auto cost = [&](int w) {
-            const double S = pl.windows[9 * w + 8] + text_length;
-            return S * S;
+            const int S = pl.windows[9 * w + 8] + text_length;
+            return static_cast<double>(((S + 255) / 256) * ((S + 127) / 128 + 1));
         };
         double total = 0.0;
         for (int w = 0; w < nw; w++)
@@ -97,7 +103,7 @@ int build_shard(const int* shape, int text_length, const int* window, int window
         {
             const int hi = static_cast<int>(std::max_element(load.begin(), load.end()) - load.begin());
             const int lo = static_cast<int>(std::min_element(load.begin(), load.end()) - load.begin());
-            if (load[hi] <= 1.05 * mean) break;
+            if (load[hi] <= mean) break;
             int pick = -1;
             double pick_key = -1.0;
             for (int w = 0; w < nw; w++)

@@ -452,6 +452,15 @@ int s2_shard_lists(const s2_shard* sh, int shifted, int* local_tokens, int* send
     return S2_OK;
 }
 
+int s2_shard_windows(const s2_shard* sh, int shifted, int* count, int* windows)
+{
+    if (!sh || shifted < 0 || shifted > 1 || !count) return S2_ERR_INVALID;
+    const std::vector<int>& wm = sh->sp.win_mine[shifted];
+    *count = static_cast<int>(wm.size());
+    if (windows) std::memcpy(windows, wm.data(), wm.size() * 4);
+    return S2_OK;
+}
+
 void s2_shard_free(s2_shard* sh)
 {
     delete sh;
