@@ -115,6 +115,17 @@ void s2_plan_free(s2_plan* plan);
 int s2_plan_schedule_copy(s2_context* ctx, s2_plan* plan, const int* text_lengths, int* sizes, int* row_src,
                           int* row_pos, int* win_info, int* video_indices, int* pack_dst);
 
+/* Test hook of the checked build (libseedvr2_cuda_checked.so, compiled with
+ * S2_DEBUG_BOUNDS): overwrites entry `index` of one table of the plan's
+ * device schedule (built by s2_plan_schedule_copy or a forward) with
+ * `value` -- table 0 = row_src (the gather), 1 = video_indices (the
+ * scatter).  The checked build's kernels test every index they read from
+ * these tables, so a forward over a corrupted schedule records a bad index
+ * (s2_status then returns -1) and skips the access.  Any other build returns
+ * S2_ERR_INVALID and changes nothing.  No counterpart in the reference (its
+ * tables live in host vectors). */
+int s2_debug_poke_schedule(s2_context* ctx, s2_plan* plan, int table, int index, int value);
+
 /* ---------------------------------------------------------------------------
  * AdaptiveWindowAttention forward.  Replaces
  * AdaptiveWindowAttention::forward (CPU :764-978, Vulkan :1059-1270) with

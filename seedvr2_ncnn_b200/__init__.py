@@ -11,6 +11,9 @@ library is missing, importing :mod:`seedvr2_ncnn_b200.abi` raises.
 
 import os
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libseedvr2_cuda.so")
+# S2_CUDA_LIB selects another build of the same library (the tests use it to load the
+# index-checked libseedvr2_cuda_checked.so in a separate process).
+LIB_PATH = os.environ.get("S2_CUDA_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)),
+                                                         "libseedvr2_cuda.so")
 
 __all__ = ["LIB_PATH"]

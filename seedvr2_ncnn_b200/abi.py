@@ -46,7 +46,7 @@ S2_EPI_GATE_RESIDUAL = 2
 EXPORTED = [
     "s2_init", "s2_destroy", "s2_set_stream", "s2_status", "s2_error_string", "s2_version", "s2_launch_count",
     "s2_profile_enable", "s2_profile_read",
-    "s2_plan_build", "s2_plan_info", "s2_plan_copy", "s2_plan_free", "s2_plan_schedule_copy",
+    "s2_plan_build", "s2_plan_info", "s2_plan_copy", "s2_plan_free", "s2_plan_schedule_copy", "s2_debug_poke_schedule",
     "s2_awa_forward", "s2_awa_forward_static", "s2_awa_static_status", "s2_shared_linear", "s2_ada_rmsnorm", "s2_ada_layernorm",
     "s2_convert_f32_bf16",
     "s2_count_nonfinite", "s2_binary_op", "s2_norm_f32", "s2_gelu_f32",
@@ -151,6 +151,7 @@ def lib() -> C.CDLL:
     L.s2_plan_free.argtypes = [vp]
     L.s2_plan_free.restype = None
     L.s2_plan_schedule_copy.argtypes = [vp, vp, pint, pint, vp, vp, vp, vp, vp]
+    L.s2_debug_poke_schedule.argtypes = [vp, vp, ip, ip, ip]
     L.s2_awa_forward.argtypes = [vp, C.POINTER(AwaParams), vp, pint, pint, ip, ip, vp, vp, vp, i64, vp, vp, vp, i64,
                                  ip, vp, vp]
     L.s2_awa_forward_static.argtypes = [C.POINTER(AwaParams), pint, pint, ip, ip, vp, vp, vp, i64, vp, vp, vp, i64,
@@ -349,6 +350,11 @@ class Plan:
                                                                          "video_indices", "pack_dst")]),
               "s2_plan_schedule_copy")
         return out
+
+    def debug_poke(self, ctx, table: int, index: int, value: int) -> int:
+        """Overwrites one entry of the device schedule (table 0 row_src, 1 video_indices): checked
+        build only (libseedvr2_cuda_checked.so); any other build returns S2_ERR_INVALID untouched."""
+        return lib().s2_debug_poke_schedule(ctx.handle, self.handle, int(table), int(index), int(value))
 
 
 def awa_forward(ctx: Context, *, heads, head_dim, window, window_mode, shifted, eps, rope_pairs, norms, freqs,

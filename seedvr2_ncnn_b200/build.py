@@ -19,6 +19,12 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libseedvr2_cuda.so")
+# The checked build: the same sources with S2_DEBUG_BOUNDS, whose kernels test
+# every index read from a schedule table before it addresses memory (a bad one
+# records an error status instead of faulting).  Tests load it by setting
+# S2_CUDA_LIB to its path; nothing else uses it.
+BUILD_CHECKED = os.path.join(HERE, "_build_checked")
+LIB_CHECKED = os.path.join(HERE, "libseedvr2_cuda_checked.so")
 LAYER_LIB = os.path.join(HERE, "libseedvr2_ncnn.so")
 LAYER_SOURCES = ["adaptive_window_attention.cpp", "shared_linear.cpp", "vae_layers.cpp", "net.cpp", "layer_capi.cpp"]
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
@@ -42,8 +48,8 @@ def _headers_digest() -> str:
     return h.hexdigest()[:16]
 
 
-def _compile(src: str, extra: list[str], hdr: str) -> str:
-    obj = os.path.join(BUILD, os.path.splitext(src)[0] + ".o")
+def _compile(src: str, extra: list[str], hdr: str, build_dir: str = BUILD) -> str:
+    obj = os.path.join(build_dir, os.path.splitext(src)[0] + ".o")
     stamp = obj + ".hdr"
     path = os.path.join(CSRC, src)
     fresh = (os.path.exists(obj) and os.path.getmtime(obj) >= os.path.getmtime(path) and os.path.exists(stamp)
@@ -63,21 +69,34 @@ def _compile(src: str, extra: list[str], hdr: str) -> str:
     return obj
 
 
-def build(verbose: bool = False, extra: list[str] | None = None) -> str:
-    extra = list(extra or [])
-    os.makedirs(BUILD, exist_ok=True)
+def _build_lib(lib: str, build_dir: str, extra: list[str]) -> str:
+    os.makedirs(build_dir, exist_ok=True)
     hdr = _headers_digest()
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 2)) as ex:
-        objs = list(ex.map(lambda s: _compile(s, extra, hdr), SOURCES))
-    if not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-cudart", "static", "-ldl"]
+        objs = list(ex.map(lambda s: _compile(s, extra, hdr, build_dir), SOURCES))
+    if not os.path.exists(lib) or any(os.path.getmtime(o) > os.path.getmtime(lib) for o in objs):
+        cmd = [NVCC] + ARCH + ["-shared", "-o", lib] + objs + ["-cudart", "static", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    return lib
+
+
+def build(verbose: bool = False, extra: list[str] | None = None) -> str:
+    _build_lib(LIB, BUILD, list(extra or []))
     build_layers(verbose)
+    build_checked(verbose)
     if verbose:
         print(LIB)
     return LIB
+
+
+def build_checked(verbose: bool = False) -> str:
+    """libseedvr2_cuda_checked.so: the S2_DEBUG_BOUNDS build (index checks in the table-driven kernels)."""
+    _build_lib(LIB_CHECKED, BUILD_CHECKED, ["-DS2_DEBUG_BOUNDS"])
+    if verbose:
+        print(LIB_CHECKED)
+    return LIB_CHECKED
 
 
 def build_layers(verbose: bool = False) -> str:

@@ -102,6 +102,12 @@ struct AttnArgs
     int* status;
     int heads;
     int num_work; // items x heads
+    // bounds of the checked (S2_DEBUG_BOUNDS) build: video_indices entries,
+    // output rows, text partial rows, peer outputs
+    int num_video_indices;
+    int out_rows;
+    int partial_rows;
+    int num_peers;
     // peer output bases (multi-GPU): a video_indices entry with a non-zero
     // peer field is stored into peer_out[peer - 1] over NVLink
     void* peer_out[kMaxPeers];
@@ -300,7 +306,18 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity)
 __device__ __forceinline__ int row_target(const AttnArgs& a, int window, int part_off, int L, int S_len, int qi)
 {
     if (qi >= S_len) return -1;
-    return qi < L ? a.video_indices[part_off + qi] : a.win_pool[window] + (qi - L);
+    if (qi < L)
+    {
+        if (!index_ok((int64_t)part_off + qi, a.num_video_indices, a.status)) return -1;
+        const int v = a.video_indices[part_off + qi];
+        // (checked build) the peer field names a peer output, the row lies in the outputs
+        if (kCheckedIndices && !(index_ok(v >> kPeerShift, a.num_peers + 1, a.status) &&
+                                 index_ok(v & ((1 << kPeerShift) - 1), a.out_rows, a.status)))
+            return -1;
+        return v;
+    }
+    const int t = a.win_pool[window] + (qi - L);
+    return index_ok(t, a.partial_rows, a.status) ? t : -1;
 }
 
 // Stores 32 output columns [col0, col0+32) of one query row with 32-byte
@@ -916,6 +933,10 @@ int launch_window_attention(Context& ctx, const AttnSchedule& s, int heads, cons
     }
     a.heads = heads;
     a.num_work = s.num_items * heads;
+    a.num_video_indices = s.num_video_indices;
+    a.out_rows = s.out_rows;
+    a.partial_rows = s.partial_rows;
+    a.num_peers = num_peers;
     const int grid = a.num_work < ctx.num_sms ? a.num_work : ctx.num_sms;
     const double video_rows = (double)s.packed_rows - s.partial_rows;
     ProfileScope prof(ctx, K_ATTN, s.attn_flops_per_head * heads,

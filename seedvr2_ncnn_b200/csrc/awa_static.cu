@@ -351,6 +351,8 @@ extern "C" int s2_awa_forward_static(const s2_awa_params* prm, const int* video_
     s.num_items = L.ni;
     s.total_text = L.nt;
     s.partial_rows = L.pool;
+    // video rows are the tokens themselves here (gather and scatter by token id)
+    s.num_video_indices = s.src_rows = s.out_rows = L.n;
     s.row_src = dt + L.o_src;
     s.row_pos = dt + L.o_pos;
     s.win_info = reinterpret_cast<int4*>(dt + L.o_win);

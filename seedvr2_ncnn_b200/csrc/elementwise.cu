@@ -55,7 +55,8 @@ __global__ void prepare_qkv_kernel(const int* __restrict__ row_src, const int* _
                                    int head_dim, int pairs, float eps, const float* __restrict__ norms,
                                    const float* __restrict__ freqs, const Tin* vq, const Tin* vk, const Tin* vv,
                                    int64_t v_ld, const Tin* tq, const Tin* tk, const Tin* tv, int64_t t_ld,
-                                   __nv_bfloat16* qo, __nv_bfloat16* ko, __nv_bfloat16* vo)
+                                   __nv_bfloat16* qo, __nv_bfloat16* ko, __nv_bfloat16* vo, int src_rows,
+                                   int text_rows, int* status)
 {
     const int r = blockIdx.x;
     // The block is rounded up to whole warps; lanes past the last head work on
@@ -65,6 +66,8 @@ __global__ void prepare_qkv_kernel(const int* __restrict__ row_src, const int* _
     const int sub = threadIdx.x & 15;
     const int d0 = sub * 8;
     const int src = row_src[r];
+    // (uniform over the block: every thread works on packed row r)
+    if (!(src >= 0 ? index_ok(src, src_rows, status) : index_ok(-1 - (int64_t)src, text_rows, status))) return;
     const Tin *pq, *pk, *pv;
     const float *wq, *wk;
     if (src >= 0)
@@ -143,12 +146,17 @@ __global__ void prepare_qkv_kernel(const int* __restrict__ row_src, const int* _
 // text_out[t] = sum over the sample's windows (in window order) of
 // partial[w][t] * (1 / windows in sample).
 __global__ void text_pool_kernel(const int4* __restrict__ reduce, const float* __restrict__ scale_of, int inner,
-                                 const float* __restrict__ partial, int out_f32, void* out)
+                                 const float* __restrict__ partial, int out_f32, void* out, int partial_rows,
+                                 int* status)
 {
     const int t = blockIdx.x;
     const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
     if (c >= inner) return;
     const int4 rd = reduce[t];
+    // every partial row summed lies in the partial buffer (first and last, stride >= 0)
+    if (rd.z > 0 && !(index_ok(rd.x, partial_rows, status) && rd.y >= 0 &&
+                      index_ok(rd.x + (int64_t)(rd.z - 1) * rd.y, partial_rows, status)))
+        return;
     const float sc = scale_of[t];
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     const float* base = partial + (int64_t)rd.x * inner + c;
@@ -376,12 +384,12 @@ int launch_prepare_qkv(Context& ctx, const AttnSchedule& s, int heads, int head_
             s.row_src, s.row_pos, heads, head_dim, rope_pairs, eps, norms, freqs, (const __nv_bfloat16*)vq,
             (const __nv_bfloat16*)vk, (const __nv_bfloat16*)vv, v_ld, (const __nv_bfloat16*)tq,
             (const __nv_bfloat16*)tk, (const __nv_bfloat16*)tv, t_ld, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_out,
-            (__nv_bfloat16*)v_out);
+            (__nv_bfloat16*)v_out, s.src_rows, s.total_text, ctx.status);
     else
         prepare_qkv_kernel<float><<<grid, block, 0, ctx.stream>>>(
             s.row_src, s.row_pos, heads, head_dim, rope_pairs, eps, norms, freqs, (const float*)vq, (const float*)vk,
             (const float*)vv, v_ld, (const float*)tq, (const float*)tk, (const float*)tv, t_ld, (__nv_bfloat16*)q_out,
-            (__nv_bfloat16*)k_out, (__nv_bfloat16*)v_out);
+            (__nv_bfloat16*)k_out, (__nv_bfloat16*)v_out, s.src_rows, s.total_text, ctx.status);
     return finish(ctx);
 }
 
@@ -396,7 +404,7 @@ int launch_text_pool(Context& ctx, const AttnSchedule& s, int inner, const float
     ProfileScope prof(ctx, K_POOL, 0.0,
                       (double)s.partial_rows * inner * 4.0 + (double)s.total_text * inner * (out_f32 ? 4.0 : 2.0));
     text_pool_kernel<<<grid, threads, 0, ctx.stream>>>(s.text_reduce, s.text_scale, inner, partial, out_f32,
-                                                        text_out);
+                                                        text_out, s.partial_rows, ctx.status);
     return finish(ctx);
 }
 

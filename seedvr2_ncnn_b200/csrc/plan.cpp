@@ -335,6 +335,10 @@ int build_schedule_ex(const Plan& plan, const int* text_lengths, const std::vect
     s.total_text = total_text;
     s.max_text = max_text;
     s.partial_rows = pool;
+    s.num_video_indices = static_cast<int>(n_tok);
+    s.src_rows = max_row + 1;
+    s.out_rows = 0;
+    for (int v : vidx) s.out_rows = std::max(s.out_rows, (v & ((1 << kPeerShift) - 1)) + 1);
     return S2_OK;
 }
 

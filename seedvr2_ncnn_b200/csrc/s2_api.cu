@@ -221,6 +221,23 @@ int s2_plan_schedule_copy(s2_context* ctx, s2_plan* p, const int* text_lengths, 
     return S2_OK;
 }
 
+int s2_debug_poke_schedule(s2_context* ctx, s2_plan* p, int table, int index, int value)
+{
+#ifdef S2_DEBUG_BOUNDS
+    if (!ctx || !p || !p->sched || (table != 0 && table != 1) || index < 0) return S2_ERR_INVALID;
+    const s2::AttnSchedule& s = *p->sched;
+    int* base = table == 0 ? s.row_src : s.video_indices;
+    const int n = table == 0 ? s.packed_rows : s.num_video_indices;
+    if (index >= n) return S2_ERR_INVALID;
+    if (cudaSetDevice(ctx->c.device) != cudaSuccess) return S2_ERR_CUDA;
+    return cudaMemcpy(base + index, &value, 4, cudaMemcpyHostToDevice) == cudaSuccess ? S2_OK : S2_ERR_CUDA;
+#else
+    // only a build whose kernels check table indices may run a corrupted table
+    (void)ctx, (void)p, (void)table, (void)index, (void)value;
+    return S2_ERR_INVALID;
+#endif
+}
+
 void s2_plan_free(s2_plan* p)
 {
     delete p;

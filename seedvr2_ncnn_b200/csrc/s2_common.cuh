@@ -48,6 +48,25 @@ __device__ __forceinline__ void record_status(int* status, int code)
     if (status) atomicCAS(status, 0, code);
 }
 
+// A S2_DEBUG_BOUNDS build checks every index it reads from a schedule table
+// (gather rows, scatter targets, text partial rows) before the index
+// addresses memory: one outside [0, n) records kStatusBadIndex and the access
+// is skipped, so a corrupted table ends in an error status instead of a
+// memory fault.  Other builds compile the check away (the host validates
+// every table before upload).
+#ifdef S2_DEBUG_BOUNDS
+constexpr bool kCheckedIndices = true;
+#else
+constexpr bool kCheckedIndices = false;
+#endif
+
+__device__ __forceinline__ bool index_ok(int64_t i, int64_t n, int* status)
+{
+    if (!kCheckedIndices || (i >= 0 && i < n)) return true;
+    record_status(status, kStatusBadIndex);
+    return false;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p)
 {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -126,6 +126,12 @@ struct AttnSchedule
     int* text_dst = nullptr;      // packed rows of each text row (one per window of its sample)
     int max_pos = 0;              // 1 + largest RoPE position in row_pos
     int partial_rows = 0;         // sum over windows of T_s
+    // bounds the table-driven gathers / scatters are checked against in a
+    // S2_DEBUG_BOUNDS build: video_indices entries, 1 + largest video row
+    // row_src gathers, 1 + largest output row video_indices scatters to
+    int num_video_indices = 0;
+    int src_rows = 0;
+    int out_rows = 0;
     double attn_flops_per_head = 0; // sum over windows of 4 * S^2 * 128 (QK^T + PV)
     void* block = nullptr;        // single device allocation backing the arrays
     ~AttnSchedule();
