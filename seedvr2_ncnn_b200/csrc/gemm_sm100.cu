@@ -85,6 +85,7 @@ struct GemmArgs
     int M0, M1, N, K;
     int mblk0, mblk1, nblk, num_tiles, num_kb;
     int group_m; // M blocks per raster group (tiles walk M fastest inside a group)
+    int ksplit;  // K halves per tile (2: split-K units, gate-residual CTA pairs only; else 1)
     int epilogue;
     int out_f32;
     int tma_out; // outputs written through tmap_o0 / tmap_o1
@@ -112,6 +113,34 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& a, int t, int& strea
     stream = mb < a.mblk0 ? 0 : 1;
     m0 = (stream ? mb - a.mblk0 : mb) * BMT;
     n0 = nb * BN;
+}
+
+// Work unit t -> its tile and K part: with split-K the units of one tile are
+// adjacent (t = tile * ksplit + khalf); khalf = -1 without a split.
+__device__ __forceinline__ int unit_tile(const GemmArgs& a, int t, int& khalf)
+{
+    if (a.ksplit > 1)
+    {
+        const int tile = t / a.ksplit;
+        khalf = t - tile * a.ksplit;
+        return tile;
+    }
+    khalf = -1;
+    return t;
+}
+
+// The unit's K blocks [kb0, kb1).
+__device__ __forceinline__ void unit_kblocks(const GemmArgs& a, int khalf, int& kb0, int& kb1)
+{
+    if (khalf < 0)
+    {
+        kb0 = 0;
+        kb1 = a.num_kb;
+        return;
+    }
+    const int per = (a.num_kb + a.ksplit - 1) / a.ksplit;
+    kb0 = khalf * per;
+    kb1 = min(a.num_kb, kb0 + per);
 }
 
 // Tile walk of one CTA: a single CTA per tile, or a CTA pair (cluster of 2)
@@ -257,10 +286,15 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int stream, in
 // 128-byte swizzle (16-byte unit u of row r at unit u ^ (r & 7), which is
 // free of bank conflicts) and stored by lane 0.  `stg` holds the warp's two
 // 4 KB boxes; `slot` alternates between them.
+// khalf >= 0: a split-K unit of a gate-residual tile -- (acc [+ bias on the
+// first half]) * gate is reduce-added into the fp32 output in L2 (the two
+// halves' adds land in either order), no residual is read.
 template <int BN>
 __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const CUtensorMap* tmap_out, uint8_t* stg, int& slot,
-                                                  uint32_t t_row, int stream, int m0, int n0, int quarter, int lane)
+                                                  uint32_t t_row, int stream, int m0, int n0, int quarter, int lane,
+                                                  int khalf = -1)
 {
+    const bool split = khalf >= 0;
     const int M = stream ? a.M1 : a.M0;
     const int N = a.N;
     const int row = m0 + quarter * 32 + lane;
@@ -281,7 +315,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const CUten
             const int n = n0 + c0 + 32 * k;
             const bool full = n + 32 <= N;
             float4 r[8];
-            if (a.epilogue == EPI_GATE_RESIDUAL)
+            if (a.epilogue == EPI_GATE_RESIDUAL && !split)
             {
                 if (live && full)
                 {
@@ -306,7 +340,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const CUten
             float x[32];
 #pragma unroll
             for (int j = 0; j < 32; j++) x[j] = __uint_as_float(v[j]);
-            if (a.bias)
+            if (a.bias && khalf <= 0)
             {
                 if (full)
                 {
@@ -342,10 +376,20 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const CUten
                         g.z = n + 4 * j + 2 < N ? __ldg(a.gate + n + 4 * j + 2) : 0.f;
                         g.w = n + 4 * j + 3 < N ? __ldg(a.gate + n + 4 * j + 3) : 0.f;
                     }
-                    x[4 * j] = r[j].x + x[4 * j] * g.x;
-                    x[4 * j + 1] = r[j].y + x[4 * j + 1] * g.y;
-                    x[4 * j + 2] = r[j].z + x[4 * j + 2] * g.z;
-                    x[4 * j + 3] = r[j].w + x[4 * j + 3] * g.w;
+                    if (split)
+                    {
+                        x[4 * j] *= g.x;
+                        x[4 * j + 1] *= g.y;
+                        x[4 * j + 2] *= g.z;
+                        x[4 * j + 3] *= g.w;
+                    }
+                    else
+                    {
+                        x[4 * j] = r[j].x + x[4 * j] * g.x;
+                        x[4 * j + 1] = r[j].y + x[4 * j + 1] * g.y;
+                        x[4 * j + 2] = r[j].z + x[4 * j + 2] * g.z;
+                        x[4 * j + 3] = r[j].w + x[4 * j + 3] * g.w;
+                    }
                 }
             }
             else if (a.epilogue == EPI_GELU_TANH)
@@ -378,7 +422,13 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const CUten
         __syncwarp();
         if (lane == 0)
         {
-            if (box_live) tma_store_2d(tmap_out, stg + slot * 4096, n0 + c0, m0 + quarter * 32);
+            if (box_live)
+            {
+                if (split)
+                    tma_reduce_add_2d(tmap_out, stg + slot * 4096, n0 + c0, m0 + quarter * 32);
+                else
+                    tma_store_2d(tmap_out, stg + slot * 4096, n0 + c0, m0 + quarter * 32);
+            }
             bulk_commit();
         }
         slot ^= 1;
@@ -1025,12 +1075,15 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
             for (int s = 0; s < STAGES; s++) issued[s] = 0, last_phase[s] = 0;
             for (int t = walk.first(); t < args.num_tiles && !*abort_flag; t += walk.step())
             {
+                int khalf, kb0, kb1;
+                const int tile = unit_tile(args, t, khalf);
+                unit_kblocks(args, khalf, kb0, kb1);
                 int stream, m0, n0p;
-                decode_tile<BN, 2 * BM>(args, t, stream, m0, n0p);
+                decode_tile<BN, 2 * BM>(args, tile, stream, m0, n0p);
                 m0 += (int)walk.rank * BM;
                 const int nb = n0p + (int)walk.rank * 128;
                 const CUtensorMap* ta = stream ? &tmap_a1 : &tmap_a0;
-                for (int kb = 0; kb < args.num_kb; kb++)
+                for (int kb = kb0; kb < kb1; kb++)
                 {
                     if (!mbar_wait<true>(&empty[stage], phase ^ 1, abort_flag, args.status)) break;
                     uint8_t* sa = smem + stage * STAGE_BYTES;
@@ -1071,8 +1124,11 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                 if (!mbar_wait<true>(&tempty[acc], acc_phase ^ 1, abort_flag, args.status)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
+                int khalf, kb0, kb1;
+                unit_tile(args, t, khalf);
+                unit_kblocks(args, khalf, kb0, kb1);
                 bool ok = true;
-                for (int kb = 0; kb < args.num_kb; kb++)
+                for (int kb = kb0; kb < kb1; kb++)
                 {
                     if (!mbar_wait<true>(&full[stage], phase, abort_flag, args.status))
                     {
@@ -1087,7 +1143,7 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                     {
                         const uint64_t ad = umma_desc_sw128(a_addr + k * 32, 16, 1024);
                         const uint64_t bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
-                        umma_bf16_pair(d_tmem, ad, bd, TL::IDESC, (kb | k) != 0);
+                        umma_bf16_pair(d_tmem, ad, bd, TL::IDESC, (kb != kb0) || k != 0);
                     }
                     umma_commit_pair(&empty[stage], 0x3);
                     if (++stage == STAGES)
@@ -1124,12 +1180,18 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                 rope = tab;
             }
         }
+        bool done = false;
         if constexpr (GR)
         {
-            epilogue_gate_residual<BN, TL::R>(args, walk, &tmap_o0, &tmap_o1, stg, rfull + quarter * TL::R, tfull,
-                                              tempty, tmem_base, quarter, lane, abort_flag);
+            // split-K units take the reduce-add path of the generic loop below
+            if (args.ksplit <= 1)
+            {
+                epilogue_gate_residual<BN, TL::R>(args, walk, &tmap_o0, &tmap_o1, stg, rfull + quarter * TL::R,
+                                                  tfull, tempty, tmem_base, quarter, lane, abort_flag);
+                done = true;
+            }
         }
-        else
+        if (!done)
         {
             int slot = 0;
             int acc = 0;
@@ -1142,8 +1204,10 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                 if (!ok) break;
                 __syncwarp();
                 tc_fence_after();
+                int khalf;
+                const int tile = unit_tile(args, t, khalf);
                 int stream, m0, n0;
-                walk.decode<BN>(args, t, stream, m0, n0);
+                walk.decode<BN>(args, tile, stream, m0, n0);
                 const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
                 if constexpr (EK == 2)
                 {
@@ -1152,7 +1216,7 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                 else if (args.tma_out)
                 {
                     epilogue_tile_tma<BN>(args, stream ? &tmap_o1 : &tmap_o0, stg, slot, t_row, stream, m0, n0,
-                                          quarter, lane);
+                                          quarter, lane, khalf);
                 }
                 else
                 {
@@ -1259,7 +1323,7 @@ enum TileMode
 // The pair tile needs fewer operand bytes per MMA; a narrower tile is taken
 // only when it fills the SMs markedly more evenly.
 int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const void* A1, const void* W,
-               CUtensorMap& ta0, CUtensorMap& ta1, CUtensorMap& tw, GemmArgs& a, int& mode)
+               CUtensorMap& ta0, CUtensorMap& ta1, CUtensorMap& tw, GemmArgs& a, int& mode, bool allow_split)
 {
     int r = make_tmap_bf16_2d(&ta0, A0, K, M0 > 0 ? M0 : 1, (uint64_t)K * 2, BK, BM);
     if (r == 0) r = make_tmap_bf16_2d(&ta1, M1 > 0 ? A1 : A0, K, M1 > 0 ? M1 : (M0 > 0 ? M0 : 1), (uint64_t)K * 2, BK, BM);
@@ -1273,6 +1337,7 @@ int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const
     a.mblk1 = (M1 + BM - 1) / BM;
     a.num_kb = (K + BK - 1) / BK;
     a.status = ctx.status;
+    a.ksplit = 1;
     auto wave_eff = [&](int tiles, int slots) {
         const int waves = (tiles + slots - 1) / slots;
         return (double)tiles / ((double)waves * slots);
@@ -1284,19 +1349,36 @@ int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const
     const int pairs = ctx.num_sms / 2;
     const double e256 = wave_eff(t256, ctx.num_sms), e128 = wave_eff(t128, ctx.num_sms);
     const double esingle = e128 > 1.15 * e256 ? e128 : e256;
-    if (tpair >= pairs && 1.1 * wave_eff(tpair, pairs) >= esingle)
+    // Split-K by two (gate-residual epilogues, reduce-add into the fp32
+    // output) when whole pair tiles leave a part-empty last wave that half-K
+    // units fill: one GPU's 2,765 rows x N 2560 make 110 pair tiles for 74
+    // pairs (1.49 waves), 220 half-K units make 2.97 -- instead of falling
+    // back to 128 x 128 single-CTA tiles, which read shared memory at the full
+    // 128 B per clock and re-read A for every 128 columns (MLP down at that
+    // size: 116 vs 149 us).  Only long K: half units of K = 2560 are too short
+    // for their epilogue (attention out: 62 vs 49 us).  Large M keeps whole
+    // tiles (and the bit-reproducible store epilogue).
+    int ks = 1;
+    double epair = wave_eff(tpair, pairs);
+    if (allow_split && a.num_kb >= 64 && wave_eff(2 * tpair, pairs) > 1.15 * epair)
+    {
+        ks = 2;
+        epair = wave_eff(2 * tpair, pairs);
+    }
+    if (ks * tpair >= pairs && 1.1 * epair >= esingle)
     {
         mode = TILE_PAIR;
         a.mblk0 = pm0;
         a.mblk1 = pm1;
         a.nblk = (N + 255) / 256;
+        a.ksplit = ks;
     }
     else
     {
         mode = e128 > 1.15 * e256 ? TILE_128 : TILE_256;
         a.nblk = (N + (mode == TILE_128 ? 127 : 255)) / (mode == TILE_128 ? 128 : 256);
     }
-    a.num_tiles = (a.mblk0 + a.mblk1) * a.nblk;
+    a.num_tiles = (a.mblk0 + a.mblk1) * a.nblk * a.ksplit;
     // Raster group height: long-K operands (MLP down) walk N first (height
     // 1: each A block is read once while the weight stays in L2), narrow-N
     // short-K ones (attention out) a medium group; measured on the 720p
@@ -1322,11 +1404,6 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
     if (epilogue == EPI_GELU_TANH && out_f32) return S2_ERR_INVALID;
     if (epilogue < 0 || epilogue > EPI_GATE_RESIDUAL) return S2_ERR_INVALID;
 
-    CUtensorMap ta0, ta1, tw;
-    GemmArgs a;
-    int mode = TILE_256;
-    int r = gemm_setup(ctx, M0, M1, N, K, A0, A1, W, ta0, ta1, tw, a, mode);
-    if (r != 0) return r;
     // TMA-store epilogue when both outputs admit a tensor map (16-byte aligned
     // bases and row strides); the per-thread store path otherwise.
     CUtensorMap to0, to1;
@@ -1338,6 +1415,12 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
     if (tma_out)
         tma_out = make_tmap_2d(&to1, M1 > 0 ? out1 : out0, out_f32, N, M1 > 0 ? M1 : (M0 > 0 ? M0 : 1),
                                (uint64_t)N * esz, box_cols, 32) == S2_OK;
+    CUtensorMap ta0, ta1, tw;
+    GemmArgs a;
+    int mode = TILE_256;
+    int r = gemm_setup(ctx, M0, M1, N, K, A0, A1, W, ta0, ta1, tw, a, mode,
+                       tma_out && epilogue == EPI_GATE_RESIDUAL);
+    if (r != 0) return r;
     if (!tma_out) to1 = to0 = tw;
     a.epilogue = epilogue;
     a.out_f32 = out_f32;
@@ -1391,7 +1474,7 @@ int launch_qkv_packed(Context& ctx, const AttnSchedule& s, int M0, int M1, int K
     CUtensorMap ta0, ta1, tw;
     GemmArgs a;
     int mode = TILE_256;
-    int r = gemm_setup(ctx, M0, M1, N, K, A0, A1, W, ta0, ta1, tw, a, mode);
+    int r = gemm_setup(ctx, M0, M1, N, K, A0, A1, W, ta0, ta1, tw, a, mode, false);
     if (r != 0) return r;
     a.epilogue = EPI_STORE;
     a.bias = bias;

@@ -189,6 +189,16 @@ __device__ __forceinline__ void tma_store_2d(const void* desc, const void* smem_
                  : "memory");
 }
 
+// Tiled 2D reduce-add shared -> global (the tensor map's element type, here
+// f32; the add happens in L2); same extents rule and completion as the store.
+__device__ __forceinline__ void tma_reduce_add_2d(const void* desc, const void* smem_src, int x, int y)
+{
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     desc),
+                 "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+                 : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit()
 {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
