@@ -728,8 +728,37 @@ def main():
         "clocks": clk,
         "device_status": status,
     }
+    # The drop-in layer surface at config 1: AdaptiveWindowAttention::forward(Mat) with host fp32
+    # blobs (upload, prepare + attention + text pool, download), the way an ncnn graph calls it.
+    layer_path = None
+    if rank == 0 and world == 1:
+        import numpy as np
+
+        from seedvr2_ncnn_b200 import layers
+
+        c1_shape, c1_window, c1_mode, _ = CONFIGS["c1"]
+        lrng = np.random.default_rng(5)
+        c1_nv, c1_inner = int(np.prod(c1_shape)), HEADS * 128
+        lkw = dict(heads=HEADS, head_dim=128, target=c1_window, shifted=False, eps=1e-5, rope_pairs=21,
+                   norms=np.ones((4, 128), np.float32),
+                   freqs=(1.0 / 10000 ** (np.arange(21) * 2 / 42)).astype(np.float32), shapes=[c1_shape],
+                   text_lengths=[TEXT],
+                   video_qkv=lrng.standard_normal((c1_nv, 3 * c1_inner)).astype(np.float32),
+                   text_qkv=lrng.standard_normal((TEXT, 3 * c1_inner)).astype(np.float32))
+        times = []
+        for _ in range(6):
+            t0 = time.perf_counter()
+            code, _, _ = layers.awa_forward(**lkw)
+            times.append(time.perf_counter() - t0)
+            if code != 0:
+                raise RuntimeError(f"layer forward returned {code}")
+        layer_path = {"layer": "AdaptiveWindowAttention::forward(Mat), host fp32 blobs in and out",
+                      "workload": CONFIGS["c1"][3] + f", {TEXT} text tokens, {HEADS} heads",
+                      "ms_per_call": 1000.0 * statistics.median(times[1:]),
+                      "host_bytes_per_call": int((c1_nv + TEXT) * c1_inner * 4 * 4)}
     # Everything else goes to a second JSON line on stderr, so the contract line stays short.
     details = {
+        "layer_path_c1": layer_path,
         "kernel_times": "CUDA events around every launch in an instrumented pass of the same steps",
         "ms_per_step_instrumented": ms_instr,
         "sharding": (f"rank 0 owns {n_local} video tokens; qkv rows stored into the window owners' buffers and "
