@@ -8,7 +8,8 @@ Gates:
   frequencies), so only sinf/cosf rounding differs: |gpu - ref| <= 5e-7.
 * frontend / tail with the oracle emulating the device's bf16 activations and
   bf16-valued weights: rel max-abs <= 1e-3 (video, text, prediction),
-  <= 1e-4 (modulation, an fp32 matrix-vector chain).
+  <= 1e-4 (modulation, an fp32 matrix-vector chain); at 720p also against the
+  plain fp32 oracle (fp32 activations): the block gate below.
 * whole DiT step (frontend, blocks, tail) vs the oracle chain in fp32: the
   block gate, cosine >= 0.9995 and rel max-abs <= 2e-2.
 """
@@ -111,7 +112,7 @@ def _frontend_case(gpu_ctx, s2lib, port, *, D, heads, shapes, text_lengths, time
                                      torch.from_numpy(text).cuda())
     torch.cuda.synchronize()
     rv, rt, rmod = port.frontend_forward(io, shapes, timesteps, video, text, emulate_bf16=True)
-    return dit, io, (v, t, mod), (rv, rt, rmod), rng
+    return dit, io, (v, t, mod), (rv, rt, rmod), rng, (video, text)
 
 
 def test_frontend_and_tail_full_width(gpu_ctx, s2lib, port):
@@ -119,11 +120,15 @@ def test_frontend_and_tail_full_width(gpu_ctx, s2lib, port):
     import torch
 
     shapes, tl, ts = [[6, 90, 160]], [58], [437.0]
-    dit, io, (v, t, mod), (rv, rt, rmod), rng = _frontend_case(gpu_ctx, s2lib, port, D=2560, heads=20,
-                                                               shapes=shapes, text_lengths=tl, timesteps=ts, seed=21)
+    dit, io, (v, t, mod), (rv, rt, rmod), rng, (vin, tin) = _frontend_case(
+        gpu_ctx, s2lib, port, D=2560, heads=20, shapes=shapes, text_lengths=tl, timesteps=ts, seed=21)
     assert rel_maxabs(v.cpu().numpy(), rv) <= 1e-3
     assert rel_maxabs(t.cpu().numpy(), rt) <= 1e-3
     assert rel_maxabs(mod.cpu().numpy(), rmod) <= 1e-4
+    # and against the plain fp32 reference (no bf16 rounding anywhere) at the north-star gate
+    fv, ft, _ = port.frontend_forward(io, shapes, ts, vin, tin, emulate_bf16=False)
+    for got, ref in ((v.cpu().numpy(), fv), (t.cpu().numpy(), ft)):
+        assert cosine(got, ref) >= 0.9995 and rel_maxabs(got, ref) <= 2e-2
     # tail on perturbed block output
     x = (rv + rng.standard_normal(rv.shape).astype(np.float32)).astype(np.float32)
     pred = dit.forward_tail(shapes, torch.from_numpy(x).cuda(), mod)
@@ -132,11 +137,13 @@ def test_frontend_and_tail_full_width(gpu_ctx, s2lib, port):
     got = pred.cpu().numpy()
     assert cosine(got, ref) >= 0.99999
     assert rel_maxabs(got, ref) <= 1e-2
+    ref32 = port.tail_forward(io, shapes, x, mod.cpu().numpy(), emulate_bf16=False)
+    assert cosine(got, ref32) >= 0.9995 and rel_maxabs(got, ref32) <= 2e-2
     dit.close()
 
 
 def test_frontend_batch_two(gpu_ctx, s2lib, port):
-    dit, io, (v, t, mod), (rv, rt, rmod), _ = _frontend_case(gpu_ctx, s2lib, port, D=512, heads=4,
+    dit, io, (v, t, mod), (rv, rt, rmod), _, _ = _frontend_case(gpu_ctx, s2lib, port, D=512, heads=4,
                                                              shapes=[[2, 6, 8], [1, 4, 10]], text_lengths=[5, 9],
                                                              timesteps=[999.0, 3.5], seed=22)
     assert rel_maxabs(v.cpu().numpy(), rv) <= 1e-3
