@@ -86,6 +86,12 @@ struct GemmArgs
     int mblk0, mblk1, nblk, num_tiles, num_kb;
     int group_m; // M blocks per raster group (tiles walk M fastest inside a group)
     int ksplit;  // K halves per tile (2: split-K units, gate-residual CTA pairs only; else 1)
+    // split-K ordering: one flag per 32-row x 256-column output box (rows of
+    // stream 1 start at box row split_row32_1); the first half's unit writes
+    // split_epoch into it once its adds have completed
+    unsigned* split_flags;
+    unsigned split_epoch;
+    int split_row32_1;
     int epilogue;
     int out_f32;
     int tma_out; // outputs written through tmap_o0 / tmap_o1
@@ -141,6 +147,40 @@ __device__ __forceinline__ void unit_kblocks(const GemmArgs& a, int khalf, int& 
     const int per = (a.num_kb + a.ksplit - 1) / a.ksplit;
     kb0 = khalf * per;
     kb1 = min(a.num_kb, kb0 + per);
+}
+
+// Split-K ordering flag of the output box whose first row is `row` (a
+// multiple of 32) in `stream`, columns [256 nb, 256 nb + 256).
+__device__ __forceinline__ unsigned* split_flag(const GemmArgs& a, int stream, int row, int nb)
+{
+    return a.split_flags + (size_t)((stream ? a.split_row32_1 : 0) + row / 32) * a.nblk + nb;
+}
+
+// The wait is bounded: a grid that is not resident all at once (other work
+// on the GPU holding SMs) may leave the first half unstarted, and past the
+// limit the add goes ahead unordered -- the sum is complete either way, only
+// its rounding order is then open.  Within one stream's kernels both halves
+// run in the same wave and the wait is the first half's epilogue.
+constexpr uint64_t kSplitWaitNs = 1000000ull;
+
+__device__ __forceinline__ void split_wait_first_half(const unsigned* flag, unsigned epoch)
+{
+    const uint64_t t0 = global_timer_ns();
+    while (ld_acquire_gpu(flag) != epoch)
+    {
+        if (global_timer_ns() - t0 > kSplitWaitNs) break;
+        __nanosleep(64);
+    }
+    fence_proxy_async_global();
+}
+
+// First half done: its reduces have completed (all of this thread's bulk
+// groups), then the flag is released to the second half.
+__device__ __forceinline__ void split_signal_first_half(unsigned* flag, unsigned epoch)
+{
+    bulk_wait<0>();
+    fence_proxy_async_global();
+    st_release_gpu(flag, epoch);
 }
 
 // Tile walk of one CTA: a single CTA per tile, or a CTA pair (cluster of 2)
@@ -287,8 +327,9 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int stream, in
 // free of bank conflicts) and stored by lane 0.  `stg` holds the warp's two
 // 4 KB boxes; `slot` alternates between them.
 // khalf >= 0: a split-K unit of a gate-residual tile -- (acc [+ bias on the
-// first half]) * gate is reduce-added into the fp32 output in L2 (the two
-// halves' adds land in either order), no residual is read.
+// first half]) * gate is reduce-added into the fp32 output in L2, no residual
+// is read.  The second half's first add waits for the first half's flag, so
+// every element is (r + first) + second on every run.
 template <int BN>
 __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const CUtensorMap* tmap_out, uint8_t* stg, int& slot,
                                                   uint32_t t_row, int stream, int m0, int n0, int quarter, int lane,
@@ -424,6 +465,8 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const CUten
         {
             if (box_live)
             {
+                if (split && khalf == 1 && c0 == 0)
+                    split_wait_first_half(split_flag(a, stream, m0 + quarter * 32, n0 / BN), a.split_epoch);
                 if (split)
                     tma_reduce_add_2d(tmap_out, stg + slot * 4096, n0 + c0, m0 + quarter * 32);
                 else
@@ -1232,6 +1275,12 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) walk.arrive_tempty(&tempty[acc]);
+                if constexpr (GR)
+                {
+                    if (khalf == 0 && lane == 0)
+                        split_signal_first_half(split_flag(args, stream, m0 + quarter * 32, n0 / BN),
+                                                args.split_epoch);
+                }
                 acc ^= 1;
                 if (acc == 0) acc_phase ^= 1;
             }
@@ -1357,10 +1406,13 @@ int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const
     // 128 B per clock and re-read A for every 128 columns (MLP down at that
     // size: 116 vs 149 us).  Only long K: half units of K = 2560 are too short
     // for their epilogue (attention out: 62 vs 49 us).  Large M keeps whole
-    // tiles (and the bit-reproducible store epilogue).
+    // tiles.  The halves' adds are ordered through one flag per 32 x 256
+    // output box, so results do not depend on the run.
     int ks = 1;
     double epair = wave_eff(tpair, pairs);
-    if (allow_split && a.num_kb >= 64 && wave_eff(2 * tpair, pairs) > 1.15 * epair)
+    const int split_boxes = (pm0 + pm1) * (2 * BM / 32) * ((N + 255) / 256);
+    if (allow_split && ctx.split_flags && split_boxes <= ctx.split_slots && a.num_kb >= 64 &&
+        wave_eff(2 * tpair, pairs) > 1.15 * epair)
     {
         ks = 2;
         epair = wave_eff(2 * tpair, pairs);
@@ -1372,6 +1424,21 @@ int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const
         a.mblk1 = pm1;
         a.nblk = (N + 255) / 256;
         a.ksplit = ks;
+        if (ks > 1)
+        {
+            // a fresh epoch per split launch; flags left by earlier launches
+            // (or by one that stopped early) hold other values
+            if (++ctx.split_epoch == 0)
+            {
+                if (cudaMemsetAsync(ctx.split_flags, 0, (size_t)ctx.split_slots * sizeof(unsigned), ctx.stream) !=
+                    cudaSuccess)
+                    return S2_ERR_CUDA;
+                ctx.split_epoch = 1;
+            }
+            a.split_flags = ctx.split_flags;
+            a.split_epoch = ctx.split_epoch;
+            a.split_row32_1 = pm0 * (2 * BM / 32);
+        }
     }
     else
     {

@@ -95,6 +95,16 @@ int s2_init(int device, void* stream, s2_context** out)
         delete c;
         return S2_ERR_CUDA;
     }
+    constexpr int kSplitFlagSlots = 16384;
+    if (cudaMalloc(&c->c.split_flags, kSplitFlagSlots * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(c->c.split_flags, 0, kSplitFlagSlots * sizeof(unsigned)) != cudaSuccess)
+    {
+        if (c->c.split_flags) cudaFree(c->c.split_flags);
+        cudaFree(c->c.status);
+        delete c;
+        return S2_ERR_ALLOC;
+    }
+    c->c.split_slots = kSplitFlagSlots;
     *out = c;
     return S2_OK;
 }
@@ -109,6 +119,7 @@ void s2_destroy(s2_context* ctx)
     ctx->dist.reset();
     ctx->c.prof.release();
     for (auto& b : ctx->c.ws) b.release();
+    if (ctx->c.split_flags) cudaFree(ctx->c.split_flags);
     if (ctx->c.status) cudaFree(ctx->c.status);
     delete ctx;
 }

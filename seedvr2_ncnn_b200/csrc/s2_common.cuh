@@ -225,6 +225,27 @@ __device__ __forceinline__ void fence_proxy_async_smem()
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// The same between the async proxy (bulk stores and reduces) and the generic
+// proxy for global memory: after bulk_wait<0>, it orders this thread's
+// completed bulk writes before its later flag store; after a flag load, it
+// orders the load before this thread's later bulk writes.
+__device__ __forceinline__ void fence_proxy_async_global()
+{
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__device__ __forceinline__ void st_release_gpu(unsigned* p, unsigned v)
+{
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // ---------------------------------------------------------------- tcgen05
 // Shared-memory matrix descriptor (tcgen05 "matrix descriptor"):
 //  [0,14) start address >> 4, [16,30) leading byte offset >> 4,

@@ -69,6 +69,12 @@ struct Context
     cudaStream_t stream = nullptr;
     int num_sms = 148;
     int* status = nullptr; // device status word
+    // Split-K ordering flags (one per 32-row x 256-column output box of a
+    // split GEMM; zero at creation) and the launch epoch written into them.
+    // A context without them runs no split-K GEMM.
+    unsigned* split_flags = nullptr;
+    int split_slots = 0;
+    unsigned split_epoch = 0;
     uint64_t launches = 0;
     Profiler prof;
     // workspace slots (see s2_api.cu for their use)

@@ -72,6 +72,35 @@ def test_shared_linear_vs_torch(gpu_ctx, s2lib, M0, M1, N, K, epi):
         assert rel_maxabs(x, y) <= 1e-2
 
 
+@pytest.mark.parametrize("M0,M1", [(2758, 0), (2500, 58)])
+def test_split_k_gate_residual_reproducible(gpu_ctx, s2lib, M0, M1):
+    """Split-K units (K = 10240 at these M: 110 CTA-pair tiles for 74 pairs,
+    run as 220 half-K units) reduce-add both halves into the fp32 residual;
+    the second half waits for the first, so repeated runs agree bit for bit
+    (the 8-GPU step relies on it for the text rows every rank computes)."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(5)
+    N, K = 2560, 10240
+    a0 = torch.randn(M0, K, device="cuda", generator=g).bfloat16()
+    a1 = torch.randn(M1, K, device="cuda", generator=g).bfloat16() if M1 else None
+    w = (0.05 * torch.randn(N, K, device="cuda", generator=g)).bfloat16()
+    bias = 0.1 * torch.randn(N, device="cuda", generator=g)
+    gate = torch.randn(N, device="cuda", generator=g)
+    r0 = torch.randn(M0, N, device="cuda", generator=g)
+    r1 = torch.randn(M1, N, device="cuda", generator=g) if M1 else None
+    runs = []
+    for _ in range(6):
+        o0, o1 = r0.clone(), (r1.clone() if M1 else None)
+        s2lib.shared_linear(gpu_ctx, a0, w, bias, a1=a1, epilogue=s2lib.S2_EPI_GATE_RESIDUAL, gate=gate,
+                            out_dtype=s2lib.S2_DTYPE_F32, out0=o0, out1=o1)
+        runs.append(torch.cat([o0] + ([o1] if M1 else [])))
+    torch.cuda.synchronize()
+    assert gpu_ctx.status() == 0
+    for x in runs[1:]:
+        assert torch.equal(x, runs[0])
+
+
 def test_shared_linear_full_width_qkv(gpu_ctx, s2lib):
     """720p QKV projection shape (M = 21600 + 58, N = 7680, K = 2560), rows sampled."""
     import torch

@@ -4,7 +4,9 @@ single-GPU forward.  Runs only where the box has at least 2 GPUs; NVLS is off
 (NCCL_NVLS_ENABLE=0; NCCL only sets up the communicator and the IPC handle
 exchange).  Cases with D % 256 == 0 take the fused path (the QKV projection
 stores rows into the window owners' packed buffers); D = 384 takes the qkv
-push + prepare path.
+push + prepare path.  The 1 x 45 x 120 case leaves 2,758 rows per rank, where
+the MLP-down projection (K = 10240) runs as split-K CTA pairs reduce-adding
+into the residual, against whole tiles in the single-GPU run (5,458 rows).
 
 Rows are computed by the same kernels in both runs; only the text-pool sum
 order (partials summed over ranks) differs, which can flip the bf16 rounding
@@ -26,6 +28,7 @@ CASES = [
     ([2, 12, 20], [1, 8, 8], 1, 512, 4, 2048, 2),
     ([6, 45, 80], [4, 3, 4], 0, 2560, 20, 10240, 2),
     ([2, 8, 12], [1, 4, 6], 1, 384, 3, 1536, 2),
+    ([1, 45, 120], [1, 15, 20], 0, 2560, 20, 10240, 2),
 ]
 
 
