@@ -121,15 +121,17 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& a, int t, int& strea
     n0 = nb * BN;
 }
 
-// Work unit t -> its tile and K part: with split-K the units of one tile are
-// adjacent (t = tile * ksplit + khalf); khalf = -1 without a split.
+// Work unit t -> its tile and K part: with split-K every tile's first half
+// comes before any second half (t = khalf * tiles + tile), so a second half
+// -- which adds only after its first half's adds have landed -- normally
+// runs a round after it and finds its flag set; khalf = -1 without a split.
 __device__ __forceinline__ int unit_tile(const GemmArgs& a, int t, int& khalf)
 {
     if (a.ksplit > 1)
     {
-        const int tile = t / a.ksplit;
-        khalf = t - tile * a.ksplit;
-        return tile;
+        const int tiles = a.num_tiles / a.ksplit;
+        khalf = t / tiles;
+        return t - khalf * tiles;
     }
     khalf = -1;
     return t;
@@ -160,7 +162,8 @@ __device__ __forceinline__ unsigned* split_flag(const GemmArgs& a, int stream, i
 // on the GPU holding SMs) may leave the first half unstarted, and past the
 // limit the add goes ahead unordered -- the sum is complete either way, only
 // its rounding order is then open.  Within one stream's kernels both halves
-// run in the same wave and the wait is the first half's epilogue.
+// run a round apart (or, with fewer tiles than CTA pairs, side by side) and
+// the wait is at most the first half's epilogue.
 constexpr uint64_t kSplitWaitNs = 1000000ull;
 
 __device__ __forceinline__ void split_wait_first_half(const unsigned* flag, unsigned epoch)
