@@ -1407,7 +1407,7 @@ int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const
     // pairs (1.49 waves), 220 half-K units make 2.97 -- instead of falling
     // back to 128 x 128 single-CTA tiles, which read shared memory at the full
     // 128 B per clock and re-read A for every 128 columns (MLP down at that
-    // size: 116 vs 149 us).  Only long K: half units of K = 2560 are too short
+    // size: 110 vs 149 us).  Only long K: half units of K = 2560 are too short
     // for their epilogue (attention out: 62 vs 49 us).  Large M keeps whole
     // tiles.  The halves' adds are ordered through one flag per 32 x 256
     // output box, so results do not depend on the run.
