@@ -143,41 +143,70 @@ __global__ void prepare_qkv_kernel(const int* __restrict__ row_src, const int* _
 
 // ---------------------------------------------------------------- text pool
 // Replaces the text branch of the scatter (CPU :963-974, shader :395-407):
-// text_out[t] = sum over the sample's windows (in window order) of
-// partial[w][t] * (1 / windows in sample).
-__global__ void text_pool_kernel(const int4* __restrict__ reduce, const float* __restrict__ scale_of, int inner,
-                                 const float* __restrict__ partial, int out_f32, void* out, int partial_rows,
-                                 int* status)
+// text_out[t] = sum over the sample's windows of partial[w][t] * (1 / windows
+// in sample).  A block covers 128 column quads of one text row with
+// kTextPoolParts threads per quad: part g sums the g-th contiguous run of the
+// windows in window order, and the parts are added in part order through
+// shared memory -- a fixed order, so the result does not depend on the run,
+// with four times the loads in flight of one thread per quad (the pass is
+// bound by memory latency: 36-80 dependent rows per quad).
+constexpr int kTextPoolParts = 4;
+constexpr int kTextPoolQuads = 128;
+
+__global__ void __launch_bounds__(kTextPoolQuads * kTextPoolParts)
+    text_pool_kernel(const int4* __restrict__ reduce, const float* __restrict__ scale_of, int inner,
+                     const float* __restrict__ partial, int out_f32, void* out, int partial_rows, int* status)
 {
+    __shared__ float4 part_sum[kTextPoolParts - 1][kTextPoolQuads];
     const int t = blockIdx.x;
-    const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
-    if (c >= inner) return;
+    const int g = threadIdx.y;
+    const int c = (blockIdx.y * kTextPoolQuads + threadIdx.x) * 4;
     const int4 rd = reduce[t];
-    // every partial row summed lies in the partial buffer (first and last, stride >= 0)
+    // every partial row summed lies in the partial buffer (first and last,
+    // stride >= 0); the outcome is the same for the whole block
     if (rd.z > 0 && !(index_ok(rd.x, partial_rows, status) && rd.y >= 0 &&
                       index_ok(rd.x + (int64_t)(rd.z - 1) * rd.y, partial_rows, status)))
         return;
+    const bool live = c < inner;
     const float sc = scale_of[t];
+    // windows [w0, w1) of this part
+    const int w0 = (int)((int64_t)rd.z * g / kTextPoolParts), w1 = (int)((int64_t)rd.z * (g + 1) / kTextPoolParts);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    const float* base = partial + (int64_t)rd.x * inner + c;
-    const int64_t step = (int64_t)rd.y * inner;
-    auto add = [&](const float4 p) {
-        acc.x += p.x * sc;
-        acc.y += p.y * sc;
-        acc.z += p.z * sc;
-        acc.w += p.w * sc;
-    };
-    // eight loads in flight, summed in window order
-    int i = 0;
-    for (; i + 8 <= rd.z; i += 8)
+    if (live)
     {
-        float4 p[8];
+        const float* base = partial + (int64_t)rd.x * inner + c;
+        const int64_t step = (int64_t)rd.y * inner;
+        auto add = [&](const float4 p) {
+            acc.x += p.x * sc;
+            acc.y += p.y * sc;
+            acc.z += p.z * sc;
+            acc.w += p.w * sc;
+        };
+        // rounds of eight loads; the last round's surplus loads re-read the
+        // part's last row and are replaced by zero before the add
+        const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i = w0; i < w1; i += 8)
+        {
+            float4 p[8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) p[k] = __ldg(reinterpret_cast<const float4*>(base + (i + k) * step));
+            for (int k = 0; k < 8; k++)
+                p[k] = __ldg(reinterpret_cast<const float4*>(base + min(i + k, w1 - 1) * step));
 #pragma unroll
-        for (int k = 0; k < 8; k++) add(p[k]);
+            for (int k = 0; k < 8; k++) add(i + k < w1 ? p[k] : zero);
+        }
     }
-    for (; i < rd.z; i++) add(__ldg(reinterpret_cast<const float4*>(base + i * step)));
+    if (g > 0) part_sum[g - 1][threadIdx.x] = acc;
+    __syncthreads();
+    if (g > 0 || !live) return;
+#pragma unroll
+    for (int k = 0; k < kTextPoolParts - 1; k++)
+    {
+        const float4 q = part_sum[k][threadIdx.x];
+        acc.x += q.x;
+        acc.y += q.y;
+        acc.z += q.z;
+        acc.w += q.w;
+    }
     if (out_f32)
         *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (int64_t)t * inner + c) = acc;
     else
@@ -399,11 +428,12 @@ int launch_text_pool(Context& ctx, const AttnSchedule& s, int inner, const float
     (void)round_bf16;
     if (s.total_text == 0) return S2_OK;
     if (inner % 4) return S2_ERR_INVALID;
-    const int threads = 256;
-    const dim3 grid(s.total_text, (inner / 4 + threads - 1) / threads);
+    // 128 column quads per block: D = 2560 fills five blocks per text row exactly
+    const dim3 block(kTextPoolQuads, kTextPoolParts);
+    const dim3 grid(s.total_text, (inner / 4 + kTextPoolQuads - 1) / kTextPoolQuads);
     ProfileScope prof(ctx, K_POOL, 0.0,
                       (double)s.partial_rows * inner * 4.0 + (double)s.total_text * inner * (out_f32 ? 4.0 : 2.0));
-    text_pool_kernel<<<grid, threads, 0, ctx.stream>>>(s.text_reduce, s.text_scale, inner, partial, out_f32,
+    text_pool_kernel<<<grid, block, 0, ctx.stream>>>(s.text_reduce, s.text_scale, inner, partial, out_f32,
                                                         text_out, s.partial_rows, ctx.status);
     return finish(ctx);
 }
