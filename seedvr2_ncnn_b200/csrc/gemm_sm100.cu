@@ -92,6 +92,10 @@ struct GemmArgs
     unsigned* split_flags;
     unsigned split_epoch;
     int split_row32_1;
+    // narrow tail (CTA pairs, no split): units from full_units on are the two
+    // 128-column halves of the last tiles
+    int narrow;
+    int full_units;
     int epilogue;
     int out_f32;
     int tma_out; // outputs written through tmap_o0 / tmap_o1
@@ -186,16 +190,40 @@ __device__ __forceinline__ void split_signal_first_half(unsigned* flag, unsigned
     st_release_gpu(flag, epoch);
 }
 
+// Pair-mode unit t -> its tile's stream, first row (of the 256-row pair
+// tile) and first column; returns the unit's width.  Split-K units cover
+// their tile's full width.  With a narrow tail, a last wave of at most half
+// the CTA pairs' worth of tiles runs as one round of 256 x 128 units (both
+// halves of each of those tiles) instead of one round of full tiles.
+__device__ __forceinline__ int pair_unit(const GemmArgs& a, int t, int& stream, int& m0, int& n0)
+{
+    int khalf;
+    int tile = unit_tile(a, t, khalf);
+    int half = -1;
+    if (a.narrow && t >= a.full_units)
+    {
+        const int u = t - a.full_units;
+        tile = a.full_units + (u >> 1);
+        half = u & 1;
+    }
+    decode_tile<256, 2 * BM>(a, tile, stream, m0, n0);
+    if (half < 0) return 256;
+    n0 += half * 128;
+    return 128;
+}
+
 // Tile walk of one CTA: a single CTA per tile, or a CTA pair (cluster of 2)
 // per 256-row tile, each CTA owning 128 of its rows.
 struct SingleWalk
 {
     __device__ int first() const { return blockIdx.x; }
     __device__ int step() const { return gridDim.x; }
+    // unit t -> (stream, first row, first column); returns the unit's width
     template <int BN>
-    __device__ void decode(const GemmArgs& a, int t, int& stream, int& m0, int& n0) const
+    __device__ int decode(const GemmArgs& a, int t, int& stream, int& m0, int& n0) const
     {
         decode_tile<BN>(a, t, stream, m0, n0);
+        return BN;
     }
     __device__ void arrive_tempty(uint64_t* bar) const { mbar_arrive(bar); }
 };
@@ -205,11 +233,14 @@ struct PairWalk
     uint32_t rank; // 0 = leader (issues the MMAs)
     __device__ int first() const { return blockIdx.x >> 1; }
     __device__ int step() const { return gridDim.x >> 1; }
+    // unit t -> this CTA's rows (stream, first row, first column); returns
+    // the unit's width
     template <int BN>
-    __device__ void decode(const GemmArgs& a, int t, int& stream, int& m0, int& n0) const
+    __device__ int decode(const GemmArgs& a, int t, int& stream, int& m0, int& n0) const
     {
-        decode_tile<BN, 2 * BM>(a, t, stream, m0, n0);
+        const int w = pair_unit(a, t, stream, m0, n0);
         m0 += (int)rank * BM;
+        return w;
     }
     // accumulator release goes to the leader's barrier
     __device__ void arrive_tempty(uint64_t* bar) const { mbar_arrive_cluster(mapa_shared(bar, 0)); }
@@ -336,7 +367,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int stream, in
 template <int BN>
 __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const CUtensorMap* tmap_out, uint8_t* stg, int& slot,
                                                   uint32_t t_row, int stream, int m0, int n0, int quarter, int lane,
-                                                  int khalf = -1)
+                                                  int khalf = -1, int width = BN)
 {
     const bool split = khalf >= 0;
     const int M = stream ? a.M1 : a.M0;
@@ -348,7 +379,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& a, const CUten
     const float* res_row = reinterpret_cast<const float*>(stream ? a.out1 : a.out0) + (size_t)row * N;
     const int sw = lane & 7;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN && n0 + c0 < N; c0 += box_cols)
+    for (int c0 = 0; c0 < width && n0 + c0 < N; c0 += box_cols)
     {
         if (lane == 0) bulk_wait_read<1>(); // this slot's previous store has read it
         __syncwarp();
@@ -677,13 +708,13 @@ __device__ __forceinline__ bool epilogue_gate_residual(const GemmArgs& a, const 
     auto issue_load = [&]() {
         if (lt >= a.num_tiles) return;
         int s_, m0_, n0_;
-        wk.template decode<BN>(a, lt, s_, m0_, n0_);
+        const int w_ = wk.template decode<BN>(a, lt, s_, m0_, n0_);
         const int slot = lq % R;
         mbar_arrive_expect_tx(&rfull[slot], 4096);
         tma_load_2d(stg + slot * 4096, s_ ? tmap_o1 : tmap_o0, &rfull[slot], n0_ + lc, m0_ + quarter * 32);
         lq++;
         lc += 32;
-        if (lc >= BN || n0_ + lc >= N)
+        if (lc >= w_ || n0_ + lc >= N)
         {
             lc = 0;
             lt += wk.step();
@@ -708,12 +739,12 @@ __device__ __forceinline__ bool epilogue_gate_residual(const GemmArgs& a, const 
         __syncwarp();
         tc_fence_after();
         int stream, m0, n0;
-        wk.template decode<BN>(a, t, stream, m0, n0);
+        const int width = wk.template decode<BN>(a, t, stream, m0, n0);
         const int M = stream ? a.M1 : a.M0;
         const bool box_live = m0 + quarter * 32 < M;
         const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN && n0 + c0 < N; c0 += 32, q++)
+        for (int c0 = 0; c0 < width && n0 + c0 < N; c0 += 32, q++)
         {
             const int slot = q % R;
             int r = 0;
@@ -1040,6 +1071,7 @@ struct PairTile
     static constexpr int R = (224 * 1024 - STAGES * STAGE_BYTES) / (4 * 4096);
     static constexpr int TMEM_COLS = 512; // two 256-column accumulators
     static constexpr uint32_t IDESC = umma_idesc_bf16(256, 256, 0, 0);
+    static constexpr uint32_t IDESC_NARROW = umma_idesc_bf16(256, 128, 0, 0); // narrow-tail units
     static constexpr int EPI_BYTES = 4 * R * 4096;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 512;
     static_assert(SMEM_BYTES <= 232448, "shared memory");
@@ -1048,8 +1080,9 @@ struct PairTile
 template <int SKB, int EK>
 __global__ void __launch_bounds__(num_threads(EK), 1)
     shared_linear_pair_kernel(const __grid_constant__ CUtensorMap tmap_a0, const __grid_constant__ CUtensorMap tmap_a1,
-                              const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_o0,
-                              const __grid_constant__ CUtensorMap tmap_o1, const GemmArgs args)
+                              const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_w64,
+                              const __grid_constant__ CUtensorMap tmap_o0, const __grid_constant__ CUtensorMap tmap_o1,
+                              const GemmArgs args)
 {
     constexpr int BN = 256;
     using TL = PairTile<SKB, EK>;
@@ -1095,6 +1128,7 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
         tma_prefetch_desc(&tmap_a0);
         tma_prefetch_desc(&tmap_a1);
         tma_prefetch_desc(&tmap_w);
+        if (args.narrow) tma_prefetch_desc(&tmap_w64);
         if (args.tma_out)
         {
             tma_prefetch_desc(&tmap_o0);
@@ -1122,22 +1156,24 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
             for (int t = walk.first(); t < args.num_tiles && !*abort_flag; t += walk.step())
             {
                 int khalf, kb0, kb1;
-                const int tile = unit_tile(args, t, khalf);
+                unit_tile(args, t, khalf);
                 unit_kblocks(args, khalf, kb0, kb1);
                 int stream, m0, n0p;
-                decode_tile<BN, 2 * BM>(args, tile, stream, m0, n0p);
-                m0 += (int)walk.rank * BM;
-                const int nb = n0p + (int)walk.rank * 128;
+                const int width = walk.decode<BN>(args, t, stream, m0, n0p);
+                // each CTA loads its half of the unit's W rows (a 64-row box for narrow units)
+                const int nb = n0p + (int)walk.rank * (width / 2);
                 const CUtensorMap* ta = stream ? &tmap_a1 : &tmap_a0;
+                const CUtensorMap* tw = width == BN ? &tmap_w : &tmap_w64;
+                const uint32_t stage_tx = width == BN ? 2 * STAGE_BYTES : 2 * (TL::A_STAGE + TL::B_STAGE / 2);
                 for (int kb = kb0; kb < kb1; kb++)
                 {
                     if (!mbar_wait<true>(&empty[stage], phase ^ 1, abort_flag, args.status)) break;
                     uint8_t* sa = smem + stage * STAGE_BYTES;
                     uint8_t* sb = sa + TL::A_STAGE;
-                    if (leader) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
+                    if (leader) mbar_arrive_expect_tx(&full[stage], stage_tx);
                     const uint32_t fb = mapa_shared(&full[stage], 0);
                     tma_load_2d_pair(sa, ta, fb, kb * BK, m0);
-                    tma_load_2d_pair(sb, &tmap_w, fb, kb * BK, nb);
+                    tma_load_2d_pair(sb, tw, fb, kb * BK, nb);
                     issued[stage] = 1;
                     last_phase[stage] = phase;
                     if (++stage == STAGES)
@@ -1173,6 +1209,8 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                 int khalf, kb0, kb1;
                 unit_tile(args, t, khalf);
                 unit_kblocks(args, khalf, kb0, kb1);
+                int us, um, un;
+                const uint32_t idesc = walk.decode<BN>(args, t, us, um, un) == BN ? TL::IDESC : TL::IDESC_NARROW;
                 bool ok = true;
                 for (int kb = kb0; kb < kb1; kb++)
                 {
@@ -1189,7 +1227,7 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                     {
                         const uint64_t ad = umma_desc_sw128(a_addr + k * 32, 16, 1024);
                         const uint64_t bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
-                        umma_bf16_pair(d_tmem, ad, bd, TL::IDESC, (kb != kb0) || k != 0);
+                        umma_bf16_pair(d_tmem, ad, bd, idesc, (kb != kb0) || k != 0);
                     }
                     umma_commit_pair(&empty[stage], 0x3);
                     if (++stage == STAGES)
@@ -1251,9 +1289,9 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                 __syncwarp();
                 tc_fence_after();
                 int khalf;
-                const int tile = unit_tile(args, t, khalf);
+                unit_tile(args, t, khalf);
                 int stream, m0, n0;
-                walk.decode<BN>(args, tile, stream, m0, n0);
+                const int width = walk.decode<BN>(args, t, stream, m0, n0);
                 const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
                 if constexpr (EK == 2)
                 {
@@ -1262,12 +1300,12 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
                 else if (args.tma_out)
                 {
                     epilogue_tile_tma<BN>(args, stream ? &tmap_o1 : &tmap_o0, stg, slot, t_row, stream, m0, n0,
-                                          quarter, lane, khalf);
+                                          quarter, lane, khalf, width);
                 }
                 else
                 {
 #pragma unroll 1
-                    for (int c = 0; c < BN / 32; c++)
+                    for (int c = 0; c < width / 32; c++)
                     {
                         uint32_t v[32];
                         tmem_ld32(t_row + c * 32, v);
@@ -1303,8 +1341,8 @@ __global__ void __launch_bounds__(num_threads(EK), 1)
 // that can be resident at once (cudaOccupancyMaxActiveClusters).
 template <int SKB, int EK>
 cudaError_t launch_pair_variant(cudaStream_t stream, const CUtensorMap& ta0, const CUtensorMap& ta1,
-                                const CUtensorMap& tw, const CUtensorMap& to0, const CUtensorMap& to1,
-                                const GemmArgs& a)
+                                const CUtensorMap& tw, const CUtensorMap& tw64, const CUtensorMap& to0,
+                                const CUtensorMap& to1, const GemmArgs& a)
 {
     static std::atomic<uint64_t> configured{0}; // per instantiation and device
     static std::atomic<int> max_clusters{0};     // the same on every B200
@@ -1340,7 +1378,39 @@ cudaError_t launch_pair_variant(cudaStream_t stream, const CUtensorMap& ta0, con
     cfg.gridDim = dim3(2 * pairs);
     cfg.blockDim = dim3(num_threads(EK));
     cfg.dynamicSmemBytes = PairTile<SKB, EK>::SMEM_BYTES;
-    return cudaLaunchKernelEx(&cfg, shared_linear_pair_kernel<SKB, EK>, ta0, ta1, tw, to0, to1, a);
+    return cudaLaunchKernelEx(&cfg, shared_linear_pair_kernel<SKB, EK>, ta0, ta1, tw, tw64, to0, to1, a);
+}
+
+// CTA pairs resident at once (every pair kernel holds one CTA per SM, so
+// one configuration answers for all), queried once per process; half the
+// SMs if the query fails.
+int pair_slots(const Context& ctx)
+{
+    static std::atomic<int> slots{0};
+    int n = slots.load();
+    if (n > 0) return n;
+    using TL = PairTile<192, 1>;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(num_threads(1));
+    cfg.dynamicSmemBytes = TL::SMEM_BYTES;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    n = 0;
+    if (cudaFuncSetAttribute(shared_linear_pair_kernel<192, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             TL::SMEM_BYTES) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, shared_linear_pair_kernel<192, 1>, &cfg) != cudaSuccess || n <= 0)
+    {
+        (void)cudaGetLastError();
+        n = ctx.num_sms / 2;
+    }
+    slots.store(n);
+    return n;
 }
 
 template <int BN, int SKB, int EK>
@@ -1375,7 +1445,8 @@ enum TileMode
 // The pair tile needs fewer operand bytes per MMA; a narrower tile is taken
 // only when it fills the SMs markedly more evenly.
 int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const void* A1, const void* W,
-               CUtensorMap& ta0, CUtensorMap& ta1, CUtensorMap& tw, GemmArgs& a, int& mode, bool allow_split)
+               CUtensorMap& ta0, CUtensorMap& ta1, CUtensorMap& tw, CUtensorMap& tw64, GemmArgs& a, int& mode,
+               bool allow_split, bool allow_narrow)
 {
     int r = make_tmap_bf16_2d(&ta0, A0, K, M0 > 0 ? M0 : 1, (uint64_t)K * 2, BK, BM);
     if (r == 0) r = make_tmap_bf16_2d(&ta1, M1 > 0 ? A1 : A0, K, M1 > 0 ? M1 : (M0 > 0 ? M0 : 1), (uint64_t)K * 2, BK, BM);
@@ -1398,7 +1469,7 @@ int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const
     const int t128 = (a.mblk0 + a.mblk1) * ((N + 127) / 128);
     const int pm0 = (M0 + 2 * BM - 1) / (2 * BM), pm1 = (M1 + 2 * BM - 1) / (2 * BM);
     const int tpair = (pm0 + pm1) * ((N + 255) / 256);
-    const int pairs = ctx.num_sms / 2;
+    const int pairs = pair_slots(ctx);
     const double e256 = wave_eff(t256, ctx.num_sms), e128 = wave_eff(t128, ctx.num_sms);
     const double esingle = e128 > 1.15 * e256 ? e128 : e256;
     // Split-K by two (gate-residual epilogues, reduce-add into the fp32
@@ -1420,6 +1491,14 @@ int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const
         ks = 2;
         epair = wave_eff(2 * tpair, pairs);
     }
+    // Narrow tail: a last wave of r <= pairs / 2 tiles runs as 2r units of
+    // 256 x 128 in one round of about 0.65 of a full one (half the MMAs; the
+    // operand traffic per MMA is higher).  Attention-out at 2,765 rows: 110
+    // tiles for 74 pairs, 1.49 rounds of whole tiles -> 1 + 0.65.
+    constexpr double kNarrowRound = 0.65;
+    const int tail = tpair % pairs;
+    const bool narrow = allow_narrow && ks == 1 && tpair >= pairs && tail > 0 && 2 * tail <= pairs;
+    if (narrow) epair = (double)tpair / (((double)(tpair / pairs) + kNarrowRound) * pairs);
     if (ks * tpair >= pairs && 1.1 * epair >= esingle)
     {
         mode = TILE_PAIR;
@@ -1449,12 +1528,23 @@ int gemm_setup(Context& ctx, int M0, int M1, int N, int K, const void* A0, const
         a.nblk = (N + (mode == TILE_128 ? 127 : 255)) / (mode == TILE_128 ? 128 : 256);
     }
     a.num_tiles = (a.mblk0 + a.mblk1) * a.nblk * a.ksplit;
+    if (mode == TILE_PAIR && narrow)
+    {
+        a.narrow = 1;
+        a.full_units = tpair - tail;
+        a.num_tiles = tpair + tail;
+    }
     // Raster group height: long-K operands (MLP down) walk N first (height
     // 1: each A block is read once while the weight stays in L2), narrow-N
     // short-K ones (attention out) a medium group; measured on the 720p
     // shapes (differences of 2-4 %).
     a.group_m = K >= 8192 ? 1 : (N <= 4096 ? 8 : 16);
-    return make_tmap_bf16_2d(&tw, W, K, N, (uint64_t)K * 2, BK, mode == TILE_256 ? 256 : 128);
+    r = make_tmap_bf16_2d(&tw, W, K, N, (uint64_t)K * 2, BK, mode == TILE_256 ? 256 : 128);
+    if (r != 0) return r;
+    // narrow units load 64 of W's rows per CTA
+    if (a.narrow) return make_tmap_bf16_2d(&tw64, W, K, N, (uint64_t)K * 2, BK, 64);
+    tw64 = tw;
+    return 0;
 }
 
 int grid_of(const Context& ctx, const GemmArgs& a)
@@ -1485,11 +1575,11 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
     if (tma_out)
         tma_out = make_tmap_2d(&to1, M1 > 0 ? out1 : out0, out_f32, N, M1 > 0 ? M1 : (M0 > 0 ? M0 : 1),
                                (uint64_t)N * esz, box_cols, 32) == S2_OK;
-    CUtensorMap ta0, ta1, tw;
+    CUtensorMap ta0, ta1, tw, tw64;
     GemmArgs a;
     int mode = TILE_256;
-    int r = gemm_setup(ctx, M0, M1, N, K, A0, A1, W, ta0, ta1, tw, a, mode,
-                       tma_out && epilogue == EPI_GATE_RESIDUAL);
+    int r = gemm_setup(ctx, M0, M1, N, K, A0, A1, W, ta0, ta1, tw, tw64, a, mode,
+                       tma_out && epilogue == EPI_GATE_RESIDUAL, true);
     if (r != 0) return r;
     if (!tma_out) to1 = to0 = tw;
     a.epilogue = epilogue;
@@ -1508,9 +1598,9 @@ int launch_shared_linear(Context& ctx, int M0, int M1, int N, int K, const void*
     const bool deep = gr && K < 4096; // deep residual prefetch for short K
     cudaError_t e;
     if (mode == TILE_PAIR)
-        e = deep ? launch_pair_variant<160, 1>(ctx.stream, ta0, ta1, tw, to0, to1, a)
-            : gr ? launch_pair_variant<192, 1>(ctx.stream, ta0, ta1, tw, to0, to1, a)
-                 : launch_pair_variant<192, 0>(ctx.stream, ta0, ta1, tw, to0, to1, a);
+        e = deep ? launch_pair_variant<160, 1>(ctx.stream, ta0, ta1, tw, tw64, to0, to1, a)
+            : gr ? launch_pair_variant<192, 1>(ctx.stream, ta0, ta1, tw, tw64, to0, to1, a)
+                 : launch_pair_variant<192, 0>(ctx.stream, ta0, ta1, tw, tw64, to0, to1, a);
     else if (mode == TILE_128)
         e = deep ? launch_variant<128, 144, 1>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
             : gr ? launch_variant<128, 192, 1>(grid, ctx.stream, ta0, ta1, tw, to0, to1, a)
@@ -1541,10 +1631,10 @@ int launch_qkv_packed(Context& ctx, const AttnSchedule& s, int M0, int M1, int K
         if (reinterpret_cast<uintptr_t>(o) & 15) return S2_ERR_INVALID;
     if (s.packed_rows == 0) return S2_OK;
     const int N = 3 * D;
-    CUtensorMap ta0, ta1, tw;
+    CUtensorMap ta0, ta1, tw, tw64;
     GemmArgs a;
     int mode = TILE_256;
-    int r = gemm_setup(ctx, M0, M1, N, K, A0, A1, W, ta0, ta1, tw, a, mode, false);
+    int r = gemm_setup(ctx, M0, M1, N, K, A0, A1, W, ta0, ta1, tw, tw64, a, mode, false, false);
     if (r != 0) return r;
     a.epilogue = EPI_STORE;
     a.bias = bias;
@@ -1574,7 +1664,7 @@ int launch_qkv_packed(Context& ctx, const AttnSchedule& s, int M0, int M1, int K
     const double M = (double)M0 + M1;
     ProfileScope prof(ctx, K_GEMM, 2.0 * M * N * K,
                       (M * K + (double)N * K) * 2.0 + (double)s.packed_rows * N * 2.0);
-    const cudaError_t e = mode == TILE_PAIR ? launch_pair_variant<192, 2>(ctx.stream, ta0, ta1, tw, tw, tw, a)
+    const cudaError_t e = mode == TILE_PAIR ? launch_pair_variant<192, 2>(ctx.stream, ta0, ta1, tw, tw, tw, tw, a)
                           : mode == TILE_128 ? launch_variant<128, 192, 2>(grid, ctx.stream, ta0, ta1, tw, tw, tw, a)
                                              : launch_variant<256, 192, 2>(grid, ctx.stream, ta0, ta1, tw, tw, tw, a);
     if (e != cudaSuccess) return S2_ERR_CUDA;
