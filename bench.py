@@ -12,8 +12,9 @@ blocks.
 
 Prints one JSON line (rank 0).  ``value`` = tokens/s of the whole job
 (all GPUs; ``value_per_gpu`` beside it) for the device-resident forward;
-``e2e`` = the same metric through s2_dit_forward_host with host buffers
-(H2D + D2H inside the timed region); ``roofline`` = the dominant kernel from
+``e2e`` = the same metric through the host-buffer entry point
+(s2_dit_forward_host_async; every step's H2D + D2H inside the timed region,
+overlapped with the neighbouring steps' forwards); ``roofline`` = the dominant kernel from
 the library's own per-kernel counters (CUDA events inside the timed region),
 with the window attention's figures as ``attn_*`` keys in it;
 ``cpu_baseline`` = the reference's CPU layer code (oracle/_ref; the oracle
@@ -484,38 +485,68 @@ def main():
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
 
-    # end to end with host buffers (pinned): H2D of this rank's rows and the
-    # modulation, the forward, D2H of the result -- inside the timed region
+    # end to end with host buffers (pinned): every step uploads this rank's
+    # rows and the modulation, runs the forward and downloads the result --
+    # all inside the timed region, pipelined as a serving loop runs them: two
+    # device buffers used in turn, uploads and downloads on copy streams under
+    # the previous / next step's forward (one GPU: s2_dit_forward_host_async;
+    # several: the same around s2_dit_forward_sharded, whose callers own the
+    # host copies)
     e2e_ms = float("nan")
     if not args.no_e2e:
         hx = x0.cpu().pin_memory()
         hm = mod.cpu().pin_memory()
         hout = torch.empty_like(hx).pin_memory()
         if sharded:
-            dx = torch.empty_like(x0)
-            dm = torch.empty_like(mod)
+            up, down = torch.cuda.Stream(), torch.cuda.Stream()
+            dxs = [torch.empty_like(x0) for _ in range(2)]
+            dms = [torch.empty_like(mod) for _ in range(2)]
+            ev = {k: [torch.cuda.Event(), torch.cuda.Event()] for k in ("up", "fwd", "down")}
+            turn = [0]
 
             def e2e_step():
-                dx.copy_(hx, non_blocking=True)
-                dm.copy_(hm, non_blocking=True)
-                forward(dx)
-                hout.copy_(dx, non_blocking=True)
+                b = turn[0] & 1
+                turn[0] += 1
+                with torch.cuda.stream(up):
+                    up.wait_event(ev["down"][b])  # the buffer's previous download has read it
+                    dxs[b].copy_(hx, non_blocking=True)
+                    dms[b].copy_(hm, non_blocking=True)
+                    ev["up"][b].record(up)
+                stream.wait_event(ev["up"][b])
+                dit.forward_sharded(shape, TEXT, dxs[b], dms[b])
+                ev["fwd"][b].record(stream)
+                with torch.cuda.stream(down):
+                    down.wait_event(ev["fwd"][b])
+                    hout.copy_(dxs[b], non_blocking=True)
+                    ev["down"][b].record(down)
+
+            def e2e_finish():
+                down.synchronize()
+                up.synchronize()
         else:
             hv, ht = hx[:nv], hx[nv:]
             ov, ot = hout[:nv], hout[nv:]
             hm3 = hm.reshape(6, 1, D)
 
             def e2e_step():
-                dit.forward_host([shape], [TEXT], hv, ht, hm3, ov, ot)
+                dit.forward_host_async([shape], [TEXT], hv, ht, hm3, ov, ot)
+
+            def e2e_finish():
+                dit.host_wait()
 
         e2e_step()
+        e2e_finish()
         barrier()
-        e2e_steps = max(1, min(args.steps, 5))
+        e2e_steps = max(1, args.steps)
         e0.record(stream)
+        if sharded:
+            up.wait_event(e0)
         for _ in range(e2e_steps):
             e2e_step()
+        e2e_finish()
         e1.record(stream)
         barrier()
+        torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1) / e2e_steps
         if sharded:
             t = torch.tensor([e2e_ms], device="cuda")
@@ -723,7 +754,8 @@ def main():
         "e2e": {"value": None if args.no_e2e else M / (e2e_ms / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": int((n_local + TEXT) * D * 4 + 6 * D * 4),
                 "d2h_bytes_per_step": int((n_local + TEXT) * D * 4), "ms_per_step": None if args.no_e2e else e2e_ms,
-                "entry_point": "s2_dit_forward_sharded + pinned H2D/D2H" if sharded else "s2_dit_forward_host"},
+                "entry_point": ("s2_dit_forward_sharded + pinned H2D/D2H on copy streams, two buffers in turn"
+                                if sharded else "s2_dit_forward_host_async (pinned buffers), s2_dit_host_wait")},
         "gpu_launches": launches,
         "clocks": clk,
         "device_status": status,

@@ -327,6 +327,19 @@ int s2_dit_forward(s2_dit* dit, const int* video_shape, int text_length, float* 
 int s2_dit_forward_host(s2_dit* dit, const int* video_shapes, const int* text_lengths, int batch,
                         const float* video, const float* text, const float* modulation, float* video_out,
                         float* text_out);
+/* Pipelined form of s2_dit_forward_host (same arguments and results): it
+ * enqueues the uploads, the forward and the downloads and returns without
+ * waiting.  Uploads and downloads run on two copy streams of the DiT against
+ * two device staging buffers used in turn, so consecutive calls overlap: call
+ * i+1's upload and call i-1's download run under call i's forward.  For that
+ * overlap the host buffers must be pinned (page-locked); any buffer works,
+ * but pageable ones make the copies wait.  Host buffers stay untouched (inputs)
+ * and unread (outputs) until s2_dit_host_wait returns, which waits for all
+ * enqueued calls and reports a CUDA error among them. */
+int s2_dit_forward_host_async(s2_dit* dit, const int* video_shapes, const int* text_lengths, int batch,
+                              const float* video, const float* text, const float* modulation, float* video_out,
+                              float* text_out);
+int s2_dit_host_wait(s2_dit* dit);
 
 /* ---------------------------------------------------------------------------
  * Token formats and the frontend / tail nets around the block stack

@@ -53,7 +53,7 @@ EXPORTED = [
     "s2_dit_create", "s2_dit_free", "s2_dit_set_block_weights", "s2_dit_set_block_norm", "s2_dit_init_random",
     "s2_dit_forward",
     "s2_dit_set_check_finite", "s2_dit_nonfinite_report", "s2_dit_set_checkpoints",
-    "s2_dit_forward_host", "s2_shard_build", "s2_shard_counts", "s2_shard_lists", "s2_shard_windows", "s2_shard_free",
+    "s2_dit_forward_host", "s2_dit_forward_host_async", "s2_dit_host_wait", "s2_shard_build", "s2_shard_counts", "s2_shard_lists", "s2_shard_windows", "s2_shard_free",
     "s2_dist_unique_id", "s2_dist_init", "s2_dist_sync", "s2_dist_destroy", "s2_peer_barrier",
     "s2_dit_forward_sharded",
     "s2_patchify_video", "s2_unpatchify_prediction", "s2_timestep_embedding", "s2_dit_set_io_weights",
@@ -176,6 +176,8 @@ def lib() -> C.CDLL:
     L.s2_dit_nonfinite_report.argtypes = [vp, C.POINTER(C.c_int), C.POINTER(C.c_int64), C.POINTER(C.c_int64)]
     L.s2_dit_forward.argtypes = [vp, pint, ip, vp, vp]
     L.s2_dit_forward_host.argtypes = [vp, pint, pint, ip, vp, vp, vp, vp, vp]
+    L.s2_dit_forward_host_async.argtypes = [vp, pint, pint, ip, vp, vp, vp, vp, vp]
+    L.s2_dit_host_wait.argtypes = [vp]
     L.s2_shard_build.argtypes = [pint, ip, pint, ip, ip, ip, C.POINTER(vp)]
     L.s2_shard_counts.argtypes = [vp, ip, pint, pint, pint]
     L.s2_shard_lists.argtypes = [vp, ip, pint, pint, pint]
@@ -588,6 +590,18 @@ class Dit:
         check(lib().s2_dit_forward_host(self.handle, _ints(flat), _ints(text_lengths), len(video_shapes),
                                         ptr(video), ptr(text), ptr(modulation), ptr(video_out), ptr(text_out)),
               "s2_dit_forward_host")
+
+    def forward_host_async(self, video_shapes, text_lengths, video, text, modulation, video_out, text_out):
+        """Pipelined forward_host: enqueues and returns; the buffers (pinned for overlap) must
+        stay alive and untouched until host_wait()."""
+        flat = [int(v) for s in video_shapes for v in s]
+        check(lib().s2_dit_forward_host_async(self.handle, _ints(flat), _ints(text_lengths), len(video_shapes),
+                                              ptr(video), ptr(text), ptr(modulation), ptr(video_out),
+                                              ptr(text_out)),
+              "s2_dit_forward_host_async")
+
+    def host_wait(self):
+        check(lib().s2_dit_host_wait(self.handle), "s2_dit_host_wait")
 
 
     def set_io_weights(self, w: dict):

@@ -46,6 +46,17 @@ struct s2_dit
     s2::DeviceBuffer act; // activations of one forward
     s2::DeviceBuffer mods; // [blocks][6][D]
     s2::DeviceBuffer host_x; // staging for s2_dit_forward_host
+    // s2_dit_forward_host_async: two staging buffers used in turn, an upload
+    // and a download stream beside the context's compute stream, and per
+    // buffer the events that order the three
+    struct HostPipe
+    {
+        s2::DeviceBuffer x[2];
+        cudaStream_t up = nullptr, down = nullptr;
+        cudaEvent_t uploaded[2] = {}, computed[2] = {}, downloaded[2] = {};
+        int next = 0;
+        bool ready = false;
+    } pipe;
     // RoPE rotation tables [blocks][rope_pos][pairs] (cos, sin), rebuilt when
     // the weights change or a shape needs more positions
     s2::DeviceBuffer rope;
@@ -429,6 +440,16 @@ void s2_dit_free(s2_dit* d)
     if (!d) return;
     cudaSetDevice(d->ctx->c.device);
     cudaStreamSynchronize(d->ctx->c.stream);
+    s2_dit::HostPipe& hp = d->pipe;
+    for (cudaStream_t st : {hp.up, hp.down})
+        if (st)
+        {
+            cudaStreamSynchronize(st);
+            cudaStreamDestroy(st);
+        }
+    for (int b = 0; b < 2; b++)
+        for (cudaEvent_t e : {hp.uploaded[b], hp.computed[b], hp.downloaded[b]})
+            if (e) cudaEventDestroy(e);
     d->plans.clear();
     d->shards.clear();
     if (d->weights) cudaFree(d->weights);
@@ -1006,6 +1027,101 @@ int s2_dit_forward_host(s2_dit* d, const int* video_shapes, const int* text_leng
     }
     if (cudaStreamSynchronize(c.stream) != cudaSuccess) return S2_ERR_CUDA;
     return r;
+}
+
+namespace {
+
+int host_pipe_init(s2_dit* d)
+{
+    s2_dit::HostPipe& p = d->pipe;
+    if (p.ready) return S2_OK;
+    if (!p.up && cudaStreamCreateWithFlags(&p.up, cudaStreamNonBlocking) != cudaSuccess) return S2_ERR_CUDA;
+    if (!p.down && cudaStreamCreateWithFlags(&p.down, cudaStreamNonBlocking) != cudaSuccess) return S2_ERR_CUDA;
+    for (int b = 0; b < 2; b++)
+        for (cudaEvent_t* e : {&p.uploaded[b], &p.computed[b], &p.downloaded[b]})
+            if (!*e && cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess) return S2_ERR_CUDA;
+    p.ready = true;
+    return S2_OK;
+}
+
+} // namespace
+
+int s2_dit_forward_host_async(s2_dit* d, const int* video_shapes, const int* text_lengths, int batch,
+                              const float* video, const float* text, const float* modulation, float* video_out,
+                              float* text_out)
+{
+    if (!d || !video_shapes || !text_lengths || batch <= 0 || !video || !text || !modulation || !video_out ||
+        !text_out)
+        return S2_ERR_INVALID;
+    for (int s = 0; s < batch; s++)
+        if (video_shapes[3 * s] <= 0 || video_shapes[3 * s + 1] <= 0 || video_shapes[3 * s + 2] <= 0 ||
+            text_lengths[s] <= 0)
+            return S2_ERR_INVALID;
+    s2::Context& c = d->ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    int r = host_pipe_init(d);
+    if (r != S2_OK) return r;
+    s2_dit::HostPipe& p = d->pipe;
+    const int D = d->cfg.hidden;
+    size_t v_off = 0, t_off = 0;
+    for (int s = 0; s < batch; s++)
+    {
+        const int* shp = video_shapes + 3 * s;
+        const size_t nv = (size_t)shp[0] * shp[1] * shp[2], nt = text_lengths[s];
+        const size_t x_bytes = (nv + nt) * D * 4 + (size_t)6 * D * 4;
+        const int b = p.next;
+        p.next ^= 1;
+        if (p.x[b].bytes < x_bytes)
+        {
+            // growing frees the old buffer: every stream finishes with it first
+            if (cudaStreamSynchronize(p.up) != cudaSuccess || cudaStreamSynchronize(p.down) != cudaSuccess ||
+                cudaStreamSynchronize(c.stream) != cudaSuccess)
+                return S2_ERR_CUDA;
+            if ((r = p.x[b].ensure(x_bytes)) != S2_OK) return r;
+        }
+        float* x = static_cast<float*>(p.x[b].ptr);
+        float* mod = x + (nv + nt) * D;
+        // upload once the buffer's previous download has read it
+        if (cudaStreamWaitEvent(p.up, p.downloaded[b], 0) != cudaSuccess ||
+            cudaMemcpyAsync(x, video + v_off * D, nv * D * 4, cudaMemcpyHostToDevice, p.up) != cudaSuccess ||
+            cudaMemcpyAsync(x + nv * D, text + t_off * D, nt * D * 4, cudaMemcpyHostToDevice, p.up) != cudaSuccess)
+            return S2_ERR_CUDA;
+        for (int k = 0; k < 6; k++)
+            if (cudaMemcpyAsync(mod + (size_t)k * D, modulation + ((size_t)k * batch + s) * D, (size_t)D * 4,
+                                cudaMemcpyHostToDevice, p.up) != cudaSuccess)
+                return S2_ERR_CUDA;
+        if (cudaEventRecord(p.uploaded[b], p.up) != cudaSuccess ||
+            cudaStreamWaitEvent(c.stream, p.uploaded[b], 0) != cudaSuccess)
+            return S2_ERR_CUDA;
+        d->cp_video_row = v_off;
+        d->cp_text_row = t_off;
+        r = s2_dit_forward(d, shp, text_lengths[s], x, mod);
+        d->cp_video_row = d->cp_text_row = 0;
+        if (r != S2_OK) return r;
+        // download once the forward is done
+        if (cudaEventRecord(p.computed[b], c.stream) != cudaSuccess ||
+            cudaStreamWaitEvent(p.down, p.computed[b], 0) != cudaSuccess ||
+            cudaMemcpyAsync(video_out + v_off * D, x, nv * D * 4, cudaMemcpyDeviceToHost, p.down) != cudaSuccess ||
+            cudaMemcpyAsync(text_out + t_off * D, x + nv * D, nt * D * 4, cudaMemcpyDeviceToHost, p.down) !=
+                cudaSuccess ||
+            cudaEventRecord(p.downloaded[b], p.down) != cudaSuccess)
+            return S2_ERR_CUDA;
+        v_off += nv;
+        t_off += nt;
+    }
+    return S2_OK;
+}
+
+int s2_dit_host_wait(s2_dit* d)
+{
+    if (!d) return S2_ERR_INVALID;
+    s2::Context& c = d->ctx->c;
+    if (cudaSetDevice(c.device) != cudaSuccess) return S2_ERR_CUDA;
+    const s2_dit::HostPipe& p = d->pipe;
+    if ((p.down && cudaStreamSynchronize(p.down) != cudaSuccess) ||
+        (p.up && cudaStreamSynchronize(p.up) != cudaSuccess) || cudaStreamSynchronize(c.stream) != cudaSuccess)
+        return S2_ERR_CUDA;
+    return S2_OK;
 }
 
 // ---------------------------------------------------------------- frontend / tail

@@ -131,6 +131,36 @@ def test_forward_host_matches_device(gpu_ctx, s2lib):
     dit.close()
 
 
+def test_forward_host_async_pipeline(gpu_ctx, s2lib):
+    """s2_dit_forward_host_async: five calls back to back (pinned buffers, each a batch of two samples, the
+    staging buffers used in turn and one grown on the way) give what s2_dit_forward_host gives for each."""
+    import torch
+
+    D, heads, F = 256, 2, 1024
+    dit = s2lib.Dit(gpu_ctx, num_blocks=2, hidden=D, heads=heads, head_dim=128, mlp_hidden=F, window=[1, 4, 4],
+                    window_mode=1)
+    dit.init_random(11)
+    g = torch.Generator().manual_seed(3)
+    calls = []
+    for i in range(5):
+        shapes = [[1, 6, 8], [2, 4, 4]] if i != 3 else [[2, 8, 8], [1, 4, 4]]
+        tls = [5, 3]
+        nvt = sum(a * b * c for a, b, c in shapes)
+        pin = lambda *sz: torch.randn(*sz, generator=g).pin_memory()
+        calls.append((shapes, tls, pin(nvt, D), pin(sum(tls), D), pin(6, 2, D),
+                      torch.zeros(nvt, D).pin_memory(), torch.zeros(sum(tls), D).pin_memory()))
+    for shapes, tls, v, t, m, vo, to in calls:
+        dit.forward_host_async(shapes, tls, v, t, m, vo, to)
+    dit.host_wait()
+    for shapes, tls, v, t, m, vo, to in calls:
+        rv, rt = torch.zeros_like(vo), torch.zeros_like(to)
+        dit.forward_host(shapes, tls, v, t, m, rv, rt)
+        assert torch.equal(vo, rv) and torch.equal(to, rt)
+        assert not torch.equal(vo, v)
+    assert gpu_ctx.status() == 0
+    dit.close()
+
+
 def test_block_checkpoints(gpu_ctx, s2lib):
     """s2_dit_set_checkpoints: block 0's copy equals a one-block stack's output bit for bit, the last block's
     equals the final rows, s2_dit_forward_host writes each sample at its rows, and a block outside the stack
