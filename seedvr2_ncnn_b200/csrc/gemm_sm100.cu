@@ -706,9 +706,17 @@ __device__ __forceinline__ bool epilogue_gate_residual(const GemmArgs& a, const 
     // loader cursor (lane 0): next box to load
     int lt = wk.first(), lc = 0, lq = 0;
     auto issue_load = [&]() {
-        if (lt >= a.num_tiles) return;
-        int s_, m0_, n0_;
-        const int w_ = wk.template decode<BN>(a, lt, s_, m0_, n0_);
+        int s_, m0_, n0_, w_;
+        for (;;)
+        {
+            if (lt >= a.num_tiles) return;
+            w_ = wk.template decode<BN>(a, lt, s_, m0_, n0_);
+            if (lc < w_ && n0_ + lc < N) break;
+            // a unit with no columns inside N (the second half of a narrow
+            // tile past N) has no boxes, as in the consumer loop below
+            lc = 0;
+            lt += wk.step();
+        }
         const int slot = lq % R;
         mbar_arrive_expect_tx(&rfull[slot], 4096);
         tma_load_2d(stg + slot * 4096, s_ ? tmap_o1 : tmap_o0, &rfull[slot], n0_ + lc, m0_ + quarter * 32);
