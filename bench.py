@@ -493,31 +493,47 @@ def main():
     # several: the same around s2_dit_forward_sharded, whose callers own the
     # host copies)
     e2e_ms = float("nan")
+    e2e_copy_ms = None
     if not args.no_e2e:
         hx = x0.cpu().pin_memory()
         hm = mod.cpu().pin_memory()
         hout = torch.empty_like(hx).pin_memory()
         if sharded:
+            # three buffers: a step's upload never waits for the download two
+            # steps back, so uploads and downloads run side by side (both
+            # directions of the link) under the forwards
+            NB = 3
             up, down = torch.cuda.Stream(), torch.cuda.Stream()
-            dxs = [torch.empty_like(x0) for _ in range(2)]
-            dms = [torch.empty_like(mod) for _ in range(2)]
-            ev = {k: [torch.cuda.Event(), torch.cuda.Event()] for k in ("up", "fwd", "down")}
+            dxs = [torch.empty_like(x0) for _ in range(NB)]
+            dms = [torch.empty_like(mod) for _ in range(NB)]
+            ev = {k: [torch.cuda.Event() for _ in range(NB)] for k in ("up", "fwd", "down")}
+            # copy durations of one step, for the details line
+            ct = {k: [torch.cuda.Event(enable_timing=True) for _ in range(2)] for k in ("up", "down")}
             turn = [0]
 
             def e2e_step():
-                b = turn[0] & 1
+                b = turn[0] % NB
+                timed = turn[0] == 1
                 turn[0] += 1
                 with torch.cuda.stream(up):
                     up.wait_event(ev["down"][b])  # the buffer's previous download has read it
+                    if timed:
+                        ct["up"][0].record(up)
                     dxs[b].copy_(hx, non_blocking=True)
                     dms[b].copy_(hm, non_blocking=True)
+                    if timed:
+                        ct["up"][1].record(up)
                     ev["up"][b].record(up)
                 stream.wait_event(ev["up"][b])
                 dit.forward_sharded(shape, TEXT, dxs[b], dms[b])
                 ev["fwd"][b].record(stream)
                 with torch.cuda.stream(down):
                     down.wait_event(ev["fwd"][b])
+                    if timed:
+                        ct["down"][0].record(down)
                     hout.copy_(dxs[b], non_blocking=True)
+                    if timed:
+                        ct["down"][1].record(down)
                     ev["down"][b].record(down)
 
             def e2e_finish():
@@ -549,6 +565,7 @@ def main():
         torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1) / e2e_steps
         if sharded:
+            e2e_copy_ms = {k: ct[k][0].elapsed_time(ct[k][1]) for k in ("up", "down")}
             t = torch.tensor([e2e_ms], device="cuda")
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             e2e_ms = float(t.item())
@@ -805,6 +822,8 @@ def main():
                  "peer_bytes_per_step": counters["comm"]["bytes"] / args.steps,
                  "host_wait_ms_per_step": counters["host_wait"]["ms"] / args.steps,
                  "other_kernels_ms_per_step": counters["other"]["ms"] / args.steps},
+        # one step's pinned upload / download on rank 0 (sharded e2e)
+        "e2e_copy_ms": e2e_copy_ms,
         "dit_step": dit_step,
         "vae_conv": vae_conv,
     }
