@@ -771,7 +771,7 @@ def main():
         "e2e": {"value": None if args.no_e2e else M / (e2e_ms / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": int((n_local + TEXT) * D * 4 + 6 * D * 4),
                 "d2h_bytes_per_step": int((n_local + TEXT) * D * 4), "ms_per_step": None if args.no_e2e else e2e_ms,
-                "entry_point": ("s2_dit_forward_sharded + pinned H2D/D2H on copy streams, two buffers in turn"
+                "entry_point": ("s2_dit_forward_sharded + pinned H2D/D2H on copy streams, three buffers in turn"
                                 if sharded else "s2_dit_forward_host_async (pinned buffers), s2_dit_host_wait")},
         "gpu_launches": launches,
         "clocks": clk,
