@@ -526,6 +526,41 @@ int s2_vae_mha_create(s2_context* ctx, int embed_dim, int num_heads, float scale
 int s2_vae_mha_forward(s2_vae_mha* layer, const float* x, int tokens, float* out);
 void s2_vae_mha_free(s2_vae_mha* layer);
 
+/* VAE runtime around the encoder / decoder graphs (SeedVR2VAE, seedvr2_vae.h
+ * :17-43).  The graphs are exported .param/.bin files outside the reference
+ * tree; these are the runtime's own steps.
+ *
+ * s2_vae_temporal_segments: extract_temporal_slices (seedvr2_vae.cpp:408-451)
+ * -- the graph runs over frames [start, start + count) with temporal-memory
+ * state S2_VAE_MEMORY_*: one DISABLED run when frames <= first, else a first
+ * run of `first` frames (INITIALIZING) and runs of `active` frames (ACTIVE).
+ * The encoder uses first 5, active 4; the decoder first 2 (1 under the
+ * reference's SEEDVR2_VAE_DECODER_FIRST_ONE), active 1.  Writes up to
+ * `capacity` (start, count, state) triples and returns the number of runs, or
+ * -1 for invalid arguments.
+ * s2_vae_encode_frames / s2_vae_decode_frames: the latent frames of a video
+ * ((frames - 1) / 4 + 1; more than five frames must be 4n + 1, else -1) and
+ * the video frames of a latent ((frames - 1) * 4 + 1), as encode_moments and
+ * decode check them (:551-565, :578-599). */
+#define S2_VAE_SCALING_FACTOR 0.9152f
+int s2_vae_temporal_segments(int frames, int first, int active, int capacity, int* segments);
+int s2_vae_encode_frames(int frames);
+int s2_vae_decode_frames(int latent_frames);
+/* moments_to_latent (seedvr2_vae.cpp:454-478): moments fp32 [32][d][h][w] on
+ * the device (16 mean channels, then 16 log-variance channels) -> latent fp32
+ * [16][d][h][w] = (mean + exp(0.5 clamp(logvar, -30, 20)) * noise) * 0.9152,
+ * or mean * 0.9152 when noise is NULL (sample_posterior false).  noise: fp32
+ * [16][d][h][w] device standard normals; s2_vae_posterior_noise writes the
+ * reference's sequence for a seed into host memory (std::mt19937_64(seed),
+ * std::normal_distribution<float>(0, 1), channel-major; the reference's
+ * default seed is 666). */
+int s2_vae_posterior_noise(uint64_t seed, int64_t count, float* out_host);
+int s2_vae_moments_to_latent(s2_context* ctx, const float* moments, int w, int h, int d, const float* noise,
+                             float* latent);
+/* decode's unscaling (seedvr2_vae.cpp:583-587): latent /= 0.9152 in place
+ * (device fp32, correctly rounded division as the reference's). */
+int s2_vae_unscale_latent(s2_context* ctx, float* latent, int64_t count);
+
 /* ---------------------------------------------------------------------------
  * Multi-GPU (one process per GPU over NVLink).  The reference has no
  * distributed path (seedvr2_main.cpp:89-100 forces --sp-size 1); this is the

@@ -146,6 +146,12 @@ public:
         allocate();
     }
 
+    // ncnn's 4-D create(w, h, d, c[, elemsize, allocator]): pack 1, n 1
+    void create(int _w, int _h, int _d, int _c, size_t _elemsize = 4u, Allocator* a = 0)
+    {
+        create(_w, _h, _d, _c, _elemsize, 1, 1, a);
+    }
+
     void fill(float v)
     {
         float* p = (float*)data;

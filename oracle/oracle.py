@@ -26,6 +26,7 @@ PORT_SO = os.path.join(HERE, "libs2_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libs2_ref.so")
 REF_IO_SO = os.path.join(HERE, "_ref", "libs2_ref_dit_io.so")
 REF_VAE_SO = os.path.join(HERE, "_ref", "libs2_ref_vae.so")
+REF_VAE_RT_SO = os.path.join(HERE, "_ref", "libs2_ref_vae_rt.so")
 
 # DecomposedConv3D memory states (seedvr2::MemoryState)
 VAE_MEMORY_DISABLED = 0
@@ -448,6 +449,22 @@ def ref_mha_forward(E, heads, scale, weights, x, chunk=128, path: str = REF_VAE_
     w = _f32(weights)
     out = np.zeros_like(x)
     r = lib.s2ref_mha_forward(_i32([E, heads, E * E, E, E, chunk]), scale, w, w.size, x, x.shape[0], out)
+    if r != 0:
+        raise ValueError(r)
+    return out
+
+
+def ref_moments_to_latent(moments, sample_posterior=True, seed=666, path: str = REF_VAE_RT_SO):
+    """The reference's own moments_to_latent (seedvr2_vae.cpp:454-478): moments fp32 [32, d, h, w] ->
+    latent fp32 [16, d, h, w], posterior noise from its own generator."""
+    if not os.path.exists(path):
+        raise FileNotFoundError(path)
+    lib = C.CDLL(path)
+    lib.ref_vae_moments_to_latent.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64, _f32p]
+    m = _f32(moments)
+    _, d, h, w = m.shape
+    out = np.zeros((16, d, h, w), dtype=np.float32)
+    r = lib.ref_vae_moments_to_latent(m, w, h, d, int(bool(sample_posterior)), int(seed), out)
     if r != 0:
         raise ValueError(r)
     return out

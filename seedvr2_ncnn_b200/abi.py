@@ -53,7 +53,9 @@ EXPORTED = [
     "s2_dit_create", "s2_dit_free", "s2_dit_set_block_weights", "s2_dit_set_block_norm", "s2_dit_init_random",
     "s2_dit_forward",
     "s2_dit_set_check_finite", "s2_dit_nonfinite_report", "s2_dit_set_checkpoints",
-    "s2_dit_forward_host", "s2_dit_forward_host_async", "s2_dit_host_wait", "s2_shard_build", "s2_shard_counts", "s2_shard_lists", "s2_shard_windows", "s2_shard_free",
+    "s2_dit_forward_host", "s2_dit_forward_host_async", "s2_dit_host_wait", "s2_vae_temporal_segments",
+    "s2_vae_encode_frames", "s2_vae_decode_frames", "s2_vae_posterior_noise", "s2_vae_moments_to_latent",
+    "s2_vae_unscale_latent", "s2_shard_build", "s2_shard_counts", "s2_shard_lists", "s2_shard_windows", "s2_shard_free",
     "s2_dist_unique_id", "s2_dist_init", "s2_dist_sync", "s2_dist_destroy", "s2_peer_barrier",
     "s2_dit_forward_sharded",
     "s2_patchify_video", "s2_unpatchify_prediction", "s2_timestep_embedding", "s2_dit_set_io_weights",
@@ -178,6 +180,12 @@ def lib() -> C.CDLL:
     L.s2_dit_forward_host.argtypes = [vp, pint, pint, ip, vp, vp, vp, vp, vp]
     L.s2_dit_forward_host_async.argtypes = [vp, pint, pint, ip, vp, vp, vp, vp, vp]
     L.s2_dit_host_wait.argtypes = [vp]
+    L.s2_vae_temporal_segments.argtypes = [ip, ip, ip, ip, pint]
+    L.s2_vae_encode_frames.argtypes = [ip]
+    L.s2_vae_decode_frames.argtypes = [ip]
+    L.s2_vae_posterior_noise.argtypes = [C.c_uint64, C.c_int64, vp]
+    L.s2_vae_moments_to_latent.argtypes = [vp, vp, ip, ip, ip, vp, vp]
+    L.s2_vae_unscale_latent.argtypes = [vp, vp, C.c_int64]
     L.s2_shard_build.argtypes = [pint, ip, pint, ip, ip, ip, C.POINTER(vp)]
     L.s2_shard_counts.argtypes = [vp, ip, pint, pint, pint]
     L.s2_shard_lists.argtypes = [vp, ip, pint, pint, pint]
@@ -821,6 +829,55 @@ class VaeMha:
             self.close()
         except Exception:
             pass
+
+
+VAE_SCALING_FACTOR = 0.9152
+
+
+def vae_temporal_segments(frames, first, active):
+    """The VAE runtime's graph runs over a video or latent: list of (start, count, memory_state)."""
+    n = lib().s2_vae_temporal_segments(int(frames), int(first), int(active), 0, None)
+    if n < 0:
+        raise S2Error(n, "s2_vae_temporal_segments")
+    buf = (C.c_int * (3 * n))()
+    lib().s2_vae_temporal_segments(int(frames), int(first), int(active), n, buf)
+    return [tuple(buf[3 * i:3 * i + 3]) for i in range(n)]
+
+
+def vae_encode_frames(frames) -> int:
+    return lib().s2_vae_encode_frames(int(frames))
+
+
+def vae_decode_frames(latent_frames) -> int:
+    return lib().s2_vae_decode_frames(int(latent_frames))
+
+
+def vae_posterior_noise(seed, count):
+    """The reference's posterior noise sequence (host fp32 numpy)."""
+    import numpy as np
+
+    out = np.empty(int(count), dtype=np.float32)
+    check(lib().s2_vae_posterior_noise(C.c_uint64(int(seed)), int(count), out.ctypes.data), "s2_vae_posterior_noise")
+    return out
+
+
+def vae_moments_to_latent(ctx: Context, moments, noise=None, latent=None):
+    """moments: fp32 CUDA [32, d, h, w] -> latent fp32 CUDA [16, d, h, w]; noise fp32 CUDA [16, d, h, w]
+    (None: no posterior sample)."""
+    import torch
+
+    _, d, h, w = moments.shape
+    if latent is None:
+        latent = torch.empty((16, d, h, w), dtype=torch.float32, device=moments.device)
+    check(lib().s2_vae_moments_to_latent(ctx.handle, moments.data_ptr(), w, h, d, ptr(noise), latent.data_ptr()),
+          "s2_vae_moments_to_latent")
+    return latent
+
+
+def vae_unscale_latent(ctx: Context, latent):
+    """latent /= 0.9152 in place (fp32 CUDA)."""
+    check(lib().s2_vae_unscale_latent(ctx.handle, latent.data_ptr(), latent.numel()), "s2_vae_unscale_latent")
+    return latent
 
 
 def shard(video_shape, text_length, window, window_mode, rank, world, shifted=1) -> dict:

@@ -35,7 +35,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I" + os.path.join(ROOT, "include"),
           "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills", "-Wno-deprecated-gpu-targets"]
 
-SOURCES = ["s2_api.cu", "dit.cu", "gemm_sm100.cu", "attention_sm100.cu", "elementwise.cu", "plan.cpp", "awa_static.cu", "dist.cpp", "peer.cu", "dit_io.cu", "conv_sm100.cu", "vae_mha.cu", "graph_ops.cu"]
+SOURCES = ["s2_api.cu", "dit.cu", "gemm_sm100.cu", "attention_sm100.cu", "elementwise.cu", "plan.cpp", "awa_static.cu", "dist.cpp", "peer.cu", "dit_io.cu", "conv_sm100.cu", "vae_mha.cu", "graph_ops.cu", "vae_runtime.cu"]
 
 
 def _headers_digest() -> str:
