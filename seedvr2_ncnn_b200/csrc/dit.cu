@@ -1097,7 +1097,16 @@ int s2_dit_forward_host_async(s2_dit* d, const int* video_shapes, const int* tex
         d->cp_text_row = t_off;
         r = s2_dit_forward(d, shp, text_lengths[s], x, mod);
         d->cp_video_row = d->cp_text_row = 0;
-        if (r != S2_OK) return r;
+        if (r != S2_OK)
+        {
+            // whatever the failed forward enqueued still reads and writes
+            // buffer b: its next upload waits for that work, through the
+            // events a download would have recorded
+            if (cudaEventRecord(p.computed[b], c.stream) == cudaSuccess &&
+                cudaStreamWaitEvent(p.down, p.computed[b], 0) == cudaSuccess)
+                cudaEventRecord(p.downloaded[b], p.down);
+            return r;
+        }
         // download once the forward is done
         if (cudaEventRecord(p.computed[b], c.stream) != cudaSuccess ||
             cudaStreamWaitEvent(p.down, p.computed[b], 0) != cudaSuccess ||
